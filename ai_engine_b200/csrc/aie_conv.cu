@@ -1,0 +1,422 @@
+// C ABI of the B200 conv hot path (declared in include/aie_conv.h).
+//
+// Host side: descriptor validation, kernel/math choice (the Conv arm of
+// ai-gpu-runtime's lower_op, crates/ai-gpu-runtime/src/lowering.rs:99-187),
+// weight packing, and launch dispatch.  Device side: the kernels in the
+// included .cuh files.  Built as one translation unit for sm_100a.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/aie_conv.h"
+#include "common.cuh"
+#include "k_simt.cuh"
+#include "k_tc.cuh"
+
+using namespace aie;
+
+// ------------------------------------------------------------ errors ---
+
+static thread_local char t_err[512];
+
+static int fail(int status, const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof t_err, fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+static int cuda_fail(cudaError_t e, const char *what)
+{
+    return fail(AIE_E_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define CUDA_TRY(call)                                  \
+    do {                                                \
+        cudaError_t e_ = (call);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+// -------------------------------------------------------------- plan ---
+
+struct aie_plan {
+    aie_conv_desc d;
+    int kernel;
+    int math;  // AIE_MATH_FFMA, AIE_MATH_TF32, or kMathStrict
+    bool strict;
+    uint32_t oh, ow;
+    long long M;
+    long long x_stride, y_stride, r_stride;
+    int x_coff, y_coff, r_coff;
+    int y_pad_to;
+    int wn;            // FFMA GEMM weight row stride
+    int cin_pad;       // TF32 weight K stride within a tap
+    uint32_t split, tile_m, tile_n;
+    uint64_t wbytes, bbytes, wsbytes;
+    uint64_t flops, min_bytes, grid;
+    TcGeom tc;         // tensor-core launch geometry (TF32 only)
+};
+
+static const int kMathStrict = AIE_MATH_FP32_STRICT;
+
+static inline uint32_t rup(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+extern "C" int32_t aie_abi_version(void) { return AIE_ABI_VERSION; }
+
+extern "C" const char *aie_build_info(void)
+{
+    return "aie_conv sm_100a (tcgen05 TF32 GEMM, FFMA implicit GEMM, depthwise); nvcc " __DATE__;
+}
+
+extern "C" const char *aie_status_string(int s)
+{
+    switch (s) {
+    case AIE_OK: return "ok";
+    case AIE_E_FAILURE: return "failure";
+    case AIE_E_INVALID: return "invalid argument";
+    case AIE_E_UNSUPPORTED: return "unsupported convolution";
+    case AIE_E_CUDA: return "CUDA error";
+    case AIE_E_ALIGN: return "alignment requirement not met";
+    case AIE_E_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case AIE_E_NOMEM: return "out of host memory";
+    default: return "unknown status";
+    }
+}
+
+extern "C" int aie_last_error(char *buf, size_t len)
+{
+    size_t n = strlen(t_err);
+    if (buf && len) {
+        size_t c = n < len - 1 ? n : len - 1;
+        memcpy(buf, t_err, c);
+        buf[c] = 0;
+    }
+    return (int)n;
+}
+
+static bool tf32_eligible(const aie_plan &p, const char **why)
+{
+    const aie_conv_desc &d = p.d;
+    if (!tc_available()) { *why = "tensor-core kernel not built"; return false; }
+    if (d.groups != 1) { *why = "depthwise"; return false; }
+    if (d.cin % 4 || p.x_stride % 4 || p.x_coff % 4) { *why = "input channels/stride not a multiple of 4"; return false; }
+    if (d.dil != 1 && !(d.kh == 1 && d.kw == 1)) { *why = "dilation"; return false; }
+    if (d.kh != 1 || d.kw != 1 || d.sh != 1 || d.sw != 1 || d.pad[0] || d.pad[1] || d.pad[2] || d.pad[3]) {
+        if (!tc_igemm_supported(d.kh, d.kw, d.sh, d.sw, p.ow)) { *why = "conv geometry"; return false; }
+    }
+    return true;
+}
+
+extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
+{
+    if (!desc || !out) return fail(AIE_E_INVALID, "null argument");
+    *out = nullptr;
+    const aie_conv_desc &d = *desc;
+    if (!d.n || !d.ih || !d.iw || !d.cin || !d.cout || !d.kh || !d.kw || !d.sh || !d.sw || !d.dil || !d.groups)
+        return fail(AIE_E_INVALID, "zero-sized dimension in descriptor");
+    if (d.act < 0 || d.act > AIE_ACT_RECIP) return fail(AIE_E_INVALID, "activation %d out of range", d.act);
+    if (d.layout != AIE_LAYOUT_NHWC && d.layout != AIE_LAYOUT_NHWC_C4)
+        return fail(AIE_E_INVALID, "layout %d out of range", d.layout);
+    if (d.math < AIE_MATH_AUTO || d.math > kMathStrict) return fail(AIE_E_INVALID, "math %d out of range", d.math);
+    if (d.kh > 16 || d.kw > 16) return fail(AIE_E_UNSUPPORTED, "kernel larger than 16x16");
+    // Conv2d::out_hw (crates/ai-core/src/ops/conv.rs:49-55)
+    const long long ekh = (long long)d.dil * (d.kh - 1) + 1, ekw = (long long)d.dil * (d.kw - 1) + 1;
+    const long long hh = (long long)d.ih + d.pad[0] + d.pad[2] - ekh;
+    const long long ww = (long long)d.iw + d.pad[1] + d.pad[3] - ekw;
+    if (hh < 0 || ww < 0) return fail(AIE_E_INVALID, "kernel larger than padded input");
+
+    aie_plan *p = new (std::nothrow) aie_plan();
+    if (!p) return fail(AIE_E_NOMEM, "plan allocation");
+    p->d = d;
+    p->oh = (uint32_t)(hh / d.sh + 1);
+    p->ow = (uint32_t)(ww / d.sw + 1);
+    p->M = (long long)d.n * p->oh * p->ow;
+    const bool c4 = d.layout == AIE_LAYOUT_NHWC_C4;
+    p->x_stride = d.in_stride ? d.in_stride : (c4 ? rup(d.cin, 4) : d.cin);
+    p->x_coff = d.in_coff;
+    p->y_stride = d.out_stride ? d.out_stride : (c4 ? rup(d.cout, 4) : d.cout);
+    p->y_coff = d.out_coff;
+    p->r_stride = d.res_stride ? d.res_stride : (c4 ? rup(d.cout, 4) : d.cout);
+    p->r_coff = d.res_coff;
+    p->y_pad_to = (c4 && !d.out_stride) ? (int)rup(d.cout, 4) : (int)d.cout;
+    if (p->x_coff + (long long)d.cin > p->x_stride || p->y_coff + (long long)d.cout > p->y_stride ||
+        (d.has_res && p->r_coff + (long long)d.cout > p->r_stride)) {
+        delete p;
+        return fail(AIE_E_INVALID, "channel view exceeds its pixel stride");
+    }
+
+    // Kernel family: lowering.rs:130-168 (dw / 1x1 GEMM / implicit GEMM).
+    const uint32_t taps = d.kh * d.kw;
+    if (d.groups > 1) {
+        if (d.groups != d.cin || d.cin != d.cout) {
+            delete p;
+            return fail(AIE_E_UNSUPPORTED, "grouped conv g=%u cin=%u cout=%u", d.groups, d.cin, d.cout);
+        }
+        p->kernel = AIE_KERNEL_DW;
+    } else if (d.kh == 1 && d.kw == 1 && d.sh == 1 && d.sw == 1 && !d.pad[0] && !d.pad[1] && !d.pad[2] &&
+               !d.pad[3]) {
+        // cout <= 4 without a residual takes the dot kernel, as ai-cpu's
+        // PwDot arm does (crates/ai-cpu/src/plan.rs:546-566)
+        p->kernel = (d.cout <= 4 && !d.has_res) ? AIE_KERNEL_PW_DOT : AIE_KERNEL_PW;
+    } else {
+        p->kernel = AIE_KERNEL_IGEMM;
+    }
+
+    // Math.
+    const char *why = "";
+    if (p->kernel == AIE_KERNEL_DW || p->kernel == AIE_KERNEL_PW_DOT) {
+        p->math = d.math == kMathStrict ? kMathStrict : AIE_MATH_FFMA;
+        if (d.math == AIE_MATH_TF32) {
+            delete p;
+            return fail(AIE_E_UNSUPPORTED, "TF32 requested for a memory-bound kernel (depthwise / cout<=4)");
+        }
+    } else if (d.math == AIE_MATH_FFMA || d.math == kMathStrict) {
+        p->math = d.math;
+    } else if (tf32_eligible(*p, &why)) {
+        p->math = AIE_MATH_TF32;
+    } else if (d.math == AIE_MATH_TF32) {
+        delete p;
+        return fail(AIE_E_UNSUPPORTED, "TF32 path needs TMA-compatible operands: %s", why);
+    } else {
+        p->math = AIE_MATH_FFMA;
+    }
+    p->strict = p->math == kMathStrict;
+
+    // Packed sizes and launch geometry.
+    const uint32_t cpad4 = rup(d.cout, 4);
+    p->bbytes = (uint64_t)cpad4 * 4;
+    p->split = 1;
+    if (p->kernel == AIE_KERNEL_DW) {
+        p->wbytes = (uint64_t)taps * cpad4 * 4;
+        p->grid = (uint64_t)((p->M * (cpad4 / 4) + 255) / 256);
+    } else if (p->kernel == AIE_KERNEL_PW_DOT) {
+        p->wbytes = (uint64_t)d.cout * d.cin * 4;
+        p->grid = (uint64_t)((p->M + 255) / 256);
+    } else if (p->math == AIE_MATH_TF32) {
+        p->cin_pad = (int)rup(d.cin, 4);
+        p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
+        int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.pad[0], d.pad[1], p->oh, p->ow,
+                         d.split_k, &p->tc);
+        if (rc) {
+            delete p;
+            return fail(AIE_E_UNSUPPORTED, "tensor-core geometry rejected (%d)", rc);
+        }
+        p->split = p->tc.split;
+        p->tile_m = p->tc.bm;
+        p->tile_n = p->tc.bn;
+        p->wsbytes = p->tc.workspace_bytes;
+        p->grid = p->tc.grid;
+    } else {
+        p->wn = (int)cpad4;
+        p->wbytes = (uint64_t)taps * d.cin * p->wn * 4;
+        p->tile_m = kFfmaBM;
+        p->tile_n = kFfmaBN;
+        p->grid = (uint64_t)((p->M + kFfmaBM - 1) / kFfmaBM) * ((d.cout + kFfmaBN - 1) / kFfmaBN);
+    }
+    // Algorithmic work (ai-cpu prof_meta rule, crates/ai-cpu/src/model.rs:249-260):
+    // border taps counted as full; bytes = input + weights + bias + output (+ res).
+    const uint64_t cin_g = d.cin / d.groups;
+    p->flops = 2ull * (uint64_t)p->M * d.cout * cin_g * taps;
+    p->min_bytes = 4ull * ((uint64_t)d.n * d.ih * d.iw * d.cin + (uint64_t)d.cout * cin_g * taps + d.cout +
+                           (uint64_t)p->M * d.cout * (d.has_res ? 2 : 1));
+    *out = p;
+    return AIE_OK;
+}
+
+extern "C" int aie_conv_plan_info(const aie_plan *p, aie_plan_info *info)
+{
+    if (!p || !info) return fail(AIE_E_INVALID, "null argument");
+    memset(info, 0, sizeof *info);
+    info->kernel = p->kernel;
+    info->math = p->math;
+    info->oh = p->oh;
+    info->ow = p->ow;
+    info->split_k = p->split;
+    info->tile_m = p->tile_m;
+    info->tile_n = p->tile_n;
+    info->weight_bytes = p->wbytes;
+    info->bias_bytes = p->bbytes;
+    info->workspace_bytes = p->wsbytes;
+    info->flops = p->flops;
+    info->min_bytes = p->min_bytes;
+    info->grid_ctas = p->grid;
+    return AIE_OK;
+}
+
+extern "C" void aie_plan_free(aie_plan *p) { delete p; }
+
+// ------------------------------------------------------- weight packing ---
+
+// Unpack the .sw blob layouts (crates/ai-core/src/pack.rs:124-184) to OIHW.
+static void unpack_sw(const aie_conv_desc &d, const float *src, std::vector<float> &oihw)
+{
+    const uint32_t taps = d.kh * d.kw;
+    if (d.groups > 1) {
+        // depthwise [tap][cg][4] (pack.rs:105-122, unpack_weights_dw :153-164)
+        const uint32_t cg = (d.cout + 3) / 4;
+        oihw.assign((size_t)d.cout * taps, 0.f);
+        for (uint32_t ch = 0; ch < d.cout; ch++)
+            for (uint32_t t = 0; t < taps; t++) oihw[(size_t)ch * taps + t] = src[((size_t)t * cg + ch / 4) * 4 + ch % 4];
+    } else {
+        // [tap][kg_pad][ng][4][4] with kg_pad = ceil(cin/4) rounded up to 4
+        // (pack.rs:68-102 with kg_align = 4, as ai-convert lower.rs:151 uses)
+        const uint32_t kg = rup((d.cin + 3) / 4, 4), ng = (d.cout + 3) / 4;
+        oihw.assign((size_t)d.cout * d.cin * taps, 0.f);
+        for (uint32_t t = 0; t < taps; t++)
+            for (uint32_t oc = 0; oc < d.cout; oc++)
+                for (uint32_t ic = 0; ic < d.cin; ic++)
+                    oihw[((size_t)oc * d.cin + ic) * taps + t] =
+                        src[((((size_t)t * kg + ic / 4) * ng + oc / 4) * 4 + oc % 4) * 4 + ic % 4];
+    }
+}
+
+extern "C" int aie_conv_pack_weights(const aie_plan *p, int32_t wfmt, const float *w_host, const float *bias_host,
+                                     void *dev_w, void *dev_b, void *stream)
+{
+    if (!p || !w_host || !dev_w || !dev_b) return fail(AIE_E_INVALID, "null argument");
+    if (wfmt != AIE_WFMT_OIHW && wfmt != AIE_WFMT_SW_PACKED) return fail(AIE_E_INVALID, "weight format %d", wfmt);
+    const aie_conv_desc &d = p->d;
+    const uint32_t taps = d.kh * d.kw;
+    const uint32_t cin_g = d.cin / d.groups;
+    std::vector<float> tmp;
+    const float *w = w_host;
+    if (wfmt == AIE_WFMT_SW_PACKED) {
+        unpack_sw(d, w_host, tmp);
+        w = tmp.data();
+    }
+    std::vector<float> pw(p->wbytes / 4, 0.f), pb(p->bbytes / 4, 0.f);
+    if (p->kernel == AIE_KERNEL_DW) {
+        const uint32_t cpad = rup(d.cout, 4);  // [tap][c_pad4], dw.rs:22-34
+        for (uint32_t ch = 0; ch < d.cout; ch++)
+            for (uint32_t t = 0; t < taps; t++) pw[(size_t)t * cpad + ch] = w[(size_t)ch * taps + t];
+    } else if (p->kernel == AIE_KERNEL_PW_DOT) {
+        memcpy(pw.data(), w, (size_t)d.cout * d.cin * 4);  // [cout][cin]
+    } else if (p->math == AIE_MATH_TF32) {
+        // [tap][cout][cin_pad]: K-major rows for the tcgen05 B operand
+        for (uint32_t t = 0; t < taps; t++)
+            for (uint32_t oc = 0; oc < d.cout; oc++)
+                for (uint32_t ic = 0; ic < d.cin; ic++)
+                    pw[((size_t)t * d.cout + oc) * p->cin_pad + ic] = w[((size_t)oc * cin_g + ic) * taps + t];
+    } else {
+        // [tap][cin][wn] (conv.rs:44-66 with cout padded to 4)
+        for (uint32_t t = 0; t < taps; t++)
+            for (uint32_t ic = 0; ic < d.cin; ic++)
+                for (uint32_t oc = 0; oc < d.cout; oc++)
+                    pw[((size_t)t * d.cin + ic) * p->wn + oc] = w[((size_t)oc * cin_g + ic) * taps + t];
+    }
+    if (bias_host) {
+        if (wfmt == AIE_WFMT_SW_PACKED) memcpy(pb.data(), bias_host, p->bbytes);  // [ng][4]
+        else memcpy(pb.data(), bias_host, (size_t)d.cout * 4);
+        for (uint32_t i = d.cout; i < pb.size(); i++) pb[i] = 0.f;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    CUDA_TRY(cudaMemcpyAsync(dev_w, pw.data(), p->wbytes, cudaMemcpyHostToDevice, s));
+    CUDA_TRY(cudaMemcpyAsync(dev_b, pb.data(), p->bbytes, cudaMemcpyHostToDevice, s));
+    CUDA_TRY(cudaStreamSynchronize(s));  // the host staging vectors die here
+    return AIE_OK;
+}
+
+// ---------------------------------------------------------------- run ---
+
+static ConvArgs make_args(const aie_plan *p, const void *in, const void *w, const void *b, const void *res,
+                          void *out)
+{
+    const aie_conv_desc &d = p->d;
+    ConvArgs a;
+    a.x = (const float *)in;
+    a.w = (const float *)w;
+    a.bias = (const float *)b;
+    a.res = d.has_res ? (const float *)res : nullptr;
+    a.y = (float *)out;
+    a.n = d.n; a.ih = d.ih; a.iw = d.iw; a.cin = d.cin; a.oh = p->oh; a.ow = p->ow; a.cout = d.cout;
+    a.kh = d.kh; a.kw = d.kw; a.sh = d.sh; a.sw = d.sw; a.dil = d.dil; a.pt = d.pad[0]; a.pl = d.pad[1];
+    a.x_stride = p->x_stride; a.y_stride = p->y_stride; a.r_stride = p->r_stride;
+    a.x_coff = p->x_coff; a.y_coff = p->y_coff; a.r_coff = p->r_coff;
+    a.act = d.act;
+    a.y_pad_to = p->y_pad_to;
+    a.M = p->M;
+    a.wn = p->wn;
+    const uintptr_t xa = (uintptr_t)(a.x + a.x_coff), ya = (uintptr_t)(a.y + a.y_coff);
+    const uintptr_t ra = a.res ? (uintptr_t)(a.res + a.r_coff) : 0;
+    a.vec_x = (d.cin % 4 == 0 || d.groups > 1) && a.x_stride % 4 == 0 && xa % 16 == 0;
+    a.vec_y = a.y_stride % 4 == 0 && ya % 16 == 0 && (!a.res || (a.r_stride % 4 == 0 && ra % 16 == 0));
+    return a;
+}
+
+extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, const void *b, const void *res,
+                            void *out, void *workspace, void *stream)
+{
+    if (!p || !in || !w || !b || !out) return fail(AIE_E_INVALID, "null tensor pointer");
+    if (p->d.has_res && !res) return fail(AIE_E_INVALID, "plan has a residual but res is NULL");
+    if (p->wsbytes && !workspace) return fail(AIE_E_INVALID, "plan needs %llu workspace bytes",
+                                              (unsigned long long)p->wsbytes);
+    if (((uintptr_t)w | (uintptr_t)b) % 16) return fail(AIE_E_ALIGN, "weights/bias must be 16-byte aligned");
+    cudaStream_t s = (cudaStream_t)stream;
+    const ConvArgs a = make_args(p, in, w, b, res, out);
+    if (p->kernel == AIE_KERNEL_DW) {
+        if (p->strict) dw_kernel<true><<<(unsigned)p->grid, 256, 0, s>>>(a);
+        else dw_kernel<false><<<(unsigned)p->grid, 256, 0, s>>>(a);
+    } else if (p->kernel == AIE_KERNEL_PW_DOT) {
+        const size_t smem = (size_t)p->d.cout * p->d.cin * 4;
+        if (smem > 200 * 1024) return fail(AIE_E_UNSUPPORTED, "cout*cin too large for the dot kernel");
+        if (smem > 48 * 1024) {
+            CUDA_TRY(cudaFuncSetAttribute(pw_dot_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            CUDA_TRY(cudaFuncSetAttribute(pw_dot_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        }
+        if (p->strict) pw_dot_kernel<true><<<(unsigned)p->grid, 256, smem, s>>>(a);
+        else pw_dot_kernel<false><<<(unsigned)p->grid, 256, smem, s>>>(a);
+    } else if (p->math == AIE_MATH_TF32) {
+        int rc = tc_launch(p->tc, a, workspace, s, t_err, sizeof t_err);
+        if (rc) return rc;
+    } else {
+        dim3 grid((unsigned)((p->M + kFfmaBM - 1) / kFfmaBM), (p->d.cout + kFfmaBN - 1) / kFfmaBN);
+        if (grid.y > 65535) return fail(AIE_E_UNSUPPORTED, "cout too large");
+        if (p->strict) igemm_ffma_kernel<true><<<grid, kFfmaThreads, 0, s>>>(a);
+        else igemm_ffma_kernel<false><<<grid, kFfmaThreads, 0, s>>>(a);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, uint32_t oh,
+                                   uint32_t ow, int32_t mode, const void *add, int32_t act, void *out, void *stream)
+{
+    if (!in || !out) return fail(AIE_E_INVALID, "null tensor pointer");
+    if (!n || !ih || !iw || !c || !oh || !ow) return fail(AIE_E_INVALID, "zero-sized resize");
+    if (mode != 0 && mode != 1) return fail(AIE_E_INVALID, "resize mode %d", mode);
+    if (act < 0 || act > AIE_ACT_RECIP) return fail(AIE_E_INVALID, "activation %d", act);
+    ResizeArgs a;
+    a.x = (const float *)in;
+    a.add = (const float *)add;
+    a.y = (float *)out;
+    a.n = n; a.ih = ih; a.iw = iw; a.c = c; a.oh = oh; a.ow = ow; a.mode = mode; a.act = act;
+    a.sy = (float)ih / (float)oh;
+    a.sx = (float)iw / (float)ow;
+    a.vec = 0;
+    const long long total = (long long)n * oh * ow * ((c + 3) / 4);
+    resize_bilinear_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "resize launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_device_status(void *stream, uint32_t *code_out)
+{
+    CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+    uint32_t v = 0, zero = 0;
+    CUDA_TRY(cudaMemcpyFromSymbol(&v, g_aie_error, sizeof v));
+    if (v) CUDA_TRY(cudaMemcpyToSymbol(g_aie_error, &zero, sizeof zero));
+    if (code_out) *code_out = v;
+    if (v) return fail(AIE_E_DEVICE_TIMEOUT, "device wait gave up, code 0x%08x", v);
+    return AIE_OK;
+}

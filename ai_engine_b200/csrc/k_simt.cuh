@@ -1,0 +1,372 @@
+// CUDA-core kernels of the conv path: implicit-GEMM conv / 1x1 GEMM on FFMA,
+// the cout<=4 pointwise dot kernel, and the depthwise conv.
+//
+// All three accumulate every output starting from its bias and walk taps in
+// (ky, kx) order, then input channels in ascending order -- the order of
+// ai-cpu's conv_std / conv_dw (crates/ai-cpu/src/kernels/conv.rs:238-334,
+// dw.rs:100-200).  With kStrict the multiply and add are rounded separately
+// (__fmul_rn/__fadd_rn), which reproduces ai-cpu's x86 results bit for bit
+// (transcendental activations aside); without it each step is one FFMA.
+#pragma once
+
+#include "common.cuh"
+
+namespace aie {
+
+struct ConvArgs {
+    const float *x;
+    const float *w;
+    const float *bias;
+    const float *res;
+    float *y;
+    int n, ih, iw, cin, oh, ow, cout;
+    int kh, kw, sh, sw, dil, pt, pl;
+    long long x_stride, y_stride, r_stride;  // pixel strides in floats
+    int x_coff, y_coff, r_coff;              // first channel of each view
+    int act;
+    int y_pad_to;    // output lanes [cout, y_pad_to) are written as zero
+    long long M;     // n * oh * ow
+    int wn;          // weight row stride in floats (GEMM: cout padded to 4)
+    int vec_x;       // float4 input loads are aligned
+    int vec_y;       // float4 output / residual accesses are aligned
+};
+
+// ---------------------------------------------------------------------------
+// Implicit-GEMM conv on FFMA.  C[M, cout] = sum_taps X_tap[M, cin] W_tap[cin, cout].
+// CTA tile 128 x 64, K step 16, 256 threads, 8 x 4 outputs per thread.
+// Weights: [tap][cin][wn] (the K-major form of ai-cpu's repack_weights,
+// conv.rs:44-66, with cout padded to 4 instead of 8).
+// ---------------------------------------------------------------------------
+constexpr int kFfmaBM = 128, kFfmaBN = 64, kFfmaBK = 16, kFfmaThreads = 256;
+
+template <bool kStrict>
+__global__ void __launch_bounds__(kFfmaThreads) igemm_ffma_kernel(const ConvArgs a)
+{
+    constexpr int BM = kFfmaBM, BN = kFfmaBN, BK = kFfmaBK;
+    __shared__ __align__(16) float As[2][BK][BM + 4];
+    __shared__ __align__(16) float Bs[2][BK][BN];
+
+    const int tid = threadIdx.x;
+    const long long m0 = (long long)blockIdx.x * BM;
+    const int n0 = blockIdx.y * BN;
+
+    // A-load role: one output pixel (row) and 8 consecutive channels of it.
+    const int ar = tid >> 1, ah = (tid & 1) * 8;
+    const long long am = m0 + ar;
+    const bool am_ok = am < a.M;
+    int iy0 = 0, ix0 = 0;
+    const float *xb = a.x;
+    if (am_ok) {
+        const long long hw = (long long)a.oh * a.ow;
+        const int img = (int)(am / hw);
+        const int rem = (int)(am - (long long)img * hw);
+        const int oy = rem / a.ow, ox = rem - (rem / a.ow) * a.ow;
+        iy0 = oy * a.sh - a.pt;
+        ix0 = ox * a.sw - a.pl;
+        xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff;
+    }
+    // B-load role: one K row, 4 consecutive output channels.
+    const int bk = tid >> 4, bn = (tid & 15) * 4;
+    // Compute role.
+    const int ty = tid >> 4, tx = tid & 15;
+
+    const int kblocks = (a.cin + BK - 1) / BK;
+    const int iters = a.kh * a.kw * kblocks;
+
+    float ra[8];
+    float4 rb;
+
+    auto load = [&](int it) {
+        const int t = it / kblocks, kb = it - t * kblocks;
+        const int ky = t / a.kw, kx = t - ky * a.kw;
+        const int iy = iy0 + ky * a.dil, ix = ix0 + kx * a.dil;
+        const int c0 = kb * BK + ah;
+        const bool ok = am_ok && iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
+        if (ok) {
+            const float *p = xb + ((long long)iy * a.iw + ix) * a.x_stride + c0;
+            if (a.vec_x && c0 + 8 <= a.cin) {
+                const float4 v0 = __ldg(reinterpret_cast<const float4 *>(p));
+                const float4 v1 = __ldg(reinterpret_cast<const float4 *>(p + 4));
+                ra[0] = v0.x; ra[1] = v0.y; ra[2] = v0.z; ra[3] = v0.w;
+                ra[4] = v1.x; ra[5] = v1.y; ra[6] = v1.z; ra[7] = v1.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) ra[j] = (c0 + j < a.cin) ? __ldg(p + j) : 0.0f;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) ra[j] = 0.0f;
+        }
+        const int kr = kb * BK + bk;
+        const int col = n0 + bn;
+        if (kr < a.cin && col < a.wn)
+            rb = __ldg(reinterpret_cast<const float4 *>(a.w + ((long long)t * a.cin + kr) * a.wn + col));
+        else
+            rb = make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+
+    float acc[8][4];
+    {
+        float bv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int col = n0 + tx * 4 + j;
+            bv[j] = col < a.cout ? a.bias[col] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = bv[j];
+    }
+
+    if (iters > 0) load(0);
+    for (int it = 0; it < iters; it++) {
+        const int buf = it & 1;
+#pragma unroll
+        for (int j = 0; j < 8; j++) As[buf][ah + j][ar] = ra[j];
+        *reinterpret_cast<float4 *>(&Bs[buf][bk][bn]) = rb;
+        __syncthreads();
+        if (it + 1 < iters) load(it + 1);
+#pragma unroll
+        for (int k = 0; k < BK; k++) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 8]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 8 + 4]);
+            const float4 b = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = madd<kStrict>(acc[i][j], av[i], bv[j]);
+        }
+    }
+
+    // Epilogue: bias (already in acc) -> act -> +residual
+    // (crates/ai-gpu/src/kernels/common/epilogue.rs:13-30).
+    const int col0 = n0 + tx * 4;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const long long m = m0 + ty * 8 + i;
+        if (m >= a.M) break;
+        float *yr = a.y + m * a.y_stride + a.y_coff;
+        const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff : nullptr;
+        if (a.vec_y && col0 + 4 <= a.cout) {
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = epi_act<kStrict>(a.act, acc[i][j], col0 + j, a.cout);
+            if (rr) {
+                const float4 r = __ldg(reinterpret_cast<const float4 *>(rr + col0));
+                v[0] = add_res<kStrict>(v[0], r.x); v[1] = add_res<kStrict>(v[1], r.y);
+                v[2] = add_res<kStrict>(v[2], r.z); v[3] = add_res<kStrict>(v[3], r.w);
+            }
+            *reinterpret_cast<float4 *>(yr + col0) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int col = col0 + j;
+                if (col < a.cout) {
+                    float v = epi_act<kStrict>(a.act, acc[i][j], col, a.cout);
+                    if (rr) v = add_res<kStrict>(v, rr[col]);
+                    yr[col] = v;
+                } else if (col < a.y_pad_to) {
+                    yr[col] = 0.0f;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 1x1 conv with cout <= 4: one thread per pixel, cout dot products over cin.
+// Weights [cout][cin] staged in shared memory.  Order of
+// crates/ai-cpu/src/kernels/pw_dot.rs:44-58: four lane accumulators from
+// zero (channel c feeds lane c % 4), summed as (l0+l1)+(l2+l3), then the
+// bias, then the scalar activation on every channel.
+// ---------------------------------------------------------------------------
+template <bool kStrict>
+__global__ void __launch_bounds__(256) pw_dot_kernel(const ConvArgs a)
+{
+    extern __shared__ float ws[];  // [cout][cin]
+    const int nw = a.cout * a.cin;
+    for (int i = threadIdx.x; i < nw; i += blockDim.x) ws[i] = a.w[i];
+    __syncthreads();
+    const long long m = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= a.M) return;
+    const float *xr = a.x + m * a.x_stride + a.x_coff;
+    float lane[4][4];
+#pragma unroll
+    for (int o = 0; o < 4; o++)
+#pragma unroll
+        for (int l = 0; l < 4; l++) lane[o][l] = 0.0f;
+    int c = 0;
+    if (a.vec_x) {
+        for (; c + 4 <= a.cin; c += 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + c));
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                if (o < a.cout) {
+                    const float *wr = ws + o * a.cin + c;
+                    lane[o][0] = madd<kStrict>(lane[o][0], v.x, wr[0]);
+                    lane[o][1] = madd<kStrict>(lane[o][1], v.y, wr[1]);
+                    lane[o][2] = madd<kStrict>(lane[o][2], v.z, wr[2]);
+                    lane[o][3] = madd<kStrict>(lane[o][3], v.w, wr[3]);
+                }
+            }
+        }
+    }
+    for (; c < a.cin; c++) {
+        const float v = __ldg(xr + c);
+#pragma unroll
+        for (int o = 0; o < 4; o++)
+            if (o < a.cout) lane[o][c & 3] = madd<kStrict>(lane[o][c & 3], v, ws[o * a.cin + c]);
+    }
+    float *yr = a.y + m * a.y_stride + a.y_coff;
+    const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff : nullptr;
+#pragma unroll
+    for (int o = 0; o < 4; o++) {
+        if (o < a.cout) {
+            const float s = __fadd_rn(__fadd_rn(lane[o][0], lane[o][1]), __fadd_rn(lane[o][2], lane[o][3]));
+            // scalar activation form on every channel: ch=0 of c=0 selects it
+            float v = epi_act<kStrict>(a.act, __fadd_rn(s, a.bias[o]), 0, 0);
+            if (rr) v = add_res<kStrict>(v, rr[o]);
+            yr[o] = v;
+        } else if (o < a.y_pad_to) {
+            yr[o] = 0.0f;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Depthwise conv: one thread per (output pixel, 4-channel group); adjacent
+// threads take adjacent channel groups so every tap load is a coalesced
+// 128-bit access.  Weights [tap][c_pad4] (crates/ai-cpu/src/kernels/dw.rs:22-34),
+// bias [c_pad4].  Memory-bound: the accumulation is always done unfused in
+// ai-cpu's order, which costs nothing here.
+// ---------------------------------------------------------------------------
+template <bool kStrict>
+__global__ void __launch_bounds__(256) dw_kernel(const ConvArgs a)
+{
+    const int cg = (a.cout + 3) >> 2;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= a.M * cg) return;
+    const int g = (int)(idx % cg);
+    const long long m = idx / cg;
+    const long long hw = (long long)a.oh * a.ow;
+    const int img = (int)(m / hw);
+    const int rem = (int)(m - (long long)img * hw);
+    const int oy = rem / a.ow, ox = rem - (rem / a.ow) * a.ow;
+    const int c0 = g * 4;
+    const int cpad = cg * 4;
+    const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.bias) + g);
+    float acc[4] = {b4.x, b4.y, b4.z, b4.w};
+    const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;
+    const bool full = a.vec_x && c0 + 4 <= a.cout;
+    for (int ky = 0; ky < a.kh; ky++) {
+        const int iy = oy * a.sh - a.pt + ky * a.dil;
+        if (iy < 0 || iy >= a.ih) continue;
+        for (int kx = 0; kx < a.kw; kx++) {
+            const int ix = ox * a.sw - a.pl + kx * a.dil;
+            if (ix < 0 || ix >= a.iw) continue;
+            const float *p = xb + ((long long)iy * a.iw + ix) * a.x_stride;
+            const float4 w4 = __ldg(reinterpret_cast<const float4 *>(a.w + (ky * a.kw + kx) * cpad + c0));
+            float xv[4];
+            if (full) {
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(p));
+                xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
+            } else {
+#pragma unroll
+                for (int l = 0; l < 4; l++) xv[l] = c0 + l < a.cout ? __ldg(p + l) : 0.0f;
+            }
+            acc[0] = madd<true>(acc[0], xv[0], w4.x);
+            acc[1] = madd<true>(acc[1], xv[1], w4.y);
+            acc[2] = madd<true>(acc[2], xv[2], w4.z);
+            acc[3] = madd<true>(acc[3], xv[3], w4.w);
+        }
+    }
+    float *yr = a.y + m * a.y_stride + a.y_coff + c0;
+    const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff + c0 : nullptr;
+    if (a.vec_y && c0 + 4 <= a.cout) {
+        float v[4];
+#pragma unroll
+        for (int l = 0; l < 4; l++) v[l] = epi_act<kStrict>(a.act, acc[l], c0 + l, a.cout);
+        if (rr) {
+            const float4 r = __ldg(reinterpret_cast<const float4 *>(rr));
+            v[0] = add_res<true>(v[0], r.x); v[1] = add_res<true>(v[1], r.y);
+            v[2] = add_res<true>(v[2], r.z); v[3] = add_res<true>(v[3], r.w);
+        }
+        *reinterpret_cast<float4 *>(yr) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const int ch = c0 + l;
+            if (ch < a.cout) {
+                float v = epi_act<kStrict>(a.act, acc[l], ch, a.cout);
+                if (rr) v = add_res<true>(v, rr[l]);
+                yr[l] = v;
+            } else if (ch < a.y_pad_to) {
+                yr[l] = 0.0f;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Bilinear resize (crates/ai-core/src/reference/resize.rs:5-42) with an
+// optional fused add and activation.  One thread per (pixel, 4 channels).
+// Multiplies and adds are rounded separately in the reference's order, so
+// the result equals the CPU restatement bit for bit.
+// ---------------------------------------------------------------------------
+struct ResizeArgs {
+    const float *x;
+    const float *add;
+    float *y;
+    int n, ih, iw, c, oh, ow, mode, act;
+    float sy, sx;
+    int vec;
+};
+
+__global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a)
+{
+    const int cg = (a.c + 3) >> 2;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = (long long)a.n * a.oh * a.ow * cg;
+    if (idx >= total) return;
+    const int g = (int)(idx % cg);
+    const long long px = idx / cg;
+    const int ox = (int)(px % a.ow);
+    const long long t = px / a.ow;
+    const int oy = (int)(t % a.oh);
+    const int img = (int)(t / a.oh);
+
+    const float fy = a.mode == 0 ? __fsub_rn(__fmul_rn(__fadd_rn((float)oy, 0.5f), a.sy), 0.5f)
+                                 : __fmul_rn((float)oy, a.sy);
+    const float fx = a.mode == 0 ? __fsub_rn(__fmul_rn(__fadd_rn((float)ox, 0.5f), a.sx), 0.5f)
+                                 : __fmul_rn((float)ox, a.sx);
+    const float fly = floorf(fy), flx = floorf(fx);
+    const int y0 = min(max((int)fly, 0), a.ih - 1), y1 = min(max((int)fly + 1, 0), a.ih - 1);
+    const int x0 = min(max((int)flx, 0), a.iw - 1), x1 = min(max((int)flx + 1, 0), a.iw - 1);
+    const float ty = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
+    const float tx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
+    const float ty1 = __fsub_rn(1.0f, ty), tx1 = __fsub_rn(1.0f, tx);
+
+    const float *xb = a.x + (long long)img * a.ih * a.iw * a.c;
+    const int c0 = g * 4;
+    const float *p00 = xb + ((long long)y0 * a.iw + x0) * a.c + c0;
+    const float *p01 = xb + ((long long)y0 * a.iw + x1) * a.c + c0;
+    const float *p10 = xb + ((long long)y1 * a.iw + x0) * a.c + c0;
+    const float *p11 = xb + ((long long)y1 * a.iw + x1) * a.c + c0;
+    float *yr = a.y + px * a.c + c0;
+    const float *ar = a.add ? a.add + px * a.c + c0 : nullptr;
+    const int nl = min(4, a.c - c0);
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+        if (l >= nl) break;
+        const float top = __fadd_rn(__fmul_rn(__ldg(p00 + l), tx1), __fmul_rn(__ldg(p01 + l), tx));
+        const float bot = __fadd_rn(__fmul_rn(__ldg(p10 + l), tx1), __fmul_rn(__ldg(p11 + l), tx));
+        float v = __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
+        if (ar) v = __fadd_rn(v, __ldg(ar + l));
+        yr[l] = act_apply_strict(a.act, v, c0 + l, a.c);
+    }
+}
+
+}  // namespace aie

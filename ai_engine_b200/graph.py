@@ -1,0 +1,140 @@
+"""Minimal graph executor over the conv path.
+
+Plays the part of ai-gpu-runtime's ``Model`` (crates/ai-gpu-runtime/src/
+model.rs:56-426) for graphs made of convs and bilinear resizes:
+
+* ``load``: infer shapes, lower every conv (``ConvPlan`` = lower_op's Conv
+  arm) and pack its weights, allocate every activation buffer once
+  (no allocation per frame, model.rs:1-5);
+* ``infer``: record all dispatches on one CUDA stream (kernel::record,
+  crates/ai-gpu/src/kernel.rs:181-191), optionally replayed from a
+  captured CUDA graph instead of being re-issued from Python.
+
+A graph is a list of ops; tensors are named, ``"input"`` is the batch.
+  ("conv",   out, src, Conv2d, res_or_None)
+  ("resize", out, src, (oh, ow), add_or_None)
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from .conv import Conv2d, ConvPlan, resize_bilinear
+
+
+@dataclass
+class OpRecord:
+    kind: str
+    out: str
+    src: str
+    conv: Optional[Conv2d] = None
+    res: Optional[str] = None
+    size: Optional[Tuple[int, int]] = None
+    plan: Optional[ConvPlan] = None
+
+
+def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
+    shapes = {"input": tuple(in_hwc)}
+    for op in graph:
+        kind, out, src = op[0], op[1], op[2]
+        h, w, c = shapes[src]
+        if kind == "conv":
+            cv: Conv2d = op[3]
+            if cv.cin != c:
+                raise ValueError(f"{out}: conv expects {cv.cin} channels, {src} has {c}")
+            oh, ow = cv.out_hw(h, w)
+            shapes[out] = (oh, ow, cv.cout)
+            if op[4] is not None and shapes[op[4]] != shapes[out]:
+                raise ValueError(f"{out}: residual {op[4]} shape {shapes[op[4]]} != {shapes[out]}")
+        elif kind == "resize":
+            oh, ow = op[3]
+            shapes[out] = (oh, ow, c)
+            if op[4] is not None and shapes[op[4]] != shapes[out]:
+                raise ValueError(f"{out}: add operand shape mismatch")
+        else:
+            raise ValueError(f"unknown op kind {kind}")
+    return shapes
+
+
+class Model:
+    """Load-time lowering + per-batch execution of a conv graph on one GPU."""
+
+    def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
+                 in_hwc: Tuple[int, int, int], *, math: str = "auto", device=None):
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.n = n
+        self.graph = list(graph)
+        self.shapes = infer_shapes(self.graph, in_hwc)
+        self.output = self.graph[-1][1]
+        self.ops: List[OpRecord] = []
+        self.bufs: Dict[str, torch.Tensor] = {}
+        with torch.cuda.device(self.device):
+            self.bufs["input"] = torch.empty((n, *in_hwc), dtype=torch.float32, device=self.device)
+            for op in self.graph:
+                kind, out, src = op[0], op[1], op[2]
+                h, w, c = self.shapes[src]
+                rec = OpRecord(kind, out, src)
+                if kind == "conv":
+                    rec.conv, rec.res = op[3], op[4]
+                    rec.plan = ConvPlan(rec.conv, n, h, w, has_res=rec.res is not None, math=math,
+                                        device=self.device)
+                    wt, b = weights[out]
+                    rec.plan.load_weights(wt, b)
+                else:
+                    rec.size, rec.res = op[3], op[4]
+                self.bufs[out] = torch.empty((n, *self.shapes[out]), dtype=torch.float32, device=self.device)
+                self.ops.append(rec)
+        self.graph_exec = None
+
+    # -- accounting ------------------------------------------------------------
+    def conv_flops(self) -> int:
+        return sum(r.plan.flops for r in self.ops if r.plan is not None)
+
+    def layer_table(self):
+        rows = []
+        for r in self.ops:
+            if r.plan is not None:
+                rows.append((r.out, r.plan.kernel, r.plan.math, r.plan.flops, r.plan.min_bytes))
+        return rows
+
+    # -- execution -----------------------------------------------------------------
+    def record(self, stream=None):
+        """Issue every op of the graph on `stream` (default: current stream)."""
+        for r in self.ops:
+            src = self.bufs[r.src]
+            out = self.bufs[r.out]
+            if r.kind == "conv":
+                r.plan(src, self.bufs[r.res] if r.res else None, out=out, stream=stream)
+            else:
+                oh, ow = r.size
+                resize_bilinear(src, oh, ow, add=self.bufs[r.res] if r.res else None, out=out, stream=stream)
+        return self.bufs[self.output]
+
+    def capture(self):
+        """Capture the whole batch as one CUDA graph (replaces the per-op
+        Python dispatch; the kernels are the same)."""
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.record()  # warm-up outside capture
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.record()
+        self.graph_exec = g
+        return g
+
+    def infer(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x is not None:
+            self.bufs["input"].copy_(x, non_blocking=True)
+        if self.graph_exec is not None:
+            self.graph_exec.replay()
+        else:
+            self.record()
+        return self.bufs[self.output]
+
+    def release(self):
+        self.graph_exec = None

@@ -1,0 +1,202 @@
+/*
+ * aie_conv.h -- C ABI of the B200 (sm_100a) convolution hot path.
+ *
+ * One plan per convolution layer; caller-owned device buffers; every call is
+ * asynchronous on the caller's CUDA stream and returns an aie_status.  No
+ * entry point aborts, and aie_conv_run allocates nothing.
+ *
+ * What each entry point replaces in ai_engine (paths relative to its root):
+ *
+ *   aie_conv_plan          the SwOp::Conv arm of ai-gpu-runtime's lower_op
+ *                          (crates/ai-gpu-runtime/src/lowering.rs:99-187):
+ *                          groups>1 -> depthwise (ConvDwSpec, conv_dw.rs:21),
+ *                          kh==1 -> pointwise GEMM (GemmPwSpec + pick_variant,
+ *                          gemm_pw.rs:91-149), else implicit GEMM
+ *                          (ConvIgemmSpec::from_op, conv_igemm.rs:79).
+ *   aie_conv_plan_info     KernelSpec::cache_key / workgroups introspection
+ *                          (crates/ai-gpu/src/kernel.rs:26-36).
+ *   aie_conv_pack_weights  the converter's weight packing
+ *                          (crates/ai-core/src/pack.rs:68-184, consumed by
+ *                          ai-convert plan/lower.rs:116-190); accepts the
+ *                          logical OIHW form or the .sw blob's packed form.
+ *   aie_conv_run           kernel::record of one OpDispatch
+ *                          (crates/ai-gpu/src/kernel.rs:181-191) with the
+ *                          binding order of lowering.rs:169-178:
+ *                          input, weights, bias, optional residual, output.
+ *   aie_resize_bilinear    ResizeBilinearSpec (crates/ai-gpu/src/kernels/
+ *                          resize_bilinear.rs) fused with an optional Binary
+ *                          add (crates/ai-gpu/src/kernels/elementwise.rs).
+ *   aie_status_string      RuntimeError's Display
+ *                          (crates/ai-gpu-runtime/src/error.rs:5-13).
+ *   aie_device_status      GpuContext::lost_reason polling
+ *                          (crates/ai-gpu/src/context.rs:145).
+ *
+ * Status convention follows ai-ffi's VbResult (include/ai_engine_ffi.h:15-18
+ * in ai_engine): 0 success, negative failure.
+ */
+#ifndef AIE_CONV_H
+#define AIE_CONV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AIE_ABI_VERSION 1
+
+#ifndef AIE_API
+#define AIE_API __attribute__((visibility("default")))
+#endif
+
+typedef enum aie_status {
+    AIE_OK = 0,
+    AIE_E_FAILURE = -1,        /* VbResult::Failure */
+    AIE_E_INVALID = -2,        /* bad descriptor, null pointer, bad size */
+    AIE_E_UNSUPPORTED = -3,    /* valid conv this library does not run */
+    AIE_E_CUDA = -4,           /* a CUDA runtime/driver call failed */
+    AIE_E_ALIGN = -5,          /* pointer/stride alignment the kernel needs */
+    AIE_E_DEVICE_TIMEOUT = -6, /* a bounded device-side wait gave up */
+    AIE_E_NOMEM = -7           /* host allocation failed (plan time only) */
+} aie_status;
+
+/* Order of ai-core's Activation enum (crates/ai-core/src/activation.rs:7-24). */
+typedef enum aie_act {
+    AIE_ACT_NONE = 0,
+    AIE_ACT_RELU = 1,
+    AIE_ACT_SIGMOID = 2,
+    AIE_ACT_TANH = 3,
+    AIE_ACT_HARDSWISH = 4,
+    AIE_ACT_HARDSIGMOID = 5,
+    AIE_ACT_CLAMP01 = 6,
+    AIE_ACT_RELU6 = 7,
+    AIE_ACT_SQRT = 8,
+    AIE_ACT_NEG = 9,
+    AIE_ACT_RECIP = 10
+} aie_act;
+
+/* Activation memory layouts.  NHWC is ai-cpu's dense logical layout
+ * (crates/ai-cpu/src/view.rs); NHWC_C4 is ai-gpu's layout with channels
+ * zero-padded to a multiple of 4 (crates/ai-core/src/tensor.rs:1-9).  With
+ * NHWC_C4 the output's padding lanes are written as zero, so the output
+ * buffer equals pack_nhwc() of the logical result. */
+typedef enum aie_layout { AIE_LAYOUT_NHWC = 0, AIE_LAYOUT_NHWC_C4 = 1 } aie_layout;
+
+/* Arithmetic of the dense contractions.  FFMA: fp32 fused multiply-add on
+ * the CUDA cores.  TF32: tcgen05 tensor cores, fp32 operands read as TF32,
+ * fp32 accumulate in tensor memory.  FP32_STRICT: fp32 on the CUDA cores with
+ * every multiply and add rounded separately, in ai-cpu's accumulation order
+ * (bias, then taps in (ky, kx) order, then input channels ascending), which
+ * reproduces ai-cpu's x86 results bit for bit apart from the transcendental
+ * activations.  AUTO picks TF32 where the operand layout allows TMA, else
+ * FFMA.  Depthwise runs the unfused order under every setting. */
+typedef enum aie_math {
+    AIE_MATH_AUTO = 0,
+    AIE_MATH_FFMA = 1,
+    AIE_MATH_TF32 = 2,
+    AIE_MATH_FP32_STRICT = 3
+} aie_math;
+
+/* Kernel family chosen by aie_conv_plan. */
+typedef enum aie_kernel {
+    AIE_KERNEL_DW = 1,         /* depthwise */
+    AIE_KERNEL_PW = 2,         /* 1x1 GEMM (M = n*h*w, K = cin, N = cout) */
+    AIE_KERNEL_IGEMM = 3,      /* implicit-GEMM k x k conv */
+    AIE_KERNEL_PW_DOT = 4      /* 1x1 with cout <= 4: per-pixel dot products */
+} aie_kernel;
+
+/* Weight formats accepted by aie_conv_pack_weights. */
+typedef enum aie_wfmt {
+    AIE_WFMT_OIHW = 0,     /* logical [cout][cin/groups][kh][kw], bias [cout] */
+    AIE_WFMT_SW_PACKED = 1 /* .sw blob form: conv [tap][kg_pad][ng][4][4]
+                              (pack.rs:68-102, kg_pad = ceil(cin/4) rounded up
+                              to a multiple of 4), depthwise [tap][cg][4]
+                              (pack.rs:105-122), bias [ng][4] (pack.rs:178) */
+} aie_wfmt;
+
+/* Conv2d (crates/ai-core/src/ops/conv.rs:6-21) plus batch, layout and math.
+ * Zero view fields mean "dense per layout". */
+typedef struct aie_conv_desc {
+    uint32_t n;          /* frames in the batch (the reference is batch 1) */
+    uint32_t ih, iw;     /* input spatial size */
+    uint32_t cin, cout;
+    uint32_t kh, kw;
+    uint32_t sh, sw;
+    uint32_t pad[4];     /* top, left, bottom, right */
+    uint32_t dil;        /* isotropic dilation */
+    uint32_t groups;     /* 1 = dense, cin (== cout) = depthwise */
+    int32_t act;         /* aie_act; epilogue order bias -> act -> +residual */
+    int32_t has_res;     /* residual tensor of the output's shape */
+    int32_t layout;      /* aie_layout of in / res / out */
+    int32_t math;        /* aie_math */
+    uint32_t split_k;    /* tensor-core 1x1 GEMM K split; 0 = auto, 1 = off */
+    /* channel views (SrcView, crates/ai-gpu/src/kernels/common/source.rs:17):
+     * pixel stride and first channel, in floats */
+    uint32_t in_stride, in_coff;
+    uint32_t res_stride, res_coff;
+    uint32_t out_stride, out_coff;
+} aie_conv_desc;
+
+typedef struct aie_plan_info {
+    int32_t kernel;            /* aie_kernel */
+    int32_t math;              /* resolved aie_math (FFMA, TF32 or FP32_STRICT) */
+    uint32_t oh, ow;
+    uint32_t split_k;          /* resolved split (1 = none) */
+    uint32_t tile_m, tile_n;   /* CTA tile of the GEMM kernels */
+    uint32_t reserved;
+    uint64_t weight_bytes;     /* size of dev_w for aie_conv_pack_weights */
+    uint64_t bias_bytes;       /* size of dev_b */
+    uint64_t workspace_bytes;  /* scratch aie_conv_run needs (0 = none) */
+    uint64_t flops;            /* algorithmic 2*MACs, border taps counted */
+    uint64_t min_bytes;        /* input + weights + bias + output (+ res), fp32 */
+    uint64_t grid_ctas;        /* CTAs of the main launch */
+} aie_plan_info;
+
+typedef struct aie_plan aie_plan;
+
+/* ABI version and a build string. */
+AIE_API int32_t aie_abi_version(void);
+AIE_API const char *aie_build_info(void);
+
+/* Validate a conv, choose its kernel and math, and allocate a host-side plan
+ * (immutable, shareable across threads).  Replaces lowering.rs:99-187. */
+AIE_API int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out);
+AIE_API int aie_conv_plan_info(const aie_plan *plan, aie_plan_info *info);
+AIE_API void aie_plan_free(aie_plan *plan);
+
+/* Pack host weights (format aie_wfmt) into the plan's device layout.
+ * dev_w / dev_b must hold info.weight_bytes / info.bias_bytes; bias may be
+ * NULL (zeros).  Synchronous with respect to the host buffers; the device
+ * copy is ordered on `stream` (a cudaStream_t, NULL = legacy default). */
+AIE_API int aie_conv_pack_weights(const aie_plan *plan, int32_t wfmt, const float *w_host, const float *bias_host,
+                          void *dev_w, void *dev_b, void *stream);
+
+/* Run one conv over the batch.  in / res / out are device pointers in the
+ * plan's layout; workspace must hold info.workspace_bytes (may be NULL when
+ * that is 0).  Asynchronous on `stream`. */
+AIE_API int aie_conv_run(const aie_plan *plan, const void *in, const void *dev_w, const void *dev_b, const void *res,
+                 void *out, void *workspace, void *stream);
+
+/* Bilinear resize of a dense NHWC batch [n, ih, iw, c] to [n, oh, ow, c]
+ * (crates/ai-core/src/reference/resize.rs:5-42; mode 0 = half_pixel,
+ * 1 = asymmetric), then out = act(resized + add) when add is non-NULL
+ * (add has the output's shape), else act(resized). */
+AIE_API int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, uint32_t oh,
+                        uint32_t ow, int32_t mode, const void *add, int32_t act, void *out, void *stream);
+
+/* Human-readable status, and the detail message of this thread's last
+ * failure (copied into buf, NUL-terminated; returns its full length). */
+AIE_API const char *aie_status_string(int status);
+AIE_API int aie_last_error(char *buf, size_t len);
+
+/* Read and clear the device error word that bounded device-side waits set
+ * when they give up (synchronises `stream`).  AIE_OK or
+ * AIE_E_DEVICE_TIMEOUT; *code_out (nullable) receives the raw word. */
+AIE_API int aie_device_status(void *stream, uint32_t *code_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AIE_CONV_H */

@@ -1,0 +1,124 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol
+include/aie_conv.h declares, and plans convs the way ai-gpu-runtime's
+lower_op picks kernels (crates/ai-gpu-runtime/src/lowering.rs:130-168).
+aie_conv_plan is host-only, so no CUDA call is made here."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from ai_engine_b200 import _lib
+from ai_engine_b200.build import build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def header_symbols():
+    src = open(os.path.join(ROOT, "include", "aie_conv.h")).read()
+    return sorted(set(re.findall(r"AIE_API\s+[\w\s\*]*?\b(aie_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_binding(lib):
+    names = header_symbols()
+    assert len(names) >= 11
+    assert sorted(_lib.SIGNATURES) == names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in header_symbols():
+        assert hasattr(lib, name), name
+    assert lib.aie_abi_version() == 1
+    assert b"sm_100a" in lib.aie_build_info()
+
+
+def test_struct_sizes_match_header(lib):
+    # 11 u32 + pad[4] + 4 i32 + 7 u32 = 26 * 4 bytes
+    assert C.sizeof(_lib.ConvDesc) == 26 * 4
+    assert C.sizeof(_lib.PlanInfo) == 8 * 4 + 6 * 8
+
+
+def plan(lib, **kw):
+    d = _lib.ConvDesc()
+    base = dict(n=1, ih=8, iw=8, cin=16, cout=16, kh=3, kw=3, sh=1, sw=1, dil=1, groups=1, act=0, layout=0,
+                math=0)
+    base.update(kw)
+    pad = base.pop("pad", (1, 1, 1, 1))
+    for k, v in base.items():
+        setattr(d, k, v)
+    for i in range(4):
+        d.pad[i] = pad[i]
+    h = C.c_void_p()
+    st = lib.aie_conv_plan(C.byref(d), C.byref(h))
+    info = _lib.PlanInfo()
+    if st == 0:
+        assert lib.aie_conv_plan_info(h, C.byref(info)) == 0
+        lib.aie_plan_free(h)
+    return st, info
+
+
+def test_kernel_choice_mirrors_lower_op(lib):
+    st, i = plan(lib, groups=16)
+    assert st == 0 and i.kernel == _lib.KERNEL_DW
+    st, i = plan(lib, kh=1, kw=1, pad=(0, 0, 0, 0), cout=64)
+    assert st == 0 and i.kernel == _lib.KERNEL_PW
+    st, i = plan(lib, kh=1, kw=1, pad=(0, 0, 0, 0), cout=2)
+    assert st == 0 and i.kernel == _lib.KERNEL_PW_DOT
+    st, i = plan(lib)
+    assert st == 0 and i.kernel == _lib.KERNEL_IGEMM and (i.oh, i.ow) == (8, 8)
+    # 1x1 with stride: the reference GPU rejects it; ai-cpu runs it as conv_std
+    st, i = plan(lib, kh=1, kw=1, sh=2, sw=2, pad=(0, 0, 0, 0))
+    assert st == 0 and i.kernel == _lib.KERNEL_IGEMM and (i.oh, i.ow) == (4, 4)
+
+
+def test_out_hw_and_work_accounting(lib):
+    st, i = plan(lib, ih=160, iw=288, cin=16, cout=16, sh=2, sw=2, n=2)
+    assert st == 0 and (i.oh, i.ow) == (80, 144)
+    assert i.flops == 2 * 2 * 80 * 144 * 16 * 16 * 9
+    assert i.min_bytes == 4 * (2 * 160 * 288 * 16 + 16 * 16 * 9 + 16 + 2 * 80 * 144 * 16)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(n=0), _lib.STATUS and -2), (dict(cin=0), -2), (dict(act=11), -2), (dict(layout=5), -2),
+    (dict(math=9), -2), (dict(groups=4, cin=16, cout=16), -3), (dict(ih=1, iw=1, pad=(0, 0, 0, 0)), -2),
+    (dict(in_stride=8), -2), (dict(kh=17, kw=17), -3)])
+def test_invalid_descriptors_are_rejected(lib, kw, status):
+    st, _ = plan(lib, **kw)
+    assert st == status
+    msg = _lib.last_error()
+    assert msg, "a failure must leave a detail message"
+
+
+def test_tf32_request_on_depthwise_is_unsupported(lib):
+    st, _ = plan(lib, groups=16, math=_lib.MATH_TF32)
+    assert st == -3
+
+
+def test_status_strings(lib):
+    for s in (0, -1, -2, -3, -4, -5, -6, -7):
+        assert lib.aie_status_string(s)
+    assert lib.aie_status_string(-99) == b"unknown status"
+
+
+def test_null_arguments(lib):
+    assert lib.aie_conv_plan(None, None) == -2
+    assert lib.aie_conv_plan_info(None, None) == -2
+    assert lib.aie_conv_run(None, None, None, None, None, None, None, None) == -2
+    assert lib.aie_conv_pack_weights(None, 0, None, None, None, None, None) == -2
+    assert lib.aie_resize_bilinear(1, 1, 1, 1, None, 1, 1, 0, None, 0, None, None) == -2
+    lib.aie_plan_free(None)
+
+
+def test_views_and_c4_layout_strides(lib):
+    st, i = plan(lib, cin=6, cout=10, layout=_lib.LAYOUT_NHWC_C4)
+    assert st == 0
+    st, _ = plan(lib, cin=6, in_stride=10, in_coff=4)
+    assert st == 0
+    st, _ = plan(lib, cin=6, in_stride=10, in_coff=5)
+    assert st == -2

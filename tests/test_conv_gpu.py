@@ -1,0 +1,258 @@
+"""GPU parity of the conv kernels against the CPU oracle, through the C ABI.
+
+The shape grids, seeds and draw order restate ai_engine's GPU-vs-CPU
+accuracy suite (crates/ai-gpu/src/testsuite.rs:373-411 pointwise,
+:466-495 depthwise, :722-785 implicit GEMM).  Tolerances
+(normalised error of tests/_util.py):
+  fp32_strict  bit-exact with the ai-cpu restatement (non-transcendental acts)
+  ffma         <= 1e-5
+  tf32         <= 5e-3
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from ai_engine_b200 import Conv2d, View, pack
+from ai_engine_b200.conv import ConvPlan
+from tests._util import EXACT_ACTS, TOL_FFMA, TOL_TF32, case_tensors, normalised_error, oracle_conv
+
+pytestmark = pytest.mark.gpu
+
+MATHS = ["fp32_strict", "ffma"]
+
+
+def run_gpu(op, x, w, b, res=None, *, layout="nhwc", math="ffma", wfmt="oihw", **kw):
+    n, ih, iw, cin = x.shape
+    plan = ConvPlan(op, n, ih, iw, has_res=res is not None, layout=layout, math=math, **kw)
+    if wfmt == "sw":
+        if op.groups > 1:
+            wp = pack.pack_weights_dw(w, op.cout, op.kh, op.kw)
+        else:
+            wp, _ = pack.pack_weights_conv(w, op.cout, op.cin, op.kh, op.kw, 4)
+        plan.load_weights(wp, pack.pack_bias(b, op.cout), fmt="sw")
+    else:
+        plan.load_weights(w, b)
+    if layout == "nhwc_c4":
+        xd = torch.from_numpy(pack.pack_nhwc(x)).cuda()
+        rd = None if res is None else torch.from_numpy(pack.pack_nhwc(res)).cuda()
+    else:
+        xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        rd = None if res is None else torch.from_numpy(np.ascontiguousarray(res)).cuda()
+    out = plan(xd, rd)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    if layout == "nhwc_c4":
+        # bit-exact layout: padding lanes are zero, i.e. out == pack_nhwc(logical)
+        assert got.shape[-1] == pack.cg(op.cout) * 4
+        assert not got[..., op.cout:].any(), "C4 padding lanes must be zero"
+        got = got[..., :op.cout]
+    return plan, got
+
+
+def check(op, x, w, b, res, math, **kw):
+    want, scale = oracle_conv(op, x, w, b, res)
+    plan, got = run_gpu(op, x, w, b, res, math=math, **kw)
+    assert got.shape == want.shape
+    assert plan.math == math or (math == "auto")
+    if math == "fp32_strict" and op.act in EXACT_ACTS:
+        diff = np.flatnonzero(got.reshape(-1) != want.reshape(-1))
+        assert diff.size == 0, f"{diff.size} outputs differ from ai-cpu, first {diff[:5]}"
+    else:
+        tol = TOL_TF32 if plan.math == "tf32" else TOL_FFMA
+        err = normalised_error(got, want, scale)
+        assert err <= tol, f"normalised error {err:.3g} > {tol} ({plan.kernel}/{plan.math})"
+    return plan, got
+
+
+# ---------------------------------------------------------------- pointwise ---
+
+PW_SHAPES = [(1, 1, 64, 16), (9, 16, 128, 24), (3, 5, 6, 10), (72, 128, 16, 64), (24, 32, 6, 10),
+             (23, 33, 8, 20), (9, 16, 960, 160), (9, 16, 240, 68), (11, 13, 72, 68)]
+PW_ACTS = ["none", "relu", "hardswish", "sigmoid"]
+
+
+def pw_cases():
+    seed = 2000
+    for (h, w, cin, cout) in PW_SHAPES:
+        for act in PW_ACTS:
+            seed += 1
+            yield pytest.param(h, w, cin, cout, act, seed, id=f"{h}x{w}-{cin}-{cout}-{act}")
+
+
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("h,w,cin,cout,act,seed", list(pw_cases()))
+def test_pointwise_grid(cuda_ok, math, h, w, cin, cout, act, seed):
+    """testsuite.rs:373-391 (pw_case grid)"""
+    op = Conv2d.pointwise(cin, cout, act)
+    x, wt, b, _ = case_tensors(op, 1, h, w, seed, False)
+    check(op, x, wt, b, None, math)
+
+
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("h,w,cin,cout,act,seed", [(9, 16, 32, 32, "relu", 3001), (9, 16, 960, 160, "relu", 3003),
+                                                   (72, 128, 16, 16, "hardswish", 3002)])
+def test_pointwise_residual(cuda_ok, math, h, w, cin, cout, act, seed):
+    """testsuite.rs:393-398: residual added after the activation"""
+    op = Conv2d.pointwise(cin, cout, act)
+    x, wt, b, res = case_tensors(op, 1, h, w, seed, True)
+    check(op, x, wt, b, res, math)
+
+
+# ---------------------------------------------------------------- depthwise ---
+
+DW_SHAPES = [(72, 128, 64, 3, 1), (36, 64, 96, 5, 2), (33, 17, 6, 3, 2), (16, 16, 10, 5, 1)]
+
+
+def dw_cases():
+    seed = 4000
+    for (ih, iw, c, k, s) in DW_SHAPES:
+        for act in ["none", "relu", "hardswish"]:
+            seed += 1
+            yield pytest.param(ih, iw, c, k, s, act, seed, id=f"{ih}x{iw}-c{c}-k{k}s{s}-{act}")
+
+
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("ih,iw,c,k,s,act,seed", list(dw_cases()))
+def test_depthwise_grid(cuda_ok, math, ih, iw, c, k, s, act, seed):
+    """testsuite.rs:469-484 (dw_case grid)"""
+    op = Conv2d.depthwise(c, k, s, act)
+    x, wt, b, _ = case_tensors(op, 1, ih, iw, seed, False)
+    check(op, x, wt, b, None, math)
+
+
+@pytest.mark.parametrize("math", MATHS)
+def test_depthwise_residual_and_dilation(cuda_ok, math):
+    """testsuite.rs:485-488 (residual 5001, dilated dw 5201, dilated igemm 5202)"""
+    op = Conv2d.depthwise(32, 3, 1, "relu")
+    x, wt, b, res = case_tensors(op, 1, 36, 64, 5001, True)
+    check(op, x, wt, b, res, math)
+    op = Conv2d(40, 40, 3, 3, 1, 1, (2, 2, 2, 2), 2, 40, "relu")
+    x, wt, b, _ = case_tensors(op, 1, 18, 32, 5201, False)
+    check(op, x, wt, b, None, math)
+    op = Conv2d(8, 12, 3, 3, 1, 1, (2, 2, 2, 2), 2, 1, "hardswish")
+    x, wt, b, _ = case_tensors(op, 1, 24, 32, 5202, False)
+    check(op, x, wt, b, None, math)
+
+
+# ------------------------------------------------------------ implicit GEMM ---
+
+IG_SHAPES = [(36, 64, 3, 16, 3, 2), (24, 32, 16, 24, 3, 1), (40, 64, 20, 32, 3, 1), (17, 23, 6, 8, 3, 2),
+             (33, 45, 8, 12, 5, 2), (9, 16, 128, 128, 3, 1), (18, 32, 171, 80, 3, 1)]
+
+
+def ig_cases():
+    seed = 6000
+    for (ih, iw, cin, cout, k, s) in IG_SHAPES:
+        for act in ["none", "relu", "hardswish"]:
+            seed += 1
+            yield pytest.param(ih, iw, cin, cout, k, s, act, seed, id=f"{ih}x{iw}-{cin}-{cout}-k{k}s{s}-{act}")
+
+
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("ih,iw,cin,cout,k,s,act,seed", list(ig_cases()))
+def test_igemm_grid(cuda_ok, math, ih, iw, cin, cout, k, s, act, seed):
+    """testsuite.rs:725-743 (igemm_case grid)"""
+    op = Conv2d.same(cin, cout, k, s, act)
+    x, wt, b, _ = case_tensors(op, 1, ih, iw, seed, False)
+    check(op, x, wt, b, None, math)
+
+
+IG_SPECIAL = [  # testsuite.rs:745-773: asymmetric SAME pads, real stem size, residuals
+    (16, 16, 4, 8, 3, 1, (1, 0, 0, 1), "relu", False, 7001),
+    (128, 128, 3, 16, 3, 2, (0, 0, 1, 1), "none", False, 7008),
+    (32, 32, 3, 16, 3, 2, (0, 0, 1, 1), "none", False, 7005),
+    (32, 32, 3, 24, 5, 2, (1, 1, 2, 2), "none", False, 7006),
+    (24, 24, 16, 16, 3, 2, (0, 0, 1, 1), "relu", False, 7007),
+    (24, 32, 16, 16, 3, 1, (1, 1, 1, 1), "hardswish", True, 7002),
+    (9, 16, 8, 8, 3, 1, (1, 1, 1, 1), "none", True, 7003),
+    (9, 16, 128, 128, 3, 1, (1, 1, 1, 1), "relu", True, 7004),
+]
+
+
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("ih,iw,cin,cout,k,s,pad,act,res,seed", IG_SPECIAL, ids=[str(c[-1]) for c in IG_SPECIAL])
+def test_igemm_special(cuda_ok, math, ih, iw, cin, cout, k, s, pad, act, res, seed):
+    op = Conv2d(cin, cout, k, k, s, s, pad, 1, 1, act)
+    x, wt, b, r = case_tensors(op, 1, ih, iw, seed, res)
+    check(op, x, wt, b, r, math)
+
+
+# ------------------------------------------------- layouts, formats, views ---
+
+@pytest.mark.parametrize("kind", ["pw", "dw", "igemm", "pw_dot"])
+def test_c4_layout_and_sw_packed_weights(cuda_ok, kind):
+    """The reference GPU layout: NHWC-C4 activations and .sw-packed weights
+    (crates/ai-core/src/pack.rs:34-184).  Output padding lanes must be zero."""
+    op = {"pw": Conv2d.pointwise(6, 10, "relu"), "dw": Conv2d.depthwise(7, 3, 2, "hardswish"),
+          "igemm": Conv2d.same(6, 10, 3, 1, "none"), "pw_dot": Conv2d.pointwise(7, 3, "sigmoid")}[kind]
+    x, wt, b, res = case_tensors(op, 2, 9, 11, 77, kind != "pw_dot")
+    plan, _ = check(op, x, wt, b, res, "ffma", layout="nhwc_c4", wfmt="sw")
+    assert plan.kernel == kind
+
+
+def test_strided_view_input(cuda_ok):
+    """dw.rs:313-347 on the GPU: the input is a channel slice of a wider tensor."""
+    ih, iw, big_c, c, c_off = 6, 5, 10, 6, 3
+    from oracle import XorShift32
+    rng = XorShift32(4)
+    big = rng.vec_f32(ih * iw * big_c).reshape(1, ih, iw, big_c)
+    wt = rng.vec_f32(c * 9)
+    b = rng.vec_f32(c)
+    op = Conv2d.depthwise(c, 3, 1, "relu")
+    xm = np.ascontiguousarray(big[..., c_off:c_off + c])
+    want, scale = oracle_conv(op, xm, wt, b, None)
+    plan = ConvPlan(op, 1, ih, iw, in_view=View(big_c, c_off), math="fp32_strict").load_weights(wt, b)
+    got = plan(torch.from_numpy(big).cuda()).cpu().numpy()
+    assert np.array_equal(got, want)
+
+
+def test_output_view_writes_only_its_channels(cuda_ok):
+    """An output view (concat slot) leaves the other channels untouched."""
+    op = Conv2d.pointwise(16, 8, "relu")
+    x, wt, b, _ = case_tensors(op, 2, 5, 7, 91, False)
+    want, _ = oracle_conv(op, x, wt, b, None)
+    big = torch.full((2, 5, 7, 20), 7.0, device="cuda")
+    plan = ConvPlan(op, 2, 5, 7, out_view=View(20, 4), math="fp32_strict").load_weights(wt, b)
+    plan(torch.from_numpy(x).cuda(), out=big)
+    got = big.cpu().numpy()
+    assert np.array_equal(got[..., 4:12], want)
+    assert (got[..., :4] == 7).all() and (got[..., 12:] == 7).all()
+
+
+@pytest.mark.parametrize("math", MATHS)
+def test_batch_matches_per_frame(cuda_ok, math):
+    """Frames are independent: a batch of 5 equals 5 single-frame runs."""
+    op = Conv2d.same(16, 24, 3, 2, "relu")
+    x, wt, b, _ = case_tensors(op, 5, 17, 19, 123, False)
+    _, batched = run_gpu(op, x, wt, b, math=math)
+    for f in range(5):
+        _, single = run_gpu(op, x[f:f + 1], wt, b, math=math)
+        assert np.array_equal(single[0], batched[f])
+
+
+def test_canary_no_write_outside_output(cuda_ok):
+    """Layout check: nothing is written past the output tensor."""
+    op = Conv2d.same(8, 12, 3, 1, "none")
+    x, wt, b, _ = case_tensors(op, 1, 7, 9, 5, False)
+    plan = ConvPlan(op, 1, 7, 9).load_weights(wt, b)
+    n_out = 7 * 9 * 12
+    buf = torch.full((n_out + 4096,), 1234.5, device="cuda")
+    plan(torch.from_numpy(x).cuda(), out=buf[:n_out].view(1, 7, 9, 12))
+    assert (buf[n_out:] == 1234.5).all()
+
+
+def test_resize_bilinear_bit_exact(cuda_ok):
+    """GPU resize (+ fused add) equals the CPU restatement bit for bit."""
+    from ai_engine_b200 import resize_bilinear
+    from oracle import XorShift32
+    rng = XorShift32(31)
+    x = rng.vec_f32(2 * 5 * 9 * 6).reshape(2, 5, 9, 6)
+    add = rng.vec_f32(2 * 10 * 18 * 6).reshape(2, 10, 18, 6)
+    for mode in ["half_pixel", "asymmetric"]:
+        want = oracle.resize_bilinear(x, 10, 18, mode)
+        got = resize_bilinear(torch.from_numpy(x).cuda(), 10, 18, mode).cpu().numpy()
+        assert np.array_equal(got, want)
+    want = oracle.add(oracle.resize_bilinear(x, 10, 18), add)
+    got = resize_bilinear(torch.from_numpy(x).cuda(), 10, 18, add=torch.from_numpy(add).cuda()).cpu().numpy()
+    assert np.array_equal(got, want)
