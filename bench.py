@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Benchmark: MNv4-style segmentation net at 160x288, 256 frames per GPU.
+
+One step = one forward pass of the conv graph over a batch of 256 frames
+resident in HBM (configs 1-3 are parity-test cases).
+Frames shard across GPUs with no collective on the hot path (weak
+scaling); the only collective is a max-reduce of the timings.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  --impl reference times the CPU
+restatement of ai_engine's ai-cpu path on all host cores (the Rust
+reference itself cannot be built here: no Rust toolchain).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MNv4-seg 160x288 frames/s at 1/2/4/8 B200; conv GEMM TFLOP/s vs TF32 peak"
+UNIT = "frames/s"
+BATCH = 256
+H, W = 160, 288
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks ---
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU during the timed region."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+        except Exception as e:  # clocks are reported as unavailable, the bench still runs
+            self.error = repr(e)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if self._h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- CPU baseline ---
+
+_CPU_MODEL = {}
+
+
+def cpu_baseline(frames: int, threads: int):
+    """ai-cpu restatement, throughput mode (one frame per core), on a sample
+    of `frames` frames of the same workload."""
+    from ai_engine_b200 import segnet
+    from oracle.graph import OracleModel
+    if "m" not in _CPU_MODEL:
+        g = segnet.build_graph()
+        _CPU_MODEL["m"] = OracleModel(g, segnet.init_weights(g), (H, W, 3))
+        _CPU_MODEL["x"] = segnet.synthetic_input(max(frames, threads), seed=1)
+        _CPU_MODEL["m"].run_batch(_CPU_MODEL["x"][:threads], threads=threads)  # warm-up
+    m, x = _CPU_MODEL["m"], _CPU_MODEL["x"]
+    if x.shape[0] < frames:
+        x = _CPU_MODEL["x"] = segnet.synthetic_input(frames, seed=1)
+    t0 = time.perf_counter()
+    m.run_batch(x[:frames], threads=threads)
+    dt = time.perf_counter() - t0
+    return frames / dt, dt
+
+
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank):
+    """--impl reference: the CPU restatement of ai-cpu on all host cores."""
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    frames = max(threads, 64)
+    for _ in range(args.warmup):
+        cpu_baseline(threads, threads)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, _ = cpu_baseline(frames, threads)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / max(args.steps, 1), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "MNv4-style seg net 160x288 (BASELINE config 4), CPU sample", "frames_per_step": frames,
+                   "h": H, "w": W},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{frames} frames per step, one frame per core (ai-cpu throughput mode), "
+                                   f"CPU restatement of crates/ai-cpu compiled -O3 -ffp-contract=off; "
+                                   f"{cpu_model_name()}"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the Rust reference cannot be built here (no Rust toolchain); this arm runs its C restatement",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- GPU arm ---
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--math", default="auto", choices=["auto", "ffma", "tf32", "fp32_strict"])
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from ai_engine_b200 import segnet
+    from ai_engine_b200.graph import Model
+
+    n = args.batch
+    g = segnet.build_graph()
+    weights = segnet.init_weights(g)  # same weights on every rank (replicas)
+    model = Model(g, weights, n, (H, W, 3), math=args.math, device=dev)
+    x_host = torch.from_numpy(segnet.synthetic_input(n, seed=100 + rank)).pin_memory()
+    model.bufs["input"].copy_(x_host)
+    stream = torch.cuda.current_stream(dev)
+    out_host = torch.empty(model.bufs[model.output].shape, dtype=torch.float32).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up
+    for _ in range(max(args.warmup, 3)):
+        model.record()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, per-op CUDA events on the launching stream
+    ops = model.ops
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        for k in range(args.steps):
+            ev = evs[k]
+            ev[0].record(stream)
+            for i, r in enumerate(ops):
+                src, out = model.bufs[r.src], model.bufs[r.out]
+                if r.kind == "conv":
+                    r.plan(src, model.bufs[r.res] if r.res else None, out=out)
+                else:
+                    from ai_engine_b200.conv import resize_bilinear
+                    resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
+                ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = evs[0][0].elapsed_time(evs[-1][-1])
+    total_ms = max_over_ranks(total_ms)
+    frames = n * world * args.steps
+    value = frames / (total_ms / 1000.0)
+
+    # per-op durations (ms) averaged over the K timed steps
+    per_op = np.zeros(len(ops))
+    for ev in evs:
+        for i in range(len(ops)):
+            per_op[i] += ev[i].elapsed_time(ev[i + 1])
+    per_op /= args.steps
+
+    # ---- CUDA-graph replay of the same step (launch overhead removed)
+    graph_value = None
+    try:
+        model.capture()
+        for _ in range(3):
+            model.infer()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.infer()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        gms = max_over_ranks(e0.elapsed_time(e1))
+        graph_value = n * world * args.steps / (gms / 1000.0)
+    except Exception as e:  # reported, not fatal
+        graph_value = f"capture failed: {e!r}"
+
+    # ---- end to end through the public API: pinned host frames in, mask out
+    for _ in range(2):
+        model.infer(x_host.to(dev, non_blocking=True))
+        out_host.copy_(model.bufs[model.output], non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        model.bufs["input"].copy_(x_host, non_blocking=True)
+        model.infer()
+        out_host.copy_(model.bufs[model.output], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = n * world * args.steps / (e2e_ms / 1000.0)
+    model.release()
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    # ---- roofline of the dominant launch
+    pk = peaks()
+    hbm = pk["hbm_gbs"]
+    tf32_peak = pk["bf16_tflops"] / 2.0  # TF32 dense = half the bf16 rate
+    layers = []
+    for r, ms in zip(ops, per_op):
+        if r.plan is not None:
+            fl, by = r.plan.flops, r.plan.min_bytes
+            kern, math = r.plan.kernel, r.plan.math
+        else:
+            oh, ow = r.size
+            c = model.shapes[r.out][2]
+            ih, iw, _ = model.shapes[r.src]
+            fl, by = 0, 4 * n * c * (ih * iw + oh * ow + (oh * ow if r.res else 0))
+            kern, math = "resize", "f32"
+        layers.append({"op": r.out, "kernel": kern, "math": math, "ms": float(ms), "flops": int(fl),
+                       "bytes": int(by)})
+    dom = max(layers, key=lambda l: l["ms"])
+    sec = dom["ms"] / 1000.0
+    ai = dom["flops"] / max(dom["bytes"], 1)
+    ridge = tf32_peak * 1e12 / (hbm * 1e9)
+    if dom["kernel"] in ("pw", "igemm") and dom["math"] == "tf32" and ai >= ridge:
+        roof = {"bound": "tensor", "achieved": dom["flops"] / sec / 1e12, "peak": tf32_peak, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": dom["bytes"] / sec / 1e9, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = None
+    roof["kernel"] = f"{dom['op']} ({dom['kernel']}/{dom['math']})"
+    roof["share"] = dom["ms"] / float(per_op.sum())
+    roof["peak_src"] = pk["src"] + (" (TF32 = bf16/2)" if roof["bound"] == "tensor" else "")
+    for k in ("achieved", "peak", "frac", "share"):
+        roof[k] = round(roof[k], 4)
+
+    conv_flops = sum(l["flops"] for l in layers)
+    conv_ms = float(per_op.sum())
+    dtype = "tf32" if any(l["math"] == "tf32" for l in layers) else "f32"
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": {"workload": "MNv4-style seg net 160x288, 256 frames per GPU (BASELINE config 4)",
+                   "global_batch": n * world, "per_gpu_batch": n, "h": H, "w": W, "parallelism": f"dp{world}",
+                   "math": args.math, "l2": "inputs larger than L2 (141 MB frames, ~2.5 GB activations per step)",
+                   "conv_mflop_per_frame": round(conv_flops / n / 1e6, 2)},
+        "conv_tflops": round(conv_flops * world / (total_ms / args.steps / 1000.0) / 1e12, 3),
+        "roofline": roof,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(x_host.numel() * 4),
+                "d2h_bytes_per_step": int(out_host.numel() * 4)},
+        "graph_replay_value": round(graph_value, 2) if isinstance(graph_value, float) else graph_value,
+        "gpu_launches": len(ops) * args.steps,
+        "clocks": sampler.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        frames = 128
+        v, dt = cpu_baseline(frames, threads)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": f"{frames} frames of the same workload, one frame per core, "
+                                          f"{dt:.1f} s on {cpu_model_name()}"}
+    if args.layers:
+        for l in layers:
+            t = l["ms"] / 1000
+            print(f"{l['op']:14s} {l['kernel']:7s} {l['math']:11s} {l['ms']*1000:9.1f} us "
+                  f"{l['bytes']/t/1e9 if t else 0:8.1f} GB/s {l['flops']/t/1e12 if t else 0:8.2f} TF/s",
+                  file=sys.stderr)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
