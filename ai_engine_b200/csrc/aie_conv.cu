@@ -109,7 +109,6 @@ static bool tf32_eligible(const aie_plan &p, const char **why)
     if (!tc_available()) { *why = "tensor-core kernel not built"; return false; }
     if (d.groups != 1) { *why = "depthwise"; return false; }
     if (d.cin % 4 || p.x_stride % 4 || p.x_coff % 4) { *why = "input channels/stride not a multiple of 4"; return false; }
-    if (d.dil != 1 && !(d.kh == 1 && d.kw == 1)) { *why = "dilation"; return false; }
     if (d.kh != 1 || d.kw != 1 || d.sh != 1 || d.sw != 1 || d.pad[0] || d.pad[1] || d.pad[2] || d.pad[3]) {
         if (!tc_igemm_supported(d.kh, d.kw, d.sh, d.sw, p.ow)) { *why = "conv geometry"; return false; }
     }

@@ -1,28 +1,696 @@
-// tcgen05 / TMEM TF32 GEMM for the 1x1 and implicit-GEMM convs.
-// (Geometry planner and launcher; the kernel body is filled in by the
-// tensor-core implementation.)
+// tcgen05 / TMEM TF32 implicit-GEMM conv for sm_100a (1x1 and k x k).
+//
+//   C[M, N] = sum over (tap, k-block) of A_tap[M, 32] * B_tap[32, N]
+//
+// M = output pixels, N = cout, K = taps x cin.  Persistent, warp-specialised:
+//   warp 0       TMA producer (one elected lane)
+//   warp 1       TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5   epilogue: tcgen05.ld -> bias -> act -> +residual -> global
+// Accumulators are double-buffered in TMEM so the epilogue of one tile
+// overlaps the mainloop of the next.  Operands are fp32 in HBM and are read
+// by the tensor core as TF32; both are K-major with the 128-byte swizzle.
+//
+// A operand (activations, NHWC):
+//   1x1 conv : 2-D tensor map (cin, M), box (32, 128)
+//   k x k    : 4-D tensor map (cin, iw, ih, n) with element strides
+//              (1, sw, sh, 1), box (32, bw*sw, bh*sh, 1): one M tile is a
+//              bh x bw block of output pixels of one frame, and each tap is
+//              the same box shifted by (kx*dil - pl, ky*dil - pt).  TMA's
+//              out-of-bounds zero fill is the convolution's zero padding.
+// B operand (weights [tap][cout][cin_pad]): 3-D map, box (32, bn, 1).
+//
+// Split-K (small M, deep K): units = m_tiles x n_tiles x split.  Each unit
+// writes its raw partial tile to the workspace; the last unit of a tile
+// (atomic ticket) sums the partials in split order -- deterministic -- and
+// runs the epilogue.
+//
+// Every wait on an mbarrier is bounded (1 s of %globaltimer); on expiry the
+// CTA records an error code in g_aie_error, stops issuing work, waits
+// (bounded) for its own copies in flight, frees its TMEM and exits.
 #pragma once
+
+#include <cuda.h>
 
 #include "k_simt.cuh"
 
 namespace aie {
 
+constexpr int kTcThreads = 192;
+constexpr int kTcBM = 128;
+constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
+constexpr uint32_t kTcABytes = kTcBM * kTcBK * 4;  // 16 KB
+constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s
+
 struct TcGeom {
-    uint32_t bm, bn, split;
+    uint32_t bm, bn;
+    uint32_t igemm;            // 0: 2-D A map (1x1), 1: 4-D A map (k x k)
+    uint32_t bw, bh;           // M tile box (k x k)
+    uint32_t tiles_x, tiles_y; // output-pixel tiles per frame (k x k)
+    uint32_t m_tiles, n_tiles, split, k_iters, k_per_split, kblocks, taps;
+    uint32_t stages, tmem_cols;
+    uint64_t units, grid;
     uint64_t workspace_bytes;
-    uint64_t grid;
+    uint32_t smem_bytes;
+    uint32_t b_bytes;
 };
 
-static inline bool tc_available() { return false; }
+struct TcArgs {
+    ConvArgs c;
+    uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
+    uint32_t stages, tmem_cols, b_bytes, igemm;
+    uint64_t units;
+    float *ws;            // split-K partials [tile][split][128][bn]
+    uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
+};
 
-static inline bool tc_igemm_supported(uint32_t, uint32_t, uint32_t, uint32_t, uint32_t) { return false; }
+// --------------------------------------------------------------- PTX ---
 
-static inline int tc_plan(uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
-                          uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, TcGeom *)
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long gtime()
 {
-    return -1;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
-static inline int tc_launch(const TcGeom &, const ConvArgs &, void *, cudaStream_t, char *, size_t) { return -3; }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: true when the phase completed, false after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtime();
+    while (true) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (gtime() - t0 > kWaitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1, int c2)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1, int c2,
+                                            int c3)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 B apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);       // start address
+    d |= (uint64_t)1 << 16;                        // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset
+    d |= (uint64_t)1 << 46;                        // version
+    d |= (uint64_t)2 << 61;                        // layout: SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n)
+{
+    return (1u << 4)            // D format f32
+           | (2u << 7)          // A format tf32
+           | (2u << 10)         // B format tf32
+           | ((n >> 3) << 17)   // N / 8
+           | ((m >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
+{
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// --------------------------------------------------------------- kernel ---
+
+struct TcShared {
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+
+// Output rows of unit `u`: decode (m tile, n tile, split).
+struct TcUnit {
+    uint32_t mt, nt, s;
+};
+
+__device__ __forceinline__ TcUnit tc_unit(const TcArgs &a, uint64_t u)
+{
+    TcUnit t;
+    t.nt = (uint32_t)(u % a.n_tiles);
+    const uint64_t r = u / a.n_tiles;
+    t.s = (uint32_t)(r % a.split);
+    t.mt = (uint32_t)(r / a.split);
+    return t;
+}
+
+// Output pixel of accumulator row `row` of M tile `mt`, or -1 if outside.
+__device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, uint32_t row)
+{
+    if (!a.igemm) {
+        const long long m = (long long)mt * kTcBM + row;
+        return m < a.c.M ? m : -1;
+    }
+    const uint32_t per_img = a.tiles_x * a.tiles_y;
+    const uint32_t img = mt / per_img, rem = mt - img * per_img;
+    const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
+    const int oy = (int)(ty * a.bh + row / a.bw), ox = (int)(tx * a.bw + row % a.bw);
+    if (oy >= a.c.oh || ox >= a.c.ow) return -1;
+    return ((long long)img * a.c.oh + oy) * a.c.ow + ox;
+}
+
+__device__ __forceinline__ void tc_store16(const TcArgs &a, long long m, int col0, const float (&acc)[16])
+{
+    const ConvArgs &c = a.c;
+    float *yr = c.y + m * c.y_stride + c.y_coff;
+    const float *rr = c.res ? c.res + m * c.r_stride + c.r_coff : nullptr;
+    if (c.vec_y && col0 + 16 <= c.cout) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int col = col0 + 4 * q;
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(c.bias + col));
+            float v0 = act_apply(c.act, acc[4 * q + 0] + b.x);
+            float v1 = act_apply(c.act, acc[4 * q + 1] + b.y);
+            float v2 = act_apply(c.act, acc[4 * q + 2] + b.z);
+            float v3 = act_apply(c.act, acc[4 * q + 3] + b.w);
+            if (rr) {
+                const float4 r = __ldg(reinterpret_cast<const float4 *>(rr + col));
+                v0 += r.x; v1 += r.y; v2 += r.z; v3 += r.w;
+            }
+            *reinterpret_cast<float4 *>(yr + col) = make_float4(v0, v1, v2, v3);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int col = col0 + j;
+            if (col < c.cout) {
+                float v = act_apply(c.act, acc[j] + c.bias[col]);
+                if (rr) v += rr[col];
+                yr[col] = v;
+            } else if (col < c.y_pad_to) {
+                yr[col] = 0.0f;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-align the stage buffers (128-byte swizzle atoms)
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t stage_bytes = kTcABytes + a.b_bytes;
+    TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.stages * stage_bytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < a.stages; s++) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&sh.acc_full[b], 1);
+            mbar_init(&sh.acc_empty[b], 4);
+        }
+        sh.abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                     "r"(a.tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sh.tmem_base;
+    volatile uint32_t *abort_flag = &sh.abort;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+                const TcUnit t = tc_unit(a, u);
+                const uint32_t k0 = t.s * a.k_per_split;
+                const uint32_t k1 = min(a.k_iters, k0 + a.k_per_split);
+                int img = 0, ybase = 0, xbase = 0;
+                if (a.igemm) {
+                    const uint32_t per_img = a.tiles_x * a.tiles_y;
+                    img = (int)(t.mt / per_img);
+                    const uint32_t rem = t.mt - img * per_img;
+                    const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
+                    ybase = (int)(ty * a.bh) * a.c.sh - a.c.pt;
+                    xbase = (int)(tx * a.bw) * a.c.sw - a.c.pl;
+                }
+                for (uint32_t k = k0; k < k1; k++, it++) {
+                    const uint32_t s = it % a.stages, ph = (it / a.stages) & 1;
+                    if (*abort_flag || !mbar_wait(&sh.empty[s], ph ^ 1)) {
+                        report_error(0x01000001);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + s * stage_bytes;
+                    uint8_t *sb = sa + kTcABytes;
+                    mbar_expect_tx(&sh.full[s], kTcABytes + a.b_bytes);
+                    const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
+                    const int kc = (int)(kb * kTcBK);
+                    if (a.igemm) {
+                        const int ky = (int)(tap / a.c.kw), kx = (int)(tap - ky * a.c.kw);
+                        tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + kx * a.c.dil, ybase + ky * a.c.dil, img);
+                    } else {
+                        tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
+                    }
+                    tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
+                }
+            }
+            // drain: wait (bounded) until the copies this thread issued have landed
+            if (it > 0) {
+                const uint32_t last = it - 1;
+                mbar_wait(&sh.full[last % a.stages], (last / a.stages) & 1);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_tf32(kTcBM, a.bn);
+            uint32_t it = 0, acc_it = 0;
+            bool ok = true;
+            for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x, acc_it++) {
+                const TcUnit t = tc_unit(a, u);
+                const uint32_t k0 = t.s * a.k_per_split;
+                const uint32_t k1 = min(a.k_iters, k0 + a.k_per_split);
+                const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+                if (*abort_flag || !mbar_wait(&sh.acc_empty[ab], aph ^ 1)) {
+                    report_error(0x01000002);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + ab * a.bn;
+                for (uint32_t k = k0; k < k1; k++, it++) {
+                    const uint32_t s = it % a.stages, ph = (it / a.stages) & 1;
+                    if (*abort_flag || !mbar_wait(&sh.full[s], ph)) {
+                        report_error(0x01000003);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * stage_bytes);
+                    const uint32_t sb = sa + kTcABytes;
+                    const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kTcBK / 8; kk++) {
+                        // advance 8 tf32 = 32 bytes along K inside the swizzle row
+                        mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                 (k > k0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&sh.empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&sh.acc_full[ab]);
+            }
+            // drain: wait (bounded) for the MMAs this thread issued before the
+            // TMEM they write can be freed
+            if (it > 0) {
+                const uint32_t last = it - 1;
+                mbar_wait(&sh.empty[last % a.stages], (last / a.stages) & 1);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..5)
+        const uint32_t quad = warp & 3;           // TMEM lane quadrant this warp may access
+        const uint32_t row = quad * 32 + lane;    // accumulator row = TMEM lane
+        uint32_t acc_it = 0;
+        for (uint64_t u = blockIdx.x; u < a.units; u += gridDim.x, acc_it++) {
+            const TcUnit t = tc_unit(a, u);
+            const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+            if (*abort_flag || !mbar_wait(&sh.acc_full[ab], aph)) {
+                report_error(0x01000004);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const long long m = tc_row_pixel(a, t.mt, row);
+            const int ncol = (int)min(a.bn, (uint32_t)a.c.y_pad_to - t.nt * a.bn);
+            const uint32_t tbase = tmem + ((quad * 32) << 16) + ab * a.bn;
+            const uint64_t tile = (uint64_t)t.mt * a.n_tiles + t.nt;
+            if (a.split == 1) {
+                for (int c0 = 0; c0 < ncol; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(tbase + c0, v);
+                    if (m >= 0) tc_store16(a, m, (int)(t.nt * a.bn) + c0, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.acc_empty[ab]);
+            } else {
+                // raw partial -> workspace, release the accumulator, then take
+                // this warp's ticket for its 32 rows (no cross-warp barrier:
+                // every warp finishes on its own even if another gave up)
+                float *wrow = a.ws + ((tile * a.split + t.s) * kTcBM + row) * a.bn;
+                for (int c0 = 0; c0 < (int)a.bn; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(tbase + c0, v);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        *reinterpret_cast<float4 *>(wrow + c0 + 4 * q) =
+                            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.acc_empty[ab]);
+                __threadfence();
+                __syncwarp();
+                uint32_t *ticket = a.tickets + tile * 4 + quad;
+                uint32_t last = 0;
+                if (lane == 0) last = atomicAdd(ticket, 1u) == a.split - 1 ? 1u : 0u;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    if (m >= 0) {
+                        const float *base = a.ws + (tile * a.split * kTcBM + row) * a.bn;
+                        for (int c0 = 0; c0 < ncol; c0 += 16) {
+                            float v[16];
+#pragma unroll
+                            for (int j = 0; j < 16; j++) v[j] = 0.0f;
+                            for (uint32_t s = 0; s < a.split; s++) {
+                                const float *p = base + (uint64_t)s * kTcBM * a.bn + c0;
+#pragma unroll
+                                for (int q = 0; q < 4; q++) {
+                                    const float4 x = __ldcg(reinterpret_cast<const float4 *>(p + 4 * q));
+                                    v[4 * q] += x.x; v[4 * q + 1] += x.y; v[4 * q + 2] += x.z; v[4 * q + 3] += x.w;
+                                }
+                            }
+                            tc_store16(a, m, (int)(t.nt * a.bn) + c0, v);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) *ticket = 0;  // reusable by the next launch
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols));
+    }
+}
+
+// --------------------------------------------------------------- host ---
+
+static inline uint32_t tc_pow2_ceil(uint32_t v)
+{
+    uint32_t p = 32;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+static inline bool tc_available() { return true; }
+
+// k x k geometries the tensor-core path takes: strides 1-2 (the TMA box
+// spans bw*sw <= 256 elements).
+static inline bool tc_igemm_supported(uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ow)
+{
+    (void)kh; (void)kw; (void)ow;
+    return sh >= 1 && sh <= 2 && sw >= 1 && sw <= 2;
+}
+
+// Plan the tensor-core launch.  Returns 0 or a negative code.
+static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, uint32_t cout, uint32_t kh, uint32_t kw,
+                          uint32_t sh, uint32_t sw, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
+                          uint32_t split_req, TcGeom *g)
+{
+    (void)ih; (void)iw; (void)pt; (void)pl;
+    *g = TcGeom{};
+    g->bm = kTcBM;
+    const bool pw = kh == 1 && kw == 1 && sh == 1 && sw == 1;
+    g->igemm = pw ? 0 : 1;
+    g->taps = kh * kw;
+    g->kblocks = (cin + kTcBK - 1) / kTcBK;
+    g->k_iters = g->taps * g->kblocks;
+    // N tile: fewest tiles of <= 256 columns, each a multiple of 16
+    const uint32_t nt = (cout + 255) / 256;
+    g->bn = ((cout + nt - 1) / nt + 15) / 16 * 16;
+    g->n_tiles = (cout + g->bn - 1) / g->bn;
+    if (g->igemm) {
+        // M tile = bh x bw output pixels of one frame, bh*bw = 128; pick the
+        // shape that wastes the fewest rows
+        double best = 1e30;
+        for (uint32_t bw = 1; bw <= 128; bw <<= 1) {
+            const uint32_t bh = 128 / bw;
+            if (bw * sw > 256 || bh * sh > 256) continue;
+            const double cover = (double)((ow + bw - 1) / bw * bw) * ((oh + bh - 1) / bh * bh);
+            if (cover < best) {
+                best = cover;
+                g->bw = bw;
+                g->bh = bh;
+            }
+        }
+        g->tiles_x = (ow + g->bw - 1) / g->bw;
+        g->tiles_y = (oh + g->bh - 1) / g->bh;
+        g->m_tiles = n * g->tiles_x * g->tiles_y;
+    } else {
+        const uint64_t M = (uint64_t)n * oh * ow;
+        g->m_tiles = (uint32_t)((M + kTcBM - 1) / kTcBM);
+    }
+    const uint64_t tiles = (uint64_t)g->m_tiles * g->n_tiles;
+    uint32_t split = 1;
+    if (split_req == 0) {
+        if (tiles < 148 && g->k_iters >= 8) {
+            split = (uint32_t)std::min<uint64_t>(16, std::max<uint64_t>(1, 148 / tiles));
+            split = std::min(split, g->k_iters / 4 ? g->k_iters / 4 : 1u);
+        }
+    } else {
+        split = std::min(split_req, g->k_iters);
+    }
+    if (split < 1) split = 1;
+    g->k_per_split = (g->k_iters + split - 1) / split;
+    g->split = (g->k_iters + g->k_per_split - 1) / g->k_per_split;  // no empty splits
+    g->units = tiles * g->split;
+    g->b_bytes = g->bn * kTcBK * 4;
+    const uint32_t stage = kTcABytes + g->b_bytes;
+    const uint32_t budget = 200 * 1024;
+    g->stages = std::min<uint32_t>(8, budget / stage);
+    if (g->stages < 2) return -2;
+    g->tmem_cols = tc_pow2_ceil(2 * g->bn);
+    if (g->tmem_cols > 512) return -3;
+    g->smem_bytes = g->stages * stage + 1024 /*align slack*/ + (uint32_t)sizeof(TcShared);
+    g->grid = std::min<uint64_t>(g->units, 148);
+    if (g->split > 1) {
+        const uint64_t ws = tiles * g->split * kTcBM * g->bn * 4;
+        g->workspace_bytes = (ws + 255) / 256 * 256 + (tiles * 16 + 255) / 256 * 256;
+    }
+    return 0;
+}
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled tc_encoder()
+{
+    static PFN_encodeTiled fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_encodeTiled)p;
+    }
+    return fn;
+}
+
+static int tc_sm_count()
+{
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    }
+    return n;
+}
+
+static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace, cudaStream_t stream, char *err,
+                            size_t errlen)
+{
+    PFN_encodeTiled enc = tc_encoder();
+    if (!enc) {
+        snprintf(err, errlen, "cuTensorMapEncodeTiled unavailable");
+        return -4;
+    }
+    const uintptr_t abase = (uintptr_t)(c.x + c.x_coff);
+    if (abase % 16 || (c.x_stride * 4) % 16 || (uintptr_t)c.w % 16) {
+        snprintf(err, errlen, "TMA operands must be 16-byte aligned (input + channel offset, pixel stride, weights)");
+        return -5;
+    }
+    CUtensorMap tmA, tmB;
+    CUresult r;
+    if (g.igemm) {
+        const cuuint64_t dims[4] = {(cuuint64_t)c.cin, (cuuint64_t)c.iw, (cuuint64_t)c.ih, (cuuint64_t)c.n};
+        const cuuint64_t strides[3] = {(cuuint64_t)c.x_stride * 4, (cuuint64_t)c.x_stride * 4 * c.iw,
+                                       (cuuint64_t)c.x_stride * 4 * c.iw * c.ih};
+        const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.bw * (cuuint32_t)c.sw, g.bh * (cuuint32_t)c.sh, 1};
+        const cuuint32_t estr[4] = {1, (cuuint32_t)c.sw, (cuuint32_t)c.sh, 1};
+        r = enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)abase, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[2] = {(cuuint64_t)c.cin, (cuuint64_t)c.M};
+        const cuuint64_t strides[1] = {(cuuint64_t)c.x_stride * 4};
+        const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+        const cuuint32_t estr[2] = {1, 1};
+        r = enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)abase, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) {
+        snprintf(err, errlen, "cuTensorMapEncodeTiled(A) failed: %d", (int)r);
+        return -4;
+    }
+    {
+        const uint32_t cin_pad = (c.cin + 3) / 4 * 4;
+        const cuuint64_t dims[3] = {(cuuint64_t)cin_pad, (cuuint64_t)c.cout, (cuuint64_t)(c.kh * c.kw)};
+        const cuuint64_t strides[2] = {(cuuint64_t)cin_pad * 4, (cuuint64_t)cin_pad * 4 * c.cout};
+        const cuuint32_t box[3] = {(cuuint32_t)kTcBK, g.bn, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        r = enc(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)c.w, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            snprintf(err, errlen, "cuTensorMapEncodeTiled(B) failed: %d", (int)r);
+            return -4;
+        }
+    }
+    TcArgs a;
+    a.c = c;
+    a.bn = g.bn; a.bw = g.bw; a.bh = g.bh; a.tiles_x = g.tiles_x; a.tiles_y = g.tiles_y;
+    a.m_tiles = g.m_tiles; a.n_tiles = g.n_tiles; a.split = g.split; a.k_iters = g.k_iters;
+    a.k_per_split = g.k_per_split; a.kblocks = g.kblocks; a.stages = g.stages; a.tmem_cols = g.tmem_cols;
+    a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
+    a.ws = nullptr;
+    a.tickets = nullptr;
+    if (g.split > 1) {
+        if (!workspace || (uintptr_t)workspace % 256) {
+            snprintf(err, errlen, "split-K workspace missing or not 256-byte aligned");
+            return -2;
+        }
+        const uint64_t tiles = (uint64_t)g.m_tiles * g.n_tiles;
+        const uint64_t ws = (tiles * g.split * kTcBM * g.bn * 4 + 255) / 256 * 256;
+        a.ws = (float *)workspace;
+        a.tickets = (uint32_t *)((uint8_t *)workspace + ws);
+        cudaError_t e = cudaMemsetAsync(a.tickets, 0, tiles * 16, stream);
+        if (e != cudaSuccess) {
+            snprintf(err, errlen, "ticket reset: %s", cudaGetErrorString(e));
+            return -4;
+        }
+    }
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(tc_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        attr_set = true;
+    }
+    const unsigned grid = (unsigned)std::min<uint64_t>(g.units, (uint64_t)tc_sm_count());
+    tc_conv_kernel<<<grid, kTcThreads, g.smem_bytes, stream>>>(tmA, tmB, a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        snprintf(err, errlen, "tc_conv_kernel launch: %s", cudaGetErrorString(e));
+        return -4;
+    }
+    return 0;
+}
 
 }  // namespace aie
