@@ -139,6 +139,10 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     p->oh = (uint32_t)(hh / d.sh + 1);
     p->ow = (uint32_t)(ww / d.sw + 1);
     p->M = (long long)d.n * p->oh * p->ow;
+    if (p->M >= (1ll << 31) || (long long)d.n * d.ih * d.iw >= (1ll << 31)) {
+        delete p;
+        return fail(AIE_E_UNSUPPORTED, "more than 2^31 pixels in one call; split the batch");
+    }
     const bool c4 = d.layout == AIE_LAYOUT_NHWC_C4;
     p->x_stride = d.in_stride ? d.in_stride : (c4 ? rup(d.cin, 4) : d.cin);
     p->x_coff = d.in_coff;
@@ -204,7 +208,7 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
         p->cin_pad = (int)rup(d.cin, 4);
         p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
         int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.pad[0], d.pad[1], p->oh, p->ow,
-                         d.split_k, &p->tc);
+                         d.split_k, d.has_res != 0, &p->tc);
         if (rc) {
             delete p;
             return fail(AIE_E_UNSUPPORTED, "tensor-core geometry rejected (%d)", rc);

@@ -150,10 +150,9 @@ __global__ void __launch_bounds__(kFfmaThreads) igemm_ffma_kernel(const ConvArgs
         if (m >= a.M) break;
         float *yr = a.y + m * a.y_stride + a.y_coff;
         const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff : nullptr;
+        float v[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
+        epi_act_n<kStrict, 4>(a.act, v, col0, a.cout);
         if (a.vec_y && col0 + 4 <= a.cout) {
-            float v[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) v[j] = epi_act<kStrict>(a.act, acc[i][j], col0 + j, a.cout);
             if (rr) {
                 const float4 r = __ldg(reinterpret_cast<const float4 *>(rr + col0));
                 v[0] = add_res<kStrict>(v[0], r.x); v[1] = add_res<kStrict>(v[1], r.y);
@@ -164,13 +163,8 @@ __global__ void __launch_bounds__(kFfmaThreads) igemm_ffma_kernel(const ConvArgs
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const int col = col0 + j;
-                if (col < a.cout) {
-                    float v = epi_act<kStrict>(a.act, acc[i][j], col, a.cout);
-                    if (rr) v = add_res<kStrict>(v, rr[col]);
-                    yr[col] = v;
-                } else if (col < a.y_pad_to) {
-                    yr[col] = 0.0f;
-                }
+                if (col < a.cout) yr[col] = rr ? add_res<kStrict>(v[j], rr[col]) : v[j];
+                else if (col < a.y_pad_to) yr[col] = 0.0f;
             }
         }
     }
@@ -222,17 +216,18 @@ __global__ void __launch_bounds__(256) pw_dot_kernel(const ConvArgs a)
     }
     float *yr = a.y + m * a.y_stride + a.y_coff;
     const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff : nullptr;
+    float v[4];
 #pragma unroll
     for (int o = 0; o < 4; o++) {
-        if (o < a.cout) {
-            const float s = __fadd_rn(__fadd_rn(lane[o][0], lane[o][1]), __fadd_rn(lane[o][2], lane[o][3]));
-            // scalar activation form on every channel: ch=0 of c=0 selects it
-            float v = epi_act<kStrict>(a.act, __fadd_rn(s, a.bias[o]), 0, 0);
-            if (rr) v = add_res<kStrict>(v, rr[o]);
-            yr[o] = v;
-        } else if (o < a.y_pad_to) {
-            yr[o] = 0.0f;
-        }
+        const float s = __fadd_rn(__fadd_rn(lane[o][0], lane[o][1]), __fadd_rn(lane[o][2], lane[o][3]));
+        v[o] = __fadd_rn(s, o < a.cout ? a.bias[o] : 0.0f);
+    }
+    // scalar activation form on every channel (pw_dot.rs:57): channel 0 of c=0 selects it
+    epi_act_n<kStrict, 4>(a.act, v, 0, 0);
+#pragma unroll
+    for (int o = 0; o < 4; o++) {
+        if (o < a.cout) yr[o] = rr ? add_res<kStrict>(v[o], rr[o]) : v[o];
+        else if (o < a.y_pad_to) yr[o] = 0.0f;
     }
 }
 
@@ -285,10 +280,9 @@ __global__ void __launch_bounds__(256) dw_kernel(const ConvArgs a)
     }
     float *yr = a.y + m * a.y_stride + a.y_coff + c0;
     const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff + c0 : nullptr;
+    float v[4] = {acc[0], acc[1], acc[2], acc[3]};
+    epi_act_n<kStrict, 4>(a.act, v, c0, a.cout);
     if (a.vec_y && c0 + 4 <= a.cout) {
-        float v[4];
-#pragma unroll
-        for (int l = 0; l < 4; l++) v[l] = epi_act<kStrict>(a.act, acc[l], c0 + l, a.cout);
         if (rr) {
             const float4 r = __ldg(reinterpret_cast<const float4 *>(rr));
             v[0] = add_res<true>(v[0], r.x); v[1] = add_res<true>(v[1], r.y);
@@ -299,13 +293,8 @@ __global__ void __launch_bounds__(256) dw_kernel(const ConvArgs a)
 #pragma unroll
         for (int l = 0; l < 4; l++) {
             const int ch = c0 + l;
-            if (ch < a.cout) {
-                float v = epi_act<kStrict>(a.act, acc[l], ch, a.cout);
-                if (rr) v = add_res<true>(v, rr[l]);
-                yr[l] = v;
-            } else if (ch < a.y_pad_to) {
-                yr[l] = 0.0f;
-            }
+            if (ch < a.cout) yr[l] = rr ? add_res<true>(v[l], rr[l]) : v[l];
+            else if (ch < a.y_pad_to) yr[l] = 0.0f;
         }
     }
 }
@@ -358,15 +347,22 @@ __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a
     float *yr = a.y + px * a.c + c0;
     const float *ar = a.add ? a.add + px * a.c + c0 : nullptr;
     const int nl = min(4, a.c - c0);
+    float v[4];
 #pragma unroll
     for (int l = 0; l < 4; l++) {
-        if (l >= nl) break;
-        const float top = __fadd_rn(__fmul_rn(__ldg(p00 + l), tx1), __fmul_rn(__ldg(p01 + l), tx));
-        const float bot = __fadd_rn(__fmul_rn(__ldg(p10 + l), tx1), __fmul_rn(__ldg(p11 + l), tx));
-        float v = __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
-        if (ar) v = __fadd_rn(v, __ldg(ar + l));
-        yr[l] = act_apply_strict(a.act, v, c0 + l, a.c);
+        if (l < nl) {
+            const float top = __fadd_rn(__fmul_rn(__ldg(p00 + l), tx1), __fmul_rn(__ldg(p01 + l), tx));
+            const float bot = __fadd_rn(__fmul_rn(__ldg(p10 + l), tx1), __fmul_rn(__ldg(p11 + l), tx));
+            v[l] = __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
+            if (ar) v[l] = __fadd_rn(v[l], __ldg(ar + l));
+        } else {
+            v[l] = 0.0f;
+        }
     }
+    act_apply_strict_n<4>(a.act, v, c0, a.c);
+#pragma unroll
+    for (int l = 0; l < 4; l++)
+        if (l < nl) yr[l] = v[l];
 }
 
 }  // namespace aie

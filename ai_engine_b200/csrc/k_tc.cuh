@@ -3,9 +3,12 @@
 //   C[M, N] = sum over (tap, k-block) of A_tap[M, 32] * B_tap[32, N]
 //
 // M = output pixels, N = cout, K = taps x cin.  Persistent, warp-specialised:
-//   warp 0       TMA producer (one elected lane)
-//   warp 1       TMEM allocator + MMA issuer (one elected lane)
-//   warps 2..5   epilogue: tcgen05.ld -> bias -> act -> +residual -> global
+//   warp 0       TMEM allocator + MMA issuer (one elected lane)
+//   warps 1..4   epilogue: tcgen05.ld -> bias -> act, transposed through
+//                shared memory -> +residual -> coalesced row stores
+//   warps 5..7   TMA producers, one elected lane each, taking stages in turn
+//                (TMA issue rate is per issuing thread: one thread issuing
+//                16 KB boxes reaches ~3.5 TB/s on B200, four reach HBM speed)
 // Accumulators are double-buffered in TMEM so the epilogue of one tile
 // overlaps the mainloop of the next.  Operands are fp32 in HBM and are read
 // by the tensor core as TF32; both are K-major with the 128-byte swizzle.
@@ -31,11 +34,15 @@
 
 #include <cuda.h>
 
+#include <cstring>
+
 #include "k_simt.cuh"
 
 namespace aie {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcProducers = 3;                   // TMA issue is per-thread limited
+constexpr int kTcThreads = 32 * (5 + kTcProducers); // MMA, 4 epilogue, producers
+constexpr uint32_t kTcStageOut = 32 * 32 * 4;      // one 32x32 fp32 epilogue chunk per warp
 constexpr int kTcBM = 128;
 constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 4;  // 16 KB
@@ -52,6 +59,7 @@ struct TcGeom {
     uint64_t workspace_bytes;
     uint32_t smem_bytes;
     uint32_t b_bytes;
+    uint32_t out_off, shared_off;
 };
 
 struct TcArgs {
@@ -61,6 +69,7 @@ struct TcArgs {
     uint64_t units;
     float *ws;            // split-K partials [tile][split][128][bn]
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
+    uint32_t out_off, shared_off;  // shared-memory carve-up (bytes)
 };
 
 // --------------------------------------------------------------- PTX ---
@@ -240,38 +249,40 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
     return ((long long)img * a.c.oh + oy) * a.c.ow + ox;
 }
 
+// Direct-store epilogue for 16 columns of one output row (used when the
+// output view cannot be described to TMA).
 __device__ __forceinline__ void tc_store16(const TcArgs &a, long long m, int col0, const float (&acc)[16])
 {
     const ConvArgs &c = a.c;
     float *yr = c.y + m * c.y_stride + c.y_coff;
     const float *rr = c.res ? c.res + m * c.r_stride + c.r_coff : nullptr;
-    if (c.vec_y && col0 + 16 <= c.cout) {
+    float v[16];
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int col = col0 + 4 * q;
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(c.bias + col));
-            float v0 = act_apply(c.act, acc[4 * q + 0] + b.x);
-            float v1 = act_apply(c.act, acc[4 * q + 1] + b.y);
-            float v2 = act_apply(c.act, acc[4 * q + 2] + b.z);
-            float v3 = act_apply(c.act, acc[4 * q + 3] + b.w);
-            if (rr) {
-                const float4 r = __ldg(reinterpret_cast<const float4 *>(rr + col));
-                v0 += r.x; v1 += r.y; v2 += r.z; v3 += r.w;
-            }
-            *reinterpret_cast<float4 *>(yr + col) = make_float4(v0, v1, v2, v3);
-        }
-    } else {
+    for (int j = 0; j < 16; j++) v[j] = acc[j] + (col0 + j < c.cout ? c.bias[col0 + j] : 0.0f);
+    act_apply_n<16>(c.act, v);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const int col = col0 + j;
-            if (col < c.cout) {
-                float v = act_apply(c.act, acc[j] + c.bias[col]);
-                if (rr) v += rr[col];
-                yr[col] = v;
-            } else if (col < c.y_pad_to) {
-                yr[col] = 0.0f;
-            }
-        }
+    for (int j = 0; j < 16; j++) {
+        const int col = col0 + j;
+        if (col < c.cout) yr[col] = rr ? v[j] + rr[col] : v[j];
+        else if (col < c.y_pad_to) yr[col] = 0.0f;
+    }
+}
+
+// 32 accumulator columns of this lane's row.  Columns past `bn` of the tile
+// are not read (they may lie outside the TMEM allocation).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int remaining, float (&v)[32])
+{
+    float lo[16], hi[16];
+    tmem_ld16(taddr, lo);
+    if (remaining > 16) tmem_ld16(taddr + 16, hi);
+    else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) hi[i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        v[i] = lo[i];
+        v[16 + i] = hi[i];
     }
 }
 
@@ -282,7 +293,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // 1024-align the stage buffers (128-byte swizzle atoms)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t stage_bytes = kTcABytes + a.b_bytes;
-    TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.stages * stage_bytes);
+    TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.shared_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -296,10 +307,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         sh.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x == 32) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
     }
-    if (warp == 1) {
+    if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
                      "r"(a.tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -310,10 +323,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = sh.tmem_base;
     volatile uint32_t *abort_flag = &sh.abort;
 
-    if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+    if (warp >= 5) {
+        // ------------------------------------------------ TMA producers
+        const uint32_t pidx = (uint32_t)(warp - 5);
         if (lane == 0) {
-            uint32_t it = 0;
+            uint32_t it = 0, last_mine = 0xFFFFFFFFu;
             bool ok = true;
             for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
                 const TcUnit t = tc_unit(a, u);
@@ -329,6 +343,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     xbase = (int)(tx * a.bw) * a.c.sw - a.c.pl;
                 }
                 for (uint32_t k = k0; k < k1; k++, it++) {
+                    if (it % kTcProducers != pidx) continue;
                     const uint32_t s = it % a.stages, ph = (it / a.stages) & 1;
                     if (*abort_flag || !mbar_wait(&sh.empty[s], ph ^ 1)) {
                         report_error(0x01000001);
@@ -348,16 +363,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                     }
                     tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
+                    last_mine = it;
                 }
             }
             // drain: wait (bounded) until the copies this thread issued have landed
-            if (it > 0) {
-                const uint32_t last = it - 1;
-                mbar_wait(&sh.full[last % a.stages], (last / a.stages) & 1);
-            }
+            if (last_mine != 0xFFFFFFFFu)
+                mbar_wait(&sh.full[last_mine % a.stages], (last_mine / a.stages) & 1);
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == 0) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32(kTcBM, a.bn);
@@ -407,28 +421,99 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------ epilogue (warps 2..5)
-        const uint32_t quad = warp & 3;           // TMEM lane quadrant this warp may access
-        const uint32_t row = quad * 32 + lane;    // accumulator row = TMEM lane
+        // ------------------------------------------------ epilogue (warps 1..4)
+        const uint32_t ew = (uint32_t)(warp - 1);  // epilogue warp index: staging buffers, barriers
+        const uint32_t quad = warp & 3;            // TMEM lane quadrant this warp may access
+        const uint32_t row = quad * 32 + lane;     // accumulator row = TMEM lane
+        uint8_t *obuf = smem + a.out_off + ew * kTcStageOut;  // 32 x 32 fp32 staging
         uint32_t acc_it = 0;
+        const ConvArgs &c = a.c;
+        const int bias_len = (c.cout + 3) & ~3;
+
+        // bias -> act on this lane's row, staged through shared memory, then
+        // written back by the warp 8 lanes per 128-byte row segment so every
+        // store (and residual load) instruction covers 4 whole rows instead
+        // of 32 scattered 16-byte pieces; residual added after the activation
+        auto emit = [&](uint32_t mt, int col0, float (&v)[32]) {
+            const int seg = lane & 7;
+            const int col = col0 + seg * 4;
+            // the rows this lane writes, and their residual values, fetched
+            // first so the eight loads overlap each other and the math below
+            int mrow[8];  // output pixel of each row, -1 outside (M < 2^31, checked at plan time)
+            float4 rv[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                mrow[i] = (int)tc_row_pixel(a, mt, quad * 32 + i * 4 + (lane >> 3));
+                rv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c.res && mrow[i] >= 0) {
+                    const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
+                    if (c.vec_y && col + 4 <= c.cout) rv[i] = __ldg(reinterpret_cast<const float4 *>(rr));
+                    else {
+                        float t4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int l = 0; l < 4; l++)
+                            if (col + l < c.cout) t4[l] = __ldg(rr + l);
+                        rv[i] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                    }
+                }
+            }
+            if (col0 + 32 <= bias_len) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; q4++) {
+                    const float4 b = __ldg(reinterpret_cast<const float4 *>(c.bias + col0 + 4 * q4));
+                    v[4 * q4] += b.x; v[4 * q4 + 1] += b.y; v[4 * q4 + 2] += b.z; v[4 * q4 + 3] += b.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] += (col0 + j < c.cout) ? c.bias[col0 + j] : 0.0f;
+            }
+            act_apply_n<32>(c.act, v);
+            __syncwarp();  // previous chunk's readers are done with the buffer
+            uint8_t *st = obuf + lane * 128;
+#pragma unroll
+            for (int ch = 0; ch < 8; ch++)
+                *reinterpret_cast<float4 *>(st + ((ch ^ (lane & 7)) * 16)) =
+                    make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int r = i * 4 + (lane >> 3);
+                const long long m = mrow[i];
+                if (m < 0 || col >= c.y_pad_to) continue;  // (m < 0: row outside the output)
+                float4 x = *reinterpret_cast<const float4 *>(obuf + r * 128 + ((seg ^ (r & 7)) * 16));
+                x.x += rv[i].x; x.y += rv[i].y; x.z += rv[i].z; x.w += rv[i].w;  // residual after act
+                float *yr = c.y + m * c.y_stride + c.y_coff + col;
+                if (c.vec_y && col + 4 <= c.cout) {
+                    *reinterpret_cast<float4 *>(yr) = x;
+                } else {
+                    const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                    for (int l = 0; l < 4; l++) {
+                        if (col + l < c.cout) yr[l] = xs[l];
+                        else if (col + l < c.y_pad_to) yr[l] = 0.0f;
+                    }
+                }
+            }
+        };
+
         for (uint64_t u = blockIdx.x; u < a.units; u += gridDim.x, acc_it++) {
             const TcUnit t = tc_unit(a, u);
             const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+            const int ncol = (int)min(a.bn, (uint32_t)c.y_pad_to - t.nt * a.bn);
+            const int nbase = (int)(t.nt * a.bn);
+            const uint32_t tbase = tmem + ((quad * 32) << 16) + ab * a.bn;
+            const uint64_t tile = (uint64_t)t.mt * a.n_tiles + t.nt;
             if (*abort_flag || !mbar_wait(&sh.acc_full[ab], aph)) {
                 report_error(0x01000004);
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            const long long m = tc_row_pixel(a, t.mt, row);
-            const int ncol = (int)min(a.bn, (uint32_t)a.c.y_pad_to - t.nt * a.bn);
-            const uint32_t tbase = tmem + ((quad * 32) << 16) + ab * a.bn;
-            const uint64_t tile = (uint64_t)t.mt * a.n_tiles + t.nt;
             if (a.split == 1) {
-                for (int c0 = 0; c0 < ncol; c0 += 16) {
-                    float v[16];
-                    tmem_ld16(tbase + c0, v);
-                    if (m >= 0) tc_store16(a, m, (int)(t.nt * a.bn) + c0, v);
+                for (int c0 = 0; c0 < ncol; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(tbase + c0, (int)a.bn - c0, v);
+                    emit(t.mt, nbase + c0, v);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -457,22 +542,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
-                    if (m >= 0) {
-                        const float *base = a.ws + (tile * a.split * kTcBM + row) * a.bn;
-                        for (int c0 = 0; c0 < ncol; c0 += 16) {
-                            float v[16];
+                    const float *base = a.ws + (tile * a.split * kTcBM + row) * a.bn;
+                    for (int c0 = 0; c0 < ncol; c0 += 32) {
+                        float v[32];
 #pragma unroll
-                            for (int j = 0; j < 16; j++) v[j] = 0.0f;
-                            for (uint32_t s = 0; s < a.split; s++) {
-                                const float *p = base + (uint64_t)s * kTcBM * a.bn + c0;
+                        for (int j = 0; j < 32; j++) v[j] = 0.0f;
+                        for (uint32_t s = 0; s < a.split; s++) {
+                            const float *p = base + (uint64_t)s * kTcBM * a.bn + c0;
 #pragma unroll
-                                for (int q = 0; q < 4; q++) {
+                            for (int q = 0; q < 8; q++) {
+                                if (c0 + 4 * q < (int)a.bn) {
                                     const float4 x = __ldcg(reinterpret_cast<const float4 *>(p + 4 * q));
                                     v[4 * q] += x.x; v[4 * q + 1] += x.y; v[4 * q + 2] += x.z; v[4 * q + 3] += x.w;
                                 }
                             }
-                            tc_store16(a, m, (int)(t.nt * a.bn) + c0, v);
                         }
+                        emit(t.mt, nbase + c0, v);
                     }
                     __syncwarp();
                     if (lane == 0) *ticket = 0;  // reusable by the next launch
@@ -483,7 +568,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols));
     }
@@ -511,7 +596,7 @@ static inline bool tc_igemm_supported(uint32_t kh, uint32_t kw, uint32_t sh, uin
 // Plan the tensor-core launch.  Returns 0 or a negative code.
 static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, uint32_t cout, uint32_t kh, uint32_t kw,
                           uint32_t sh, uint32_t sw, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
-                          uint32_t split_req, TcGeom *g)
+                          uint32_t split_req, bool has_res, TcGeom *g)
 {
     (void)ih; (void)iw; (void)pt; (void)pl;
     *g = TcGeom{};
@@ -521,9 +606,10 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->taps = kh * kw;
     g->kblocks = (cin + kTcBK - 1) / kTcBK;
     g->k_iters = g->taps * g->kblocks;
-    // N tile: fewest tiles of <= 256 columns, each a multiple of 16
+    // N tile: fewest tiles of <= 256 columns, each a multiple of 32 so the
+    // epilogue's 32-column store boxes never reach into the next tile
     const uint32_t nt = (cout + 255) / 256;
-    g->bn = ((cout + nt - 1) / nt + 15) / 16 * 16;
+    g->bn = ((cout + nt - 1) / nt + 31) / 32 * 32;
     g->n_tiles = (cout + g->bn - 1) / g->bn;
     if (g->igemm) {
         // M tile = bh x bw output pixels of one frame, bh*bw = 128; pick the
@@ -562,12 +648,17 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->units = tiles * g->split;
     g->b_bytes = g->bn * kTcBK * 4;
     const uint32_t stage = kTcABytes + g->b_bytes;
-    const uint32_t budget = 200 * 1024;
-    g->stages = std::min<uint32_t>(8, budget / stage);
+    // shared memory: [stages][epilogue staging, 4 warps x 4 KB][barriers];
+    // the stage buffers are 1024-aligned
+    const uint32_t out_bytes = 4 * kTcStageOut;
+    const uint32_t limit = 227 * 1024 - 1024 /*align slack*/ - 256 /*barriers*/;
+    g->stages = std::min<uint32_t>(8, (limit - out_bytes) / stage);
     if (g->stages < 2) return -2;
+    g->out_off = g->stages * stage;
+    g->shared_off = g->out_off + out_bytes;
     g->tmem_cols = tc_pow2_ceil(2 * g->bn);
     if (g->tmem_cols > 512) return -3;
-    g->smem_bytes = g->stages * stage + 1024 /*align slack*/ + (uint32_t)sizeof(TcShared);
+    g->smem_bytes = g->shared_off + 1024 + (uint32_t)sizeof(TcShared);
     g->grid = std::min<uint64_t>(g->units, 148);
     if (g->split > 1) {
         const uint64_t ws = tiles * g->split * kTcBM * g->bn * 4;
@@ -661,6 +752,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.m_tiles = g.m_tiles; a.n_tiles = g.n_tiles; a.split = g.split; a.k_iters = g.k_iters;
     a.k_per_split = g.k_per_split; a.kblocks = g.kblocks; a.stages = g.stages; a.tmem_cols = g.tmem_cols;
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
+    a.out_off = g.out_off; a.shared_off = g.shared_off;
     a.ws = nullptr;
     a.tickets = nullptr;
     if (g.split > 1) {

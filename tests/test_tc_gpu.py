@@ -180,3 +180,31 @@ def test_splitk_is_deterministic_and_reusable(cuda_ok):
         assert torch.equal(plan(xd), first)
     from ai_engine_b200 import device_status
     assert device_status() == 0
+
+
+@pytest.mark.parametrize("coff", [4, 2])
+def test_tf32_output_view(cuda_ok, coff):
+    """Output written into a channel slice of a wider buffer: 16-byte aligned
+    slices take the TMA-store epilogue, unaligned ones the direct-store one;
+    both leave the other channels untouched."""
+    from ai_engine_b200 import View
+    op = Conv2d.same(16, 24, 3, 1, "relu")
+    x, wt, b, res = case_tensors(op, 2, 13, 21, 92, True)
+    want, scale = oracle_conv(op, x, wt, b, res)
+    big = torch.full((2, 13, 21, 32), 7.0, device="cuda")
+    plan = ConvPlan(op, 2, 13, 21, has_res=True, out_view=View(32, coff), math="tf32").load_weights(wt, b)
+    plan(torch.from_numpy(x).cuda(), torch.from_numpy(res).cuda(), out=big)
+    got = big.cpu().numpy()
+    assert normalised_error(got[..., coff:coff + 24], want, scale) <= TOL_TF32
+    assert (got[..., :coff] == 7).all() and (got[..., coff + 24:] == 7).all()
+
+
+@pytest.mark.parametrize("n,h,w,cin,cout", [(3, 10, 18, 64, 96), (2, 7, 9, 32, 200), (1, 40, 72, 128, 48)])
+def test_tf32_partial_tiles_residual(cuda_ok, n, h, w, cin, cout):
+    """Ragged M (pixels not a multiple of 128), ragged N tiles, residual."""
+    op = Conv2d.pointwise(cin, cout, "hardswish")
+    x, wt, b, res = case_tensors(op, n, h, w, 93 + cout, True)
+    check_tf32(op, x, wt, b, res)
+    op3 = Conv2d.same(cin, cout, 3, 2, "relu")
+    x, wt, b, res = case_tensors(op3, n, h, w, 94 + cout, True)
+    check_tf32(op3, x, wt, b, res)
