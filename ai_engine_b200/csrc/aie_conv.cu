@@ -64,6 +64,9 @@ struct aie_plan {
     uint64_t wbytes, bbytes, wsbytes;
     uint64_t flops, min_bytes, grid;
     TcGeom tc;         // tensor-core launch geometry (TF32 only)
+    bool stem;         // small-cin direct conv (FFMA), see stem_kernel
+    StemGeom sg;
+    uint32_t stem_smem;
 };
 
 static const int kMathStrict = AIE_MATH_FP32_STRICT;
@@ -221,6 +224,37 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     } else {
         p->wn = (int)cpad4;
         p->wbytes = (uint64_t)taps * d.cin * p->wn * 4;
+        // small-cin k x k convs (the stem) take the direct-conv kernel: the
+        // GEMM's K tiles would be mostly padding (cin=3 -> 3 of 16 lanes)
+        const uint32_t lpp = d.cout / 4;
+        if (p->kernel == AIE_KERNEL_IGEMM && d.cin <= 4 && d.kh == 3 && d.kw == 3 && d.cout % 4 == 0 &&
+            lpp >= 1 && lpp <= 32 && 32 % lpp == 0) {
+            p->stem = true;
+            int best = -1;
+            const int shapes[3][2] = {{8, 32}, {16, 16}, {32, 8}};
+            long long best_cover = 0;
+            for (int i = 0; i < 3; i++) {
+                const int th = shapes[i][0], tw = shapes[i][1];
+                const long long cover = (long long)((p->oh + th - 1) / th * th) * ((p->ow + tw - 1) / tw * tw);
+                if (best < 0 || cover < best_cover) { best = i; best_cover = cover; }
+            }
+            StemGeom &g = p->sg;
+            g.tile_h = shapes[best][0];
+            g.tile_w = shapes[best][1];
+            g.halo_h = (g.tile_h - 1) * d.sh + (d.kh - 1) * d.dil + 1;
+            g.halo_w = (g.tile_w - 1) * d.sw + (d.kw - 1) * d.dil + 1;
+            g.tiles_x = (p->ow + g.tile_w - 1) / g.tile_w;
+            g.tiles_y = (p->oh + g.tile_h - 1) / g.tile_h;
+            p->stem_smem = (uint32_t)(g.halo_h * g.halo_w * d.cin * 4);
+            if (p->stem_smem > 48 * 1024) p->stem = false;  // very large strides/dilations: GEMM path
+            if (p->stem) {
+                p->tile_m = g.tile_h * g.tile_w;
+                p->tile_n = d.cout;
+                p->grid = (uint64_t)d.n * g.tiles_x * g.tiles_y;
+            }
+        }
+    }
+    if (!p->stem && (p->kernel == AIE_KERNEL_IGEMM || p->kernel == AIE_KERNEL_PW) && p->math != AIE_MATH_TF32) {
         p->tile_m = kFfmaBM;
         p->tile_n = kFfmaBN;
         p->grid = (uint64_t)((p->M + kFfmaBM - 1) / kFfmaBM) * ((d.cout + kFfmaBN - 1) / kFfmaBN);
@@ -366,7 +400,26 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
     cudaStream_t s = (cudaStream_t)stream;
     const ConvArgs a = make_args(p, in, w, b, res, out);
     if (p->kernel == AIE_KERNEL_DW) {
-        if (p->strict) dw_kernel<true><<<(unsigned)p->grid, 256, 0, s>>>(a);
+        const aie_conv_desc &d = p->d;
+        const bool blocked = d.cout % 4 == 0 && a.vec_x && a.vec_y && a.x_coff % 4 == 0 && a.y_coff % 4 == 0 &&
+                             (!a.res || (a.r_stride % 4 == 0 && a.r_coff % 4 == 0)) && d.dil == 1 &&
+                             d.kh == d.kw && d.sh == d.sw && (d.kh == 3 || d.kh == 5) && (d.sh == 1 || d.sh == 2) &&
+                             (long long)d.n * p->oh * ((p->ow + 3) / 4) * (d.cout / 4) < (1ll << 31);
+        if (blocked) {
+            constexpr int PB = 4;
+            const int segs = (int)((p->ow + PB - 1) / PB), cg = (int)(d.cout / 4);
+            const long long threads = (long long)d.n * p->oh * segs * cg;
+            const unsigned grid = (unsigned)((threads + 255) / 256);
+#define AIE_DW(S_, K_, ST_) dw_block_kernel<S_, K_, ST_, PB><<<grid, 256, 0, s>>>(a, segs, cg)
+#define AIE_DW2(S_)                                            \
+    if (d.kh == 3 && d.sh == 1) AIE_DW(S_, 3, 1);              \
+    else if (d.kh == 3) AIE_DW(S_, 3, 2);                      \
+    else if (d.sh == 1) AIE_DW(S_, 5, 1);                      \
+    else AIE_DW(S_, 5, 2);
+            if (p->strict) { AIE_DW2(true) } else { AIE_DW2(false) }
+#undef AIE_DW2
+#undef AIE_DW
+        } else if (p->strict) dw_kernel<true><<<(unsigned)p->grid, 256, 0, s>>>(a);
         else dw_kernel<false><<<(unsigned)p->grid, 256, 0, s>>>(a);
     } else if (p->kernel == AIE_KERNEL_PW_DOT) {
         const size_t smem = (size_t)p->d.cout * p->d.cin * 4;
@@ -380,6 +433,18 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
     } else if (p->math == AIE_MATH_TF32) {
         int rc = tc_launch(p->tc, a, workspace, s, t_err, sizeof t_err);
         if (rc) return rc;
+    } else if (p->stem && a.vec_y && (a.y_stride % 4 == 0) && !(a.res && (a.r_stride % 4 || a.r_coff % 4)) &&
+               ((uintptr_t)w % 16 == 0)) {
+#define AIE_STEM(S, C) stem_kernel<S, 3, 3, C><<<(unsigned)p->grid, 256, p->stem_smem, s>>>(a, p->sg)
+        const int cin = (int)p->d.cin;
+        if (p->strict) {
+            if (cin == 1) AIE_STEM(true, 1); else if (cin == 2) AIE_STEM(true, 2);
+            else if (cin == 3) AIE_STEM(true, 3); else AIE_STEM(true, 4);
+        } else {
+            if (cin == 1) AIE_STEM(false, 1); else if (cin == 2) AIE_STEM(false, 2);
+            else if (cin == 3) AIE_STEM(false, 3); else AIE_STEM(false, 4);
+        }
+#undef AIE_STEM
     } else {
         dim3 grid((unsigned)((p->M + kFfmaBM - 1) / kFfmaBM), (p->d.cout + kFfmaBN - 1) / kFfmaBN);
         if (grid.y > 65535) return fail(AIE_E_UNSUPPORTED, "cout too large");

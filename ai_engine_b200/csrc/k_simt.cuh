@@ -366,3 +366,171 @@ __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a
 }
 
 }  // namespace aie
+
+namespace aie {
+
+// ---------------------------------------------------------------------------
+// Small-cin direct conv (the stem: cin <= 4, k x k).  A CTA computes a
+// tile_h x tile_w block of output pixels of one frame for all cout channels.
+// The input halo block is staged in shared memory; each thread owns 4 output
+// channels (lane % (cout/4)) and keeps their KK = kh*kw*cin weights in
+// registers, so the inner loop is one shared load per KK step feeding 4 FMAs.
+// cout/4 consecutive lanes share one pixel, so every output store
+// instruction writes whole 128-byte rows.  Accumulation order is bias, then
+// (ky, kx, ic) -- ai-cpu's im2row stem order (crates/ai-cpu/src/kernels/
+// im2row.rs:22-85 feeding conv_std).  Weights use the FFMA layout
+// [tap][cin][wn].
+// ---------------------------------------------------------------------------
+struct StemGeom {
+    int tile_h, tile_w, halo_h, halo_w, tiles_x, tiles_y;
+};
+
+template <bool kStrict, int KH, int KW, int CIN>
+__global__ void __launch_bounds__(256) stem_kernel(const ConvArgs a, const StemGeom g)
+{
+    constexpr int KK = KH * KW * CIN;
+    extern __shared__ float halo[];  // [halo_h][halo_w][CIN]
+    const int tiles = g.tiles_x * g.tiles_y;
+    const int img = blockIdx.x / tiles;
+    const int rem = blockIdx.x - img * tiles;
+    const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+    const int oy0 = ty * g.tile_h, ox0 = tx * g.tile_w;
+    const int iy0 = oy0 * a.sh - a.pt, ix0 = ox0 * a.sw - a.pl;
+
+    // stage the halo (zero outside the frame = the conv's padding)
+    const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff;
+    const int hn = g.halo_h * g.halo_w * CIN;
+    for (int i = threadIdx.x; i < hn; i += blockDim.x) {
+        const int c = i % CIN, p = i / CIN;
+        const int hy = p / g.halo_w, hx = p - hy * g.halo_w;
+        const int iy = iy0 + hy, ix = ix0 + hx;
+        float v = 0.0f;
+        if (iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw) v = __ldg(xb + ((long long)iy * a.iw + ix) * a.x_stride + c);
+        halo[i] = v;
+    }
+
+    const int lpp = a.cout >> 2;  // lanes per pixel
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = (lane % lpp) * 4;  // this thread's 4 output channels
+    float w[KK][4];
+#pragma unroll
+    for (int k = 0; k < KK; k++) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(a.w + (long long)k * a.wn + c0));
+        w[k][0] = v.x; w[k][1] = v.y; w[k][2] = v.z; w[k][3] = v.w;
+    }
+    const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.bias + c0));
+    __syncthreads();
+
+    const int ppw = 32 / lpp;  // pixels per warp per step
+    const int npx = g.tile_h * g.tile_w;
+    const int hrow = g.halo_w * CIN;
+    for (int p = warp * ppw + lane / lpp; p < npx; p += 8 * ppw) {
+        const int dy = p / g.tile_w, dx = p - dy * g.tile_w;
+        const int oy = oy0 + dy, ox = ox0 + dx;
+        if (oy >= a.oh || ox >= a.ow) continue;
+        float acc[4] = {b4.x, b4.y, b4.z, b4.w};
+        const float *hp0 = halo + (dy * a.sh) * hrow + (dx * a.sw) * CIN;
+#pragma unroll
+        for (int ky = 0; ky < KH; ky++)
+#pragma unroll
+            for (int kx = 0; kx < KW; kx++)
+#pragma unroll
+                for (int ic = 0; ic < CIN; ic++) {
+                    const float xv = hp0[ky * a.dil * hrow + kx * a.dil * CIN + ic];
+                    const int k = (ky * KW + kx) * CIN + ic;
+                    acc[0] = madd<kStrict>(acc[0], xv, w[k][0]);
+                    acc[1] = madd<kStrict>(acc[1], xv, w[k][1]);
+                    acc[2] = madd<kStrict>(acc[2], xv, w[k][2]);
+                    acc[3] = madd<kStrict>(acc[3], xv, w[k][3]);
+                }
+        epi_act_n<kStrict, 4>(a.act, acc, c0, a.cout);
+        const long long m = ((long long)img * a.oh + oy) * a.ow + ox;
+        float *yr = a.y + m * a.y_stride + a.y_coff + c0;
+        if (a.res) {
+            const float4 r = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.r_stride + a.r_coff + c0));
+            acc[0] = add_res<kStrict>(acc[0], r.x); acc[1] = add_res<kStrict>(acc[1], r.y);
+            acc[2] = add_res<kStrict>(acc[2], r.z); acc[3] = add_res<kStrict>(acc[3], r.w);
+        }
+        *reinterpret_cast<float4 *>(yr) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+}
+
+}  // namespace aie
+
+namespace aie {
+
+// ---------------------------------------------------------------------------
+// Depthwise conv, register-blocked: one thread computes PB horizontally
+// adjacent output pixels x 4 channels.  Each input column it loads feeds
+// every one of its outputs that the column's taps touch, so a row costs
+// (PB-1)*S + K loads for PB outputs instead of PB*K (the 4-pixel blocking of
+// crates/ai-cpu/src/kernels/dw.rs:100-145 and conv_dw.rs's PB).  Adjacent
+// threads take adjacent channel groups, so every load and store is a
+// coalesced 128-bit access.  Taps accumulate in (ky, kx) order, unfused --
+// bit-identical to ai-cpu's conv_dw.  Requires C % 4 == 0, aligned views,
+// dilation 1.
+// ---------------------------------------------------------------------------
+template <bool kStrict, int K, int S, int PB>
+__global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, int segs_per_row, int cg)
+{
+    const int idx = blockIdx.x * 256 + threadIdx.x;
+    const int g = idx % cg;
+    const int t = idx / cg;
+    const int seg = t % segs_per_row;
+    const int rowid = t / segs_per_row;  // img * oh + oy
+    if (rowid >= a.n * a.oh) return;
+    const int img = rowid / a.oh, oy = rowid - img * a.oh;
+    const int ox0 = seg * PB;
+    const int c0 = g * 4;
+    const int cpad = cg * 4;
+    const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.bias) + g);
+    float acc[PB][4];
+#pragma unroll
+    for (int p = 0; p < PB; p++) {
+        acc[p][0] = b4.x; acc[p][1] = b4.y; acc[p][2] = b4.z; acc[p][3] = b4.w;
+    }
+    constexpr int NJ = (PB - 1) * S + K;  // input columns one row needs
+    const int ixb = ox0 * S - a.pl;
+#pragma unroll
+    for (int ky = 0; ky < K; ky++) {
+        const int iy = oy * S - a.pt + ky;
+        if (iy < 0 || iy >= a.ih) continue;
+        const float *row = a.x + ((long long)(img * a.ih + iy) * a.iw) * a.x_stride + a.x_coff + c0;
+        float4 wk[K];
+#pragma unroll
+        for (int kx = 0; kx < K; kx++)
+            wk[kx] = __ldg(reinterpret_cast<const float4 *>(a.w + (ky * K + kx) * cpad + c0));
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int ix = ixb + j;
+            float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ix >= 0 && ix < a.iw) xv = __ldg(reinterpret_cast<const float4 *>(row + (long long)ix * a.x_stride));
+#pragma unroll
+            for (int p = 0; p < PB; p++) {
+                const int kx = j - p * S;
+                if (kx >= 0 && kx < K) {
+                    acc[p][0] = madd<true>(acc[p][0], xv.x, wk[kx].x);
+                    acc[p][1] = madd<true>(acc[p][1], xv.y, wk[kx].y);
+                    acc[p][2] = madd<true>(acc[p][2], xv.z, wk[kx].z);
+                    acc[p][3] = madd<true>(acc[p][3], xv.w, wk[kx].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < PB; p++) {
+        const int ox = ox0 + p;
+        if (ox >= a.ow) break;
+        epi_act_n<kStrict, 4>(a.act, acc[p], c0, a.cout);
+        const long long m = (long long)rowid * a.ow + ox;
+        if (a.res) {
+            const float4 r = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.r_stride + a.r_coff + c0));
+            acc[p][0] = add_res<true>(acc[p][0], r.x); acc[p][1] = add_res<true>(acc[p][1], r.y);
+            acc[p][2] = add_res<true>(acc[p][2], r.z); acc[p][3] = add_res<true>(acc[p][3], r.w);
+        }
+        *reinterpret_cast<float4 *>(a.y + m * a.y_stride + a.y_coff + c0) =
+            make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
+    }
+}
+
+}  // namespace aie

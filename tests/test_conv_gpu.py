@@ -101,7 +101,9 @@ def test_pointwise_residual(cuda_ok, math, h, w, cin, cout, act, seed):
 
 # ---------------------------------------------------------------- depthwise ---
 
-DW_SHAPES = [(72, 128, 64, 3, 1), (36, 64, 96, 5, 2), (33, 17, 6, 3, 2), (16, 16, 10, 5, 1)]
+DW_SHAPES = [(72, 128, 64, 3, 1), (36, 64, 96, 5, 2), (33, 17, 6, 3, 2), (16, 16, 10, 5, 1),
+             # beyond the reference grid: the register-blocked variants (C % 4 == 0)
+             (20, 37, 64, 5, 1), (41, 72, 32, 3, 2), (10, 18, 512, 3, 1), (9, 7, 8, 5, 2)]
 
 
 def dw_cases():
