@@ -20,6 +20,7 @@ LAYOUT_NHWC, LAYOUT_NHWC_C4 = 0, 1
 MATH_AUTO, MATH_FFMA, MATH_TF32, MATH_FP32_STRICT = 0, 1, 2, 3
 KERNEL_DW, KERNEL_PW, KERNEL_IGEMM, KERNEL_PW_DOT = 1, 2, 3, 4
 WFMT_OIHW, WFMT_SW_PACKED = 0, 1
+NOALLOC_SCRATCH_BYTES = 16 << 20  # AIE_NOALLOC_SCRATCH_BYTES
 
 
 class AieError(RuntimeError):
@@ -56,6 +57,7 @@ SIGNATURES = {
     "aie_plan_free": (None, [_vp]),
     "aie_conv_pack_weights": (C.c_int, [_vp, C.c_int32, _fp, _fp, _vp, _vp, _vp]),
     "aie_conv_run": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "aie_conv_run_noalloc": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "aie_resize_bilinear": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _vp, C.c_uint32,
                                       C.c_uint32, C.c_int32, _vp, C.c_int32, _vp, _vp]),
     "aie_status_string": (C.c_char_p, [C.c_int]),

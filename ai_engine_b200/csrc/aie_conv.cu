@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -487,4 +488,52 @@ extern "C" int aie_device_status(void *stream, uint32_t *code_out)
     if (code_out) *code_out = v;
     if (v) return fail(AIE_E_DEVICE_TIMEOUT, "device wait gave up, code 0x%08x", v);
     return AIE_OK;
+}
+
+// ------------------------------------------------- no-allocation entry ---
+//
+// Some callers cannot allocate device memory once they are running.
+// Examples: a real-time frame loop whose latency budget cannot absorb
+// cudaMalloc's device synchronisation; a plugin inside a host application
+// that hands over only its own tensors; code that runs while a stream is
+// being captured into a CUDA graph.  For them the split-K scratch comes from
+// this fixed array inside the library instead of a caller workspace.
+//
+// The array lives in every GPU's memory that loads this library, from
+// module load until process exit.  All calls share it and it keeps the
+// previous call's contents: the split-K tickets are cleared on the stream
+// before every launch and the partials are written before they are read,
+// so no state leaks between calls -- but two calls that overlap on the GPU
+// (e.g. on different streams) race on it.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[AIE_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_addr[64];  // device address of the array, per device ordinal
+
+extern "C" int aie_conv_run_noalloc(const aie_plan *p, const void *in, const void *w, const void *b,
+                                    const void *res, void *out, void *stream)
+{
+    if (!p) return fail(AIE_E_INVALID, "null plan");
+    if (p->wsbytes > AIE_NOALLOC_SCRATCH_BYTES)
+        return fail(AIE_E_UNSUPPORTED,
+                    "plan needs %llu bytes of split-K scratch but the built-in scratch holds %u; "
+                    "use aie_conv_run with a workspace, or plan with a smaller split_k",
+                    (unsigned long long)p->wsbytes, (unsigned)AIE_NOALLOC_SCRATCH_BYTES);
+    void *ws = nullptr;
+    if (p->wsbytes) {
+        int dev = -1;
+        CUDA_TRY(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= 64) return fail(AIE_E_UNSUPPORTED, "device ordinal %d out of range", dev);
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_addr[dev]) {
+            // first call on this device (which is current): the array's name is
+            // only a host-side stand-in; ask the runtime for its device address
+            void *addr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+            g_noalloc_addr[dev] = addr;
+        }
+        ws = g_noalloc_addr[dev];
+    }
+    return aie_conv_run(p, in, w, b, res, out, ws, stream);
 }
