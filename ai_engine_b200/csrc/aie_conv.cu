@@ -479,6 +479,15 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     return AIE_OK;
 }
 
+extern "C" int aie_selftest_wait_timeout(uint32_t timeout_us, void *stream)
+{
+    if (timeout_us == 0 || timeout_us > 2000000) return fail(AIE_E_INVALID, "timeout must be 1..2000000 us");
+    selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned long long)timeout_us * 1000ull);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+    return AIE_OK;
+}
+
 extern "C" int aie_device_status(void *stream, uint32_t *code_out)
 {
     CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));

@@ -112,15 +112,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
-// Bounded wait: true when the phase completed, false after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
+// Bounded wait: true when the phase completed, false after `limit_ns`.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, unsigned long long limit_ns)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtime();
     while (true) {
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
-        if (gtime() - t0 > kWaitNs) return false;
+        if (gtime() - t0 > limit_ns) return false;
+    }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) { return mbar_wait_for(bar, parity, kWaitNs); }
+
+// Self-test of the bounded-wait path: one thread waits on an mbarrier that
+// nothing ever arrives at.  The wait gives up after `limit_ns`, records
+// kSelftestCode in the device error word and the kernel returns normally --
+// the same path every role of tc_conv_kernel takes when a wait expires.
+constexpr uint32_t kSelftestCode = 0x7F000001u;
+
+__global__ void selftest_wait_kernel(unsigned long long limit_ns)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (!mbar_wait_for(&bar, 0, limit_ns)) report_error(kSelftestCode);
     }
 }
 

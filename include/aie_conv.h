@@ -206,6 +206,14 @@ AIE_API int aie_last_error(char *buf, size_t len);
 AIE_API int aie_conv_run_noalloc(const aie_plan *plan, const void *in, const void *dev_w, const void *dev_b,
                                  const void *res, void *out, void *stream);
 
+/* Failure-detection self-test: launch a kernel whose only wait (an
+ * mbarrier nothing arrives at) gives up after timeout_us (1..2e6), records
+ * its code in the device error word and returns -- the bounded-wait path of
+ * the conv kernels, exercised without a fault.  Follow with
+ * aie_device_status, which must report AIE_E_DEVICE_TIMEOUT.  Counterpart
+ * of ai-gpu's device-loss test (crates/ai-gpu/tests/device_lost.rs). */
+AIE_API int aie_selftest_wait_timeout(uint32_t timeout_us, void *stream);
+
 /* Read and clear the device error word that bounded device-side waits set
  * when they give up (synchronises `stream`).  AIE_OK or
  * AIE_E_DEVICE_TIMEOUT; *code_out (nullable) receives the raw word. */
