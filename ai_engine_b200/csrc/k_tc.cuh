@@ -4,13 +4,16 @@
 //
 // M = output pixels, N = cout, K = taps x cin.  Persistent, warp-specialised:
 //   warp 0       TMEM allocator + MMA issuer (one elected lane)
-//   warps 1..4   epilogue: tcgen05.ld -> bias -> act, transposed through
-//                shared memory -> +residual -> coalesced row stores
-//   warps 5..7   TMA producers, one elected lane each, taking stages in turn
+//   warps 1..8   epilogue, two groups of four: group g drains TMEM
+//                accumulator buffer g (every other tile), so two tiles'
+//                epilogues overlap.  tcgen05.ld -> bias -> act, transposed
+//                through shared memory -> +residual -> coalesced row stores
+//   warps 9..11  TMA producers, one elected lane each, taking stages in turn
 //                (TMA issue rate is per issuing thread: one thread issuing
 //                16 KB boxes reaches ~3.5 TB/s on B200, four reach HBM speed)
 // Accumulators are double-buffered in TMEM so the epilogue of one tile
-// overlaps the mainloop of the next.  Operands are fp32 in HBM and are read
+// overlaps the mainloop of the next.  (The epilogue is issue-latency bound
+// with one warp per SM sub-partition: ~550 instructions per 32x32 chunk.)  Operands are fp32 in HBM and are read
 // by the tensor core as TF32; both are K-major with the 128-byte swizzle.
 //
 // A operand (activations, NHWC):
@@ -41,7 +44,8 @@
 namespace aie {
 
 constexpr int kTcProducers = 3;                   // TMA issue is per-thread limited
-constexpr int kTcThreads = 32 * (5 + kTcProducers); // MMA, 4 epilogue, producers
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcThreads = 32 * (1 + kTcEpiWarps + kTcProducers); // MMA, epilogue, producers
 constexpr uint32_t kTcStageOut = 32 * 32 * 4;      // one 32x32 fp32 epilogue chunk per warp
 constexpr int kTcBM = 128;
 constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
@@ -212,18 +216,64 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar)
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
+// TMEM -> registers.  tcgen05.ld is asynchronous until tcgen05.wait::ld;
+// the wait names the destination registers as read-write operands so the
+// compiler cannot move any use of them above it.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t *r)
 {
-    uint32_t r[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_wait16(uint32_t *r)
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// compiler-only fence on 16 registers (a wait already covered them)
+__device__ __forceinline__ void reg_fence16(uint32_t *r)
+{
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]));
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
+{
+    uint32_t r[16];
+    tmem_ld16_issue(taddr, r);
+    tmem_wait16(r);
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Issue the load of 32 accumulator columns (16 when only `remaining` <= 16
+// are inside the tile; columns past `bn` may lie outside the TMEM
+// allocation).  Complete with tmem_wait32.
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, int remaining, uint32_t (&r)[32])
+{
+    tmem_ld16_issue(taddr, r);
+    if (remaining > 16) tmem_ld16_issue(taddr + 16, r + 16);
+}
+
+__device__ __forceinline__ void tmem_wait32(int remaining, uint32_t (&r)[32])
+{
+    tmem_wait16(r);
+    reg_fence16(r + 16);
+    if (remaining <= 16) {
+#pragma unroll
+        for (int i = 16; i < 32; i++) r[i] = 0u;
+    }
 }
 
 // --------------------------------------------------------------- kernel ---
@@ -267,43 +317,6 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
     return ((long long)img * a.c.oh + oy) * a.c.ow + ox;
 }
 
-// Direct-store epilogue for 16 columns of one output row (used when the
-// output view cannot be described to TMA).
-__device__ __forceinline__ void tc_store16(const TcArgs &a, long long m, int col0, const float (&acc)[16])
-{
-    const ConvArgs &c = a.c;
-    float *yr = c.y + m * c.y_stride + c.y_coff;
-    const float *rr = c.res ? c.res + m * c.r_stride + c.r_coff : nullptr;
-    float v[16];
-#pragma unroll
-    for (int j = 0; j < 16; j++) v[j] = acc[j] + (col0 + j < c.cout ? c.bias[col0 + j] : 0.0f);
-    act_apply_n<16>(c.act, v);
-#pragma unroll
-    for (int j = 0; j < 16; j++) {
-        const int col = col0 + j;
-        if (col < c.cout) yr[col] = rr ? v[j] + rr[col] : v[j];
-        else if (col < c.y_pad_to) yr[col] = 0.0f;
-    }
-}
-
-// 32 accumulator columns of this lane's row.  Columns past `bn` of the tile
-// are not read (they may lie outside the TMEM allocation).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int remaining, float (&v)[32])
-{
-    float lo[16], hi[16];
-    tmem_ld16(taddr, lo);
-    if (remaining > 16) tmem_ld16(taddr + 16, hi);
-    else {
-#pragma unroll
-        for (int i = 0; i < 16; i++) hi[i] = 0.0f;
-    }
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-        v[i] = lo[i];
-        v[16 + i] = hi[i];
-    }
-}
-
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
 {
@@ -341,9 +354,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = sh.tmem_base;
     volatile uint32_t *abort_flag = &sh.abort;
 
-    if (warp >= 5) {
+    if (warp >= 1 + kTcEpiWarps) {
         // ------------------------------------------------ TMA producers
-        const uint32_t pidx = (uint32_t)(warp - 5);
+        const uint32_t pidx = (uint32_t)(warp - 1 - kTcEpiWarps);
         if (lane == 0) {
             uint32_t it = 0, last_mine = 0xFFFFFFFFu;
             bool ok = true;
@@ -439,51 +452,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------ epilogue (warps 1..4)
-        const uint32_t ew = (uint32_t)(warp - 1);  // epilogue warp index: staging buffers, barriers
+        // ------------------------------------------------ epilogue (warps 1..8)
+        // Two groups of four warps; group g drains TMEM accumulator buffer g,
+        // i.e. every other tile, so two tiles' epilogues run at once.  Within
+        // a group, warp w owns TMEM lane quadrant w % 4 (= accumulator rows).
+        const uint32_t ew = (uint32_t)(warp - 1);  // 0..7: staging buffer, bias cache
+        const uint32_t grp = ew >> 2;              // accumulator buffer this group drains
         const uint32_t quad = warp & 3;            // TMEM lane quadrant this warp may access
         const uint32_t row = quad * 32 + lane;     // accumulator row = TMEM lane
         uint8_t *obuf = smem + a.out_off + ew * kTcStageOut;  // 32 x 32 fp32 staging
-        uint32_t acc_it = 0;
+        // this warp's copy of the n-tile's bias (zero past cout), reloaded
+        // only when the n-tile changes; read as broadcasts
+        float *bcache = reinterpret_cast<float *>(smem + a.out_off + 8 * kTcStageOut) + ew * 256;
+        uint32_t bias_nt = 0xFFFFFFFFu;
+        int bias_base = 0;  // first column of the cached bias
         const ConvArgs &c = a.c;
-        const int bias_len = (c.cout + 3) & ~3;
+        const int seg = lane & 7;
+        int mrow[8];  // output pixel of the 8 rows this lane stores, -1 outside (M < 2^31)
 
         // bias -> act on this lane's row, staged through shared memory, then
         // written back by the warp 8 lanes per 128-byte row segment so every
         // store (and residual load) instruction covers 4 whole rows instead
         // of 32 scattered 16-byte pieces; residual added after the activation
-        auto emit = [&](uint32_t mt, int col0, float (&v)[32]) {
-            const int seg = lane & 7;
+        auto emit = [&](int col0, float (&v)[32]) {
             const int col = col0 + seg * 4;
-            // the rows this lane writes, and their residual values, fetched
-            // first so the eight loads overlap each other and the math below
-            int mrow[8];  // output pixel of each row, -1 outside (M < 2^31, checked at plan time)
-            float4 rv[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                mrow[i] = (int)tc_row_pixel(a, mt, quad * 32 + i * 4 + (lane >> 3));
-                rv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (c.res && mrow[i] >= 0) {
-                    const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
-                    if (c.vec_y && col + 4 <= c.cout) rv[i] = __ldg(reinterpret_cast<const float4 *>(rr));
-                    else {
-                        float t4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                        for (int l = 0; l < 4; l++)
-                            if (col + l < c.cout) t4[l] = __ldg(rr + l);
-                        rv[i] = make_float4(t4[0], t4[1], t4[2], t4[3]);
-                    }
-                }
-            }
-            if (col0 + 32 <= bias_len) {
+            const bool vec = c.vec_y && col + 4 <= c.cout;
+            {
+                const float4 *bb = reinterpret_cast<const float4 *>(bcache + (col0 - bias_base));
 #pragma unroll
                 for (int q4 = 0; q4 < 8; q4++) {
-                    const float4 b = __ldg(reinterpret_cast<const float4 *>(c.bias + col0 + 4 * q4));
+                    const float4 b = bb[q4];
                     v[4 * q4] += b.x; v[4 * q4 + 1] += b.y; v[4 * q4 + 2] += b.z; v[4 * q4 + 3] += b.w;
                 }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; j++) v[j] += (col0 + j < c.cout) ? c.bias[col0 + j] : 0.0f;
             }
             act_apply_n<32>(c.act, v);
             __syncwarp();  // previous chunk's readers are done with the buffer
@@ -493,34 +493,66 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 *reinterpret_cast<float4 *>(st + ((ch ^ (lane & 7)) * 16)) =
                     make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
             __syncwarp();
+            if (col >= c.y_pad_to) return;
+            // four rows at a time: their residual loads are issued together
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int r = i * 4 + (lane >> 3);
-                const long long m = mrow[i];
-                if (m < 0 || col >= c.y_pad_to) continue;  // (m < 0: row outside the output)
-                float4 x = *reinterpret_cast<const float4 *>(obuf + r * 128 + ((seg ^ (r & 7)) * 16));
-                x.x += rv[i].x; x.y += rv[i].y; x.z += rv[i].z; x.w += rv[i].w;  // residual after act
-                float *yr = c.y + m * c.y_stride + c.y_coff + col;
-                if (c.vec_y && col + 4 <= c.cout) {
-                    *reinterpret_cast<float4 *>(yr) = x;
-                } else {
-                    const float xs[4] = {x.x, x.y, x.z, x.w};
+            for (int h = 0; h < 2; h++) {
+                float4 rv[4];
 #pragma unroll
-                    for (int l = 0; l < 4; l++) {
-                        if (col + l < c.cout) yr[l] = xs[l];
-                        else if (col + l < c.y_pad_to) yr[l] = 0.0f;
+                for (int q = 0; q < 4; q++) {
+                    const int i = 4 * h + q;
+                    rv[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (c.res && mrow[i] >= 0) {
+                        const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
+                        if (vec) rv[q] = __ldg(reinterpret_cast<const float4 *>(rr));
+                        else {
+                            float t4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                            for (int l = 0; l < 4; l++)
+                                if (col + l < c.cout) t4[l] = __ldg(rr + l);
+                            rv[q] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int i = 4 * h + q;
+                    const int r = i * 4 + (lane >> 3);
+                    if (mrow[i] < 0) continue;
+                    float4 x = *reinterpret_cast<const float4 *>(obuf + r * 128 + ((seg ^ (r & 7)) * 16));
+                    x.x += rv[q].x; x.y += rv[q].y; x.z += rv[q].z; x.w += rv[q].w;  // residual after act
+                    float *yr = c.y + (long long)mrow[i] * c.y_stride + c.y_coff + col;
+                    if (vec) {
+                        *reinterpret_cast<float4 *>(yr) = x;
+                    } else {
+                        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int l = 0; l < 4; l++) {
+                            if (col + l < c.cout) yr[l] = xs[l];
+                            else if (col + l < c.y_pad_to) yr[l] = 0.0f;
+                        }
                     }
                 }
             }
         };
 
-        for (uint64_t u = blockIdx.x; u < a.units; u += gridDim.x, acc_it++) {
+        uint32_t k = 0;  // tiles this group has drained: the phase of its buffer
+        for (uint64_t u = blockIdx.x + (uint64_t)grp * gridDim.x; u < a.units; u += 2ull * gridDim.x, k++) {
             const TcUnit t = tc_unit(a, u);
-            const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+            const uint32_t ab = grp, aph = k & 1;
             const int ncol = (int)min(a.bn, (uint32_t)c.y_pad_to - t.nt * a.bn);
             const int nbase = (int)(t.nt * a.bn);
             const uint32_t tbase = tmem + ((quad * 32) << 16) + ab * a.bn;
             const uint64_t tile = (uint64_t)t.mt * a.n_tiles + t.nt;
+#pragma unroll
+            for (int i = 0; i < 8; i++) mrow[i] = (int)tc_row_pixel(a, t.mt, quad * 32 + i * 4 + (lane >> 3));
+            if (t.nt != bias_nt) {
+                __syncwarp();
+                for (int i = lane; i < 256; i += 32) bcache[i] = (nbase + i < c.cout) ? __ldg(c.bias + nbase + i) : 0.0f;
+                __syncwarp();
+                bias_nt = t.nt;
+                bias_base = nbase;
+            }
             if (*abort_flag || !mbar_wait(&sh.acc_full[ab], aph)) {
                 report_error(0x01000004);
                 *abort_flag = 1;
@@ -529,9 +561,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             if (a.split == 1) {
                 for (int c0 = 0; c0 < ncol; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld32_issue(tbase + c0, (int)a.bn - c0, r);
+                    tmem_wait32((int)a.bn - c0, r);
                     float v[32];
-                    tmem_ld32(tbase + c0, (int)a.bn - c0, v);
-                    emit(t.mt, nbase + c0, v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+                    emit(nbase + c0, v);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -575,7 +611,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 }
                             }
                         }
-                        emit(t.mt, nbase + c0, v);
+                        emit(nbase + c0, v);
                     }
                     __syncwarp();
                     if (lane == 0) *ticket = 0;  // reusable by the next launch
@@ -668,7 +704,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     const uint32_t stage = kTcABytes + g->b_bytes;
     // shared memory: [stages][epilogue staging, 4 warps x 4 KB][barriers];
     // the stage buffers are 1024-aligned
-    const uint32_t out_bytes = 4 * kTcStageOut;
+    const uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + 256 * 4);  // staging + per-warp bias caches
     const uint32_t limit = 227 * 1024 - 1024 /*align slack*/ - 256 /*barriers*/;
     g->stages = std::min<uint32_t>(8, (limit - out_bytes) / stage);
     if (g->stages < 2) return -2;
