@@ -20,6 +20,7 @@ LAYOUT_NHWC, LAYOUT_NHWC_C4 = 0, 1
 MATH_AUTO, MATH_FFMA, MATH_TF32, MATH_FP32_STRICT = 0, 1, 2, 3
 KERNEL_DW, KERNEL_PW, KERNEL_IGEMM, KERNEL_PW_DOT = 1, 2, 3, 4
 WFMT_OIHW, WFMT_SW_PACKED = 0, 1
+RES_TENSOR, RES_BILINEAR_HALF_PIXEL, RES_BILINEAR_ASYMMETRIC = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20  # AIE_NOALLOC_SCRATCH_BYTES
 
 
@@ -36,7 +37,7 @@ class ConvDesc(C.Structure):
                 ("act", C.c_int32), ("has_res", C.c_int32), ("layout", C.c_int32), ("math", C.c_int32),
                 ("split_k", C.c_uint32), ("in_stride", C.c_uint32), ("in_coff", C.c_uint32),
                 ("res_stride", C.c_uint32), ("res_coff", C.c_uint32), ("out_stride", C.c_uint32),
-                ("out_coff", C.c_uint32)]
+                ("out_coff", C.c_uint32), ("res_mode", C.c_int32), ("res_h", C.c_uint32), ("res_w", C.c_uint32)]
 
 
 class PlanInfo(C.Structure):

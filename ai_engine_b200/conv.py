@@ -98,7 +98,8 @@ class ConvPlan:
 
     def __init__(self, op: Conv2d, n: int, ih: int, iw: int, *, has_res: bool = False, layout: str = "nhwc",
                  math: str = "auto", split_k: int = 0, in_view: Optional[View] = None,
-                 res_view: Optional[View] = None, out_view: Optional[View] = None, device=None):
+                 res_view: Optional[View] = None, out_view: Optional[View] = None,
+                 res_resize: Optional[Tuple[int, int, str]] = None, device=None):
         self.lib = _lib.load()
         self.op, self.n, self.ih, self.iw = op, n, ih, iw
         self.layout = layout
@@ -115,6 +116,12 @@ class ConvPlan:
             if v is not None:
                 setattr(d, s, v.stride)
                 setattr(d, c, v.coff)
+        if res_resize is not None:
+            # residual = bilinear sample of a [n, rh, rw, cout] tensor (fused Resize -> Conv(res))
+            rh, rw, mode = res_resize
+            d.res_mode = _lib.RES_BILINEAR_HALF_PIXEL if mode == "half_pixel" else _lib.RES_BILINEAR_ASYMMETRIC
+            d.res_h, d.res_w = rh, rw
+        self.res_resize = res_resize
         self.desc = d
         h = C.c_void_p()
         check(self.lib.aie_conv_plan(C.byref(d), C.byref(h)), "aie_conv_plan")

@@ -78,7 +78,7 @@ extern "C" int32_t aie_abi_version(void) { return AIE_ABI_VERSION; }
 
 extern "C" const char *aie_build_info(void)
 {
-    return "aie_conv sm_100a (tcgen05 TF32 GEMM, FFMA implicit GEMM, depthwise); nvcc " __DATE__;
+    return "aie_conv abi 2 sm_100a (tcgen05 TF32 GEMM, FFMA implicit GEMM, depthwise); nvcc " __DATE__;
 }
 
 extern "C" const char *aie_status_string(int s)
@@ -131,6 +131,10 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
         return fail(AIE_E_INVALID, "layout %d out of range", d.layout);
     if (d.math < AIE_MATH_AUTO || d.math > kMathStrict) return fail(AIE_E_INVALID, "math %d out of range", d.math);
     if (d.kh > 16 || d.kw > 16) return fail(AIE_E_UNSUPPORTED, "kernel larger than 16x16");
+    if (d.res_mode < AIE_RES_TENSOR || d.res_mode > AIE_RES_BILINEAR_ASYMMETRIC)
+        return fail(AIE_E_INVALID, "res_mode %d out of range", d.res_mode);
+    if (d.res_mode != AIE_RES_TENSOR && (!d.has_res || !d.res_h || !d.res_w))
+        return fail(AIE_E_INVALID, "a bilinear residual needs has_res and res_h/res_w");
     // Conv2d::out_hw (crates/ai-core/src/ops/conv.rs:49-55)
     const long long ekh = (long long)d.dil * (d.kh - 1) + 1, ekw = (long long)d.dil * (d.kw - 1) + 1;
     const long long hh = (long long)d.ih + d.pad[0] + d.pad[2] - ekh;
@@ -176,6 +180,11 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
         p->kernel = (d.cout <= 4 && !d.has_res) ? AIE_KERNEL_PW_DOT : AIE_KERNEL_PW;
     } else {
         p->kernel = AIE_KERNEL_IGEMM;
+    }
+
+    if (d.res_mode != AIE_RES_TENSOR && p->kernel != AIE_KERNEL_PW && p->kernel != AIE_KERNEL_IGEMM) {
+        delete p;
+        return fail(AIE_E_UNSUPPORTED, "a bilinear residual is fused into the GEMM kernels only");
     }
 
     // Math.
@@ -225,34 +234,23 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     } else {
         p->wn = (int)cpad4;
         p->wbytes = (uint64_t)taps * d.cin * p->wn * 4;
-        // small-cin k x k convs (the stem) take the direct-conv kernel: the
+        // small-cin 3x3 convs (the stem) take the direct-conv kernel: the
         // GEMM's K tiles would be mostly padding (cin=3 -> 3 of 16 lanes)
         const uint32_t lpp = d.cout / 4;
-        if (p->kernel == AIE_KERNEL_IGEMM && d.cin <= 4 && d.kh == 3 && d.kw == 3 && d.cout % 4 == 0 &&
-            lpp >= 1 && lpp <= 32 && 32 % lpp == 0) {
+        if (p->kernel == AIE_KERNEL_IGEMM && d.res_mode == AIE_RES_TENSOR && d.cin <= 4 && d.kh == 3 && d.kw == 3 && d.dil == 1 &&
+            d.sh == d.sw && (d.sh == 1 || d.sh == 2) && d.cout % 4 == 0 && lpp >= 1 && lpp <= 32 && 32 % lpp == 0) {
             p->stem = true;
-            int best = -1;
-            const int shapes[3][2] = {{8, 32}, {16, 16}, {32, 8}};
-            long long best_cover = 0;
-            for (int i = 0; i < 3; i++) {
-                const int th = shapes[i][0], tw = shapes[i][1];
-                const long long cover = (long long)((p->oh + th - 1) / th * th) * ((p->ow + tw - 1) / tw * tw);
-                if (best < 0 || cover < best_cover) { best = i; best_cover = cover; }
-            }
             StemGeom &g = p->sg;
-            g.tile_h = shapes[best][0];
-            g.tile_w = shapes[best][1];
-            g.halo_h = (g.tile_h - 1) * d.sh + (d.kh - 1) * d.dil + 1;
-            g.halo_w = (g.tile_w - 1) * d.sw + (d.kw - 1) * d.dil + 1;
+            g.tile_h = 16;
+            g.tile_w = 16;
+            g.halo_h = (g.tile_h - 1) * d.sh + d.kh;
+            g.halo_w = (g.tile_w - 1) * d.sw + d.kw;
             g.tiles_x = (p->ow + g.tile_w - 1) / g.tile_w;
             g.tiles_y = (p->oh + g.tile_h - 1) / g.tile_h;
             p->stem_smem = (uint32_t)(g.halo_h * g.halo_w * d.cin * 4);
-            if (p->stem_smem > 48 * 1024) p->stem = false;  // very large strides/dilations: GEMM path
-            if (p->stem) {
-                p->tile_m = g.tile_h * g.tile_w;
-                p->tile_n = d.cout;
-                p->grid = (uint64_t)d.n * g.tiles_x * g.tiles_y;
-            }
+            p->tile_m = g.tile_h * g.tile_w;
+            p->tile_n = d.cout;
+            p->grid = (uint64_t)d.n * g.tiles_x * g.tiles_y;
         }
     }
     if (!p->stem && (p->kernel == AIE_KERNEL_IGEMM || p->kernel == AIE_KERNEL_PW) && p->math != AIE_MATH_TF32) {
@@ -264,8 +262,9 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     // border taps counted as full; bytes = input + weights + bias + output (+ res).
     const uint64_t cin_g = d.cin / d.groups;
     p->flops = 2ull * (uint64_t)p->M * d.cout * cin_g * taps;
+    const uint64_t res_px = !d.has_res ? 0 : (d.res_mode ? (uint64_t)d.n * d.res_h * d.res_w : (uint64_t)p->M);
     p->min_bytes = 4ull * ((uint64_t)d.n * d.ih * d.iw * d.cin + (uint64_t)d.cout * cin_g * taps + d.cout +
-                           (uint64_t)p->M * d.cout * (d.has_res ? 2 : 1));
+                           (uint64_t)p->M * d.cout + res_px * d.cout);
     *out = p;
     return AIE_OK;
 }
@@ -385,6 +384,13 @@ static ConvArgs make_args(const aie_plan *p, const void *in, const void *w, cons
     a.wn = p->wn;
     const uintptr_t xa = (uintptr_t)(a.x + a.x_coff), ya = (uintptr_t)(a.y + a.y_coff);
     const uintptr_t ra = a.res ? (uintptr_t)(a.res + a.r_coff) : 0;
+    a.res_mode = d.res_mode;
+    a.rh = d.res_mode ? (int)d.res_h : (int)p->oh;
+    a.rw = d.res_mode ? (int)d.res_w : (int)p->ow;
+    a.div_ow = make_fastdiv((int)p->ow);
+    a.div_oh = make_fastdiv((int)p->oh);
+    a.rsy = (float)a.rh / (float)p->oh;
+    a.rsx = (float)a.rw / (float)p->ow;
     a.vec_x = (d.cin % 4 == 0 || d.groups > 1) && a.x_stride % 4 == 0 && xa % 16 == 0;
     a.vec_y = a.y_stride % 4 == 0 && ya % 16 == 0 && (!a.res || (a.r_stride % 4 == 0 && ra % 16 == 0));
     return a;
@@ -436,15 +442,21 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         if (rc) return rc;
     } else if (p->stem && a.vec_y && (a.y_stride % 4 == 0) && !(a.res && (a.r_stride % 4 || a.r_coff % 4)) &&
                ((uintptr_t)w % 16 == 0)) {
-#define AIE_STEM(S, C) stem_kernel<S, 3, 3, C><<<(unsigned)p->grid, 256, p->stem_smem, s>>>(a, p->sg)
+        const unsigned stem_grid = (unsigned)std::min<uint64_t>(p->grid, (uint64_t)tc_sm_count());
+        const unsigned smem = 2 * p->stem_smem;
+#define AIE_STEM(S, C, ST) stem_kernel<S, 3, 3, C, ST, 16, 16><<<stem_grid, 256, smem, s>>>(a, p->sg)
+#define AIE_STEM2(S, ST)                                        \
+    if (cin == 1) AIE_STEM(S, 1, ST);                           \
+    else if (cin == 2) AIE_STEM(S, 2, ST);                      \
+    else if (cin == 3) AIE_STEM(S, 3, ST);                      \
+    else AIE_STEM(S, 4, ST);
         const int cin = (int)p->d.cin;
         if (p->strict) {
-            if (cin == 1) AIE_STEM(true, 1); else if (cin == 2) AIE_STEM(true, 2);
-            else if (cin == 3) AIE_STEM(true, 3); else AIE_STEM(true, 4);
+            if (p->d.sh == 1) { AIE_STEM2(true, 1) } else { AIE_STEM2(true, 2) }
         } else {
-            if (cin == 1) AIE_STEM(false, 1); else if (cin == 2) AIE_STEM(false, 2);
-            else if (cin == 3) AIE_STEM(false, 3); else AIE_STEM(false, 4);
+            if (p->d.sh == 1) { AIE_STEM2(false, 1) } else { AIE_STEM2(false, 2) }
         }
+#undef AIE_STEM2
 #undef AIE_STEM
     } else {
         dim3 grid((unsigned)((p->M + kFfmaBM - 1) / kFfmaBM), (p->d.cout + kFfmaBN - 1) / kFfmaBN);
@@ -464,6 +476,8 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     if (!n || !ih || !iw || !c || !oh || !ow) return fail(AIE_E_INVALID, "zero-sized resize");
     if (mode != 0 && mode != 1) return fail(AIE_E_INVALID, "resize mode %d", mode);
     if (act < 0 || act > AIE_ACT_RECIP) return fail(AIE_E_INVALID, "activation %d", act);
+    if ((long long)n * oh * ow * ((c + 3) / 4) >= (1ll << 31) || (long long)n * ih * iw * c >= (1ll << 31))
+        return fail(AIE_E_UNSUPPORTED, "resize larger than 2^31 elements; split the batch");
     ResizeArgs a;
     a.x = (const float *)in;
     a.add = (const float *)add;
@@ -471,9 +485,16 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     a.n = n; a.ih = ih; a.iw = iw; a.c = c; a.oh = oh; a.ow = ow; a.mode = mode; a.act = act;
     a.sy = (float)ih / (float)oh;
     a.sx = (float)iw / (float)ow;
-    a.vec = 0;
-    const long long total = (long long)n * oh * ow * ((c + 3) / 4);
-    resize_bilinear_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a);
+    const int cg = (int)((c + 3) / 4);
+    a.px_per_thread = c == 1 ? 4 : 1;
+    a.vec = c == 1 ? ((uintptr_t)out % 16 == 0 && ow % 4 == 0)
+                   : ((c % 4 == 0) && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0 &&
+                      (!add || (uintptr_t)add % 16 == 0));
+    a.div_cg = make_fastdiv(cg);
+    a.div_ow = make_fastdiv((int)ow);
+    a.div_oh = make_fastdiv((int)oh);
+    const long long groups = (long long)n * oh * ((ow + a.px_per_thread - 1) / a.px_per_thread) * cg;
+    resize_bilinear_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "resize launch");
     return AIE_OK;

@@ -152,6 +152,35 @@ __device__ __forceinline__ float add_res(float v, float r)
     else return v + r;
 }
 
+// Division by a run-time divisor as multiply-high + shift (valid for
+// 0 <= n < 2^31): the divisor's (mul, shift) pair is computed on the host.
+struct FastDiv {
+    int d;
+    unsigned mul, shr;
+};
+
+static inline FastDiv make_fastdiv(int d)
+{
+    FastDiv f;
+    f.d = d;
+    if (d <= 1) {
+        f.mul = 0;
+        f.shr = 0;
+        return f;
+    }
+    unsigned l = 0;
+    while ((1ull << l) < (unsigned long long)d) l++;  // ceil(log2 d)
+    const unsigned p = 31 + l;
+    f.mul = (unsigned)(((1ull << p) + (unsigned long long)d - 1) / (unsigned long long)d);
+    f.shr = p - 32;
+    return f;
+}
+
+__device__ __forceinline__ int fdiv(int n, const FastDiv &f)
+{
+    return f.d <= 1 ? n : (int)(__umulhi((unsigned)n, f.mul) >> f.shr);
+}
+
 // Device error word set by bounded waits that give up (read and cleared by
 // aie_device_status).  Bit layout: [31:24] kernel id, [23:0] site code.
 // The library is one translation unit, so the definition lives here.

@@ -29,7 +29,62 @@ struct ConvArgs {
     int wn;          // weight row stride in floats (GEMM: cout padded to 4)
     int vec_x;       // float4 input loads are aligned
     int vec_y;       // float4 output / residual accesses are aligned
+    int res_mode;    // 0: residual tensor of the output's shape; 1/2: bilinear
+                     // sample (half_pixel / asymmetric) of an rh x rw tensor
+    int rh, rw;
+    float rsy, rsx;  // rh / oh, rw / ow (f32 division, as the reference)
+    FastDiv div_ow, div_oh;  // output pixel -> (frame, row, column)
 };
+
+// Residual of output pixel m, channels [col, col+4), sampled bilinearly
+// from the rh x rw residual tensor.  Same arithmetic, rounded step by step,
+// as resize_bilinear_kernel / reference/resize.rs:5-42, so the fused
+// Resize -> Conv(res) equals the unfused pair bit for bit.
+__device__ __forceinline__ float4 bilinear_res4(const ConvArgs &c, long long m, int col, bool vec)
+{
+    const int mi = (int)m;  // pixel counts are < 2^31 (checked at plan time)
+    const int t = fdiv(mi, c.div_ow);
+    const int ox = mi - t * c.ow;
+    const int img = fdiv(t, c.div_oh);
+    const int oy = t - img * c.oh;
+    const float fy = c.res_mode == 1 ? __fsub_rn(__fmul_rn(__fadd_rn((float)oy, 0.5f), c.rsy), 0.5f)
+                                     : __fmul_rn((float)oy, c.rsy);
+    const float fx = c.res_mode == 1 ? __fsub_rn(__fmul_rn(__fadd_rn((float)ox, 0.5f), c.rsx), 0.5f)
+                                     : __fmul_rn((float)ox, c.rsx);
+    const float fly = floorf(fy), flx = floorf(fx);
+    const int y0 = min(max((int)fly, 0), c.rh - 1), y1 = min(max((int)fly + 1, 0), c.rh - 1);
+    const int x0 = min(max((int)flx, 0), c.rw - 1), x1 = min(max((int)flx + 1, 0), c.rw - 1);
+    const float ty = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
+    const float tx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
+    const float ty1 = __fsub_rn(1.0f, ty), tx1 = __fsub_rn(1.0f, tx);
+    const float *rb = c.res + (long long)img * c.rh * c.rw * c.r_stride + c.r_coff + col;
+    const float *p00 = rb + ((long long)y0 * c.rw + x0) * c.r_stride, *p01 = rb + ((long long)y0 * c.rw + x1) * c.r_stride;
+    const float *p10 = rb + ((long long)y1 * c.rw + x0) * c.r_stride, *p11 = rb + ((long long)y1 * c.rw + x1) * c.r_stride;
+    float g00[4], g01[4], g10[4], g11[4];
+    if (vec) {
+        const float4 a0 = __ldg(reinterpret_cast<const float4 *>(p00)), a1 = __ldg(reinterpret_cast<const float4 *>(p01));
+        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(p10)), b1 = __ldg(reinterpret_cast<const float4 *>(p11));
+        g00[0] = a0.x; g00[1] = a0.y; g00[2] = a0.z; g00[3] = a0.w;
+        g01[0] = a1.x; g01[1] = a1.y; g01[2] = a1.z; g01[3] = a1.w;
+        g10[0] = b0.x; g10[1] = b0.y; g10[2] = b0.z; g10[3] = b0.w;
+        g11[0] = b1.x; g11[1] = b1.y; g11[2] = b1.z; g11[3] = b1.w;
+    } else {
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const bool ok = col + l < c.cout;
+            g00[l] = ok ? __ldg(p00 + l) : 0.0f; g01[l] = ok ? __ldg(p01 + l) : 0.0f;
+            g10[l] = ok ? __ldg(p10 + l) : 0.0f; g11[l] = ok ? __ldg(p11 + l) : 0.0f;
+        }
+    }
+    float v[4];
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+        const float top = __fadd_rn(__fmul_rn(g00[l], tx1), __fmul_rn(g01[l], tx));
+        const float bot = __fadd_rn(__fmul_rn(g10[l], tx1), __fmul_rn(g11[l], tx));
+        v[l] = __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
+    }
+    return make_float4(v[0], v[1], v[2], v[3]);
+}
 
 // ---------------------------------------------------------------------------
 // Implicit-GEMM conv on FFMA.  C[M, cout] = sum_taps X_tap[M, cin] W_tap[cin, cout].
@@ -152,7 +207,14 @@ __global__ void __launch_bounds__(kFfmaThreads) igemm_ffma_kernel(const ConvArgs
         const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff : nullptr;
         float v[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
         epi_act_n<kStrict, 4>(a.act, v, col0, a.cout);
-        if (a.vec_y && col0 + 4 <= a.cout) {
+        const bool vec = a.vec_y && col0 + 4 <= a.cout;
+        if (a.res && a.res_mode) {
+            const float4 r = bilinear_res4(a, m, col0, vec);
+            v[0] = add_res<kStrict>(v[0], r.x); v[1] = add_res<kStrict>(v[1], r.y);
+            v[2] = add_res<kStrict>(v[2], r.z); v[3] = add_res<kStrict>(v[3], r.w);
+            rr = nullptr;
+        }
+        if (vec) {
             if (rr) {
                 const float4 r = __ldg(reinterpret_cast<const float4 *>(rr + col0));
                 v[0] = add_res<kStrict>(v[0], r.x); v[1] = add_res<kStrict>(v[1], r.y);
@@ -312,48 +374,107 @@ struct ResizeArgs {
     int n, ih, iw, c, oh, ow, mode, act;
     float sy, sx;
     int vec;
+    FastDiv div_cg, div_ow, div_oh;
+    int px_per_thread;  // 4 for single-channel tensors (4 adjacent output pixels), else 1
 };
+
+// Source coordinate along one axis (reference/resize.rs:16-29), rounded step
+// by step: index pair, weight of the far sample.
+__device__ __forceinline__ void resize_axis(int o, float scale, int mode, int in, int &i0, int &i1, float &t)
+{
+    const float f = mode == 0 ? __fsub_rn(__fmul_rn(__fadd_rn((float)o, 0.5f), scale), 0.5f) : __fmul_rn((float)o, scale);
+    const float fl = floorf(f);
+    i0 = min(max((int)fl, 0), in - 1);
+    i1 = min(max((int)fl + 1, 0), in - 1);
+    t = fminf(fmaxf(__fsub_rn(f, fl), 0.0f), 1.0f);
+}
+
+__device__ __forceinline__ float lerp2(float g00, float g01, float g10, float g11, float tx, float tx1, float ty,
+                                       float ty1)
+{
+    const float top = __fadd_rn(__fmul_rn(g00, tx1), __fmul_rn(g01, tx));
+    const float bot = __fadd_rn(__fmul_rn(g10, tx1), __fmul_rn(g11, tx));
+    return __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
+}
 
 __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a)
 {
     const int cg = (a.c + 3) >> 2;
-    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long total = (long long)a.n * a.oh * a.ow * cg;
+    const int idx = blockIdx.x * 256 + threadIdx.x;
+    const int total = a.n * a.oh * ((a.ow + a.px_per_thread - 1) / a.px_per_thread) * cg;
     if (idx >= total) return;
-    const int g = (int)(idx % cg);
-    const long long px = idx / cg;
-    const int ox = (int)(px % a.ow);
-    const long long t = px / a.ow;
-    const int oy = (int)(t % a.oh);
-    const int img = (int)(t / a.oh);
-
-    const float fy = a.mode == 0 ? __fsub_rn(__fmul_rn(__fadd_rn((float)oy, 0.5f), a.sy), 0.5f)
-                                 : __fmul_rn((float)oy, a.sy);
-    const float fx = a.mode == 0 ? __fsub_rn(__fmul_rn(__fadd_rn((float)ox, 0.5f), a.sx), 0.5f)
-                                 : __fmul_rn((float)ox, a.sx);
-    const float fly = floorf(fy), flx = floorf(fx);
-    const int y0 = min(max((int)fly, 0), a.ih - 1), y1 = min(max((int)fly + 1, 0), a.ih - 1);
-    const int x0 = min(max((int)flx, 0), a.iw - 1), x1 = min(max((int)flx + 1, 0), a.iw - 1);
-    const float ty = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
-    const float tx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
-    const float ty1 = __fsub_rn(1.0f, ty), tx1 = __fsub_rn(1.0f, tx);
-
+    const int g = idx - fdiv(idx, a.div_cg) * cg;
+    const int pxg = fdiv(idx, a.div_cg);  // pixel group index
+    const int owg = (a.ow + a.px_per_thread - 1) / a.px_per_thread;
+    const int row = pxg / owg;            // img * oh + oy
+    const int ox0 = (pxg - row * owg) * a.px_per_thread;
+    const int img = fdiv(row, a.div_oh);
+    const int oy = row - img * a.oh;
+    int y0, y1;
+    float ty;
+    resize_axis(oy, a.sy, a.mode, a.ih, y0, y1, ty);
+    const float ty1 = __fsub_rn(1.0f, ty);
     const float *xb = a.x + (long long)img * a.ih * a.iw * a.c;
+    const float *r0 = xb + (long long)y0 * a.iw * a.c, *r1 = xb + (long long)y1 * a.iw * a.c;
+    if (a.px_per_thread > 1) {  // single channel: 4 adjacent output pixels
+        float v[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int ox = min(ox0 + p, a.ow - 1);
+            int x0, x1;
+            float tx;
+            resize_axis(ox, a.sx, a.mode, a.iw, x0, x1, tx);
+            v[p] = lerp2(__ldg(r0 + x0), __ldg(r0 + x1), __ldg(r1 + x0), __ldg(r1 + x1), tx, __fsub_rn(1.0f, tx), ty, ty1);
+        }
+        const long long ob = (long long)row * a.ow + ox0;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            if (ox0 + p >= a.ow) break;
+            if (a.add) v[p] = __fadd_rn(v[p], __ldg(a.add + ob + p));
+        }
+        act_apply_strict_n<4>(a.act, v, 0, 0);
+        if (a.vec && ox0 + 4 <= a.ow) {
+            *reinterpret_cast<float4 *>(a.y + ob) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int p = 0; p < 4; p++)
+                if (ox0 + p < a.ow) a.y[ob + p] = v[p];
+        }
+        return;
+    }
+    int x0, x1;
+    float tx;
+    resize_axis(ox0, a.sx, a.mode, a.iw, x0, x1, tx);
+    const float tx1 = __fsub_rn(1.0f, tx);
     const int c0 = g * 4;
-    const float *p00 = xb + ((long long)y0 * a.iw + x0) * a.c + c0;
-    const float *p01 = xb + ((long long)y0 * a.iw + x1) * a.c + c0;
-    const float *p10 = xb + ((long long)y1 * a.iw + x0) * a.c + c0;
-    const float *p11 = xb + ((long long)y1 * a.iw + x1) * a.c + c0;
+    const long long px = (long long)row * a.ow + ox0;
     float *yr = a.y + px * a.c + c0;
     const float *ar = a.add ? a.add + px * a.c + c0 : nullptr;
     const int nl = min(4, a.c - c0);
     float v[4];
+    if (a.vec && nl == 4) {
+        const float4 g00 = __ldg(reinterpret_cast<const float4 *>(r0 + x0 * a.c + c0));
+        const float4 g01 = __ldg(reinterpret_cast<const float4 *>(r0 + x1 * a.c + c0));
+        const float4 g10 = __ldg(reinterpret_cast<const float4 *>(r1 + x0 * a.c + c0));
+        const float4 g11 = __ldg(reinterpret_cast<const float4 *>(r1 + x1 * a.c + c0));
+        v[0] = lerp2(g00.x, g01.x, g10.x, g11.x, tx, tx1, ty, ty1);
+        v[1] = lerp2(g00.y, g01.y, g10.y, g11.y, tx, tx1, ty, ty1);
+        v[2] = lerp2(g00.z, g01.z, g10.z, g11.z, tx, tx1, ty, ty1);
+        v[3] = lerp2(g00.w, g01.w, g10.w, g11.w, tx, tx1, ty, ty1);
+        if (ar) {
+            const float4 ad = __ldg(reinterpret_cast<const float4 *>(ar));
+            v[0] = __fadd_rn(v[0], ad.x); v[1] = __fadd_rn(v[1], ad.y);
+            v[2] = __fadd_rn(v[2], ad.z); v[3] = __fadd_rn(v[3], ad.w);
+        }
+        act_apply_strict_n<4>(a.act, v, c0, a.c);
+        *reinterpret_cast<float4 *>(yr) = make_float4(v[0], v[1], v[2], v[3]);
+        return;
+    }
 #pragma unroll
     for (int l = 0; l < 4; l++) {
         if (l < nl) {
-            const float top = __fadd_rn(__fmul_rn(__ldg(p00 + l), tx1), __fmul_rn(__ldg(p01 + l), tx));
-            const float bot = __fadd_rn(__fmul_rn(__ldg(p10 + l), tx1), __fmul_rn(__ldg(p11 + l), tx));
-            v[l] = __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
+            v[l] = lerp2(__ldg(r0 + x0 * a.c + c0 + l), __ldg(r0 + x1 * a.c + c0 + l), __ldg(r1 + x0 * a.c + c0 + l),
+                         __ldg(r1 + x1 * a.c + c0 + l), tx, tx1, ty, ty1);
             if (ar) v[l] = __fadd_rn(v[l], __ldg(ar + l));
         } else {
             v[l] = 0.0f;
@@ -370,11 +491,13 @@ __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a
 namespace aie {
 
 // ---------------------------------------------------------------------------
-// Small-cin direct conv (the stem: cin <= 4, k x k).  A CTA computes a
-// tile_h x tile_w block of output pixels of one frame for all cout channels.
-// The input halo block is staged in shared memory; each thread owns 4 output
+// Small-cin direct conv (the stem: cin <= 4, k x k).  Persistent: each CTA
+// walks tile_h x tile_w blocks of output pixels (all cout channels), with the
+// next block's input halo prefetched into a second shared-memory buffer by
+// cp.async while the current one is computed.  Each thread owns 4 output
 // channels (lane % (cout/4)) and keeps their KK = kh*kw*cin weights in
-// registers, so the inner loop is one shared load per KK step feeding 4 FMAs.
+// registers for the whole kernel, so the inner loop is one shared load per
+// KK step feeding 4 FMAs.
 // cout/4 consecutive lanes share one pixel, so every output store
 // instruction writes whole 128-byte rows.  Accumulation order is bias, then
 // (ky, kx, ic) -- ai-cpu's im2row stem order (crates/ai-cpu/src/kernels/
@@ -385,29 +508,37 @@ struct StemGeom {
     int tile_h, tile_w, halo_h, halo_w, tiles_x, tiles_y;
 };
 
-template <bool kStrict, int KH, int KW, int CIN>
-__global__ void __launch_bounds__(256) stem_kernel(const ConvArgs a, const StemGeom g)
+template <bool kStrict, int KH, int KW, int CIN, int S, int TH, int TW>
+__global__ void __launch_bounds__(256, 1) stem_kernel(const ConvArgs a, const StemGeom g)
 {
     constexpr int KK = KH * KW * CIN;
-    extern __shared__ float halo[];  // [halo_h][halo_w][CIN]
-    const int tiles = g.tiles_x * g.tiles_y;
-    const int img = blockIdx.x / tiles;
-    const int rem = blockIdx.x - img * tiles;
-    const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
-    const int oy0 = ty * g.tile_h, ox0 = tx * g.tile_w;
-    const int iy0 = oy0 * a.sh - a.pt, ix0 = ox0 * a.sw - a.pl;
+    constexpr int HH = (TH - 1) * S + KH, HW = (TW - 1) * S + KW;  // halo block (dilation 1)
+    constexpr int HROW = HW * CIN, HN = HH * HROW;
+    constexpr int NPX = TH * TW;
+    extern __shared__ float halo[];  // 2 x [HH][HW][CIN]
+    const int tiles_per_img = g.tiles_x * g.tiles_y;
+    const int ntiles = a.n * tiles_per_img;
 
-    // stage the halo (zero outside the frame = the conv's padding)
-    const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff;
-    const int hn = g.halo_h * g.halo_w * CIN;
-    for (int i = threadIdx.x; i < hn; i += blockDim.x) {
-        const int c = i % CIN, p = i / CIN;
-        const int hy = p / g.halo_w, hx = p - hy * g.halo_w;
-        const int iy = iy0 + hy, ix = ix0 + hx;
-        float v = 0.0f;
-        if (iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw) v = __ldg(xb + ((long long)iy * a.iw + ix) * a.x_stride + c);
-        halo[i] = v;
-    }
+    // Stage tile t's input halo into buffer `buf` with 4-byte cp.async;
+    // out-of-frame elements are zero-filled (src-size 0) = the padding.
+    auto stage = [&](int t, int buf) {
+        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
+        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int iy0 = ty * TH * S - a.pt, ix0 = tx * TW * S - a.pl;
+        const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff;
+        float *dst = halo + buf * HN;
+        for (int i = threadIdx.x; i < HN; i += 256) {
+            const int cc = i % CIN, p = i / CIN;
+            const int hy = p / HW, hx = p - hy * HW;
+            const int iy = iy0 + hy, ix = ix0 + hx;
+            const bool ok = iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
+            const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cc : xb;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(
+                             (uint32_t)__cvta_generic_to_shared(dst + i)),
+                         "l"(src), "r"(ok ? 4 : 0)
+                         : "memory");
+        }
+    };
 
     const int lpp = a.cout >> 2;  // lanes per pixel
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -419,40 +550,67 @@ __global__ void __launch_bounds__(256) stem_kernel(const ConvArgs a, const StemG
         w[k][0] = v.x; w[k][1] = v.y; w[k][2] = v.z; w[k][3] = v.w;
     }
     const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.bias + c0));
-    __syncthreads();
+    const int ppw = 32 / lpp;       // pixels per warp per step
+    const int step = 8 * ppw;       // pixels per CTA per step
 
-    const int ppw = 32 / lpp;  // pixels per warp per step
-    const int npx = g.tile_h * g.tile_w;
-    const int hrow = g.halo_w * CIN;
-    for (int p = warp * ppw + lane / lpp; p < npx; p += 8 * ppw) {
-        const int dy = p / g.tile_w, dx = p - dy * g.tile_w;
-        const int oy = oy0 + dy, ox = ox0 + dx;
-        if (oy >= a.oh || ox >= a.ow) continue;
-        float acc[4] = {b4.x, b4.y, b4.z, b4.w};
-        const float *hp0 = halo + (dy * a.sh) * hrow + (dx * a.sw) * CIN;
-#pragma unroll
-        for (int ky = 0; ky < KH; ky++)
-#pragma unroll
-            for (int kx = 0; kx < KW; kx++)
-#pragma unroll
-                for (int ic = 0; ic < CIN; ic++) {
-                    const float xv = hp0[ky * a.dil * hrow + kx * a.dil * CIN + ic];
-                    const int k = (ky * KW + kx) * CIN + ic;
-                    acc[0] = madd<kStrict>(acc[0], xv, w[k][0]);
-                    acc[1] = madd<kStrict>(acc[1], xv, w[k][1]);
-                    acc[2] = madd<kStrict>(acc[2], xv, w[k][2]);
-                    acc[3] = madd<kStrict>(acc[3], xv, w[k][3]);
-                }
+    auto store = [&](int img, int oy, int ox, float (&acc)[4]) {
         epi_act_n<kStrict, 4>(a.act, acc, c0, a.cout);
         const long long m = ((long long)img * a.oh + oy) * a.ow + ox;
-        float *yr = a.y + m * a.y_stride + a.y_coff + c0;
         if (a.res) {
             const float4 r = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.r_stride + a.r_coff + c0));
             acc[0] = add_res<kStrict>(acc[0], r.x); acc[1] = add_res<kStrict>(acc[1], r.y);
             acc[2] = add_res<kStrict>(acc[2], r.z); acc[3] = add_res<kStrict>(acc[3], r.w);
         }
-        *reinterpret_cast<float4 *>(yr) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4 *>(a.y + m * a.y_stride + a.y_coff + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    };
+
+    int t = blockIdx.x;
+    if (t < ntiles) stage(t, 0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int i = 0; t < ntiles; t += gridDim.x, i++) {
+        const int tn = t + gridDim.x;
+        if (tn < ntiles) stage(tn, (i + 1) & 1);  // prefetch the next tile's halo
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // this tile's halo has landed
+        __syncthreads();
+        const float *hb = halo + (i & 1) * HN;
+        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
+        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int oy0 = ty * TH, ox0 = tx * TW;
+        // two pixels per thread per pass: 8 independent accumulator chains
+        for (int p = warp * ppw + lane / lpp; p < NPX; p += 2 * step) {
+            const int q = p + step;
+            const bool has_q = q < NPX;
+            const int dyp = p / TW, dxp = p - dyp * TW;
+            const int dyq = q / TW, dxq = q - dyq * TW;
+            const float *hp = hb + (dyp * S) * HROW + (dxp * S) * CIN;
+            const float *hq = hb + (dyq * S) * HROW + (dxq * S) * CIN;
+            float accp[4] = {b4.x, b4.y, b4.z, b4.w};
+            float accq[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int ky = 0; ky < KH; ky++)
+#pragma unroll
+                for (int kx = 0; kx < KW; kx++)
+#pragma unroll
+                    for (int ic = 0; ic < CIN; ic++) {
+                        constexpr int dummy = 0;
+                        (void)dummy;
+                        const int off = ky * HROW + kx * CIN + ic;
+                        const int k = (ky * KW + kx) * CIN + ic;
+                        const float xp = hp[off];
+                        const float xq = has_q ? hq[off] : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            accp[j] = madd<kStrict>(accp[j], xp, w[k][j]);
+                            accq[j] = madd<kStrict>(accq[j], xq, w[k][j]);
+                        }
+                    }
+            if (oy0 + dyp < a.oh && ox0 + dxp < a.ow) store(img, oy0 + dyp, ox0 + dxp, accp);
+            if (has_q && oy0 + dyq < a.oh && ox0 + dxq < a.ow) store(img, oy0 + dyq, ox0 + dxq, accq);
+        }
+        __syncthreads();  // every thread is done with this buffer before it is refilled
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 }  // namespace aie

@@ -38,6 +38,7 @@
 #include <cuda.h>
 
 #include <cstring>
+#include <type_traits>
 
 #include "k_simt.cuh"
 
@@ -474,7 +475,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // written back by the warp 8 lanes per 128-byte row segment so every
         // store (and residual load) instruction covers 4 whole rows instead
         // of 32 scattered 16-byte pieces; residual added after the activation
-        auto emit = [&](int col0, float (&v)[32]) {
+        // RES: 0 none, 1 residual tensor, 2 bilinear-sampled residual; a
+        // template argument so each layer's epilogue carries only its code
+        auto emit = [&](auto res_kind, int col0, float (&v)[32]) {
+            constexpr int RES = decltype(res_kind)::value;
             const int col = col0 + seg * 4;
             const bool vec = c.vec_y && col + 4 <= c.cout;
             {
@@ -502,15 +506,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int q = 0; q < 4; q++) {
                     const int i = 4 * h + q;
                     rv[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (c.res && mrow[i] >= 0) {
-                        const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
-                        if (vec) rv[q] = __ldg(reinterpret_cast<const float4 *>(rr));
-                        else {
-                            float t4[4] = {0.f, 0.f, 0.f, 0.f};
+                    if constexpr (RES == 2) {
+                        if (mrow[i] >= 0) rv[q] = bilinear_res4(c, mrow[i], col, vec);
+                    } else if constexpr (RES == 1) {
+                        if (mrow[i] >= 0) {
+                            const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
+                            if (vec) rv[q] = __ldg(reinterpret_cast<const float4 *>(rr));
+                            else {
+                                float t4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                            for (int l = 0; l < 4; l++)
-                                if (col + l < c.cout) t4[l] = __ldg(rr + l);
-                            rv[q] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                                for (int l = 0; l < 4; l++)
+                                    if (col + l < c.cout) t4[l] = __ldg(rr + l);
+                                rv[q] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                            }
                         }
                     }
                 }
@@ -520,7 +528,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const int r = i * 4 + (lane >> 3);
                     if (mrow[i] < 0) continue;
                     float4 x = *reinterpret_cast<const float4 *>(obuf + r * 128 + ((seg ^ (r & 7)) * 16));
-                    x.x += rv[q].x; x.y += rv[q].y; x.z += rv[q].z; x.w += rv[q].w;  // residual after act
+                    if constexpr (RES != 0) {
+                        x.x += rv[q].x; x.y += rv[q].y; x.z += rv[q].z; x.w += rv[q].w;  // residual after act
+                    }
                     float *yr = c.y + (long long)mrow[i] * c.y_stride + c.y_coff + col;
                     if (vec) {
                         *reinterpret_cast<float4 *>(yr) = x;
@@ -534,6 +544,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
             }
+        };
+
+        auto emit_any = [&](int col0, float (&v)[32]) {
+            if (!c.res) emit(std::integral_constant<int, 0>{}, col0, v);
+            else if (!c.res_mode) emit(std::integral_constant<int, 1>{}, col0, v);
+            else emit(std::integral_constant<int, 2>{}, col0, v);
         };
 
         uint32_t k = 0;  // tiles this group has drained: the phase of its buffer
@@ -567,7 +583,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     float v[32];
 #pragma unroll
                     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-                    emit(nbase + c0, v);
+                    emit_any(nbase + c0, v);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -611,7 +627,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 }
                             }
                         }
-                        emit(nbase + c0, v);
+                        emit_any(nbase + c0, v);
                     }
                     __syncwarp();
                     if (lane == 0) *ticket = 0;  // reusable by the next launch

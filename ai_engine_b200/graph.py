@@ -63,7 +63,7 @@ class Model:
     """Load-time lowering + per-batch execution of a conv graph on one GPU."""
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
-                 in_hwc: Tuple[int, int, int], *, math: str = "auto", device=None):
+                 in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -71,16 +71,39 @@ class Model:
         self.output = self.graph[-1][1]
         self.ops: List[OpRecord] = []
         self.bufs: Dict[str, torch.Tensor] = {}
+        # Resize -> Conv(res) fusion (fuse=True): a bilinear resize whose
+        # output only feeds the next conv's residual is folded into that
+        # conv's epilogue (the residual is sampled from the low-resolution
+        # tensor directly).  Off by default: on B200 the per-row bilinear
+        # gathers make the issue-bound GEMM epilogue slower than a separate
+        # resize pass for the FPN's 32-64 channel laterals.
+        uses: Dict[str, int] = {}
+        for op in self.graph:
+            for t in (op[2], op[4]):
+                if t is not None:
+                    uses[t] = uses.get(t, 0) + 1
+        fused_resize: Dict[str, str] = {}  # resize output -> its source
+        if fuse:
+            for op in self.graph:
+                if op[0] == "resize" and op[4] is None and uses.get(op[1], 0) == 1 and op[1] != self.output:
+                    fused_resize[op[1]] = op[2]
         with torch.cuda.device(self.device):
             self.bufs["input"] = torch.empty((n, *in_hwc), dtype=torch.float32, device=self.device)
             for op in self.graph:
                 kind, out, src = op[0], op[1], op[2]
                 h, w, c = self.shapes[src]
+                if kind == "resize" and out in fused_resize:
+                    continue
                 rec = OpRecord(kind, out, src)
                 if kind == "conv":
                     rec.conv, rec.res = op[3], op[4]
+                    res_resize = None
+                    if rec.res in fused_resize:
+                        lo = fused_resize[rec.res]
+                        res_resize = (self.shapes[lo][0], self.shapes[lo][1], "half_pixel")
+                        rec.res = lo
                     rec.plan = ConvPlan(rec.conv, n, h, w, has_res=rec.res is not None, math=math,
-                                        device=self.device)
+                                        res_resize=res_resize, device=self.device)
                     wt, b = weights[out]
                     rec.plan.load_weights(wt, b)
                 else:

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define AIE_ABI_VERSION 1
+#define AIE_ABI_VERSION 2
 
 #ifndef AIE_API
 #define AIE_API __attribute__((visibility("default")))
@@ -136,7 +136,20 @@ typedef struct aie_conv_desc {
     uint32_t in_stride, in_coff;
     uint32_t res_stride, res_coff;
     uint32_t out_stride, out_coff;
+    /* residual source: AIE_RES_TENSOR reads a tensor of the output's shape;
+     * AIE_RES_BILINEAR_* reads a [n][res_h][res_w][cout] tensor and samples
+     * it bilinearly at every output pixel (crates/ai-core/src/reference/
+     * resize.rs:5-42), i.e. the Resize -> Conv(res) pair of an FPN merge
+     * fused into the conv epilogue. */
+    int32_t res_mode;
+    uint32_t res_h, res_w;
 } aie_conv_desc;
+
+typedef enum aie_res_mode {
+    AIE_RES_TENSOR = 0,
+    AIE_RES_BILINEAR_HALF_PIXEL = 1,
+    AIE_RES_BILINEAR_ASYMMETRIC = 2
+} aie_res_mode;
 
 typedef struct aie_plan_info {
     int32_t kernel;            /* aie_kernel */

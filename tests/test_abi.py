@@ -34,13 +34,13 @@ def test_header_declares_the_binding(lib):
 def test_every_declared_symbol_is_exported(lib):
     for name in header_symbols():
         assert hasattr(lib, name), name
-    assert lib.aie_abi_version() == 1
+    assert lib.aie_abi_version() == 2
     assert b"sm_100a" in lib.aie_build_info()
 
 
 def test_struct_sizes_match_header(lib):
     # 11 u32 + pad[4] + 4 i32 + 7 u32 = 26 * 4 bytes
-    assert C.sizeof(_lib.ConvDesc) == 26 * 4
+    assert C.sizeof(_lib.ConvDesc) == 29 * 4
     assert C.sizeof(_lib.PlanInfo) == 8 * 4 + 6 * 8
 
 

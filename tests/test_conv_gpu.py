@@ -244,17 +244,22 @@ def test_canary_no_write_outside_output(cuda_ok):
     assert (buf[n_out:] == 1234.5).all()
 
 
-def test_resize_bilinear_bit_exact(cuda_ok):
-    """GPU resize (+ fused add) equals the CPU restatement bit for bit."""
+@pytest.mark.parametrize("c,ih,iw,oh,ow", [
+    (6, 5, 9, 10, 18), (4, 5, 9, 10, 18), (3, 7, 5, 14, 10), (1, 5, 9, 20, 36), (1, 5, 9, 13, 23),
+    (1, 40, 72, 160, 288), (8, 9, 7, 4, 3)])
+def test_resize_bilinear_bit_exact(cuda_ok, c, ih, iw, oh, ow):
+    """GPU resize (+ fused add) equals the CPU restatement bit for bit:
+    vector channel groups, ragged channel tails, the 4-pixel single-channel
+    path with aligned and ragged widths, and downsampling."""
     from ai_engine_b200 import resize_bilinear
     from oracle import XorShift32
-    rng = XorShift32(31)
-    x = rng.vec_f32(2 * 5 * 9 * 6).reshape(2, 5, 9, 6)
-    add = rng.vec_f32(2 * 10 * 18 * 6).reshape(2, 10, 18, 6)
+    rng = XorShift32(31 + c + ow)
+    x = rng.vec_f32(2 * ih * iw * c).reshape(2, ih, iw, c)
+    add = rng.vec_f32(2 * oh * ow * c).reshape(2, oh, ow, c)
     for mode in ["half_pixel", "asymmetric"]:
-        want = oracle.resize_bilinear(x, 10, 18, mode)
-        got = resize_bilinear(torch.from_numpy(x).cuda(), 10, 18, mode).cpu().numpy()
+        want = oracle.resize_bilinear(x, oh, ow, mode)
+        got = resize_bilinear(torch.from_numpy(x).cuda(), oh, ow, mode).cpu().numpy()
         assert np.array_equal(got, want)
-    want = oracle.add(oracle.resize_bilinear(x, 10, 18), add)
-    got = resize_bilinear(torch.from_numpy(x).cuda(), 10, 18, add=torch.from_numpy(add).cuda()).cpu().numpy()
+    want = oracle.add(oracle.resize_bilinear(x, oh, ow), add)
+    got = resize_bilinear(torch.from_numpy(x).cuda(), oh, ow, add=torch.from_numpy(add).cuda()).cpu().numpy()
     assert np.array_equal(got, want)

@@ -208,3 +208,43 @@ def test_tf32_partial_tiles_residual(cuda_ok, n, h, w, cin, cout):
     op3 = Conv2d.same(cin, cout, 3, 2, "relu")
     x, wt, b, res = case_tensors(op3, n, h, w, 94 + cout, True)
     check_tf32(op3, x, wt, b, res)
+
+
+@pytest.mark.parametrize("math", ["fp32_strict", "ffma", "tf32"])
+@pytest.mark.parametrize("kind", ["pw", "igemm"])
+@pytest.mark.parametrize("mode", ["half_pixel", "asymmetric"])
+def test_fused_bilinear_residual(cuda_ok, math, kind, mode):
+    """Resize -> Conv(res) fused into the conv epilogue equals the unfused
+    pair (oracle resize, then oracle conv with that residual): bit for bit
+    in fp32_strict mode."""
+    import oracle
+    from oracle import XorShift32
+    op = Conv2d.pointwise(32, 40, "relu") if kind == "pw" else Conv2d.same(32, 40, 3, 1, "hardswish")
+    n, h, w, rh, rw = 2, 18, 26, 9, 13
+    rng = XorShift32(777)
+    x = rng.vec_f32(n * h * w * 32).reshape(n, h, w, 32)
+    wt = rng.vec_f32(op.cout * op.cin * op.kh * op.kw)
+    b = rng.vec_f32(op.cout)
+    lo = rng.vec_f32(n * rh * rw * op.cout).reshape(n, rh, rw, op.cout)
+    up = oracle.resize_bilinear(lo, h, w, mode)
+    want, scale = oracle_conv(op, x, wt, b, up)
+    plan = ConvPlan(op, n, h, w, has_res=True, math=math, res_resize=(rh, rw, mode)).load_weights(wt, b)
+    got = plan(torch.from_numpy(x).cuda(), torch.from_numpy(lo).cuda()).cpu().numpy()
+    if math == "fp32_strict":
+        assert np.array_equal(got, want)
+    else:
+        assert normalised_error(got, want, scale) <= (TOL_TF32 if math == "tf32" else TOL_FFMA)
+
+
+def test_graph_fusion_matches_unfused(cuda_ok):
+    """The whole benchmark network with Resize->Conv fusion equals the same
+    network run op by op (FFMA path, so the only difference is the fusion)."""
+    from ai_engine_b200 import segnet
+    from ai_engine_b200.graph import Model
+    g = segnet.build_graph()
+    wts = segnet.init_weights(g)
+    x = torch.from_numpy(segnet.synthetic_input(2, seed=3)).cuda()
+    a = Model(g, wts, 2, (segnet.H, segnet.W, 3), math="fp32_strict", fuse=True)
+    b = Model(g, wts, 2, (segnet.H, segnet.W, 3), math="fp32_strict", fuse=False)
+    assert len(a.ops) < len(b.ops)
+    assert torch.equal(a.infer(x), b.infer(x))
