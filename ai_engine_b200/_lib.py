@@ -43,7 +43,7 @@ class ConvDesc(C.Structure):
 class PlanInfo(C.Structure):
     _fields_ = [("kernel", C.c_int32), ("math", C.c_int32), ("oh", C.c_uint32), ("ow", C.c_uint32),
                 ("split_k", C.c_uint32), ("tile_m", C.c_uint32), ("tile_n", C.c_uint32),
-                ("reserved", C.c_uint32), ("weight_bytes", C.c_uint64), ("bias_bytes", C.c_uint64),
+                ("variant", C.c_uint32), ("weight_bytes", C.c_uint64), ("bias_bytes", C.c_uint64),
                 ("workspace_bytes", C.c_uint64), ("flops", C.c_uint64), ("min_bytes", C.c_uint64),
                 ("grid_ctas", C.c_uint64)]
 

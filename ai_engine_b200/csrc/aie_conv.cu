@@ -280,6 +280,7 @@ extern "C" int aie_conv_plan_info(const aie_plan *p, aie_plan_info *info)
     info->split_k = p->split;
     info->tile_m = p->tile_m;
     info->tile_n = p->tile_n;
+    info->variant = p->stem ? 1u : 0u;
     info->weight_bytes = p->wbytes;
     info->bias_bytes = p->bbytes;
     info->workspace_bytes = p->wsbytes;

@@ -136,9 +136,7 @@ class Model:
                 resize_bilinear(src, oh, ow, add=self.bufs[r.res] if r.res else None, out=out, stream=stream)
         return self.bufs[self.output]
 
-    def capture(self):
-        """Capture the whole batch as one CUDA graph (replaces the per-op
-        Python dispatch; the kernels are the same)."""
+    def _capture_one(self):
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
@@ -147,8 +145,13 @@ class Model:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             self.record()
-        self.graph_exec = g
         return g
+
+    def capture(self):
+        """Capture the whole batch as one CUDA graph (replaces the per-op
+        Python dispatch; the kernels are the same)."""
+        self.graph_exec = self._capture_one()
+        return self.graph_exec
 
     def infer(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
         if x is not None:
@@ -159,5 +162,73 @@ class Model:
             self.record()
         return self.bufs[self.output]
 
+    # -- pipelined host -> device -> host ------------------------------------------
+    def capture_slots(self, slots: int = 2):
+        """One CUDA graph per I/O slot: graph s reads input slot s and writes
+        output slot s; the intermediate activations are shared, so the graphs
+        run one after another on the compute stream while the copies of the
+        neighbouring batches use the other slots."""
+        if slots < 2:
+            raise ValueError("pipelining needs at least two slots")
+        in0, out0 = self.bufs["input"], self.bufs[self.output]
+        self.in_slots = [in0] + [torch.empty_like(in0) for _ in range(slots - 1)]
+        self.out_slots = [out0] + [torch.empty_like(out0) for _ in range(slots - 1)]
+        self.slot_graphs = []
+        try:
+            for s in range(slots):
+                self.bufs["input"], self.bufs[self.output] = self.in_slots[s], self.out_slots[s]
+                self.slot_graphs.append(self._capture_one())
+        finally:
+            self.bufs["input"], self.bufs[self.output] = in0, out0
+        self._copy_in = torch.cuda.Stream(device=self.device)
+        self._copy_out = torch.cuda.Stream(device=self.device)
+
+    def run_pipelined(self, host_in: Sequence[torch.Tensor], host_out: Sequence[torch.Tensor], stream=None):
+        """Run batch k = host_in[k] (pinned [n, h, w, c] frames) through the
+        graph into host_out[k], end to end.  ai-gpu-runtime uploads, runs and
+        reads back one frame per call (upload_input, infer and read_output,
+        crates/ai-gpu-runtime/src/model.rs:387-470); here the upload of batch k+1 and the read-back of batch
+        k-1 run on their own copy streams while batch k computes, so the
+        steady state costs max(upload, compute, read-back) per batch.
+
+        Asynchronous on `stream` (default: current stream): the outputs are
+        complete once that stream is synchronised."""
+        if len(host_in) != len(host_out):
+            raise ValueError("one output buffer per input batch")
+        if not getattr(self, "slot_graphs", None):
+            self.capture_slots()
+        S = len(self.slot_graphs)
+        compute = torch.cuda.current_stream(self.device) if stream is None else stream
+        cin, cout = self._copy_in, self._copy_out
+        h2d = [torch.cuda.Event() for _ in range(S)]
+        done = [torch.cuda.Event() for _ in range(S)]
+        d2h = [torch.cuda.Event() for _ in range(S)]
+        start = torch.cuda.Event()
+        start.record(compute)
+        cin.wait_event(start)
+        cout.wait_event(start)
+        for k, (hi, ho) in enumerate(zip(host_in, host_out)):
+            s = k % S
+            if k >= S:
+                cin.wait_event(done[s])      # batch k-S no longer reads input slot s
+            with torch.cuda.stream(cin):
+                self.in_slots[s].copy_(hi, non_blocking=True)
+            h2d[s].record(cin)
+            compute.wait_event(h2d[s])
+            if k >= S:
+                compute.wait_event(d2h[s])   # output slot s of batch k-S has been read back
+            with torch.cuda.stream(compute):
+                self.slot_graphs[s].replay()
+            done[s].record(compute)
+            cout.wait_event(done[s])
+            with torch.cuda.stream(cout):
+                ho.copy_(self.out_slots[s], non_blocking=True)
+            d2h[s].record(cout)
+        for s in range(min(S, len(host_in))):
+            compute.wait_event(d2h[s])
+            compute.wait_event(h2d[s])
+        return host_out
+
     def release(self):
         self.graph_exec = None
+        self.slot_graphs = []

@@ -77,7 +77,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.1)
+            self._stop.wait(0.02)
 
     def __enter__(self):
         if self._h is not None:
@@ -102,9 +102,10 @@ class ClockSampler:
 _CPU_MODEL = {}
 
 
-def cpu_baseline(frames: int, threads: int):
-    """ai-cpu restatement, throughput mode (one frame per core), on a sample
-    of `frames` frames of the same workload."""
+def cpu_baseline(frames: int, threads: int, min_seconds: float = 0.0):
+    """ai-cpu restatement, throughput mode (one frame per core): `frames`
+    frames of the same workload per pass, passes repeated until at least
+    `min_seconds` have elapsed.  Returns (frames/s, seconds, frames run)."""
     from ai_engine_b200 import segnet
     from oracle.graph import OracleModel
     if "m" not in _CPU_MODEL:
@@ -115,10 +116,15 @@ def cpu_baseline(frames: int, threads: int):
     m, x = _CPU_MODEL["m"], _CPU_MODEL["x"]
     if x.shape[0] < frames:
         x = _CPU_MODEL["x"] = segnet.synthetic_input(frames, seed=1)
+    done = 0
     t0 = time.perf_counter()
-    m.run_batch(x[:frames], threads=threads)
-    dt = time.perf_counter() - t0
-    return frames / dt, dt
+    while True:
+        m.run_batch(x[:frames], threads=threads)
+        done += frames
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    return done / dt, dt, done
 
 
 def cpu_model_name():
@@ -142,7 +148,7 @@ def run_reference(args, rank):
     vals = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        v, _ = cpu_baseline(frames, threads)
+        v, _, _ = cpu_baseline(frames, threads)
         vals.append(v)
     wall = time.perf_counter() - t0
     value = statistics.median(vals)
@@ -168,7 +174,7 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--math", default="auto", choices=["auto", "ffma", "tf32", "fp32_strict"])
@@ -193,6 +199,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     from ai_engine_b200 import segnet
+    from ai_engine_b200.conv import resize_bilinear
     from ai_engine_b200.graph import Model
 
     n = args.batch
@@ -215,74 +222,66 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- warm-up
+    # ---- warm-up (eager and captured)
     for _ in range(max(args.warmup, 3)):
         model.record()
+    model.capture()
+    for _ in range(max(args.warmup, 3)):
+        model.infer()
     torch.cuda.synchronize()
 
-    # ---- timed region: K steps, per-op CUDA events on the launching stream
-    ops = model.ops
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    # ---- timed region (value): K steps of the captured batch graph, inputs
+    # resident in HBM, CUDA events on the replaying stream
     sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     with sampler:
-        for k in range(args.steps):
-            ev = evs[k]
-            ev[0].record(stream)
-            for i, r in enumerate(ops):
-                src, out = model.bufs[r.src], model.bufs[r.out]
-                if r.kind == "conv":
-                    r.plan(src, model.bufs[r.res] if r.res else None, out=out)
-                else:
-                    from ai_engine_b200.conv import resize_bilinear
-                    resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
-                ev[i + 1].record(stream)
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.infer()
+        e1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    total_ms = evs[0][0].elapsed_time(evs[-1][-1])
-    total_ms = max_over_ranks(total_ms)
-    frames = n * world * args.steps
-    value = frames / (total_ms / 1000.0)
+    total_ms = max_over_ranks(e0.elapsed_time(e1))
+    value = n * world * args.steps / (total_ms / 1000.0)
 
-    # per-op durations (ms) averaged over the K timed steps
+    # ---- per-op breakdown: the same ops issued eagerly, one CUDA event
+    # after each launch on the launching stream (roofline of the top kernel)
+    ops = model.ops
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        ev = evs[k]
+        ev[0].record(stream)
+        for i, r in enumerate(ops):
+            src, out = model.bufs[r.src], model.bufs[r.out]
+            if r.kind == "conv":
+                r.plan(src, model.bufs[r.res] if r.res else None, out=out)
+            else:
+                resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
+            ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    eager_ms = max_over_ranks(evs[0][0].elapsed_time(evs[-1][-1]))
+    eager_value = n * world * args.steps / (eager_ms / 1000.0)
     per_op = np.zeros(len(ops))
     for ev in evs:
         for i in range(len(ops)):
             per_op[i] += ev[i].elapsed_time(ev[i + 1])
     per_op /= args.steps
 
-    # ---- CUDA-graph replay of the same step (launch overhead removed)
-    graph_value = None
-    try:
-        model.capture()
-        for _ in range(3):
-            model.infer()
-        torch.cuda.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            model.infer()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        gms = max_over_ranks(e0.elapsed_time(e1))
-        graph_value = n * world * args.steps / (gms / 1000.0)
-    except Exception as e:  # reported, not fatal
-        graph_value = f"capture failed: {e!r}"
-
-    # ---- end to end through the public API: pinned host frames in, mask out
-    for _ in range(2):
-        model.infer(x_host.to(dev, non_blocking=True))
-        out_host.copy_(model.bufs[model.output], non_blocking=True)
+    # ---- end to end through the public API: every step uploads its pinned
+    # host frames and reads its mask back (Model.run_pipelined overlaps the
+    # copies of neighbouring batches with compute)
+    outs_host = [out_host, torch.empty_like(out_host).pin_memory()]
+    model.run_pipelined([x_host] * 3, [outs_host[k % 2] for k in range(3)])
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        model.bufs["input"].copy_(x_host, non_blocking=True)
-        model.infer()
-        out_host.copy_(model.bufs[model.output], non_blocking=True)
+    model.run_pipelined([x_host] * args.steps, [outs_host[k % 2] for k in range(args.steps)])
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -344,16 +343,15 @@ def main():
         "roofline": roof,
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(x_host.numel() * 4),
                 "d2h_bytes_per_step": int(out_host.numel() * 4)},
-        "graph_replay_value": round(graph_value, 2) if isinstance(graph_value, float) else graph_value,
+        "eager_value": round(eager_value, 2),
         "gpu_launches": len(ops) * args.steps,
         "clocks": sampler.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        frames = 128
-        v, dt = cpu_baseline(frames, threads)
+        v, dt, done = cpu_baseline(2 * threads, threads, min_seconds=10.0)
         line["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": f"{frames} frames of the same workload, one frame per core, "
+                                "sample": f"{done} frames of the same workload, one frame per core, "
                                           f"{dt:.1f} s on {cpu_model_name()}"}
     if args.layers:
         for l in layers:

@@ -77,6 +77,13 @@ def test_kernel_choice_mirrors_lower_op(lib):
     assert st == 0 and i.kernel == _lib.KERNEL_IGEMM and (i.oh, i.ow) == (4, 4)
 
 
+def test_stem_variant_is_reported(lib):
+    st, i = plan(lib, ih=160, iw=288, cin=3, cout=32, sh=2, sw=2)
+    assert st == 0 and i.kernel == _lib.KERNEL_IGEMM and i.variant == 1
+    st, i = plan(lib, cin=6, cout=32)
+    assert st == 0 and i.variant == 0
+
+
 def test_out_hw_and_work_accounting(lib):
     st, i = plan(lib, ih=160, iw=288, cin=16, cout=16, sh=2, sw=2, n=2)
     assert st == 0 and (i.oh, i.ow) == (80, 144)
