@@ -129,7 +129,7 @@ class ConvPlan:
         info = _lib.PlanInfo()
         check(self.lib.aie_conv_plan_info(h, C.byref(info)), "aie_conv_plan_info")
         self.info = info
-        self.kernel = "stem" if info.variant == 1 else KERNEL_NAME[info.kernel]
+        self.kernel = "stem" if info.variant in (1, 2) else KERNEL_NAME[info.kernel]
         self.math = MATH_NAME[info.math]
         self.oh, self.ow = info.oh, info.ow
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())

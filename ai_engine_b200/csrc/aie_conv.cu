@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "k_simt.cuh"
 #include "k_tc.cuh"
+#include "k_stem_tc.cuh"
 
 using namespace aie;
 
@@ -65,7 +66,8 @@ struct aie_plan {
     uint64_t wbytes, bbytes, wsbytes;
     uint64_t flops, min_bytes, grid;
     TcGeom tc;         // tensor-core launch geometry (TF32 only)
-    bool stem;         // small-cin direct conv (FFMA), see stem_kernel
+    bool stem;         // small-cin direct conv, see stem_kernel / stem_tc_kernel
+    bool stem_tc;      // ... on the tensor cores (TF32, cin <= 3, cout = 32)
     StemGeom sg;
     uint32_t stem_smem;
 };
@@ -187,9 +189,21 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
         return fail(AIE_E_UNSUPPORTED, "a bilinear residual is fused into the GEMM kernels only");
     }
 
+    // Small-cin 3x3 convs (the stem) take a direct-conv kernel: the GEMM's
+    // per-tap K tiles would be mostly padding (cin=3 -> 3 of 32 lanes).
+    const bool stem_shape = p->kernel == AIE_KERNEL_IGEMM && d.res_mode == AIE_RES_TENSOR && d.cin <= 4 &&
+                            d.kh == 3 && d.kw == 3 && d.dil == 1 && d.sh == d.sw && (d.sh == 1 || d.sh == 2) &&
+                            d.cout % 4 == 0 && d.cout / 4 >= 1 && d.cout / 4 <= 32 && 32 % (d.cout / 4) == 0;
+    // cin <= 3 (K = 27 fits one 32-wide K row), cout = 32, no residual: the
+    // tensor-core variant, an im2col GEMM of K = 32
+    const bool stem_tc_shape = stem_shape && d.cin <= 3 && d.cout == (uint32_t)kStemCout && !d.has_res;
+
     // Math.
     const char *why = "";
-    if (p->kernel == AIE_KERNEL_DW || p->kernel == AIE_KERNEL_PW_DOT) {
+    if (stem_tc_shape && (d.math == AIE_MATH_AUTO || d.math == AIE_MATH_TF32)) {
+        p->math = AIE_MATH_TF32;
+        p->stem_tc = true;
+    } else if (p->kernel == AIE_KERNEL_DW || p->kernel == AIE_KERNEL_PW_DOT) {
         p->math = d.math == kMathStrict ? kMathStrict : AIE_MATH_FFMA;
         if (d.math == AIE_MATH_TF32) {
             delete p;
@@ -217,7 +231,7 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     } else if (p->kernel == AIE_KERNEL_PW_DOT) {
         p->wbytes = (uint64_t)d.cout * d.cin * 4;
         p->grid = (uint64_t)((p->M + 255) / 256);
-    } else if (p->math == AIE_MATH_TF32) {
+    } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         p->cin_pad = (int)rup(d.cin, 4);
         p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
         int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.pad[0], d.pad[1], p->oh, p->ow,
@@ -234,11 +248,8 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     } else {
         p->wn = (int)cpad4;
         p->wbytes = (uint64_t)taps * d.cin * p->wn * 4;
-        // small-cin 3x3 convs (the stem) take the direct-conv kernel: the
-        // GEMM's K tiles would be mostly padding (cin=3 -> 3 of 16 lanes)
-        const uint32_t lpp = d.cout / 4;
-        if (p->kernel == AIE_KERNEL_IGEMM && d.res_mode == AIE_RES_TENSOR && d.cin <= 4 && d.kh == 3 && d.kw == 3 && d.dil == 1 &&
-            d.sh == d.sw && (d.sh == 1 || d.sh == 2) && d.cout % 4 == 0 && lpp >= 1 && lpp <= 32 && 32 % lpp == 0) {
+        // (the tensor-core stem reads the same [tap][cin][wn] packing)
+        if (stem_shape) {
             p->stem = true;
             StemGeom &g = p->sg;
             g.tile_h = 16;
@@ -280,7 +291,7 @@ extern "C" int aie_conv_plan_info(const aie_plan *p, aie_plan_info *info)
     info->split_k = p->split;
     info->tile_m = p->tile_m;
     info->tile_n = p->tile_n;
-    info->variant = p->stem ? 1u : 0u;
+    info->variant = p->stem_tc ? 2u : p->stem ? 1u : 0u;
     info->weight_bytes = p->wbytes;
     info->bias_bytes = p->bbytes;
     info->workspace_bytes = p->wsbytes;
@@ -338,7 +349,7 @@ extern "C" int aie_conv_pack_weights(const aie_plan *p, int32_t wfmt, const floa
             for (uint32_t t = 0; t < taps; t++) pw[(size_t)t * cpad + ch] = w[(size_t)ch * taps + t];
     } else if (p->kernel == AIE_KERNEL_PW_DOT) {
         memcpy(pw.data(), w, (size_t)d.cout * d.cin * 4);  // [cout][cin]
-    } else if (p->math == AIE_MATH_TF32) {
+    } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         // [tap][cout][cin_pad]: K-major rows for the tcgen05 B operand
         for (uint32_t t = 0; t < taps; t++)
             for (uint32_t oc = 0; oc < d.cout; oc++)
@@ -438,10 +449,18 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         }
         if (p->strict) pw_dot_kernel<true><<<(unsigned)p->grid, 256, smem, s>>>(a);
         else pw_dot_kernel<false><<<(unsigned)p->grid, 256, smem, s>>>(a);
-    } else if (p->math == AIE_MATH_TF32) {
+    } else if (p->stem_tc && a.vec_y) {
+        int rc;
+        const int cin = (int)p->d.cin;
+        if (p->d.sh == 1) rc = cin == 1 ? stem_tc_launch<1, 1>(a, p->sg, s) : cin == 2 ? stem_tc_launch<2, 1>(a, p->sg, s)
+                                                                                      : stem_tc_launch<3, 1>(a, p->sg, s);
+        else rc = cin == 1 ? stem_tc_launch<1, 2>(a, p->sg, s) : cin == 2 ? stem_tc_launch<2, 2>(a, p->sg, s)
+                                                                         : stem_tc_launch<3, 2>(a, p->sg, s);
+        if (rc) return cuda_fail(cudaGetLastError(), "tensor-core stem setup");
+    } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         int rc = tc_launch(p->tc, a, workspace, s, t_err, sizeof t_err);
         if (rc) return rc;
-    } else if (p->stem && a.vec_y && (a.y_stride % 4 == 0) && !(a.res && (a.r_stride % 4 || a.r_coff % 4)) &&
+    } else if (p->stem && !p->stem_tc && a.vec_y && (a.y_stride % 4 == 0) && !(a.res && (a.r_stride % 4 || a.r_coff % 4)) &&
                ((uintptr_t)w % 16 == 0)) {
         const unsigned stem_grid = (unsigned)std::min<uint64_t>(p->grid, (uint64_t)tc_sm_count());
         const unsigned smem = 2 * p->stem_smem;

@@ -1,0 +1,232 @@
+// Tensor-core stem: a 3x3 conv with cin <= 3 and cout = 32 (the network's
+// first layer, crates/ai-cpu/src/kernels/conv.rs's conv_std on a 3-channel
+// frame) as a TF32 GEMM with K = 9*cin <= 27, zero-padded to 32 so that
+// one im2col row is exactly one 128-byte swizzle row.
+//
+// Per 16x16 output tile (256 pixels = two M=128 MMA tiles):
+//   1. the input halo is staged with 4-byte cp.async (zero-fill = padding),
+//      double-buffered across tiles;
+//   2. each thread writes its pixel's 32-value im2col row into the A
+//      operand (K-major, 128-byte swizzle) -- 27 shared loads, 8 stores;
+//   3. one thread issues 2 x 4 tcgen05.mma (M=128, N=32, K=8) into TMEM;
+//   4. each warp drains its 32 TMEM lanes, adds bias, applies the
+//      activation, transposes through its own A rows and writes 512-byte
+//      contiguous pieces of the NHWC output.
+// Three CTAs share an SM so their phases overlap.  Every wait is bounded.
+#pragma once
+
+namespace aie {
+
+constexpr int kStemCout = 32;
+constexpr int kStemTile = 16;
+constexpr int kStemThreads = 256;                 // one thread per output pixel of a tile
+constexpr uint32_t kStemABytes = 256 * 128;       // im2col rows; also the epilogue staging
+constexpr uint32_t kStemBBytes = kStemCout * 128; // weights [n][k], K-major
+constexpr uint32_t kStemTmemCols = 64;            // two 128 x 32 fp32 accumulators
+
+template <int CIN, int S>
+struct StemTcLayout {
+    static constexpr int HH = (kStemTile - 1) * S + 3, HW = HH;
+    static constexpr int HROW = HW * CIN, HN = HH * HROW;
+    static constexpr uint32_t kHaloOff = kStemABytes + kStemBBytes;
+    static constexpr uint32_t kHaloFloats = (HN + 3) / 4 * 4;
+    static constexpr uint32_t kBiasOff = kHaloOff + 2 * kHaloFloats * 4;
+    static constexpr uint32_t kBarOff = kBiasOff + kStemCout * 4;
+    static constexpr uint32_t kBytes = kBarOff + 16 + 1024;  // + slack to 1024-align the base
+};
+
+// byte offset of element (row, k) in a K-major operand with 128-byte rows
+// and the 128-byte swizzle (16-byte chunk index XOR row % 8)
+__device__ __forceinline__ uint32_t sw128_off(int row, int k)
+{
+    return (uint32_t)(row * 128 + ((((k >> 2) ^ row) & 7) << 4) + ((k & 3) << 2));
+}
+
+template <int CIN, int S>
+__global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs a, const StemGeom g)
+{
+    using L = StemTcLayout<CIN, S>;
+    constexpr int K = 9 * CIN;
+    static_assert(K <= 32, "im2col row must fit one 128-byte swizzle row");
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + kStemABytes;
+    float *halo = reinterpret_cast<float *>(smem + L::kHaloOff);
+    float *sbias = reinterpret_cast<float *>(smem + L::kBiasOff);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kBarOff + 8);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tiles_per_img = g.tiles_x * g.tiles_y;
+    const int ntiles = a.n * tiles_per_img;
+
+    auto stage = [&](int t, int buf) {
+        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
+        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int iy0 = ty * kStemTile * S - a.pt, ix0 = tx * kStemTile * S - a.pl;
+        const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff;
+        float *dst = halo + buf * L::kHaloFloats;
+        for (int i = tid; i < L::HN; i += kStemThreads) {
+            const int cc = i % CIN, p = i / CIN;
+            const int hy = p / L::HW, hx = p - hy * L::HW;
+            const int iy = iy0 + hy, ix = ix0 + hx;
+            const bool ok = iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
+            const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cc : xb;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst + i)), "l"(src),
+                         "r"(ok ? 4 : 0)
+                         : "memory");
+        }
+    };
+
+    // B operand: packed weights [k][wn] -> rows n (output channel), K-major
+    for (int i = tid; i < kStemCout * 32; i += kStemThreads) {
+        const int n = i >> 5, k = i & 31;
+        *reinterpret_cast<float *>(sB + sw128_off(n, k)) = k < K ? __ldg(a.w + k * a.wn + n) : 0.0f;
+    }
+    if (tid < kStemCout) sbias[tid] = __ldg(a.bias + tid);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kStemTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t idesc = idesc_tf32(128, kStemCout);
+    const uint64_t bdesc = smem_desc_sw128(smem_u32(sB));
+
+    uint32_t phase = 0;
+    bool failed = false, mma_pending = false;
+    int t = blockIdx.x;
+    if (t < ntiles) stage(t, 0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int i = 0; t < ntiles; t += gridDim.x, i++) {
+        const int tn = t + gridDim.x;
+        if (tn < ntiles) stage(tn, (i + 1) & 1);  // prefetch the next tile's halo
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // this tile's halo has landed
+        tc_fence_before();
+        if (__syncthreads_or(failed)) break;
+        tc_fence_after();
+
+        // ---- im2col: this thread's pixel -> A row `tid`, k = (ky*3 + kx)*CIN + ic
+        {
+            const float *hp = halo + (i & 1) * L::kHaloFloats + (tid >> 4) * S * L::HROW + (tid & 15) * S * CIN;
+            float v[32];
+#pragma unroll
+            for (int k = 0; k < 32; k++) {
+                if (k < K) {
+                    const int tap = k / CIN, ic = k - tap * CIN;
+                    v[k] = hp[(tap / 3) * L::HROW + (tap % 3) * CIN + ic];
+                } else {
+                    v[k] = 0.0f;
+                }
+            }
+            uint8_t *row = sA + tid * 128;
+#pragma unroll
+            for (int c = 0; c < 8; c++)
+                *reinterpret_cast<float4 *>(row + (((c ^ tid) & 7) << 4)) =
+                    make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // A visible to the tensor core
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {
+#pragma unroll
+            for (int m = 0; m < 2; m++) {
+                const uint64_t adesc = smem_desc_sw128(smem_u32(sA + m * (kStemABytes / 2)));
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    mma_tf32(tmem + (uint32_t)(m * kStemCout), adesc + 2 * kk, bdesc + 2 * kk, idesc, kk > 0);
+            }
+            mma_commit(bar);
+        }
+        mma_pending = true;
+        // warp-uniform outcome: the TMEM loads below are warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait(bar, phase))) {
+            if (lane == 0) report_error(0x03000001u);
+            failed = true;
+            continue;  // the next tile's barrier turns this into a CTA-wide exit
+        }
+        mma_pending = false;
+        phase ^= 1;
+        tc_fence_after();
+
+        // ---- epilogue: TMEM lanes (warp%4)*32.., accumulator warp/4 -> pixel
+        // tid, in two halves of 16 channels; staged in this warp's own A rows
+        // (free once the MMA completed), 128-byte swizzled
+        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * kStemCout);
+        uint8_t *srow = sA + tid * 128;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            uint32_t r[16];
+            tmem_ld16_issue(taddr + 16 * h, r);
+            tmem_wait16(r);
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                const float4 b4 = *reinterpret_cast<const float4 *>(sbias + 16 * h + j);
+                o[j] = __uint_as_float(r[j]) + b4.x;
+                o[j + 1] = __uint_as_float(r[j + 1]) + b4.y;
+                o[j + 2] = __uint_as_float(r[j + 2]) + b4.z;
+                o[j + 3] = __uint_as_float(r[j + 3]) + b4.w;
+            }
+            act_apply_n<16>(a.act, o);
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                *reinterpret_cast<float4 *>(srow + ((((4 * h + c) ^ tid) & 7) << 4)) =
+                    make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        }
+        __syncwarp();
+        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
+        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int oy0 = ty * kStemTile, ox0 = tx * kStemTile;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int f = j * 32 + lane;
+            const int p = warp * 32 + (f >> 3), c = f & 7;  // pixel of the tile, 4-channel chunk
+            const float4 val = *reinterpret_cast<const float4 *>(sA + p * 128 + (((c ^ p) & 7) << 4));
+            const int oy = oy0 + (p >> 4), ox = ox0 + (p & 15);
+            if (oy < a.oh && ox < a.ow)
+                *reinterpret_cast<float4 *>(a.y + (((long long)img * a.oh + oy) * a.ow + ox) * a.y_stride + a.y_coff +
+                                            4 * c) = val;
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (mma_pending && tid == 0) mbar_wait(bar, phase);  // drain before the TMEM is released
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kStemTmemCols));
+}
+
+// Host: launch with one wave of resident CTAs (persistent over tiles).
+template <int CIN, int S>
+static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s)
+{
+    using L = StemTcLayout<CIN, S>;
+    static int per_sm = -1;  // resident CTAs per SM, computed once per instantiation
+    if (per_sm < 0) {
+        cudaError_t e = cudaFuncSetAttribute(stem_tc_kernel<CIN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)L::kBytes);
+        if (e != cudaSuccess) return -1;
+        int nb = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, stem_tc_kernel<CIN, S>, kStemThreads, L::kBytes);
+        if (e != cudaSuccess || nb < 1) return -1;
+        per_sm = nb;
+    }
+    const long long ntiles = (long long)a.n * g.tiles_x * g.tiles_y;
+    const unsigned grid = (unsigned)std::min<long long>(ntiles, (long long)per_sm * tc_sm_count());
+    stem_tc_kernel<CIN, S><<<grid, kStemThreads, L::kBytes, s>>>(a, g);
+    return 0;
+}
+
+}  // namespace aie

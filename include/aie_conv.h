@@ -157,9 +157,11 @@ typedef struct aie_plan_info {
     uint32_t oh, ow;
     uint32_t split_k;          /* resolved split (1 = none) */
     uint32_t tile_m, tile_n;   /* CTA tile of the GEMM kernels */
-    uint32_t variant;          /* 1 = IGEMM runs as the small-cin direct conv
-                                  (cin <= 4, 3x3) when the output is 16-byte
-                                  aligned; 0 = the family's main kernel */
+    uint32_t variant;          /* IGEMM run as a small-cin direct conv when the
+                                  output is 16-byte aligned: 1 = FFMA (cin <= 4,
+                                  3x3), 2 = tensor-core im2col GEMM (TF32,
+                                  cin <= 3, cout = 32, no residual);
+                                  0 = the family's main kernel */
     uint64_t weight_bytes;     /* size of dev_w for aie_conv_pack_weights */
     uint64_t bias_bytes;       /* size of dev_b */
     uint64_t workspace_bytes;  /* scratch aie_conv_run needs (0 = none) */

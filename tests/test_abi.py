@@ -78,8 +78,21 @@ def test_kernel_choice_mirrors_lower_op(lib):
 
 
 def test_stem_variant_is_reported(lib):
-    st, i = plan(lib, ih=160, iw=288, cin=3, cout=32, sh=2, sw=2)
-    assert st == 0 and i.kernel == _lib.KERNEL_IGEMM and i.variant == 1
+    # auto / tf32: the tensor-core stem (cin <= 3, cout = 32, no residual)
+    for math in (_lib.MATH_AUTO, _lib.MATH_TF32):
+        st, i = plan(lib, ih=160, iw=288, cin=3, cout=32, sh=2, sw=2, math=math)
+        assert st == 0 and i.kernel == _lib.KERNEL_IGEMM and i.variant == 2 and i.math == _lib.MATH_TF32
+        assert i.weight_bytes == 9 * 3 * 32 * 4 and i.workspace_bytes == 0
+    # explicit FFMA, 4 input channels or another cout: the FFMA direct conv
+    st, i = plan(lib, ih=160, iw=288, cin=3, cout=32, sh=2, sw=2, math=_lib.MATH_FFMA)
+    assert st == 0 and i.variant == 1
+    st, i = plan(lib, cin=4, cout=32, math=_lib.MATH_FFMA)
+    assert st == 0 and i.variant == 1
+    # cin = 4 under auto is TMA-compatible: the general tensor-core GEMM
+    st, i = plan(lib, cin=4, cout=32)
+    assert st == 0 and i.variant == 0 and i.math == _lib.MATH_TF32
+    st, i = plan(lib, cin=3, cout=16)
+    assert st == 0 and i.variant == 1
     st, i = plan(lib, cin=6, cout=32)
     assert st == 0 and i.variant == 0
 

@@ -18,12 +18,19 @@ from tests.test_conv_gpu import IG_SHAPES, IG_SPECIAL, PW_SHAPES, check, run_gpu
 pytestmark = pytest.mark.gpu
 
 
-def tf32_eligible(op):
-    return op.groups == 1 and op.cin % 4 == 0 and op.sh <= 2 and op.sw <= 2
+def stem_tc_shape(op, res=False):
+    """The tensor-core stem's domain: 3x3, cin <= 3, cout = 32, stride 1 or 2,
+    dilation 1, no residual."""
+    return (op.groups == 1 and op.cin <= 3 and op.cout == 32 and op.kh == 3 and op.kw == 3 and op.dil == 1
+            and op.sh == op.sw and op.sh in (1, 2) and not res)
+
+
+def tf32_eligible(op, res=False):
+    return (op.groups == 1 and op.cin % 4 == 0 and op.sh <= 2 and op.sw <= 2) or stem_tc_shape(op, res)
 
 
 def check_tf32(op, x, w, b, res=None, **kw):
-    if not tf32_eligible(op):
+    if not tf32_eligible(op, res is not None):
         with pytest.raises(AieError) as e:
             run_gpu(op, x, w, b, res, math="tf32", **kw)
         assert e.value.status == -3
@@ -273,3 +280,46 @@ def test_pipelined_run_matches_per_batch(cuda_ok):
     for k in range(5):
         assert torch.equal(outs2[k], want[4 - k]), k
     m.release()
+
+
+STEM_TC = [  # n, ih, iw, cin, stride, pad (t, l, b, r), act
+    (2, 160, 288, 3, 2, (1, 1, 1, 1), "relu"),       # the benchmark stem
+    (1, 37, 51, 3, 2, (0, 0, 1, 1), "hardswish"),   # ragged tiles, asymmetric SAME pad
+    (3, 20, 33, 1, 1, (1, 1, 1, 1), "none"),
+    (1, 17, 16, 2, 1, (1, 1, 1, 1), "sigmoid"),
+    (2, 64, 64, 3, 1, (1, 1, 1, 1), "relu6"),
+    (1, 5, 7, 3, 2, (1, 1, 1, 1), "none"),          # smaller than one tile
+]
+
+
+@pytest.mark.parametrize("math", ["tf32", "auto"])
+@pytest.mark.parametrize("n,ih,iw,cin,s,pad,act", STEM_TC, ids=[f"{c[1]}x{c[2]}c{c[3]}s{c[4]}" for c in STEM_TC])
+def test_tc_stem(cuda_ok, math, n, ih, iw, cin, s, pad, act):
+    """The tensor-core stem (im2col GEMM, K = 9*cin padded to 32) against
+    the ai-cpu restatement; auto picks it for the stem shape."""
+    op = Conv2d(cin, 32, 3, 3, s, s, pad, 1, 1, act)
+    x, wt, b, _ = case_tensors(op, n, ih, iw, 9100 + ih + cin, False)
+    plan, _ = check(op, x, wt, b, None, math)
+    assert plan.math == "tf32" and plan.kernel == "stem" and plan.info.variant == 2
+
+
+def test_tc_stem_views_and_fallback(cuda_ok):
+    """C4 input (pixel stride 4); an aligned output view takes the tensor-core
+    stem, a misaligned one (coff 2: 8-byte offset) falls back to the FFMA
+    implicit GEMM with the same packed weights."""
+    from tests.test_conv_gpu import case_tensors as ct
+    op = Conv2d(3, 32, 3, 3, 2, 2, (1, 1, 1, 1), 1, 1, "relu")
+    x, wt, b, _ = ct(op, 2, 30, 46, 9201, False)
+    want, scale = oracle_conv(op, x, wt, b, None)
+    plan, got = run_gpu(op, x, wt, b, None, layout="nhwc_c4", math="tf32")
+    assert normalised_error(got, want, scale) <= TOL_TF32
+    from ai_engine_b200 import View
+    for coff in (4, 2):
+        stride = 40
+        plan = ConvPlan(op, 2, 30, 46, math="tf32", out_view=View(stride, coff)).load_weights(wt, b)
+        buf = torch.full((2, plan.oh, plan.ow, stride), 7.0, device="cuda")
+        plan(torch.from_numpy(x).cuda(), out=buf)
+        torch.cuda.synchronize()
+        g = buf.cpu().numpy()
+        assert normalised_error(g[..., coff:coff + 32], want, scale) <= TOL_TF32
+        assert (g[..., :coff] == 7.0).all() and (g[..., coff + 32:] == 7.0).all()
