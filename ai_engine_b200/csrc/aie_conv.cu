@@ -423,13 +423,24 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         const bool blocked = d.cout % 4 == 0 && a.vec_x && a.vec_y && a.x_coff % 4 == 0 && a.y_coff % 4 == 0 &&
                              (!a.res || (a.r_stride % 4 == 0 && a.r_coff % 4 == 0)) && d.dil == 1 &&
                              d.kh == d.kw && d.sh == d.sw && (d.kh == 3 || d.kh == 5) && (d.sh == 1 || d.sh == 2) &&
-                             (long long)d.n * p->oh * ((p->ow + 3) / 4) * (d.cout / 4) < (1ll << 31);
+                             (long long)d.n * p->oh * ((p->ow + 3) / 4) * (d.cout / 4) + 256 < (1ll << 31);
         if (blocked) {
-            constexpr int PB = 4;
-            const int segs = (int)((p->ow + PB - 1) / PB), cg = (int)(d.cout / 4);
-            const long long threads = (long long)d.n * p->oh * segs * cg;
+            // 4 output pixels per thread (8 measured slower on B200: fewer
+            // threads in flight for the same bytes)
+            const int PB = 4;
+            DwGrid gd;
+            gd.segs_per_row = (int)((p->ow + PB - 1) / PB);
+            gd.cg = (int)(d.cout / 4);
+            gd.div_cg = make_fastdiv(gd.cg);
+            gd.div_segs = make_fastdiv(gd.segs_per_row);
+            gd.div_oh = make_fastdiv((int)p->oh);
+            const long long threads = (long long)d.n * p->oh * gd.segs_per_row * gd.cg;
             const unsigned grid = (unsigned)((threads + 255) / 256);
-#define AIE_DW(S_, K_, ST_) dw_block_kernel<S_, K_, ST_, PB><<<grid, 256, 0, s>>>(a, segs, cg)
+#define AIE_DW(S_, K_, ST_)                                                          \
+    do {                                                                             \
+        if (PB == 8) dw_block_kernel<S_, K_, ST_, 8><<<grid, 256, 0, s>>>(a, gd);    \
+        else dw_block_kernel<S_, K_, ST_, 4><<<grid, 256, 0, s>>>(a, gd);            \
+    } while (0)
 #define AIE_DW2(S_)                                            \
     if (d.kh == 3 && d.sh == 1) AIE_DW(S_, 3, 1);              \
     else if (d.kh == 3) AIE_DW(S_, 3, 2);                      \
@@ -440,6 +451,30 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
 #undef AIE_DW
         } else if (p->strict) dw_kernel<true><<<(unsigned)p->grid, 256, 0, s>>>(a);
         else dw_kernel<false><<<(unsigned)p->grid, 256, 0, s>>>(a);
+    } else if (p->kernel == AIE_KERNEL_PW_DOT && a.vec_x && a.x_coff % 4 == 0 &&
+               (p->d.cin == 8 || p->d.cin == 16 || p->d.cin == 32 || p->d.cin == 64) && p->M + 256 < (1ll << 31)) {
+        // coalesced tile form: weights + 8 warps x 32 staged input rows
+        const int cin = (int)p->d.cin;
+        const size_t smem = (size_t)cin * 4 * 4 + (size_t)8 * 32 * cin * 4;
+        const unsigned grid = (unsigned)((p->M + 255) / 256);
+#define AIE_PWD(S_, CG_)                                                                                     \
+    do {                                                                                                     \
+        static bool attr_##CG_ = false;                                                                      \
+        if (!attr_##CG_) {                                                                                   \
+            CUDA_TRY(cudaFuncSetAttribute(pw_dot_tile_kernel<S_, CG_>,                                       \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));          \
+            attr_##CG_ = true;                                                                               \
+        }                                                                                                    \
+        pw_dot_tile_kernel<S_, CG_><<<grid, 256, smem, s>>>(a);                                              \
+    } while (0)
+        if (p->strict) {
+            if (cin == 8) AIE_PWD(true, 2); else if (cin == 16) AIE_PWD(true, 4);
+            else if (cin == 32) AIE_PWD(true, 8); else AIE_PWD(true, 16);
+        } else {
+            if (cin == 8) AIE_PWD(false, 2); else if (cin == 16) AIE_PWD(false, 4);
+            else if (cin == 32) AIE_PWD(false, 8); else AIE_PWD(false, 16);
+        }
+#undef AIE_PWD
     } else if (p->kernel == AIE_KERNEL_PW_DOT) {
         const size_t smem = (size_t)p->d.cout * p->d.cin * 4;
         if (smem > 200 * 1024) return fail(AIE_E_UNSUPPORTED, "cout*cin too large for the dot kernel");
@@ -506,12 +541,12 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     a.sy = (float)ih / (float)oh;
     a.sx = (float)iw / (float)ow;
     const int cg = (int)((c + 3) / 4);
-    a.px_per_thread = c == 1 ? 4 : 1;
     a.vec = c == 1 ? ((uintptr_t)out % 16 == 0 && ow % 4 == 0)
                    : ((c % 4 == 0) && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0 &&
                       (!add || (uintptr_t)add % 16 == 0));
+    a.px_per_thread = (c == 1 || (c % 4 == 0 && a.vec)) ? 4 : 1;
     a.div_cg = make_fastdiv(cg);
-    a.div_ow = make_fastdiv((int)ow);
+    a.div_owg = make_fastdiv((int)((ow + a.px_per_thread - 1) / a.px_per_thread));
     a.div_oh = make_fastdiv((int)oh);
     const long long groups = (long long)n * oh * ((ow + a.px_per_thread - 1) / a.px_per_thread) * cg;
     resize_bilinear_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a);

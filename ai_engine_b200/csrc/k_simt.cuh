@@ -293,6 +293,72 @@ __global__ void __launch_bounds__(256) pw_dot_kernel(const ConvArgs a)
     }
 }
 
+// Same op, memory-efficient form for cin = 4*CG (CG = 2, 4, 8, 16), 16-byte
+// aligned input rows: each warp stages 32 pixels' input rows in shared
+// memory with coalesced 16-byte loads (consecutive lanes read consecutive
+// chunks), then each lane reduces its own pixel exactly as pw_dot_kernel
+// does (lanes 4c..4c+3 in channel order, (l0+l1)+(l2+l3), + bias, act).
+// Chunk q of row r is stored at position q ^ (r mod CG) so that both the
+// row-major writes and the per-lane row reads are bank-conflict free.
+template <bool kStrict, int CG>
+__global__ void __launch_bounds__(256) pw_dot_tile_kernel(const ConvArgs a)
+{
+    constexpr int CIN = 4 * CG;
+    extern __shared__ float4 sm4[];
+    float *ws = reinterpret_cast<float *>(sm4);  // [cout][CIN], cout <= 4
+    float4 *buf = sm4 + CIN + (threadIdx.x >> 5) * 32 * CG;  // this warp's 32 rows
+    for (int i = threadIdx.x; i < a.cout * CIN; i += 256) ws[i] = a.w[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const long long m0 = ((long long)blockIdx.x * 8 + (threadIdx.x >> 5)) * 32;
+    if (m0 >= a.M) return;
+    const float *xb = a.x + a.x_coff;
+#pragma unroll
+    for (int j = 0; j < CG; j++) {
+        const int f = j * 32 + lane;
+        const int r = f / CG, q = f % CG;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m0 + r < a.M) v = __ldg(reinterpret_cast<const float4 *>(xb + (m0 + r) * a.x_stride + 4 * q));
+        buf[r * CG + (q ^ (r % CG))] = v;
+    }
+    __syncwarp();
+    const long long m = m0 + lane;
+    float acc[4][4];
+#pragma unroll
+    for (int o = 0; o < 4; o++)
+#pragma unroll
+        for (int l = 0; l < 4; l++) acc[o][l] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < CG; q++) {
+        const float4 v = buf[lane * CG + (q ^ (lane % CG))];
+#pragma unroll
+        for (int o = 0; o < 4; o++) {
+            if (o < a.cout) {
+                const float4 w = reinterpret_cast<const float4 *>(ws + o * CIN)[q];
+                acc[o][0] = madd<kStrict>(acc[o][0], v.x, w.x);
+                acc[o][1] = madd<kStrict>(acc[o][1], v.y, w.y);
+                acc[o][2] = madd<kStrict>(acc[o][2], v.z, w.z);
+                acc[o][3] = madd<kStrict>(acc[o][3], v.w, w.w);
+            }
+        }
+    }
+    if (m >= a.M) return;
+    float *yr = a.y + m * a.y_stride + a.y_coff;
+    const float *rr = a.res ? a.res + m * a.r_stride + a.r_coff : nullptr;
+    float v[4];
+#pragma unroll
+    for (int o = 0; o < 4; o++) {
+        const float s = __fadd_rn(__fadd_rn(acc[o][0], acc[o][1]), __fadd_rn(acc[o][2], acc[o][3]));
+        v[o] = __fadd_rn(s, o < a.cout ? a.bias[o] : 0.0f);
+    }
+    epi_act_n<kStrict, 4>(a.act, v, 0, 0);  // scalar activation form (pw_dot.rs:57)
+#pragma unroll
+    for (int o = 0; o < 4; o++) {
+        if (o < a.cout) yr[o] = rr ? add_res<kStrict>(v[o], rr[o]) : v[o];
+        else if (o < a.y_pad_to) yr[o] = 0.0f;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Depthwise conv: one thread per (output pixel, 4-channel group); adjacent
 // threads take adjacent channel groups so every tap load is a coalesced
@@ -374,8 +440,9 @@ struct ResizeArgs {
     int n, ih, iw, c, oh, ow, mode, act;
     float sy, sx;
     int vec;
-    FastDiv div_cg, div_ow, div_oh;
-    int px_per_thread;  // 4 for single-channel tensors (4 adjacent output pixels), else 1
+    FastDiv div_cg, div_owg, div_oh;
+    int px_per_thread;  // output pixels per thread along x: 4 (c == 1, or c % 4 == 0 with
+                        // aligned rows: a run of 4 pixels for one channel group), else 1
 };
 
 // Source coordinate along one axis (reference/resize.rs:16-29), rounded step
@@ -403,10 +470,10 @@ __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a
     const int idx = blockIdx.x * 256 + threadIdx.x;
     const int total = a.n * a.oh * ((a.ow + a.px_per_thread - 1) / a.px_per_thread) * cg;
     if (idx >= total) return;
-    const int g = idx - fdiv(idx, a.div_cg) * cg;
     const int pxg = fdiv(idx, a.div_cg);  // pixel group index
+    const int g = idx - pxg * cg;
     const int owg = (a.ow + a.px_per_thread - 1) / a.px_per_thread;
-    const int row = pxg / owg;            // img * oh + oy
+    const int row = fdiv(pxg, a.div_owg);  // img * oh + oy
     const int ox0 = (pxg - row * owg) * a.px_per_thread;
     const int img = fdiv(row, a.div_oh);
     const int oy = row - img * a.oh;
@@ -416,6 +483,36 @@ __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a
     const float ty1 = __fsub_rn(1.0f, ty);
     const float *xb = a.x + (long long)img * a.ih * a.iw * a.c;
     const float *r0 = xb + (long long)y0 * a.iw * a.c, *r1 = xb + (long long)y1 * a.iw * a.c;
+    if (a.px_per_thread > 1 && a.c % 4 == 0) {  // a run of 4 output pixels, channels 4g..4g+3
+        const int c0 = g * 4;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int ox = ox0 + p;
+            if (ox >= a.ow) break;
+            int x0, x1;
+            float tx;
+            resize_axis(ox, a.sx, a.mode, a.iw, x0, x1, tx);
+            const float tx1 = __fsub_rn(1.0f, tx);
+            const float4 g00 = __ldg(reinterpret_cast<const float4 *>(r0 + x0 * a.c + c0));
+            const float4 g01 = __ldg(reinterpret_cast<const float4 *>(r0 + x1 * a.c + c0));
+            const float4 g10 = __ldg(reinterpret_cast<const float4 *>(r1 + x0 * a.c + c0));
+            const float4 g11 = __ldg(reinterpret_cast<const float4 *>(r1 + x1 * a.c + c0));
+            float v[4];
+            v[0] = lerp2(g00.x, g01.x, g10.x, g11.x, tx, tx1, ty, ty1);
+            v[1] = lerp2(g00.y, g01.y, g10.y, g11.y, tx, tx1, ty, ty1);
+            v[2] = lerp2(g00.z, g01.z, g10.z, g11.z, tx, tx1, ty, ty1);
+            v[3] = lerp2(g00.w, g01.w, g10.w, g11.w, tx, tx1, ty, ty1);
+            const long long px = (long long)row * a.ow + ox;
+            if (a.add) {
+                const float4 ad = __ldg(reinterpret_cast<const float4 *>(a.add + px * a.c + c0));
+                v[0] = __fadd_rn(v[0], ad.x); v[1] = __fadd_rn(v[1], ad.y);
+                v[2] = __fadd_rn(v[2], ad.z); v[3] = __fadd_rn(v[3], ad.w);
+            }
+            act_apply_strict_n<4>(a.act, v, c0, a.c);
+            *reinterpret_cast<float4 *>(a.y + px * a.c + c0) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        return;
+    }
     if (a.px_per_thread > 1) {  // single channel: 4 adjacent output pixels
         float v[4];
 #pragma unroll
@@ -624,20 +721,26 @@ namespace aie {
 // (PB-1)*S + K loads for PB outputs instead of PB*K (the 4-pixel blocking of
 // crates/ai-cpu/src/kernels/dw.rs:100-145 and conv_dw.rs's PB).  Adjacent
 // threads take adjacent channel groups, so every load and store is a
-// coalesced 128-bit access.  Taps accumulate in (ky, kx) order, unfused --
-// bit-identical to ai-cpu's conv_dw.  Requires C % 4 == 0, aligned views,
-// dilation 1.
+// coalesced 128-bit access.  Taps accumulate in (ky, kx) order: unfused
+// (bit-identical to ai-cpu's conv_dw) in strict mode, fused multiply-adds
+// otherwise.  Requires C % 4 == 0, aligned views, dilation 1.
 // ---------------------------------------------------------------------------
+struct DwGrid {
+    int segs_per_row, cg;
+    FastDiv div_cg, div_segs, div_oh;
+};
+
 template <bool kStrict, int K, int S, int PB>
-__global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, int segs_per_row, int cg)
+__global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, const DwGrid gd)
 {
-    const int idx = blockIdx.x * 256 + threadIdx.x;
-    const int g = idx % cg;
-    const int t = idx / cg;
-    const int seg = t % segs_per_row;
-    const int rowid = t / segs_per_row;  // img * oh + oy
+    const int idx = blockIdx.x * 256 + threadIdx.x;  // < 2^31 (checked on the host)
+    const int t = fdiv(idx, gd.div_cg);
+    const int g = idx - t * gd.cg;
+    const int rowid = fdiv(t, gd.div_segs);          // img * oh + oy
+    const int seg = t - rowid * gd.segs_per_row;
     if (rowid >= a.n * a.oh) return;
-    const int img = rowid / a.oh, oy = rowid - img * a.oh;
+    const int img = fdiv(rowid, gd.div_oh), oy = rowid - img * a.oh;
+    const int cg = gd.cg;
     const int ox0 = seg * PB;
     const int c0 = g * 4;
     const int cpad = cg * 4;
@@ -667,10 +770,10 @@ __global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, int seg
             for (int p = 0; p < PB; p++) {
                 const int kx = j - p * S;
                 if (kx >= 0 && kx < K) {
-                    acc[p][0] = madd<true>(acc[p][0], xv.x, wk[kx].x);
-                    acc[p][1] = madd<true>(acc[p][1], xv.y, wk[kx].y);
-                    acc[p][2] = madd<true>(acc[p][2], xv.z, wk[kx].z);
-                    acc[p][3] = madd<true>(acc[p][3], xv.w, wk[kx].w);
+                    acc[p][0] = madd<kStrict>(acc[p][0], xv.x, wk[kx].x);
+                    acc[p][1] = madd<kStrict>(acc[p][1], xv.y, wk[kx].y);
+                    acc[p][2] = madd<kStrict>(acc[p][2], xv.z, wk[kx].z);
+                    acc[p][3] = madd<kStrict>(acc[p][3], xv.w, wk[kx].w);
                 }
             }
         }

@@ -208,23 +208,30 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kStemTmemCols));
 }
 
-// Host: launch with one wave of resident CTAs (persistent over tiles).
+// Host: launch one wave of kStemCtasPerSm resident CTAs per SM (persistent
+// over tiles).  The occupancy API reports one CTA per SM for this kernel on
+// B200 (driver 580) although registers (80 x 256 x 3) and shared memory
+// (3 x (64 KB + 1 KB)) admit three; the grid is sized from those limits
+// directly, and the strided tile loop stays correct however many are resident.
+constexpr int kStemCtasPerSm = 3;
+
 template <int CIN, int S>
 static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s)
 {
     using L = StemTcLayout<CIN, S>;
-    static int per_sm = -1;  // resident CTAs per SM, computed once per instantiation
-    if (per_sm < 0) {
+    static_assert(kStemCtasPerSm * (L::kBytes + 1024) <= 228 * 1024, "shared memory for three CTAs per SM");
+    static bool attr_set = false;
+    if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(stem_tc_kernel<CIN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)L::kBytes);
         if (e != cudaSuccess) return -1;
-        int nb = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, stem_tc_kernel<CIN, S>, kStemThreads, L::kBytes);
-        if (e != cudaSuccess || nb < 1) return -1;
-        per_sm = nb;
+        e = cudaFuncSetAttribute(stem_tc_kernel<CIN, S>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return -1;
+        attr_set = true;
     }
     const long long ntiles = (long long)a.n * g.tiles_x * g.tiles_y;
-    const unsigned grid = (unsigned)std::min<long long>(ntiles, (long long)per_sm * tc_sm_count());
+    const unsigned grid = (unsigned)std::min<long long>(ntiles, (long long)kStemCtasPerSm * tc_sm_count());
     stem_tc_kernel<CIN, S><<<grid, kStemThreads, L::kBytes, s>>>(a, g);
     return 0;
 }

@@ -52,6 +52,7 @@ constexpr int kTcBM = 128;
 constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 4;  // 16 KB
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s
+constexpr uint32_t kTcBResidentMax = 112 * 1024;   // largest B kept in shared memory for a whole kernel
 
 struct TcGeom {
     uint32_t bm, bn;
@@ -64,6 +65,9 @@ struct TcGeom {
     uint64_t workspace_bytes;
     uint32_t smem_bytes;
     uint32_t b_bytes;
+    uint32_t b_resident;       // 1: the CTA's whole B (all taps and K blocks) is loaded once
+    uint32_t bres_off;         // shared-memory offset of the resident B
+    uint32_t res_off;          // per-warp residual prefetch buffers (0 = none)
     uint32_t out_off, shared_off;
 };
 
@@ -71,6 +75,7 @@ struct TcArgs {
     ConvArgs c;
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
+    uint32_t b_resident, bres_off, res_off;
     uint64_t units;
     float *ws;            // split-K partials [tile][split][128][bn]
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
@@ -284,6 +289,7 @@ struct TcShared {
     uint64_t empty[8];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
+    uint64_t bfull;  // resident B landed
     uint32_t tmem_base;
     uint32_t abort;
 };
@@ -324,7 +330,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-align the stage buffers (128-byte swizzle atoms)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t stage_bytes = kTcABytes + a.b_bytes;
+    // stage = A tile (+ B tile unless B is resident for the whole kernel)
+    const uint32_t stage_bytes = kTcABytes + (a.b_resident ? 0u : a.b_bytes);
     TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.shared_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -337,6 +344,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&sh.acc_full[b], 1);
             mbar_init(&sh.acc_empty[b], 4);
         }
+        mbar_init(&sh.bfull, 1);
         sh.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -361,6 +369,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             uint32_t it = 0, last_mine = 0xFFFFFFFFu;
             bool ok = true;
+            if (a.b_resident && pidx == 0) {
+                // the whole B of the (single) n-tile, one box per (tap, K block),
+                // in k order: k = tap * kblocks + kb at bres_off + k * b_bytes
+                mbar_expect_tx(&sh.bfull, a.k_iters * a.b_bytes);
+                for (uint32_t k = 0; k < a.k_iters; k++) {
+                    const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
+                    tma_load_3d(smem + a.bres_off + k * a.b_bytes, &tmB, &sh.bfull, (int)(kb * kTcBK), 0, (int)tap);
+                }
+            }
             for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
                 const TcUnit t = tc_unit(a, u);
                 const uint32_t k0 = t.s * a.k_per_split;
@@ -385,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     uint8_t *sa = smem + s * stage_bytes;
                     uint8_t *sb = sa + kTcABytes;
-                    mbar_expect_tx(&sh.full[s], kTcABytes + a.b_bytes);
+                    mbar_expect_tx(&sh.full[s], stage_bytes);
                     const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
                     const int kc = (int)(kb * kTcBK);
                     if (a.igemm) {
@@ -394,13 +411,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     } else {
                         tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                     }
-                    tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
+                    if (!a.b_resident) tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
                     last_mine = it;
                 }
             }
             // drain: wait (bounded) until the copies this thread issued have landed
             if (last_mine != 0xFFFFFFFFu)
                 mbar_wait(&sh.full[last_mine % a.stages], (last_mine / a.stages) & 1);
+            if (a.b_resident && pidx == 0) mbar_wait(&sh.bfull, 0);
         }
         __syncwarp();
     } else if (warp == 0) {
@@ -409,6 +427,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t idesc = idesc_tf32(kTcBM, a.bn);
             uint32_t it = 0, acc_it = 0;
             bool ok = true;
+            if (a.b_resident && blockIdx.x < a.units) {
+                if (*abort_flag || !mbar_wait(&sh.bfull, 0)) {
+                    report_error(0x01000005);
+                    *abort_flag = 1;
+                    ok = false;
+                }
+            }
             for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x, acc_it++) {
                 const TcUnit t = tc_unit(a, u);
                 const uint32_t k0 = t.s * a.k_per_split;
@@ -431,7 +456,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * stage_bytes);
-                    const uint32_t sb = sa + kTcABytes;
+                    const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + kTcABytes;
                     const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
 #pragma unroll
                     for (uint32_t kk = 0; kk < kTcBK / 8; kk++) {
@@ -477,6 +502,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // of 32 scattered 16-byte pieces; residual added after the activation
         // RES: 0 none, 1 residual tensor, 2 bilinear-sampled residual; a
         // template argument so each layer's epilogue carries only its code
+        // residual tensor (RES 1, 16-byte aligned rows): the 8 x 16 bytes this
+        // lane adds for the chunk at col0 are fetched with cp.async into this
+        // warp's residual buffer ahead of use, so their latency overlaps the
+        // MMA wait and the TMEM drain without holding registers; each lane
+        // later reads back only what it fetched itself
+        auto prefetch_res = [&](int col0) {
+            const int col = col0 + seg * 4;
+            const bool vec = c.vec_y && col + 4 <= c.cout;
+            if (!a.res_off || !vec) return;
+            uint8_t *rbuf = smem + a.res_off + ew * kTcStageOut;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int r = i * 4 + (lane >> 3);
+                const bool ok = mrow[i] >= 0;
+                const float *src = ok ? c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col : c.res;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                                 smem_u32(rbuf + r * 128 + ((seg ^ (r & 7)) * 16))),
+                             "l"(src), "r"(ok ? 16 : 0)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+
         auto emit = [&](auto res_kind, int col0, float (&v)[32]) {
             constexpr int RES = decltype(res_kind)::value;
             const int col = col0 + seg * 4;
@@ -497,6 +545,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 *reinterpret_cast<float4 *>(st + ((ch ^ (lane & 7)) * 16)) =
                     make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
             __syncwarp();
+            if constexpr (RES == 1) {
+                if (a.res_off) asm volatile("cp.async.wait_all;" ::: "memory");  // this lane's prefetched rows
+            }
             if (col >= c.y_pad_to) return;
             // four rows at a time: their residual loads are issued together
 #pragma unroll
@@ -510,14 +561,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         if (mrow[i] >= 0) rv[q] = bilinear_res4(c, mrow[i], col, vec);
                     } else if constexpr (RES == 1) {
                         if (mrow[i] >= 0) {
-                            const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
-                            if (vec) rv[q] = __ldg(reinterpret_cast<const float4 *>(rr));
-                            else {
-                                float t4[4] = {0.f, 0.f, 0.f, 0.f};
+                            if (a.res_off && vec) {
+                                const int r = i * 4 + (lane >> 3);
+                                rv[q] = *reinterpret_cast<const float4 *>(smem + a.res_off + ew * kTcStageOut + r * 128 +
+                                                                          ((seg ^ (r & 7)) * 16));
+                            } else {
+                                const float *rr = c.res + (long long)mrow[i] * c.r_stride + c.r_coff + col;
+                                if (vec) rv[q] = __ldg(reinterpret_cast<const float4 *>(rr));
+                                else {
+                                    float t4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                                for (int l = 0; l < 4; l++)
-                                    if (col + l < c.cout) t4[l] = __ldg(rr + l);
-                                rv[q] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                                    for (int l = 0; l < 4; l++)
+                                        if (col + l < c.cout) t4[l] = __ldg(rr + l);
+                                    rv[q] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                                }
                             }
                         }
                     }
@@ -551,6 +608,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             else if (!c.res_mode) emit(std::integral_constant<int, 1>{}, col0, v);
             else emit(std::integral_constant<int, 2>{}, col0, v);
         };
+        const bool res_tensor = c.res && !c.res_mode;
 
         uint32_t k = 0;  // tiles this group has drained: the phase of its buffer
         for (uint64_t u = blockIdx.x + (uint64_t)grp * gridDim.x; u < a.units; u += 2ull * gridDim.x, k++) {
@@ -569,26 +627,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 bias_nt = t.nt;
                 bias_base = nbase;
             }
-            if (*abort_flag || !mbar_wait(&sh.acc_full[ab], aph)) {
-                report_error(0x01000004);
-                *abort_flag = 1;
-                break;
-            }
-            tc_fence_after();
+            if (res_tensor && a.split == 1) prefetch_res(nbase);  // first chunk, ahead of the MMA wait
             if (a.split == 1) {
-                for (int c0 = 0; c0 < ncol; c0 += 32) {
-                    uint32_t r[32];
-                    tmem_ld32_issue(tbase + c0, (int)a.bn - c0, r);
-                    tmem_wait32((int)a.bn - c0, r);
-                    float v[32];
+                const bool ok = !*abort_flag && mbar_wait(&sh.acc_full[ab], aph);
+                if (ok) {
+                    tc_fence_after();
+                    for (int c0 = 0; c0 < ncol; c0 += 32) {
+                        uint32_t r[32];
+                        tmem_ld32_issue(tbase + c0, (int)a.bn - c0, r);
+                        tmem_wait32((int)a.bn - c0, r);
+                        float v[32];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-                    emit_any(nbase + c0, v);
+                        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+                        emit_any(nbase + c0, v);
+                        if (res_tensor && c0 + 32 < ncol) {
+                            __syncwarp();  // every lane has read its rows of the buffer
+                            prefetch_res(nbase + c0 + 32);
+                        }
+                    }
+                }
+                if (!ok) {
+                    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy may land after exit
+                    report_error(0x01000004);
+                    *abort_flag = 1;
+                    break;
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sh.acc_empty[ab]);
             } else {
+                if (*abort_flag || !mbar_wait(&sh.acc_full[ab], aph)) {
+                    report_error(0x01000004);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
                 // raw partial -> workspace, release the accumulator, then take
                 // this warp's ticket for its 32 rows (no cross-warp barrier:
                 // every warp finishes on its own even if another gave up)
@@ -614,6 +687,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     __threadfence();
                     const float *base = a.ws + (tile * a.split * kTcBM + row) * a.bn;
                     for (int c0 = 0; c0 < ncol; c0 += 32) {
+                        if (res_tensor) {
+                            __syncwarp();  // every lane has read its rows of the buffer
+                            prefetch_res(nbase + c0);  // lands while the partials are summed
+                        }
                         float v[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) v[j] = 0.0f;
@@ -717,14 +794,24 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->split = (g->k_iters + g->k_per_split - 1) / g->k_per_split;  // no empty splits
     g->units = tiles * g->split;
     g->b_bytes = g->bn * kTcBK * 4;
-    const uint32_t stage = kTcABytes + g->b_bytes;
-    // shared memory: [stages][epilogue staging, 4 warps x 4 KB][barriers];
-    // the stage buffers are 1024-aligned
-    const uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + 256 * 4);  // staging + per-warp bias caches
+    // shared memory: [stages][resident B][epilogue staging + bias caches]
+    // [barriers]; stage buffers and the resident B are 1024-aligned
+    // staging + per-warp bias caches (+ residual prefetch buffers)
+    const uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + 256 * 4 + (has_res ? kTcStageOut : 0u));
     const uint32_t limit = 227 * 1024 - 1024 /*align slack*/ - 256 /*barriers*/;
-    g->stages = std::min<uint32_t>(8, (limit - out_bytes) / stage);
+    // Resident B: with one n-tile and no K split every unit of a CTA uses the
+    // same B, so it is loaded once (one TMA box per tap and K block) and each
+    // stage carries only its A tile -- half the TMA operations per stage.
+    const uint64_t bres = (uint64_t)g->k_iters * g->b_bytes;
+    g->b_resident = (g->n_tiles == 1 && g->split == 1 && bres <= kTcBResidentMax &&
+                     (limit - out_bytes - bres) / kTcABytes >= 4) ? 1u : 0u;
+    const uint32_t stage = kTcABytes + (g->b_resident ? 0u : g->b_bytes);
+    const uint32_t fixed = out_bytes + (g->b_resident ? (uint32_t)bres : 0u);
+    g->stages = std::min<uint32_t>(8, (limit - fixed) / stage);
     if (g->stages < 2) return -2;
-    g->out_off = g->stages * stage;
+    g->bres_off = g->stages * stage;
+    g->out_off = g->bres_off + (g->b_resident ? (uint32_t)bres : 0u);
+    g->res_off = has_res ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;
     g->shared_off = g->out_off + out_bytes;
     g->tmem_cols = tc_pow2_ceil(2 * g->bn);
     if (g->tmem_cols > 512) return -3;
@@ -822,6 +909,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.m_tiles = g.m_tiles; a.n_tiles = g.n_tiles; a.split = g.split; a.k_iters = g.k_iters;
     a.k_per_split = g.k_per_split; a.kblocks = g.kblocks; a.stages = g.stages; a.tmem_cols = g.tmem_cols;
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
+    a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off;
     a.out_off = g.out_off; a.shared_off = g.shared_off;
     a.ws = nullptr;
     a.tickets = nullptr;
