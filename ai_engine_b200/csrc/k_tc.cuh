@@ -8,13 +8,20 @@
 //                accumulator buffer g (every other tile), so two tiles'
 //                epilogues overlap.  tcgen05.ld -> bias -> act, transposed
 //                through shared memory -> +residual -> coalesced row stores
-//   warps 9..11  TMA producers, one elected lane each, taking stages in turn
-//                (TMA issue rate is per issuing thread: one thread issuing
-//                16 KB boxes reaches ~3.5 TB/s on B200, four reach HBM speed)
+//   warp 9       TMA producer: up to 8 free-running lanes, each issuing
+//                every 8th stage of its pipeline (TMA issue is limited per
+//                issuing thread, about one box in flight each: on B200 one
+//                lane moves ~0.65 us per 16 KB box per SM, four ~0.23 us)
+//   warp 10      second MMA issuer.  A tcgen05.mma costs its issuing thread
+//                ~80-90 ns whatever N is (M=128, K=8 TF32), so narrow tiles
+//                (N <= 64) run two pipelines: the CTA's even units use stage
+//                ring 0, MMA warp 0, accumulator 0 and epilogue group 0, the
+//                odd units ring 1, warp 10, accumulator 1 and group 1.
 // Accumulators are double-buffered in TMEM so the epilogue of one tile
-// overlaps the mainloop of the next.  (The epilogue is issue-latency bound
-// with one warp per SM sub-partition: ~550 instructions per 32x32 chunk.)  Operands are fp32 in HBM and are read
+// overlaps the mainloop of the next.  Operands are fp32 in HBM and are read
 // by the tensor core as TF32; both are K-major with the 128-byte swizzle.
+// With one n-tile and no K split the whole B is resident in shared memory
+// (loaded once per CTA) and the stages carry only A.
 //
 // A operand (activations, NHWC):
 //   1x1 conv : 2-D tensor map (cin, M), box (32, 128)
@@ -44,9 +51,11 @@
 
 namespace aie {
 
-constexpr int kTcProducers = 3;                   // TMA issue is per-thread limited
+constexpr int kTcProducers = 1;                   // one producer warp ...
+constexpr int kTcIssueLanes = 8;                  // ... issuing from up to 8 lanes at once
 constexpr int kTcEpiWarps = 8;
-constexpr int kTcThreads = 32 * (1 + kTcEpiWarps + kTcProducers); // MMA, epilogue, producers
+constexpr int kTcMmaWarp1 = 1 + kTcEpiWarps + kTcProducers;  // second MMA issuer (pipeline 1)
+constexpr int kTcThreads = 32 * (kTcMmaWarp1 + 1);           // MMA 0, epilogue, producer, MMA 1
 constexpr uint32_t kTcStageOut = 32 * 32 * 4;      // one 32x32 fp32 epilogue chunk per warp
 constexpr int kTcBM = 128;
 constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
@@ -65,6 +74,7 @@ struct TcGeom {
     uint64_t workspace_bytes;
     uint32_t smem_bytes;
     uint32_t b_bytes;
+    uint32_t pipes;            // independent MMA pipelines (1 or 2), see tc_conv_kernel
     uint32_t b_resident;       // 1: the CTA's whole B (all taps and K blocks) is loaded once
     uint32_t bres_off;         // shared-memory offset of the resident B
     uint32_t res_off;          // per-warp residual prefetch buffers (0 = none)
@@ -75,7 +85,7 @@ struct TcArgs {
     ConvArgs c;
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
-    uint32_t b_resident, bres_off, res_off;
+    uint32_t b_resident, bres_off, res_off, pipes;
     uint64_t units;
     float *ws;            // split-K partials [tile][split][128][bn]
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
@@ -363,82 +373,107 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = sh.tmem_base;
     volatile uint32_t *abort_flag = &sh.abort;
 
-    if (warp >= 1 + kTcEpiWarps) {
-        // ------------------------------------------------ TMA producers
-        const uint32_t pidx = (uint32_t)(warp - 1 - kTcEpiWarps);
-        if (lane == 0) {
-            uint32_t it = 0, last_mine = 0xFFFFFFFFu;
-            bool ok = true;
-            if (a.b_resident && pidx == 0) {
-                // the whole B of the (single) n-tile, one box per (tap, K block),
-                // in k order: k = tap * kblocks + kb at bres_off + k * b_bytes
-                mbar_expect_tx(&sh.bfull, a.k_iters * a.b_bytes);
-                for (uint32_t k = 0; k < a.k_iters; k++) {
-                    const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
-                    tma_load_3d(smem + a.bres_off + k * a.b_bytes, &tmB, &sh.bfull, (int)(kb * kTcBK), 0, (int)tap);
-                }
+    if (warp == 1 + kTcEpiWarps) {
+        // ------------------------------------------------ TMA producer warp
+        // Pipeline p owns stages [p*RS, (p+1)*RS) and the CTA's units j with
+        // j % pipes == p.  Lane l serves pipeline p = l % pipes and issues
+        // that pipeline's iterations q, q+LQ, q+2LQ, ... (q = l / pipes), each
+        // lane on its own: a lane waits only for the stage it fills next.
+        const uint32_t P = a.pipes, RS = a.stages / a.pipes;
+        const uint32_t LQ = min((uint32_t)kTcIssueLanes / P, RS);
+        const uint32_t pl = (uint32_t)lane % P, q = (uint32_t)lane / P;
+        struct Cursor {
+            uint32_t u;  // units < 2^32 (m tiles < 2^24)
+            uint32_t k, k1;
+        };
+        auto enter = [&](Cursor &cu) {  // first K iteration of unit cu.u
+            if (cu.u < a.units) {
+                const TcUnit t = tc_unit(a, cu.u);
+                cu.k = t.s * a.k_per_split;
+                cu.k1 = min(a.k_iters, cu.k + a.k_per_split);
             }
-            for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-                const TcUnit t = tc_unit(a, u);
-                const uint32_t k0 = t.s * a.k_per_split;
-                const uint32_t k1 = min(a.k_iters, k0 + a.k_per_split);
-                int img = 0, ybase = 0, xbase = 0;
+        };
+        auto advance = [&](Cursor &cu) {
+            if (++cu.k >= cu.k1) {
+                cu.u += P * gridDim.x;
+                enter(cu);
+            }
+        };
+        if (a.b_resident && lane == 0) {
+            // the whole B of the (single) n-tile, one box per (tap, K block),
+            // in k order: k = tap * kblocks + kb at bres_off + k * b_bytes
+            mbar_expect_tx(&sh.bfull, a.k_iters * a.b_bytes);
+            for (uint32_t k = 0; k < a.k_iters; k++) {
+                const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
+                tma_load_3d(smem + a.bres_off + k * a.b_bytes, &tmB, &sh.bfull, (int)(kb * kTcBK), 0, (int)tap);
+            }
+        }
+        uint32_t last_mine = 0xFFFFFFFFu;
+        if (q < LQ) {
+            Cursor cur{(uint32_t)blockIdx.x + pl * gridDim.x, 0u, 0u};
+            enter(cur);
+            uint32_t it = 0;  // this pipeline's iteration index
+            for (uint32_t i = 0; i < q && cur.u < a.units; i++, it++) advance(cur);
+            while (cur.u < a.units) {
+                const uint32_t s = pl * RS + it % RS, ph = (it / RS) & 1;
+                if (*abort_flag || !mbar_wait(&sh.empty[s], ph ^ 1)) {
+                    report_error(0x01000001);
+                    *abort_flag = 1;
+                    break;
+                }
+                const TcUnit t = tc_unit(a, cur.u);
+                uint8_t *sa = smem + s * stage_bytes;
+                uint8_t *sb = sa + kTcABytes;
+                mbar_expect_tx(&sh.full[s], stage_bytes);
+                const uint32_t k = cur.k;
+                const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
+                const int kc = (int)(kb * kTcBK);
                 if (a.igemm) {
                     const uint32_t per_img = a.tiles_x * a.tiles_y;
-                    img = (int)(t.mt / per_img);
+                    const int img = (int)(t.mt / per_img);
                     const uint32_t rem = t.mt - img * per_img;
                     const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
-                    ybase = (int)(ty * a.bh) * a.c.sh - a.c.pt;
-                    xbase = (int)(tx * a.bw) * a.c.sw - a.c.pl;
+                    const int ybase = (int)(ty * a.bh) * a.c.sh - a.c.pt;
+                    const int xbase = (int)(tx * a.bw) * a.c.sw - a.c.pl;
+                    const int ky = (int)(tap / a.c.kw), kx = (int)(tap - ky * a.c.kw);
+                    tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + kx * a.c.dil, ybase + ky * a.c.dil, img);
+                } else {
+                    tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                 }
-                for (uint32_t k = k0; k < k1; k++, it++) {
-                    if (it % kTcProducers != pidx) continue;
-                    const uint32_t s = it % a.stages, ph = (it / a.stages) & 1;
-                    if (*abort_flag || !mbar_wait(&sh.empty[s], ph ^ 1)) {
-                        report_error(0x01000001);
-                        *abort_flag = 1;
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sa = smem + s * stage_bytes;
-                    uint8_t *sb = sa + kTcABytes;
-                    mbar_expect_tx(&sh.full[s], stage_bytes);
-                    const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
-                    const int kc = (int)(kb * kTcBK);
-                    if (a.igemm) {
-                        const int ky = (int)(tap / a.c.kw), kx = (int)(tap - ky * a.c.kw);
-                        tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + kx * a.c.dil, ybase + ky * a.c.dil, img);
-                    } else {
-                        tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
-                    }
-                    if (!a.b_resident) tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
-                    last_mine = it;
-                }
+                if (!a.b_resident) tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
+                last_mine = s | (ph << 16);
+                for (uint32_t i = 0; i < LQ && cur.u < a.units; i++, it++) advance(cur);
             }
-            // drain: wait (bounded) until the copies this thread issued have landed
-            if (last_mine != 0xFFFFFFFFu)
-                mbar_wait(&sh.full[last_mine % a.stages], (last_mine / a.stages) & 1);
-            if (a.b_resident && pidx == 0) mbar_wait(&sh.bfull, 0);
         }
+        // drain: wait (bounded) until the copies this lane issued have landed
+        if (last_mine != 0xFFFFFFFFu) mbar_wait(&sh.full[last_mine & 0xFFFF], last_mine >> 16);
+        if (a.b_resident && lane == 0) mbar_wait(&sh.bfull, 0);
         __syncwarp();
-    } else if (warp == 0) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+    } else if (warp == 0 || warp == kTcMmaWarp1) {
+        // ------------------------------------------------ MMA issuers
+        // pipeline p: units j = p, p + pipes, ... of this CTA, stage ring p,
+        // accumulator buffer (tile count) as the epilogue group that drains it
+        auto mma_pipeline = [&](auto pc) {
+        constexpr uint32_t p = decltype(pc)::value;
+        if (lane == 0 && p < a.pipes) {
+            const uint32_t P = a.pipes, RS = a.stages / a.pipes;
             const uint32_t idesc = idesc_tf32(kTcBM, a.bn);
-            uint32_t it = 0, acc_it = 0;
+            uint32_t it = 0, nt = 0;
             bool ok = true;
-            if (a.b_resident && blockIdx.x < a.units) {
+            if (a.b_resident && blockIdx.x + p * gridDim.x < a.units) {
                 if (*abort_flag || !mbar_wait(&sh.bfull, 0)) {
                     report_error(0x01000005);
                     *abort_flag = 1;
                     ok = false;
                 }
             }
-            for (uint64_t u = blockIdx.x; u < a.units && ok; u += gridDim.x, acc_it++) {
+            for (uint64_t u = blockIdx.x + (uint64_t)p * gridDim.x; u < a.units && ok; u += (uint64_t)P * gridDim.x, nt++) {
                 const TcUnit t = tc_unit(a, u);
                 const uint32_t k0 = t.s * a.k_per_split;
                 const uint32_t k1 = min(a.k_iters, k0 + a.k_per_split);
-                const uint32_t ab = acc_it & 1, aph = (acc_it >> 1) & 1;
+                // accumulator buffer: with two pipelines each owns one; with one,
+                // tiles alternate between the two buffers
+                const uint32_t ab = P == 2 ? p : (nt & 1), aph = P == 2 ? (nt & 1) : ((nt >> 1) & 1);
                 if (*abort_flag || !mbar_wait(&sh.acc_empty[ab], aph ^ 1)) {
                     report_error(0x01000002);
                     *abort_flag = 1;
@@ -447,7 +482,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 const uint32_t d = tmem + ab * a.bn;
                 for (uint32_t k = k0; k < k1; k++, it++) {
-                    const uint32_t s = it % a.stages, ph = (it / a.stages) & 1;
+                    const uint32_t s = p * RS + it % RS, ph = (it / RS) & 1;
                     if (*abort_flag || !mbar_wait(&sh.full[s], ph)) {
                         report_error(0x01000003);
                         *abort_flag = 1;
@@ -473,9 +508,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // TMEM they write can be freed
             if (it > 0) {
                 const uint32_t last = it - 1;
-                mbar_wait(&sh.empty[last % a.stages], (last / a.stages) & 1);
+                mbar_wait(&sh.empty[p * RS + last % RS], (last / RS) & 1);
             }
         }
+        };
+        if (warp == 0) mma_pipeline(std::integral_constant<uint32_t, 0>{});
+        else mma_pipeline(std::integral_constant<uint32_t, 1>{});
         __syncwarp();
     } else {
         // ------------------------------------------------ epilogue (warps 1..8)
@@ -809,6 +847,10 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     const uint32_t fixed = out_bytes + (g->b_resident ? (uint32_t)bres : 0u);
     g->stages = std::min<uint32_t>(8, (limit - fixed) / stage);
     if (g->stages < 2) return -2;
+    // narrow k x k tiles (long K loops, N <= 64) are bound by the per-thread
+    // MMA issue cost: two pipelines.  1x1 GEMMs keep one deep ring (their
+    // short K loops are bound by load latency, which halved rings expose).
+    g->pipes = (g->igemm && g->bn <= 64 && g->stages >= 4) ? 2u : 1u;
     g->bres_off = g->stages * stage;
     g->out_off = g->bres_off + (g->b_resident ? (uint32_t)bres : 0u);
     g->res_off = has_res ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;
@@ -909,7 +951,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.m_tiles = g.m_tiles; a.n_tiles = g.n_tiles; a.split = g.split; a.k_iters = g.k_iters;
     a.k_per_split = g.k_per_split; a.kblocks = g.kblocks; a.stages = g.stages; a.tmem_cols = g.tmem_cols;
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
-    a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off;
+    a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
     a.out_off = g.out_off; a.shared_off = g.shared_off;
     a.ws = nullptr;
     a.tickets = nullptr;
