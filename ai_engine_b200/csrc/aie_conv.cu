@@ -234,7 +234,7 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         p->cin_pad = (int)rup(d.cin, 4);
         p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
-        int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.pad[0], d.pad[1], p->oh, p->ow,
+        int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.dil, d.pad[0], d.pad[1], p->oh, p->ow,
                          d.split_k, d.has_res != 0, &p->tc);
         if (rc) {
             delete p;

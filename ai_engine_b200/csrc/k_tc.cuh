@@ -75,6 +75,8 @@ struct TcGeom {
     uint32_t smem_bytes;
     uint32_t b_bytes;
     uint32_t pipes;            // independent MMA pipelines (1 or 2), see tc_conv_kernel
+    uint32_t halo;             // k x k stride 1: one A box per (kx, K block), see tc_conv_kernel
+    uint32_t a_bytes;          // A bytes per stage
     uint32_t b_resident;       // 1: the CTA's whole B (all taps and K blocks) is loaded once
     uint32_t bres_off;         // shared-memory offset of the resident B
     uint32_t res_off;          // per-warp residual prefetch buffers (0 = none)
@@ -85,7 +87,7 @@ struct TcArgs {
     ConvArgs c;
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
-    uint32_t b_resident, bres_off, res_off, pipes;
+    uint32_t b_resident, bres_off, res_off, pipes, halo, a_bytes;
     uint64_t units;
     float *ws;            // split-K partials [tile][split][128][bn]
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // 1024-align the stage buffers (128-byte swizzle atoms)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // stage = A tile (+ B tile unless B is resident for the whole kernel)
-    const uint32_t stage_bytes = kTcABytes + (a.b_resident ? 0u : a.b_bytes);
+    const uint32_t stage_bytes = a.a_bytes + (a.b_resident ? 0u : (a.halo ? a.c.kh : 1u) * a.b_bytes);
     TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.shared_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -402,8 +404,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (a.b_resident && lane == 0) {
             // the whole B of the (single) n-tile, one box per (tap, K block),
             // in k order: k = tap * kblocks + kb at bres_off + k * b_bytes
-            mbar_expect_tx(&sh.bfull, a.k_iters * a.b_bytes);
-            for (uint32_t k = 0; k < a.k_iters; k++) {
+            const uint32_t nb = (uint32_t)(a.c.kh * a.c.kw) * a.kblocks;
+            mbar_expect_tx(&sh.bfull, nb * a.b_bytes);
+            for (uint32_t k = 0; k < nb; k++) {
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
                 tma_load_3d(smem + a.bres_off + k * a.b_bytes, &tmB, &sh.bfull, (int)(kb * kTcBK), 0, (int)tap);
             }
@@ -423,12 +426,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 const TcUnit t = tc_unit(a, cur.u);
                 uint8_t *sa = smem + s * stage_bytes;
-                uint8_t *sb = sa + kTcABytes;
+                uint8_t *sb = sa + a.a_bytes;
                 mbar_expect_tx(&sh.full[s], stage_bytes);
                 const uint32_t k = cur.k;
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
                 const int kc = (int)(kb * kTcBK);
-                if (a.igemm) {
+                if (a.halo) {
+                    // stage = column shift kx (= tap here), K block kb: rows
+                    // [ybase, ybase + bh + kh - 1) x the bw columns at xbase + kx
+                    const uint32_t per_img = a.tiles_x * a.tiles_y;
+                    const int img = (int)(t.mt / per_img);
+                    const uint32_t rem = t.mt - img * per_img;
+                    const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
+                    const int ybase = (int)(ty * a.bh) - a.c.pt;
+                    const int xbase = (int)(tx * a.bw) - a.c.pl;
+                    tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + (int)tap, ybase, img);
+                    if (!a.b_resident)
+                        for (int ky = 0; ky < a.c.kh; ky++)
+                            tma_load_3d(sb + ky * a.b_bytes, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn),
+                                        ky * a.c.kw + (int)tap);
+                } else if (a.igemm) {
                     const uint32_t per_img = a.tiles_x * a.tiles_y;
                     const int img = (int)(t.mt / per_img);
                     const uint32_t rem = t.mt - img * per_img;
@@ -440,7 +457,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 } else {
                     tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                 }
-                if (!a.b_resident) tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
+                if (!a.b_resident && !a.halo) tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
                 last_mine = s | (ph << 16);
                 for (uint32_t i = 0; i < LQ && cur.u < a.units; i++, it++) advance(cur);
             }
@@ -491,13 +508,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * stage_bytes);
-                    const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + kTcABytes;
-                    const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
+                    if (a.halo) {
+                        // tap (ky, kx): the stage's copy shifted down ky rows
+                        // (ky * bw A rows, a multiple of 8 rows: swizzle-aligned)
+                        const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
+                        for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++) {
+                            const uint32_t tap = ky * a.c.kw + kx;
+                            const uint32_t sb = a.b_resident
+                                                    ? smem_u32(smem + a.bres_off + (tap * a.kblocks + kb) * a.b_bytes)
+                                                    : sa + a.a_bytes + ky * a.b_bytes;
+                            const uint64_t ad = smem_desc_sw128(sa + ky * a.bw * 128), bd = smem_desc_sw128(sb);
 #pragma unroll
-                    for (uint32_t kk = 0; kk < kTcBK / 8; kk++) {
-                        // advance 8 tf32 = 32 bytes along K inside the swizzle row
-                        mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                 (k > k0 || kk > 0) ? 1u : 0u);
+                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                         (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    } else {
+                        const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + kTcABytes;
+                        const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
+#pragma unroll
+                        for (uint32_t kk = 0; kk < kTcBK / 8; kk++) {
+                            // advance 8 tf32 = 32 bytes along K inside the swizzle row
+                            mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                     (k > k0 || kk > 0) ? 1u : 0u);
+                        }
                     }
                     mma_commit(&sh.empty[s]);
                 }
@@ -780,8 +814,8 @@ static inline bool tc_igemm_supported(uint32_t kh, uint32_t kw, uint32_t sh, uin
 
 // Plan the tensor-core launch.  Returns 0 or a negative code.
 static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, uint32_t cout, uint32_t kh, uint32_t kw,
-                          uint32_t sh, uint32_t sw, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
-                          uint32_t split_req, bool has_res, TcGeom *g)
+                          uint32_t sh, uint32_t sw, uint32_t dil, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
+                          uint32_t split_req, bool has_res, TcGeom *g, bool allow_halo = true)
 {
     (void)ih; (void)iw; (void)pt; (void)pl;
     *g = TcGeom{};
@@ -791,12 +825,29 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->taps = kh * kw;
     g->kblocks = (cin + kTcBK - 1) / kTcBK;
     g->k_iters = g->taps * g->kblocks;
+    // Halo mode (k x k, stride 1, dilation 1): a 16 x 8 pixel tile's A for
+    // tap (ky, kx) is rows [ky*16, ky*16 + 128) of one (8 + kh - 1) x 16
+    // pixel box shifted by kx, so a stage loads one box per (kx, K block)
+    // and feeds kh MMA groups: kw x kblocks boxes per tile instead of
+    // kh x kw x kblocks.
+    g->halo = (allow_halo && !pw && sh == 1 && sw == 1 && dil == 1 && kh >= 2 && kh <= 7) ? 1u : 0u;
+    g->a_bytes = kTcABytes;
+    if (g->halo) {
+        g->k_iters = kw * g->kblocks;
+        g->a_bytes = (8 + kh - 1) * 16 * kTcBK * 4;
+    }
     // N tile: fewest tiles of <= 256 columns, each a multiple of 32 so the
     // epilogue's 32-column store boxes never reach into the next tile
     const uint32_t nt = (cout + 255) / 256;
     g->bn = ((cout + nt - 1) / nt + 31) / 32 * 32;
     g->n_tiles = (cout + g->bn - 1) / g->bn;
-    if (g->igemm) {
+    if (g->halo) {
+        g->bw = 16;
+        g->bh = 8;
+        g->tiles_x = (ow + g->bw - 1) / g->bw;
+        g->tiles_y = (oh + g->bh - 1) / g->bh;
+        g->m_tiles = n * g->tiles_x * g->tiles_y;
+    } else if (g->igemm) {
         // M tile = bh x bw output pixels of one frame, bh*bw = 128; pick the
         // shape that wastes the fewest rows
         double best = 1e30;
@@ -840,12 +891,14 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     // Resident B: with one n-tile and no K split every unit of a CTA uses the
     // same B, so it is loaded once (one TMA box per tap and K block) and each
     // stage carries only its A tile -- half the TMA operations per stage.
-    const uint64_t bres = (uint64_t)g->k_iters * g->b_bytes;
+    const uint64_t bres = (uint64_t)g->taps * g->kblocks * g->b_bytes;
     g->b_resident = (g->n_tiles == 1 && g->split == 1 && bres <= kTcBResidentMax &&
-                     (limit - out_bytes - bres) / kTcABytes >= 4) ? 1u : 0u;
-    const uint32_t stage = kTcABytes + (g->b_resident ? 0u : g->b_bytes);
+                     (limit - out_bytes - bres) / g->a_bytes >= 4) ? 1u : 0u;
+    const uint32_t stage = g->a_bytes + (g->b_resident ? 0u : (g->halo ? kh : 1u) * g->b_bytes);
     const uint32_t fixed = out_bytes + (g->b_resident ? (uint32_t)bres : 0u);
     g->stages = std::min<uint32_t>(8, (limit - fixed) / stage);
+    if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
+        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, has_res, g, false);
     if (g->stages < 2) return -2;
     // narrow k x k tiles (long K loops, N <= 64) are bound by the per-thread
     // MMA issue cost: two pipelines.  1x1 GEMMs keep one deep ring (their
@@ -913,7 +966,8 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         const cuuint64_t dims[4] = {(cuuint64_t)c.cin, (cuuint64_t)c.iw, (cuuint64_t)c.ih, (cuuint64_t)c.n};
         const cuuint64_t strides[3] = {(cuuint64_t)c.x_stride * 4, (cuuint64_t)c.x_stride * 4 * c.iw,
                                        (cuuint64_t)c.x_stride * 4 * c.iw * c.ih};
-        const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.bw * (cuuint32_t)c.sw, g.bh * (cuuint32_t)c.sh, 1};
+        const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.bw * (cuuint32_t)c.sw,
+                                   g.halo ? g.bh + (cuuint32_t)c.kh - 1 : g.bh * (cuuint32_t)c.sh, 1};
         const cuuint32_t estr[4] = {1, (cuuint32_t)c.sw, (cuuint32_t)c.sh, 1};
         r = enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)abase, dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -952,6 +1006,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.k_per_split = g.k_per_split; a.kblocks = g.kblocks; a.stages = g.stages; a.tmem_cols = g.tmem_cols;
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
     a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
+    a.halo = g.halo; a.a_bytes = g.a_bytes;
     a.out_off = g.out_off; a.shared_off = g.shared_off;
     a.ws = nullptr;
     a.tickets = nullptr;
