@@ -424,10 +424,43 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
                              (!a.res || (a.r_stride % 4 == 0 && a.r_coff % 4 == 0)) && d.dil == 1 &&
                              d.kh == d.kw && d.sh == d.sw && (d.kh == 3 || d.kh == 5) && (d.sh == 1 || d.sh == 2) &&
                              (long long)d.n * p->oh * ((p->ow + 3) / 4) * (d.cout / 4) + 256 < (1ll << 31);
-        if (blocked) {
+        // Large frames take the shared-memory halo tiles (8 x 16 output
+        // pixels at stride 1, else 8 x 8; one 32-channel slice per CTA);
+        // small frames (the deep 10x18 / 20x36 layers) would waste most of a
+        // tile and re-read wide halos, and keep the register-blocked kernel.
+        const bool tiled = blocked && p->oh >= 40 && p->ow >= 64;
+        if (tiled) {
+            DwTile tg;
+            const bool wide = d.sh == 1 && p->ow > 12;
+            const int TW = wide ? 16 : 8;
+            tg.tiles_x = (int)((p->ow + TW - 1) / TW);
+            tg.tiles_y = (int)((p->oh + 7) / 8);
+            tg.slices = (int)((d.cout + 31) / 32);
+            const long long blocks = (long long)d.n * tg.tiles_y * tg.tiles_x * tg.slices;
+            if (blocks >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "depthwise grid too large; split the batch");
+#define AIE_DWT(S_, K_, ST_, TW_)                                                                             \
+    do {                                                                                                      \
+        using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
+        static bool attr_ = false;                                                                            \
+        if (!attr_) {                                                                                         \
+            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<S_, K_, ST_, TW_>,                                   \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
+            attr_ = true;                                                                                     \
+        }                                                                                                     \
+        dw_tile_kernel<S_, K_, ST_, TW_><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(a, tg);                  \
+    } while (0)
+#define AIE_DWT2(S_)                                                         \
+    if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWT(S_, 3, 1, 16); else AIE_DWT(S_, 3, 1, 8); } \
+    else if (d.kh == 3) AIE_DWT(S_, 3, 2, 8);                               \
+    else if (d.sh == 1) { if (wide) AIE_DWT(S_, 5, 1, 16); else AIE_DWT(S_, 5, 1, 8); } \
+    else AIE_DWT(S_, 5, 2, 8);
+            if (p->strict) { AIE_DWT2(true) } else { AIE_DWT2(false) }
+#undef AIE_DWT2
+#undef AIE_DWT
+        } else if (blocked) {
             // 4 output pixels per thread (8 measured slower on B200: fewer
             // threads in flight for the same bytes)
-            const int PB = 4;
+            constexpr int PB = 4;
             DwGrid gd;
             gd.segs_per_row = (int)((p->ow + PB - 1) / PB);
             gd.cg = (int)(d.cout / 4);
@@ -436,11 +469,7 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
             gd.div_oh = make_fastdiv((int)p->oh);
             const long long threads = (long long)d.n * p->oh * gd.segs_per_row * gd.cg;
             const unsigned grid = (unsigned)((threads + 255) / 256);
-#define AIE_DW(S_, K_, ST_)                                                          \
-    do {                                                                             \
-        if (PB == 8) dw_block_kernel<S_, K_, ST_, 8><<<grid, 256, 0, s>>>(a, gd);    \
-        else dw_block_kernel<S_, K_, ST_, 4><<<grid, 256, 0, s>>>(a, gd);            \
-    } while (0)
+#define AIE_DW(S_, K_, ST_) dw_block_kernel<S_, K_, ST_, PB><<<grid, 256, 0, s>>>(a, gd)
 #define AIE_DW2(S_)                                            \
     if (d.kh == 3 && d.sh == 1) AIE_DW(S_, 3, 1);              \
     else if (d.kh == 3) AIE_DW(S_, 3, 2);                      \

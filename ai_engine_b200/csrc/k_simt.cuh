@@ -725,6 +725,108 @@ namespace aie {
 // (bit-identical to ai-cpu's conv_dw) in strict mode, fused multiply-adds
 // otherwise.  Requires C % 4 == 0, aligned views, dilation 1.
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Depthwise conv, shared-memory halo tiles.  A CTA owns an 8 x TW block of
+// output pixels and one 32-channel slice; it stages the input halo
+// ((8-1)*S+K) x ((TW-1)*S+K) pixels x 32 channels with 16-byte cp.async
+// (coalesced 128-byte pixel slices, zero fill = padding), then each thread
+// computes 4 horizontally adjacent pixels x 4 channels from shared memory:
+// every input element is read from L2/HBM once per CTA and no per-tap global
+// address arithmetic remains.  Taps accumulate in (ky, kx) order, unfused in
+// strict mode (bit-identical to ai-cpu's conv_dw, dw.rs:40-204) and fused
+// otherwise.  Requires C % 4 == 0, 16-byte aligned views, dilation 1.
+// ---------------------------------------------------------------------------
+struct DwTile {
+    int tiles_x, tiles_y, slices;
+};
+
+template <int K, int S, int TW>
+struct DwTileGeom {
+    static constexpr int TH = 8, PB = 4, RUNS = TW / PB, NT = TH * RUNS * 8;
+    static constexpr int HH = (TH - 1) * S + K, HW = (TW - 1) * S + K;
+    static constexpr int SMEM = HH * HW * 8 * 16;
+};
+
+template <bool kStrict, int K, int S, int TW>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const ConvArgs a, const DwTile g)
+{
+    using G = DwTileGeom<K, S, TW>;
+    constexpr int TH = G::TH, PB = G::PB, RUNS = G::RUNS, NT = G::NT, HH = G::HH, HW = G::HW;
+    extern __shared__ float4 halo4[];  // [HH][HW][8 channel groups]
+    int b = blockIdx.x;
+    const int slice = b % g.slices;
+    b /= g.slices;
+    const int tx = b % g.tiles_x;
+    b /= g.tiles_x;
+    const int ty = b % g.tiles_y;
+    const int img = b / g.tiles_y;
+    const int c0 = slice * 32;
+    const int ncg = min(8, (a.cout - c0) >> 2);
+    const int iy0 = ty * TH * S - a.pt, ix0 = tx * TW * S - a.pl;
+    const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;
+    for (int i = threadIdx.x; i < HH * HW * 8; i += NT) {
+        const int cgi = i & 7, pix = i >> 3;
+        const int hy = pix / HW, hx = pix - hy * HW;
+        const int iy = iy0 + hy, ix = ix0 + hx;
+        const bool ok = cgi < ncg && iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
+        const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cgi * 4 : a.x;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(halo4 + i)),
+                     "l"(src), "r"(ok ? 16 : 0)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const int cgi = threadIdx.x & 7, run = (threadIdx.x >> 3) % RUNS, row = threadIdx.x / (8 * RUNS);
+    const int oy = ty * TH + row, ox0 = tx * TW + run * PB;
+    if (cgi >= ncg || oy >= a.oh || ox0 >= a.ow) return;
+    const int ch = c0 + cgi * 4;
+    const int cpad = ((a.cout + 3) >> 2) << 2;
+    const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.bias + ch));
+    float acc[PB][4];
+#pragma unroll
+    for (int p = 0; p < PB; p++) {
+        acc[p][0] = b4.x; acc[p][1] = b4.y; acc[p][2] = b4.z; acc[p][3] = b4.w;
+    }
+    constexpr int NJ = (PB - 1) * S + K;
+#pragma unroll
+    for (int ky = 0; ky < K; ky++) {
+        float4 wk[K];
+#pragma unroll
+        for (int kx = 0; kx < K; kx++) wk[kx] = __ldg(reinterpret_cast<const float4 *>(a.w + (ky * K + kx) * cpad + ch));
+        const float4 *hr = halo4 + ((row * S + ky) * HW + run * PB * S) * 8 + cgi;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const float4 xv = hr[j * 8];
+#pragma unroll
+            for (int p = 0; p < PB; p++) {
+                const int kx = j - p * S;
+                if (kx >= 0 && kx < K) {
+                    acc[p][0] = madd<kStrict>(acc[p][0], xv.x, wk[kx].x);
+                    acc[p][1] = madd<kStrict>(acc[p][1], xv.y, wk[kx].y);
+                    acc[p][2] = madd<kStrict>(acc[p][2], xv.z, wk[kx].z);
+                    acc[p][3] = madd<kStrict>(acc[p][3], xv.w, wk[kx].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < PB; p++) {
+        const int ox = ox0 + p;
+        if (ox >= a.ow) break;
+        epi_act_n<kStrict, 4>(a.act, acc[p], ch, a.cout);
+        const long long m = ((long long)img * a.oh + oy) * a.ow + ox;
+        if (a.res) {
+            const float4 r = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.r_stride + a.r_coff + ch));
+            acc[p][0] = add_res<kStrict>(acc[p][0], r.x); acc[p][1] = add_res<kStrict>(acc[p][1], r.y);
+            acc[p][2] = add_res<kStrict>(acc[p][2], r.z); acc[p][3] = add_res<kStrict>(acc[p][3], r.w);
+        }
+        *reinterpret_cast<float4 *>(a.y + m * a.y_stride + a.y_coff + ch) =
+            make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
+    }
+}
+
 struct DwGrid {
     int segs_per_row, cg;
     FastDiv div_cg, div_segs, div_oh;

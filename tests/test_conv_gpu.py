@@ -103,7 +103,10 @@ def test_pointwise_residual(cuda_ok, math, h, w, cin, cout, act, seed):
 
 DW_SHAPES = [(72, 128, 64, 3, 1), (36, 64, 96, 5, 2), (33, 17, 6, 3, 2), (16, 16, 10, 5, 1),
              # beyond the reference grid: the register-blocked variants (C % 4 == 0)
-             (20, 37, 64, 5, 1), (41, 72, 32, 3, 2), (10, 18, 512, 3, 1), (9, 7, 8, 5, 2)]
+             (20, 37, 64, 5, 1), (41, 72, 32, 3, 2), (10, 18, 512, 3, 1), (9, 7, 8, 5, 2),
+             # the shared-memory halo-tile variants (frames >= 40 x 64): ragged
+             # tiles, partial 32-channel slices, both strides and kernel sizes
+             (100, 150, 32, 3, 2), (44, 70, 36, 5, 1), (96, 130, 8, 5, 2), (41, 67, 48, 3, 1)]
 
 
 def dw_cases():
