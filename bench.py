@@ -286,6 +286,25 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = n * world * args.steps / (e2e_ms / 1000.0)
+
+    # ---- optional output gather (N > 1): every rank's masks into one
+    # buffer on rank 0 over NCCL; not part of the hot path, timed apart
+    gather = None
+    if world > 1:
+        from ai_engine_b200.dist import gather_outputs
+        mask = model.bufs[model.output]
+        gather_outputs(mask, n * world)  # warm-up (allocations, NCCL channels)
+        torch.cuda.synchronize()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        g0.record(stream)
+        for _ in range(reps):
+            gather_outputs(mask, n * world)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather = {"ms": round(max_over_ranks(g0.elapsed_time(g1)) / reps, 4),
+                  "bytes_per_rank": int(mask.numel() * 4), "collective": "all_gather_into_tensor (NCCL)"}
     model.release()
 
     if world > 1:
@@ -347,6 +366,8 @@ def main():
         "gpu_launches": len(ops) * args.steps,
         "clocks": sampler.summary(),
     }
+    if gather is not None:
+        line["gather"] = gather
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         v, dt, done = cpu_baseline(2 * threads, threads, min_seconds=10.0)
