@@ -28,12 +28,24 @@ template <int CIN, int S>
 struct StemTcLayout {
     static constexpr int HH = (kStemTile - 1) * S + 3, HW = HH;
     static constexpr int HROW = HW * CIN, HN = HH * HROW;
+    // TMA halo rows: the row's floats from a 16-byte-aligned start (up to 3
+    // floats early) rounded up to 16 bytes
+    static constexpr int BX = (HROW + 3 + 3) / 4 * 4;
+    static constexpr int HN_MAX = HH * BX > HN ? HH * BX : HN;
     static constexpr uint32_t kHaloOff = kStemABytes + kStemBBytes;
-    static constexpr uint32_t kHaloFloats = (HN + 3) / 4 * 4;
+    // each halo buffer starts 256-byte aligned (a TMA destination must be at
+    // least 128-byte aligned)
+    static constexpr uint32_t kHaloFloats = (HN_MAX + 63) / 64 * 64;
     static constexpr uint32_t kBiasOff = kHaloOff + 2 * kHaloFloats * 4;
     static constexpr uint32_t kBarOff = kBiasOff + kStemCout * 4;
-    static constexpr uint32_t kBytes = kBarOff + 16 + 1024;  // + slack to 1024-align the base
+    static constexpr uint32_t kBytes = kBarOff + 32 + 1024;  // + slack to 1024-align the base
+    static_assert(kHaloOff % 256 == 0 && (kHaloFloats * 4) % 256 == 0, "TMA halo buffers 256-byte aligned");
+    static_assert(kBarOff % 8 == 0, "mbarriers 8-byte aligned");
 };
+
+// First float of the halo row for a tile starting at column ix0, rounded
+// down to a 16-byte boundary (TMA's innermost coordinate rule).
+__device__ __forceinline__ int stem_row_start(int ix0, int cin) { return (ix0 * cin) & ~3; }
 
 // byte offset of element (row, k) in a K-major operand with 128-byte rows
 // and the 128-byte swizzle (16-byte chunk index XOR row % 8)
@@ -42,8 +54,12 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int k)
     return (uint32_t)(row * 128 + ((((k >> 2) ^ row) & 7) << 4) + ((k & 3) << 2));
 }
 
-template <int CIN, int S>
-__global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs a, const StemGeom g)
+// kTma: the dense input (pixel stride = cin, 16-byte aligned rows) is staged
+// with one 3-D TMA box (W*cin floats, H, N) per tile -- out-of-frame rows and
+// columns read as zeros -- instead of one 4-byte cp.async per element.
+template <int CIN, int S, bool kTma>
+__global__ void __launch_bounds__(kStemThreads, 3)
+    stem_tc_kernel(const __grid_constant__ CUtensorMap tmx, const ConvArgs a, const StemGeom g)
 {
     using L = StemTcLayout<CIN, S>;
     constexpr int K = 9 * CIN;
@@ -55,7 +71,9 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs
     float *halo = reinterpret_cast<float *>(smem + L::kHaloOff);
     float *sbias = reinterpret_cast<float *>(smem + L::kBiasOff);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kBarOff + 8);
+    uint64_t *hbar = bar + 1;  // [2] halo buffer full (TMA path)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kBarOff + 24);
+    constexpr int ROW = kTma ? L::BX : L::HROW;  // halo row stride in floats
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tiles_per_img = g.tiles_x * g.tiles_y;
     const int ntiles = a.n * tiles_per_img;
@@ -78,6 +96,17 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs
         }
     };
 
+    // one TMA box per tile (thread 0): rows [iy0, iy0 + HH) of the frame,
+    // floats [start, start + BX) of each row
+    auto stage_tma = [&](int t, int buf) {
+        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
+        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int iy0 = ty * kStemTile * S - a.pt, ix0 = tx * kStemTile * S - a.pl;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of the buffer
+        mbar_expect_tx(&hbar[buf], (uint32_t)(L::HH * L::BX * 4));
+        tma_load_3d(halo + buf * L::kHaloFloats, &tmx, &hbar[buf], stem_row_start(ix0, CIN), iy0, img);
+    };
+
     // B operand: packed weights [k][wn] -> rows n (output channel), K-major
     for (int i = tid; i < kStemCout * 32; i += kStemThreads) {
         const int n = i >> 5, k = i & 31;
@@ -86,6 +115,8 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs
     if (tid < kStemCout) sbias[tid] = __ldg(a.bias + tid);
     if (tid == 0) {
         mbar_init(bar, 1);
+        mbar_init(&hbar[0], 1);
+        mbar_init(&hbar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -103,27 +134,60 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs
 
     uint32_t phase = 0;
     bool failed = false, mma_pending = false;
+    uint32_t halo_pending = 0;  // TMA path, thread 0: buffers with a copy in flight
+    uint32_t halo_parity = 0;   // ... and the phase parity each of those copies completes
     int t = blockIdx.x;
-    if (t < ntiles) stage(t, 0);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    if constexpr (kTma) {
+        if (t < ntiles && tid == 0) {
+            stage_tma(t, 0);
+            halo_pending |= 1u;  // use 0 of buffer 0: parity 0
+        }
+    } else {
+        if (t < ntiles) stage(t, 0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     for (int i = 0; t < ntiles; t += gridDim.x, i++) {
         const int tn = t + gridDim.x;
-        if (tn < ntiles) stage(tn, (i + 1) & 1);  // prefetch the next tile's halo
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");  // this tile's halo has landed
+        if constexpr (kTma) {
+            // prefetch the next tile's halo: its buffer was last read by the
+            // previous tile's im2col, which every thread finished before the
+            // previous tile's MMA barrier
+            if (tn < ntiles && tid == 0) {
+                const int nb = (i + 1) & 1;
+                stage_tma(tn, nb);
+                halo_pending |= 1u << nb;
+                halo_parity = (halo_parity & ~(1u << nb)) | ((((uint32_t)(i + 1) >> 1) & 1u) << nb);
+            }
+            if (!mbar_wait(&hbar[i & 1], (uint32_t)(i >> 1) & 1)) {
+                report_error(0x03000002u);
+                failed = true;
+            } else if (tid == 0) {
+                halo_pending &= ~(1u << (i & 1));
+            }
+        } else {
+            if (tn < ntiles) stage(tn, (i + 1) & 1);  // prefetch the next tile's halo
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            asm volatile("cp.async.wait_group 1;" ::: "memory");  // this tile's halo has landed
+        }
         tc_fence_before();
         if (__syncthreads_or(failed)) break;
         tc_fence_after();
 
         // ---- im2col: this thread's pixel -> A row `tid`, k = (ky*3 + kx)*CIN + ic
         {
-            const float *hp = halo + (i & 1) * L::kHaloFloats + (tid >> 4) * S * L::HROW + (tid & 15) * S * CIN;
+            int hoff = 0;  // TMA path: the row data starts up to 3 floats into the row
+            if constexpr (kTma) {
+                const int rem = t % tiles_per_img, tx = rem % g.tiles_x;
+                const int ix0 = tx * kStemTile * S - a.pl;
+                hoff = ix0 * CIN - stem_row_start(ix0, CIN);
+            }
+            const float *hp = halo + (i & 1) * L::kHaloFloats + hoff + (tid >> 4) * S * ROW + (tid & 15) * S * CIN;
             float v[32];
 #pragma unroll
             for (int k = 0; k < 32; k++) {
                 if (k < K) {
                     const int tap = k / CIN, ic = k - tap * CIN;
-                    v[k] = hp[(tap / 3) * L::HROW + (tap % 3) * CIN + ic];
+                    v[k] = hp[(tap / 3) * ROW + (tap % 3) * CIN + ic];
                 } else {
                     v[k] = 0.0f;
                 }
@@ -201,6 +265,11 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_tc_kernel(const ConvArgs
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (mma_pending && tid == 0) mbar_wait(bar, phase);  // drain before the TMEM is released
+    if constexpr (kTma) {
+        // a prefetch left in flight by an early exit must land before the CTA ends
+        for (int b = 0; b < 2; b++)
+            if (tid == 0 && (halo_pending >> b & 1)) mbar_wait(&hbar[b], halo_parity >> b & 1);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -222,17 +291,35 @@ static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s)
     static_assert(kStemCtasPerSm * (L::kBytes + 1024) <= 228 * 1024, "shared memory for three CTAs per SM");
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(stem_tc_kernel<CIN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)L::kBytes);
-        if (e != cudaSuccess) return -1;
-        e = cudaFuncSetAttribute(stem_tc_kernel<CIN, S>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 (int)cudaSharedmemCarveoutMaxShared);
-        if (e != cudaSuccess) return -1;
+        for (auto fn : {stem_tc_kernel<CIN, S, true>, stem_tc_kernel<CIN, S, false>}) {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes);
+            if (e != cudaSuccess) return -1;
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+            if (e != cudaSuccess) return -1;
+        }
         attr_set = true;
     }
     const long long ntiles = (long long)a.n * g.tiles_x * g.tiles_y;
     const unsigned grid = (unsigned)std::min<long long>(ntiles, (long long)kStemCtasPerSm * tc_sm_count());
-    stem_tc_kernel<CIN, S><<<grid, kStemThreads, L::kBytes, s>>>(a, g);
+    // TMA halo when the input is a dense, 16-byte aligned [n][ih][iw][cin] tensor
+    CUtensorMap tm;
+    memset(&tm, 0, sizeof tm);
+    const uintptr_t base = (uintptr_t)(a.x + a.x_coff);
+    const uint64_t row_bytes = (uint64_t)a.iw * CIN * 4;
+    PFN_encodeTiled enc = tc_encoder();
+    bool tma = enc && a.x_stride == CIN && a.x_coff == 0 && base % 16 == 0 && row_bytes % 16 == 0;
+    if (tma) {
+        const cuuint64_t dims[3] = {(cuuint64_t)a.iw * CIN, (cuuint64_t)a.ih, (cuuint64_t)a.n};
+        const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)row_bytes * a.ih};
+        const cuuint32_t box[3] = {(cuuint32_t)L::BX, (cuuint32_t)L::HH, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        tma = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    if (tma) stem_tc_kernel<CIN, S, true><<<grid, kStemThreads, L::kBytes, s>>>(tm, a, g);
+    else stem_tc_kernel<CIN, S, false><<<grid, kStemThreads, L::kBytes, s>>>(tm, a, g);
     return 0;
 }
 

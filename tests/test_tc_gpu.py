@@ -289,6 +289,8 @@ STEM_TC = [  # n, ih, iw, cin, stride, pad (t, l, b, r), act
     (1, 17, 16, 2, 1, (1, 1, 1, 1), "sigmoid"),
     (2, 64, 64, 3, 1, (1, 1, 1, 1), "relu6"),
     (1, 5, 7, 3, 2, (1, 1, 1, 1), "none"),          # smaller than one tile
+    (12, 160, 288, 3, 2, (1, 1, 1, 1), "relu"),      # 540 tiles: more than the resident CTAs,
+                                                     # so each CTA cycles both halo buffers
 ]
 
 
