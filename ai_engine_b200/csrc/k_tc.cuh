@@ -88,7 +88,10 @@ struct TcArgs {
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
     uint32_t b_resident, bres_off, res_off, pipes, halo, a_bytes;
-    uint64_t units;
+    uint64_t units;                   // < 2^31 (checked at launch)
+    FastDiv div_ntiles, div_split;    // unit -> (m tile, n tile, split)
+    FastDiv div_perimg, div_tilesx;   // m tile -> (frame, tile row, tile column)
+    uint32_t lbw;                     // log2(bw): bw is a power of two
     float *ws;            // split-K partials [tile][split][128][bn]
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
     uint32_t out_off, shared_off;  // shared-memory carve-up (bytes)
@@ -311,29 +314,47 @@ struct TcUnit {
     uint32_t mt, nt, s;
 };
 
-__device__ __forceinline__ TcUnit tc_unit(const TcArgs &a, uint64_t u)
+// 32-bit multiply-high divisions: a 64-bit division has no hardware divider
+// and cost ~1 us per tile in the epilogue
+__device__ __forceinline__ TcUnit tc_unit(const TcArgs &a, uint64_t u64)
 {
+    const int u = (int)u64;
     TcUnit t;
-    t.nt = (uint32_t)(u % a.n_tiles);
-    const uint64_t r = u / a.n_tiles;
-    t.s = (uint32_t)(r % a.split);
-    t.mt = (uint32_t)(r / a.split);
+    const int r = fdiv(u, a.div_ntiles);
+    t.nt = (uint32_t)(u - r * (int)a.n_tiles);
+    const int q = fdiv(r, a.div_split);
+    t.s = (uint32_t)(r - q * (int)a.split);
+    t.mt = (uint32_t)q;
     return t;
 }
 
-// Output pixel of accumulator row `row` of M tile `mt`, or -1 if outside.
-__device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, uint32_t row)
+// First output pixel (frame, row, column) of k x k M tile mt
+struct TcOrigin {
+    int img, oy0, ox0;
+};
+
+__device__ __forceinline__ TcOrigin tc_origin(const TcArgs &a, uint32_t mt)
+{
+    TcOrigin o;
+    o.img = fdiv((int)mt, a.div_perimg);
+    const int rem = (int)mt - o.img * (int)(a.tiles_x * a.tiles_y);
+    const int ty = fdiv(rem, a.div_tilesx), tx = rem - ty * (int)a.tiles_x;
+    o.oy0 = ty * (int)a.bh;
+    o.ox0 = tx * (int)a.bw;
+    return o;
+}
+
+// Output pixel of accumulator row `row` of M tile `mt` (origin o for k x k
+// tiles), or -1 if outside.
+__device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, const TcOrigin &o, uint32_t row)
 {
     if (!a.igemm) {
         const long long m = (long long)mt * kTcBM + row;
         return m < a.c.M ? m : -1;
     }
-    const uint32_t per_img = a.tiles_x * a.tiles_y;
-    const uint32_t img = mt / per_img, rem = mt - img * per_img;
-    const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
-    const int oy = (int)(ty * a.bh + row / a.bw), ox = (int)(tx * a.bw + row % a.bw);
+    const int oy = o.oy0 + (int)(row >> a.lbw), ox = o.ox0 + (int)(row & (a.bw - 1));
     if (oy >= a.c.oh || ox >= a.c.ow) return -1;
-    return ((long long)img * a.c.oh + oy) * a.c.ow + ox;
+    return ((long long)o.img * a.c.oh + oy) * a.c.ow + ox;
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -434,26 +455,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (a.halo) {
                     // stage = column shift kx (= tap here), K block kb: rows
                     // [ybase, ybase + bh + kh - 1) x the bw columns at xbase + kx
-                    const uint32_t per_img = a.tiles_x * a.tiles_y;
-                    const int img = (int)(t.mt / per_img);
-                    const uint32_t rem = t.mt - img * per_img;
-                    const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
-                    const int ybase = (int)(ty * a.bh) - a.c.pt;
-                    const int xbase = (int)(tx * a.bw) - a.c.pl;
-                    tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + (int)tap, ybase, img);
+                    const TcOrigin o = tc_origin(a, t.mt);
+                    tma_load_4d(sa, &tmA, &sh.full[s], kc, o.ox0 - a.c.pl + (int)tap, o.oy0 - a.c.pt, o.img);
                     if (!a.b_resident)
                         for (int ky = 0; ky < a.c.kh; ky++)
                             tma_load_3d(sb + ky * a.b_bytes, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn),
                                         ky * a.c.kw + (int)tap);
                 } else if (a.igemm) {
-                    const uint32_t per_img = a.tiles_x * a.tiles_y;
-                    const int img = (int)(t.mt / per_img);
-                    const uint32_t rem = t.mt - img * per_img;
-                    const uint32_t ty = rem / a.tiles_x, tx = rem - ty * a.tiles_x;
-                    const int ybase = (int)(ty * a.bh) * a.c.sh - a.c.pt;
-                    const int xbase = (int)(tx * a.bw) * a.c.sw - a.c.pl;
+                    const TcOrigin o = tc_origin(a, t.mt);
+                    const int ybase = o.oy0 * a.c.sh - a.c.pt;
+                    const int xbase = o.ox0 * a.c.sw - a.c.pl;
                     const int ky = (int)(tap / a.c.kw), kx = (int)(tap - ky * a.c.kw);
-                    tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + kx * a.c.dil, ybase + ky * a.c.dil, img);
+                    tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + kx * a.c.dil, ybase + ky * a.c.dil, o.img);
                 } else {
                     tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                 }
@@ -690,8 +703,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int nbase = (int)(t.nt * a.bn);
             const uint32_t tbase = tmem + ((quad * 32) << 16) + ab * a.bn;
             const uint64_t tile = (uint64_t)t.mt * a.n_tiles + t.nt;
+            const TcOrigin org = a.igemm ? tc_origin(a, t.mt) : TcOrigin{0, 0, 0};
 #pragma unroll
-            for (int i = 0; i < 8; i++) mrow[i] = (int)tc_row_pixel(a, t.mt, quad * 32 + i * 4 + (lane >> 3));
+            for (int i = 0; i < 8; i++) mrow[i] = (int)tc_row_pixel(a, t.mt, org, quad * 32 + i * 4 + (lane >> 3));
             if (t.nt != bias_nt) {
                 __syncwarp();
                 for (int i = lane; i < 256; i += 32) bcache[i] = (nbase + i < c.cout) ? __ldg(c.bias + nbase + i) : 0.0f;
@@ -1007,6 +1021,17 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
     a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
     a.halo = g.halo; a.a_bytes = g.a_bytes;
+    if (g.units >= (1ull << 31) || (uint64_t)g.m_tiles * g.n_tiles * g.split >= (1ull << 31)) {
+        snprintf(err, errlen, "too many tensor-core tiles in one call (%llu); split the batch",
+                 (unsigned long long)g.units);
+        return -2;
+    }
+    a.div_ntiles = make_fastdiv((int)g.n_tiles);
+    a.div_split = make_fastdiv((int)g.split);
+    a.div_perimg = make_fastdiv((int)std::max<uint32_t>(1, g.tiles_x * g.tiles_y));
+    a.div_tilesx = make_fastdiv((int)std::max<uint32_t>(1, g.tiles_x));
+    a.lbw = 0;
+    while ((1u << a.lbw) < g.bw) a.lbw++;
     a.out_off = g.out_off; a.shared_off = g.shared_off;
     a.ws = nullptr;
     a.tickets = nullptr;
