@@ -403,7 +403,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // that pipeline's iterations q, q+LQ, q+2LQ, ... (q = l / pipes), each
         // lane on its own: a lane waits only for the stage it fills next.
         const uint32_t P = a.pipes, RS = a.stages / a.pipes;
-        const uint32_t LQ = min((uint32_t)kTcIssueLanes / P, RS);
+        // the lanes of one warp issue in lockstep rounds and a round waits for
+        // all of its stages, so a round leaves two stages of the ring in flight
+        const uint32_t LQ = max(1u, min((uint32_t)kTcIssueLanes / P, RS > 2 ? RS - 2 : 1u));
         const uint32_t pl = (uint32_t)lane % P, q = (uint32_t)lane / P;
         struct Cursor {
             uint32_t u;  // units < 2^32 (m tiles < 2^24)
