@@ -404,8 +404,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // lane on its own: a lane waits only for the stage it fills next.
         const uint32_t P = a.pipes, RS = a.stages / a.pipes;
         // the lanes of one warp issue in lockstep rounds and a round waits for
-        // all of its stages, so a round leaves two stages of the ring in flight
-        const uint32_t LQ = max(1u, min((uint32_t)kTcIssueLanes / P, RS > 2 ? RS - 2 : 1u));
+        // all of its stages, so a round leaves two stages of the ring in
+        // flight; more than 4 lanes measured no faster (about one box in
+        // flight per lane: 4 lanes already reach ~0.23 us per box per SM)
+        const uint32_t LQ = max(1u, min(min((uint32_t)kTcIssueLanes / P, 4u), RS > 2 ? RS - 2 : 1u));
         const uint32_t pl = (uint32_t)lane % P, q = (uint32_t)lane / P;
         struct Cursor {
             uint32_t u;  // units < 2^32 (m tiles < 2^24)
