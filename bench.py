@@ -33,6 +33,51 @@ BATCH = 256
 H, W = 160, 288
 
 
+# DRAM bytes per frame that each layer's launch moved (dram__bytes_read.sum +
+# dram__bytes_write.sum from one ncu capture of an eager step at 128 frames,
+# divided by 128; the capture command and the per-layer table sit with the
+# ncu summaries under profiles/).  Traffic scales with frames, so the
+# roofline's per-launch traffic is this times the batch.
+TRAFFIC_PER_FRAME = {
+    "stem": 1561896,
+    "e1.conv": 1689324,
+    "e1.pw": 375476,
+    "e2.conv": 371014,
+    "e2.pw": 277432,
+    "e3.dw5": 184758,
+    "e3.exp": 254280,
+    "e3.dw5s2": 558364,
+    "e3.proj": 139570,
+    "e4.0.exp": 70450,
+    "e4.0.dw3": 138600,
+    "e4.0.proj": 208764,
+    "e4.1.exp": 70452,
+    "e4.1.dw3": 138602,
+    "e4.1.proj": 208772,
+    "e5.exp": 71036,
+    "e5.dw3": 277100,
+    "e5.proj": 278804,
+    "e5.0.exp": 95090,
+    "e5.0.dw3": 423670,
+    "e5.0.proj": 463694,
+    "e5.1.exp": 94994,
+    "e5.1.dw3": 419244,
+    "e5.1.proj": 463698,
+    "head960": 298942,
+    "fpn.lat16": 694810,
+    "fpn.up16": 46598,
+    "fpn.lat8": 369666,
+    "fpn.up8": 445744,
+    "fpn.lat4": 1490640,
+    "fpn.smooth4": 866972,
+    "fpn.up4": 1359882,
+    "fpn.lat2": 4139136,
+    "head.dw3": 2577380,
+    "head.pw": 1499020,
+    "mask": 46602,
+}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -339,7 +384,9 @@ def main():
     else:
         roof = {"bound": "hbm", "achieved": dom["bytes"] / sec / 1e9, "peak": hbm, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = None
+    tpf = TRAFFIC_PER_FRAME.get(dom["op"])
+    roof["traffic"] = int(tpf * n) if tpf is not None else None
+    roof["traffic_src"] = "ncu dram bytes at 128 frames, scaled by frames" if tpf is not None else None
     roof["kernel"] = f"{dom['op']} ({dom['kernel']}/{dom['math']})"
     roof["share"] = dom["ms"] / float(per_op.sum())
     roof["peak_src"] = pk["src"] + (" (TF32 = bf16/2)" if roof["bound"] == "tensor" else "")
