@@ -188,6 +188,22 @@ class ConvPlan:
         return out
 
 
+def run_dw_pw(dw: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, out: Optional[torch.Tensor] = None,
+              stream=None) -> torch.Tensor:
+    """Depthwise conv `dw` and the 1x1 conv `pw` (cout <= 4) that consumes its
+    output, in one launch (aie_conv_run_dw_pw): the depthwise result never
+    reaches memory.  Raises AieError(AIE_E_UNSUPPORTED) for shapes the fused
+    kernel does not cover."""
+    if dw.w is None or pw.w is None:
+        raise RuntimeError("load_weights() first")
+    if out is None:
+        out = torch.empty(pw.out_shape(), dtype=torch.float32, device=x.device)
+    check(dw.lib.aie_conv_run_dw_pw(dw._h, pw._h, _dptr(x), C.c_void_p(dw.w.data_ptr()), C.c_void_p(dw.b.data_ptr()),
+                                    C.c_void_p(pw.w.data_ptr()), C.c_void_p(pw.b.data_ptr()), _dptr(out),
+                                    C.c_void_p(_stream_handle(stream))), "aie_conv_run_dw_pw")
+    return out
+
+
 def lower_conv(op: Conv2d, n: int, ih: int, iw: int, w: np.ndarray, bias: Optional[np.ndarray] = None, *,
                has_res: bool = False, layout: str = "nhwc", math: str = "auto", wfmt: str = "oihw",
                **kw) -> ConvPlan:

@@ -553,6 +553,63 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
     return AIE_OK;
 }
 
+extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *dw_w,
+                                  const void *dw_b, const void *pw_w, const void *pw_b, void *out, void *stream)
+{
+    if (!dw || !pw || !in || !dw_w || !dw_b || !pw_w || !pw_b || !out) return fail(AIE_E_INVALID, "null argument");
+    const aie_conv_desc &d = dw->d, &q = pw->d;
+    if (dw->kernel != AIE_KERNEL_DW || dw->strict || d.has_res || d.dil != 1 || d.kh != d.kw || d.sh != d.sw ||
+        (d.kh != 3 && d.kh != 5) || (d.sh != 1 && d.sh != 2) || d.cout % 4 || d.cout > 32)
+        return fail(AIE_E_UNSUPPORTED, "fused head: depthwise plan must be k3/k5, s1/s2, dil 1, cout %% 4 == 0 and <= 32, "
+                                       "no residual, not FP32_STRICT");
+    if (pw->kernel != AIE_KERNEL_PW_DOT || pw->strict || q.has_res || q.cin != d.cout || q.n != d.n ||
+        q.ih != dw->oh || q.iw != dw->ow)
+        return fail(AIE_E_UNSUPPORTED, "fused head: the 1x1 plan must be a cout <= 4 dot over the depthwise output "
+                                       "(no residual, not FP32_STRICT)");
+    if (((uintptr_t)dw_w | (uintptr_t)dw_b | (uintptr_t)pw_w | (uintptr_t)pw_b) % 16)
+        return fail(AIE_E_ALIGN, "weights/bias must be 16-byte aligned");
+    ConvArgs a = make_args(dw, in, dw_w, dw_b, nullptr, out);
+    if (!a.vec_x || a.x_coff % 4 || a.x_stride % 4)
+        return fail(AIE_E_ALIGN, "fused head: input rows must be 16-byte aligned");
+    PwHead hd;
+    hd.w = (const float *)pw_w;
+    hd.bias = (const float *)pw_b;
+    hd.y = (float *)out;
+    hd.y_stride = pw->y_stride;
+    hd.y_coff = pw->y_coff;
+    hd.cout = (int)q.cout;
+    hd.act = q.act;
+    hd.y_pad_to = pw->y_pad_to;
+    DwTile tg;
+    const bool wide = d.sh == 1 && dw->ow > 12;
+    const int TW = wide ? 16 : 8;
+    tg.tiles_x = (int)((dw->ow + TW - 1) / TW);
+    tg.tiles_y = (int)((dw->oh + 7) / 8);
+    tg.slices = 1;
+    const long long blocks = (long long)d.n * tg.tiles_y * tg.tiles_x;
+    if (blocks >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "fused head grid too large; split the batch");
+    cudaStream_t s = (cudaStream_t)stream;
+#define AIE_DWH(K_, ST_, TW_)                                                                                 \
+    do {                                                                                                      \
+        using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
+        static bool attr_ = false;                                                                            \
+        if (!attr_) {                                                                                         \
+            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<false, K_, ST_, TW_, true>,                          \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
+            attr_ = true;                                                                                     \
+        }                                                                                                     \
+        dw_tile_kernel<false, K_, ST_, TW_, true><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(a, tg, hd);      \
+    } while (0)
+    if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWH(3, 1, 16); else AIE_DWH(3, 1, 8); }
+    else if (d.kh == 3) AIE_DWH(3, 2, 8);
+    else if (d.sh == 1) { if (wide) AIE_DWH(5, 1, 16); else AIE_DWH(5, 1, 8); }
+    else AIE_DWH(5, 2, 8);
+#undef AIE_DWH
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "fused head launch");
+    return AIE_OK;
+}
+
 extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, uint32_t oh,
                                    uint32_t ow, int32_t mode, const void *add, int32_t act, void *out, void *stream)
 {

@@ -747,8 +747,23 @@ struct DwTileGeom {
     static constexpr int SMEM = HH * HW * 8 * 16;
 };
 
-template <bool kStrict, int K, int S, int TW>
-__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const ConvArgs a, const DwTile g)
+// Head mode (HEAD = true): the depthwise output feeds a 1x1 conv with at most
+// 4 outputs (a segmentation head) that is applied in the same kernel: each
+// thread dots its 4 channels of each of its 4 pixels with the 1x1 weights,
+// the 8 lanes of a pixel group (its 32 channels) reduce by warp shuffle, and
+// lane 0 of the group adds the bias, applies the activation and writes the
+// <= 4 outputs.  The depthwise output never reaches memory.
+struct PwHead {
+    const float *w;     // [cout][cin] (pw_dot packing), cin = the depthwise channels (<= 32)
+    const float *bias;  // [cout_pad4]
+    float *y;
+    long long y_stride;
+    int y_coff, cout, act, y_pad_to;
+};
+
+template <bool kStrict, int K, int S, int TW, bool HEAD = false>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const ConvArgs a, const DwTile g,
+                                                                            const PwHead hd = PwHead{})
 {
     using G = DwTileGeom<K, S, TW>;
     constexpr int TH = G::TH, PB = G::PB, RUNS = G::RUNS, NT = G::NT, HH = G::HH, HW = G::HW;
@@ -780,8 +795,9 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const
     __syncthreads();
     const int cgi = threadIdx.x & 7, run = (threadIdx.x >> 3) % RUNS, row = threadIdx.x / (8 * RUNS);
     const int oy = ty * TH + row, ox0 = tx * TW + run * PB;
-    if (cgi >= ncg || oy >= a.oh || ox0 >= a.ow) return;
-    const int ch = c0 + cgi * 4;
+    const bool valid = cgi < ncg && oy < a.oh && ox0 < a.ow;
+    if (!HEAD && !valid) return;  // head mode: every lane takes part in the shuffles
+    const int ch = c0 + (valid ? cgi : 0) * 4;
     const int cpad = ((a.cout + 3) >> 2) << 2;
     const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.bias + ch));
     float acc[PB][4];
@@ -810,6 +826,46 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const
                 }
             }
         }
+    }
+    if constexpr (HEAD) {
+        // partial dots of this lane's 4 channels, reduced over the 8 lanes of
+        // the pixel group: afterwards every lane holds every pixel's sums
+        float tot[PB][4];
+#pragma unroll
+        for (int p = 0; p < PB; p++) {
+            epi_act_n<kStrict, 4>(a.act, acc[p], ch, a.cout);
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                tot[p][o] = 0.0f;
+                if (o < hd.cout) {
+                    if (valid) {
+                        const float4 w = __ldg(reinterpret_cast<const float4 *>(hd.w + o * a.cout + ch));
+                        tot[p][o] = fmaf(acc[p][3], w.w, fmaf(acc[p][2], w.z, fmaf(acc[p][1], w.y, acc[p][0] * w.x)));
+                    }
+#pragma unroll
+                    for (int sh = 1; sh < 8; sh <<= 1) tot[p][o] += __shfl_xor_sync(0xffffffffu, tot[p][o], sh);
+                }
+            }
+        }
+        // lane cgi < PB of the group finishes pixel cgi: bias, activation on
+        // the real outputs only, store (padding lanes of a C4 view are zero)
+        const int ox = ox0 + cgi;
+        if (cgi < PB && oy < a.oh && ox < a.ow) {
+            float v[4];
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                float t = tot[0][o];
+#pragma unroll
+                for (int q = 1; q < PB; q++)
+                    if (cgi == q) t = tot[q][o];
+                v[o] = o < hd.cout ? act_apply(hd.act, t + __ldg(hd.bias + o)) : 0.0f;
+            }
+            float *yr = hd.y + (((long long)img * a.oh + oy) * a.ow + ox) * hd.y_stride + hd.y_coff;
+#pragma unroll
+            for (int o = 0; o < 4; o++)
+                if (o < hd.y_pad_to) yr[o] = v[o];
+        }
+        return;
     }
 #pragma unroll
     for (int p = 0; p < PB; p++) {

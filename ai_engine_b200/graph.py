@@ -22,7 +22,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from .conv import Conv2d, ConvPlan, resize_bilinear
+from .conv import Conv2d, ConvPlan, resize_bilinear, run_dw_pw
 
 
 @dataclass
@@ -34,6 +34,7 @@ class OpRecord:
     res: Optional[str] = None
     size: Optional[Tuple[int, int]] = None
     plan: Optional[ConvPlan] = None
+    head: Optional[ConvPlan] = None   # kind "dwpw": the fused 1x1 (cout <= 4) after the depthwise plan
 
 
 def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
@@ -63,7 +64,8 @@ class Model:
     """Load-time lowering + per-batch execution of a conv graph on one GPU."""
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
-                 in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, device=None):
+                 in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
+                 device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -87,6 +89,22 @@ class Model:
             for op in self.graph:
                 if op[0] == "resize" and op[4] is None and uses.get(op[1], 0) == 1 and op[1] != self.output:
                     fused_resize[op[1]] = op[2]
+        # Depthwise -> 1x1 head fusion (fuse_heads): a depthwise conv whose
+        # output only feeds a 1x1 conv with cout <= 4 runs with it as one
+        # launch (aie_conv_run_dw_pw) when both plans qualify.
+        head_of: Dict[str, tuple] = {}  # depthwise output name -> the consuming 1x1 op
+        if fuse_heads and math != "fp32_strict":
+            for op in self.graph:
+                if op[0] != "conv" or op[4] is not None:
+                    continue
+                cv: Conv2d = op[3]
+                prev = next((p for p in self.graph if p[1] == op[2]), None)
+                if (cv.kh == 1 and cv.kw == 1 and cv.sh == 1 and cv.sw == 1 and cv.cout <= 4 and cv.pad == (0, 0, 0, 0)
+                        and prev is not None and prev[0] == "conv" and prev[3].is_depthwise() and prev[4] is None
+                        and uses.get(prev[1], 0) == 1 and prev[1] != self.output and prev[3].cout <= 32
+                        and prev[3].cout % 4 == 0):
+                    head_of[prev[1]] = op
+        fused_heads = set(op[1] for op in head_of.values())
         with torch.cuda.device(self.device):
             self.bufs["input"] = torch.empty((n, *in_hwc), dtype=torch.float32, device=self.device)
             for op in self.graph:
@@ -94,6 +112,22 @@ class Model:
                 h, w, c = self.shapes[src]
                 if kind == "resize" and out in fused_resize:
                     continue
+                if out in fused_heads:
+                    continue  # recorded with its depthwise producer
+                if out in head_of:
+                    hop = head_of[out]
+                    rec = OpRecord("dwpw", hop[1], src, conv=op[3])
+                    rec.plan = ConvPlan(op[3], n, h, w, math=math, device=self.device)
+                    rec.plan.load_weights(*weights[out])
+                    oh, ow, oc = self.shapes[out]
+                    rec.head = ConvPlan(hop[3], n, oh, ow, math=math, device=self.device)
+                    rec.head.load_weights(*weights[hop[1]])
+                    if rec.plan.kernel == "dw" and rec.head.kernel == "pw_dot" and rec.plan.math != "fp32_strict":
+                        self.bufs[hop[1]] = torch.empty((n, *self.shapes[hop[1]]), dtype=torch.float32,
+                                                        device=self.device)
+                        self.ops.append(rec)
+                        continue
+                    fused_heads.discard(hop[1])  # plans do not qualify: run the two convs
                 rec = OpRecord(kind, out, src)
                 if kind == "conv":
                     rec.conv, rec.res = op[3], op[4]
@@ -114,7 +148,7 @@ class Model:
 
     # -- accounting ------------------------------------------------------------
     def conv_flops(self) -> int:
-        return sum(r.plan.flops for r in self.ops if r.plan is not None)
+        return sum(r.plan.flops + (r.head.flops if r.head is not None else 0) for r in self.ops if r.plan is not None)
 
     def layer_table(self):
         rows = []
@@ -131,6 +165,8 @@ class Model:
             out = self.bufs[r.out]
             if r.kind == "conv":
                 r.plan(src, self.bufs[r.res] if r.res else None, out=out, stream=stream)
+            elif r.kind == "dwpw":
+                run_dw_pw(r.plan, r.head, src, out=out, stream=stream)
             else:
                 oh, ow = r.size
                 resize_bilinear(src, oh, ow, add=self.bufs[r.res] if r.res else None, out=out, stream=stream)

@@ -244,7 +244,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     from ai_engine_b200 import segnet
-    from ai_engine_b200.conv import resize_bilinear
+    from ai_engine_b200.conv import resize_bilinear, run_dw_pw
     from ai_engine_b200.graph import Model
 
     n = args.batch
@@ -304,6 +304,8 @@ def main():
             src, out = model.bufs[r.src], model.bufs[r.out]
             if r.kind == "conv":
                 r.plan(src, model.bufs[r.res] if r.res else None, out=out)
+            elif r.kind == "dwpw":
+                run_dw_pw(r.plan, r.head, src, out=out)
             else:
                 resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
             ev[i + 1].record(stream)
@@ -364,7 +366,12 @@ def main():
     tf32_peak = pk["bf16_tflops"] / 2.0  # TF32 dense = half the bf16 rate
     layers = []
     for r, ms in zip(ops, per_op):
-        if r.plan is not None:
+        if r.kind == "dwpw":
+            # fused depthwise + 1x1 head: the intermediate is neither written nor read
+            inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout
+            fl, by = r.plan.flops + r.head.flops, r.plan.min_bytes + r.head.min_bytes - 2 * inter
+            kern, math = "dw+pw", r.plan.math
+        elif r.plan is not None:
             fl, by = r.plan.flops, r.plan.min_bytes
             kern, math = r.plan.kernel, r.plan.math
         else:

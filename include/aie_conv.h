@@ -195,6 +195,21 @@ AIE_API int aie_conv_pack_weights(const aie_plan *plan, int32_t wfmt, const floa
 AIE_API int aie_conv_run(const aie_plan *plan, const void *in, const void *dev_w, const void *dev_b, const void *res,
                  void *out, void *workspace, void *stream);
 
+/* Depthwise conv followed by the 1x1 conv that consumes its output, fused
+ * into one launch: the depthwise result never reaches memory.  This is the
+ * segmentation head of the MobileNet-style nets (dw k x k -> 1x1 to <= 4
+ * logits/mask channels).  `dw` must be a depthwise plan (k 3 or 5, stride 1
+ * or 2, dilation 1, cout a multiple of 4 and <= 32, no residual, not
+ * FP32_STRICT) over a dense input; `pw` a plan of kind AIE_KERNEL_PW_DOT
+ * over dw's output shape (cin = dw's cout, no residual, not FP32_STRICT).
+ * Weights and biases as packed for each plan; `out` is pw's output.
+ * Otherwise AIE_E_UNSUPPORTED: run the two plans with aie_conv_run.
+ * No counterpart in the reference, which dispatches the two convs in turn
+ * (ai-gpu-runtime's lower_op emits one spec per SwOp::Conv,
+ * crates/ai-gpu-runtime/src/lowering.rs:99-187). */
+AIE_API int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *dw_w,
+                       const void *dw_b, const void *pw_w, const void *pw_b, void *out, void *stream);
+
 /* Bilinear resize of a dense NHWC batch [n, ih, iw, c] to [n, oh, ow, c]
  * (crates/ai-core/src/reference/resize.rs:5-42; mode 0 = half_pixel,
  * 1 = asymmetric), then out = act(resized + add) when add is non-NULL

@@ -142,3 +142,32 @@ def test_views_and_c4_layout_strides(lib):
     assert st == 0
     st, _ = plan(lib, cin=6, in_stride=10, in_coff=5)
     assert st == -2
+
+
+def test_fused_head_rejects_plans_that_do_not_qualify(lib):
+    """aie_conv_run_dw_pw checks both plans before any device call."""
+    def mk(**kw):
+        d = _lib.ConvDesc()
+        base = dict(n=1, ih=8, iw=8, cin=16, cout=16, kh=3, kw=3, sh=1, sw=1, dil=1, groups=1, act=0, layout=0, math=0)
+        base.update(kw)
+        pad = base.pop("pad", (1, 1, 1, 1))
+        for k, v in base.items():
+            setattr(d, k, v)
+        for i in range(4):
+            d.pad[i] = pad[i]
+        h = C.c_void_p()
+        assert lib.aie_conv_plan(C.byref(d), C.byref(h)) == 0
+        return h
+    dw = mk(groups=16)
+    pw = mk(kh=1, kw=1, pad=(0, 0, 0, 0), cout=2)
+    conv = mk()
+    strict_dw = mk(groups=16, math=_lib.MATH_FP32_STRICT)
+    big_pw = mk(kh=1, kw=1, pad=(0, 0, 0, 0), cout=8)
+    other_shape = mk(kh=1, kw=1, pad=(0, 0, 0, 0), cout=2, ih=4)
+    p = C.c_void_p(16)
+    for a, b in [(conv, pw), (strict_dw, pw), (dw, big_pw), (dw, other_shape), (dw, conv)]:
+        assert lib.aie_conv_run_dw_pw(a, b, p, p, p, p, p, p, None) == -3
+        assert _lib.last_error()
+    assert lib.aie_conv_run_dw_pw(None, pw, p, p, p, p, p, p, None) == -2
+    for h in (dw, pw, conv, strict_dw, big_pw, other_shape):
+        lib.aie_plan_free(h)

@@ -266,3 +266,59 @@ def test_resize_bilinear_bit_exact(cuda_ok, c, ih, iw, oh, ow):
     want = oracle.add(oracle.resize_bilinear(x, oh, ow), add)
     got = resize_bilinear(torch.from_numpy(x).cuda(), oh, ow, add=torch.from_numpy(add).cuda()).cpu().numpy()
     assert np.array_equal(got, want)
+
+
+HEADS = [  # n, ih, iw, c, k, s, dw act, pw cout, pw act, layout
+    (2, 40, 72, 32, 3, 1, "relu", 1, "sigmoid", "nhwc"),      # the benchmark head's shape
+    (3, 33, 50, 16, 5, 2, "hardswish", 3, "none", "nhwc"),    # ragged tiles, k5 s2, 3 outputs
+    (1, 17, 9, 8, 3, 2, "relu6", 2, "sigmoid", "nhwc_c4"),    # narrow frame, C4 output padding
+    (2, 21, 30, 32, 5, 1, "none", 4, "relu", "nhwc"),
+]
+
+
+@pytest.mark.parametrize("n,ih,iw,c,k,s,act,cout,act2,layout", HEADS, ids=[f"{h[1]}x{h[2]}c{h[3]}k{h[4]}s{h[5]}" for h in HEADS])
+def test_fused_dw_pw_head(cuda_ok, n, ih, iw, c, k, s, act, cout, act2, layout):
+    """Depthwise + 1x1 (cout <= 4) in one launch equals the two convs run in
+    turn on the GPU (FFMA tolerance) and the ai-cpu restatement of the chain."""
+    from ai_engine_b200.conv import run_dw_pw
+    from oracle import XorShift32
+    dw_op = Conv2d.depthwise(c, k, s, act)
+    pw_op = Conv2d.pointwise(c, cout, act2)
+    x, wd, bd, _ = case_tensors(dw_op, n, ih, iw, 8300 + c + k, False)
+    dwp = ConvPlan(dw_op, n, ih, iw, math="ffma").load_weights(wd, bd)
+    rng = XorShift32(8400 + cout)
+    wp = rng.vec_f32(cout * c)
+    bp = (rng.vec_f32(cout) * 0.1).astype(np.float32)
+    pwp = ConvPlan(pw_op, n, dwp.oh, dwp.ow, math="ffma", layout=layout).load_weights(wp, bp)
+    assert dwp.kernel == "dw" and pwp.kernel == "pw_dot"
+    xd = torch.from_numpy(x).cuda()
+    fused = run_dw_pw(dwp, pwp, xd)
+    inter = dwp(xd)
+    pw_in = torch.from_numpy(pack.pack_nhwc(inter.cpu().numpy())).cuda() if layout == "nhwc_c4" else inter
+    ref = pwp(pw_in)
+    torch.cuda.synchronize()
+    got, want = fused.cpu().numpy(), ref.cpu().numpy()
+    if layout == "nhwc_c4":
+        assert not got[..., cout:].any(), "C4 padding lanes must be zero"
+        got, want = got[..., :cout], want[..., :cout]
+    scale = oracle.dot_scale(pw_op, inter.cpu().numpy(), wp, bp)
+    assert normalised_error(got, want, scale) <= TOL_FFMA
+    # against the CPU restatement of the two convs
+    want_dw, _ = oracle_conv(dw_op, x, wd, bd, None)
+    want_pw, _ = oracle_conv(pw_op, want_dw, wp, bp, None)
+    assert normalised_error(got, want_pw, scale) <= 10 * TOL_FFMA
+
+
+def test_model_head_fusion(cuda_ok):
+    """The benchmark network with its dw3 -> 1x1 sigmoid head fused equals
+    the same network run op by op (FFMA path)."""
+    from ai_engine_b200 import segnet
+    from ai_engine_b200.graph import Model
+    g = segnet.build_graph()
+    wts = segnet.init_weights(g)
+    x = torch.from_numpy(segnet.synthetic_input(2, seed=5)).cuda()
+    a = Model(g, wts, 2, (segnet.H, segnet.W, 3), math="ffma", fuse_heads=True)
+    b = Model(g, wts, 2, (segnet.H, segnet.W, 3), math="ffma", fuse_heads=False)
+    assert any(r.kind == "dwpw" for r in a.ops) and not any(r.kind == "dwpw" for r in b.ops)
+    d = (a.infer(x) - b.infer(x)).abs().max().item()
+    assert d <= 1e-5, d
