@@ -121,6 +121,25 @@ static bool tf32_eligible(const aie_plan &p, const char **why)
     return true;
 }
 
+// 4-D tensor map (cin, iw, ih, n) of a depthwise input view with a box of
+// (32 channels, hw, hh, 1) for dw_tile_kernel's TMA halo; false when the
+// view is not TMA-compatible (the kernel then stages with cp.async).
+static bool dw_tile_tmap(const ConvArgs &a, int hw, int hh, CUtensorMap *tm)
+{
+    memset(tm, 0, sizeof *tm);
+    PFN_encodeTiled enc = tc_encoder();
+    const uintptr_t base = (uintptr_t)(a.x + a.x_coff);
+    if (!enc || base % 16 || (a.x_stride * 4) % 16) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.iw, (cuuint64_t)a.ih, (cuuint64_t)a.n};
+    const cuuint64_t strides[3] = {(cuuint64_t)a.x_stride * 4, (cuuint64_t)a.x_stride * 4 * a.iw,
+                                   (cuuint64_t)a.x_stride * 4 * a.iw * a.ih};
+    const cuuint32_t box[4] = {32, (cuuint32_t)hw, (cuuint32_t)hh, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)base, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
 {
     if (!desc || !out) return fail(AIE_E_INVALID, "null argument");
@@ -443,11 +462,19 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
         static bool attr_ = false;                                                                            \
         if (!attr_) {                                                                                         \
-            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<S_, K_, ST_, TW_>,                                   \
+            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<S_, K_, ST_, TW_, false, true>,                      \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
+            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<S_, K_, ST_, TW_, false, false>,                     \
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
             attr_ = true;                                                                                     \
         }                                                                                                     \
-        dw_tile_kernel<S_, K_, ST_, TW_><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(a, tg);                  \
+        CUtensorMap tm_;                                                                                      \
+        if (dw_tile_tmap(a, G_::HW, G_::HH, &tm_))                                                            \
+            dw_tile_kernel<S_, K_, ST_, TW_, false, true><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, \
+                                                                                                 PwHead{});  \
+        else                                                                                                  \
+            dw_tile_kernel<S_, K_, ST_, TW_, false, false><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, \
+                                                                                                  PwHead{}); \
     } while (0)
 #define AIE_DWT2(S_)                                                         \
     if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWT(S_, 3, 1, 16); else AIE_DWT(S_, 3, 1, 8); } \
@@ -594,11 +621,17 @@ extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const 
         using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
         static bool attr_ = false;                                                                            \
         if (!attr_) {                                                                                         \
-            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<false, K_, ST_, TW_, true>,                          \
+            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<false, K_, ST_, TW_, true, true>,                    \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
+            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<false, K_, ST_, TW_, true, false>,                   \
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
             attr_ = true;                                                                                     \
         }                                                                                                     \
-        dw_tile_kernel<false, K_, ST_, TW_, true><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(a, tg, hd);      \
+        CUtensorMap tm_;                                                                                      \
+        if (dw_tile_tmap(a, G_::HW, G_::HH, &tm_))                                                            \
+            dw_tile_kernel<false, K_, ST_, TW_, true, true><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, hd); \
+        else                                                                                                  \
+            dw_tile_kernel<false, K_, ST_, TW_, true, false><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, hd); \
     } while (0)
     if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWH(3, 1, 16); else AIE_DWH(3, 1, 8); }
     else if (d.kh == 3) AIE_DWH(3, 2, 8);

@@ -744,7 +744,7 @@ template <int K, int S, int TW>
 struct DwTileGeom {
     static constexpr int TH = 8, PB = 4, RUNS = TW / PB, NT = TH * RUNS * 8;
     static constexpr int HH = (TH - 1) * S + K, HW = (TW - 1) * S + K;
-    static constexpr int SMEM = HH * HW * 8 * 16;
+    static constexpr int SMEM = HH * HW * 8 * 16 + 128;  // + slack for 128-byte alignment
 };
 
 // Head mode (HEAD = true): the depthwise output feeds a 1x1 conv with at most
@@ -761,13 +761,20 @@ struct PwHead {
     int y_coff, cout, act, y_pad_to;
 };
 
-template <bool kStrict, int K, int S, int TW, bool HEAD = false>
-__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const ConvArgs a, const DwTile g,
-                                                                            const PwHead hd = PwHead{})
+// kTma: the halo is one 4-D TMA box (32 channels, HW, HH, 1) of the input's
+// (cin, iw, ih, n) tensor map, issued by one thread -- out-of-range pixels and
+// channels read as zeros -- instead of one 16-byte cp.async per chunk with its
+// index arithmetic (the staging was a sixth of the kernel's instructions).
+template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
+    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const ConvArgs a, const DwTile g, const PwHead hd)
 {
     using G = DwTileGeom<K, S, TW>;
     constexpr int TH = G::TH, PB = G::PB, RUNS = G::RUNS, NT = G::NT, HH = G::HH, HW = G::HW;
-    extern __shared__ float4 halo4[];  // [HH][HW][8 channel groups]
+    extern __shared__ __align__(128) uint8_t dw_smem_raw[];
+    // [HH][HW][8 channel groups], 128-byte aligned (a TMA destination)
+    float4 *halo4 = reinterpret_cast<float4 *>((reinterpret_cast<uintptr_t>(dw_smem_raw) + 127) & ~uintptr_t(127));
+    __shared__ uint64_t halo_bar;
     int b = blockIdx.x;
     const int slice = b % g.slices;
     b /= g.slices;
@@ -778,21 +785,39 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT) dw_tile_kernel(const
     const int c0 = slice * 32;
     const int ncg = min(8, (a.cout - c0) >> 2);
     const int iy0 = ty * TH * S - a.pt, ix0 = tx * TW * S - a.pl;
-    const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;
-    for (int i = threadIdx.x; i < HH * HW * 8; i += NT) {
-        const int cgi = i & 7, pix = i >> 3;
-        const int hy = pix / HW, hx = pix - hy * HW;
-        const int iy = iy0 + hy, ix = ix0 + hx;
-        const bool ok = cgi < ncg && iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
-        const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cgi * 4 : a.x;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                         (uint32_t)__cvta_generic_to_shared(halo4 + i)),
-                     "l"(src), "r"(ok ? 16 : 0)
-                     : "memory");
+    if constexpr (kTma) {
+        if (threadIdx.x == 0) {
+            mbar_init(&halo_bar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(&halo_bar, (uint32_t)(HH * HW * 128));
+            tma_load_4d(halo4, &tmx, &halo_bar, c0, ix0, iy0, img);
+        }
+        // bounded wait; the outcome is made CTA-uniform (head mode shuffles)
+        const bool landed = mbar_wait(&halo_bar, 0);
+        if (!__syncthreads_and(landed)) {
+            if (threadIdx.x == 0) report_error(0x04000001u);
+            return;
+        }
+    } else {
+        const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;
+        for (int i = threadIdx.x; i < HH * HW * 8; i += NT) {
+            const int cgi = i & 7, pix = i >> 3;
+            const int hy = pix / HW, hx = pix - hy * HW;
+            const int iy = iy0 + hy, ix = ix0 + hx;
+            const bool ok = cgi < ncg && iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
+            const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cgi * 4 : a.x;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                             (uint32_t)__cvta_generic_to_shared(halo4 + i)),
+                         "l"(src), "r"(ok ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();
     const int cgi = threadIdx.x & 7, run = (threadIdx.x >> 3) % RUNS, row = threadIdx.x / (8 * RUNS);
     const int oy = ty * TH + row, ox0 = tx * TW + run * PB;
     const bool valid = cgi < ncg && oy < a.oh && ox0 < a.ow;
