@@ -663,6 +663,31 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     a.vec = c == 1 ? ((uintptr_t)out % 16 == 0 && ow % 4 == 0)
                    : ((c % 4 == 0) && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0 &&
                       (!add || (uintptr_t)add % 16 == 0));
+    // exact 2x half_pixel upsampling: the source-pixel-per-thread kernel
+    if (mode == 0 && oh == 2 * ih && ow == 2 * iw) {
+        const bool c4 = c % 4 == 0 && a.vec;
+        const bool c1 = c == 1 && iw % 4 == 0 && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0;
+        if (c4 || c1) {
+            Up2Args u;
+            u.x = (const float *)in;
+            u.add = (const float *)add;
+            u.y = (float *)out;
+            u.n = n; u.ih = ih; u.iw = iw; u.c = c; u.act = act;
+            const int G = c1 ? 1 : (int)(c / 4), Wt = c1 ? (int)(iw / 4) : (int)iw;
+            u.div_g = make_fastdiv(G);
+            u.div_w = make_fastdiv(Wt);
+            u.div_h = make_fastdiv((int)ih);
+            const long long threads = (long long)n * ih * Wt * G;
+            if (threads + 256 < (1ll << 31)) {
+                const unsigned grid = (unsigned)((threads + 255) / 256);
+                if (c1) resize_up2_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(u);
+                else resize_up2_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(u);
+                cudaError_t e = cudaGetLastError();
+                if (e != cudaSuccess) return cuda_fail(e, "resize launch");
+                return AIE_OK;
+            }
+        }
+    }
     a.px_per_thread = (c == 1 || (c % 4 == 0 && a.vec)) ? 4 : 1;
     a.div_cg = make_fastdiv(cg);
     a.div_owg = make_fastdiv((int)((ow + a.px_per_thread - 1) / a.px_per_thread));

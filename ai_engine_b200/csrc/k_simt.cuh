@@ -464,6 +464,104 @@ __device__ __forceinline__ float lerp2(float g00, float g01, float g10, float g1
     return __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
 }
 
+// Exact 2x upsampling in half_pixel mode (oh = 2*ih, ow = 2*iw; the FPN's
+// and the mask's resizes).  Output (2i+a, 2j+b) samples source rows
+// clamp(i-1+a), clamp(i+a) and columns clamp(j-1+b), clamp(j+b) with far
+// weight 0.75 (a = 0) or 0.25 (a = 1): exactly the values resize_axis
+// computes for this scale, combined in lerp2's order, so the result is bit
+// for bit the general kernel's.  One thread owns a source pixel and writes
+// its 2x2 output block from its 3x3 neighbourhood (2.25 loads per output
+// instead of 4); C4: 4 channels per thread (C % 4 == 0, aligned), else C == 1
+// with 4 source pixels per thread (iw % 4 == 0, aligned).
+struct Up2Args {
+    const float *x, *add;
+    float *y;
+    int n, ih, iw, c, act;
+    FastDiv div_g, div_w, div_h;  // thread -> (group, source column, source row)
+};
+
+__device__ __forceinline__ float up2_lerp(float g00, float g01, float g10, float g11, float tx, float ty)
+{
+    return lerp2(g00, g01, g10, g11, tx, __fsub_rn(1.0f, tx), ty, __fsub_rn(1.0f, ty));
+}
+
+template <bool C1>
+__global__ void __launch_bounds__(256) resize_up2_kernel(const Up2Args a)
+{
+    const int G = C1 ? 1 : a.c >> 2;                 // channel groups (C4) / 1
+    const int W = C1 ? a.iw >> 2 : a.iw;             // thread columns per source row
+    const int idx = blockIdx.x * 256 + threadIdx.x;  // < n*ih*W*G < 2^31 (checked on the host)
+    if (idx >= a.n * a.ih * W * G) return;
+    const int t = fdiv(idx, a.div_g), g = idx - t * G;
+    const int r = fdiv(t, a.div_w), jw = t - r * W;
+    const int img = fdiv(r, a.div_h), i = r - img * a.ih;
+    const int oh = 2 * a.ih, ow = 2 * a.iw;
+    const int rows[3] = {max(i - 1, 0), i, min(i + 1, a.ih - 1)};
+    const float *xb = a.x + (long long)img * a.ih * a.iw * a.c;
+    if constexpr (!C1) {
+        const int j = jw, c0 = g * 4;
+        const int cols[3] = {max(j - 1, 0), j, min(j + 1, a.iw - 1)};
+        float4 v[3][3];
+#pragma unroll
+        for (int rr = 0; rr < 3; rr++)
+#pragma unroll
+            for (int cc = 0; cc < 3; cc++)
+                v[rr][cc] = __ldg(reinterpret_cast<const float4 *>(xb + ((long long)rows[rr] * a.iw + cols[cc]) * a.c + c0));
+#pragma unroll
+        for (int ar = 0; ar < 2; ar++) {
+            const float ty = ar ? 0.25f : 0.75f;
+#pragma unroll
+            for (int bc = 0; bc < 2; bc++) {
+                const float tx = bc ? 0.25f : 0.75f;
+                const float4 g00 = v[ar][bc], g01 = v[ar][bc + 1], g10 = v[ar + 1][bc], g11 = v[ar + 1][bc + 1];
+                float o[4] = {up2_lerp(g00.x, g01.x, g10.x, g11.x, tx, ty), up2_lerp(g00.y, g01.y, g10.y, g11.y, tx, ty),
+                              up2_lerp(g00.z, g01.z, g10.z, g11.z, tx, ty), up2_lerp(g00.w, g01.w, g10.w, g11.w, tx, ty)};
+                const long long px = ((long long)img * oh + 2 * i + ar) * ow + 2 * j + bc;
+                if (a.add) {
+                    const float4 ad = __ldg(reinterpret_cast<const float4 *>(a.add + px * a.c + c0));
+                    o[0] = __fadd_rn(o[0], ad.x); o[1] = __fadd_rn(o[1], ad.y);
+                    o[2] = __fadd_rn(o[2], ad.z); o[3] = __fadd_rn(o[3], ad.w);
+                }
+                act_apply_strict_n<4>(a.act, o, c0, a.c);
+                *reinterpret_cast<float4 *>(a.y + px * a.c + c0) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    } else {
+        // 4 source pixels j0..j0+3 (one float4 per row) plus their left and
+        // right neighbours -> 8 output columns x 2 output rows
+        const int j0 = jw * 4;
+        float s[3][6];
+#pragma unroll
+        for (int rr = 0; rr < 3; rr++) {
+            const float *row = xb + (long long)rows[rr] * a.iw;
+            const float4 m = __ldg(reinterpret_cast<const float4 *>(row + j0));
+            s[rr][0] = __ldg(row + max(j0 - 1, 0));
+            s[rr][1] = m.x; s[rr][2] = m.y; s[rr][3] = m.z; s[rr][4] = m.w;
+            s[rr][5] = __ldg(row + min(j0 + 4, a.iw - 1));
+        }
+#pragma unroll
+        for (int ar = 0; ar < 2; ar++) {
+            const float ty = ar ? 0.25f : 0.75f;
+            float o[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const int bc = q & 1, k = (q >> 1) + bc;  // source columns k, k+1 of s (s[.][0] = j0-1)
+                const float tx = bc ? 0.25f : 0.75f;
+                o[q] = up2_lerp(s[ar][k], s[ar][k + 1], s[ar + 1][k], s[ar + 1][k + 1], tx, ty);
+            }
+            const long long px = ((long long)img * oh + 2 * i + ar) * ow + 2 * j0;
+            if (a.add) {
+#pragma unroll
+                for (int q = 0; q < 8; q++) o[q] = __fadd_rn(o[q], __ldg(a.add + px + q));
+            }
+            act_apply_strict_n<8>(a.act, o, 0, 0);
+            float4 *yr = reinterpret_cast<float4 *>(a.y + px);
+            yr[0] = make_float4(o[0], o[1], o[2], o[3]);
+            yr[1] = make_float4(o[4], o[5], o[6], o[7]);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a)
 {
     const int cg = (a.c + 3) >> 2;
