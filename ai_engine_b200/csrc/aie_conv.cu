@@ -277,6 +277,8 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
             g.halo_w = (g.tile_w - 1) * d.sw + d.kw;
             g.tiles_x = (p->ow + g.tile_w - 1) / g.tile_w;
             g.tiles_y = (p->oh + g.tile_h - 1) / g.tile_h;
+            g.div_tpi = make_fastdiv(g.tiles_x * g.tiles_y);
+            g.div_tx = make_fastdiv(g.tiles_x);
             p->stem_smem = (uint32_t)(g.halo_h * g.halo_w * d.cin * 4);
             p->tile_m = g.tile_h * g.tile_w;
             p->tile_n = d.cout;

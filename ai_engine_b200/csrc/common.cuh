@@ -238,6 +238,32 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, un
 
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) { return mbar_wait_for(bar, parity, kWaitNs); }
 
+// try_wait with a suspend-time hint: the thread may sleep (up to hint_ns)
+// until the phase completes instead of polling, which frees issue slots for
+// the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for waits many warps share (they sleep between checks).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtime();
+    while (!mbar_try_wait_sleep(bar, parity, 2000u))
+        if (gtime() - t0 > kWaitNs) return false;
+    return true;
+}
+
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1)
 {
     asm volatile(

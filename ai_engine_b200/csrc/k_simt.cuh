@@ -701,6 +701,7 @@ namespace aie {
 // ---------------------------------------------------------------------------
 struct StemGeom {
     int tile_h, tile_w, halo_h, halo_w, tiles_x, tiles_y;
+    FastDiv div_tpi, div_tx;  // tile -> (frame, tile row, tile column)
 };
 
 template <bool kStrict, int KH, int KW, int CIN, int S, int TH, int TW>

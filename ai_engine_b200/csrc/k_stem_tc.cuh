@@ -79,8 +79,8 @@ __global__ void __launch_bounds__(kStemThreads, 3)
     const int ntiles = a.n * tiles_per_img;
 
     auto stage = [&](int t, int buf) {
-        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
-        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int img = fdiv(t, g.div_tpi), rem = t - img * tiles_per_img;
+        const int ty = fdiv(rem, g.div_tx), tx = rem - ty * g.tiles_x;
         const int iy0 = ty * kStemTile * S - a.pt, ix0 = tx * kStemTile * S - a.pl;
         const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff;
         float *dst = halo + buf * L::kHaloFloats;
@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(kStemThreads, 3)
     // one TMA box per tile (thread 0): rows [iy0, iy0 + HH) of the frame,
     // floats [start, start + BX) of each row
     auto stage_tma = [&](int t, int buf) {
-        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
-        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+        const int img = fdiv(t, g.div_tpi), rem = t - img * tiles_per_img;
+        const int ty = fdiv(rem, g.div_tx), tx = rem - ty * g.tiles_x;
         const int iy0 = ty * kStemTile * S - a.pt, ix0 = tx * kStemTile * S - a.pl;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of the buffer
         mbar_expect_tx(&hbar[buf], (uint32_t)(L::HH * L::BX * 4));
@@ -148,6 +148,8 @@ __global__ void __launch_bounds__(kStemThreads, 3)
     }
     for (int i = 0; t < ntiles; t += gridDim.x, i++) {
         const int tn = t + gridDim.x;
+        const int t_img = fdiv(t, g.div_tpi), t_rem = t - t_img * tiles_per_img;
+        const int t_ty = fdiv(t_rem, g.div_tx), t_tx = t_rem - t_ty * g.tiles_x;
         if constexpr (kTma) {
             // prefetch the next tile's halo: its buffer was last read by the
             // previous tile's im2col, which every thread finished before the
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(kStemThreads, 3)
                 halo_pending |= 1u << nb;
                 halo_parity = (halo_parity & ~(1u << nb)) | ((((uint32_t)(i + 1) >> 1) & 1u) << nb);
             }
-            if (!mbar_wait(&hbar[i & 1], (uint32_t)(i >> 1) & 1)) {
+            if (!mbar_wait_sleep(&hbar[i & 1], (uint32_t)(i >> 1) & 1)) {
                 report_error(0x03000002u);
                 failed = true;
             } else if (tid == 0) {
@@ -177,8 +179,7 @@ __global__ void __launch_bounds__(kStemThreads, 3)
         {
             int hoff = 0;  // TMA path: the row data starts up to 3 floats into the row
             if constexpr (kTma) {
-                const int rem = t % tiles_per_img, tx = rem % g.tiles_x;
-                const int ix0 = tx * kStemTile * S - a.pl;
+                const int ix0 = t_tx * kStemTile * S - a.pl;
                 hoff = ix0 * CIN - stem_row_start(ix0, CIN);
             }
             const float *hp = halo + (i & 1) * L::kHaloFloats + hoff + (tid >> 4) * S * ROW + (tid & 15) * S * CIN;
@@ -214,7 +215,7 @@ __global__ void __launch_bounds__(kStemThreads, 3)
         }
         mma_pending = true;
         // warp-uniform outcome: the TMEM loads below are warp-collective
-        if (!__all_sync(0xffffffffu, mbar_wait(bar, phase))) {
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar, phase))) {
             if (lane == 0) report_error(0x03000001u);
             failed = true;
             continue;  // the next tile's barrier turns this into a CTA-wide exit
@@ -249,18 +250,17 @@ __global__ void __launch_bounds__(kStemThreads, 3)
                     make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
         }
         __syncwarp();
-        const int img = t / tiles_per_img, rem = t - img * tiles_per_img;
-        const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
-        const int oy0 = ty * kStemTile, ox0 = tx * kStemTile;
+        const int oy0 = t_ty * kStemTile, ox0 = t_tx * kStemTile;
+        const int c = lane & 7;                          // this lane's 4-channel chunk
+        const int mrow0 = (t_img * a.oh + oy0) * a.ow + ox0;  // first pixel of the tile (M < 2^31)
+        float *ybase = a.y + a.y_coff + 4 * c;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const int f = j * 32 + lane;
-            const int p = warp * 32 + (f >> 3), c = f & 7;  // pixel of the tile, 4-channel chunk
+            const int p = warp * 32 + j * 4 + (lane >> 3);  // pixel of the tile
             const float4 val = *reinterpret_cast<const float4 *>(sA + p * 128 + (((c ^ p) & 7) << 4));
-            const int oy = oy0 + (p >> 4), ox = ox0 + (p & 15);
-            if (oy < a.oh && ox < a.ow)
-                *reinterpret_cast<float4 *>(a.y + (((long long)img * a.oh + oy) * a.ow + ox) * a.y_stride + a.y_coff +
-                                            4 * c) = val;
+            const int dy = p >> 4, dx = p & 15;
+            if (oy0 + dy < a.oh && ox0 + dx < a.ow)
+                *reinterpret_cast<float4 *>(ybase + (long long)(mrow0 + dy * a.ow + dx) * a.y_stride) = val;
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
