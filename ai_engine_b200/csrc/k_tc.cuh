@@ -638,7 +638,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (res_tensor && a.split == 1) prefetch_res(nbase);  // first chunk, ahead of the MMA wait
             if (a.split == 1) {
-                const bool ok = !*abort_flag && mbar_wait(&sh.acc_full[ab], aph);
+                // the epilogue warps sleep on the accumulator barrier so that
+                // their polling does not take issue slots from the MMA and
+                // producer warps sharing their sub-partitions
+                const bool ok = !*abort_flag && mbar_wait_sleep(&sh.acc_full[ab], aph);
                 if (ok) {
                     tc_fence_after();
                     for (int c0 = 0; c0 < ncol; c0 += 32) {
@@ -665,7 +668,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sh.acc_empty[ab]);
             } else {
-                if (*abort_flag || !mbar_wait(&sh.acc_full[ab], aph)) {
+                if (*abort_flag || !mbar_wait_sleep(&sh.acc_full[ab], aph)) {
                     report_error(0x01000004);
                     *abort_flag = 1;
                     break;
