@@ -204,6 +204,20 @@ def run_dw_pw(dw: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, out: Optional[tor
     return out
 
 
+def input_u8(frames: torch.Tensor, layout: str = "nhwc", out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """u8 RGB / RGBA frames [n, h, w, 3|4] on the GPU -> the network's f32
+    input [n, h, w, 3] (NHWC) or [n, h, w, 4] (NHWC-C4), value / 255
+    (aie_input_u8)."""
+    if not frames.is_cuda or frames.dtype != torch.uint8 or frames.dim() != 4:
+        raise TypeError("frames must be a uint8 CUDA tensor [n, h, w, c]")
+    n, h, w, c = frames.shape
+    if out is None:
+        out = torch.empty((n, h, w, 4 if layout == "nhwc_c4" else 3), dtype=torch.float32, device=frames.device)
+    check(_lib.load().aie_input_u8(n, h, w, c, C.c_void_p(frames.data_ptr()), LAYOUT[layout], _dptr(out),
+                                   C.c_void_p(_stream_handle(stream))), "aie_input_u8")
+    return out
+
+
 def lower_conv(op: Conv2d, n: int, ih: int, iw: int, w: np.ndarray, bias: Optional[np.ndarray] = None, *,
                has_res: bool = False, layout: str = "nhwc", math: str = "auto", wfmt: str = "oihw",
                **kw) -> ConvPlan:

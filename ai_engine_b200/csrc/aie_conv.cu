@@ -645,6 +645,26 @@ extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const 
     return AIE_OK;
 }
 
+extern "C" int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, const void *in, int32_t layout,
+                            void *out, void *stream)
+{
+    if (!in || !out) return fail(AIE_E_INVALID, "null tensor pointer");
+    if (!n || !h || !w) return fail(AIE_E_INVALID, "zero-sized frame batch");
+    if (cin != 3 && cin != 4) return fail(AIE_E_INVALID, "u8 frames must be RGB (3) or RGBA (4), got %u", cin);
+    if (layout != AIE_LAYOUT_NHWC && layout != AIE_LAYOUT_NHWC_C4)
+        return fail(AIE_E_INVALID, "layout %d out of range", layout);
+    const int stride = layout == AIE_LAYOUT_NHWC_C4 ? 4 : 3;
+    if (stride == 4 && (uintptr_t)out % 16) return fail(AIE_E_ALIGN, "C4 output must be 16-byte aligned");
+    const long long npix = (long long)n * h * w;
+    const long long threads = (npix + 3) / 4;
+    if (threads >= (1ll << 31) * 256ll) return fail(AIE_E_UNSUPPORTED, "frame batch too large");
+    input_u8_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        (const uint8_t *)in, (float *)out, npix, (int)cin, stride);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "input staging launch");
+    return AIE_OK;
+}
+
 extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, uint32_t oh,
                                    uint32_t ow, int32_t mode, const void *add, int32_t act, void *out, void *stream)
 {

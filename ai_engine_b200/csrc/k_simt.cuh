@@ -464,6 +464,47 @@ __device__ __forceinline__ float lerp2(float g00, float g01, float g10, float g1
     return __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
 }
 
+// Input staging: interleaved u8 RGB (cin = 3) or RGBA (cin = 4, alpha
+// dropped) frames -> NHWC f32 in [0, 1], value = u8 / 255 with IEEE division
+// (the reference normalises camera frames the same way: `v as f32 / 255.0`
+// on the CPU, unorm texture sampling in ai-tasks' preprocess.wgsl:11-16).
+// One thread converts 4 pixels; the C4 layout writes the 4th lane as zero.
+__global__ void __launch_bounds__(256) input_u8_kernel(const uint8_t *__restrict__ in, float *__restrict__ out,
+                                                        long long npix, int cin, int cout_stride)
+{
+    const long long p0 = ((long long)blockIdx.x * 256 + threadIdx.x) * 4;
+    if (p0 >= npix) return;
+    const int np = (int)min(4ll, npix - p0);
+    uint8_t px[16];
+    if (np == 4 && cin == 3 && ((uintptr_t)(in + p0 * 3) & 3) == 0) {
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(in + p0 * 3);
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            const uint32_t v = __ldg(w + i);
+            px[4 * i] = v & 255; px[4 * i + 1] = (v >> 8) & 255; px[4 * i + 2] = (v >> 16) & 255; px[4 * i + 3] = v >> 24;
+        }
+    } else if (np == 4 && cin == 4 && ((uintptr_t)(in + p0 * 4) & 15) == 0) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(in + p0 * 4));
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            px[4 * i] = vv[i] & 255; px[4 * i + 1] = (vv[i] >> 8) & 255; px[4 * i + 2] = (vv[i] >> 16) & 255;
+            px[4 * i + 3] = vv[i] >> 24;
+        }
+    } else {
+        for (int i = 0; i < np * cin; i++) px[i] = in[p0 * cin + i];
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        if (q >= np) break;
+        float *o = out + (p0 + q) * cout_stride;
+        const float r = __fdiv_rn((float)px[q * cin], 255.0f), gch = __fdiv_rn((float)px[q * cin + 1], 255.0f),
+                    b = __fdiv_rn((float)px[q * cin + 2], 255.0f);
+        if (cout_stride == 4) *reinterpret_cast<float4 *>(o) = make_float4(r, gch, b, 0.0f);
+        else { o[0] = r; o[1] = gch; o[2] = b; }
+    }
+}
+
 // Exact 2x upsampling in half_pixel mode (oh = 2*ih, ow = 2*iw; the FPN's
 // and the mask's resizes).  Output (2i+a, 2j+b) samples source rows
 // clamp(i-1+a), clamp(i+a) and columns clamp(j-1+b), clamp(j+b) with far

@@ -22,7 +22,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from .conv import Conv2d, ConvPlan, resize_bilinear, run_dw_pw
+from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_dw_pw
 
 
 @dataclass
@@ -65,7 +65,7 @@ class Model:
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
                  in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
-                 device=None):
+                 input_u8: bool = False, device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -105,8 +105,17 @@ class Model:
                         and prev[3].cout % 4 == 0):
                     head_of[prev[1]] = op
         fused_heads = set(op[1] for op in head_of.values())
+        # input_u8: the batch arrives as u8 RGB frames ("input_u8", 3 bytes per
+        # pixel); the first op normalises them into the f32 "input" (u8 / 255)
+        self.input_u8 = input_u8
+        self.input_name = "input_u8" if input_u8 else "input"
         with torch.cuda.device(self.device):
             self.bufs["input"] = torch.empty((n, *in_hwc), dtype=torch.float32, device=self.device)
+            if input_u8:
+                if in_hwc[2] != 3:
+                    raise ValueError("u8 frames feed a 3-channel input")
+                self.bufs["input_u8"] = torch.empty((n, *in_hwc), dtype=torch.uint8, device=self.device)
+                self.ops.append(OpRecord("u8in", "input", "input_u8"))
             for op in self.graph:
                 kind, out, src = op[0], op[1], op[2]
                 h, w, c = self.shapes[src]
@@ -167,6 +176,8 @@ class Model:
                 r.plan(src, self.bufs[r.res] if r.res else None, out=out, stream=stream)
             elif r.kind == "dwpw":
                 run_dw_pw(r.plan, r.head, src, out=out, stream=stream)
+            elif r.kind == "u8in":
+                input_u8(src, out=out, stream=stream)
             else:
                 oh, ow = r.size
                 resize_bilinear(src, oh, ow, add=self.bufs[r.res] if r.res else None, out=out, stream=stream)
@@ -191,7 +202,7 @@ class Model:
 
     def infer(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
         if x is not None:
-            self.bufs["input"].copy_(x, non_blocking=True)
+            self.bufs[self.input_name].copy_(x, non_blocking=True)
         if self.graph_exec is not None:
             self.graph_exec.replay()
         else:
@@ -206,21 +217,23 @@ class Model:
         neighbouring batches use the other slots."""
         if slots < 2:
             raise ValueError("pipelining needs at least two slots")
-        in0, out0 = self.bufs["input"], self.bufs[self.output]
+        iname = self.input_name
+        in0, out0 = self.bufs[iname], self.bufs[self.output]
         self.in_slots = [in0] + [torch.empty_like(in0) for _ in range(slots - 1)]
         self.out_slots = [out0] + [torch.empty_like(out0) for _ in range(slots - 1)]
         self.slot_graphs = []
         try:
             for s in range(slots):
-                self.bufs["input"], self.bufs[self.output] = self.in_slots[s], self.out_slots[s]
+                self.bufs[iname], self.bufs[self.output] = self.in_slots[s], self.out_slots[s]
                 self.slot_graphs.append(self._capture_one())
         finally:
-            self.bufs["input"], self.bufs[self.output] = in0, out0
+            self.bufs[iname], self.bufs[self.output] = in0, out0
         self._copy_in = torch.cuda.Stream(device=self.device)
         self._copy_out = torch.cuda.Stream(device=self.device)
 
     def run_pipelined(self, host_in: Sequence[torch.Tensor], host_out: Sequence[torch.Tensor], stream=None):
-        """Run batch k = host_in[k] (pinned [n, h, w, c] frames) through the
+        """Run batch k = host_in[k] (pinned [n, h, w, c] frames: f32, or u8 RGB
+        for a model built with input_u8) through the
         graph into host_out[k], end to end.  ai-gpu-runtime uploads, runs and
         reads back one frame per call (upload_input, infer and read_output,
         crates/ai-gpu-runtime/src/model.rs:387-470); here the upload of batch k+1 and the read-back of batch

@@ -210,6 +210,18 @@ AIE_API int aie_conv_run(const aie_plan *plan, const void *in, const void *dev_w
 AIE_API int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *dw_w,
                        const void *dw_b, const void *pw_w, const void *pw_b, void *out, void *stream);
 
+/* Input staging: a batch of interleaved u8 RGB (cin = 3) or RGBA (cin = 4,
+ * alpha dropped) frames [n, h, w, cin] -> the network's f32 input
+ * [n, h, w, 3] (layout NHWC) or [n, h, w, 4] (NHWC_C4, 4th lane 0), each
+ * value u8 / 255 (IEEE division).  Replaces the reference's frame
+ * normalisation -- on the GPU, ai-tasks' preprocess pass
+ * (crates/ai-tasks/src/features/vb/shaders/preprocess.wgsl:11-16, unorm
+ * texture sample -> [0, 1]); on the CPU, `v as f32 / 255.0`
+ * (crates/ai-tasks/src/detect/roi.rs:166) -- at the model's resolution.
+ * Lets a caller upload 3 bytes per pixel instead of 12. */
+AIE_API int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, const void *in, int32_t layout,
+                 void *out, void *stream);
+
 /* Bilinear resize of a dense NHWC batch [n, ih, iw, c] to [n, oh, ow, c]
  * (crates/ai-core/src/reference/resize.rs:5-42; mode 0 = half_pixel,
  * 1 = asymmetric), then out = act(resized + add) when add is non-NULL

@@ -171,3 +171,12 @@ def test_fused_head_rejects_plans_that_do_not_qualify(lib):
     assert lib.aie_conv_run_dw_pw(None, pw, p, p, p, p, p, p, None) == -2
     for h in (dw, pw, conv, strict_dw, big_pw, other_shape):
         lib.aie_plan_free(h)
+
+
+def test_input_u8_argument_checks(lib):
+    p = C.c_void_p(16)
+    assert lib.aie_input_u8(1, 2, 2, 2, p, 0, p, None) == -2    # not RGB/RGBA
+    assert lib.aie_input_u8(1, 2, 2, 3, p, 7, p, None) == -2    # bad layout
+    assert lib.aie_input_u8(0, 2, 2, 3, p, 0, p, None) == -2    # empty batch
+    assert lib.aie_input_u8(1, 2, 2, 3, None, 0, p, None) == -2
+    assert lib.aie_input_u8(1, 2, 2, 3, p, 1, C.c_void_p(20), None) == -5  # C4 output must be 16-byte aligned

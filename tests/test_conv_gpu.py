@@ -326,3 +326,43 @@ def test_model_head_fusion(cuda_ok):
     assert any(r.kind == "dwpw" for r in a.ops) and not any(r.kind == "dwpw" for r in b.ops)
     d = (a.infer(x) - b.infer(x)).abs().max().item()
     assert d <= 1e-5, d
+
+
+@pytest.mark.parametrize("cin,layout,n,h,w", [(3, "nhwc", 2, 17, 23), (4, "nhwc", 3, 8, 8), (3, "nhwc_c4", 1, 5, 7),
+                                              (4, "nhwc_c4", 2, 160, 288), (3, "nhwc", 4, 160, 288)])
+def test_input_u8_staging_bit_exact(cuda_ok, cin, layout, n, h, w):
+    """u8 RGB/RGBA frames -> f32 network input equals u8 / 255 in IEEE f32
+    (ragged pixel counts, alpha dropped, C4 padding lane zero)."""
+    from ai_engine_b200.conv import input_u8
+    rng = np.random.default_rng(cin * 100 + h)
+    fr = rng.integers(0, 256, (n, h, w, cin), dtype=np.uint8)
+    got = input_u8(torch.from_numpy(fr).cuda(), layout=layout).cpu().numpy()
+    want = fr[..., :3].astype(np.float32) / np.float32(255.0)
+    assert np.array_equal(got[..., :3], want)
+    if layout == "nhwc_c4":
+        assert got.shape[-1] == 4 and not got[..., 3].any()
+
+
+def test_model_u8_input_equals_normalised_f32(cuda_ok):
+    """A model fed u8 frames (normalised by its first op) equals the same
+    model fed the f32 frames u8 / 255, also through the pipelined path."""
+    from ai_engine_b200 import segnet
+    from ai_engine_b200.graph import Model
+    g = segnet.build_graph()
+    wts = segnet.init_weights(g)
+    rng = np.random.default_rng(9)
+    fr = [rng.integers(0, 256, (2, segnet.H, segnet.W, 3), dtype=np.uint8) for _ in range(3)]
+    a = Model(g, wts, 2, (segnet.H, segnet.W, 3), input_u8=True)
+    b = Model(g, wts, 2, (segnet.H, segnet.W, 3))
+    for f in fr:
+        ya = a.infer(torch.from_numpy(f).cuda()).clone()
+        yb = b.infer(torch.from_numpy(f.astype(np.float32) / np.float32(255.0)).cuda()).clone()
+        assert torch.equal(ya, yb)
+    hin = [torch.from_numpy(f).pin_memory() for f in fr]
+    outs = [torch.empty(ya.shape, dtype=torch.float32).pin_memory() for _ in fr]
+    a.run_pipelined(hin, outs)
+    torch.cuda.synchronize()
+    for f, o in zip(fr, outs):
+        yb = b.infer(torch.from_numpy(f.astype(np.float32) / np.float32(255.0)).cuda()).cpu()
+        assert torch.equal(o, yb)
+    a.release()
