@@ -457,6 +457,9 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
             tg.tiles_x = (int)((p->ow + TW - 1) / TW);
             tg.tiles_y = (int)((p->oh + 7) / 8);
             tg.slices = (int)((d.cout + 31) / 32);
+            tg.div_slices = make_fastdiv(tg.slices);
+            tg.div_tx = make_fastdiv(tg.tiles_x);
+            tg.div_ty = make_fastdiv(tg.tiles_y);
             const long long blocks = (long long)d.n * tg.tiles_y * tg.tiles_x * tg.slices;
             if (blocks >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "depthwise grid too large; split the batch");
 #define AIE_DWT(S_, K_, ST_, TW_)                                                                             \
@@ -615,6 +618,9 @@ extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const 
     tg.tiles_x = (int)((dw->ow + TW - 1) / TW);
     tg.tiles_y = (int)((dw->oh + 7) / 8);
     tg.slices = 1;
+    tg.div_slices = make_fastdiv(1);
+    tg.div_tx = make_fastdiv(tg.tiles_x);
+    tg.div_ty = make_fastdiv(tg.tiles_y);
     const long long blocks = (long long)d.n * tg.tiles_y * tg.tiles_x;
     if (blocks >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "fused head grid too large; split the batch");
     cudaStream_t s = (cudaStream_t)stream;

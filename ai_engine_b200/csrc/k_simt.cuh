@@ -878,6 +878,7 @@ namespace aie {
 // ---------------------------------------------------------------------------
 struct DwTile {
     int tiles_x, tiles_y, slices;
+    FastDiv div_slices, div_tx, div_ty;  // block -> (slice, tile column, tile row, frame)
 };
 
 template <int K, int S, int TW>
@@ -916,12 +917,9 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
     float4 *halo4 = reinterpret_cast<float4 *>((reinterpret_cast<uintptr_t>(dw_smem_raw) + 127) & ~uintptr_t(127));
     __shared__ uint64_t halo_bar;
     int b = blockIdx.x;
-    const int slice = b % g.slices;
-    b /= g.slices;
-    const int tx = b % g.tiles_x;
-    b /= g.tiles_x;
-    const int ty = b % g.tiles_y;
-    const int img = b / g.tiles_y;
+    const int q1 = fdiv(b, g.div_slices), slice = b - q1 * g.slices;
+    const int q2 = fdiv(q1, g.div_tx), tx = q1 - q2 * g.tiles_x;
+    const int img = fdiv(q2, g.div_ty), ty = q2 - img * g.tiles_y;
     const int c0 = slice * 32;
     const int ncg = min(8, (a.cout - c0) >> 2);
     const int iy0 = ty * TH * S - a.pt, ix0 = tx * TW * S - a.pl;
