@@ -129,7 +129,7 @@ class ConvPlan:
         info = _lib.PlanInfo()
         check(self.lib.aie_conv_plan_info(h, C.byref(info)), "aie_conv_plan_info")
         self.info = info
-        self.kernel = "stem" if info.variant in (1, 2) else KERNEL_NAME[info.kernel]
+        self.kernel = "stem" if info.variant in (1, 2) else "pw_simt" if info.variant == 3 else KERNEL_NAME[info.kernel]
         self.math = MATH_NAME[info.math]
         self.oh, self.ow = info.oh, info.ow
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -189,18 +189,28 @@ class ConvPlan:
 
 
 def run_dw_pw(dw: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, out: Optional[torch.Tensor] = None,
-              stream=None) -> torch.Tensor:
+              stream=None, up: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Depthwise conv `dw` and the 1x1 conv `pw` (cout <= 4) that consumes its
     output, in one launch (aie_conv_run_dw_pw): the depthwise result never
-    reaches memory.  Raises AieError(AIE_E_UNSUPPORTED) for shapes the fused
-    kernel does not cover."""
+    reaches memory.  With `up` (a dense [n, h/2, w/2, C] tensor) the
+    depthwise input is x + the exact-2x half_pixel resize of `up`
+    (aie_conv_run_dw_pw_up2).  Raises AieError(AIE_E_UNSUPPORTED) for shapes
+    the fused kernel does not cover."""
     if dw.w is None or pw.w is None:
         raise RuntimeError("load_weights() first")
     if out is None:
         out = torch.empty(pw.out_shape(), dtype=torch.float32, device=x.device)
-    check(dw.lib.aie_conv_run_dw_pw(dw._h, pw._h, _dptr(x), C.c_void_p(dw.w.data_ptr()), C.c_void_p(dw.b.data_ptr()),
-                                    C.c_void_p(pw.w.data_ptr()), C.c_void_p(pw.b.data_ptr()), _dptr(out),
-                                    C.c_void_p(_stream_handle(stream))), "aie_conv_run_dw_pw")
+    weights = (C.c_void_p(dw.w.data_ptr()), C.c_void_p(dw.b.data_ptr()), C.c_void_p(pw.w.data_ptr()),
+               C.c_void_p(pw.b.data_ptr()))
+    if up is None:
+        check(dw.lib.aie_conv_run_dw_pw(dw._h, pw._h, _dptr(x), *weights, _dptr(out),
+                                        C.c_void_p(_stream_handle(stream))), "aie_conv_run_dw_pw")
+    else:
+        if up.dim() != 4 or not up.is_contiguous():
+            raise ValueError("up must be a dense [n, h, w, c] tensor")
+        check(dw.lib.aie_conv_run_dw_pw_up2(dw._h, pw._h, _dptr(x), _dptr(up), up.shape[1], up.shape[2], *weights,
+                                            _dptr(out), C.c_void_p(_stream_handle(stream))),
+              "aie_conv_run_dw_pw_up2")
     return out
 
 

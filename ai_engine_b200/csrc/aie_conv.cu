@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -21,6 +22,7 @@
 #include "k_simt.cuh"
 #include "k_tc.cuh"
 #include "k_stem_tc.cuh"
+#include "k_pw_simt.cuh"
 
 using namespace aie;
 
@@ -70,9 +72,11 @@ struct aie_plan {
     bool stem_tc;      // ... on the tensor cores (TF32, cin <= 3, cout = 32)
     StemGeom sg;
     uint32_t stem_smem;
+    bool pws;          // 1x1 on the FP32 pipes for cin, cout in {32, 64}, see pw_simt_kernel
 };
 
 static const int kMathStrict = AIE_MATH_FP32_STRICT;
+
 
 static inline uint32_t rup(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
 
@@ -137,6 +141,66 @@ static bool dw_tile_tmap(const ConvArgs &a, int hw, int hh, CUtensorMap *tm)
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)base, dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// pw_simt_kernel<CIN, COUT, RES>: a 2-D tensor map (cin, M) over the input
+// view with [TP pixels][32 channels] boxes and 128-byte swizzle; false when
+// the operands are not TMA- and float4-compatible (the FFMA implicit GEMM
+// runs the conv instead).
+template <int CIN, int COUT, int RES>
+static bool pws_launch_t(const ConvArgs &a, cudaStream_t s)
+{
+    using S = PwsShape<CIN, COUT>;
+    PFN_encodeTiled enc = tc_encoder();
+    const uintptr_t base = (uintptr_t)(a.x + a.x_coff);
+    if (!enc || base % 16 || (a.x_stride * 4) % 16) return false;
+    CUtensorMap tm;
+    memset(&tm, 0, sizeof tm);
+    const cuuint64_t dims[2] = {(cuuint64_t)CIN, (cuuint64_t)a.M};
+    const cuuint64_t strides[1] = {(cuuint64_t)a.x_stride * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)S::TP};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return false;
+    if (ensure_smem_attr((const void *)pw_simt_kernel<CIN, COUT, RES>, (int)S::SMEM) != cudaSuccess) return false;
+    PwsGeom g;
+    g.tiles = (int)((a.M + S::TP - 1) / S::TP);
+    const unsigned grid = (unsigned)std::min<long long>(g.tiles, 2ll * tc_sm_count());
+    pw_simt_kernel<CIN, COUT, RES><<<grid, kPwsThreads, S::SMEM, s>>>(tm, a, g);
+    return true;
+}
+
+static bool pws_launch(const aie_plan *p, const ConvArgs &a, cudaStream_t s)
+{
+    if (!a.vec_y || a.y_stride % 4 || a.y_coff % 4 || (a.res && (a.r_stride % 4 || a.r_coff % 4))) return false;
+    const int res = !a.res ? 0 : !a.res_mode ? 1 : 2;
+    const int cin = (int)p->d.cin, cout = (int)p->d.cout;
+#define AIE_PWS(CI, CO)                                                      \
+    if (cin == CI && cout == CO)                                             \
+        return res == 0 ? pws_launch_t<CI, CO, 0>(a, s) : res == 1 ? pws_launch_t<CI, CO, 1>(a, s) \
+                                                              : pws_launch_t<CI, CO, 2>(a, s);
+    AIE_PWS(32, 32) AIE_PWS(32, 64) AIE_PWS(64, 32) AIE_PWS(64, 64)
+#undef AIE_PWS
+    return false;
+}
+
+// 4-D tensor map (c, w, h, n) of a dense source tensor for the up-sampled
+// depthwise input, box (32 channels, hwq, hhq, 1)
+static bool dw_up2_tmap(const void *q, uint32_t n, uint32_t h, uint32_t w, uint32_t c, int hwq, int hhq,
+                        CUtensorMap *tm)
+{
+    memset(tm, 0, sizeof *tm);
+    PFN_encodeTiled enc = tc_encoder();
+    if (!enc || (uintptr_t)q % 16 || (c * 4) % 16) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
+    const cuuint64_t strides[3] = {(cuuint64_t)c * 4, (cuuint64_t)c * 4 * w, (cuuint64_t)c * 4 * w * h};
+    const cuuint32_t box[4] = {32, (cuuint32_t)hwq, (cuuint32_t)hhq, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -217,6 +281,14 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     // tensor-core variant, an im2col GEMM of K = 32
     const bool stem_tc_shape = stem_shape && d.cin <= 3 && d.cout == (uint32_t)kStemCout && !d.has_res;
 
+    // 1x1 shapes of the FP32-pipe pointwise kernel (pw_simt_kernel):
+    // residual tensor or exact-2x half_pixel sample, 32-bit pixel indices
+    const bool up2_res = d.has_res && d.res_mode == AIE_RES_BILINEAR_HALF_PIXEL &&
+                         p->oh == 2 * (uint64_t)d.res_h && p->ow == 2 * (uint64_t)d.res_w;
+    const bool pws_shape = p->kernel == AIE_KERNEL_PW && (d.cin == 32 || d.cin == 64) &&
+                           (d.cout == 32 || d.cout == 64) && (d.res_mode == AIE_RES_TENSOR || up2_res) &&
+                           p->M < (1ll << 31);
+
     // Math.
     const char *why = "";
     if (stem_tc_shape && (d.math == AIE_MATH_AUTO || d.math == AIE_MATH_TF32)) {
@@ -230,6 +302,13 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
         }
     } else if (d.math == AIE_MATH_FFMA || d.math == kMathStrict) {
         p->math = d.math;
+        p->pws = pws_shape && d.math == AIE_MATH_FFMA;
+    } else if (d.math == AIE_MATH_AUTO && pws_shape && up2_res) {
+        // an FPN lateral with its upsampled coarser level as the residual:
+        // the FP32-pipe kernel reads the half-size tensor directly, where the
+        // tensor-core GEMM's epilogue would be the bottleneck
+        p->math = AIE_MATH_FFMA;
+        p->pws = true;
     } else if (tf32_eligible(*p, &why)) {
         p->math = AIE_MATH_TF32;
     } else if (d.math == AIE_MATH_TF32) {
@@ -253,8 +332,20 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         p->cin_pad = (int)rup(d.cin, 4);
         p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
+        // residual buffers: rows of a residual tensor, or per-warp patches
+        // of an exact-2x half_pixel residual on 1x1 tiles (32 consecutive
+        // output pixels within two rows: ow >= 32; whole float4 pieces)
+        const bool pw_tile = d.kh == 1 && d.kw == 1 && d.sh == 1 && d.sw == 1;
+        const bool up2 = d.res_mode == AIE_RES_BILINEAR_HALF_PIXEL && p->oh == 2 * (uint64_t)d.res_h &&
+                         p->ow == 2 * (uint64_t)d.res_w;
+        const uint32_t res_kind = !d.has_res ? kTcResNone
+                                  : d.res_mode == AIE_RES_TENSOR ? kTcResTensor
+                                  : (up2 && pw_tile && p->ow >= 32 && d.cout % 4 == 0 && p->r_stride % 4 == 0 &&
+                                     p->r_coff % 4 == 0)
+                                      ? kTcResUp2
+                                      : kTcResNone;
         int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.dil, d.pad[0], d.pad[1], p->oh, p->ow,
-                         d.split_k, d.has_res != 0, &p->tc);
+                         d.split_k, res_kind, &p->tc);
         if (rc) {
             delete p;
             return fail(AIE_E_UNSUPPORTED, "tensor-core geometry rejected (%d)", rc);
@@ -312,7 +403,7 @@ extern "C" int aie_conv_plan_info(const aie_plan *p, aie_plan_info *info)
     info->split_k = p->split;
     info->tile_m = p->tile_m;
     info->tile_n = p->tile_n;
-    info->variant = p->stem_tc ? 2u : p->stem ? 1u : 0u;
+    info->variant = p->stem_tc ? 2u : p->stem ? 1u : p->pws ? 3u : 0u;
     info->weight_bytes = p->wbytes;
     info->bias_bytes = p->bbytes;
     info->workspace_bytes = p->wsbytes;
@@ -424,6 +515,7 @@ static ConvArgs make_args(const aie_plan *p, const void *in, const void *w, cons
     a.div_oh = make_fastdiv((int)p->oh);
     a.rsy = (float)a.rh / (float)p->oh;
     a.rsx = (float)a.rw / (float)p->ow;
+    a.res_up2 = d.res_mode == AIE_RES_BILINEAR_HALF_PIXEL && p->oh == 2 * (uint64_t)a.rh && p->ow == 2 * (uint64_t)a.rw;
     a.vec_x = (d.cin % 4 == 0 || d.groups > 1) && a.x_stride % 4 == 0 && xa % 16 == 0;
     a.vec_y = a.y_stride % 4 == 0 && ya % 16 == 0 && (!a.res || (a.r_stride % 4 == 0 && ra % 16 == 0));
     return a;
@@ -465,21 +557,13 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
 #define AIE_DWT(S_, K_, ST_, TW_)                                                                             \
     do {                                                                                                      \
         using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
-        static bool attr_ = false;                                                                            \
-        if (!attr_) {                                                                                         \
-            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<S_, K_, ST_, TW_, false, true>,                      \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
-            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<S_, K_, ST_, TW_, false, false>,                     \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
-            attr_ = true;                                                                                     \
-        }                                                                                                     \
+        auto k1_ = dw_tile_kernel<S_, K_, ST_, TW_, false, true>;                                             \
+        auto k0_ = dw_tile_kernel<S_, K_, ST_, TW_, false, false>;                                            \
+        CUDA_TRY(ensure_smem_attr((const void *)k1_, G_::SMEM));                                              \
+        CUDA_TRY(ensure_smem_attr((const void *)k0_, G_::SMEM));                                              \
         CUtensorMap tm_;                                                                                      \
-        if (dw_tile_tmap(a, G_::HW, G_::HH, &tm_))                                                            \
-            dw_tile_kernel<S_, K_, ST_, TW_, false, true><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, \
-                                                                                                 PwHead{});  \
-        else                                                                                                  \
-            dw_tile_kernel<S_, K_, ST_, TW_, false, false><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, \
-                                                                                                  PwHead{}); \
+        const bool tma_ = dw_tile_tmap(a, G_::HW, G_::HH, &tm_);                                              \
+        (tma_ ? k1_ : k0_)<<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, tm_, a, tg, PwHead{}, DwUp2{0, 0}); \
     } while (0)
 #define AIE_DWT2(S_)                                                         \
     if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWT(S_, 3, 1, 16); else AIE_DWT(S_, 3, 1, 8); } \
@@ -520,12 +604,7 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         const unsigned grid = (unsigned)((p->M + 255) / 256);
 #define AIE_PWD(S_, CG_)                                                                                     \
     do {                                                                                                     \
-        static bool attr_##CG_ = false;                                                                      \
-        if (!attr_##CG_) {                                                                                   \
-            CUDA_TRY(cudaFuncSetAttribute(pw_dot_tile_kernel<S_, CG_>,                                       \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));          \
-            attr_##CG_ = true;                                                                               \
-        }                                                                                                    \
+        CUDA_TRY(ensure_smem_attr((const void *)pw_dot_tile_kernel<S_, CG_>, (int)smem));                     \
         pw_dot_tile_kernel<S_, CG_><<<grid, 256, smem, s>>>(a);                                              \
     } while (0)
         if (p->strict) {
@@ -574,6 +653,8 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         }
 #undef AIE_STEM2
 #undef AIE_STEM
+    } else if (p->pws && pws_launch(p, a, s)) {
+        // launched: the FP32-pipe 1x1 kernel
     } else {
         dim3 grid((unsigned)((p->M + kFfmaBM - 1) / kFfmaBM), (p->d.cout + kFfmaBN - 1) / kFfmaBN);
         if (grid.y > 65535) return fail(AIE_E_UNSUPPORTED, "cout too large");
@@ -585,8 +666,11 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
     return AIE_OK;
 }
 
-extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *dw_w,
-                                  const void *dw_b, const void *pw_w, const void *pw_b, void *out, void *stream)
+// up != NULL: the depthwise input is in + up2(up), up a dense [n][up_h][up_w][C]
+// tensor with ih = 2 up_h, iw = 2 up_w (exact-2x half_pixel resize)
+static int run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *up, uint32_t up_h,
+                     uint32_t up_w, const void *dw_w, const void *dw_b, const void *pw_w, const void *pw_b, void *out,
+                     void *stream)
 {
     if (!dw || !pw || !in || !dw_w || !dw_b || !pw_w || !pw_b || !out) return fail(AIE_E_INVALID, "null argument");
     const aie_conv_desc &d = dw->d, &q = pw->d;
@@ -624,22 +708,35 @@ extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const 
     const long long blocks = (long long)d.n * tg.tiles_y * tg.tiles_x;
     if (blocks >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "fused head grid too large; split the batch");
     cudaStream_t s = (cudaStream_t)stream;
+    CUtensorMap tmq;
+    memset(&tmq, 0, sizeof tmq);
+    if (up) {
+        if ((uintptr_t)up % 16) return fail(AIE_E_ALIGN, "up-sampled input: source must be 16-byte aligned");
+        if (!up_h || !up_w || d.ih != 2 * up_h || d.iw != 2 * up_w)
+            return fail(AIE_E_UNSUPPORTED, "up-sampled input: source %ux%u is not half of the depthwise input %ux%u",
+                        up_h, up_w, d.ih, d.iw);
+        if ((long long)d.n * up_h * up_w * d.cin >= (1ll << 31))
+            return fail(AIE_E_UNSUPPORTED, "up-sampled input larger than 2^31 elements; split the batch");
+    }
 #define AIE_DWH(K_, ST_, TW_)                                                                                 \
     do {                                                                                                      \
         using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
-        static bool attr_ = false;                                                                            \
-        if (!attr_) {                                                                                         \
-            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<false, K_, ST_, TW_, true, true>,                    \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
-            CUDA_TRY(cudaFuncSetAttribute(dw_tile_kernel<false, K_, ST_, TW_, true, false>,                   \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, G_::SMEM));            \
-            attr_ = true;                                                                                     \
-        }                                                                                                     \
         CUtensorMap tm_;                                                                                      \
-        if (dw_tile_tmap(a, G_::HW, G_::HH, &tm_))                                                            \
-            dw_tile_kernel<false, K_, ST_, TW_, true, true><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, hd); \
-        else                                                                                                  \
-            dw_tile_kernel<false, K_, ST_, TW_, true, false><<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, a, tg, hd); \
+        const bool tma_ = dw_tile_tmap(a, G_::HW, G_::HH, &tm_);                                              \
+        if (up) {                                                                                             \
+            auto ku_ = dw_tile_kernel<false, K_, ST_, TW_, true, true, true>;                                 \
+            if (!tma_ || !dw_up2_tmap(up, d.n, up_h, up_w, d.cin, G_::HWQ, G_::HHQ, &tmq))                      \
+                return fail(AIE_E_UNSUPPORTED, "up-sampled input: operands are not TMA-compatible");          \
+            CUDA_TRY(ensure_smem_attr((const void *)ku_, G_::SMEM + G_::QSMEM));                              \
+            ku_<<<(unsigned)blocks, G_::NT, G_::SMEM + G_::QSMEM, s>>>(tm_, tmq, a, tg, hd,                   \
+                                                                      DwUp2{(int)up_h, (int)up_w});           \
+        } else {                                                                                              \
+            auto k1_ = dw_tile_kernel<false, K_, ST_, TW_, true, true>;                                       \
+            auto k0_ = dw_tile_kernel<false, K_, ST_, TW_, true, false>;                                      \
+            CUDA_TRY(ensure_smem_attr((const void *)k1_, G_::SMEM));                                          \
+            CUDA_TRY(ensure_smem_attr((const void *)k0_, G_::SMEM));                                          \
+            (tma_ ? k1_ : k0_)<<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, tm_, a, tg, hd, DwUp2{0, 0});  \
+        }                                                                                                     \
     } while (0)
     if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWH(3, 1, 16); else AIE_DWH(3, 1, 8); }
     else if (d.kh == 3) AIE_DWH(3, 2, 8);
@@ -649,6 +746,20 @@ extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "fused head launch");
     return AIE_OK;
+}
+
+extern "C" int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *dw_w,
+                                  const void *dw_b, const void *pw_w, const void *pw_b, void *out, void *stream)
+{
+    return run_dw_pw(dw, pw, in, nullptr, 0, 0, dw_w, dw_b, pw_w, pw_b, out, stream);
+}
+
+extern "C" int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, const void *in, const void *up,
+                                      uint32_t up_h, uint32_t up_w, const void *dw_w, const void *dw_b,
+                                      const void *pw_w, const void *pw_b, void *out, void *stream)
+{
+    if (!up) return fail(AIE_E_INVALID, "null up-sampled source");
+    return run_dw_pw(dw, pw, in, up, up_h, up_w, dw_w, dw_b, pw_w, pw_b, out, stream);
 }
 
 extern "C" int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, const void *in, int32_t layout,

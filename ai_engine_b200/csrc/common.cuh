@@ -2,6 +2,9 @@
 #pragma once
 
 #include <cuda.h>
+#include <mutex>
+#include <utility>
+#include <vector>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -298,5 +301,26 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *tm, ui
 __device__ uint32_t g_aie_error = 0;
 
 __device__ __forceinline__ void report_error(uint32_t code) { atomicCAS(&g_aie_error, 0u, code); }
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize, and the shared-memory
+// carveout when asked) once per kernel and device: the attributes belong to
+// the function in each device's context
+static inline cudaError_t ensure_smem_attr(const void *func, int bytes, bool max_carveout = false)
+{
+    static std::mutex mu;
+    static std::vector<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    for (const auto &f : done)
+        if (f.first == func && f.second == dev) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && max_carveout)
+        e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+    if (e == cudaSuccess) done.emplace_back(func, dev);
+    return e;
+}
 
 }  // namespace aie

@@ -34,32 +34,74 @@ struct ConvArgs {
     int rh, rw;
     float rsy, rsx;  // rh / oh, rw / ow (f32 division, as the reference)
     FastDiv div_ow, div_oh;  // output pixel -> (frame, row, column)
+    int res_up2;     // half_pixel sample with oh == 2 rh and ow == 2 rw
 };
 
 // Residual of output pixel m, channels [col, col+4), sampled bilinearly
 // from the rh x rw residual tensor.  Same arithmetic, rounded step by step,
 // as resize_bilinear_kernel / reference/resize.rs:5-42, so the fused
 // Resize -> Conv(res) equals the unfused pair bit for bit.
-__device__ __forceinline__ float4 bilinear_res4(const ConvArgs &c, long long m, int col, bool vec)
+struct BiTap {
+    const float *p00, *p01, *p10, *p11;  // the four source pixels, channel col
+    float tx, ty;                        // weights of the right column / lower row
+};
+
+__device__ __forceinline__ BiTap bilinear_tap(const ConvArgs &c, int mi, int col)
 {
-    const int mi = (int)m;  // pixel counts are < 2^31 (checked at plan time)
     const int t = fdiv(mi, c.div_ow);
     const int ox = mi - t * c.ow;
     const int img = fdiv(t, c.div_oh);
     const int oy = t - img * c.oh;
-    const float fy = c.res_mode == 1 ? __fsub_rn(__fmul_rn(__fadd_rn((float)oy, 0.5f), c.rsy), 0.5f)
-                                     : __fmul_rn((float)oy, c.rsy);
-    const float fx = c.res_mode == 1 ? __fsub_rn(__fmul_rn(__fadd_rn((float)ox, 0.5f), c.rsx), 0.5f)
-                                     : __fmul_rn((float)ox, c.rsx);
-    const float fly = floorf(fy), flx = floorf(fx);
-    const int y0 = min(max((int)fly, 0), c.rh - 1), y1 = min(max((int)fly + 1, 0), c.rh - 1);
-    const int x0 = min(max((int)flx, 0), c.rw - 1), x1 = min(max((int)flx + 1, 0), c.rw - 1);
-    const float ty = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
-    const float tx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
-    const float ty1 = __fsub_rn(1.0f, ty), tx1 = __fsub_rn(1.0f, tx);
+    int y0, y1, x0, x1;
+    float ty, tx;
+    if (c.res_up2) {
+        // exact 2x: (oy + 0.5) * 0.5 - 0.5 = oy / 2 - 1/4 exactly, so its
+        // floor is (oy - 1) >> 1 and its fraction 0.75 (oy even) or 0.25
+        // (odd); the same rows and weights as the float path below
+        const int fy = (oy - 1) >> 1, fx = (ox - 1) >> 1;
+        y0 = max(fy, 0); y1 = min(fy + 1, c.rh - 1);
+        x0 = max(fx, 0); x1 = min(fx + 1, c.rw - 1);
+        ty = (oy & 1) ? 0.25f : 0.75f;
+        tx = (ox & 1) ? 0.25f : 0.75f;
+    } else {
+        const float fy = c.res_mode == 1 ? __fsub_rn(__fmul_rn(__fadd_rn((float)oy, 0.5f), c.rsy), 0.5f)
+                                         : __fmul_rn((float)oy, c.rsy);
+        const float fx = c.res_mode == 1 ? __fsub_rn(__fmul_rn(__fadd_rn((float)ox, 0.5f), c.rsx), 0.5f)
+                                         : __fmul_rn((float)ox, c.rsx);
+        const float fly = floorf(fy), flx = floorf(fx);
+        y0 = min(max((int)fly, 0), c.rh - 1); y1 = min(max((int)fly + 1, 0), c.rh - 1);
+        x0 = min(max((int)flx, 0), c.rw - 1); x1 = min(max((int)flx + 1, 0), c.rw - 1);
+        ty = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
+        tx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
+    }
     const float *rb = c.res + (long long)img * c.rh * c.rw * c.r_stride + c.r_coff + col;
-    const float *p00 = rb + ((long long)y0 * c.rw + x0) * c.r_stride, *p01 = rb + ((long long)y0 * c.rw + x1) * c.r_stride;
-    const float *p10 = rb + ((long long)y1 * c.rw + x0) * c.r_stride, *p11 = rb + ((long long)y1 * c.rw + x1) * c.r_stride;
+    BiTap b;
+    b.p00 = rb + ((long long)y0 * c.rw + x0) * c.r_stride; b.p01 = rb + ((long long)y0 * c.rw + x1) * c.r_stride;
+    b.p10 = rb + ((long long)y1 * c.rw + x0) * c.r_stride; b.p11 = rb + ((long long)y1 * c.rw + x1) * c.r_stride;
+    b.tx = tx; b.ty = ty;
+    return b;
+}
+
+// top = g00 (1-tx) + g01 tx, bot likewise, top (1-ty) + bot ty: each product
+// and sum rounded on its own, the reference's order
+__device__ __forceinline__ float4 bilinear_mix4(float4 g00, float4 g01, float4 g10, float4 g11, float tx, float ty)
+{
+    const float ty1 = __fsub_rn(1.0f, ty), tx1 = __fsub_rn(1.0f, tx);
+    auto mix = [&](float a, float b, float c, float d) {
+        const float top = __fadd_rn(__fmul_rn(a, tx1), __fmul_rn(b, tx));
+        const float bot = __fadd_rn(__fmul_rn(c, tx1), __fmul_rn(d, tx));
+        return __fadd_rn(__fmul_rn(top, ty1), __fmul_rn(bot, ty));
+    };
+    return make_float4(mix(g00.x, g01.x, g10.x, g11.x), mix(g00.y, g01.y, g10.y, g11.y),
+                       mix(g00.z, g01.z, g10.z, g11.z), mix(g00.w, g01.w, g10.w, g11.w));
+}
+
+__device__ __forceinline__ float4 bilinear_res4(const ConvArgs &c, long long m, int col, bool vec)
+{
+    const BiTap b = bilinear_tap(c, (int)m, col);  // pixel counts are < 2^31 (checked at plan time)
+    const float *p00 = b.p00, *p01 = b.p01, *p10 = b.p10, *p11 = b.p11;
+    const float tx = b.tx, ty = b.ty;
+    const float ty1 = __fsub_rn(1.0f, ty), tx1 = __fsub_rn(1.0f, tx);
     float g00[4], g01[4], g10[4], g11[4];
     if (vec) {
         const float4 a0 = __ldg(reinterpret_cast<const float4 *>(p00)), a1 = __ldg(reinterpret_cast<const float4 *>(p01));
@@ -886,6 +928,20 @@ struct DwTileGeom {
     static constexpr int TH = 8, PB = 4, RUNS = TW / PB, NT = TH * RUNS * 8;
     static constexpr int HH = (TH - 1) * S + K, HW = (TW - 1) * S + K;
     static constexpr int SMEM = HH * HW * 8 * 16 + 128;  // + slack for 128-byte alignment
+    // exact-2x residual source patch (up-sampled-input mode): the source rows
+    // and columns that the halo's pixels sample
+    static constexpr int HHQ = (HH + 4) / 2, HWQ = (HW + 4) / 2;
+    static constexpr int QSMEM = HHQ * HWQ * 8 * 16;
+};
+
+// Up-sampled input (UP2 = true): the depthwise input is x + up2(q), with q a
+// dense [n][rh][rw][C] tensor and up2 the exact-2x half_pixel bilinear resize
+// (reference/resize.rs:5-42): the FPN's Resize -> Conv(res) -> depthwise
+// chain, where x is the lateral conv's output without its residual.  The sum
+// is formed in the staged halo, so neither the up-sampled tensor nor the sum
+// is written to memory.
+struct DwUp2 {
+    int rh, rw;
 };
 
 // Head mode (HEAD = true): the depthwise output feeds a 1x1 conv with at most
@@ -906,10 +962,12 @@ struct PwHead {
 // (cin, iw, ih, n) tensor map, issued by one thread -- out-of-range pixels and
 // channels read as zeros -- instead of one 16-byte cp.async per chunk with its
 // index arithmetic (the staging was a sixth of the kernel's instructions).
-template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false>
+template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false, bool UP2 = false>
 __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
-    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const ConvArgs a, const DwTile g, const PwHead hd)
+    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq, const ConvArgs a,
+                   const DwTile g, const PwHead hd, const DwUp2 up)
 {
+    static_assert(!UP2 || kTma, "the up-sampled input is staged by TMA");
     using G = DwTileGeom<K, S, TW>;
     constexpr int TH = G::TH, PB = G::PB, RUNS = G::RUNS, NT = G::NT, HH = G::HH, HW = G::HW;
     extern __shared__ __align__(128) uint8_t dw_smem_raw[];
@@ -929,15 +987,64 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
         __syncthreads();
+        // UP2: source patch rows / columns from floor((first halo row - 1) / 2)
+        constexpr int HWQ = G::HWQ;
+        float4 *qp = halo4 + HH * HW * 8;  // [G::HHQ][HWQ][8 channel groups]
+        const int qy0 = (iy0 - 1) >> 1, qx0 = (ix0 - 1) >> 1;
         if (threadIdx.x == 0) {
-            mbar_expect_tx(&halo_bar, (uint32_t)(HH * HW * 128));
+            mbar_expect_tx(&halo_bar, (uint32_t)(HH * HW * 128 + (UP2 ? G::QSMEM : 0)));
             tma_load_4d(halo4, &tmx, &halo_bar, c0, ix0, iy0, img);
+            if constexpr (UP2) tma_load_4d(qp, &tmq, &halo_bar, c0, qx0, qy0, img);
         }
         // bounded wait; the outcome is made CTA-uniform (head mode shuffles)
         const bool landed = mbar_wait(&halo_bar, 0);
         if (!__syncthreads_and(landed)) {
             if (threadIdx.x == 0) report_error(0x04000001u);
             return;
+        }
+        if constexpr (UP2) {
+            // halo += up2(q) at every in-range pixel (padding stays zero):
+            // thread (column hx, channel group) walks down its column keeping
+            // the horizontally interpolated source rows it needs (top / bot
+            // of the resize, rounded step by step as the resize kernels do)
+            // in a two-row window; each source row is interpolated once.
+            for (int t = threadIdx.x; t < HW * 8; t += NT) {  // stride-2 halos are wider than the CTA
+                const int hx = t >> 3, cg = t & 7;
+                const int ix = ix0 + hx;
+                if (ix >= 0 && ix < a.iw) {
+                    const int fx = (ix - 1) >> 1;
+                    const int x0 = max(fx, 0) - qx0, x1 = min(fx + 1, up.rw - 1) - qx0;
+                    const float tx = (ix & 1) ? 0.25f : 0.75f, tx1 = __fsub_rn(1.0f, tx);
+                    auto lerp_x = [&](int r) {
+                        const float4 g0 = qp[(r * HWQ + x0) * 8 + cg], g1 = qp[(r * HWQ + x1) * 8 + cg];
+                        return make_float4(__fadd_rn(__fmul_rn(g0.x, tx1), __fmul_rn(g1.x, tx)),
+                                           __fadd_rn(__fmul_rn(g0.y, tx1), __fmul_rn(g1.y, tx)),
+                                           __fadd_rn(__fmul_rn(g0.z, tx1), __fmul_rn(g1.z, tx)),
+                                           __fadd_rn(__fmul_rn(g0.w, tx1), __fmul_rn(g1.w, tx)));
+                    };
+                    int ia = -1, ib = -1;
+                    float4 ta = make_float4(0.f, 0.f, 0.f, 0.f), tb = ta;
+#pragma unroll
+                    for (int hy = 0; hy < HH; hy++) {
+                        const int iy = iy0 + hy;
+                        if (iy < 0 || iy >= a.ih) continue;
+                        const int fy = (iy - 1) >> 1;
+                        const int y0 = max(fy, 0) - qy0, y1 = min(fy + 1, up.rh - 1) - qy0;
+                        if (y0 == ib) { ta = tb; ia = ib; }
+                        if (y0 != ia) { ta = lerp_x(y0); ia = y0; }
+                        if (y1 != ib) { tb = y1 == ia ? ta : lerp_x(y1); ib = y1; }
+                        const float ty = (iy & 1) ? 0.25f : 0.75f, ty1 = __fsub_rn(1.0f, ty);
+                        float4 &h = halo4[(hy * HW + hx) * 8 + cg];
+                        float4 v = h;
+                        v.x = __fadd_rn(v.x, __fadd_rn(__fmul_rn(ta.x, ty1), __fmul_rn(tb.x, ty)));
+                        v.y = __fadd_rn(v.y, __fadd_rn(__fmul_rn(ta.y, ty1), __fmul_rn(tb.y, ty)));
+                        v.z = __fadd_rn(v.z, __fadd_rn(__fmul_rn(ta.z, ty1), __fmul_rn(tb.z, ty)));
+                        v.w = __fadd_rn(v.w, __fadd_rn(__fmul_rn(ta.w, ty1), __fmul_rn(tb.w, ty)));
+                        h = v;
+                    }
+                }
+            }
+            __syncthreads();
         }
     } else {
         const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;

@@ -289,17 +289,8 @@ static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s)
 {
     using L = StemTcLayout<CIN, S>;
     static_assert(kStemCtasPerSm * (L::kBytes + 1024) <= 228 * 1024, "shared memory for three CTAs per SM");
-    static bool attr_set = false;
-    if (!attr_set) {
-        for (auto fn : {stem_tc_kernel<CIN, S, true>, stem_tc_kernel<CIN, S, false>}) {
-            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes);
-            if (e != cudaSuccess) return -1;
-            e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     (int)cudaSharedmemCarveoutMaxShared);
-            if (e != cudaSuccess) return -1;
-        }
-        attr_set = true;
-    }
+    for (auto fn : {stem_tc_kernel<CIN, S, true>, stem_tc_kernel<CIN, S, false>})
+        if (ensure_smem_attr((const void *)fn, (int)L::kBytes, true) != cudaSuccess) return -1;
     const long long ntiles = (long long)a.n * g.tiles_x * g.tiles_y;
     const unsigned grid = (unsigned)std::min<long long>(ntiles, (long long)kStemCtasPerSm * tc_sm_count());
     // TMA halo when the input is a dense, 16-byte aligned [n][ih][iw][cin] tensor

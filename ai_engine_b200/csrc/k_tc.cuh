@@ -41,6 +41,7 @@
 // CTA records an error code in g_aie_error, stops issuing work, waits
 // (bounded) for its own copies in flight, frees its TMEM and exits.
 #pragma once
+#include <atomic>
 
 #include <cuda.h>
 
@@ -61,6 +62,15 @@ constexpr int kTcBM = 128;
 constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 4;  // 16 KB
 constexpr uint32_t kTcBResidentMax = 112 * 1024;   // largest B kept in shared memory for a whole kernel
+constexpr int kTcPatchCols = 18;                   // source columns per segment of an exact-2x residual patch
+constexpr uint32_t kTcPatchBytes = 2 * 2 * kTcPatchCols * 128;  // [segment][source row][column] x 32 channels
+
+// Residual buffer kinds of a tensor-core plan (tc_plan's res_kind)
+enum TcResKind : uint32_t {
+    kTcResNone = 0,    // no residual, or one read directly by the epilogue
+    kTcResTensor = 1,  // residual tensor of the output's shape, cp.async rows
+    kTcResUp2 = 2,     // exact-2x half_pixel bilinear residual, cp.async patches
+};
 
 struct TcGeom {
     uint32_t bm, bn;
@@ -79,6 +89,7 @@ struct TcGeom {
     uint32_t b_resident;       // 1: the CTA's whole B (all taps and K blocks) is loaded once
     uint32_t bres_off;         // shared-memory offset of the resident B
     uint32_t res_off;          // per-warp residual prefetch buffers (0 = none)
+    uint32_t res_patch;        // the buffers hold exact-2x residual patches (kTcResUp2)
     uint32_t out_off, shared_off;
 };
 
@@ -87,6 +98,7 @@ struct TcArgs {
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
     uint32_t b_resident, bres_off, res_off, pipes, halo, a_bytes;
+    uint32_t res_patch;               // RES 3 epilogue: residual from per-warp exact-2x patches
     uint64_t units;                   // < 2^31 (checked at launch)
     FastDiv div_ntiles, div_split;    // unit -> (m tile, n tile, split)
     FastDiv div_perimg, div_tilesx;   // m tile -> (frame, tile row, tile column)
@@ -95,6 +107,41 @@ struct TcArgs {
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
     uint32_t out_off, shared_off;  // shared-memory carve-up (bytes)
 };
+
+// Exact-2x residual patch of one epilogue warp.  On 1x1 tiles a warp's 32
+// rows are the consecutive output pixels m0..m0+31; with ow >= 32 they lie
+// in at most two output rows: segment 0 (the row of m0, from column ox0)
+// and segment 1 (the next row, from column 0).  Output column ox reads
+// source columns clamp((ox - 1) >> 1) and the one after, so a segment's 32
+// columns need at most 18 source columns, from qc0 (segment 0) or 0
+// (segment 1), on two source rows each.
+struct Up2Patch {
+    int ox0, qc0;            // first output / source column of segment 0
+    int img0, y00, y01;      // segment 0: frame and source rows
+    int img1, y10, y11;      // segment 1 (frame clamped to the batch when past it)
+    int odd0, odd1;          // output row parity: lower-row weight 0.25 if odd, else 0.75
+};
+
+__device__ __forceinline__ Up2Patch up2_patch(const ConvArgs &c, int m0)
+{
+    Up2Patch p;
+    const int t = fdiv(m0, c.div_ow);
+    p.ox0 = m0 - t * c.ow;
+    p.img0 = fdiv(t, c.div_oh);
+    const int oy0 = t - p.img0 * c.oh;
+    int oy1 = oy0 + 1;
+    p.img1 = p.img0;
+    if (oy1 == c.oh) {
+        oy1 = 0;
+        p.img1 = min(p.img0 + 1, c.n - 1);
+    }
+    p.qc0 = max((p.ox0 - 1) >> 1, 0);
+    const int f0 = (oy0 - 1) >> 1, f1 = (oy1 - 1) >> 1;
+    p.y00 = max(f0, 0); p.y01 = min(f0 + 1, c.rh - 1);
+    p.y10 = max(f1, 0); p.y11 = min(f1 + 1, c.rh - 1);
+    p.odd0 = oy0 & 1; p.odd1 = oy1 & 1;
+    return p;
+}
 
 // --------------------------------------------------------------- PTX ---
 
@@ -276,6 +323,10 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
     return ((long long)o.img * a.c.oh + oy) * a.c.ow + ox;
 }
 
+// RES (the epilogue's residual source, one kernel per kind so that each
+// layer's epilogue carries only its own code): 0 none, 1 residual tensor,
+// 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches
+template <int RES>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
 {
@@ -508,8 +559,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // written back by the warp 8 lanes per 128-byte row segment so every
         // store (and residual load) instruction covers 4 whole rows instead
         // of 32 scattered 16-byte pieces; residual added after the activation
-        // RES: 0 none, 1 residual tensor, 2 bilinear-sampled residual; a
-        // template argument so each layer's epilogue carries only its code
+        // RES (the kernel's template argument) picks the residual source
         // residual tensor (RES 1, 16-byte aligned rows): the 8 x 16 bytes this
         // lane adds for the chunk at col0 are fetched with cp.async into this
         // warp's residual buffer ahead of use, so their latency overlaps the
@@ -533,8 +583,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             asm volatile("cp.async.commit_group;" ::: "memory");
         };
 
-        auto emit = [&](auto res_kind, int col0, float (&v)[32]) {
-            constexpr int RES = decltype(res_kind)::value;
+        // exact-2x residual (RES 3): the source pixels of this warp's 32 rows
+        // for the chunk at col0, [segment][row][column] x 128 bytes, fetched
+        // with cp.async ahead of use like the residual rows above (columns
+        // past the source's edge repeat its last column; channels past cout
+        // are zero-filled)
+        int wm0 = -1;  // first output pixel of this warp's rows (1x1 tiles), -1 past M
+        auto prefetch_patch = [&](int col0) {
+            if (wm0 < 0) return;
+            const Up2Patch p = up2_patch(c, wm0);
+            uint8_t *pb = smem + a.res_off + ew * kTcPatchBytes;
+            const float *rb = c.res + c.r_coff + col0;
+#pragma unroll 6
+            for (int j = 0; j < (int)(kTcPatchBytes / 16 / 32); j++) {
+                const int idx = j * 32 + lane;
+                const int slot = idx >> 3, piece = idx & 7;
+                const int sg = slot >= 2 * kTcPatchCols ? 1 : 0;
+                const int rem = slot - 2 * kTcPatchCols * sg;
+                const int ry = rem >= kTcPatchCols ? 1 : 0;
+                const int cx = rem - kTcPatchCols * ry;
+                const int img = sg ? p.img1 : p.img0;
+                const int y = sg ? (ry ? p.y11 : p.y10) : (ry ? p.y01 : p.y00);
+                const int x = min((sg ? 0 : p.qc0) + cx, c.rw - 1);
+                const bool ok = col0 + piece * 4 < c.cout;
+                const float *src = ok ? rb + (((long long)img * c.rh + y) * c.rw + x) * c.r_stride + piece * 4 : c.res;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(pb + slot * 128 + piece * 16)),
+                             "l"(src), "r"(ok ? 16 : 0)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        auto prefetch_any = [&](int col0) {
+            if constexpr (RES == 3) prefetch_patch(col0);
+            else if constexpr (RES == 1) prefetch_res(col0);
+        };
+        // row r of this warp (pixel wm0 + r), channels seg*4.. of the chunk
+        auto patch_res4 = [&](const Up2Patch &p, int r) {
+            const int oxr = p.ox0 + r;
+            const int sg = oxr >= c.ow ? 1 : 0;
+            const int ox = sg ? oxr - c.ow : oxr;
+            const int fx = (ox - 1) >> 1, qc = sg ? 0 : p.qc0;
+            const int x0 = max(fx, 0) - qc, x1 = min(fx + 1, c.rw - 1) - qc;
+            const uint8_t *sb = smem + a.res_off + ew * kTcPatchBytes + sg * (2 * kTcPatchCols * 128) + seg * 16;
+            const float4 g00 = *reinterpret_cast<const float4 *>(sb + x0 * 128);
+            const float4 g01 = *reinterpret_cast<const float4 *>(sb + x1 * 128);
+            const float4 g10 = *reinterpret_cast<const float4 *>(sb + (kTcPatchCols + x0) * 128);
+            const float4 g11 = *reinterpret_cast<const float4 *>(sb + (kTcPatchCols + x1) * 128);
+            return bilinear_mix4(g00, g01, g10, g11, (ox & 1) ? 0.25f : 0.75f, (sg ? p.odd1 : p.odd0) ? 0.25f : 0.75f);
+        };
+
+        auto emit = [&](int col0, float (&v)[32]) {
             const int col = col0 + seg * 4;
             const bool vec = c.vec_y && col + 4 <= c.cout;
             {
@@ -556,6 +654,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if constexpr (RES == 1) {
                 if (a.res_off) asm volatile("cp.async.wait_all;" ::: "memory");  // this lane's prefetched rows
             }
+            Up2Patch pt{};
+            if constexpr (RES == 3) {
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                __syncwarp();  // the patch was fetched by the whole warp
+                pt = up2_patch(c, max(wm0, 0));
+            }
             if (col >= c.y_pad_to) return;
             // four rows at a time: their residual loads are issued together
 #pragma unroll
@@ -567,7 +671,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     rv[q] = make_float4(0.f, 0.f, 0.f, 0.f);
                     if constexpr (RES == 2) {
                         if (mrow[i] >= 0) rv[q] = bilinear_res4(c, mrow[i], col, vec);
-                    } else if constexpr (RES == 1) {
+                    } else if constexpr (RES == 3) {
+                        if (mrow[i] >= 0) rv[q] = patch_res4(pt, i * 4 + (lane >> 3));
+                    }
+                    if constexpr (RES == 1) {
                         if (mrow[i] >= 0) {
                             if (a.res_off && vec) {
                                 const int r = i * 4 + (lane >> 3);
@@ -611,12 +718,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         };
 
-        auto emit_any = [&](int col0, float (&v)[32]) {
-            if (!c.res) emit(std::integral_constant<int, 0>{}, col0, v);
-            else if (!c.res_mode) emit(std::integral_constant<int, 1>{}, col0, v);
-            else emit(std::integral_constant<int, 2>{}, col0, v);
-        };
-        const bool res_tensor = c.res && !c.res_mode;
+        auto emit_any = [&](int col0, float (&v)[32]) { emit(col0, v); };
+        // residuals fetched into the per-warp buffers ahead of use
+        constexpr bool res_tensor = RES == 1 || RES == 3;
 
         uint32_t k = 0;  // tiles this group has drained: the phase of its buffer
         for (uint64_t u = blockIdx.x + (uint64_t)grp * gridDim.x; u < a.units; u += 2ull * gridDim.x, k++) {
@@ -629,6 +733,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const TcOrigin org = a.igemm ? tc_origin(a, t.mt) : TcOrigin{0, 0, 0};
 #pragma unroll
             for (int i = 0; i < 8; i++) mrow[i] = (int)tc_row_pixel(a, t.mt, org, quad * 32 + i * 4 + (lane >> 3));
+            if constexpr (RES == 3) {
+                const long long m0 = (long long)t.mt * kTcBM + quad * 32;
+                wm0 = m0 < c.M ? (int)m0 : -1;
+            }
             if (t.nt != bias_nt) {
                 __syncwarp();
                 for (int i = lane; i < 256; i += 32) bcache[i] = (nbase + i < c.cout) ? __ldg(c.bias + nbase + i) : 0.0f;
@@ -636,7 +744,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 bias_nt = t.nt;
                 bias_base = nbase;
             }
-            if (res_tensor && a.split == 1) prefetch_res(nbase);  // first chunk, ahead of the MMA wait
+            if (res_tensor && a.split == 1) prefetch_any(nbase);  // first chunk, ahead of the MMA wait
             if (a.split == 1) {
                 // the epilogue warps sleep on the accumulator barrier so that
                 // their polling does not take issue slots from the MMA and
@@ -654,7 +762,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         emit_any(nbase + c0, v);
                         if (res_tensor && c0 + 32 < ncol) {
                             __syncwarp();  // every lane has read its rows of the buffer
-                            prefetch_res(nbase + c0 + 32);
+                            prefetch_any(nbase + c0 + 32);
                         }
                     }
                 }
@@ -701,7 +809,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     for (int c0 = 0; c0 < ncol; c0 += 32) {
                         if (res_tensor) {
                             __syncwarp();  // every lane has read its rows of the buffer
-                            prefetch_res(nbase + c0);  // lands while the partials are summed
+                            prefetch_any(nbase + c0);  // lands while the partials are summed
                         }
                         float v[32];
 #pragma unroll
@@ -755,7 +863,7 @@ static inline bool tc_igemm_supported(uint32_t kh, uint32_t kw, uint32_t sh, uin
 // Plan the tensor-core launch.  Returns 0 or a negative code.
 static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, uint32_t cout, uint32_t kh, uint32_t kw,
                           uint32_t sh, uint32_t sw, uint32_t dil, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
-                          uint32_t split_req, bool has_res, TcGeom *g, bool allow_halo = true)
+                          uint32_t split_req, uint32_t res_kind, TcGeom *g, bool allow_halo = true)
 {
     (void)ih; (void)iw; (void)pt; (void)pl;
     *g = TcGeom{};
@@ -826,7 +934,8 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     // shared memory: [stages][resident B][epilogue staging + bias caches]
     // [barriers]; stage buffers and the resident B are 1024-aligned
     // staging + per-warp bias caches (+ residual prefetch buffers)
-    const uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + 256 * 4 + (has_res ? kTcStageOut : 0u));
+    const uint32_t res_buf = res_kind == kTcResTensor ? kTcStageOut : res_kind == kTcResUp2 ? kTcPatchBytes : 0u;
+    const uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + 256 * 4 + res_buf);
     const uint32_t limit = 227 * 1024 - 1024 /*align slack*/ - 256 /*barriers*/;
     // Resident B: with one n-tile and no K split every unit of a CTA uses the
     // same B, so it is loaded once (one TMA box per tap and K block) and each
@@ -838,7 +947,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     const uint32_t fixed = out_bytes + (g->b_resident ? (uint32_t)bres : 0u);
     g->stages = std::min<uint32_t>(8, (limit - fixed) / stage);
     if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
-        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, has_res, g, false);
+        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false);
     if (g->stages < 2) return -2;
     // narrow k x k tiles (long K loops, N <= 64) are bound by the per-thread
     // MMA issue cost: two pipelines.  1x1 GEMMs keep one deep ring (their
@@ -846,7 +955,8 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->pipes = (g->igemm && g->bn <= 64 && g->stages >= 4) ? 2u : 1u;
     g->bres_off = g->stages * stage;
     g->out_off = g->bres_off + (g->b_resident ? (uint32_t)bres : 0u);
-    g->res_off = has_res ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;
+    g->res_off = res_buf ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;
+    g->res_patch = (res_kind == kTcResUp2 && !g->igemm) ? 1u : 0u;
     g->shared_off = g->out_off + out_bytes;
     g->tmem_cols = tc_pow2_ceil(2 * g->bn);
     if (g->tmem_cols > 512) return -3;
@@ -947,6 +1057,8 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
     a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
     a.halo = g.halo; a.a_bytes = g.a_bytes;
+    // patches need 16-byte residual rows (the plan checked the shapes)
+    a.res_patch = (g.res_patch && c.res && c.res_mode && c.vec_y) ? 1u : 0u;
     if (g.units >= (1ull << 31) || (uint64_t)g.m_tiles * g.n_tiles * g.split >= (1ull << 31)) {
         snprintf(err, errlen, "too many tensor-core tiles in one call (%llu); split the batch",
                  (unsigned long long)g.units);
@@ -976,13 +1088,18 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
             return -4;
         }
     }
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(tc_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        attr_set = true;
+    const int kind = !c.res ? 0 : !c.res_mode ? 1 : a.res_patch ? 3 : 2;
+    auto kern = kind == 0 ? tc_conv_kernel<0> : kind == 1 ? tc_conv_kernel<1> : kind == 2 ? tc_conv_kernel<2>
+                                                                                         : tc_conv_kernel<3>;
+    {
+        cudaError_t e = ensure_smem_attr((const void *)kern, 227 * 1024);
+        if (e != cudaSuccess) {
+            snprintf(err, errlen, "tc_conv_kernel shared-memory attribute: %s", cudaGetErrorString(e));
+            return -4;
+        }
     }
     const unsigned grid = (unsigned)std::min<uint64_t>(g.units, (uint64_t)tc_sm_count());
-    tc_conv_kernel<<<grid, kTcThreads, g.smem_bytes, stream>>>(tmA, tmB, a);
+    kern<<<grid, kTcThreads, g.smem_bytes, stream>>>(tmA, tmB, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(err, errlen, "tc_conv_kernel launch: %s", cudaGetErrorString(e));

@@ -35,6 +35,7 @@ class OpRecord:
     size: Optional[Tuple[int, int]] = None
     plan: Optional[ConvPlan] = None
     head: Optional[ConvPlan] = None   # kind "dwpw": the fused 1x1 (cout <= 4) after the depthwise plan
+    up: Optional[str] = None          # kind "dwpw": source whose exact-2x resize is added to the depthwise input
 
 
 def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
@@ -65,7 +66,7 @@ class Model:
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
                  in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
-                 input_u8: bool = False, device=None):
+                 fuse_tail: bool = True, input_u8: bool = False, device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -104,7 +105,42 @@ class Model:
                         and uses.get(prev[1], 0) == 1 and prev[1] != self.output and prev[3].cout <= 32
                         and prev[3].cout % 4 == 0):
                     head_of[prev[1]] = op
+        # the fused head's plans, made up front: a head whose plans do not
+        # qualify runs as its two convs (and keeps its producers as they are)
+        head_plans: Dict[str, Tuple[ConvPlan, ConvPlan]] = {}
+        for dw_out, hop in list(head_of.items()):
+            dop = next(p for p in self.graph if p[1] == dw_out)
+            h, w, _ = self.shapes[dop[2]]
+            dplan = ConvPlan(dop[3], n, h, w, math=math, device=self.device).load_weights(*weights[dw_out])
+            oh, ow, _ = self.shapes[dw_out]
+            hplan = ConvPlan(hop[3], n, oh, ow, math=math, device=self.device).load_weights(*weights[hop[1]])
+            if dplan.kernel == "dw" and hplan.kernel == "pw_dot" and dplan.math != "fp32_strict":
+                head_plans[dw_out] = (dplan, hplan)
+            else:
+                del head_of[dw_out]
         fused_heads = set(op[1] for op in head_of.values())
+        # Feature-pyramid tail (with the head fusion): the head's depthwise
+        # input is a conv whose residual is an exact-2x resize used nowhere
+        # else.  The conv then runs without its residual and the fused head
+        # adds the up-sampled source in its staged input tile
+        # (aie_conv_run_dw_pw_up2): neither the resize's output nor the sum
+        # is written.
+        tail_up: Dict[str, str] = {}       # lateral conv output -> resize source
+        dropped_resize: set = set()
+        for dw_out in (head_of if fuse_tail else {}):
+            dop = next(p for p in self.graph if p[1] == dw_out)
+            lat = next((p for p in self.graph if p[1] == dop[2]), None)
+            if lat is None or lat[0] != "conv" or lat[4] is None or uses.get(lat[1], 0) != 1 or lat[1] == self.output:
+                continue
+            rz = next((p for p in self.graph if p[1] == lat[4]), None)
+            if rz is None or rz[0] != "resize" or rz[4] is not None or uses.get(rz[1], 0) != 1 or rz[1] == self.output:
+                continue
+            sh_, sw_, sc_ = self.shapes[rz[2]]
+            if tuple(rz[3]) != (2 * sh_, 2 * sw_) or self.shapes[lat[1]] != (2 * sh_, 2 * sw_, sc_):
+                continue
+            tail_up[lat[1]] = rz[2]
+            dropped_resize.add(rz[1])
+            fused_resize.pop(rz[1], None)  # the head takes it instead of the conv's epilogue
         # input_u8: the batch arrives as u8 RGB frames ("input_u8", 3 bytes per
         # pixel); the first op normalises them into the f32 "input" (u8 / 255)
         self.input_u8 = input_u8
@@ -119,27 +155,20 @@ class Model:
             for op in self.graph:
                 kind, out, src = op[0], op[1], op[2]
                 h, w, c = self.shapes[src]
-                if kind == "resize" and out in fused_resize:
+                if kind == "resize" and (out in fused_resize or out in dropped_resize):
                     continue
                 if out in fused_heads:
                     continue  # recorded with its depthwise producer
                 if out in head_of:
                     hop = head_of[out]
-                    rec = OpRecord("dwpw", hop[1], src, conv=op[3])
-                    rec.plan = ConvPlan(op[3], n, h, w, math=math, device=self.device)
-                    rec.plan.load_weights(*weights[out])
-                    oh, ow, oc = self.shapes[out]
-                    rec.head = ConvPlan(hop[3], n, oh, ow, math=math, device=self.device)
-                    rec.head.load_weights(*weights[hop[1]])
-                    if rec.plan.kernel == "dw" and rec.head.kernel == "pw_dot" and rec.plan.math != "fp32_strict":
-                        self.bufs[hop[1]] = torch.empty((n, *self.shapes[hop[1]]), dtype=torch.float32,
-                                                        device=self.device)
-                        self.ops.append(rec)
-                        continue
-                    fused_heads.discard(hop[1])  # plans do not qualify: run the two convs
+                    rec = OpRecord("dwpw", hop[1], src, conv=op[3], up=tail_up.get(src))
+                    rec.plan, rec.head = head_plans[out]
+                    self.bufs[hop[1]] = torch.empty((n, *self.shapes[hop[1]]), dtype=torch.float32, device=self.device)
+                    self.ops.append(rec)
+                    continue
                 rec = OpRecord(kind, out, src)
                 if kind == "conv":
-                    rec.conv, rec.res = op[3], op[4]
+                    rec.conv, rec.res = op[3], (None if out in tail_up else op[4])
                     res_resize = None
                     if rec.res in fused_resize:
                         lo = fused_resize[rec.res]
@@ -175,7 +204,7 @@ class Model:
             if r.kind == "conv":
                 r.plan(src, self.bufs[r.res] if r.res else None, out=out, stream=stream)
             elif r.kind == "dwpw":
-                run_dw_pw(r.plan, r.head, src, out=out, stream=stream)
+                run_dw_pw(r.plan, r.head, src, out=out, stream=stream, up=self.bufs[r.up] if r.up else None)
             elif r.kind == "u8in":
                 input_u8(src, out=out, stream=stream)
             else:

@@ -225,6 +225,8 @@ def main():
     ap.add_argument("--math", default="auto", choices=["auto", "ffma", "tf32", "fp32_strict"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fuse-resize", type=int, default=None, choices=[0, 1],
+                    help="fold each resize that only feeds a conv residual into that conv (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
     args = ap.parse_args()
 
@@ -250,7 +252,8 @@ def main():
     n = args.batch
     g = segnet.build_graph()
     weights = segnet.init_weights(g)  # same weights on every rank (replicas)
-    model = Model(g, weights, n, (H, W, 3), math=args.math, device=dev)
+    fuse_kw = {} if args.fuse_resize is None else {"fuse": bool(args.fuse_resize)}
+    model = Model(g, weights, n, (H, W, 3), math=args.math, device=dev, **fuse_kw)
     x_host = torch.from_numpy(segnet.synthetic_input(n, seed=100 + rank)).pin_memory()
     model.bufs["input"].copy_(x_host)
     stream = torch.cuda.current_stream(dev)
@@ -305,7 +308,7 @@ def main():
             if r.kind == "conv":
                 r.plan(src, model.bufs[r.res] if r.res else None, out=out)
             elif r.kind == "dwpw":
-                run_dw_pw(r.plan, r.head, src, out=out)
+                run_dw_pw(r.plan, r.head, src, out=out, up=model.bufs[r.up] if r.up else None)
             else:
                 resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
             ev[i + 1].record(stream)
@@ -341,7 +344,7 @@ def main():
 
     e2e_f32_value = time_e2e(model, x_host)
     model.release()
-    model_u8 = Model(g, weights, n, (H, W, 3), math=args.math, input_u8=True, device=dev)
+    model_u8 = Model(g, weights, n, (H, W, 3), math=args.math, input_u8=True, device=dev, **fuse_kw)
     x_host_u8 = torch.from_numpy(np.rint(x_host.numpy() * 255.0).astype(np.uint8)).pin_memory()
     e2e_value = time_e2e(model_u8, x_host_u8)
     model_u8.release()
@@ -380,6 +383,8 @@ def main():
             # fused depthwise + 1x1 head: the intermediate is neither written nor read
             inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout
             fl, by = r.plan.flops + r.head.flops, r.plan.min_bytes + r.head.min_bytes - 2 * inter
+            if r.up:  # the half-size source whose resize the kernel adds to its input
+                by += 4 * n * int(np.prod(model.shapes[r.up]))
             kern, math = "dw+pw", r.plan.math
         elif r.plan is not None:
             fl, by = r.plan.flops, r.plan.min_bytes

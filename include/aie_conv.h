@@ -161,6 +161,10 @@ typedef struct aie_plan_info {
                                   output is 16-byte aligned: 1 = FFMA (cin <= 4,
                                   3x3), 2 = tensor-core im2col GEMM (TF32,
                                   cin <= 3, cout = 32, no residual);
+                                  3 = PW on the FP32 pipes with TMA-staged
+                                  tiles (FFMA, cin and cout in {32, 64}:
+                                  chosen by AUTO for an exact-2x half_pixel
+                                  residual, and by FFMA);
                                   0 = the family's main kernel */
     uint64_t weight_bytes;     /* size of dev_w for aie_conv_pack_weights */
     uint64_t bias_bytes;       /* size of dev_b */
@@ -209,6 +213,22 @@ AIE_API int aie_conv_run(const aie_plan *plan, const void *in, const void *dev_w
  * crates/ai-gpu-runtime/src/lowering.rs:99-187). */
 AIE_API int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, const void *dw_w,
                        const void *dw_b, const void *pw_w, const void *pw_b, void *out, void *stream);
+
+/* aie_conv_run_dw_pw over the depthwise input in + up2(up): `up` is a dense
+ * [n][up_h][up_w][C] tensor (C = the depthwise channels, 16-byte aligned)
+ * with 2 up_h, 2 up_w the depthwise input's height and width, and up2 the
+ * exact-2x half_pixel bilinear resize (crates/ai-core/src/reference/
+ * resize.rs:5-42).  The sum is formed in the kernel's staged input tile,
+ * rounded as resize-then-add rounds it, so neither the up-sampled tensor
+ * nor the sum reaches memory.  Replaces the tail of a feature pyramid that
+ * the reference dispatches as Resize, Conv(residual = the resize's output),
+ * depthwise Conv, 1x1 Conv (ai-gpu-runtime lowering.rs:99-187, one spec per
+ * op): `in` is the lateral conv's output computed without its residual.
+ * AIE_E_UNSUPPORTED when the shapes do not match or the operands are not
+ * TMA-compatible (dense, 16-byte aligned). */
+AIE_API int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, const void *in, const void *up,
+                           uint32_t up_h, uint32_t up_w, const void *dw_w, const void *dw_b, const void *pw_w,
+                           const void *pw_b, void *out, void *stream);
 
 /* Input staging: a batch of interleaved u8 RGB (cin = 3) or RGBA (cin = 4,
  * alpha dropped) frames [n, h, w, cin] -> the network's f32 input

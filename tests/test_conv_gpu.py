@@ -313,6 +313,73 @@ def test_fused_dw_pw_head(cuda_ok, n, ih, iw, c, k, s, act, cout, act2, layout):
     assert normalised_error(got, want_pw, scale) <= 10 * TOL_FFMA
 
 
+@pytest.mark.parametrize("n,h,w,c,k,s,cout", [(2, 80, 144, 32, 3, 1, 1), (3, 18, 26, 16, 3, 1, 2),
+                                                (1, 20, 36, 32, 5, 1, 1), (2, 12, 16, 8, 3, 2, 4),
+                                                (1, 6, 10, 24, 5, 2, 3)])
+def test_fused_head_up2_input(cuda_ok, n, h, w, c, k, s, cout):
+    """aie_conv_run_dw_pw_up2: the depthwise input is x + the exact-2x
+    half_pixel resize of a half-size tensor.  Equals, bit for bit, the fused
+    head run on x + resize(q) formed by the resize kernel (whose add rounds
+    the same way), and the ai-cpu restatement within the FFMA bar."""
+    from ai_engine_b200 import resize_bilinear
+    from ai_engine_b200.conv import run_dw_pw
+    from oracle import XorShift32
+    dw_op = Conv2d.depthwise(c, k, s, "relu")
+    pw_op = Conv2d.pointwise(c, cout, "sigmoid")
+    rng = XorShift32(7100 + h + c)
+    x = rng.vec_f32(n * h * w * c).reshape(n, h, w, c)
+    q = rng.vec_f32(n * (h // 2) * (w // 2) * c).reshape(n, h // 2, w // 2, c)
+    wd, bd = rng.vec_f32(c * k * k), rng.vec_f32(c)
+    wp, bp = rng.vec_f32(cout * c), rng.vec_f32(cout)
+    dwp = ConvPlan(dw_op, n, h, w, math="ffma").load_weights(wd, bd)
+    pwp = ConvPlan(pw_op, n, dwp.oh, dwp.ow, math="ffma").load_weights(wp, bp)
+    xd, qd = torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda()
+    got = run_dw_pw(dwp, pwp, xd, up=qd).cpu().numpy()
+    summed = resize_bilinear(qd, h, w, add=xd)
+    same = run_dw_pw(dwp, pwp, summed).cpu().numpy()
+    assert np.array_equal(got, same)
+    p2 = oracle.add(oracle.resize_bilinear(q, h, w), x)
+    want_dw, _ = oracle_conv(dw_op, p2, wd, bd, None)
+    want, _ = oracle_conv(pw_op, want_dw, wp, bp, None)
+    scale = oracle.dot_scale(pw_op, want_dw, wp, bp)
+    assert normalised_error(got, want, scale) <= 10 * TOL_FFMA
+
+
+def test_fused_head_up2_rejects_bad_source(cuda_ok):
+    """The up-sampled source must be half the depthwise input and aligned."""
+    from ai_engine_b200._lib import AieError
+    from ai_engine_b200.conv import run_dw_pw
+    dwp = ConvPlan(Conv2d.depthwise(32, 3, 1, "relu"), 1, 8, 12, math="ffma")
+    pwp = ConvPlan(Conv2d.pointwise(32, 1, "sigmoid"), 1, 8, 12, math="ffma")
+    dwp.load_weights(np.zeros(32 * 9, np.float32), np.zeros(32, np.float32))
+    pwp.load_weights(np.zeros(32, np.float32), np.zeros(1, np.float32))
+    x = torch.zeros(1, 8, 12, 32, device="cuda")
+    with pytest.raises(AieError):
+        run_dw_pw(dwp, pwp, x, up=torch.zeros(1, 5, 6, 32, device="cuda"))
+
+
+@pytest.mark.parametrize("math", ["auto", "ffma"])
+def test_model_fpn_tail_fusion_is_exact(cuda_ok, math):
+    """The benchmark network with its FPN tail folded into the head (the
+    last lateral conv without its residual, the resize dropped, the head
+    adding the up-sampled coarser level) equals the network run op by op,
+    bit for bit: the sum is rounded exactly as the residual add rounds it."""
+    from ai_engine_b200 import segnet
+    from ai_engine_b200.graph import Model
+    g = segnet.build_graph()
+    wts = segnet.init_weights(g)
+    x = torch.from_numpy(segnet.synthetic_input(2, seed=15)).cuda()
+    a = Model(g, wts, 2, (segnet.H, segnet.W, 3), math=math)
+    b = Model(g, wts, 2, (segnet.H, segnet.W, 3), math=math, fuse_tail=False)
+    assert any(r.out == "fpn.up4" for r in b.ops) and next(r for r in b.ops if r.kind == "dwpw").up is None
+    heads = [r for r in a.ops if r.kind == "dwpw"]
+    assert len(heads) == 1 and heads[0].up == "fpn.smooth4"
+    assert not any(r.out == "fpn.up4" for r in a.ops)
+    lat2 = next(r for r in a.ops if r.out == "fpn.lat2")
+    assert lat2.res is None
+    assert torch.equal(a.infer(x), b.infer(x))
+
+
 def test_model_head_fusion(cuda_ok):
     """The benchmark network with its dw3 -> 1x1 sigmoid head fused equals
     the same network run op by op (FFMA path)."""

@@ -220,14 +220,16 @@ def test_tf32_partial_tiles_residual(cuda_ok, n, h, w, cin, cout):
 @pytest.mark.parametrize("math", ["fp32_strict", "ffma", "tf32"])
 @pytest.mark.parametrize("kind", ["pw", "igemm"])
 @pytest.mark.parametrize("mode", ["half_pixel", "asymmetric"])
-def test_fused_bilinear_residual(cuda_ok, math, kind, mode):
+@pytest.mark.parametrize("rh,rw", [(9, 13), (7, 10)])
+def test_fused_bilinear_residual(cuda_ok, math, kind, mode, rh, rw):
     """Resize -> Conv(res) fused into the conv epilogue equals the unfused
     pair (oracle resize, then oracle conv with that residual): bit for bit
-    in fp32_strict mode."""
+    in fp32_strict mode.  9x13 -> 18x26 is an exact 2x (the integer
+    half_pixel path), 7x10 the general one."""
     import oracle
     from oracle import XorShift32
     op = Conv2d.pointwise(32, 40, "relu") if kind == "pw" else Conv2d.same(32, 40, 3, 1, "hardswish")
-    n, h, w, rh, rw = 2, 18, 26, 9, 13
+    n, h, w = 2, 18, 26
     rng = XorShift32(777)
     x = rng.vec_f32(n * h * w * 32).reshape(n, h, w, 32)
     wt = rng.vec_f32(op.cout * op.cin * op.kh * op.kw)
@@ -241,6 +243,43 @@ def test_fused_bilinear_residual(cuda_ok, math, kind, mode):
         assert np.array_equal(got, want)
     else:
         assert normalised_error(got, want, scale) <= (TOL_TF32 if math == "tf32" else TOL_FFMA)
+
+
+@pytest.mark.parametrize("math", ["fp32_strict", "tf32"])
+@pytest.mark.parametrize("n,h,w,cin,cout,split", [
+    (2, 10, 76, 32, 40, 0),     # rows of 76: a warp's 32 pixels wrap rows and frames; ragged last tile; 2 chunks
+    (3, 12, 36, 64, 64, 0),     # 36-wide rows (the FPN's 20x36 lateral)
+    (1, 20, 144, 32, 32, 0),    # 144-wide rows (the FPN's 80x144 lateral)
+    (2, 8, 64, 256, 48, 4),     # split-K: the patch is fetched while the partials are summed
+])
+def test_fused_up2_residual_patch(cuda_ok, math, n, h, w, cin, cout, split):
+    """Exact-2x half_pixel residual on 1x1 tensor-core tiles with ow >= 32:
+    the epilogue reads each warp's source patch from shared memory.  Equals
+    the unfused pair bit for bit in fp32_strict mode (which runs the FFMA
+    kernels) and within the TF32 bar on the tensor-core path."""
+    import oracle
+    from oracle import XorShift32
+    op = Conv2d.pointwise(cin, cout, "none")
+    rng = XorShift32(900 + w + cout)
+    x = rng.vec_f32(n * h * w * cin).reshape(n, h, w, cin)
+    wt = rng.vec_f32(op.cout * op.cin)
+    b = rng.vec_f32(op.cout)
+    lo = rng.vec_f32(n * (h // 2) * (w // 2) * cout).reshape(n, h // 2, w // 2, cout)
+    up = oracle.resize_bilinear(lo, h, w, "half_pixel")
+    want, scale = oracle_conv(op, x, wt, b, up)
+    plan = ConvPlan(op, n, h, w, has_res=True, math=math, split_k=split,
+                    res_resize=(h // 2, w // 2, "half_pixel")).load_weights(wt, b)
+    got = plan(torch.from_numpy(x).cuda(), torch.from_numpy(lo).cuda()).cpu().numpy()
+    if math == "fp32_strict":
+        assert np.array_equal(got, want)
+    else:
+        assert plan.kernel == "pw" and plan.math == "tf32"
+        assert normalised_error(got, want, scale) <= TOL_TF32
+        # the same GEMM with the upsampled residual as a plain tensor: only
+        # the residual's source differs, so the outputs agree bit for bit
+        ref = ConvPlan(op, n, h, w, has_res=True, math=math, split_k=split).load_weights(wt, b)
+        same = ref(torch.from_numpy(x).cuda(), torch.from_numpy(up).cuda()).cpu().numpy()
+        assert np.array_equal(got, same)
 
 
 def test_graph_fusion_matches_unfused(cuda_ok):
