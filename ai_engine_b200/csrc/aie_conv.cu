@@ -723,19 +723,27 @@ static int run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, con
         using G_ = DwTileGeom<K_, ST_, TW_>;                                                                  \
         CUtensorMap tm_;                                                                                      \
         const bool tma_ = dw_tile_tmap(a, G_::HW, G_::HH, &tm_);                                              \
+        if (up && (!tma_ || !dw_up2_tmap(up, d.n, up_h, up_w, d.cin, G_::HWQ, G_::HHQ, &tmq)))               \
+            return fail(AIE_E_UNSUPPORTED, "up-sampled input: operands are not TMA-compatible");              \
         if (up) {                                                                                             \
+            /* one tile per CTA: four CTAs per SM overlap their staging */                                   \
             auto ku_ = dw_tile_kernel<false, K_, ST_, TW_, true, true, true>;                                 \
-            if (!tma_ || !dw_up2_tmap(up, d.n, up_h, up_w, d.cin, G_::HWQ, G_::HHQ, &tmq))                      \
-                return fail(AIE_E_UNSUPPORTED, "up-sampled input: operands are not TMA-compatible");          \
             CUDA_TRY(ensure_smem_attr((const void *)ku_, G_::SMEM + G_::QSMEM));                              \
             ku_<<<(unsigned)blocks, G_::NT, G_::SMEM + G_::QSMEM, s>>>(tm_, tmq, a, tg, hd,                   \
                                                                       DwUp2{(int)up_h, (int)up_w});           \
+        } else if (tma_) {                                                                                    \
+            /* persistent CTAs with double-buffered staging */                                               \
+            auto kp_ = dw_head_persistent_kernel<K_, ST_, TW_>;                                               \
+            const int smem_ = 2 * G_::HH * G_::HW * 128 + 128;                                                \
+            CUDA_TRY(ensure_smem_attr((const void *)kp_, smem_));                                             \
+            int occ_ = 0;                                                                                     \
+            CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_, kp_, G_::NT, smem_));               \
+            const long long grid_ = std::min<long long>(blocks, (long long)std::max(occ_, 1) * tc_sm_count()); \
+            kp_<<<(unsigned)grid_, G_::NT, smem_, s>>>(tm_, a, tg, hd, (int)blocks);                          \
         } else {                                                                                              \
-            auto k1_ = dw_tile_kernel<false, K_, ST_, TW_, true, true>;                                       \
             auto k0_ = dw_tile_kernel<false, K_, ST_, TW_, true, false>;                                      \
-            CUDA_TRY(ensure_smem_attr((const void *)k1_, G_::SMEM));                                          \
             CUDA_TRY(ensure_smem_attr((const void *)k0_, G_::SMEM));                                          \
-            (tma_ ? k1_ : k0_)<<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, tm_, a, tg, hd, DwUp2{0, 0});  \
+            k0_<<<(unsigned)blocks, G_::NT, G_::SMEM, s>>>(tm_, tm_, a, tg, hd, DwUp2{0, 0});                  \
         }                                                                                                     \
     } while (0)
     if (d.kh == 3 && d.sh == 1) { if (wide) AIE_DWH(3, 1, 16); else AIE_DWH(3, 1, 8); }

@@ -958,111 +958,63 @@ struct PwHead {
     int y_coff, cout, act, y_pad_to;
 };
 
-// kTma: the halo is one 4-D TMA box (32 channels, HW, HH, 1) of the input's
-// (cin, iw, ih, n) tensor map, issued by one thread -- out-of-range pixels and
-// channels read as zeros -- instead of one 16-byte cp.async per chunk with its
-// index arithmetic (the staging was a sixth of the kernel's instructions).
-template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false, bool UP2 = false>
-__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
-    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq, const ConvArgs a,
-                   const DwTile g, const PwHead hd, const DwUp2 up)
+// UP2 prologue: halo += up2(q) at every in-range pixel (padding stays zero).
+// Rows 2k-1 and 2k of the up-sampled tensor sample the same two source rows
+// clamp(k-1), clamp(k) (with row weights 0.25 / 0.75 swapped), and columns
+// likewise, so one thread takes a 2 x 2 block of halo pixels for one channel
+// group: four corner loads, the resize's top / bot rows for its two columns,
+// then each pixel's mix -- every product and sum rounded on its own, in the
+// resize kernels' order.  The caller synchronises afterwards.
+template <int K, int S, int TW>
+__device__ __forceinline__ void dw_up2_add(float4 *halo4, const float4 *qp, const ConvArgs &a, const DwUp2 &up, int iy0,
+                                           int ix0, int qy0, int qx0)
 {
-    static_assert(!UP2 || kTma, "the up-sampled input is staged by TMA");
     using G = DwTileGeom<K, S, TW>;
-    constexpr int TH = G::TH, PB = G::PB, RUNS = G::RUNS, NT = G::NT, HH = G::HH, HW = G::HW;
-    extern __shared__ __align__(128) uint8_t dw_smem_raw[];
-    // [HH][HW][8 channel groups], 128-byte aligned (a TMA destination)
-    float4 *halo4 = reinterpret_cast<float4 *>((reinterpret_cast<uintptr_t>(dw_smem_raw) + 127) & ~uintptr_t(127));
-    __shared__ uint64_t halo_bar;
-    int b = blockIdx.x;
-    const int q1 = fdiv(b, g.div_slices), slice = b - q1 * g.slices;
-    const int q2 = fdiv(q1, g.div_tx), tx = q1 - q2 * g.tiles_x;
-    const int img = fdiv(q2, g.div_ty), ty = q2 - img * g.tiles_y;
-    const int c0 = slice * 32;
-    const int ncg = min(8, (a.cout - c0) >> 2);
-    const int iy0 = ty * TH * S - a.pt, ix0 = tx * TW * S - a.pl;
-    if constexpr (kTma) {
-        if (threadIdx.x == 0) {
-            mbar_init(&halo_bar, 1);
-            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        }
-        __syncthreads();
-        // UP2: source patch rows / columns from floor((first halo row - 1) / 2)
-        constexpr int HWQ = G::HWQ;
-        float4 *qp = halo4 + HH * HW * 8;  // [G::HHQ][HWQ][8 channel groups]
-        const int qy0 = (iy0 - 1) >> 1, qx0 = (ix0 - 1) >> 1;
-        if (threadIdx.x == 0) {
-            mbar_expect_tx(&halo_bar, (uint32_t)(HH * HW * 128 + (UP2 ? G::QSMEM : 0)));
-            tma_load_4d(halo4, &tmx, &halo_bar, c0, ix0, iy0, img);
-            if constexpr (UP2) tma_load_4d(qp, &tmq, &halo_bar, c0, qx0, qy0, img);
-        }
-        // bounded wait; the outcome is made CTA-uniform (head mode shuffles)
-        const bool landed = mbar_wait(&halo_bar, 0);
-        if (!__syncthreads_and(landed)) {
-            if (threadIdx.x == 0) report_error(0x04000001u);
-            return;
-        }
-        if constexpr (UP2) {
-            // halo += up2(q) at every in-range pixel (padding stays zero):
-            // thread (column hx, channel group) walks down its column keeping
-            // the horizontally interpolated source rows it needs (top / bot
-            // of the resize, rounded step by step as the resize kernels do)
-            // in a two-row window; each source row is interpolated once.
-            for (int t = threadIdx.x; t < HW * 8; t += NT) {  // stride-2 halos are wider than the CTA
-                const int hx = t >> 3, cg = t & 7;
-                const int ix = ix0 + hx;
-                if (ix >= 0 && ix < a.iw) {
-                    const int fx = (ix - 1) >> 1;
-                    const int x0 = max(fx, 0) - qx0, x1 = min(fx + 1, up.rw - 1) - qx0;
-                    const float tx = (ix & 1) ? 0.25f : 0.75f, tx1 = __fsub_rn(1.0f, tx);
-                    auto lerp_x = [&](int r) {
-                        const float4 g0 = qp[(r * HWQ + x0) * 8 + cg], g1 = qp[(r * HWQ + x1) * 8 + cg];
-                        return make_float4(__fadd_rn(__fmul_rn(g0.x, tx1), __fmul_rn(g1.x, tx)),
-                                           __fadd_rn(__fmul_rn(g0.y, tx1), __fmul_rn(g1.y, tx)),
-                                           __fadd_rn(__fmul_rn(g0.z, tx1), __fmul_rn(g1.z, tx)),
-                                           __fadd_rn(__fmul_rn(g0.w, tx1), __fmul_rn(g1.w, tx)));
-                    };
-                    int ia = -1, ib = -1;
-                    float4 ta = make_float4(0.f, 0.f, 0.f, 0.f), tb = ta;
+    constexpr int NT = G::NT, HH = G::HH, HW = G::HW, HWQ = G::HWQ;
+    const int ky0 = (iy0 + 1) >> 1, kx0 = (ix0 + 1) >> 1;  // pair (2k-1, 2k) holding the first halo row / column
+    const int nky = ((iy0 + HH) >> 1) - ky0 + 1, nkx = ((ix0 + HW) >> 1) - kx0 + 1;
+    auto lerp = [](float4 p, float4 q, float w1, float w) {  // p (1 - w) + q w, rounded step by step
+        return make_float4(__fadd_rn(__fmul_rn(p.x, w1), __fmul_rn(q.x, w)), __fadd_rn(__fmul_rn(p.y, w1), __fmul_rn(q.y, w)),
+                           __fadd_rn(__fmul_rn(p.z, w1), __fmul_rn(q.z, w)), __fadd_rn(__fmul_rn(p.w, w1), __fmul_rn(q.w, w)));
+    };
+    for (int t = threadIdx.x; t < nky * nkx * 8; t += NT) {
+        const int cg = t & 7, pk = t >> 3;
+        const int kyi = pk / nkx, kxi = pk - kyi * nkx;
+        const int k = ky0 + kyi, j = kx0 + kxi;
+        const int r0 = max(k - 1, 0) - qy0, r1 = min(k, up.rh - 1) - qy0;
+        const int c0 = max(j - 1, 0) - qx0, c1 = min(j, up.rw - 1) - qx0;
+        const float4 g00 = qp[(r0 * HWQ + c0) * 8 + cg], g01 = qp[(r0 * HWQ + c1) * 8 + cg];
+        const float4 g10 = qp[(r1 * HWQ + c0) * 8 + cg], g11 = qp[(r1 * HWQ + c1) * 8 + cg];
+        // columns 2j-1 (weight 0.25 on column clamp(j)) and 2j (0.75)
+        const float4 top[2] = {lerp(g00, g01, 0.75f, 0.25f), lerp(g00, g01, 0.25f, 0.75f)};
+        const float4 bot[2] = {lerp(g10, g11, 0.75f, 0.25f), lerp(g10, g11, 0.25f, 0.75f)};
 #pragma unroll
-                    for (int hy = 0; hy < HH; hy++) {
-                        const int iy = iy0 + hy;
-                        if (iy < 0 || iy >= a.ih) continue;
-                        const int fy = (iy - 1) >> 1;
-                        const int y0 = max(fy, 0) - qy0, y1 = min(fy + 1, up.rh - 1) - qy0;
-                        if (y0 == ib) { ta = tb; ia = ib; }
-                        if (y0 != ia) { ta = lerp_x(y0); ia = y0; }
-                        if (y1 != ib) { tb = y1 == ia ? ta : lerp_x(y1); ib = y1; }
-                        const float ty = (iy & 1) ? 0.25f : 0.75f, ty1 = __fsub_rn(1.0f, ty);
-                        float4 &h = halo4[(hy * HW + hx) * 8 + cg];
-                        float4 v = h;
-                        v.x = __fadd_rn(v.x, __fadd_rn(__fmul_rn(ta.x, ty1), __fmul_rn(tb.x, ty)));
-                        v.y = __fadd_rn(v.y, __fadd_rn(__fmul_rn(ta.y, ty1), __fmul_rn(tb.y, ty)));
-                        v.z = __fadd_rn(v.z, __fadd_rn(__fmul_rn(ta.z, ty1), __fmul_rn(tb.z, ty)));
-                        v.w = __fadd_rn(v.w, __fadd_rn(__fmul_rn(ta.w, ty1), __fmul_rn(tb.w, ty)));
-                        h = v;
-                    }
-                }
+        for (int dy = 0; dy < 2; dy++) {
+            const int iy = 2 * k - 1 + dy, hy = iy - iy0;
+            if (iy < 0 || iy >= a.ih || hy < 0 || hy >= HH) continue;
+            const float ty = dy ? 0.75f : 0.25f, ty1 = dy ? 0.25f : 0.75f;
+#pragma unroll
+            for (int dx = 0; dx < 2; dx++) {
+                const int ix = 2 * j - 1 + dx, hx = ix - ix0;
+                if (ix < 0 || ix >= a.iw || hx < 0 || hx >= HW) continue;
+                const float4 u = lerp(top[dx], bot[dx], ty1, ty);
+                float4 &h = halo4[(hy * HW + hx) * 8 + cg];
+                float4 v = h;
+                v.x = __fadd_rn(v.x, u.x); v.y = __fadd_rn(v.y, u.y); v.z = __fadd_rn(v.z, u.z); v.w = __fadd_rn(v.w, u.w);
+                h = v;
             }
-            __syncthreads();
         }
-    } else {
-        const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;
-        for (int i = threadIdx.x; i < HH * HW * 8; i += NT) {
-            const int cgi = i & 7, pix = i >> 3;
-            const int hy = pix / HW, hx = pix - hy * HW;
-            const int iy = iy0 + hy, ix = ix0 + hx;
-            const bool ok = cgi < ncg && iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
-            const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cgi * 4 : a.x;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                             (uint32_t)__cvta_generic_to_shared(halo4 + i)),
-                         "l"(src), "r"(ok ? 16 : 0)
-                         : "memory");
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncthreads();
     }
+}
+
+// The depthwise conv of one staged tile (and, in head mode, the 1x1 head).
+// Every thread of the CTA calls it (head mode shuffles across lanes).
+template <bool kStrict, int K, int S, int TW, bool HEAD>
+__device__ __forceinline__ void dw_tile_compute(const float4 *halo4, const ConvArgs &a, const PwHead &hd, int img, int ty,
+                                                int tx, int c0, int ncg)
+{
+    using G = DwTileGeom<K, S, TW>;
+    constexpr int TH = G::TH, PB = G::PB, RUNS = G::RUNS, HW = G::HW;
     const int cgi = threadIdx.x & 7, run = (threadIdx.x >> 3) % RUNS, row = threadIdx.x / (8 * RUNS);
     const int oy = ty * TH + row, ox0 = tx * TW + run * PB;
     const bool valid = cgi < ncg && oy < a.oh && ox0 < a.ow;
@@ -1151,6 +1103,147 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
         *reinterpret_cast<float4 *>(a.y + m * a.y_stride + a.y_coff + ch) =
             make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
     }
+}
+
+// kTma: the halo is one 4-D TMA box (32 channels, HW, HH, 1) of the input's
+// (cin, iw, ih, n) tensor map, issued by one thread -- out-of-range pixels and
+// channels read as zeros -- instead of one 16-byte cp.async per chunk with its
+// index arithmetic (the staging was a sixth of the kernel's instructions).
+template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false, bool UP2 = false>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
+    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq, const ConvArgs a,
+                   const DwTile g, const PwHead hd, const DwUp2 up)
+{
+    static_assert(!UP2 || kTma, "the up-sampled input is staged by TMA");
+    using G = DwTileGeom<K, S, TW>;
+    constexpr int TH = G::TH, NT = G::NT, HH = G::HH, HW = G::HW;
+    extern __shared__ __align__(128) uint8_t dw_smem_raw[];
+    // [HH][HW][8 channel groups], 128-byte aligned (a TMA destination)
+    float4 *halo4 = reinterpret_cast<float4 *>((reinterpret_cast<uintptr_t>(dw_smem_raw) + 127) & ~uintptr_t(127));
+    __shared__ uint64_t halo_bar;
+    int b = blockIdx.x;
+    const int q1 = fdiv(b, g.div_slices), slice = b - q1 * g.slices;
+    const int q2 = fdiv(q1, g.div_tx), tx = q1 - q2 * g.tiles_x;
+    const int img = fdiv(q2, g.div_ty), ty = q2 - img * g.tiles_y;
+    const int c0 = slice * 32;
+    const int ncg = min(8, (a.cout - c0) >> 2);
+    const int iy0 = ty * TH * S - a.pt, ix0 = tx * TW * S - a.pl;
+    if constexpr (kTma) {
+        if (threadIdx.x == 0) {
+            mbar_init(&halo_bar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        // UP2: source patch rows / columns from floor((first halo row - 1) / 2)
+        float4 *qp = halo4 + HH * HW * 8;  // [G::HHQ][G::HWQ][8 channel groups]
+        const int qy0 = (iy0 - 1) >> 1, qx0 = (ix0 - 1) >> 1;
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(&halo_bar, (uint32_t)(HH * HW * 128 + (UP2 ? G::QSMEM : 0)));
+            tma_load_4d(halo4, &tmx, &halo_bar, c0, ix0, iy0, img);
+            if constexpr (UP2) tma_load_4d(qp, &tmq, &halo_bar, c0, qx0, qy0, img);
+        }
+        // bounded wait; the outcome is made CTA-uniform (head mode shuffles)
+        const bool landed = mbar_wait_sleep(&halo_bar, 0);
+        if (!__syncthreads_and(landed)) {
+            if (threadIdx.x == 0) report_error(0x04000001u);
+            return;
+        }
+        if constexpr (UP2) {
+            dw_up2_add<K, S, TW>(halo4, qp, a, up, iy0, ix0, qy0, qx0);
+            __syncthreads();
+        }
+    } else {
+        const float *xb = a.x + (long long)img * a.ih * a.iw * a.x_stride + a.x_coff + c0;
+        for (int i = threadIdx.x; i < HH * HW * 8; i += NT) {
+            const int cgi = i & 7, pix = i >> 3;
+            const int hy = pix / HW, hx = pix - hy * HW;
+            const int iy = iy0 + hy, ix = ix0 + hx;
+            const bool ok = cgi < ncg && iy >= 0 && iy < a.ih && ix >= 0 && ix < a.iw;
+            const float *src = ok ? xb + ((long long)iy * a.iw + ix) * a.x_stride + cgi * 4 : a.x;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                             (uint32_t)__cvta_generic_to_shared(halo4 + i)),
+                         "l"(src), "r"(ok ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
+    }
+    dw_tile_compute<kStrict, K, S, TW, HEAD>(halo4, a, hd, img, ty, tx, c0, ncg);
+}
+
+// Persistent fused head (head mode, TMA staging): a CTA walks the tiles
+// blockIdx.x, + gridDim.x, ... with two staging buffers, so the TMA loads of
+// the tiles two ahead land while this tile computes -- a one-tile CTA waits
+// for its load with nothing else to do.  Tile order and arithmetic are those
+// of dw_tile_kernel<false, K, S, TW, true, true>.  (Measured on B200 at
+// 256 x 80 x 144 x 32: 153 us against 172 us one tile per CTA.  With the
+// up-sampled input the doubled staging leaves three CTAs per SM and the
+// one-tile kernel wins, 235 against 266 us, so that mode stays one tile per
+// CTA.)
+template <int K, int S, int TW>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
+    dw_head_persistent_kernel(const __grid_constant__ CUtensorMap tmx, const ConvArgs a, const DwTile g,
+                              const PwHead hd, const int tiles)
+{
+    using G = DwTileGeom<K, S, TW>;
+    constexpr int TH = G::TH, HH = G::HH, HW = G::HW;
+    constexpr uint32_t BUF = HH * HW * 128;
+    static_assert(BUF % 128 == 0, "staging buffers stay 128-byte aligned");
+    extern __shared__ __align__(128) uint8_t dw_smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dw_smem_raw) + 127) & ~uintptr_t(127));
+    __shared__ uint64_t full[2];
+    const int ncg = min(8, a.cout >> 2);
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // tile -> (frame, tile row, tile column): one channel slice in head mode
+    auto origin = [&](int t, int &img, int &ty, int &tx) {
+        const int q2 = fdiv(t, g.div_tx);
+        tx = t - q2 * g.tiles_x;
+        img = fdiv(q2, g.div_ty);
+        ty = q2 - img * g.tiles_y;
+    };
+    bool pend[2] = {false, false};  // thread 0: loads in flight per buffer
+    auto issue = [&](int bsel, int t) {
+        int img, ty, tx;
+        origin(t, img, ty, tx);
+        // the CTA's reads of this buffer (ordered by the barrier before the
+        // call) come before the copy's writes
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&full[bsel], BUF);
+        tma_load_4d(base + bsel * BUF, &tmx, &full[bsel], 0, tx * TW * S - a.pl, ty * TH * S - a.pt, img);
+        pend[bsel] = true;
+    };
+    if (threadIdx.x == 0) {
+        if ((int)blockIdx.x < tiles) issue(0, blockIdx.x);
+        if ((int)(blockIdx.x + gridDim.x) < tiles) issue(1, blockIdx.x + gridDim.x);
+    }
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+        const int bsel = it & 1;
+        // bounded wait; the outcome is made CTA-uniform (the head shuffles)
+        const bool landed = mbar_wait_sleep(&full[bsel], (it >> 1) & 1);
+        if (!__syncthreads_and(landed)) {
+            if (threadIdx.x == 0) report_error(0x04000002u);
+            break;
+        }
+        if (threadIdx.x == 0) pend[bsel] = false;
+        int img, ty, tx;
+        origin(t, img, ty, tx);
+        dw_tile_compute<false, K, S, TW, true>(reinterpret_cast<const float4 *>(base + bsel * BUF), a, hd, img, ty, tx,
+                                               0, ncg);
+        __syncthreads();  // the buffer is free: stage the tile after next into it
+        if (threadIdx.x == 0 && t + 2 * (int)gridDim.x < tiles) issue(bsel, t + 2 * gridDim.x);
+    }
+    // no copy may land after exit: wait (bounded) for loads still in flight
+    if (threadIdx.x == 0)
+        for (int bsel = 0; bsel < 2; bsel++)
+            if (pend[bsel] && !mbar_wait(&full[bsel], ((it + (bsel != (int)(it & 1))) >> 1) & 1))
+                report_error(0x04000003u);
 }
 
 struct DwGrid {
