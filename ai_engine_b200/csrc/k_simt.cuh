@@ -971,39 +971,44 @@ __device__ __forceinline__ void dw_up2_add(float4 *halo4, const float4 *qp, cons
 {
     using G = DwTileGeom<K, S, TW>;
     constexpr int NT = G::NT, HH = G::HH, HW = G::HW, HWQ = G::HWQ;
-    const int ky0 = (iy0 + 1) >> 1, kx0 = (ix0 + 1) >> 1;  // pair (2k-1, 2k) holding the first halo row / column
-    const int nky = ((iy0 + HH) >> 1) - ky0 + 1, nkx = ((ix0 + HW) >> 1) - kx0 + 1;
+    // pairs (2k-1, 2k) overlapping the halo: at most HH / 2 + 1 of them
+    constexpr int NKY = HH / 2 + 1, NKX = HW / 2 + 1;
+    const int ky0 = (iy0 + 1) >> 1, kx0 = (ix0 + 1) >> 1;  // pair holding the first halo row / column
+    // halo rows / columns inside the image: [hy_lo, hy_hi) x [hx_lo, hx_hi)
+    const int hy_lo = max(0, -iy0), hy_hi = min(HH, a.ih - iy0);
+    const int hx_lo = max(0, -ix0), hx_hi = min(HW, a.iw - ix0);
+    // first halo row / column of pair 0 (-1 when the halo starts at its second row)
+    const int hy_k0 = 2 * ky0 - 1 - iy0, hx_k0 = 2 * kx0 - 1 - ix0;
     auto lerp = [](float4 p, float4 q, float w1, float w) {  // p (1 - w) + q w, rounded step by step
         return make_float4(__fadd_rn(__fmul_rn(p.x, w1), __fmul_rn(q.x, w)), __fadd_rn(__fmul_rn(p.y, w1), __fmul_rn(q.y, w)),
                            __fadd_rn(__fmul_rn(p.z, w1), __fmul_rn(q.z, w)), __fadd_rn(__fmul_rn(p.w, w1), __fmul_rn(q.w, w)));
     };
-    for (int t = threadIdx.x; t < nky * nkx * 8; t += NT) {
+    for (int t = threadIdx.x; t < NKY * NKX * 8; t += NT) {
         const int cg = t & 7, pk = t >> 3;
-        const int kyi = pk / nkx, kxi = pk - kyi * nkx;
+        const int kyi = pk / NKX, kxi = pk - kyi * NKX;  // compile-time divisor
+        const int hy0 = hy_k0 + 2 * kyi, hx0 = hx_k0 + 2 * kxi;  // halo row / column of the pair's first pixel
+        // rows hy0, hy0 + 1 and columns hx0, hx0 + 1 that lie in the image and the halo
+        const bool ry0 = hy0 >= hy_lo && hy0 < hy_hi, ry1 = hy0 + 1 >= hy_lo && hy0 + 1 < hy_hi;
+        const bool rx0 = hx0 >= hx_lo && hx0 < hx_hi, rx1 = hx0 + 1 >= hx_lo && hx0 + 1 < hx_hi;
+        if (!((ry0 || ry1) && (rx0 || rx1))) continue;
         const int k = ky0 + kyi, j = kx0 + kxi;
         const int r0 = max(k - 1, 0) - qy0, r1 = min(k, up.rh - 1) - qy0;
         const int c0 = max(j - 1, 0) - qx0, c1 = min(j, up.rw - 1) - qx0;
         const float4 g00 = qp[(r0 * HWQ + c0) * 8 + cg], g01 = qp[(r0 * HWQ + c1) * 8 + cg];
         const float4 g10 = qp[(r1 * HWQ + c0) * 8 + cg], g11 = qp[(r1 * HWQ + c1) * 8 + cg];
-        // columns 2j-1 (weight 0.25 on column clamp(j)) and 2j (0.75)
-        const float4 top[2] = {lerp(g00, g01, 0.75f, 0.25f), lerp(g00, g01, 0.25f, 0.75f)};
-        const float4 bot[2] = {lerp(g10, g11, 0.75f, 0.25f), lerp(g10, g11, 0.25f, 0.75f)};
-#pragma unroll
-        for (int dy = 0; dy < 2; dy++) {
-            const int iy = 2 * k - 1 + dy, hy = iy - iy0;
-            if (iy < 0 || iy >= a.ih || hy < 0 || hy >= HH) continue;
-            const float ty = dy ? 0.75f : 0.25f, ty1 = dy ? 0.25f : 0.75f;
-#pragma unroll
-            for (int dx = 0; dx < 2; dx++) {
-                const int ix = 2 * j - 1 + dx, hx = ix - ix0;
-                if (ix < 0 || ix >= a.iw || hx < 0 || hx >= HW) continue;
-                const float4 u = lerp(top[dx], bot[dx], ty1, ty);
-                float4 &h = halo4[(hy * HW + hx) * 8 + cg];
-                float4 v = h;
-                v.x = __fadd_rn(v.x, u.x); v.y = __fadd_rn(v.y, u.y); v.z = __fadd_rn(v.z, u.z); v.w = __fadd_rn(v.w, u.w);
-                h = v;
-            }
-        }
+        // columns 2j-1 (weight 0.25 on column clamp(j)) and 2j (0.75); rows likewise
+        const float4 top0 = lerp(g00, g01, 0.75f, 0.25f), top1 = lerp(g00, g01, 0.25f, 0.75f);
+        const float4 bot0 = lerp(g10, g11, 0.75f, 0.25f), bot1 = lerp(g10, g11, 0.25f, 0.75f);
+        float4 *h = halo4 + (hy0 * HW + hx0) * 8 + cg;
+        auto add = [&](float4 *dst, float4 u) {
+            float4 v = *dst;
+            v.x = __fadd_rn(v.x, u.x); v.y = __fadd_rn(v.y, u.y); v.z = __fadd_rn(v.z, u.z); v.w = __fadd_rn(v.w, u.w);
+            *dst = v;
+        };
+        if (ry0 && rx0) add(h, lerp(top0, bot0, 0.75f, 0.25f));
+        if (ry0 && rx1) add(h + 8, lerp(top1, bot1, 0.75f, 0.25f));
+        if (ry1 && rx0) add(h + HW * 8, lerp(top0, bot0, 0.25f, 0.75f));
+        if (ry1 && rx1) add(h + HW * 8 + 8, lerp(top1, bot1, 0.25f, 0.75f));
     }
 }
 

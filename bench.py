@@ -39,42 +39,40 @@ H, W = 160, 288
 # ncu summaries under profiles/).  Traffic scales with frames, so the
 # roofline's per-launch traffic is this times the batch.
 TRAFFIC_PER_FRAME = {
-    "stem": 1561896,
-    "e1.conv": 1689324,
-    "e1.pw": 375476,
-    "e2.conv": 371014,
-    "e2.pw": 277432,
-    "e3.dw5": 184758,
-    "e3.exp": 254280,
-    "e3.dw5s2": 558364,
-    "e3.proj": 139570,
-    "e4.0.exp": 70450,
-    "e4.0.dw3": 138600,
-    "e4.0.proj": 208764,
-    "e4.1.exp": 70452,
-    "e4.1.dw3": 138602,
-    "e4.1.proj": 208772,
-    "e5.exp": 71036,
-    "e5.dw3": 277100,
-    "e5.proj": 278804,
-    "e5.0.exp": 95090,
-    "e5.0.dw3": 423670,
-    "e5.0.proj": 463694,
-    "e5.1.exp": 94994,
-    "e5.1.dw3": 419244,
-    "e5.1.proj": 463698,
-    "head960": 298942,
-    "fpn.lat16": 694810,
-    "fpn.up16": 46598,
-    "fpn.lat8": 369666,
-    "fpn.up8": 445744,
-    "fpn.lat4": 1490640,
-    "fpn.smooth4": 866972,
-    "fpn.up4": 1359882,
-    "fpn.lat2": 4139136,
-    "head.dw3": 2577380,
-    "head.pw": 1499020,
-    "mask": 46602,
+    "stem": 1558886,
+    "e1.conv": 1690558,
+    "e1.pw": 373230,
+    "e2.conv": 372728,
+    "e2.pw": 277404,
+    "e3.dw5": 184760,
+    "e3.exp": 251034,
+    "e3.dw5s2": 559736,
+    "e3.proj": 139544,
+    "e4.0.exp": 70454,
+    "e4.0.dw3": 138598,
+    "e4.0.proj": 208742,
+    "e4.1.exp": 70422,
+    "e4.1.dw3": 138600,
+    "e4.1.proj": 208744,
+    "e5.exp": 71094,
+    "e5.dw3": 277086,
+    "e5.proj": 278738,
+    "e5.0.exp": 94988,
+    "e5.0.dw3": 424506,
+    "e5.0.proj": 463708,
+    "e5.1.exp": 94960,
+    "e5.1.dw3": 422446,
+    "e5.1.proj": 463724,
+    "head960": 298354,
+    "fpn.lat16": 694570,
+    "fpn.up16": 46398,
+    "fpn.lat8": 369668,
+    "fpn.up8": 444278,
+    "fpn.lat4": 1493734,
+    "fpn.smooth4": 866266,
+    "fpn.lat2": 2508778,
+    "head.pw": 1875208,
+    "mask": 46430,
 }
 
 
