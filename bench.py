@@ -39,40 +39,40 @@ H, W = 160, 288
 # ncu summaries under profiles/).  Traffic scales with frames, so the
 # roofline's per-launch traffic is this times the batch.
 TRAFFIC_PER_FRAME = {
-    "stem": 1558886,
-    "e1.conv": 1690558,
-    "e1.pw": 373230,
-    "e2.conv": 372728,
-    "e2.pw": 277404,
+    "stem": 1562008,
+    "e1.conv": 1691578,
+    "e1.pw": 373514,
+    "e2.conv": 371030,
+    "e2.pw": 277406,
     "e3.dw5": 184760,
-    "e3.exp": 251034,
-    "e3.dw5s2": 559736,
-    "e3.proj": 139544,
-    "e4.0.exp": 70454,
-    "e4.0.dw3": 138598,
-    "e4.0.proj": 208742,
-    "e4.1.exp": 70422,
-    "e4.1.dw3": 138600,
-    "e4.1.proj": 208744,
-    "e5.exp": 71094,
-    "e5.dw3": 277086,
+    "e3.exp": 255568,
+    "e3.dw5s2": 583264,
+    "e3.proj": 139546,
+    "e4.0.exp": 70424,
+    "e4.0.dw3": 138600,
+    "e4.0.proj": 208744,
+    "e4.1.exp": 70430,
+    "e4.1.dw3": 138618,
+    "e4.1.proj": 208742,
+    "e5.exp": 71016,
+    "e5.dw3": 278970,
     "e5.proj": 278738,
-    "e5.0.exp": 94988,
-    "e5.0.dw3": 424506,
-    "e5.0.proj": 463708,
-    "e5.1.exp": 94960,
-    "e5.1.dw3": 422446,
-    "e5.1.proj": 463724,
-    "head960": 298354,
-    "fpn.lat16": 694570,
-    "fpn.up16": 46398,
-    "fpn.lat8": 369668,
-    "fpn.up8": 444278,
-    "fpn.lat4": 1493734,
-    "fpn.smooth4": 866266,
-    "fpn.lat2": 2508778,
-    "head.pw": 1875208,
-    "mask": 46430,
+    "e5.0.exp": 95010,
+    "e5.0.dw3": 427214,
+    "e5.0.proj": 463672,
+    "e5.1.exp": 94980,
+    "e5.1.dw3": 421550,
+    "e5.1.proj": 464198,
+    "head960": 299468,
+    "fpn.lat16": 697642,
+    "fpn.up16": 46396,
+    "fpn.lat8": 370550,
+    "fpn.up8": 444408,
+    "fpn.lat4": 1492144,
+    "fpn.smooth4": 867448,
+    "fpn.lat2": 2504488,
+    "head.pw": 1873088,
+    "mask": 46432,
 }
 
 
