@@ -214,6 +214,25 @@ def run_dw_pw(dw: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, out: Optional[tor
     return out
 
 
+def run_mbconv(ex: "ConvPlan", dw: "ConvPlan", pj: "ConvPlan", x: torch.Tensor, res: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """An inverted-bottleneck block -- 1x1 expand `ex`, depthwise 3x3 `dw`,
+    1x1 project `pj` (+ `res`) -- in one launch (aie_conv_run_mbconv) for
+    frames up to 10 x 24: the expanded tensor never reaches memory.  Raises
+    AieError(AIE_E_UNSUPPORTED) for blocks the fused kernel does not cover."""
+    for p in (ex, dw, pj):
+        if p.w is None:
+            raise RuntimeError("load_weights() first")
+    if out is None:
+        out = torch.empty(pj.out_shape(), dtype=torch.float32, device=x.device)
+    check(ex.lib.aie_conv_run_mbconv(ex._h, dw._h, pj._h, _dptr(x), C.c_void_p(ex.w.data_ptr()),
+                                     C.c_void_p(ex.b.data_ptr()), C.c_void_p(dw.w.data_ptr()),
+                                     C.c_void_p(dw.b.data_ptr()), C.c_void_p(pj.w.data_ptr()),
+                                     C.c_void_p(pj.b.data_ptr()), _dptr(res), _dptr(out),
+                                     C.c_void_p(_stream_handle(stream))), "aie_conv_run_mbconv")
+    return out
+
+
 def input_u8(frames: torch.Tensor, layout: str = "nhwc", out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """u8 RGB / RGBA frames [n, h, w, 3|4] on the GPU -> the network's f32
     input [n, h, w, 3] (NHWC) or [n, h, w, 4] (NHWC-C4), value / 255

@@ -23,6 +23,7 @@
 #include "k_tc.cuh"
 #include "k_stem_tc.cuh"
 #include "k_pw_simt.cuh"
+#include "k_mbconv.cuh"
 
 using namespace aie;
 
@@ -768,6 +769,83 @@ extern "C" int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, co
 {
     if (!up) return fail(AIE_E_INVALID, "null up-sampled source");
     return run_dw_pw(dw, pw, in, up, up_h, up_w, dw_w, dw_b, pw_w, pw_b, out, stream);
+}
+
+extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const aie_plan *pj, const void *in,
+                                   const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b,
+                                   const void *pj_w, const void *pj_b, const void *res, void *out, void *stream)
+{
+    if (!ex || !dw || !pj || !in || !ex_w || !ex_b || !dw_w || !dw_b || !pj_w || !pj_b || !out)
+        return fail(AIE_E_INVALID, "null argument");
+    const aie_conv_desc &e = ex->d, &d = dw->d, &q = pj->d;
+    auto dense = [](const aie_plan *p) {
+        return p->d.layout == AIE_LAYOUT_NHWC && p->x_stride == (long long)p->d.cin && p->x_coff == 0 &&
+               p->y_stride == (long long)p->d.cout && p->y_coff == 0;
+    };
+    if (ex->kernel != AIE_KERNEL_PW || ex->math != AIE_MATH_TF32 || e.has_res || !dense(ex) || e.cin % 32)
+        return fail(AIE_E_UNSUPPORTED, "fused block: the expand plan must be a dense TF32 1x1 without residual, "
+                                       "cin %% 32 == 0");
+    if (dw->kernel != AIE_KERNEL_DW || dw->strict || d.has_res || d.kh != 3 || d.kw != 3 || d.sh != 1 || d.sw != 1 ||
+        d.dil != 1 || d.pad[0] != 1 || d.pad[1] != 1 || d.pad[2] != 1 || d.pad[3] != 1 || d.cin != e.cout ||
+        d.n != e.n || d.ih != e.ih || d.iw != e.iw || !dense(dw))
+        return fail(AIE_E_UNSUPPORTED, "fused block: the depthwise plan must be a dense 3x3, stride 1, pad 1 conv "
+                                       "over the expand output, not FP32_STRICT");
+    if (pj->kernel != AIE_KERNEL_PW || pj->math != AIE_MATH_TF32 || q.cin != e.cout || q.cout > 128 || q.n != e.n ||
+        q.ih != e.ih || q.iw != e.iw || !dense(pj) || (q.has_res && q.res_mode != AIE_RES_TENSOR) ||
+        (q.has_res && (pj->r_stride != (long long)q.cout || pj->r_coff != 0)))
+        return fail(AIE_E_UNSUPPORTED, "fused block: the project plan must be a dense TF32 1x1 over the depthwise "
+                                       "output with cout <= 128");
+    if (e.ih > (uint32_t)kMbRows || e.iw > (uint32_t)kMbRowStride)
+        return fail(AIE_E_UNSUPPORTED, "fused block: frames up to %dx%d, got %ux%u", kMbRows, kMbRowStride, e.ih, e.iw);
+    if (q.has_res != (res != nullptr)) return fail(AIE_E_INVALID, "residual pointer does not match the project plan");
+    if (((uintptr_t)in | (uintptr_t)ex_w | (uintptr_t)ex_b | (uintptr_t)dw_w | (uintptr_t)dw_b | (uintptr_t)pj_w |
+         (uintptr_t)pj_b | (uintptr_t)res | (uintptr_t)out) % 16)
+        return fail(AIE_E_ALIGN, "fused block: tensors must be 16-byte aligned");
+    PFN_encodeTiled enc = tc_encoder();
+    if (!enc) return fail(AIE_E_UNSUPPORTED, "tensor-map encoder unavailable");
+    CUtensorMap tmX, tmWe, tmWp;
+    memset(&tmX, 0, sizeof tmX);
+    memset(&tmWe, 0, sizeof tmWe);
+    memset(&tmWp, 0, sizeof tmWp);
+    const cuuint32_t e1[4] = {1, 1, 1, 1};
+    {
+        const cuuint64_t dims[4] = {e.cin, e.iw, e.ih, e.n};
+        const cuuint64_t str[3] = {(cuuint64_t)e.cin * 4, (cuuint64_t)e.cin * 4 * e.iw, (cuuint64_t)e.cin * 4 * e.iw * e.ih};
+        const cuuint32_t box[4] = {32, (cuuint32_t)kMbRowStride, (cuuint32_t)kMbRows, 1};
+        if (enc(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)in, dims, str, box, e1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+            return fail(AIE_E_UNSUPPORTED, "fused block: input tensor map rejected");
+    }
+    auto wmap = [&](CUtensorMap *tm, const void *w, uint32_t k, uint32_t rows) {
+        const cuuint64_t dims[2] = {k, rows};
+        const cuuint64_t str[1] = {(cuuint64_t)k * 4};
+        const cuuint32_t box[2] = {32, (cuuint32_t)kMbChunk};
+        return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)w, dims, str, box, e1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    // TF32 packing: [tap = 1][cout][cin_pad4], K-major rows
+    if (!wmap(&tmWe, ex_w, (uint32_t)ex->cin_pad, e.cout) || !wmap(&tmWp, pj_w, (uint32_t)pj->cin_pad, q.cout))
+        return fail(AIE_E_UNSUPPORTED, "fused block: weight tensor map rejected");
+    MbArgs a;
+    a.x = (const float *)in;
+    a.b_exp = (const float *)ex_b;
+    a.w_dw = (const float *)dw_w;
+    a.b_dw = (const float *)dw_b;
+    a.b_proj = (const float *)pj_b;
+    a.res = (const float *)res;
+    a.y = (float *)out;
+    a.n = (int)e.n; a.h = (int)e.ih; a.w = (int)e.iw;
+    a.cin = (int)e.cin; a.cexp = (int)e.cout; a.cout = (int)q.cout; a.cexp_pad4 = (int)rup(e.cout, 4);
+    a.act_exp = e.act; a.act_dw = d.act; a.act_proj = q.act;
+    cudaStream_t s = (cudaStream_t)stream;
+    CUDA_TRY(ensure_smem_attr((const void *)mbconv_kernel, (int)kMbSmem));
+    const unsigned grid = (unsigned)std::min<long long>(e.n, tc_sm_count());
+    mbconv_kernel<<<grid, kMbThreads, kMbSmem, s>>>(tmX, tmWe, tmWp, a);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, "fused block launch");
+    return AIE_OK;
 }
 
 extern "C" int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, const void *in, int32_t layout,

@@ -22,7 +22,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_dw_pw
+from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_dw_pw, run_mbconv
 
 
 @dataclass
@@ -36,6 +36,7 @@ class OpRecord:
     plan: Optional[ConvPlan] = None
     head: Optional[ConvPlan] = None   # kind "dwpw": the fused 1x1 (cout <= 4) after the depthwise plan
     up: Optional[str] = None          # kind "dwpw": source whose exact-2x resize is added to the depthwise input
+    blk: Optional[Tuple[ConvPlan, ConvPlan, ConvPlan]] = None  # kind "mb": expand, depthwise, project plans
 
 
 def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
@@ -66,7 +67,7 @@ class Model:
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
                  in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
-                 fuse_tail: bool = True, input_u8: bool = False, device=None):
+                 fuse_tail: bool = True, fuse_blocks: bool = False, input_u8: bool = False, device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -141,6 +142,42 @@ class Model:
             tail_up[lat[1]] = rz[2]
             dropped_resize.add(rz[1])
             fused_resize.pop(rz[1], None)  # the head takes it instead of the conv's epilogue
+        # Inverted-bottleneck blocks on small frames (fuse_blocks): a 1x1
+        # expand, a depthwise 3x3 (stride 1, pad 1) and a 1x1 project whose
+        # intermediates feed nothing else, over frames up to 10 x 24, run as
+        # one launch (aie_conv_run_mbconv) when the 1x1 plans resolve to TF32.
+        block_of: Dict[str, tuple] = {}  # project output -> (expand op, depthwise op, project op, plans)
+        block_inner: set = set()        # expand / depthwise outputs recorded with their block
+        if fuse_blocks and math not in ("fp32_strict", "ffma"):
+            def is_pw(cv):
+                return cv.kh == 1 and cv.kw == 1 and cv.sh == 1 and cv.sw == 1 and cv.groups == 1 and \
+                    tuple(cv.pad) == (0, 0, 0, 0)
+            for op in self.graph:
+                if op[0] != "conv" or not is_pw(op[3]) or op[3].cout > 128:
+                    continue
+                dop = next((p for p in self.graph if p[1] == op[2]), None)
+                if dop is None or dop[0] != "conv" or dop[4] is not None or dop[1] in head_of:
+                    continue
+                dcv = dop[3]
+                if not (dcv.is_depthwise() and dcv.kh == 3 and dcv.kw == 3 and dcv.sh == 1 and dcv.sw == 1
+                        and dcv.dil == 1 and tuple(dcv.pad) == (1, 1, 1, 1)):
+                    continue
+                eop = next((p for p in self.graph if p[1] == dop[2]), None)
+                if eop is None or eop[0] != "conv" or eop[4] is not None or not is_pw(eop[3]):
+                    continue
+                if uses.get(eop[1], 0) != 1 or uses.get(dop[1], 0) != 1 or self.output in (eop[1], dop[1]):
+                    continue
+                h, w, c = self.shapes[eop[2]]
+                if h > 10 or w > 24 or c % 32:
+                    continue
+                ex = ConvPlan(eop[3], n, h, w, math=math, device=self.device).load_weights(*weights[eop[1]])
+                dw = ConvPlan(dcv, n, h, w, math=math, device=self.device).load_weights(*weights[dop[1]])
+                pj = ConvPlan(op[3], n, h, w, has_res=op[4] is not None, math=math,
+                              device=self.device).load_weights(*weights[op[1]])
+                if ex.math != "tf32" or pj.math != "tf32" or dw.kernel != "dw" or dw.math == "fp32_strict":
+                    continue
+                block_of[op[1]] = (eop, dop, op, (ex, dw, pj))
+                block_inner.update((eop[1], dop[1]))
         # input_u8: the batch arrives as u8 RGB frames ("input_u8", 3 bytes per
         # pixel); the first op normalises them into the f32 "input" (u8 / 255)
         self.input_u8 = input_u8
@@ -157,8 +194,14 @@ class Model:
                 h, w, c = self.shapes[src]
                 if kind == "resize" and (out in fused_resize or out in dropped_resize):
                     continue
-                if out in fused_heads:
-                    continue  # recorded with its depthwise producer
+                if out in fused_heads or out in block_inner:
+                    continue  # recorded with its depthwise producer / its block
+                if out in block_of:
+                    eop, dop, pop, plans = block_of[out]
+                    rec = OpRecord("mb", out, eop[2], conv=pop[3], res=pop[4], blk=plans)
+                    self.bufs[out] = torch.empty((n, *self.shapes[out]), dtype=torch.float32, device=self.device)
+                    self.ops.append(rec)
+                    continue
                 if out in head_of:
                     hop = head_of[out]
                     rec = OpRecord("dwpw", hop[1], src, conv=op[3], up=tail_up.get(src))
@@ -186,7 +229,13 @@ class Model:
 
     # -- accounting ------------------------------------------------------------
     def conv_flops(self) -> int:
-        return sum(r.plan.flops + (r.head.flops if r.head is not None else 0) for r in self.ops if r.plan is not None)
+        total = 0
+        for r in self.ops:
+            if r.blk is not None:
+                total += sum(p.flops for p in r.blk)
+            elif r.plan is not None:
+                total += r.plan.flops + (r.head.flops if r.head is not None else 0)
+        return total
 
     def layer_table(self):
         rows = []
@@ -205,6 +254,8 @@ class Model:
                 r.plan(src, self.bufs[r.res] if r.res else None, out=out, stream=stream)
             elif r.kind == "dwpw":
                 run_dw_pw(r.plan, r.head, src, out=out, stream=stream, up=self.bufs[r.up] if r.up else None)
+            elif r.kind == "mb":
+                run_mbconv(*r.blk, src, res=self.bufs[r.res] if r.res else None, out=out, stream=stream)
             elif r.kind == "u8in":
                 input_u8(src, out=out, stream=stream)
             else:

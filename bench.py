@@ -223,6 +223,8 @@ def main():
     ap.add_argument("--math", default="auto", choices=["auto", "ffma", "tf32", "fp32_strict"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fuse-blocks", type=int, default=None, choices=[0, 1],
+                    help="run each small-frame inverted-bottleneck block as one launch (default: Model's)")
     ap.add_argument("--fuse-resize", type=int, default=None, choices=[0, 1],
                     help="fold each resize that only feeds a conv residual into that conv (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
@@ -244,13 +246,15 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     from ai_engine_b200 import segnet
-    from ai_engine_b200.conv import resize_bilinear, run_dw_pw
+    from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv
     from ai_engine_b200.graph import Model
 
     n = args.batch
     g = segnet.build_graph()
     weights = segnet.init_weights(g)  # same weights on every rank (replicas)
     fuse_kw = {} if args.fuse_resize is None else {"fuse": bool(args.fuse_resize)}
+    if args.fuse_blocks is not None:
+        fuse_kw["fuse_blocks"] = bool(args.fuse_blocks)
     model = Model(g, weights, n, (H, W, 3), math=args.math, device=dev, **fuse_kw)
     x_host = torch.from_numpy(segnet.synthetic_input(n, seed=100 + rank)).pin_memory()
     model.bufs["input"].copy_(x_host)
@@ -307,6 +311,8 @@ def main():
                 r.plan(src, model.bufs[r.res] if r.res else None, out=out)
             elif r.kind == "dwpw":
                 run_dw_pw(r.plan, r.head, src, out=out, up=model.bufs[r.up] if r.up else None)
+            elif r.kind == "mb":
+                run_mbconv(*r.blk, src, res=model.bufs[r.res] if r.res else None, out=out)
             else:
                 resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
             ev[i + 1].record(stream)
@@ -377,7 +383,15 @@ def main():
     tf32_peak = pk["bf16_tflops"] / 2.0  # TF32 dense = half the bf16 rate
     layers = []
     for r, ms in zip(ops, per_op):
-        if r.kind == "dwpw":
+        if r.kind == "mb":
+            # fused block: the expanded tensor and the depthwise output are
+            # neither written nor read
+            ex, dw, pj = r.blk
+            inter = 4 * n * ex.oh * ex.ow * ex.op.cout
+            fl = ex.flops + dw.flops + pj.flops
+            by = ex.min_bytes + dw.min_bytes + pj.min_bytes - 4 * inter
+            kern, math = "ex+dw+pj", "tf32"
+        elif r.kind == "dwpw":
             # fused depthwise + 1x1 head: the intermediate is neither written nor read
             inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout
             fl, by = r.plan.flops + r.head.flops, r.plan.min_bytes + r.head.min_bytes - 2 * inter

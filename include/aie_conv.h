@@ -230,6 +230,23 @@ AIE_API int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, const
                            uint32_t up_h, uint32_t up_w, const void *dw_w, const void *dw_b, const void *pw_w,
                            const void *pw_b, void *out, void *stream);
 
+/* A whole inverted-bottleneck block in one launch: 1x1 expand `ex` ->
+ * depthwise 3x3 (stride 1, pad 1) `dw` -> 1x1 project `pj` (+ residual),
+ * the expanded tensor never reaching memory.  For small frames (h <= 10,
+ * w <= 24, e.g. the 10x18 stages of a 160x288 MobileNet): one CTA per
+ * frame, tcgen05 TF32 GEMMs with the pixels as the MMA's N side, the
+ * depthwise on the CUDA cores between them.  All three are ordinary
+ * aie_conv_plan results over dense NHWC tensors: `ex` and `pj` 1x1 plans
+ * that resolved to TF32 (cin % 32 == 0, pj cout <= 128), `dw` a non-strict
+ * depthwise plan; weights and biases as packed for each plan; `res` is the
+ * project plan's residual (NULL without one).  Otherwise AIE_E_UNSUPPORTED:
+ * run the three plans with aie_conv_run.  Replaces the three dispatches
+ * ai-gpu-runtime's lower_op makes for the block (GemmPwSpec, ConvDwSpec,
+ * GemmPwSpec; crates/ai-gpu-runtime/src/lowering.rs:99-187). */
+AIE_API int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const aie_plan *pj, const void *in,
+                        const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b, const void *pj_w,
+                        const void *pj_b, const void *res, void *out, void *stream);
+
 /* Input staging: a batch of interleaved u8 RGB (cin = 3) or RGBA (cin = 4,
  * alpha dropped) frames [n, h, w, cin] -> the network's f32 input
  * [n, h, w, 3] (layout NHWC) or [n, h, w, 4] (NHWC_C4, 4th lane 0), each
