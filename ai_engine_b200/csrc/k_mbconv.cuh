@@ -22,9 +22,10 @@
 //   1. the MMA warp accumulates E over cin (the producer streams the
 //      [240][32] input K-blocks with the matching [128][32] expand-weight
 //      K-blocks, two stages);
-//   2. four channel warps (thread = expanded channel; warp w reads TMEM
-//      lanes 32 (w % 4)..) load E a frame row at a time (three 8-column
-//      tcgen05.ld per row), add the expand bias and activation, run the 3x3
+//   2. eight channel warps (thread = expanded channel; warp w reads TMEM
+//      lanes 32 (w % 4).. and takes half the frame's rows) load E a frame
+//      row at a time (three 8-column tcgen05.ld per row), add the expand
+//      bias and activation, run the 3x3
 //      depthwise on a sliding three-row register window (zero padding at the
 //      frame's edges), add its bias and activation, and write D[p][channel]
 //      into shared memory as the project GEMM's K-major B operand (128-byte
@@ -54,7 +55,9 @@ constexpr int kMbStages = 2;
 constexpr uint32_t kMbDOff = kMbStages * kMbStage;  // D: 4 K-blocks of [240][32]
 constexpr uint32_t kMbBarOff = kMbDOff + 4 * kMbXBytes;
 constexpr uint32_t kMbSmem = kMbBarOff + 128 + 1024;  // + barriers + alignment slack
-constexpr int kMbThreads = 192;                     // MMA, producer, 4 channel warps
+constexpr int kMbChanWarps = 8;                    // two per TMEM lane quarter: frame rows 0-4 / 5-9
+constexpr int kMbHalfRows = kMbRows / 2;
+constexpr int kMbThreads = 32 * (2 + kMbChanWarps);  // MMA, producer, channel warps
 constexpr uint32_t kMbECol = 0, kMbPCol = 256;
 static_assert(kMbStage % 1024 == 0 && kMbXBytes % 1024 == 0, "operand tiles stay 1024-aligned");
 static_assert(kMbSmem <= 227 * 1024, "shared memory");
@@ -120,11 +123,11 @@ __global__ void __launch_bounds__(kMbThreads, 1)
             mbar_init(&sh.empty[s], 1);
         }
         mbar_init(&sh.e_full, 1);
-        mbar_init(&sh.e_empty, 4);
-        mbar_init(&sh.d_full, 4);
+        mbar_init(&sh.e_empty, kMbChanWarps);
+        mbar_init(&sh.d_full, kMbChanWarps);
         mbar_init(&sh.d_empty, 1);
         mbar_init(&sh.p_full, 1);
-        mbar_init(&sh.p_empty, 4);
+        mbar_init(&sh.p_empty, kMbChanWarps);
         mbar_init(&sh.drain, 1);
         sh.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -243,9 +246,16 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         }
     } else {
         // ------------------------------------------------------ channel warps
-        const int q = warp & 3;                                // TMEM lane quarter
+        // warp w reads TMEM lanes 32 (w % 4).. (one 32-channel K-block of D)
+        // and takes frame rows [5 hf, 5 hf + 5), hf = (w - 2) / 4
+        const int q = warp & 3;
+        const int y0 = ((warp - 2) >> 2) * kMbHalfRows;
         const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
-        uint8_t *dk = smem + kMbDOff + q * kMbXBytes;          // this warp's K-block of D
+        uint8_t *dk = smem + kMbDOff + q * kMbXBytes;  // this warp's K-block of D
+        // 128-byte swizzle: pixel p = 24 y + x has p % 8 == x % 8, so the
+        // 16-byte chunk of this lane's channel in row p depends on x only
+        const uint32_t lane_off = (uint32_t)((lane & 3) << 2);
+        const int lane_chunk = lane >> 2;
         uint32_t g = 0, j = 0;
         bool ok = true;
         for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x, j++) {
@@ -275,41 +285,46 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     for (int x = 0; x < kMbRowStride; x++)
                         if (x >= a.w) v[x] = 0.0f;
                 };
-                float r0[kMbRowStride], r1[kMbRowStride], r2[kMbRowStride];
+                float rw[3][kMbRowStride];  // rows y-1, y, y+1 of the window (renamed by the unrolled loop)
+                erow(y0 - 1, rw[0]);
+                erow(y0, rw[1]);
 #pragma unroll
-                for (int x = 0; x < kMbRowStride; x++) r0[x] = 0.0f;
-                erow(0, r1);
-#pragma unroll 1
-                for (int y = 0; y < kMbRows; y++) {
-                    erow(y + 1, r2);
-                    // taps in (ky, kx) order from the bias, as the depthwise kernels
-                    float o[kMbRowStride];
+                for (int i = 0; i < kMbHalfRows; i++) {
+                    const int y = y0 + i;
+                    float(&ra)[kMbRowStride] = rw[i % 3];
+                    float(&rb)[kMbRowStride] = rw[(i + 1) % 3];
+                    float(&rc)[kMbRowStride] = rw[(i + 2) % 3];
+                    erow(y + 1, rc);
+                    // taps in (ky, kx) order from the bias, as the depthwise kernels;
+                    // half a row at a time (register budget)
+                    uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
+                    const bool yv = y < a.h;
 #pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++) {
-                        float acc = bd;
+                    for (int xh = 0; xh < kMbRowStride; xh += kMbRowStride / 2) {
+                        float o[kMbRowStride / 2];
 #pragma unroll
-                        for (int dx = -1; dx <= 1; dx++)
-                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(r0[x + dx], wd[dx + 1], acc);
+                        for (int xi = 0; xi < kMbRowStride / 2; xi++) {
+                            const int x = xh + xi;
+                            float acc = bd;
 #pragma unroll
-                        for (int dx = -1; dx <= 1; dx++)
-                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(r1[x + dx], wd[3 + dx + 1], acc);
+                            for (int dx = -1; dx <= 1; dx++)
+                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(ra[x + dx], wd[dx + 1], acc);
 #pragma unroll
-                        for (int dx = -1; dx <= 1; dx++)
-                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(r2[x + dx], wd[6 + dx + 1], acc);
-                        o[x] = acc;
-                    }
-                    act_apply_n<kMbRowStride>(a.act_dw, o);
+                            for (int dx = -1; dx <= 1; dx++)
+                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rb[x + dx], wd[3 + dx + 1], acc);
 #pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++)
-                        if (y >= a.h || x >= a.w) o[x] = 0.0f;
-                    // D[p][lane], p = 24 y + x: K-major, 128-byte swizzle
+                            for (int dx = -1; dx <= 1; dx++)
+                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rc[x + dx], wd[6 + dx + 1], acc);
+                            o[xi] = acc;
+                        }
+                        act_apply_n<kMbRowStride / 2>(a.act_dw, o);
+                        // D[p][lane], p = 24 y + x: K-major, 128-byte swizzle
 #pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++)
-                        *reinterpret_cast<float *>(dk + sw128_off(y * kMbRowStride + x, lane)) = o[x];
-#pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++) {
-                        r0[x] = r1[x];
-                        r1[x] = r2[x];
+                        for (int xi = 0; xi < kMbRowStride / 2; xi++) {
+                            const int x = xh + xi;
+                            *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ (x & 7)) << 4)) =
+                                (yv && x < a.w) ? o[xi] : 0.0f;
+                        }
                     }
                 }
                 tc_fence_before();
@@ -321,27 +336,32 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                 }
             }
             if (!ok) break;
-            // ---- project epilogue of frame f: thread = output channel
+            // ---- project epilogue of frame f: thread = output channel, this warp's rows
             if (!__all_sync(0xffffffffu, mbar_wait_sleep(&sh.p_full, j & 1))) { ok = false; break; }
             tc_fence_after();
             const int o = q * 32 + lane;
             const bool ov = o < a.cout;
             const float bp = ov ? __ldg(a.b_proj + o) : 0.0f;
             const long long fbase = (long long)f * a.h * a.w;
-            for (int y = 0; y < a.h; y++) {
+#pragma unroll 1
+            for (int y = y0; y < min(y0 + kMbHalfRows, a.h); y++) {
+                const long long m0 = fbase + (long long)y * a.w;
                 float v[kMbRowStride];
                 tmem_row24(tlane + kMbPCol + y * kMbRowStride, v);
 #pragma unroll
                 for (int x = 0; x < kMbRowStride; x++) v[x] += bp;
                 act_apply_n<kMbRowStride>(a.act_proj, v);
-                if (ov) {
+                // residual after the activation; a half row of loads in flight at once
 #pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++) {
-                        if (x >= a.w) break;
-                        const long long m = fbase + (long long)y * a.w + x;
-                        float t = v[x];
-                        if (a.res) t = t + __ldg(a.res + m * a.cout + o);  // residual after the activation
-                        a.y[m * a.cout + o] = t;
+                for (int xh = 0; xh < kMbRowStride; xh += kMbRowStride / 2) {
+                    float r[kMbRowStride / 2];
+#pragma unroll
+                    for (int xi = 0; xi < kMbRowStride / 2; xi++)
+                        r[xi] = (a.res && ov && xh + xi < a.w) ? __ldg(a.res + (m0 + xh + xi) * a.cout + o) : 0.0f;
+                    if (ov) {
+#pragma unroll
+                        for (int xi = 0; xi < kMbRowStride / 2; xi++)
+                            if (xh + xi < a.w) a.y[(m0 + xh + xi) * a.cout + o] = v[xh + xi] + r[xi];
                     }
                 }
             }
