@@ -218,7 +218,7 @@ def run_mbconv(ex: "ConvPlan", dw: "ConvPlan", pj: "ConvPlan", x: torch.Tensor, 
                out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """An inverted-bottleneck block -- 1x1 expand `ex`, depthwise 3x3 `dw`,
     1x1 project `pj` (+ `res`) -- in one launch (aie_conv_run_mbconv) for
-    frames up to 10 x 24: the expanded tensor never reaches memory.  Raises
+    frames up to 10 x 18: the expanded tensor never reaches memory.  Raises
     AieError(AIE_E_UNSUPPORTED) for blocks the fused kernel does not cover."""
     for p in (ex, dw, pj):
         if p.w is None:

@@ -6,32 +6,31 @@
 // writing and re-reading the expanded tensor twice.
 //
 // Both GEMMs are transposed so that the frame's pixels are the MMA's N side
-// (N = 240: up to 10 rows at a stride of 24 pixels, up to 24 wide) and the
-// channels its M side (M = 128):
+// (N = 192: up to 10 rows of up to 18 pixels, row-major, then 12 zero rows)
+// and the channels its M side (M = 128):
 //   E^T[c, p] = W_exp[c, :] . X[p, :]       (c: a 128-channel chunk of the
 //                                            expanded dimension)
 //   P^T[o, p] += W_proj[o, chunk] . D[p, chunk]
-// so one tcgen05.mma covers 128 x 240 x 8 instead of 128 pixels x a narrow
+// so one tcgen05.mma covers 128 x 192 x 8 instead of 128 pixels x a narrow
 // N: a chunk costs cin / 8 expand MMAs and 16 project MMAs per frame.
-// The input frame arrives by TMA as [10 rows][24 px][32 ch] boxes (128-byte
+// The input frame arrives by TMA as [10 rows][18 px][32 ch] boxes (128-byte
 // swizzle): columns and rows past the frame read as zeros, so pixel
-// p = 24 y + x of the B operand is image pixel (y, x).
+// p = 18 y + x of the B operand is image pixel (y, x).
 //
-// Per chunk of 128 expanded channels (TMEM: E at columns [0, 240), P at
-// [256, 496)):
-//   1. the MMA warp accumulates E over cin (the producer streams the
-//      [240][32] input K-blocks with the matching [128][32] expand-weight
-//      K-blocks, two stages);
+// Per chunk of 128 expanded channels (TMEM: E at columns [0, 192), P at
+// [256, 448)):
+//   1. the MMA warp accumulates E over cin from an input ring (two [192][32]
+//      K-blocks) and a weight ring (four [128][32] K-blocks);
 //   2. eight channel warps (thread = expanded channel; warp w reads TMEM
 //      lanes 32 (w % 4).. and takes half the frame's rows) load E a frame
-//      row at a time (three 8-column tcgen05.ld per row), add the expand
-//      bias and activation, run the 3x3
-//      depthwise on a sliding three-row register window (zero padding at the
-//      frame's edges), add its bias and activation, and write D[p][channel]
-//      into shared memory as the project GEMM's K-major B operand (128-byte
-//      swizzle, one 32-channel K-block per warp);
-//   3. the MMA warp accumulates P over the chunk's four K-blocks (the
-//      producer streams the [128 out][32] project-weight K-blocks).
+//      row at a time (2-column tcgen05.ld), add the expand bias and
+//      activation, run the 3x3 depthwise on a sliding three-row register
+//      window (zero padding at the frame's edges), add its bias and
+//      activation, and write D[p][channel] into shared memory as the project
+//      GEMM's K-major B operand (128-byte swizzle, one 32-channel K-block per
+//      lane quarter);
+//   3. the MMA warp accumulates P over the chunk's four K-blocks; their
+//      weights were loaded into the weight ring while the depthwise ran.
 // After the last chunk the channel warps add the project bias, activation
 // and residual and store the frame (thread = output channel: 32 lanes write
 // one pixel's 128 contiguous bytes).
@@ -44,22 +43,25 @@
 
 namespace aie {
 
-constexpr int kMbRowStride = 24;                   // pixels per frame row in the N layout
-constexpr int kMbRows = 10;                        // frame rows in the N layout
-constexpr int kMbN = kMbRowStride * kMbRows;       // 240
+constexpr int kMbRowStride = 18;                   // pixels per frame row in the N layout (frame width <= 18)
+constexpr int kMbRows = 10;                        // frame rows (frame height <= 10)
+constexpr int kMbPix = kMbRowStride * kMbRows;     // 180
+constexpr int kMbN = 192;                          // MMA N: the frame's pixels + 12 zero rows
 constexpr int kMbChunk = 128;                      // expanded channels per chunk (MMA M)
-constexpr uint32_t kMbXBytes = kMbN * 128;         // one [240][32] input K-block: 30 KB
+constexpr uint32_t kMbXBytes = kMbN * 128;         // one [192][32] operand K-block: 24 KB
+constexpr uint32_t kMbXBox = kMbPix * 128;         // the bytes a [10][18][32] TMA box writes
 constexpr uint32_t kMbWBytes = kMbChunk * 128;     // one [128][32] weight K-block: 16 KB
-constexpr uint32_t kMbStage = kMbXBytes + kMbWBytes;
-constexpr int kMbStages = 2;
-constexpr uint32_t kMbDOff = kMbStages * kMbStage;  // D: 4 K-blocks of [240][32]
+constexpr int kMbXStages = 2, kMbWStages = 4;
+constexpr uint32_t kMbWOff = kMbXStages * kMbXBytes;
+constexpr uint32_t kMbDOff = kMbWOff + kMbWStages * kMbWBytes;  // D: 4 K-blocks of [192][32]
 constexpr uint32_t kMbBarOff = kMbDOff + 4 * kMbXBytes;
-constexpr uint32_t kMbSmem = kMbBarOff + 128 + 1024;  // + barriers + alignment slack
-constexpr int kMbChanWarps = 8;                    // two per TMEM lane quarter: frame rows 0-4 / 5-9
+constexpr uint32_t kMbSmem = kMbBarOff + 256 + 1024;  // + barriers + alignment slack
+constexpr int kMbChanWarps = 8;                     // two per TMEM lane quarter: frame rows 0-4 / 5-9
 constexpr int kMbHalfRows = kMbRows / 2;
 constexpr int kMbThreads = 32 * (2 + kMbChanWarps);  // MMA, producer, channel warps
 constexpr uint32_t kMbECol = 0, kMbPCol = 256;
-static_assert(kMbStage % 1024 == 0 && kMbXBytes % 1024 == 0, "operand tiles stay 1024-aligned");
+static_assert(kMbXBytes % 1024 == 0 && kMbWBytes % 1024 == 0 && kMbWOff % 1024 == 0 && kMbDOff % 1024 == 0,
+              "operand tiles stay 1024-aligned");
 static_assert(kMbSmem <= 227 * 1024, "shared memory");
 
 struct MbArgs {
@@ -75,31 +77,28 @@ struct MbArgs {
 };
 
 struct MbShared {
-    uint64_t full[kMbStages], empty[kMbStages];
+    uint64_t xfull[kMbXStages], xempty[kMbXStages], wfull[kMbWStages], wempty[kMbWStages];
     uint64_t e_full, e_empty, d_full, d_empty, p_full, p_empty, drain;
     uint32_t tmem_base;
     uint32_t abort;
 };
+static_assert(sizeof(MbShared) <= 256, "barrier block");
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8])
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t &r0, uint32_t &r1)
 {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(taddr));
 }
 
-// loads one frame row (24 columns) of this thread's TMEM lane
-__device__ __forceinline__ void tmem_row24(uint32_t taddr, float (&v)[kMbRowStride])
+// one frame row (18 columns) of this thread's TMEM lane
+__device__ __forceinline__ void tmem_row18(uint32_t taddr, float (&v)[kMbRowStride])
 {
-    uint32_t r[24];
-    tmem_ld8(taddr, *reinterpret_cast<uint32_t(*)[8]>(r));
-    tmem_ld8(taddr + 8, *reinterpret_cast<uint32_t(*)[8]>(r + 8));
-    tmem_ld8(taddr + 16, *reinterpret_cast<uint32_t(*)[8]>(r + 16));
+    uint32_t r[kMbRowStride];
+#pragma unroll
+    for (int k = 0; k < kMbRowStride / 2; k++) tmem_ld2(taddr + 2 * k, r[2 * k], r[2 * k + 1]);
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
                    "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
-                   "+r"(r[22]), "+r"(r[23])
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17])
                  :
                  : "memory");
 #pragma unroll
@@ -118,9 +117,13 @@ __global__ void __launch_bounds__(kMbThreads, 1)
     const int kx = a.cin / 32;  // expand K-blocks (cin % 32 == 0, checked on the host)
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kMbStages; s++) {
-            mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], 1);
+        for (int s = 0; s < kMbXStages; s++) {
+            mbar_init(&sh.xfull[s], 1);
+            mbar_init(&sh.xempty[s], 1);
+        }
+        for (int s = 0; s < kMbWStages; s++) {
+            mbar_init(&sh.wfull[s], 1);
+            mbar_init(&sh.wempty[s], 1);
         }
         mbar_init(&sh.e_full, 1);
         mbar_init(&sh.e_empty, kMbChanWarps);
@@ -137,6 +140,15 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmWe)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmWp)) : "memory");
     }
+    // the operand rows past the frame's 180 pixels stay zero: the TMA boxes
+    // and the depthwise never write them
+    constexpr int kPadFloats = (kMbN - kMbPix) * 32;
+    for (int i = threadIdx.x; i < (kMbXStages + 4) * kPadFloats; i += kMbThreads) {
+        const int blk = i / kPadFloats, e = i - blk * kPadFloats;
+        const uint32_t base = blk < kMbXStages ? blk * kMbXBytes : kMbDOff + (blk - kMbXStages) * kMbXBytes;
+        reinterpret_cast<float *>(smem + base + kMbXBox)[e] = 0.0f;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // seen by the MMA (async proxy)
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&sh.tmem_base)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -150,28 +162,35 @@ __global__ void __launch_bounds__(kMbThreads, 1)
     if (warp == 1) {
         // ------------------------------------------------------ producer
         if (lane == 0) {
-            uint32_t it = 0;  // stages filled so far
-            auto take = [&](uint32_t bytes, uint32_t &s) {
-                s = it % kMbStages;
-                if (!mbar_wait(&sh.empty[s], ((it / kMbStages) & 1) ^ 1)) return false;
-                it++;
-                mbar_expect_tx(&sh.full[s], bytes);
+            uint32_t xi = 0, wi = 0;  // input / weight stages filled so far
+            auto take_x = [&](uint32_t &s) {
+                s = xi % kMbXStages;
+                if (!mbar_wait(&sh.xempty[s], ((xi / kMbXStages) & 1) ^ 1)) return false;
+                xi++;
+                mbar_expect_tx(&sh.xfull[s], kMbXBox);
+                return true;
+            };
+            auto take_w = [&](uint32_t &s) {
+                s = wi % kMbWStages;
+                if (!mbar_wait(&sh.wempty[s], ((wi / kMbWStages) & 1) ^ 1)) return false;
+                wi++;
+                mbar_expect_tx(&sh.wfull[s], kMbWBytes);
                 return true;
             };
             bool ok = true;
             for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x) {
                 for (int ch = 0; ok && ch < nchunks; ch++) {
-                    for (int kb = 0; ok && kb < kx; kb++) {
-                        uint32_t s;
-                        if (*abort_flag || !take(kMbStage, s)) { ok = false; break; }
-                        uint8_t *st = smem + s * kMbStage;
-                        tma_load_4d(st, &tmX, &sh.full[s], kb * 32, 0, 0, f);
-                        tma_load_2d(st + kMbXBytes, &tmWe, &sh.full[s], kb * 32, ch * kMbChunk);
+                    for (int kb = 0; kb < kx; kb++) {
+                        uint32_t s, t;
+                        if (*abort_flag || !take_x(s)) { ok = false; break; }
+                        tma_load_4d(smem + s * kMbXBytes, &tmX, &sh.xfull[s], kb * 32, 0, 0, f);
+                        if (!take_w(t)) { ok = false; break; }
+                        tma_load_2d(smem + kMbWOff + t * kMbWBytes, &tmWe, &sh.wfull[t], kb * 32, ch * kMbChunk);
                     }
                     for (int kb = 0; ok && kb < 4; kb++) {
-                        uint32_t s;
-                        if (*abort_flag || !take(kMbWBytes, s)) { ok = false; break; }
-                        tma_load_2d(smem + s * kMbStage + kMbXBytes, &tmWp, &sh.full[s], ch * kMbChunk + kb * 32, 0);
+                        uint32_t t;
+                        if (*abort_flag || !take_w(t)) { ok = false; break; }
+                        tma_load_2d(smem + kMbWOff + t * kMbWBytes, &tmWp, &sh.wfull[t], ch * kMbChunk + kb * 32, 0);
                     }
                 }
             }
@@ -179,23 +198,31 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                 report_error(0x06000001u);
                 *abort_flag = 1;
             }
-            // no copy may land after exit: wait (bounded) for the last stages'
-            // copies themselves (a stage is refilled only after its previous
-            // copies were consumed, so earlier ones have landed)
-            for (uint32_t j = it >= kMbStages ? it - kMbStages : 0; j < it; j++)
-                mbar_wait(&sh.full[j % kMbStages], (j / kMbStages) & 1);
+            // no copy may land after exit: wait (bounded) for the last copies
+            // of each ring (a slot is refilled only after its previous copy
+            // was consumed, so earlier ones have landed)
+            for (uint32_t j = xi >= kMbXStages ? xi - kMbXStages : 0; j < xi; j++)
+                mbar_wait(&sh.xfull[j % kMbXStages], (j / kMbXStages) & 1);
+            for (uint32_t j = wi >= kMbWStages ? wi - kMbWStages : 0; j < wi; j++)
+                mbar_wait(&sh.wfull[j % kMbWStages], (j / kMbWStages) & 1);
         }
     } else if (warp == 0) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32(128, kMbN);
-            uint32_t it = 0, g = 0, j = 0;  // stages consumed, chunks, frames
+            uint32_t xi = 0, wi = 0, g = 0, j = 0;  // stages consumed, chunks, frames
             bool ok = true;
-            auto stage = [&](uint32_t &s) {
-                s = it % kMbStages;
-                const uint32_t ph = (it / kMbStages) & 1;
-                it++;
-                return mbar_wait(&sh.full[s], ph);
+            auto xstage = [&](uint32_t &s) {
+                s = xi % kMbXStages;
+                const uint32_t ph = (xi / kMbXStages) & 1;
+                xi++;
+                return mbar_wait(&sh.xfull[s], ph);
+            };
+            auto wstage = [&](uint32_t &s) {
+                s = wi % kMbWStages;
+                const uint32_t ph = (wi / kMbWStages) & 1;
+                wi++;
+                return mbar_wait(&sh.wfull[s], ph);
             };
             for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x, j++) {
                 for (int ch = 0; ok && ch < nchunks; ch++, g++) {
@@ -203,15 +230,17 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     if (g > 0 && !mbar_wait(&sh.e_empty, (g - 1) & 1)) { ok = false; break; }
                     tc_fence_after();
                     for (int kb = 0; kb < kx; kb++) {
-                        uint32_t s;
-                        if (*abort_flag || !stage(s)) { ok = false; break; }
+                        uint32_t s, t;
+                        if (*abort_flag || !xstage(s) || !wstage(t)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t sx = smem_u32(smem + s * kMbStage), sw = sx + kMbXBytes;
+                        const uint32_t sx = smem_u32(smem + s * kMbXBytes);
+                        const uint32_t sw = smem_u32(smem + kMbWOff + t * kMbWBytes);
 #pragma unroll
                         for (int k = 0; k < 4; k++)
                             mma_tf32(tmem + kMbECol, smem_desc_sw128(sw) + 2 * k, smem_desc_sw128(sx) + 2 * k, idesc,
                                      (kb > 0 || k > 0) ? 1u : 0u);
-                        mma_commit(&sh.empty[s]);
+                        mma_commit(&sh.xempty[s]);
+                        mma_commit(&sh.wempty[t]);
                     }
                     if (!ok) break;
                     mma_commit(&sh.e_full);
@@ -220,16 +249,16 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     if (ch == 0 && j > 0 && !mbar_wait(&sh.p_empty, (j - 1) & 1)) { ok = false; break; }
                     tc_fence_after();
                     for (int kb = 0; kb < 4; kb++) {
-                        uint32_t s;
-                        if (*abort_flag || !stage(s)) { ok = false; break; }
+                        uint32_t t;
+                        if (*abort_flag || !wstage(t)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t sw = smem_u32(smem + s * kMbStage) + kMbXBytes;
+                        const uint32_t sw = smem_u32(smem + kMbWOff + t * kMbWBytes);
                         const uint32_t sd = smem_u32(smem + kMbDOff + kb * kMbXBytes);
 #pragma unroll
                         for (int k = 0; k < 4; k++)
                             mma_tf32(tmem + kMbPCol, smem_desc_sw128(sw) + 2 * k, smem_desc_sw128(sd) + 2 * k, idesc,
                                      (ch > 0 || kb > 0 || k > 0) ? 1u : 0u);
-                        mma_commit(&sh.empty[s]);
+                        mma_commit(&sh.wempty[t]);
                     }
                     if (!ok) break;
                     mma_commit(&sh.d_empty);
@@ -252,8 +281,8 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         const int y0 = ((warp - 2) >> 2) * kMbHalfRows;
         const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
         uint8_t *dk = smem + kMbDOff + q * kMbXBytes;  // this warp's K-block of D
-        // 128-byte swizzle: pixel p = 24 y + x has p % 8 == x % 8, so the
-        // 16-byte chunk of this lane's channel in row p depends on x only
+        // 128-byte swizzle: the 16-byte chunk of this lane's channel in row p
+        // is (lane / 4) ^ (p % 8); p = 18 y + x, so p % 8 = (2 y + x) % 8
         const uint32_t lane_off = (uint32_t)((lane & 3) << 2);
         const int lane_chunk = lane >> 2;
         uint32_t g = 0, j = 0;
@@ -277,7 +306,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                         for (int x = 0; x < kMbRowStride; x++) v[x] = 0.0f;
                         return;
                     }
-                    tmem_row24(tlane + kMbECol + r * kMbRowStride, v);
+                    tmem_row18(tlane + kMbECol + r * kMbRowStride, v);
 #pragma unroll
                     for (int x = 0; x < kMbRowStride; x++) v[x] += be;
                     act_apply_n<kMbRowStride>(a.act_exp, v);
@@ -295,37 +324,31 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     float(&rb)[kMbRowStride] = rw[(i + 1) % 3];
                     float(&rc)[kMbRowStride] = rw[(i + 2) % 3];
                     erow(y + 1, rc);
-                    // taps in (ky, kx) order from the bias, as the depthwise kernels;
-                    // half a row at a time (register budget)
+                    // taps in (ky, kx) order from the bias, as the depthwise kernels
+                    float o[kMbRowStride];
+#pragma unroll
+                    for (int x = 0; x < kMbRowStride; x++) {
+                        float acc = bd;
+#pragma unroll
+                        for (int dx = -1; dx <= 1; dx++)
+                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(ra[x + dx], wd[dx + 1], acc);
+#pragma unroll
+                        for (int dx = -1; dx <= 1; dx++)
+                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rb[x + dx], wd[3 + dx + 1], acc);
+#pragma unroll
+                        for (int dx = -1; dx <= 1; dx++)
+                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rc[x + dx], wd[6 + dx + 1], acc);
+                        o[x] = acc;
+                    }
+                    act_apply_n<kMbRowStride>(a.act_dw, o);
+                    // D[p][lane], p = 18 y + x: K-major, 128-byte swizzle
                     uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
                     const bool yv = y < a.h;
+                    const int ysw = 2 * y;
 #pragma unroll
-                    for (int xh = 0; xh < kMbRowStride; xh += kMbRowStride / 2) {
-                        float o[kMbRowStride / 2];
-#pragma unroll
-                        for (int xi = 0; xi < kMbRowStride / 2; xi++) {
-                            const int x = xh + xi;
-                            float acc = bd;
-#pragma unroll
-                            for (int dx = -1; dx <= 1; dx++)
-                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(ra[x + dx], wd[dx + 1], acc);
-#pragma unroll
-                            for (int dx = -1; dx <= 1; dx++)
-                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rb[x + dx], wd[3 + dx + 1], acc);
-#pragma unroll
-                            for (int dx = -1; dx <= 1; dx++)
-                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rc[x + dx], wd[6 + dx + 1], acc);
-                            o[xi] = acc;
-                        }
-                        act_apply_n<kMbRowStride / 2>(a.act_dw, o);
-                        // D[p][lane], p = 24 y + x: K-major, 128-byte swizzle
-#pragma unroll
-                        for (int xi = 0; xi < kMbRowStride / 2; xi++) {
-                            const int x = xh + xi;
-                            *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ (x & 7)) << 4)) =
-                                (yv && x < a.w) ? o[xi] : 0.0f;
-                        }
-                    }
+                    for (int x = 0; x < kMbRowStride; x++)
+                        *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ ((ysw + x) & 7)) << 4)) =
+                            (yv && x < a.w) ? o[x] : 0.0f;
                 }
                 tc_fence_before();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
@@ -346,23 +369,20 @@ __global__ void __launch_bounds__(kMbThreads, 1)
 #pragma unroll 1
             for (int y = y0; y < min(y0 + kMbHalfRows, a.h); y++) {
                 const long long m0 = fbase + (long long)y * a.w;
+                float r[kMbRowStride];
+                // the residual row first: its loads overlap the TMEM read
+#pragma unroll
+                for (int x = 0; x < kMbRowStride; x++)
+                    r[x] = (a.res && ov && x < a.w) ? __ldg(a.res + (m0 + x) * a.cout + o) : 0.0f;
                 float v[kMbRowStride];
-                tmem_row24(tlane + kMbPCol + y * kMbRowStride, v);
+                tmem_row18(tlane + kMbPCol + y * kMbRowStride, v);
 #pragma unroll
                 for (int x = 0; x < kMbRowStride; x++) v[x] += bp;
                 act_apply_n<kMbRowStride>(a.act_proj, v);
-                // residual after the activation; a half row of loads in flight at once
+                if (ov) {
 #pragma unroll
-                for (int xh = 0; xh < kMbRowStride; xh += kMbRowStride / 2) {
-                    float r[kMbRowStride / 2];
-#pragma unroll
-                    for (int xi = 0; xi < kMbRowStride / 2; xi++)
-                        r[xi] = (a.res && ov && xh + xi < a.w) ? __ldg(a.res + (m0 + xh + xi) * a.cout + o) : 0.0f;
-                    if (ov) {
-#pragma unroll
-                        for (int xi = 0; xi < kMbRowStride / 2; xi++)
-                            if (xh + xi < a.w) a.y[(m0 + xh + xi) * a.cout + o] = v[xh + xi] + r[xi];
-                    }
+                    for (int x = 0; x < kMbRowStride; x++)
+                        if (x < a.w) a.y[(m0 + x) * a.cout + o] = v[x] + r[x];  // residual after the activation
                 }
             }
             tc_fence_before();

@@ -67,7 +67,7 @@ class Model:
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
                  in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
-                 fuse_tail: bool = True, fuse_blocks: bool = False, input_u8: bool = False, device=None):
+                 fuse_tail: bool = True, fuse_blocks: bool = True, input_u8: bool = False, device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -144,7 +144,7 @@ class Model:
             fused_resize.pop(rz[1], None)  # the head takes it instead of the conv's epilogue
         # Inverted-bottleneck blocks on small frames (fuse_blocks): a 1x1
         # expand, a depthwise 3x3 (stride 1, pad 1) and a 1x1 project whose
-        # intermediates feed nothing else, over frames up to 10 x 24, run as
+        # intermediates feed nothing else, over frames up to 10 x 18, run as
         # one launch (aie_conv_run_mbconv) when the 1x1 plans resolve to TF32.
         block_of: Dict[str, tuple] = {}  # project output -> (expand op, depthwise op, project op, plans)
         block_inner: set = set()        # expand / depthwise outputs recorded with their block
@@ -168,7 +168,7 @@ class Model:
                 if uses.get(eop[1], 0) != 1 or uses.get(dop[1], 0) != 1 or self.output in (eop[1], dop[1]):
                     continue
                 h, w, c = self.shapes[eop[2]]
-                if h > 10 or w > 24 or c % 32:
+                if h > 10 or w > 18 or c % 32:
                     continue
                 ex = ConvPlan(eop[3], n, h, w, math=math, device=self.device).load_weights(*weights[eop[1]])
                 dw = ConvPlan(dcv, n, h, w, math=math, device=self.device).load_weights(*weights[dop[1]])

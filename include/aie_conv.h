@@ -233,7 +233,7 @@ AIE_API int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, const
 /* A whole inverted-bottleneck block in one launch: 1x1 expand `ex` ->
  * depthwise 3x3 (stride 1, pad 1) `dw` -> 1x1 project `pj` (+ residual),
  * the expanded tensor never reaching memory.  For small frames (h <= 10,
- * w <= 24, e.g. the 10x18 stages of a 160x288 MobileNet): one CTA per
+ * w <= 18, e.g. the 10x18 stages of a 160x288 MobileNet): one CTA per
  * frame, tcgen05 TF32 GEMMs with the pixels as the MMA's N side, the
  * depthwise on the CUDA cores between them.  All three are ordinary
  * aie_conv_plan results over dense NHWC tensors: `ex` and `pj` 1x1 plans

@@ -21,7 +21,8 @@ BLOCKS = [
     (2, 10, 18, 128, 512, 128, True, ("relu", "relu", "none")),    # e5.0 / e5.1
     (2, 10, 18, 96, 384, 128, False, ("relu", "relu", "none")),    # e5
     (5, 7, 11, 64, 160, 64, True, ("hardswish", "hardswish", "none")),
-    (1, 10, 24, 32, 128, 32, False, ("relu6", "relu", "sigmoid")),  # the widest frame
+    (1, 10, 18, 32, 128, 32, False, ("relu6", "relu", "sigmoid")),  # the largest frame
+    (4, 3, 5, 32, 256, 32, True, ("relu", "none", "relu")),        # a frame smaller than every tile
     (149, 10, 18, 32, 128, 32, True, ("relu", "relu", "none")),    # more frames than SMs
 ]
 
@@ -58,7 +59,7 @@ def test_fused_block_matches_chain(cuda_ok, n, h, w, cin, cexp, cout, res, acts)
 
 
 def test_fused_block_rejects_unsupported(cuda_ok):
-    """Frames above 10 x 24, cin not a multiple of 32, an FP32_STRICT
+    """Frames above 10 x 18, cin not a multiple of 32, an FP32_STRICT
     depthwise plan and a missing residual are refused, not run."""
     def plans(n, h, w, cin, cexp, cout, dw_math="ffma", res=False):
         ex = ConvPlan(Conv2d.pointwise(cin, cexp, "relu"), n, h, w, math="tf32")
@@ -68,7 +69,7 @@ def test_fused_block_rejects_unsupported(cuda_ok):
         dw.load_weights(np.zeros(cexp * 9, np.float32), np.zeros(cexp, np.float32))
         pj.load_weights(np.zeros(cout * cexp, np.float32), np.zeros(cout, np.float32))
         return ex, dw, pj
-    for args, kw in [((1, 11, 18, 32, 64, 32), {}), ((1, 10, 25, 32, 64, 32), {}), ((1, 10, 18, 48, 96, 32), {}),
+    for args, kw in [((1, 11, 18, 32, 64, 32), {}), ((1, 10, 19, 32, 64, 32), {}), ((1, 10, 18, 48, 96, 32), {}),
                      ((1, 10, 18, 32, 64, 32), {"dw_math": "fp32_strict"})]:
         ex, dw, pj = plans(*args, **kw)
         x = torch.zeros(1, args[1], args[2], args[3], device="cuda")
