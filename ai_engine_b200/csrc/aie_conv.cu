@@ -840,9 +840,13 @@ extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const
     a.cin = (int)e.cin; a.cexp = (int)e.cout; a.cout = (int)q.cout; a.cexp_pad4 = (int)rup(e.cout, 4);
     a.act_exp = e.act; a.act_dw = d.act; a.act_proj = q.act;
     cudaStream_t s = (cudaStream_t)stream;
-    CUDA_TRY(ensure_smem_attr((const void *)mbconv_kernel, (int)kMbSmem));
+    // compile-time activations for the usual ReLU / ReLU6 blocks
+    auto kern = (e.act == AIE_ACT_RELU && d.act == AIE_ACT_RELU)      ? mbconv_kernel<kRelu, kRelu>
+                : (e.act == AIE_ACT_RELU6 && d.act == AIE_ACT_RELU6) ? mbconv_kernel<kRelu6, kRelu6>
+                                                                     : mbconv_kernel<-1, -1>;
+    CUDA_TRY(ensure_smem_attr((const void *)kern, (int)kMbSmem));
     const unsigned grid = (unsigned)std::min<long long>(e.n, tc_sm_count());
-    mbconv_kernel<<<grid, kMbThreads, kMbSmem, s>>>(tmX, tmWe, tmWp, a);
+    kern<<<grid, kMbThreads, kMbSmem, s>>>(tmX, tmWe, tmWp, a);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "fused block launch");
     return AIE_OK;
