@@ -86,6 +86,25 @@ __device__ __forceinline__ void act_apply_n(int act, float (&v)[N])
     }
 }
 
+// Activation with a compile-time kind where a kernel is instantiated for it
+// (ACT >= 0: kNone, kRelu or kRelu6), else act_apply_n's runtime switch
+// (ACT < 0).  In unrolled code the switch inlines every kind at each call:
+// enough code to miss the instruction cache.
+template <int ACT, int N>
+__device__ __forceinline__ void act_fixed_n(int act, float (&v)[N])
+{
+    if constexpr (ACT == kNone) {
+    } else if constexpr (ACT == kRelu) {
+#pragma unroll
+        for (int i = 0; i < N; i++) v[i] = fmaxf(v[i], 0.0f);
+    } else if constexpr (ACT == kRelu6) {
+#pragma unroll
+        for (int i = 0; i < N; i++) v[i] = fminf(fmaxf(v[i], 0.0f), 6.0f);
+    } else {
+        act_apply_n<N>(act, v);
+    }
+}
+
 // The same activation with ai-cpu's rounding: channels below 4*floor(c/4)
 // take apply4's form (multiply by the f32 constant 1/6, unfused), the tail
 // takes Activation::apply's form (divide by 6)

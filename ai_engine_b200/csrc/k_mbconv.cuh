@@ -105,25 +105,6 @@ __device__ __forceinline__ void tmem_row18(uint32_t taddr, float (&v)[kMbRowStri
     for (int i = 0; i < kMbRowStride; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Activation with a compile-time kind where the block uses ReLU or ReLU6
-// (ACT >= 0): the channel warps' unrolled row loop inlines it about a dozen
-// times per chunk, and the runtime switch (ACT < 0) inlines every kind each
-// time -- enough code to miss the instruction cache.
-template <int ACT, int N>
-__device__ __forceinline__ void mb_act(int act, float (&v)[N])
-{
-    if constexpr (ACT == kNone) {
-    } else if constexpr (ACT == kRelu) {
-#pragma unroll
-        for (int i = 0; i < N; i++) v[i] = fmaxf(v[i], 0.0f);
-    } else if constexpr (ACT == kRelu6) {
-#pragma unroll
-        for (int i = 0; i < N; i++) v[i] = fminf(fmaxf(v[i], 0.0f), 6.0f);
-    } else {
-        act_apply_n<N>(act, v);
-    }
-}
-
 // AE, AD: the expand and depthwise activations (kRelu / kRelu6 / kNone, or
 // -1 for any kind at run time)
 template <int AE, int AD>
@@ -331,7 +312,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     tmem_row18(tlane + kMbECol + r * kMbRowStride, v);
 #pragma unroll
                     for (int x = 0; x < kMbRowStride; x++) v[x] += be;
-                    mb_act<AE, kMbRowStride>(a.act_exp, v);
+                    act_fixed_n<AE, kMbRowStride>(a.act_exp, v);
 #pragma unroll
                     for (int x = 0; x < kMbRowStride; x++)
                         if (x >= a.w) v[x] = 0.0f;
@@ -362,7 +343,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                             if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rc[x + dx], wd[6 + dx + 1], acc);
                         o[x] = acc;
                     }
-                    mb_act<AD, kMbRowStride>(a.act_dw, o);
+                    act_fixed_n<AD, kMbRowStride>(a.act_dw, o);
                     // D[p][lane], p = 18 y + x: K-major, 128-byte swizzle
                     uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
                     const bool yv = y < a.h;

@@ -325,8 +325,10 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
 
 // RES (the epilogue's residual source, one kernel per kind so that each
 // layer's epilogue carries only its own code): 0 none, 1 residual tensor,
-// 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches
-template <int RES>
+// 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches.
+// ACT: the activation when it is kNone or kRelu, else -1 (any kind, chosen
+// at run time)
+template <int RES, int ACT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
 {
@@ -643,7 +645,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     v[4 * q4] += b.x; v[4 * q4 + 1] += b.y; v[4 * q4 + 2] += b.z; v[4 * q4 + 3] += b.w;
                 }
             }
-            act_apply_n<32>(c.act, v);
+            act_fixed_n<ACT, 32>(c.act, v);
             __syncwarp();  // previous chunk's readers are done with the buffer
             uint8_t *st = obuf + lane * 128;
 #pragma unroll
@@ -1089,8 +1091,15 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         }
     }
     const int kind = !c.res ? 0 : !c.res_mode ? 1 : a.res_patch ? 3 : 2;
-    auto kern = kind == 0 ? tc_conv_kernel<0> : kind == 1 ? tc_conv_kernel<1> : kind == 2 ? tc_conv_kernel<2>
-                                                                                         : tc_conv_kernel<3>;
+    // the activation as a template argument where it is none or ReLU (one
+    // inlined switch over every kind per chunk costs instruction-cache misses)
+    using Kern = void (*)(CUtensorMap, CUtensorMap, TcArgs);
+    static const Kern kerns[4][3] = {
+        {tc_conv_kernel<0, kNone>, tc_conv_kernel<0, kRelu>, tc_conv_kernel<0, -1>},
+        {tc_conv_kernel<1, kNone>, tc_conv_kernel<1, kRelu>, tc_conv_kernel<1, -1>},
+        {tc_conv_kernel<2, kNone>, tc_conv_kernel<2, kRelu>, tc_conv_kernel<2, -1>},
+        {tc_conv_kernel<3, kNone>, tc_conv_kernel<3, kRelu>, tc_conv_kernel<3, -1>}};
+    auto kern = kerns[kind][c.act == kNone ? 0 : c.act == kRelu ? 1 : 2];
     {
         cudaError_t e = ensure_smem_attr((const void *)kern, 227 * 1024);
         if (e != cudaSuccess) {
