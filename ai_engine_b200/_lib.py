@@ -48,6 +48,14 @@ class PlanInfo(C.Structure):
                 ("grid_ctas", C.c_uint64)]
 
 
+class TView(C.Structure):
+    """aie_tview: a channel view of an NHWC buffer (data, pixel stride, first channel)."""
+    _fields_ = [("data", C.c_void_p), ("stride", C.c_uint32), ("coff", C.c_uint32)]
+
+
+BIN_OPS = {"add": 0, "sub": 1, "mul": 2, "prelu": 3}          # aie_binop
+OPND_TENSOR, OPND_SCALAR, OPND_SCALAR_FIRST, OPND_CVEC, OPND_CVEC_TENSOR, OPND_PVEC_TENSOR = range(6)
+
 # Every symbol include/aie_conv.h declares, with its ctypes signature.
 _vp, _fp = C.c_void_p, C.POINTER(C.c_float)
 SIGNATURES = {
@@ -69,6 +77,12 @@ SIGNATURES = {
     "aie_conv_run_mbconv": (C.c_int, [_vp] * 13),
     "aie_input_u8": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _vp, C.c_int32, _vp, _vp]),
     "aie_selftest_wait_timeout": (C.c_int, [C.c_uint32, _vp]),
+    "aie_binary": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, C.c_int32, C.c_int32, TView, C.c_float,
+                             C.c_int32, TView, _vp]),
+    "aie_mix": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, TView, TView, TView, _vp]),
+    "aie_gpool": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, _vp, _vp]),
+    "aie_avgpool": (C.c_int, [C.c_uint32] * 8 + [C.POINTER(C.c_uint32), _vp, _vp, _vp]),
+    "aie_channel_copy": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, C.c_int32, TView, _vp]),
 }
 
 _LIB = None

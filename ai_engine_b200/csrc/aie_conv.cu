@@ -24,6 +24,7 @@
 #include "k_stem_tc.cuh"
 #include "k_pw_simt.cuh"
 #include "k_mbconv.cuh"
+#include "k_elem.cuh"
 
 using namespace aie;
 
@@ -925,6 +926,174 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     resize_bilinear_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "resize launch");
+    return AIE_OK;
+}
+
+// ------------------------------------------------------- graph glue ---
+
+// Resolves a channel view of c channels; stride 0 = dense.  Fails on a null
+// pointer or a view whose channels run past its pixel stride.
+static int make_eview(const aie_tview &v, uint32_t c, const char *what, EView *out)
+{
+    if (!v.data) return fail(AIE_E_INVALID, "%s: null tensor pointer", what);
+    const uint32_t stride = v.stride ? v.stride : c;
+    if ((uint64_t)v.coff + c > stride)
+        return fail(AIE_E_INVALID, "%s: channels [%u, %u) exceed the pixel stride %u", what, v.coff, v.coff + c,
+                    stride);
+    out->p = (const float *)v.data;
+    out->stride = stride;
+    out->coff = (int)v.coff;
+    return AIE_OK;
+}
+
+static bool eview_vec(const EView &v)
+{
+    return (uintptr_t)v.p % 16 == 0 && v.stride % 4 == 0 && v.coff % 4 == 0;
+}
+
+// Grid for a grid-stride loop over `work` items of 256 threads: enough CTAs
+// to fill the SMs several times over, no more than the work needs.
+static unsigned elem_grid(long long work)
+{
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    const long long need = (work + 255) / 256;
+    return (unsigned)std::max(1ll, std::min(need, (long long)sms * 16));
+}
+
+static int elem_sizes(uint32_t n, uint32_t px, uint32_t c, const char *what)
+{
+    if (!n || !px || !c) return fail(AIE_E_INVALID, "%s: zero-sized tensor (n %u, px %u, c %u)", what, n, px, c);
+    return AIE_OK;
+}
+
+extern "C" int aie_binary(uint32_t n, uint32_t px, uint32_t c, aie_tview a, int32_t op, int32_t b_kind, aie_tview b,
+                          float scalar, int32_t act, aie_tview out, void *stream)
+{
+    int s;
+    if ((s = elem_sizes(n, px, c, "binary"))) return s;
+    if (op < AIE_BIN_ADD || op > AIE_BIN_PRELU) return fail(AIE_E_INVALID, "binary op %d out of range", op);
+    if (b_kind < AIE_OPND_TENSOR || b_kind > AIE_OPND_PVEC_TENSOR)
+        return fail(AIE_E_INVALID, "binary operand kind %d out of range", b_kind);
+    if (act < 0 || act > AIE_ACT_RECIP) return fail(AIE_E_INVALID, "activation %d out of range", act);
+    BinArgs g{};
+    EView y;
+    if ((s = make_eview(a, c, "binary a", &g.a)) || (s = make_eview(out, c, "binary out", &y))) return s;
+    if (b_kind == AIE_OPND_TENSOR) {
+        if ((s = make_eview(b, c, "binary b", &g.b))) return s;
+    } else if (b_kind != AIE_OPND_SCALAR && b_kind != AIE_OPND_SCALAR_FIRST) {
+        if (!b.data) return fail(AIE_E_INVALID, "binary b: null vector pointer");
+        g.b.p = (const float *)b.data;
+    }
+    g.y = (float *)y.p;
+    g.y_stride = y.stride;
+    g.y_coff = y.coff;
+    g.Q = (long long)n * px;
+    g.px = px;
+    g.c = (int)c;
+    g.groups = (int)((c + 3) / 4);
+    g.op = op; g.bkind = b_kind; g.act = act; g.scalar = scalar;
+    g.vec = c % 4 == 0 && eview_vec(g.a) && eview_vec(y) && (b_kind != AIE_OPND_TENSOR || eview_vec(g.b));
+    binary_kernel<<<elem_grid(g.Q * g.groups), 256, 0, (cudaStream_t)stream>>>(g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "binary launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_mix(uint32_t n, uint32_t px, uint32_t c, aie_tview z, aie_tview a, aie_tview b, aie_tview out,
+                       void *stream)
+{
+    int s;
+    if ((s = elem_sizes(n, px, c, "mix"))) return s;
+    MixArgs m{};
+    EView y;
+    if ((s = make_eview(z, c, "mix z", &m.z)) || (s = make_eview(a, c, "mix a", &m.a)) ||
+        (s = make_eview(b, c, "mix b", &m.b)) || (s = make_eview(out, c, "mix out", &y)))
+        return s;
+    m.y = (float *)y.p;
+    m.y_stride = y.stride;
+    m.y_coff = y.coff;
+    m.Q = (long long)n * px;
+    m.c = (int)c;
+    m.groups = (int)((c + 3) / 4);
+    m.vec = c % 4 == 0 && eview_vec(m.z) && eview_vec(m.a) && eview_vec(m.b) && eview_vec(y);
+    mix_kernel<<<elem_grid(m.Q * m.groups), 256, 0, (cudaStream_t)stream>>>(m);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "mix launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_gpool(uint32_t n, uint32_t px, uint32_t c, aie_tview in, void *out, void *stream)
+{
+    int s;
+    if ((s = elem_sizes(n, px, c, "gpool"))) return s;
+    if (!out) return fail(AIE_E_INVALID, "gpool out: null tensor pointer");
+    GpoolArgs g{};
+    if ((s = make_eview(in, c, "gpool in", &g.x))) return s;
+    g.y = (float *)out;
+    g.n = (int)n;
+    g.c = (int)c;
+    g.groups = (int)((c + 3) / 4);
+    g.px = px;
+    g.inv = 1.0f / (float)px;
+    g.vec = c % 4 == 0 && eview_vec(g.x);
+    const long long threads = (long long)n * g.groups;
+    if (threads >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "gpool: too many frames x channel groups");
+    gpool_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, (cudaStream_t)stream>>>(g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gpool launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_avgpool(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, uint32_t kh, uint32_t kw, uint32_t sh,
+                           uint32_t sw, const uint32_t pad[4], const void *in, void *out, void *stream)
+{
+    if (!in || !out || !pad) return fail(AIE_E_INVALID, "avgpool: null pointer");
+    if (!n || !ih || !iw || !c || !kh || !kw || !sh || !sw) return fail(AIE_E_INVALID, "avgpool: zero size");
+    const long long eh = (long long)ih + pad[0] + pad[2], ew = (long long)iw + pad[1] + pad[3];
+    if (eh < kh || ew < kw) return fail(AIE_E_INVALID, "avgpool: window larger than the padded frame");
+    AvgpoolArgs a{};
+    a.x = (const float *)in;
+    a.y = (float *)out;
+    a.n = (int)n; a.ih = (int)ih; a.iw = (int)iw; a.c = (int)c;
+    a.groups = (int)((c + 3) / 4);
+    a.oh = (int)((eh - kh) / sh + 1);
+    a.ow = (int)((ew - kw) / sw + 1);
+    a.kh = (int)kh; a.kw = (int)kw; a.sh = (int)sh; a.sw = (int)sw;
+    a.pt = (int)pad[0]; a.pl = (int)pad[1];
+    a.inv = 1.0f / (float)(kh * kw);
+    a.vec = c % 4 == 0 && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0;
+    avgpool_kernel<<<elem_grid((long long)n * a.oh * a.ow * a.groups), 256, 0, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "avgpool launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_channel_copy(uint32_t n, uint32_t px, uint32_t c, aie_tview in, int32_t act, aie_tview out,
+                                void *stream)
+{
+    int s;
+    if ((s = elem_sizes(n, px, c, "channel copy"))) return s;
+    if (act < 0 || act > AIE_ACT_RECIP) return fail(AIE_E_INVALID, "activation %d out of range", act);
+    CopyArgs a{};
+    EView y;
+    if ((s = make_eview(in, c, "channel copy in", &a.x)) || (s = make_eview(out, c, "channel copy out", &y)))
+        return s;
+    a.y = (float *)y.p;
+    a.y_stride = y.stride;
+    a.y_coff = y.coff;
+    a.Q = (long long)n * px;
+    a.c = (int)c;
+    a.groups = (int)((c + 3) / 4);
+    a.act = act;
+    a.vec = c % 4 == 0 && eview_vec(a.x) && eview_vec(y);
+    chcopy_kernel<<<elem_grid(a.Q * a.groups), 256, 0, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "channel copy launch");
     return AIE_OK;
 }
 

@@ -1,0 +1,322 @@
+"""Graph executor for conv graphs with glue ops and recurrent state.
+
+Plays the part of ai-gpu-runtime's ``Model`` (crates/ai-gpu-runtime/src/
+model.rs:56-426) for graphs that mix convs with the non-conv ops of
+``SwOp`` (crates/ai-core/src/format/model.rs:78-214) -- the recurrent
+matting net's SE gates, LR-ASPP, ConvGRU and output block -- and that carry
+state from one frame to the next (``SwState``, the ``r1..r4 -> r1o..r4o``
+pairs of a recurrent model; ai_cpu::Model keeps them the same way,
+crates/ai-cpu/src/model.rs:114-144).
+
+Load time lowers every conv (one ``ConvPlan`` each, packed weights on the
+device) and allocates every tensor once; a step records one launch per op
+on one CUDA stream, or replays a captured CUDA graph.  Recurrent state
+ping-pongs between two buffers per state, so a step never copies it: the
+executor captures one graph per parity.
+
+Nodes (``Node.kind``):
+  conv     out = conv(ins[0]) (+ res)                 SwOp::Conv
+  binary   out = act(ins[0] o ins[1] | scalar | cvec)  SwOp::Binary
+  mix      out = a + z (b - a), ins = (z, a, b)       SwOp::Mix
+  gpool    out [1, 1, C] = channel means               SwOp::Gpool
+  avgpool  window mean, k / s in ``size``              SwOp::Avgpool
+  resize   bilinear to ``size`` (half_pixel)           SwOp::Resize
+  concat   channel concat of ins                       SwOp::Concat
+  split    outs = channel slices of ins[0] (views)     Split (an alias)
+  chcopy   out = act(ins[0][coff : coff + c])          SwOp::Chcopy / Act
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from . import elementwise as ew
+from .conv import Conv2d, ConvPlan, View, resize_bilinear
+
+
+@dataclass
+class Node:
+    kind: str
+    out: object                      # a tensor name (a tuple of names for split)
+    ins: Tuple[str, ...]
+    conv: Optional[Conv2d] = None
+    res: Optional[str] = None
+    op: str = "add"                  # binary op
+    act: str = "none"
+    bkind: str = "tensor"            # binary operand: tensor / scalar / scalar_first / cvec / cvec_tensor
+    scalar: float = 0.0
+    size: Tuple[int, ...] = ()       # resize (oh, ow); avgpool (kh, kw, sh, sw)
+    parts: Tuple[int, ...] = ()      # split channel counts; chcopy (coff, c)
+
+
+def infer_shapes(nodes: Sequence[Node], inputs: Dict[str, Tuple[int, int, int]]) -> Dict[str, Tuple[int, int, int]]:
+    """(h, w, c) of every tensor, checking each op's operand shapes."""
+    sh = dict(inputs)
+    for nd in nodes:
+        s0 = sh[nd.ins[0]] if nd.ins else None
+        k = nd.kind
+        if k == "conv":
+            if s0[2] != nd.conv.cin:
+                raise ValueError(f"{nd.out}: conv expects {nd.conv.cin} channels, {nd.ins[0]} has {s0[2]}")
+            oh, ow = nd.conv.out_hw(s0[0], s0[1])
+            sh[nd.out] = (oh, ow, nd.conv.cout)
+            if nd.res is not None and sh[nd.res] != sh[nd.out]:
+                raise ValueError(f"{nd.out}: residual shape {sh[nd.res]} != {sh[nd.out]}")
+        elif k == "binary":
+            if nd.bkind == "tensor" and sh[nd.ins[1]] != s0:
+                raise ValueError(f"{nd.out}: operand shapes {s0} / {sh[nd.ins[1]]}")
+            if nd.bkind == "cvec_tensor" and sh[nd.ins[1]] != (1, 1, s0[2]):
+                raise ValueError(f"{nd.out}: channel vector {sh[nd.ins[1]]} for {s0}")
+            sh[nd.out] = s0
+        elif k == "mix":
+            if not (sh[nd.ins[1]] == sh[nd.ins[2]] == s0):
+                raise ValueError(f"{nd.out}: mix operand shapes differ")
+            sh[nd.out] = s0
+        elif k == "gpool":
+            sh[nd.out] = (1, 1, s0[2])
+        elif k == "avgpool":
+            kh, kw, sy, sx = nd.size
+            sh[nd.out] = ((s0[0] - kh) // sy + 1, (s0[1] - kw) // sx + 1, s0[2])
+        elif k == "resize":
+            sh[nd.out] = (nd.size[0], nd.size[1], s0[2])
+        elif k == "concat":
+            hw = {sh[i][:2] for i in nd.ins}
+            if len(hw) != 1:
+                raise ValueError(f"{nd.out}: concat parts differ in size {hw}")
+            sh[nd.out] = (s0[0], s0[1], sum(sh[i][2] for i in nd.ins))
+        elif k == "split":
+            if sum(nd.parts) != s0[2]:
+                raise ValueError(f"split of {nd.ins[0]}: parts {nd.parts} != {s0[2]} channels")
+            for name, c in zip(nd.out, nd.parts):
+                sh[name] = (s0[0], s0[1], c)
+        elif k == "chcopy":
+            coff, c = nd.parts
+            if coff + c > s0[2]:
+                raise ValueError(f"{nd.out}: channels past the source")
+            sh[nd.out] = (s0[0], s0[1], c)
+        else:
+            raise ValueError(f"unknown node kind {k}")
+    return sh
+
+
+def _pad4(c: int) -> int:
+    return (c + 3) // 4 * 4
+
+
+@dataclass
+class _Rec:
+    node: Node
+    plan: Optional[ConvPlan] = None
+
+
+class NetModel:
+    """Load-time lowering and per-step execution of a node graph on one GPU.
+
+    inputs: {name: (h, w, c)} of the per-frame inputs; states: {in: out}
+    pairs of recurrent tensors (out of step t is in of step t + 1, zero
+    before the first step); outputs: the names a step returns."""
+
+    def __init__(self, nodes: Sequence[Node], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
+                 inputs: Dict[str, Tuple[int, int, int]], outputs: Sequence[str],
+                 states: Optional[Dict[str, str]] = None, consts: Optional[Dict[str, np.ndarray]] = None, *,
+                 math: str = "auto", device=None):
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.n = n
+        self.nodes = list(nodes)
+        self.states = dict(states or {})
+        self.outputs = list(outputs)
+        self.shapes = infer_shapes(self.nodes, inputs)
+        for si, so in self.states.items():
+            if self.shapes[si] != self.shapes[so]:
+                raise ValueError(f"state {si} {self.shapes[si]} != {so} {self.shapes[so]}")
+        consumers: Dict[str, List[Node]] = {}
+        for nd in self.nodes:
+            for t in (*nd.ins, nd.res):
+                if t is not None:
+                    consumers.setdefault(t, []).append(nd)
+        # a concat whose consumers are all convs gets its channels padded to a
+        # multiple of 4 (zero lanes, zero weights): the conv then reads it
+        # through TMA on the tensor cores
+        self.cpad: Dict[str, int] = {}
+        for nd in self.nodes:
+            if nd.kind == "concat":
+                c = self.shapes[nd.out][2]
+                users = consumers.get(nd.out, [])
+                if c % 4 and users and all(u.kind == "conv" and u.ins[0] == nd.out for u in users) \
+                        and nd.out not in self.outputs:
+                    self.cpad[nd.out] = _pad4(c)
+        self.alias: Dict[str, Tuple[str, int, int]] = {}  # split output -> (base tensor, coff, c)
+        self.bufs: Dict[str, torch.Tensor] = {}
+        self.recs: List[_Rec] = []
+        dev = self.device
+        with torch.cuda.device(dev):
+            def alloc(name, zero=False):
+                h, w, c = self.shapes[name]
+                c = self.cpad.get(name, c)
+                self.bufs[name] = (torch.zeros if zero else torch.empty)((n, h, w, c), dtype=torch.float32, device=dev)
+
+            for name in inputs:
+                alloc(name, zero=name in self.states)
+            for nd in self.nodes:
+                rec = _Rec(nd)
+                if nd.kind == "split":
+                    base, coff0 = self._base(nd.ins[0])
+                    coff = coff0
+                    for name, c in zip(nd.out, nd.parts):
+                        self.alias[name] = (base, coff, c)
+                        coff += c
+                    self.recs.append(rec)
+                    continue
+                alloc(nd.out, zero=nd.out in self.cpad)
+                if nd.kind == "conv":
+                    src = nd.ins[0]
+                    h, w, c = self.shapes[src]
+                    cv = nd.conv
+                    wt, b = weights[nd.out]
+                    base, coff = self._base(src)
+                    bc = self.bufs[base].shape[-1]
+                    if src in self.cpad:  # padded concat: zero weight rows for the padding lanes
+                        cp = self.cpad[src]
+                        w4 = np.zeros((cv.cout, cp, cv.kh, cv.kw), np.float32)
+                        w4[:, :c] = np.asarray(wt, np.float32).reshape(cv.cout, c, cv.kh, cv.kw)
+                        wt = w4
+                        cv = Conv2d(cp, cv.cout, cv.kh, cv.kw, cv.sh, cv.sw, cv.pad, cv.dil, cv.groups, cv.act)
+                    in_view = View(bc, coff) if (base != src) else None
+                    rec.plan = ConvPlan(cv, n, h, w, has_res=nd.res is not None, math=math, in_view=in_view,
+                                        device=dev).load_weights(wt, b)
+                self.recs.append(rec)
+            for si, so in self.states.items():
+                if so in self.alias:
+                    raise ValueError(f"state output {so} must be a tensor, not a view")
+        self.consts = {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(dev)
+                       for k, v in (consts or {}).items()}
+        self.step_index = 0
+        self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+
+    # -- tensors -----------------------------------------------------------------
+    def _base(self, name: str) -> Tuple[str, int]:
+        if name in self.alias:
+            b, coff, _ = self.alias[name]
+            return b, coff
+        return name, 0
+
+    def view(self, name: str) -> ew.ChView:
+        if name in self.alias:
+            b, coff, c = self.alias[name]
+            return ew.ChView(self.bufs[b], coff, c)
+        return ew.ChView(self.bufs[name], 0, self.shapes[name][2])
+
+    def tensor(self, name: str) -> torch.Tensor:
+        """The logical [n, h, w, c] tensor (a copy if it is a view or padded)."""
+        v = self.view(name)
+        if v.coff == 0 and v.c == v.t.shape[-1]:
+            return v.t
+        return v.t[..., v.coff:v.coff + v.c].contiguous()
+
+    @property
+    def conv_flops(self) -> int:
+        return sum(r.plan.flops for r in self.recs if r.plan is not None)
+
+    # -- execution -----------------------------------------------------------------
+    def record(self, stream=None):
+        """Issue every op of one step on `stream` (default: current stream)."""
+        for r in self.recs:
+            nd = r.node
+            k = nd.kind
+            if k == "split":
+                continue
+            if k == "conv":
+                base, _ = self._base(nd.ins[0])
+                r.plan(self.bufs[base], res=None if nd.res is None else self.bufs[nd.res], out=self.bufs[nd.out],
+                       stream=stream)
+            elif k == "binary":
+                if nd.bkind == "tensor":
+                    b = self.view(nd.ins[1])
+                elif nd.bkind in ("scalar", "scalar_first"):
+                    b = nd.scalar
+                elif nd.bkind == "cvec":
+                    b = self.consts[nd.ins[1]]
+                else:
+                    b = self.bufs[nd.ins[1]]
+                ew.binary(nd.op, self.view(nd.ins[0]), b, self.view(nd.out), nd.act,
+                          kind="scalar" if nd.bkind == "scalar_first" else nd.bkind,
+                          scalar_first=nd.bkind == "scalar_first", stream=stream)
+            elif k == "mix":
+                ew.mix(self.view(nd.ins[0]), self.view(nd.ins[1]), self.view(nd.ins[2]), self.view(nd.out),
+                       stream=stream)
+            elif k == "gpool":
+                ew.gpool(self.view(nd.ins[0]), self.bufs[nd.out], stream=stream)
+            elif k == "avgpool":
+                ew.avgpool(self.bufs[nd.ins[0]], self.bufs[nd.out], nd.size[:2], nd.size[2:], stream=stream)
+            elif k == "resize":
+                resize_bilinear(self.tensor_for_resize(nd.ins[0]), nd.size[0], nd.size[1], out=self.bufs[nd.out],
+                                stream=stream)
+            elif k == "concat":
+                out = self.bufs[nd.out]
+                coff = 0
+                for part in nd.ins:
+                    c = self.shapes[part][2]
+                    ew.channel_copy(self.view(part), ew.ChView(out, coff, c), stream=stream)
+                    coff += c
+            elif k == "chcopy":
+                coff, c = nd.parts
+                b, boff = self._base(nd.ins[0])
+                ew.channel_copy(ew.ChView(self.bufs[b], boff + coff, c), self.view(nd.out), nd.act, stream=stream)
+
+    def tensor_for_resize(self, name: str) -> torch.Tensor:
+        if name in self.alias or name in self.cpad:
+            raise ValueError(f"resize reads a dense tensor, {name} is a view")
+        return self.bufs[name]
+
+    def advance(self):
+        """Make this step's state outputs the next step's state inputs."""
+        for si, so in self.states.items():
+            self.bufs[si], self.bufs[so] = self.bufs[so], self.bufs[si]
+        self.step_index += 1
+
+    def reset_state(self):
+        for si in self.states:
+            self.bufs[si].zero_()
+        self.step_index = 0
+
+    def capture(self):
+        """Capture one CUDA graph per state parity (the buffers swap roles
+        every step).  Replays with `replay()`."""
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.record(s)  # warm-up outside capture (plans, allocator)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        saved = {k: self.bufs[k] for k in (*self.states.keys(), *self.states.values())}
+        for parity in (0, 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.record()
+            self.graphs[parity] = g
+            for si, so in self.states.items():
+                self.bufs[si], self.bufs[so] = self.bufs[so], self.bufs[si]
+        self.bufs.update(saved)
+        self.reset_state()
+
+    def replay(self):
+        """One step from the captured graphs (state advances)."""
+        self.graphs[self.step_index % 2].replay()
+        self.advance()
+
+    def step(self, inputs: Dict[str, torch.Tensor], stream=None) -> Dict[str, torch.Tensor]:
+        """Copy the step's inputs in, run one step eagerly, return the outputs
+        (device tensors, valid until the next step)."""
+        for k, v in inputs.items():
+            self.bufs[k].copy_(v)
+        self.record(stream)
+        outs = {k: self.tensor(k) for k in self.outputs}
+        outs = {k: (v.clone() if k in self.states.values() else v) for k, v in outs.items()}
+        self.advance()
+        return outs
+
+    def release(self):
+        self.graphs.clear()

@@ -266,6 +266,73 @@ AIE_API int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, const
 AIE_API int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, uint32_t oh,
                         uint32_t ow, int32_t mode, const void *add, int32_t act, void *out, void *stream);
 
+/* ---- Graph glue: the non-conv ops of ai_engine's recurrent matting graph
+ * (RVM) and its segmentation heads, on NHWC f32 batches.  Each is one
+ * stream-ordered launch, allocates nothing, and rounds every result the way
+ * ai-cpu's kernels do (unfused multiply and add), so results are
+ * bit-identical to ai-cpu's except for sigmoid / tanh (libm's expf / tanhf
+ * against CUDA's, an ulp or two).
+ *
+ * A tensor argument is a channel view of an NHWC buffer -- the runtime's
+ * SrcView (crates/ai-gpu/src/kernels/common/source.rs:17-80) and ai-cpu's
+ * View (crates/ai-cpu/src/view.rs:8-16): element (pixel q, channel ch), q running
+ * over every frame's pixels, lives at data[q * stride + coff + ch].
+ * stride = 0 means dense (stride = the op's channel count). */
+typedef struct aie_tview {
+    void *data;
+    uint32_t stride;
+    uint32_t coff;
+} aie_tview;
+
+/* ai-core's BinaryOp (crates/ai-core/src/ops/elementwise.rs:5-11). */
+typedef enum aie_binop { AIE_BIN_ADD = 0, AIE_BIN_SUB = 1, AIE_BIN_MUL = 2, AIE_BIN_PRELU = 3 } aie_binop;
+
+/* Kinds of a Binary op's second operand (SwOperand,
+ * crates/ai-core/src/format/model.rs:60-75). */
+typedef enum aie_operand {
+    AIE_OPND_TENSOR = 0,       /* b: same shape as a (a view) */
+    AIE_OPND_SCALAR = 1,       /* a o scalar */
+    AIE_OPND_SCALAR_FIRST = 2, /* scalar o a */
+    AIE_OPND_CVEC = 3,         /* b.data: [c] channel vector, all frames (Cvec) */
+    AIE_OPND_CVEC_TENSOR = 4,  /* b.data: [n][c] per-frame channel vector (CvecTensor: an SE gate) */
+    AIE_OPND_PVEC_TENSOR = 5   /* b.data: [n * px] per-pixel scalar, all channels (PvecTensor) */
+} aie_operand;
+
+/* out = act(a o b) over n frames of px pixels and c channels: SwOp::Binary
+ * (crates/ai-core/src/format/model.rs:111-117; reference
+ * crates/ai-core/src/reference/elementwise.rs:7-26; ai-cpu
+ * crates/ai-cpu/src/kernels/elementwise.rs: binary_tensor, binary_scalar,
+ * binary_cvec, binary_pvec).  out may alias a or b exactly. */
+AIE_API int aie_binary(uint32_t n, uint32_t px, uint32_t c, aie_tview a, int32_t op, int32_t b_kind, aie_tview b,
+                       float scalar, int32_t act, aie_tview out, void *stream);
+
+/* ConvGRU mix out = a + z (b - a): SwOp::Mix (crates/ai-core/src/format/
+ * model.rs:193-199), ai-cpu's elementwise::mix (elementwise.rs:128-150),
+ * in its rounding order. */
+AIE_API int aie_mix(uint32_t n, uint32_t px, uint32_t c, aie_tview z, aie_tview a, aie_tview b, aie_tview out,
+                    void *stream);
+
+/* Global average pool [n][px][c] -> out [n][c] (dense): SwOp::Gpool
+ * (crates/ai-core/src/reference/pool.rs:5-19; ai-cpu segate.rs:46-57),
+ * summed in pixel order then scaled by 1/px, bit-identical to ai-cpu.
+ * Feeds an SE gate's 1x1 convs (run as aie_conv plans over n frames of
+ * 1 x 1 pixels) and AIE_OPND_CVEC_TENSOR. */
+AIE_API int aie_gpool(uint32_t n, uint32_t px, uint32_t c, aie_tview in, void *out, void *stream);
+
+/* Average pool with the fixed kh*kw divisor (taps outside the frame add
+ * nothing): SwOp::Avgpool (crates/ai-core/src/reference/pool.rs:22-46).
+ * Dense NHWC [n, ih, iw, c] -> [n, oh, ow, c]; pad = {top, left, bottom,
+ * right}; oh = (ih + pt + pb - kh) / sh + 1 (likewise ow). */
+AIE_API int aie_avgpool(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, uint32_t kh, uint32_t kw, uint32_t sh,
+                        uint32_t sw, const uint32_t pad[4], const void *in, void *out, void *stream);
+
+/* out[q, 0:c] = act(in[q, 0:c]) between channel views: one part of a
+ * channel concat written at its offset (SwOp::Concat), a channel slice
+ * (SwOp::Chcopy) or a stand-alone activation (SwOp::Act)
+ * (crates/ai-core/src/format/model.rs:156-175). */
+AIE_API int aie_channel_copy(uint32_t n, uint32_t px, uint32_t c, aie_tview in, int32_t act, aie_tview out,
+                             void *stream);
+
 /* Human-readable status, and the detail message of this thread's last
  * failure (copied into buf, NUL-terminated; returns its full length). */
 AIE_API const char *aie_status_string(int status);

@@ -65,6 +65,13 @@ def lib():
         L.orc_resize_bilinear.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, _fp, C.c_uint32, C.c_uint32,
                                           C.c_int, _fp]
         L.orc_add.argtypes = [_fp, _fp, C.c_size_t, C.c_size_t, C.c_int, _fp]
+        sz = C.c_size_t
+        L.orc_binary.argtypes = [sz, sz, sz, _fp, sz, sz, C.c_int, C.c_int, _fp, sz, sz, C.c_float, C.c_int,
+                                 _fp, sz, sz]
+        L.orc_mix.argtypes = [sz, sz, sz] + [_fp, sz, sz] * 4
+        L.orc_gpool.argtypes = [sz, sz, sz, _fp, sz, sz, _fp]
+        L.orc_avgpool.argtypes = [C.c_uint32] * 11 + [_fp, _fp]
+        L.orc_channel_copy.argtypes = [sz, sz, sz, _fp, sz, sz, C.c_int, _fp, sz, sz]
         _LIB = L
     return _LIB
 
@@ -238,3 +245,81 @@ def dot_scale(op, x: np.ndarray, w: np.ndarray, bias=None) -> np.ndarray:
                 contrib = patch * wv[:, 0, ky, kx]
             out[:, ys[:, None], xs[None, :], :] += contrib
     return out
+
+
+# ----------------------------------------------------------- graph glue ---
+# Views: (array, coff, c) selects channels [coff, coff + c) of a dense
+# [..., C] float32 array; a bare array is the whole channel range.
+
+def _view(v):
+    if isinstance(v, tuple):
+        arr, coff, c = v
+    else:
+        arr, coff, c = v, 0, v.shape[-1]
+    if arr.dtype != np.float32 or not arr.flags.c_contiguous:
+        raise TypeError("oracle views need contiguous float32 arrays")
+    return arr, arr.shape[-1], coff, c
+
+
+def _npx(arr):
+    return arr.shape[0], arr.size // (arr.shape[0] * arr.shape[-1])
+
+
+BIN_OPS = {"add": 0, "sub": 1, "mul": 2, "prelu": 3}
+OPND_KINDS = {"tensor": 0, "scalar": 1, "scalar_first": 2, "cvec": 3, "cvec_tensor": 4, "pvec_tensor": 5}
+
+
+def binary(op: str, a, b, out, act="none", kind: str = "tensor") -> None:
+    """SwOp::Binary into `out` (a view), ai-cpu rounding (elementwise.rs)."""
+    aa, as_, ao, c = _view(a)
+    oa, os_, oo, _ = _view(out)
+    n, px = _npx(aa)
+    bs = bo = 0
+    scalar = 0.0
+    if kind == "tensor":
+        ba, bs, bo, _ = _view(b)
+    elif kind in ("scalar", "scalar_first"):
+        ba, scalar = None, float(b)
+    else:
+        ba = np.ascontiguousarray(b, np.float32)
+    lib().orc_binary(n, px, c, _ptr(aa), as_, ao, BIN_OPS[op], OPND_KINDS[kind], _ptr(ba), bs, bo,
+                     C.c_float(scalar), _act(act), _ptr(oa), os_, oo)
+
+
+def mix(z, a, b, out) -> None:
+    """SwOp::Mix out = a + z (b - a) in ai-cpu's order (elementwise.rs:128-150)."""
+    za, zs, zo, c = _view(z)
+    aa, as_, ao, _ = _view(a)
+    ba, bs, bo, _ = _view(b)
+    oa, os_, oo, _ = _view(out)
+    n, px = _npx(za)
+    lib().orc_mix(n, px, c, _ptr(za), zs, zo, _ptr(aa), as_, ao, _ptr(ba), bs, bo, _ptr(oa), os_, oo)
+
+
+def gpool(x) -> np.ndarray:
+    """SwOp::Gpool: [n, ..., C] view -> [n, c] channel means (segate.rs:46-57)."""
+    xa, xs, xo, c = _view(x)
+    n, px = _npx(xa)
+    out = np.empty((n, c), np.float32)
+    lib().orc_gpool(n, px, c, _ptr(xa), xs, xo, _ptr(out))
+    return out
+
+
+def avgpool(x: np.ndarray, k, s, pad=(0, 0, 0, 0)) -> np.ndarray:
+    """SwOp::Avgpool over [n, h, w, c] (reference/pool.rs:22-46)."""
+    x = np.ascontiguousarray(x, np.float32)
+    n, ih, iw, c = x.shape
+    oh = (ih + pad[0] + pad[2] - k[0]) // s[0] + 1
+    ow = (iw + pad[1] + pad[3] - k[1]) // s[1] + 1
+    out = np.empty((n, oh, ow, c), np.float32)
+    for f in range(n):
+        lib().orc_avgpool(ih, iw, c, k[0], k[1], s[0], s[1], pad[0], pad[1], oh, ow, _ptr(x[f]), _ptr(out[f]))
+    return out
+
+
+def channel_copy(x, out, act="none") -> None:
+    """Concat part / Chcopy / Act: out view = act(x view)."""
+    xa, xs, xo, c = _view(x)
+    oa, os_, oo, _ = _view(out)
+    n, px = _npx(xa)
+    lib().orc_channel_copy(n, px, c, _ptr(xa), xs, xo, _act(act), _ptr(oa), os_, oo)

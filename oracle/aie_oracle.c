@@ -18,6 +18,10 @@
  *   - kernel choice at load time             crates/ai-cpu/src/plan.rs:462-619
  *   - bilinear resize                        crates/ai-core/src/reference/resize.rs:5-42
  *   - binary add                             crates/ai-cpu/src/kernels/elementwise.rs:30-55
+ *   - Binary (tensor/scalar/cvec/pvec), Mix, crates/ai-cpu/src/kernels/elementwise.rs,
+ *     Act, Concat/Chcopy copies              crates/ai-core/src/reference/elementwise.rs:7-26
+ *   - Gpool, Avgpool                         crates/ai-cpu/src/kernels/segate.rs:46-57,
+ *                                            crates/ai-core/src/reference/pool.rs:5-46
  *
  * Rounding.  ai-cpu on x86 runs its scalar F32x4 fallback
  * (crates/ai-cpu/src/simd.rs:189-300): `fma` is a separate multiply then add,
@@ -650,4 +654,110 @@ ORC_API void orc_add(const float *a, const float *b, size_t n, size_t c, int act
         size_t ch = c ? i % c : 0;
         out[i] = epi_act(act, a[i] + b[i], ch, c ? c : 4);
     }
+}
+
+/* ---- graph glue (crates/ai-cpu/src/kernels/elementwise.rs, segate.rs;
+ * crates/ai-core/src/reference/{elementwise,pool}.rs).  Tensors are channel
+ * views: element (pixel q, channel ch) at p[q * stride + off + ch], q over
+ * all n * px pixels (ai-cpu's View, crates/ai-cpu/src/view.rs:8-16). */
+
+/* BinaryOp::apply (crates/ai-core/src/ops/elementwise.rs:14-27).  ai-cpu's
+ * 4-lane Sub is a + b * (-1) and rounds the same as a - b. */
+static inline float bin_apply(int op, float a, float b)
+{
+    switch (op) {
+    case 0: return a + b;
+    case 1: return a - b;
+    case 2: return a * b;
+    default: return a > 0.0f ? a : a * b;
+    }
+}
+
+/* SwOp::Binary: out = act(a o b).  kind: 0 tensor view, 1 a o scalar,
+ * 2 scalar o a, 3 [c] channel vector, 4 [n][c] per-frame channel vector,
+ * 5 [n * px] per-pixel scalar (binary_tensor / binary_scalar / binary_cvec /
+ * binary_pvec, elementwise.rs:29-101 and the tail loops). */
+ORC_API void orc_binary(size_t n, size_t px, size_t c, const float *a, size_t as, size_t ao, int op, int kind,
+                        const float *b, size_t bs, size_t bo, float scalar, int act, float *out, size_t os,
+                        size_t oo)
+{
+    for (size_t q = 0; q < n * px; q++) {
+        for (size_t ch = 0; ch < c; ch++) {
+            float x = a[q * as + ao + ch], s;
+            switch (kind) {
+            case 0: s = b[q * bs + bo + ch]; break;
+            case 3: s = b[ch]; break;
+            case 4: s = b[(q / px) * c + ch]; break;
+            case 5: s = b[q]; break;
+            default: s = scalar; break;
+            }
+            float v = kind == 2 ? bin_apply(op, s, x) : bin_apply(op, x, s);
+            out[q * os + oo + ch] = epi_act(act, v, ch, c);
+        }
+    }
+}
+
+/* SwOp::Mix out = a + z (b - a), elementwise.rs:128-150: the 4-lane part is
+ * (a + z b) + (-z) a, the tail a + z (b - a). */
+ORC_API void orc_mix(size_t n, size_t px, size_t c, const float *z, size_t zs, size_t zo, const float *a, size_t as,
+                     size_t ao, const float *b, size_t bs, size_t bo, float *out, size_t os, size_t oo)
+{
+    const size_t cv = c / 4 * 4;
+    for (size_t q = 0; q < n * px; q++) {
+        for (size_t ch = 0; ch < c; ch++) {
+            float zv = z[q * zs + zo + ch], av = a[q * as + ao + ch], bv = b[q * bs + bo + ch];
+            float r;
+            if (ch < cv) {
+                float t = av + zv * bv;
+                r = t + (zv * -1.0f) * av;
+            } else {
+                r = av + zv * (bv - av);
+            }
+            out[q * os + oo + ch] = r;
+        }
+    }
+}
+
+/* SwOp::Gpool: per frame, channel sums in pixel order times 1/px
+ * (segate.rs:46-57, reference/pool.rs:5-19).  out: [n][c] dense. */
+ORC_API void orc_gpool(size_t n, size_t px, size_t c, const float *x, size_t xs, size_t xo, float *out)
+{
+    const float inv = 1.0f / (float)px;
+    for (size_t f = 0; f < n; f++) {
+        float *o = out + f * c;
+        for (size_t ch = 0; ch < c; ch++) o[ch] = 0.0f;
+        for (size_t p = 0; p < px; p++) {
+            const float *row = x + (f * px + p) * xs + xo;
+            for (size_t ch = 0; ch < c; ch++) o[ch] += row[ch];
+        }
+        for (size_t ch = 0; ch < c; ch++) o[ch] *= inv;
+    }
+}
+
+/* SwOp::Avgpool, one dense frame [ih][iw][c] -> [oh][ow][c]
+ * (reference/pool.rs:22-46): divisor kh*kw whatever the border. */
+ORC_API void orc_avgpool(uint32_t ih, uint32_t iw, uint32_t c, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
+                         uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow, const float *x, float *out)
+{
+    const float inv = 1.0f / (float)(kh * kw);
+    for (uint32_t oy = 0; oy < oh; oy++)
+        for (uint32_t ox = 0; ox < ow; ox++)
+            for (uint32_t ch = 0; ch < c; ch++) {
+                float acc = 0.0f;
+                for (uint32_t ky = 0; ky < kh; ky++)
+                    for (uint32_t kx = 0; kx < kw; kx++) {
+                        int64_t iy = (int64_t)(oy * sh + ky) - pt, ix = (int64_t)(ox * sw + kx) - pl;
+                        if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) acc += x[((size_t)iy * iw + ix) * c + ch];
+                    }
+                out[((size_t)oy * ow + ox) * c + ch] = acc * inv;
+            }
+}
+
+/* SwOp::Concat part / Chcopy / Act: out = act(x) between views
+ * (elementwise.rs:103-126 for the activation's apply4 / apply split). */
+ORC_API void orc_channel_copy(size_t n, size_t px, size_t c, const float *x, size_t xs, size_t xo, int act,
+                              float *out, size_t os, size_t oo)
+{
+    for (size_t q = 0; q < n * px; q++)
+        for (size_t ch = 0; ch < c; ch++) out[q * os + oo + ch] = epi_act(act, x[q * xs + xo + ch], ch, c);
 }

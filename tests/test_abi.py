@@ -180,3 +180,32 @@ def test_input_u8_argument_checks(lib):
     assert lib.aie_input_u8(0, 2, 2, 3, p, 0, p, None) == -2    # empty batch
     assert lib.aie_input_u8(1, 2, 2, 3, None, 0, p, None) == -2
     assert lib.aie_input_u8(1, 2, 2, 3, p, 1, C.c_void_p(20), None) == -5  # C4 output must be 16-byte aligned
+
+
+def test_glue_entry_points_reject_bad_arguments(lib):
+    """The graph-glue entry points validate on the host and return a status
+    (no launch, no CUDA call) for null pointers, zero sizes, out-of-range
+    enums and views whose channels run past their pixel stride."""
+    TV = _lib.TView
+    buf = (C.c_float * 64)()
+    good = TV(C.cast(buf, C.c_void_p), 0, 0)
+    null = TV(None, 0, 0)
+    inv = -2
+    # aie_binary(n, px, c, a, op, kind, b, scalar, act, out, stream)
+    assert lib.aie_binary(1, 4, 4, null, 0, 0, good, 0.0, 0, good, None) == inv
+    assert lib.aie_binary(0, 4, 4, good, 0, 0, good, 0.0, 0, good, None) == inv
+    assert lib.aie_binary(1, 4, 4, good, 9, 0, good, 0.0, 0, good, None) == inv
+    assert lib.aie_binary(1, 4, 4, good, 0, 9, good, 0.0, 0, good, None) == inv
+    assert lib.aie_binary(1, 4, 4, good, 0, 0, good, 0.0, 42, good, None) == inv
+    assert lib.aie_binary(1, 4, 4, TV(C.cast(buf, C.c_void_p), 6, 3), 0, 0, good, 0.0, 0, good, None) == inv
+    assert "pixel stride" in _lib.last_error()
+    assert lib.aie_binary(1, 4, 4, good, 0, _lib.OPND_CVEC, null, 0.0, 0, good, None) == inv
+    assert lib.aie_mix(1, 4, 4, good, null, good, good, None) == inv
+    assert lib.aie_gpool(1, 4, 4, good, None, None) == inv
+    assert lib.aie_gpool(1, 0, 4, good, C.cast(buf, C.c_void_p), None) == inv
+    pad = (C.c_uint32 * 4)(0, 0, 0, 0)
+    assert lib.aie_avgpool(1, 2, 2, 1, 3, 3, 1, 1, pad, C.cast(buf, C.c_void_p), C.cast(buf, C.c_void_p), None) == inv
+    assert lib.aie_avgpool(1, 2, 2, 1, 2, 2, 0, 1, pad, C.cast(buf, C.c_void_p), C.cast(buf, C.c_void_p), None) == inv
+    assert lib.aie_channel_copy(1, 4, 4, good, 11, good, None) == inv
+    assert lib.aie_channel_copy(1, 4, 4, good, 0, TV(C.cast(buf, C.c_void_p), 4, 1), None) == inv
+    assert "pixel stride" in _lib.last_error()

@@ -274,3 +274,70 @@ def test_dot_scale_bounds_error():
     s = oracle.dot_scale(op, x, w, b)
     y = oracle.conv_aicpu(op, x, w, b)
     assert s.shape == y.shape and (s + 1e-6 >= np.abs(y)).all()
+
+
+# ---- graph glue: the reference's own known answers -----------------------
+
+def test_binary_known_answers():
+    """crates/ai-core/src/reference/elementwise.rs:32-43."""
+    a = np.array([1.0, -2.0, 3.0], np.float32).reshape(1, 1, 3, 1)
+    b = np.array([0.5, 1.0, -1.0], np.float32).reshape(1, 1, 3, 1)
+    o = np.empty_like(a)
+    oracle.binary("add", a, b, o)
+    assert o.ravel().tolist() == [1.5, -1.0, 2.0]
+    oracle.binary("mul", a, b, o, act="relu")
+    assert o.ravel().tolist() == [0.5, 0.0, 0.0]
+    oracle.binary("sub", a, 1.0, o, kind="scalar_first")
+    assert o.ravel().tolist() == [0.0, 3.0, -2.0]
+
+
+def test_cvec_and_mix_known_answers():
+    """crates/ai-cpu/src/kernels/elementwise.rs:258-275 (cvec mul, GRU mix)."""
+    a = np.array([1, 4, 3, 8], np.float32).reshape(1, 1, 2, 2)
+    o = np.empty_like(a)
+    oracle.binary("mul", a, np.array([2.0, 0.5], np.float32), o, kind="cvec")
+    assert o.ravel().tolist() == [2.0, 2.0, 6.0, 4.0]
+    z = np.array([0, 1, 0.5, 0.5], np.float32).reshape(1, 1, 2, 2)
+    av = np.array([1, 1, 2, 4], np.float32).reshape(1, 1, 2, 2)
+    bv = np.array([3, 3, 4, 8], np.float32).reshape(1, 1, 2, 2)
+    oracle.mix(z, av, bv, o)
+    assert o.ravel().tolist() == [1.0, 3.0, 3.0, 6.0]
+
+
+def test_strided_view_binary_matches_dense():
+    """crates/ai-cpu/src/kernels/elementwise.rs:278-300: a channel-slice view
+    gives the same result as the materialised slice."""
+    rng = oracle.XorShift32(2)
+    px, big_c, c, off = 6, 7, 3, 2
+    big = rng.vec_f32(px * big_c).reshape(1, 1, px, big_c)
+    b = rng.vec_f32(px * c).reshape(1, 1, px, c)
+    dense = np.ascontiguousarray(big[..., off:off + c])
+    want = np.empty_like(b)
+    oracle.binary("add", dense, b, want, act="sigmoid")
+    got = np.empty_like(b)
+    oracle.binary("add", (big, off, c), b, got, act="sigmoid")
+    assert np.array_equal(want, got)
+    ref = 1.0 / (1.0 + np.exp(-(dense.astype(np.float64) + b)))
+    assert np.allclose(got, ref, rtol=1e-6)
+
+
+def test_pool_known_answers():
+    """crates/ai-core/src/reference/pool.rs:84-101 (gpool, 2x2 average pool)."""
+    x = np.array([1.0, 4.0, 2.0, 8.0, 3.0, 12.0, 4.0, 16.0], np.float32).reshape(1, 2, 2, 2)
+    assert oracle.gpool(x).ravel().tolist() == [2.5, 10.0]
+    ramp = np.arange(1, 17, dtype=np.float32).reshape(1, 4, 4, 1)
+    assert oracle.avgpool(ramp, (2, 2), (2, 2)).ravel().tolist() == [3.5, 5.5, 11.5, 13.5]
+
+
+def test_se_gate_known_answers():
+    """crates/ai-cpu/src/kernels/segate.rs:84-121: gpool then FC1 (ReLU), and
+    gpool -> FC1 (identity) -> FC2, with the FCs as 1x1 convs over a 1x1 frame."""
+    x = np.array([1.0, 2.0, 3.0, 4.0], np.float32).reshape(1, 1, 2, 2)
+    mean = oracle.gpool(x).reshape(1, 1, 1, 2)
+    assert mean.ravel().tolist() == [2.0, 3.0]
+    fc1 = conv(2, 2, 1, 1, act="relu")
+    got = oracle.conv_aicpu(fc1, mean, np.array([1, 1, 1, -2], np.float32), np.zeros(2, np.float32))
+    assert got.ravel().tolist() == [5.0, 0.0]
+    ident = oracle.conv_aicpu(conv(2, 2, 1, 1), mean, np.array([1, 0, 0, 1], np.float32), np.zeros(2, np.float32))
+    got = oracle.conv_aicpu(conv(2, 2, 1, 1), ident, np.array([2, 0, 0, 2], np.float32), np.ones(2, np.float32))
+    assert got.ravel().tolist() == [5.0, 7.0]
