@@ -24,6 +24,7 @@ Nodes (``Node.kind``):
   concat   channel concat of ins                       SwOp::Concat
   split    outs = channel slices of ins[0] (views)     Split (an alias)
   chcopy   out = act(ins[0][coff : coff + c])          SwOp::Chcopy / Act
+  view     out = ins[0][coff : coff + c], no copy       SwTensor.alias
 """
 from __future__ import annotations
 
@@ -92,7 +93,7 @@ def infer_shapes(nodes: Sequence[Node], inputs: Dict[str, Tuple[int, int, int]])
                 raise ValueError(f"split of {nd.ins[0]}: parts {nd.parts} != {s0[2]} channels")
             for name, c in zip(nd.out, nd.parts):
                 sh[name] = (s0[0], s0[1], c)
-        elif k == "chcopy":
+        elif k in ("chcopy", "view"):
             coff, c = nd.parts
             if coff + c > s0[2]:
                 raise ValueError(f"{nd.out}: channels past the source")
@@ -162,12 +163,14 @@ class NetModel:
                 alloc(name, zero=name in self.states)
             for nd in self.nodes:
                 rec = _Rec(nd)
-                if nd.kind == "split":
-                    base, coff0 = self._base(nd.ins[0])
-                    coff = coff0
-                    for name, c in zip(nd.out, nd.parts):
-                        self.alias[name] = (base, coff, c)
-                        coff += c
+                if nd.kind in ("split", "view"):
+                    base, coff = self._base(nd.ins[0])
+                    if nd.kind == "view":
+                        self.alias[nd.out] = (base, coff + nd.parts[0], nd.parts[1])
+                    else:
+                        for name, c in zip(nd.out, nd.parts):
+                            self.alias[name] = (base, coff, c)
+                            coff += c
                     self.recs.append(rec)
                     continue
                 alloc(nd.out, zero=nd.out in self.cpad)
@@ -226,7 +229,7 @@ class NetModel:
         for r in self.recs:
             nd = r.node
             k = nd.kind
-            if k == "split":
+            if k in ("split", "view"):
                 continue
             if k == "conv":
                 base, _ = self._base(nd.ins[0])

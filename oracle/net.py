@@ -44,7 +44,7 @@ def _shapes(nodes, inputs):
         elif k == "split":
             for name, c in zip(nd.out, nd.parts):
                 sh[name] = (s0[0], s0[1], c)
-        elif k == "chcopy":
+        elif k in ("chcopy", "view"):
             sh[nd.out] = (s0[0], s0[1], nd.parts[1])
     return sh
 
@@ -115,6 +115,9 @@ class OracleNet:
                 out[name] = np.ascontiguousarray(x[..., coff:coff + c])
                 coff += c
             return out
+        if k == "view":
+            coff, c = nd.parts
+            return {nd.out: np.ascontiguousarray(x[..., coff:coff + c])}
         if k == "chcopy":
             coff, c = nd.parts
             y = new(nd.out)

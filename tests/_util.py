@@ -43,3 +43,32 @@ def oracle_conv(op, x, w, b, res):
     if res is not None:
         scale = scale + np.abs(res)
     return want, scale
+
+
+def check_net_ops(model, onet, weights, label=""):
+    """Re-run every node of the step `model` (a NetModel) just recorded on
+    the oracle net, from the GPU's own inputs to that node, and hold each op
+    to its own bar: convs to the normalised tolerance of their math, glue
+    ops bit-exact.  Returns the set of (kernel, math) the convs used."""
+    kinds = set()
+    for rec in model.recs:
+        nd = rec.node
+        if nd.kind in ("split", "view"):
+            continue
+        ins = {i: model.tensor(i).cpu().numpy() for i in (*nd.ins, nd.res) if i is not None and i in model.shapes}
+        want = onet.run_node(nd, ins)[nd.out]
+        got = model.tensor(nd.out).cpu().numpy()
+        assert got.shape == want.shape, nd.out
+        if nd.kind == "conv":
+            wt, b = weights[nd.out]
+            scale = oracle.dot_scale(nd.conv, ins[nd.ins[0]], wt, b)
+            if nd.res is not None:
+                scale = scale + np.abs(ins[nd.res])
+            tol = TOL_TF32 if rec.plan.math == "tf32" else TOL_FFMA
+            err = normalised_error(got, want, scale)
+            assert err <= tol, f"{label} {nd.out} ({rec.plan.kernel}/{rec.plan.math}): {err:.2e} > {tol}"
+            kinds.add((rec.plan.kernel, rec.plan.math))
+        else:
+            assert np.array_equal(got, want), \
+                f"{label} {nd.out} ({nd.kind}): {float(np.max(np.abs(got - want))):.3e}"
+    return kinds

@@ -14,11 +14,10 @@ import numpy as np
 import pytest
 import torch
 
-import oracle
 from ai_engine_b200 import rvm
 from ai_engine_b200.net import NetModel
 from oracle.net import OracleNet
-from tests._util import TOL_FFMA, TOL_TF32, normalised_error
+from tests._util import check_net_ops
 
 pytestmark = pytest.mark.gpu
 
@@ -53,26 +52,7 @@ def test_rvm_op_by_op(cuda_ok, net, math):
         m.bufs["src"].copy_(torch.from_numpy(x[t]))
         m.record()
         torch.cuda.synchronize()
-        for rec in m.recs:
-            nd = rec.node
-            if nd.kind == "split":
-                continue
-            ins = {i: _host(m, i) for i in (*nd.ins, nd.res) if i is not None and i in m.shapes}
-            want = o.run_node(nd, ins)[nd.out]
-            got = _host(m, nd.out)
-            assert got.shape == want.shape, nd.out
-            if nd.kind == "conv":
-                wt, b = wts[nd.out]
-                scale = oracle.dot_scale(nd.conv, ins[nd.ins[0]], wt, b)
-                if nd.res is not None:
-                    scale = scale + np.abs(ins[nd.res])
-                tol = TOL_TF32 if rec.plan.math == "tf32" else TOL_FFMA
-                err = normalised_error(got, want, scale)
-                assert err <= tol, f"step {t} {nd.out} ({rec.plan.kernel}/{rec.plan.math}): {err:.2e} > {tol}"
-                kinds.add((rec.plan.kernel, rec.plan.math))
-            else:
-                assert np.array_equal(got, want), f"step {t} {nd.out} ({nd.kind}): " \
-                    f"{float(np.max(np.abs(got - want))):.3e}"
+        kinds |= check_net_ops(m, o, wts, f"step {t}")
         m.advance()
     if math == "auto":
         assert ("pw", "tf32") in kinds and ("igemm", "tf32") in kinds and ("dw", "ffma") in kinds, kinds

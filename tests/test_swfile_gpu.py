@@ -1,0 +1,62 @@
+"""ai_engine's shipped segmentation model (segm_r11_160x288.sw, real
+weights) on the GPU through the .sw reader and the node executor, against
+the ai-cpu restatement -- the counterpart of ai-gpu-runtime's graph-exec
+gate (crates/ai-gpu-runtime/tests/graph_exec.rs:12-72: seeded input
+XorShift32(77), every output within max abs error 2e-3 of the CPU
+reference)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from ai_engine_b200.net import NetModel
+from ai_engine_b200.swfile import load_sw
+from oracle.net import OracleNet
+from tests._util import check_net_ops
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.fixture(scope="module")
+def model():
+    fx = np.load(os.path.join(HERE, "golden", "segm_r11.npz"))
+    return load_sw(fx["sw"].tobytes()), fx
+
+
+def _input(sw, seeds):
+    (inp, (h, w, c)), = sw.inputs.items()
+    return inp, np.stack([oracle.XorShift32(s).vec_f32(h * w * c).reshape(h, w, c) for s in seeds])
+
+
+@pytest.mark.parametrize("math", ["ffma", "auto"])
+def test_segm_r11_graph_exec_gate(cuda_ok, model, math):
+    """The reference's bar, 2e-3 max abs error on the logits, on the seed-77
+    frame (against the committed golden output) and a second frame (against
+    the oracle run here), batched."""
+    sw, fx = model
+    inp, x = _input(sw, [int(fx["seed"]), 78])
+    m = NetModel(sw.nodes, sw.weights, 2, sw.inputs, sw.outputs, sw.states, sw.consts, math=math)
+    out = m.step({inp: torch.from_numpy(x).cuda()})[sw.outputs[0]].cpu().numpy()
+    err0 = float(np.max(np.abs(out[0] - fx["output"])))
+    o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
+    want1 = o.step({inp: x[1:]}, {})[sw.outputs[0]][0]
+    err1 = float(np.max(np.abs(out[1] - want1)))
+    assert err0 < 2e-3 and err1 < 2e-3, (math, err0, err1)
+
+
+def test_segm_r11_op_by_op(cuda_ok, model):
+    """Every op of the shipped model on the default (TF32 tensor-core) path
+    within its own bar, from the GPU's inputs to it."""
+    sw, fx = model
+    inp, x = _input(sw, [int(fx["seed"])])
+    m = NetModel(sw.nodes, sw.weights, 1, sw.inputs, sw.outputs, sw.states, sw.consts)
+    m.bufs[inp].copy_(torch.from_numpy(x))
+    m.record()
+    torch.cuda.synchronize()
+    o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
+    kinds = check_net_ops(m, o, sw.weights, "segm_r11")
+    assert ("pw", "tf32") in kinds and ("dw", "ffma") in kinds, kinds
