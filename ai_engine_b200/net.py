@@ -311,15 +311,18 @@ class NetModel:
         self.advance()
 
     def step(self, inputs: Dict[str, torch.Tensor], stream=None) -> Dict[str, torch.Tensor]:
-        """Copy the step's inputs in, run one step eagerly, return the outputs
-        (device tensors, valid until the next step)."""
+        """Copy the step's inputs in, run one step eagerly, return copies of
+        the outputs (device tensors the next step does not overwrite)."""
         for k, v in inputs.items():
             self.bufs[k].copy_(v)
         self.record(stream)
-        outs = {k: self.tensor(k) for k in self.outputs}
-        outs = {k: (v.clone() if k in self.states.values() else v) for k, v in outs.items()}
+        outs = {k: self.tensor(k).clone() for k in self.outputs}
         self.advance()
         return outs
+
+    def tf32_convs(self):
+        """Names of the convs that run on the TF32 tensor cores."""
+        return {r.node.out for r in self.recs if r.plan is not None and r.plan.math == "tf32"}
 
     def release(self):
         self.graphs.clear()

@@ -10,6 +10,12 @@ t fed back as step t + 1's state inputs.
 
 ``run_node`` runs one node on given input arrays, so a test can feed the
 oracle the GPU's own inputs of each op and compare op by op.
+
+``tf32`` names convs whose operands the oracle first truncates to TF32 (the
+low 13 mantissa bits of every activation and weight cleared), the operand
+format the GPU's tensor cores read fp32 data in.  With the GPU's own TF32
+convs named, the oracle chain follows the GPU's arithmetic closely enough
+for end-to-end comparisons of deep graphs at a tight bound.
 """
 from __future__ import annotations
 
@@ -18,6 +24,12 @@ from typing import Dict, Optional, Sequence, Tuple
 import numpy as np
 
 from . import Plan, avgpool, binary, channel_copy, gpool, lib, mix, resize_bilinear
+
+
+def tf32_truncate(a: np.ndarray) -> np.ndarray:
+    """fp32 -> the fp32 value of its TF32 truncation (10 mantissa bits kept)."""
+    b = np.ascontiguousarray(a, np.float32).view(np.uint32) & np.uint32(0xFFFFE000)
+    return b.view(np.float32)
 
 
 def _shapes(nodes, inputs):
@@ -52,8 +64,9 @@ def _shapes(nodes, inputs):
 class OracleNet:
     def __init__(self, nodes: Sequence, weights: Dict[str, Tuple[np.ndarray, np.ndarray]],
                  inputs: Dict[str, Tuple[int, int, int]], states: Optional[Dict[str, str]] = None,
-                 consts: Optional[Dict[str, np.ndarray]] = None):
+                 consts: Optional[Dict[str, np.ndarray]] = None, tf32=()):
         lib()
+        self.tf32 = set(tf32)
         self.nodes = list(nodes)
         self.states = dict(states or {})
         self.inputs = dict(inputs)
@@ -64,6 +77,8 @@ class OracleNet:
             if nd.kind == "conv":
                 h, w, _ = self.shapes[nd.ins[0]]
                 wt, b = weights[nd.out]
+                if nd.out in self.tf32:
+                    wt = tf32_truncate(wt)
                 self.plans[nd.out] = Plan(nd.conv, h, w, wt, b, True, nd.res is not None)
 
     def run_node(self, nd, t: Dict[str, np.ndarray], threads: int = 1) -> Dict[str, np.ndarray]:
@@ -78,6 +93,8 @@ class OracleNet:
 
         if k == "conv":
             res = t[nd.res] if nd.res is not None else None
+            if nd.out in self.tf32:
+                x = tf32_truncate(x)
             return {nd.out: self.plans[nd.out].run(x, res, threads)}
         if k == "binary":
             y = new(nd.out)

@@ -58,11 +58,20 @@ def test_rvm_op_by_op(cuda_ok, net, math):
         assert ("pw", "tf32") in kinds and ("igemm", "tf32") in kinds and ("dw", "ffma") in kinds, kinds
 
 
-@pytest.mark.parametrize("math,tol", [("auto", 3e-2), ("ffma", 1e-3)])
-def test_rvm_end_to_end(cuda_ok, net, math, tol):
-    """Three recurrent steps, each chain feeding back its own state."""
+@pytest.mark.parametrize("math,emulate,tol,mean_tol", [("ffma", False, 1e-3, 1e-4), ("auto", True, 2e-2, 1e-3),
+                                                        ("auto", False, 0.3, 2e-2)])
+def test_rvm_end_to_end(cuda_ok, net, math, emulate, tol, mean_tol):
+    """Three recurrent steps, each chain feeding back its own state.  The
+    FP32 (FFMA) path stays within 1e-3 of the fp32 oracle.  On the TF32
+    path the chain departs from fp32 by the operand format itself (a CPU
+    emulation of TF32 operand truncation departs by 0.07-0.18 max / 0.003-
+    0.008 mean on these outputs), so it is held to 2e-2 against the oracle
+    with the same convs' operands truncated to TF32, and loosely against
+    the plain fp32 oracle."""
+    g, wts = net
     n = 2
-    m, o = _models(net, n, math)
+    m = NetModel(g, wts, n, rvm.inputs(H, W), rvm.OUTPUTS, rvm.STATES, rvm.consts(), math=math)
+    o = OracleNet(g, wts, rvm.inputs(H, W), rvm.STATES, rvm.consts(), tf32=m.tf32_convs() if emulate else ())
     x = rvm.synthetic_frames(n, 3, H, W, seed=22)
     st = o.zero_state(n)
     for t in range(3):
@@ -70,8 +79,10 @@ def test_rvm_end_to_end(cuda_ok, net, math, tol):
         want = o.step({"src": x[t]}, st)
         st = {k: want[v] for k, v in rvm.STATES.items()}
         for k in rvm.OUTPUTS:
-            err = float(np.max(np.abs(got[k].cpu().numpy() - want[k])))
-            assert err <= tol, f"step {t} {k}: max abs error {err:.2e} > {tol}"
+            d = np.abs(got[k].cpu().numpy() - want[k])
+            err, mean = float(d.max()), float(d.mean())
+            assert err <= tol and mean <= mean_tol, f"step {t} {k}: max abs error {err:.2e} (bound {tol}), " \
+                f"mean {mean:.2e} (bound {mean_tol})"
     p = got["pha"].cpu().numpy()
     assert p.min() >= 0.0 and p.max() <= 1.0 and got["pha"].shape == (n, H, W, 1) and got["fgr"].shape == (n, H, W, 3)
 
