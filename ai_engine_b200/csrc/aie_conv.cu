@@ -1097,6 +1097,42 @@ extern "C" int aie_channel_copy(uint32_t n, uint32_t px, uint32_t c, aie_tview i
     return AIE_OK;
 }
 
+extern "C" int aie_concat(uint32_t n, uint32_t px, uint32_t nparts, const aie_tview *parts, const uint32_t *part_c,
+                          uint32_t out_c, aie_tview out, void *stream)
+{
+    int s;
+    if ((s = elem_sizes(n, px, out_c, "concat"))) return s;
+    if (!parts || !part_c) return fail(AIE_E_INVALID, "concat: null part list");
+    if (nparts < 1 || nparts > (uint32_t)kConcatMax)
+        return fail(AIE_E_INVALID, "concat: %u parts (1..%d)", nparts, kConcatMax);
+    ConcatArgs a{};
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < nparts; i++) {
+        if (!part_c[i]) return fail(AIE_E_INVALID, "concat: part %u has no channels", i);
+        if ((s = make_eview(parts[i], part_c[i], "concat part", &a.part[i]))) return s;
+        a.poff[i] = (int)total;
+        total += part_c[i];
+    }
+    if (total > out_c) return fail(AIE_E_INVALID, "concat: parts hold %llu channels, out_c is %u",
+                                   (unsigned long long)total, out_c);
+    a.poff[nparts] = (int)total;
+    a.nparts = (int)nparts;
+    EView y;
+    if ((s = make_eview(out, out_c, "concat out", &y))) return s;
+    a.y = (float *)y.p;
+    a.y_stride = y.stride;
+    a.y_coff = y.coff;
+    a.c_out = (int)out_c;
+    a.groups = (int)((out_c + 3) / 4);
+    if ((uint64_t)n * px * a.groups >= (1ull << 31)) return fail(AIE_E_UNSUPPORTED, "concat larger than 2^31 groups");
+    a.Q = n * px;
+    a.y_vec = out_c % 4 == 0 && eview_vec(y);
+    concat_kernel<<<elem_grid((long long)a.Q * a.groups), 256, 0, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "concat launch");
+    return AIE_OK;
+}
+
 extern "C" int aie_selftest_wait_timeout(uint32_t timeout_us, void *stream)
 {
     if (timeout_us == 0 || timeout_us > 2000000) return fail(AIE_E_INVALID, "timeout must be 1..2000000 us");

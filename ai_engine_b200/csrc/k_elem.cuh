@@ -312,3 +312,63 @@ __global__ void __launch_bounds__(256) chcopy_kernel(CopyArgs a)
 }
 
 }  // namespace aie
+
+namespace aie {
+
+// Channel concat of up to kConcatMax parts into one output view, one pass:
+// a thread owns one output pixel's group of four channels, gathers them
+// from whichever parts hold them and writes the group as one 16-byte store
+// where the output allows.  Lanes past the parts' total (the zero padding
+// of a buffer rounded up to a multiple of 4 channels) are written as zero.
+// Compared with one copy per part, every output row is written once and
+// whole: a part narrower than a 32-byte sector (the 3-channel frame in
+// RVM's decoder concats) no longer makes the L2 fill and write back partial
+// sectors.  (SwOp::Concat, crates/ai-core/src/format/model.rs:156-160.)
+constexpr int kConcatMax = 8;
+
+struct ConcatArgs {
+    EView part[kConcatMax];
+    int poff[kConcatMax + 1];   // first output channel of each part; poff[nparts] = parts' total
+    int nparts;
+    float *y;
+    long long y_stride;
+    int y_coff;
+    unsigned Q;                 // n * px (< 2^31 / groups)
+    int c_out, groups;          // output channels (>= the parts' total), ceil(c_out / 4)
+    bool y_vec;
+};
+
+__global__ void __launch_bounds__(256) concat_kernel(ConcatArgs a)
+{
+    const unsigned total = a.Q * (unsigned)a.groups;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const unsigned q = i / (unsigned)a.groups;
+        const int ch0 = (int)(i - q * (unsigned)a.groups) * 4;
+        float r[4];
+        int p = 0;
+        while (p + 1 < a.nparts && a.poff[p + 1] <= ch0) p++;
+        const int lc = ch0 - a.poff[p];
+        const EView &v = a.part[p];
+        if (ch0 + 4 <= a.poff[p + 1] && ((uintptr_t)(v.p + (long long)q * v.stride + v.coff + lc) & 15) == 0) {
+            const float4 t = ld_view4(v, q, lc);
+            r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int ch = ch0 + k;
+                int pp = p;
+                while (pp < a.nparts && a.poff[pp + 1] <= ch) pp++;
+                r[k] = pp < a.nparts ? ld_view(a.part[pp], q, ch - a.poff[pp]) : 0.0f;
+            }
+        }
+        float *yp = a.y + (long long)q * a.y_stride + a.y_coff + ch0;
+        if (a.y_vec) {
+            *reinterpret_cast<float4 *>(yp) = make_float4(r[0], r[1], r[2], r[3]);
+        } else {
+            const int nc = min(4, a.c_out - ch0);
+            for (int k = 0; k < nc; k++) yp[k] = r[k];
+        }
+    }
+}
+
+}  // namespace aie

@@ -130,3 +130,17 @@ def channel_copy(x: ViewLike, out: ViewLike, act: str = "none", stream=None) -> 
     n, px, c = _same(x, out)
     check(_lib.load().aie_channel_copy(n, px, c, x.tview(), ACT_ID[act], out.tview(), _stream(stream)),
           "aie_channel_copy")
+
+
+def concat(parts: Sequence[ViewLike], out: ViewLike, stream=None) -> None:
+    """Channel concat of `parts` into `out` in one pass (SwOp::Concat); `out`
+    may be wider than the parts' total, its trailing lanes are zeroed."""
+    ps = [_v(p) for p in parts]
+    out = _v(out)
+    for p in ps:
+        if (p.frames, p.px) != (out.frames, out.px):
+            raise ValueError("concat parts differ in frames or pixels from the output")
+    arr = (_lib.TView * len(ps))(*[p.tview() for p in ps])
+    cs = (C.c_uint32 * len(ps))(*[p.c for p in ps])
+    check(_lib.load().aie_concat(out.frames, out.px, len(ps), arr, cs, out.c, out.tview(), _stream(stream)),
+          "aie_concat")

@@ -258,12 +258,7 @@ class NetModel:
                 resize_bilinear(self.tensor_for_resize(nd.ins[0]), nd.size[0], nd.size[1], out=self.bufs[nd.out],
                                 stream=stream)
             elif k == "concat":
-                out = self.bufs[nd.out]
-                coff = 0
-                for part in nd.ins:
-                    c = self.shapes[part][2]
-                    ew.channel_copy(self.view(part), ew.ChView(out, coff, c), stream=stream)
-                    coff += c
+                ew.concat([self.view(p) for p in nd.ins], ew.ChView(self.bufs[nd.out]), stream=stream)
             elif k == "chcopy":
                 coff, c = nd.parts
                 b, boff = self._base(nd.ins[0])

@@ -7,8 +7,11 @@ Frames shard across GPUs with no collective on the hot path (weak
 scaling); the only collective is a max-reduce of the timings.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload rvm [--streams S]
 
-Prints one JSON line (rank 0).  --impl reference times the CPU
+Prints one JSON line (rank 0).  ``--workload rvm`` measures the recurrent
+matting net instead (144x256, S = 1024 streams sharded across the GPUs, one
+step = one frame of every stream, recurrent state resident on the GPU).  --impl reference times the CPU
 restatement of ai_engine's ai-cpu path on all host cores (the Rust
 reference itself cannot be built here: no Rust toolchain).
 """
@@ -212,6 +215,172 @@ def run_reference(args, rank):
     return 0
 
 
+# ------------------------------------------------------ config 5: RVM net ---
+
+RVM_METRIC = "RVM 144x256 frames/s, 1024 streams x 8 frames"
+
+
+def rvm_cpu_baseline(threads: int, min_seconds: float = 10.0):
+    """The oracle chain of the RVM net, one stream-frame per core at a time
+    (ai-cpu throughput mode), zero recurrent state: (frames/s, s, frames)."""
+    import concurrent.futures as cf
+
+    from ai_engine_b200 import rvm
+    from oracle.net import OracleNet
+    g = rvm.build_graph()
+    o = OracleNet(g, rvm.init_weights(g), rvm.inputs(), rvm.STATES, rvm.consts())
+    x = rvm.synthetic_frames(threads, 1, seed=1)[0]
+    st = o.zero_state(1)
+    o.step({"src": x[:1]}, st)  # warm-up
+    done = 0
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        while time.perf_counter() - t0 < min_seconds:
+            list(ex.map(lambda i: o.step({"src": x[i:i + 1]}, st), range(threads)))
+            done += threads
+    dt = time.perf_counter() - t0
+    return done / dt, dt, done
+
+
+def run_rvm(args, world, rank, dev):
+    """1024 independent streams sharded across the GPUs,
+    each GPU stepping its streams' next frame as one batch with the ConvGRU
+    state resident in HBM (strong scaling: the stream count is fixed)."""
+    import torch
+    import torch.distributed as dist
+
+    from ai_engine_b200 import rvm
+    from ai_engine_b200.net import NetModel
+
+    if args.streams % world:
+        raise SystemExit(f"{args.streams} streams do not split over {world} GPUs")
+    n = args.streams // world
+    g = rvm.build_graph()
+    model = NetModel(g, rvm.init_weights(g), n, rvm.inputs(), rvm.OUTPUTS, rvm.STATES, rvm.consts(),
+                     math=args.math, device=dev)
+    frames = torch.from_numpy(rvm.synthetic_frames(n, 2, seed=200 + rank)).pin_memory()  # two frames, alternated
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    model.bufs["src"].copy_(frames[0])
+    for _ in range(max(args.warmup, 3)):
+        model.record()
+        model.advance()
+    model.capture()
+    for _ in range(max(args.warmup, 3)):
+        model.replay()
+    torch.cuda.synchronize()
+    # ---- timed region: K steps replayed from the captured graphs, frames resident
+    sampler = ClockSampler(dev.index)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = max_over_ranks(e0.elapsed_time(e1))
+    value = n * world * args.steps / (total_ms / 1000.0)
+    # ---- per-op eager timing (dominant op)
+    recs = [r for r in model.recs if r.node.kind not in ("split", "view")]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(recs) + 1)]
+    saved = model.recs
+    evs[0].record(stream)
+    for i, r in enumerate(recs):
+        model.recs = [r]
+        model.record()
+        evs[i + 1].record(stream)
+    model.recs = saved
+    torch.cuda.synchronize()
+    per_op = [evs[i].elapsed_time(evs[i + 1]) for i in range(len(recs))]
+    model.advance()
+    # ---- end to end: per step, the pinned frame batch in, the step, fgr + pha out
+    fgr_h = torch.empty((n, rvm.H, rvm.W, 3)).pin_memory()
+    pha_h = torch.empty((n, rvm.H, rvm.W, 1)).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for k in range(args.steps):
+        model.bufs["src"].copy_(frames[k % 2], non_blocking=True)
+        model.replay()
+        fgr_h.copy_(model.bufs["fgr"], non_blocking=True)
+        pha_h.copy_(model.bufs["pha"], non_blocking=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    e2e_value = n * world * args.steps / (max_over_ranks(t0.elapsed_time(t1)) / 1000.0)
+    act_bytes = sum(b.numel() * 4 for b in model.bufs.values())
+    model.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    pk = peaks()
+    i = max(range(len(recs)), key=lambda j: per_op[j])
+    top = recs[i]
+    sec = per_op[i] / 1000.0
+    if top.plan is not None:
+        fl, by = top.plan.flops, top.plan.min_bytes
+    else:
+        nd = top.node
+        outs = [nd.out]
+        by = 4 * n * sum(int(np.prod(model.shapes[t])) for t in (*[x for x in nd.ins if x in model.shapes], *outs))
+        fl = 0
+    roof = {"bound": "hbm", "achieved": by / sec / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
+    ridge = pk["bf16_tflops"] / 2.0 * 1e12 / (pk["hbm_gbs"] * 1e9)
+    if top.plan is not None and top.plan.math == "tf32" and fl / max(by, 1) >= ridge:
+        roof = {"bound": "tensor", "achieved": fl / sec / 1e12, "peak": pk["bf16_tflops"] / 2.0, "unit": "TFLOP/s"}
+    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    roof["achieved"] = round(roof["achieved"], 3)
+    roof["traffic"] = None
+    roof["kernel"] = f"{top.node.out} ({top.node.kind}" + (f" {top.plan.kernel}/{top.plan.math})" if top.plan else ")")
+    roof["share"] = round(per_op[i] / sum(per_op), 4)
+    line = {
+        "metric": RVM_METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "tf32" if args.math in ("auto", "tf32") else "f32",
+        "data": "synthetic",
+        "config": {"workload": "RVM-style matting net 144x256 (BASELINE config 5), ConvGRU state carried",
+                   "streams": args.streams, "streams_per_gpu": n, "h": rvm.H, "w": rvm.W,
+                   "parallelism": f"streams sharded over {world} GPU(s)", "math": args.math,
+                   "l2": f"inputs larger than L2 ({frames[0].numel() * 4 / 1e6:.0f} MB of frames, "
+                         f"{act_bytes / 1e9:.1f} GB of activations per step per GPU)",
+                   "conv_gflop_per_frame": round(model.conv_flops / n / 1e9, 4)},
+        "conv_tflops": round(model.conv_flops * world / (total_ms / args.steps / 1000.0) / 1e12, 3),
+        "roofline": roof,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(frames[0].numel() * 4),
+                "d2h_bytes_per_step": int((fgr_h.numel() + pha_h.numel()) * 4)},
+        "gpu_launches": len(recs) * args.steps,
+        "clocks": sampler.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, dt, done = rvm_cpu_baseline(threads)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": f"{done} stream-frames of the same net, one per core, {dt:.1f} s on "
+                                          f"{cpu_model_name()}"}
+    if args.layers:
+        for r, ms in sorted(zip(recs, per_op), key=lambda t: -t[1]):
+            kern = f"{r.plan.kernel}/{r.plan.math}" if r.plan is not None else r.node.kind
+            print(f"{r.node.out:16s} {kern:14s} {ms * 1000:9.1f} us", file=sys.stderr)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # --------------------------------------------------------------- GPU arm ---
 
 def main():
@@ -228,6 +397,9 @@ def main():
     ap.add_argument("--fuse-resize", type=int, default=None, choices=[0, 1],
                     help="fold each resize that only feeds a conv residual into that conv (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
+    ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm"],
+                    help="segnet: BASELINE config 4 (default); rvm: the recurrent matting net of config 5")
+    ap.add_argument("--streams", type=int, default=1024, help="rvm: video streams over all GPUs")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -244,6 +416,8 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.workload == "rvm":
+        return run_rvm(args, world, rank, dev)
 
     from ai_engine_b200 import segnet
     from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv

@@ -333,6 +333,15 @@ AIE_API int aie_avgpool(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, uint32
 AIE_API int aie_channel_copy(uint32_t n, uint32_t px, uint32_t c, aie_tview in, int32_t act, aie_tview out,
                              void *stream);
 
+/* Channel concat of nparts (1..8) views, part i holding part_c[i] channels,
+ * into out[q, 0:out_c] in one pass: SwOp::Concat (crates/ai-core/src/
+ * format/model.rs:156-160) and the conv's concat-into-conv parts
+ * (Conv.srcs, model.rs:83-86; SrcView, crates/ai-gpu/src/kernels/common/
+ * source.rs:17-80).  out_c may exceed the parts' total: those trailing
+ * lanes are written as zero (a buffer padded to a multiple of 4 channels). */
+AIE_API int aie_concat(uint32_t n, uint32_t px, uint32_t nparts, const aie_tview *parts, const uint32_t *part_c,
+                       uint32_t out_c, aie_tview out, void *stream);
+
 /* Human-readable status, and the detail message of this thread's last
  * failure (copied into buf, NUL-terminated; returns its full length). */
 AIE_API const char *aie_status_string(int status);

@@ -209,3 +209,18 @@ def test_glue_entry_points_reject_bad_arguments(lib):
     assert lib.aie_channel_copy(1, 4, 4, good, 11, good, None) == inv
     assert lib.aie_channel_copy(1, 4, 4, good, 0, TV(C.cast(buf, C.c_void_p), 4, 1), None) == inv
     assert "pixel stride" in _lib.last_error()
+
+
+def test_concat_rejects_bad_arguments(lib):
+    TV = _lib.TView
+    buf = (C.c_float * 64)()
+    good = TV(C.cast(buf, C.c_void_p), 0, 0)
+    parts = (TV * 2)(good, good)
+    cs = (C.c_uint32 * 2)(2, 2)
+    assert lib.aie_concat(1, 4, 0, parts, cs, 4, good, None) == -2
+    assert lib.aie_concat(1, 4, 9, parts, cs, 4, good, None) == -2
+    assert lib.aie_concat(1, 4, 2, parts, cs, 3, good, None) == -2      # parts wider than the output
+    assert "out_c" in _lib.last_error()
+    cs0 = (C.c_uint32 * 2)(2, 0)
+    assert lib.aie_concat(1, 4, 2, parts, cs0, 4, good, None) == -2
+    assert lib.aie_concat(1, 4, 2, None, cs, 4, good, None) == -2

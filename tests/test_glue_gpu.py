@@ -167,3 +167,22 @@ def test_glue_rejects_bad_views(cuda_ok):
         ew.binary("add", x, torch.zeros((1, 2, 2, 4), device="cuda"), x)
     with pytest.raises(ValueError):
         ew.binary("add", x, torch.zeros(3, device="cuda"), x, kind="cvec")
+
+
+@pytest.mark.parametrize("widths,pad", [((128, 40, 3), 1), ((32, 3), 1), ((16, 16), 0), ((5, 7, 4), 0)])
+def test_concat(cuda_ok, widths, pad):
+    """aie_concat: the parts in one pass, trailing padding lanes zeroed;
+    one part given as a channel view of a wider tensor."""
+    rng = XorShift32(7601 + sum(widths))
+    n, h, w = 2, 3, 5
+    parts = [_rand(rng, n, h, w, c) for c in widths]
+    wide = _rand(rng, n, h, w, widths[0] + 6)
+    wide[..., 2:2 + widths[0]] = parts[0]
+    want = np.concatenate(parts, -1)
+    cout = want.shape[-1] + pad
+    out = torch.full((n, h, w, cout), 7.0, device="cuda")
+    gp = [ew.ChView(torch.from_numpy(wide).cuda(), 2, widths[0])] + [torch.from_numpy(p).cuda() for p in parts[1:]]
+    ew.concat(gp, out)
+    got = out.cpu().numpy()
+    _check(got[..., :want.shape[-1]], want)
+    assert not got[..., want.shape[-1]:].any()
