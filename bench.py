@@ -359,8 +359,8 @@ def run_rvm(args, world, rank, dev):
                    "parallelism": f"streams sharded over {world} GPU(s)", "math": args.math,
                    "l2": f"inputs larger than L2 ({frames[0].numel() * 4 / 1e6:.0f} MB of frames, "
                          f"{act_bytes / 1e9:.1f} GB of activations per step per GPU)",
-                   "conv_gflop_per_frame": round(model.conv_flops / n / 1e9, 4)},
-        "conv_tflops": round(model.conv_flops * world / (total_ms / args.steps / 1000.0) / 1e12, 3),
+                   "conv_gflop_per_frame": round(rvm.conv_flops_per_frame() / 1e9, 4)},
+        "conv_tflops": round(rvm.conv_flops_per_frame() * n * world / (total_ms / args.steps / 1000.0) / 1e12, 3),
         "roofline": roof,
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(frames[0].numel() * 4),
                 "d2h_bytes_per_step": int((fgr_h.numel() + pha_h.numel()) * 4)},
