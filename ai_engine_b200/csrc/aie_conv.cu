@@ -536,14 +536,15 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
     if (p->kernel == AIE_KERNEL_DW) {
         const aie_conv_desc &d = p->d;
         const bool blocked = d.cout % 4 == 0 && a.vec_x && a.vec_y && a.x_coff % 4 == 0 && a.y_coff % 4 == 0 &&
-                             (!a.res || (a.r_stride % 4 == 0 && a.r_coff % 4 == 0)) && d.dil == 1 &&
+                             (!a.res || (a.r_stride % 4 == 0 && a.r_coff % 4 == 0)) &&
+                             (d.dil == 1 || (d.dil == 2 && d.sh == 1)) &&
                              d.kh == d.kw && d.sh == d.sw && (d.kh == 3 || d.kh == 5) && (d.sh == 1 || d.sh == 2) &&
                              (long long)d.n * p->oh * ((p->ow + 3) / 4) * (d.cout / 4) + 256 < (1ll << 31);
         // Large frames take the shared-memory halo tiles (8 x 16 output
         // pixels at stride 1, else 8 x 8; one 32-channel slice per CTA);
         // small frames (the deep 10x18 / 20x36 layers) would waste most of a
         // tile and re-read wide halos, and keep the register-blocked kernel.
-        const bool tiled = blocked && p->oh >= 40 && p->ow >= 64;
+        const bool tiled = blocked && d.dil == 1 && p->oh >= 40 && p->ow >= 64;
         if (tiled) {
             DwTile tg;
             const bool wide = d.sh == 1 && p->ow > 12;
@@ -588,10 +589,14 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
             const long long threads = (long long)d.n * p->oh * gd.segs_per_row * gd.cg;
             const unsigned grid = (unsigned)((threads + 255) / 256);
 #define AIE_DW(S_, K_, ST_) dw_block_kernel<S_, K_, ST_, PB><<<grid, 256, 0, s>>>(a, gd)
-#define AIE_DW2(S_)                                            \
-    if (d.kh == 3 && d.sh == 1) AIE_DW(S_, 3, 1);              \
-    else if (d.kh == 3) AIE_DW(S_, 3, 2);                      \
-    else if (d.sh == 1) AIE_DW(S_, 5, 1);                      \
+#define AIE_DW2(S_)                                                                        \
+    if (d.dil == 2) {                                                                      \
+        if (d.kh == 3) dw_block_kernel<S_, 3, 1, PB, 2><<<grid, 256, 0, s>>>(a, gd);     \
+        else dw_block_kernel<S_, 5, 1, PB, 2><<<grid, 256, 0, s>>>(a, gd);               \
+    }                                                                                      \
+    else if (d.kh == 3 && d.sh == 1) AIE_DW(S_, 3, 1);                                     \
+    else if (d.kh == 3) AIE_DW(S_, 3, 2);                                                  \
+    else if (d.sh == 1) AIE_DW(S_, 5, 1);                                                  \
     else AIE_DW(S_, 5, 2);
             if (p->strict) { AIE_DW2(true) } else { AIE_DW2(false) }
 #undef AIE_DW2

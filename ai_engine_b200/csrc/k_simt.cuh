@@ -1256,7 +1256,7 @@ struct DwGrid {
     FastDiv div_cg, div_segs, div_oh;
 };
 
-template <bool kStrict, int K, int S, int PB>
+template <bool kStrict, int K, int S, int PB, int D = 1>
 __global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, const DwGrid gd)
 {
     const int idx = blockIdx.x * 256 + threadIdx.x;  // < 2^31 (checked on the host)
@@ -1276,11 +1276,11 @@ __global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, const D
     for (int p = 0; p < PB; p++) {
         acc[p][0] = b4.x; acc[p][1] = b4.y; acc[p][2] = b4.z; acc[p][3] = b4.w;
     }
-    constexpr int NJ = (PB - 1) * S + K;  // input columns one row needs
+    constexpr int NJ = (PB - 1) * S + (K - 1) * D + 1;  // input columns one row needs (dilation D)
     const int ixb = ox0 * S - a.pl;
 #pragma unroll
     for (int ky = 0; ky < K; ky++) {
-        const int iy = oy * S - a.pt + ky;
+        const int iy = oy * S - a.pt + ky * D;
         if (iy < 0 || iy >= a.ih) continue;
         const float *row = a.x + ((long long)(img * a.ih + iy) * a.iw) * a.x_stride + a.x_coff + c0;
         float4 wk[K];
@@ -1294,8 +1294,10 @@ __global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, const D
             if (ix >= 0 && ix < a.iw) xv = __ldg(reinterpret_cast<const float4 *>(row + (long long)ix * a.x_stride));
 #pragma unroll
             for (int p = 0; p < PB; p++) {
-                const int kx = j - p * S;
-                if (kx >= 0 && kx < K) {
+                // column j feeds tap kx of pixel p when j = p S + kx D
+                const int r = j - p * S;
+                const int kx = r / D;
+                if (r >= 0 && r % D == 0 && kx < K) {
                     acc[p][0] = madd<kStrict>(acc[p][0], xv.x, wk[kx].x);
                     acc[p][1] = madd<kStrict>(acc[p][1], xv.y, wk[kx].y);
                     acc[p][2] = madd<kStrict>(acc[p][2], xv.z, wk[kx].z);

@@ -951,10 +951,10 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
         return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false);
     if (g->stages < 2) return -2;
-    // narrow k x k tiles (long K loops, N <= 64) are bound by the per-thread
+    // narrow k x k tiles (long K loops, N <= 128) are bound by the per-thread
     // MMA issue cost: two pipelines.  1x1 GEMMs keep one deep ring (their
     // short K loops are bound by load latency, which halved rings expose).
-    g->pipes = (g->igemm && g->bn <= 64 && g->stages >= 4) ? 2u : 1u;
+    g->pipes = (g->igemm && g->bn <= 128 && g->stages >= 4) ? 2u : 1u;
     g->bres_off = g->stages * stage;
     g->out_off = g->bres_off + (g->b_resident ? (uint32_t)bres : 0u);
     g->res_off = res_buf ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;

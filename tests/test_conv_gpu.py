@@ -140,6 +140,20 @@ def test_depthwise_residual_and_dilation(cuda_ok, math):
     check(op, x, wt, b, None, math)
 
 
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("ih,iw,c,k,act,seed", [(9, 16, 672, 5, "hardswish", 5211), (9, 16, 960, 5, "hardswish", 5212),
+                                               (18, 32, 40, 3, "relu", 5213), (11, 13, 24, 5, "none", 5214),
+                                               (7, 6, 8, 3, "relu", 5215)])
+def test_depthwise_dilated_blocked(cuda_ok, math, ih, iw, c, k, act, seed):
+    """Dilation-2 depthwise on the register-blocked kernel (C % 4 == 0,
+    stride 1): RVM's dilated last stage (k5 d2 pad 4 at 9x16, 672 / 960
+    channels) and ragged frames smaller than the dilated window."""
+    p = 2 * (k - 1) // 2
+    op = Conv2d(c, c, k, k, 1, 1, (p, p, p, p), 2, c, act)
+    x, wt, b, res = case_tensors(op, 2, ih, iw, seed, seed % 2 == 0)
+    check(op, x, wt, b, res, math)
+
+
 # ------------------------------------------------------------ implicit GEMM ---
 
 IG_SHAPES = [(36, 64, 3, 16, 3, 2), (24, 32, 16, 24, 3, 1), (40, 64, 20, 32, 3, 1), (17, 23, 6, 8, 3, 2),
