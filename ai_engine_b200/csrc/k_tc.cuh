@@ -491,7 +491,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + ab * a.bn;
-                for (uint32_t k = k0; k < k1; k++, it++) {
+                uint32_t kbi = k0 % a.kblocks;  // K block of iteration k (non-halo order: tap-major)
+                for (uint32_t k = k0; k < k1; k++, it++, kbi = kbi + 1 == a.kblocks ? 0 : kbi + 1) {
                     const uint32_t s = p * RS + it % RS, ph = (it / RS) & 1;
                     if (*abort_flag || !mbar_wait(&sh.full[s], ph)) {
                         report_error(0x01000003);
@@ -512,19 +513,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                     ? smem_u32(smem + a.bres_off + (tap * a.kblocks + kb) * a.b_bytes)
                                                     : sa + a.a_bytes + ky * a.b_bytes;
                             const uint64_t ad = smem_desc_sw128(sa + ky * a.bw * 128), bd = smem_desc_sw128(sb);
-                            for (uint32_t kk = 0; kk < nkk; kk++)
-                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                         (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
+                            if (nkk == kTcBK / 8) {
+#pragma unroll
+                                for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                    mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                             (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
+                            } else {
+#pragma unroll
+                                for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                    if (kk < nkk)
+                                        mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                                 (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
+                            }
                         }
                     } else {
                         const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + kTcABytes;
                         const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
-                        const uint32_t kb = k % a.kblocks;
-                        const uint32_t nkk = kb + 1 == a.kblocks ? kk_last : kTcBK / 8;
-                        for (uint32_t kk = 0; kk < nkk; kk++) {
-                            // advance 8 tf32 = 32 bytes along K inside the swizzle row
-                            mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                     (k > k0 || kk > 0) ? 1u : 0u);
+                        const uint32_t nkk = kbi + 1 == a.kblocks ? kk_last : kTcBK / 8;
+                        // advance 8 tf32 = 32 bytes along K inside the swizzle row
+                        if (nkk == kTcBK / 8) {
+#pragma unroll
+                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                         (k > k0 || kk > 0) ? 1u : 0u);
+                        } else {
+#pragma unroll
+                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                if (kk < nkk)
+                                    mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                             (k > k0 || kk > 0) ? 1u : 0u);
                         }
                     }
                     mma_commit(&sh.empty[s]);
