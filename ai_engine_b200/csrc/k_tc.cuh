@@ -464,10 +464,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0 && p < a.pipes) {
             const uint32_t P = a.pipes, RS = a.stages / a.pipes;
             const uint32_t idesc = idesc_tf32(kTcBM, a.bn);
-            // K = 8 steps of the last K block that hold input channels: the
-            // rest of that block is zero fill (zero weights too), so its MMAs
-            // would add nothing (cin 16: 2 of 4, cin 36: 1 of 4 in block 2)
-            const uint32_t kk_last = min(kTcBK / 8, ((uint32_t)a.c.cin - (a.kblocks - 1) * kTcBK + 7) / 8);
             uint32_t it = 0, nt = 0;
             bool ok = true;
             if (a.b_resident && blockIdx.x + p * gridDim.x < a.units) {
@@ -491,8 +487,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + ab * a.bn;
-                uint32_t kbi = k0 % a.kblocks;  // K block of iteration k (non-halo order: tap-major)
-                for (uint32_t k = k0; k < k1; k++, it++, kbi = kbi + 1 == a.kblocks ? 0 : kbi + 1) {
+                for (uint32_t k = k0; k < k1; k++, it++) {
                     const uint32_t s = p * RS + it % RS, ph = (it / RS) & 1;
                     if (*abort_flag || !mbar_wait(&sh.full[s], ph)) {
                         report_error(0x01000003);
@@ -506,42 +501,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         // tap (ky, kx): the stage's copy shifted down ky rows
                         // (ky * bw A rows, a multiple of 8 rows: swizzle-aligned)
                         const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
-                        const uint32_t nkk = kb + 1 == a.kblocks ? kk_last : kTcBK / 8;
                         for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++) {
                             const uint32_t tap = ky * a.c.kw + kx;
                             const uint32_t sb = a.b_resident
                                                     ? smem_u32(smem + a.bres_off + (tap * a.kblocks + kb) * a.b_bytes)
                                                     : sa + a.a_bytes + ky * a.b_bytes;
                             const uint64_t ad = smem_desc_sw128(sa + ky * a.bw * 128), bd = smem_desc_sw128(sb);
-                            if (nkk == kTcBK / 8) {
 #pragma unroll
-                                for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                    mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                             (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
-                            } else {
-#pragma unroll
-                                for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                    if (kk < nkk)
-                                        mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                                 (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
-                            }
+                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                         (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
                         }
                     } else {
                         const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + kTcABytes;
                         const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
-                        const uint32_t nkk = kbi + 1 == a.kblocks ? kk_last : kTcBK / 8;
-                        // advance 8 tf32 = 32 bytes along K inside the swizzle row
-                        if (nkk == kTcBK / 8) {
 #pragma unroll
-                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                         (k > k0 || kk > 0) ? 1u : 0u);
-                        } else {
-#pragma unroll
-                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                if (kk < nkk)
-                                    mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                             (k > k0 || kk > 0) ? 1u : 0u);
+                        for (uint32_t kk = 0; kk < kTcBK / 8; kk++) {
+                            // advance 8 tf32 = 32 bytes along K inside the swizzle row
+                            mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                     (k > k0 || kk > 0) ? 1u : 0u);
                         }
                     }
                     mma_commit(&sh.empty[s]);
