@@ -233,6 +233,25 @@ def run_mbconv(ex: "ConvPlan", dw: "ConvPlan", pj: "ConvPlan", x: torch.Tensor, 
     return out
 
 
+def run_stem_pw(stem: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, stem_out: Optional[torch.Tensor] = None,
+                pw_out: Optional[torch.Tensor] = None, stream=None):
+    """The tensor-core stem and a 1x1 conv over its output (cin 32,
+    cout <= 32) in one launch (aie_conv_run_stem_pw): both outputs are
+    written, the 1x1 reads the stem's tile from shared memory.  Raises
+    AieError(AIE_E_UNSUPPORTED) for plans outside that shape."""
+    if stem.w is None or pw.w is None:
+        raise RuntimeError("load_weights() first")
+    if stem_out is None:
+        stem_out = torch.empty(stem.out_shape(), dtype=torch.float32, device=x.device)
+    if pw_out is None:
+        pw_out = torch.empty(pw.out_shape(), dtype=torch.float32, device=x.device)
+    check(stem.lib.aie_conv_run_stem_pw(stem._h, pw._h, _dptr(x), C.c_void_p(stem.w.data_ptr()),
+                                        C.c_void_p(stem.b.data_ptr()), C.c_void_p(pw.w.data_ptr()),
+                                        C.c_void_p(pw.b.data_ptr()), _dptr(stem_out), _dptr(pw_out),
+                                        C.c_void_p(_stream_handle(stream))), "aie_conv_run_stem_pw")
+    return stem_out, pw_out
+
+
 def input_u8(frames: torch.Tensor, layout: str = "nhwc", out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """u8 RGB / RGBA frames [n, h, w, 3|4] on the GPU -> the network's f32
     input [n, h, w, 3] (NHWC) or [n, h, w, 4] (NHWC-C4), value / 255

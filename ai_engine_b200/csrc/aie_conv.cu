@@ -777,6 +777,47 @@ extern "C" int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, co
     return run_dw_pw(dw, pw, in, up, up_h, up_w, dw_w, dw_b, pw_w, pw_b, out, stream);
 }
 
+extern "C" int aie_conv_run_stem_pw(const aie_plan *stem, const aie_plan *pw, const void *in, const void *stem_w,
+                                    const void *stem_b, const void *pw_w, const void *pw_b, void *stem_out,
+                                    void *pw_out, void *stream)
+{
+    if (!stem || !pw || !in || !stem_w || !stem_b || !pw_w || !pw_b || !stem_out || !pw_out)
+        return fail(AIE_E_INVALID, "null argument");
+    const aie_conv_desc &d = stem->d, &q = pw->d;
+    if (!stem->stem_tc)
+        return fail(AIE_E_UNSUPPORTED, "stem + 1x1: the first plan must run as the tensor-core stem "
+                                       "(3x3, cin <= 3, cout 32, no residual, math AUTO or TF32)");
+    if (pw->kernel != AIE_KERNEL_PW || pw->math != AIE_MATH_TF32 || q.has_res || q.cin != (uint32_t)kStemCout ||
+        q.cout > (uint32_t)kStemCout || q.cout % 4 || q.n != d.n || q.ih != stem->oh || q.iw != stem->ow ||
+        q.layout != AIE_LAYOUT_NHWC || pw->x_stride != (long long)q.cin || pw->x_coff ||
+        pw->y_stride != (long long)q.cout || pw->y_coff || pw->cin_pad != (int)kStemCout)
+        return fail(AIE_E_UNSUPPORTED, "stem + 1x1: the second plan must be a dense TF32 1x1 over the stem's output, "
+                                       "cin 32, cout <= 32 and a multiple of 4, no residual");
+    if (((uintptr_t)stem_w | (uintptr_t)stem_b | (uintptr_t)pw_w | (uintptr_t)pw_b | (uintptr_t)pw_out) % 16)
+        return fail(AIE_E_ALIGN, "weights, biases and the 1x1 output must be 16-byte aligned");
+    const ConvArgs a = make_args(stem, in, stem_w, stem_b, nullptr, stem_out);
+    if (!a.vec_y) return fail(AIE_E_ALIGN, "the stem output must be 16-byte aligned with a pixel stride of 4k floats");
+    StemPw sp;
+    sp.w = (const float *)pw_w;
+    sp.bias = (const float *)pw_b;
+    sp.y = (float *)pw_out;
+    sp.cout = (int)q.cout;
+    sp.act = q.act;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int cin = (int)d.cin;
+    int rc;
+    if (d.sh == 1)
+        rc = cin == 1 ? stem_tc_launch<1, 1, true>(a, stem->sg, s, sp)
+             : cin == 2 ? stem_tc_launch<2, 1, true>(a, stem->sg, s, sp) : stem_tc_launch<3, 1, true>(a, stem->sg, s, sp);
+    else
+        rc = cin == 1 ? stem_tc_launch<1, 2, true>(a, stem->sg, s, sp)
+             : cin == 2 ? stem_tc_launch<2, 2, true>(a, stem->sg, s, sp) : stem_tc_launch<3, 2, true>(a, stem->sg, s, sp);
+    if (rc) return cuda_fail(cudaGetLastError(), "tensor-core stem setup");
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "stem + 1x1 launch");
+    return AIE_OK;
+}
+
 extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const aie_plan *pj, const void *in,
                                    const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b,
                                    const void *pj_w, const void *pj_b, const void *res, void *out, void *stream)

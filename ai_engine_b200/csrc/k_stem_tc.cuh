@@ -13,6 +13,16 @@
 //      activation, transposes through its own A rows and writes 512-byte
 //      contiguous pieces of the NHWC output.
 // Three CTAs share an SM so their phases overlap.  Every wait is bounded.
+//
+// With PW (aie_conv_run_stem_pw) the kernel also runs the 1x1 conv that
+// reads the stem's output (cin 32, cout <= 32: a feature pyramid's lateral
+// on the stem features): the staged tile of step 4 is exactly that GEMM's A
+// operand (pixel rows, 32 channels, K-major, 128-byte swizzle), so one
+// thread issues 2 x 4 more MMAs into a second pair of accumulators while the
+// warps store the stem tile, and the warps then drain, add the 1x1's bias
+// and activation and store its output the same way.  The stem output is
+// still written (the encoder reads it); the 1x1's separate pass over it is
+// saved.
 #pragma once
 
 namespace aie {
@@ -22,9 +32,17 @@ constexpr int kStemTile = 16;
 constexpr int kStemThreads = 256;                 // one thread per output pixel of a tile
 constexpr uint32_t kStemABytes = 256 * 128;       // im2col rows; also the epilogue staging
 constexpr uint32_t kStemBBytes = kStemCout * 128; // weights [n][k], K-major
-constexpr uint32_t kStemTmemCols = 64;            // two 128 x 32 fp32 accumulators
+constexpr uint32_t kStemTmemCols = 64;            // two 128 x 32 fp32 accumulators (128 with PW: four)
 
-template <int CIN, int S>
+// The fused 1x1 conv after the stem (PW): dense [n][oh][ow][cout] output.
+struct StemPw {
+    const float *w;     // [cout][32], K-major rows (the TF32 1x1 packing)
+    const float *bias;  // [>= cout]
+    float *y;
+    int cout, act;
+};
+
+template <int CIN, int S, bool PW = false>
 struct StemTcLayout {
     static constexpr int HH = (kStemTile - 1) * S + 3, HW = HH;
     static constexpr int HROW = HW * CIN, HN = HH * HROW;
@@ -32,13 +50,15 @@ struct StemTcLayout {
     // floats early) rounded up to 16 bytes
     static constexpr int BX = (HROW + 3 + 3) / 4 * 4;
     static constexpr int HN_MAX = HH * BX > HN ? HH * BX : HN;
-    static constexpr uint32_t kHaloOff = kStemABytes + kStemBBytes;
+    static constexpr uint32_t kB2Off = kStemABytes + kStemBBytes;         // PW: the 1x1's weights
+    static constexpr uint32_t kHaloOff = kStemABytes + (PW ? 2 : 1) * kStemBBytes;
     // each halo buffer starts 256-byte aligned (a TMA destination must be at
     // least 128-byte aligned)
     static constexpr uint32_t kHaloFloats = (HN_MAX + 63) / 64 * 64;
-    static constexpr uint32_t kBiasOff = kHaloOff + 2 * kHaloFloats * 4;
-    static constexpr uint32_t kBarOff = kBiasOff + kStemCout * 4;
-    static constexpr uint32_t kBytes = kBarOff + 32 + 1024;  // + slack to 1024-align the base
+    static constexpr uint32_t kBiasOff = kHaloOff + 2 * kHaloFloats * 4;  // stem bias, then (PW) the 1x1's
+    static constexpr uint32_t kBarOff = kBiasOff + (PW ? 2 : 1) * kStemCout * 4;
+    // barriers: [0] stem MMA, [1..2] halo buffers, [3] the 1x1's MMA; then the TMEM slot
+    static constexpr uint32_t kBytes = kBarOff + 48 + 1024;  // + slack to 1024-align the base
     static_assert(kHaloOff % 256 == 0 && (kHaloFloats * 4) % 256 == 0, "TMA halo buffers 256-byte aligned");
     static_assert(kBarOff % 8 == 0, "mbarriers 8-byte aligned");
 };
@@ -57,11 +77,12 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int k)
 // kTma: the dense input (pixel stride = cin, 16-byte aligned rows) is staged
 // with one 3-D TMA box (W*cin floats, H, N) per tile -- out-of-frame rows and
 // columns read as zeros -- instead of one 4-byte cp.async per element.
-template <int CIN, int S, bool kTma>
+template <int CIN, int S, bool kTma, bool PW = false>
 __global__ void __launch_bounds__(kStemThreads, 3)
-    stem_tc_kernel(const __grid_constant__ CUtensorMap tmx, const ConvArgs a, const StemGeom g)
+    stem_tc_kernel(const __grid_constant__ CUtensorMap tmx, const ConvArgs a, const StemGeom g, const StemPw pw)
 {
-    using L = StemTcLayout<CIN, S>;
+    using L = StemTcLayout<CIN, S, PW>;
+    constexpr uint32_t kTmemCols = PW ? 2 * kStemTmemCols : kStemTmemCols;
     constexpr int K = 9 * CIN;
     static_assert(K <= 32, "im2col row must fit one 128-byte swizzle row");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -72,7 +93,8 @@ __global__ void __launch_bounds__(kStemThreads, 3)
     float *sbias = reinterpret_cast<float *>(smem + L::kBiasOff);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
     uint64_t *hbar = bar + 1;  // [2] halo buffer full (TMA path)
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kBarOff + 24);
+    uint64_t *bar2 = bar + 3;  // PW: the 1x1's MMAs done
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kBarOff + 32);
     constexpr int ROW = kTma ? L::BX : L::HROW;  // halo row stride in floats
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tiles_per_img = g.tiles_x * g.tiles_y;
@@ -113,15 +135,25 @@ __global__ void __launch_bounds__(kStemThreads, 3)
         *reinterpret_cast<float *>(sB + sw128_off(n, k)) = k < K ? __ldg(a.w + k * a.wn + n) : 0.0f;
     }
     if (tid < kStemCout) sbias[tid] = __ldg(a.bias + tid);
+    if constexpr (PW) {
+        // the 1x1's weights as a second B operand (rows past cout are zero)
+        uint8_t *sB2 = smem + L::kB2Off;
+        for (int i = tid; i < kStemCout * 32; i += kStemThreads) {
+            const int n = i >> 5, k = i & 31;
+            *reinterpret_cast<float *>(sB2 + sw128_off(n, k)) = n < pw.cout ? __ldg(pw.w + n * 32 + k) : 0.0f;
+        }
+        if (tid < kStemCout) sbias[kStemCout + tid] = tid < pw.cout ? __ldg(pw.bias + tid) : 0.0f;
+    }
     if (tid == 0) {
         mbar_init(bar, 1);
         mbar_init(&hbar[0], 1);
         mbar_init(&hbar[1], 1);
+        mbar_init(bar2, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kStemTmemCols));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B visible to the tensor core
@@ -132,8 +164,8 @@ __global__ void __launch_bounds__(kStemThreads, 3)
     const uint32_t idesc = idesc_tf32(128, kStemCout);
     const uint64_t bdesc = smem_desc_sw128(smem_u32(sB));
 
-    uint32_t phase = 0;
-    bool failed = false, mma_pending = false;
+    uint32_t phase = 0, phase2 = 0;
+    bool failed = false, mma_pending = false, mma2_pending = false;
     uint32_t halo_pending = 0;  // TMA path, thread 0: buffers with a copy in flight
     uint32_t halo_parity = 0;   // ... and the phase parity each of those copies completes
     int t = blockIdx.x;
@@ -249,7 +281,29 @@ __global__ void __launch_bounds__(kStemThreads, 3)
                 *reinterpret_cast<float4 *>(srow + ((((4 * h + c) ^ tid) & 7) << 4)) =
                     make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
         }
-        __syncwarp();
+        if constexpr (PW) {
+            // the staged tile is the 1x1's A operand: every warp's rows must
+            // be in place before thread 0 issues its MMAs
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                const uint64_t b2desc = smem_desc_sw128(smem_u32(smem + L::kB2Off));
+#pragma unroll
+                for (int m = 0; m < 2; m++) {
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(sA + m * (kStemABytes / 2)));
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_tf32(tmem + kStemTmemCols + (uint32_t)(m * kStemCout), adesc + 2 * kk, b2desc + 2 * kk,
+                                 idesc, kk > 0);
+                }
+                mma_commit(bar2);
+            }
+            mma2_pending = true;
+        } else {
+            __syncwarp();
+        }
         const int oy0 = t_ty * kStemTile, ox0 = t_tx * kStemTile;
         const int c = lane & 7;                          // this lane's 4-channel chunk
         const int mrow0 = (t_img * a.oh + oy0) * a.ow + ox0;  // first pixel of the tile (M < 2^31)
@@ -262,9 +316,56 @@ __global__ void __launch_bounds__(kStemThreads, 3)
             if (oy0 + dy < a.oh && ox0 + dx < a.ow)
                 *reinterpret_cast<float4 *>(ybase + (long long)(mrow0 + dy * a.ow + dx) * a.y_stride) = val;
         }
+        if constexpr (PW) {
+            // the 1x1's accumulators -> + bias -> activation -> this warp's own
+            // A rows (its stores above have read them; the MMAs have too once
+            // bar2 completes) -> 128-byte rows of the 1x1's output
+            if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar2, phase2))) {
+                if (lane == 0) report_error(0x03000003u);
+                failed = true;
+                continue;
+            }
+            mma2_pending = false;
+            phase2 ^= 1;
+            tc_fence_after();
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                uint32_t r[16];
+                tmem_ld16_issue(taddr + kStemTmemCols + 16 * h, r);
+                tmem_wait16(r);
+                float o[16];
+#pragma unroll
+                for (int j = 0; j < 16; j += 4) {
+                    const float4 b4 = *reinterpret_cast<const float4 *>(sbias + kStemCout + 16 * h + j);
+                    o[j] = __uint_as_float(r[j]) + b4.x;
+                    o[j + 1] = __uint_as_float(r[j + 1]) + b4.y;
+                    o[j + 2] = __uint_as_float(r[j + 2]) + b4.z;
+                    o[j + 3] = __uint_as_float(r[j + 3]) + b4.w;
+                }
+                act_apply_n<16>(pw.act, o);
+                __syncwarp();
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++)
+                    *reinterpret_cast<float4 *>(srow + ((((4 * h + cc) ^ tid) & 7) << 4)) =
+                        make_float4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
+            }
+            __syncwarp();
+            if (4 * c < pw.cout) {
+                float *y2 = pw.y + 4 * c;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int p = warp * 32 + j * 4 + (lane >> 3);
+                    const float4 val = *reinterpret_cast<const float4 *>(sA + p * 128 + (((c ^ p) & 7) << 4));
+                    const int dy = p >> 4, dx = p & 15;
+                    if (oy0 + dy < a.oh && ox0 + dx < a.ow)
+                        *reinterpret_cast<float4 *>(y2 + (long long)(mrow0 + dy * a.ow + dx) * pw.cout) = val;
+                }
+            }
+        }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (mma_pending && tid == 0) mbar_wait(bar, phase);  // drain before the TMEM is released
+    if (PW && mma2_pending && tid == 0) mbar_wait(bar2, phase2);
     if constexpr (kTma) {
         // a prefetch left in flight by an early exit must land before the CTA ends
         for (int b = 0; b < 2; b++)
@@ -274,7 +375,7 @@ __global__ void __launch_bounds__(kStemThreads, 3)
     __syncthreads();
     tc_fence_after();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kStemTmemCols));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
 // Host: launch one wave of kStemCtasPerSm resident CTAs per SM (persistent
@@ -284,12 +385,12 @@ __global__ void __launch_bounds__(kStemThreads, 3)
 // directly, and the strided tile loop stays correct however many are resident.
 constexpr int kStemCtasPerSm = 3;
 
-template <int CIN, int S>
-static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s)
+template <int CIN, int S, bool PW = false>
+static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s, const StemPw &pw = StemPw{})
 {
-    using L = StemTcLayout<CIN, S>;
+    using L = StemTcLayout<CIN, S, PW>;
     static_assert(kStemCtasPerSm * (L::kBytes + 1024) <= 228 * 1024, "shared memory for three CTAs per SM");
-    for (auto fn : {stem_tc_kernel<CIN, S, true>, stem_tc_kernel<CIN, S, false>})
+    for (auto fn : {stem_tc_kernel<CIN, S, true, PW>, stem_tc_kernel<CIN, S, false, PW>})
         if (ensure_smem_attr((const void *)fn, (int)L::kBytes, true) != cudaSuccess) return -1;
     const long long ntiles = (long long)a.n * g.tiles_x * g.tiles_y;
     const unsigned grid = (unsigned)std::min<long long>(ntiles, (long long)kStemCtasPerSm * tc_sm_count());
@@ -309,8 +410,8 @@ static int stem_tc_launch(const ConvArgs &a, const StemGeom &g, cudaStream_t s)
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
-    if (tma) stem_tc_kernel<CIN, S, true><<<grid, kStemThreads, L::kBytes, s>>>(tm, a, g);
-    else stem_tc_kernel<CIN, S, false><<<grid, kStemThreads, L::kBytes, s>>>(tm, a, g);
+    if (tma) stem_tc_kernel<CIN, S, true, PW><<<grid, kStemThreads, L::kBytes, s>>>(tm, a, g, pw);
+    else stem_tc_kernel<CIN, S, false, PW><<<grid, kStemThreads, L::kBytes, s>>>(tm, a, g, pw);
     return 0;
 }
 

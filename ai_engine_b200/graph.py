@@ -22,7 +22,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_dw_pw, run_mbconv
+from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_dw_pw, run_mbconv, run_stem_pw
 
 
 @dataclass
@@ -37,6 +37,7 @@ class OpRecord:
     head: Optional[ConvPlan] = None   # kind "dwpw": the fused 1x1 (cout <= 4) after the depthwise plan
     up: Optional[str] = None          # kind "dwpw": source whose exact-2x resize is added to the depthwise input
     blk: Optional[Tuple[ConvPlan, ConvPlan, ConvPlan]] = None  # kind "mb": expand, depthwise, project plans
+    out2: Optional[str] = None        # kind "stempw": the fused 1x1's output (its plan in `head`)
 
 
 def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
@@ -67,7 +68,8 @@ class Model:
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
                  in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
-                 fuse_tail: bool = True, fuse_blocks: bool = True, input_u8: bool = False, device=None):
+                 fuse_tail: bool = True, fuse_blocks: bool = True, fuse_stem: bool = True, input_u8: bool = False,
+                 device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -225,6 +227,19 @@ class Model:
                     rec.size, rec.res = op[3], op[4]
                 self.bufs[out] = torch.empty((n, *self.shapes[out]), dtype=torch.float32, device=self.device)
                 self.ops.append(rec)
+        # Stem + 1x1 (fuse_stem): a 1x1 TF32 conv over the tensor-core stem's
+        # output (cin 32, cout <= 32, no residual: a pyramid lateral on the
+        # stem features) runs inside the stem's launch (aie_conv_run_stem_pw)
+        # from the stem's staged tile instead of re-reading it from memory.
+        if fuse_stem:
+            for st in [r for r in self.ops if r.kind == "conv" and r.plan.info.variant == 2]:
+                pw = next((r for r in self.ops if r.kind == "conv" and r.src == st.out and r.res is None
+                           and r.plan.kernel == "pw" and r.plan.math == "tf32" and r.conv.cin == 32
+                           and r.conv.cout <= 32 and r.conv.cout % 4 == 0), None)
+                if pw is None:
+                    continue
+                st.kind, st.head, st.out2 = "stempw", pw.plan, pw.out
+                self.ops.remove(pw)
         self.graph_exec = None
 
     # -- accounting ------------------------------------------------------------
@@ -256,6 +271,8 @@ class Model:
                 run_dw_pw(r.plan, r.head, src, out=out, stream=stream, up=self.bufs[r.up] if r.up else None)
             elif r.kind == "mb":
                 run_mbconv(*r.blk, src, res=self.bufs[r.res] if r.res else None, out=out, stream=stream)
+            elif r.kind == "stempw":
+                run_stem_pw(r.plan, r.head, src, stem_out=out, pw_out=self.bufs[r.out2], stream=stream)
             elif r.kind == "u8in":
                 input_u8(src, out=out, stream=stream)
             else:

@@ -396,6 +396,8 @@ def main():
                     help="run each small-frame inverted-bottleneck block as one launch (default: Model's)")
     ap.add_argument("--fuse-resize", type=int, default=None, choices=[0, 1],
                     help="fold each resize that only feeds a conv residual into that conv (default: Model's)")
+    ap.add_argument("--fuse-stem", type=int, default=None, choices=[0, 1],
+                    help="run the 1x1 over the stem's output inside the stem's launch (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
     ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm"],
                     help="segnet: BASELINE config 4 (default); rvm: the recurrent matting net of config 5")
@@ -420,7 +422,7 @@ def main():
         return run_rvm(args, world, rank, dev)
 
     from ai_engine_b200 import segnet
-    from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv
+    from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv, run_stem_pw
     from ai_engine_b200.graph import Model
 
     n = args.batch
@@ -429,6 +431,8 @@ def main():
     fuse_kw = {} if args.fuse_resize is None else {"fuse": bool(args.fuse_resize)}
     if args.fuse_blocks is not None:
         fuse_kw["fuse_blocks"] = bool(args.fuse_blocks)
+    if args.fuse_stem is not None:
+        fuse_kw["fuse_stem"] = bool(args.fuse_stem)
     model = Model(g, weights, n, (H, W, 3), math=args.math, device=dev, **fuse_kw)
     x_host = torch.from_numpy(segnet.synthetic_input(n, seed=100 + rank)).pin_memory()
     model.bufs["input"].copy_(x_host)
@@ -487,6 +491,8 @@ def main():
                 run_dw_pw(r.plan, r.head, src, out=out, up=model.bufs[r.up] if r.up else None)
             elif r.kind == "mb":
                 run_mbconv(*r.blk, src, res=model.bufs[r.res] if r.res else None, out=out)
+            elif r.kind == "stempw":
+                run_stem_pw(r.plan, r.head, src, stem_out=out, pw_out=model.bufs[r.out2])
             else:
                 resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
             ev[i + 1].record(stream)
@@ -572,6 +578,11 @@ def main():
             if r.up:  # the half-size source whose resize the kernel adds to its input
                 by += 4 * n * int(np.prod(model.shapes[r.up]))
             kern, math = "dw+pw", r.plan.math
+        elif r.kind == "stempw":
+            # stem + the 1x1 over its output: the 1x1 does not read the stem output back
+            inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout
+            fl, by = r.plan.flops + r.head.flops, r.plan.min_bytes + r.head.min_bytes - inter
+            kern, math = "stem+pw", "tf32"
         elif r.plan is not None:
             fl, by = r.plan.flops, r.plan.min_bytes
             kern, math = r.plan.kernel, r.plan.math

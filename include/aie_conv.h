@@ -247,6 +247,19 @@ AIE_API int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const ai
                         const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b, const void *pj_w,
                         const void *pj_b, const void *res, void *out, void *stream);
 
+/* The tensor-core stem (a plan with aie_plan_info.variant 2: 3x3, cin <= 3,
+ * cout 32) and a TF32 1x1 conv that reads its output (cin 32, cout <= 32 and
+ * a multiple of 4, no residual, dense) in one launch: the stem writes its
+ * output to stem_out as aie_conv_run would, and the 1x1's result to pw_out,
+ * computed from the stem's staged output tile without reading it back from
+ * memory.  Replaces the two dispatches ai-gpu-runtime records for a stem
+ * conv and a feature-pyramid lateral on its output
+ * (crates/ai-gpu-runtime/src/lowering.rs:99-187, kernel.rs:181-191).
+ * AIE_E_UNSUPPORTED for plans outside that shape. */
+AIE_API int aie_conv_run_stem_pw(const aie_plan *stem, const aie_plan *pw, const void *in, const void *stem_w,
+                                 const void *stem_b, const void *pw_w, const void *pw_b, void *stem_out,
+                                 void *pw_out, void *stream);
+
 /* Input staging: a batch of interleaved u8 RGB (cin = 3) or RGBA (cin = 4,
  * alpha dropped) frames [n, h, w, cin] -> the network's f32 input
  * [n, h, w, 3] (layout NHWC) or [n, h, w, 4] (NHWC_C4, 4th lane 0), each
