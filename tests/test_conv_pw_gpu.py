@@ -31,8 +31,7 @@ def test_conv_pw_matches_the_two_launches(cuda_ok, n, ih, iw, op1, cout2, act2):
     rng = np.random.default_rng(8400 + cout2)
     w2 = (rng.standard_normal(cout2 * 32) * 0.25).astype(np.float32)
     b2 = rng.uniform(-0.1, 0.1, cout2).astype(np.float32)
-    # split_k=1: small batches would otherwise split K (the chain needs whole tiles)
-    p1 = ConvPlan(op1, n, ih, iw, split_k=1).load_weights(w1, b1)
+    p1 = ConvPlan(op1, n, ih, iw).load_weights(w1, b1)
     p2 = ConvPlan(op2, n, oh, ow).load_weights(w2, b2)
     assert p1.math == "tf32" and p2.kernel == "pw" and p2.math == "tf32"
     gx = torch.from_numpy(x).cuda()
@@ -55,12 +54,12 @@ def test_conv_pw_rejects_other_shapes(cuda_ok):
     w2, b2 = np.zeros(16 * 32, np.float32), np.zeros(16, np.float32)
     gx = torch.zeros((1, 16, 16, 32), device="cuda")
     wide = Conv2d.pointwise(32, 64)
-    p1 = ConvPlan(wide, 1, 16, 16, split_k=1).load_weights(np.zeros(64 * 32, np.float32), np.zeros(64, np.float32))
+    p1 = ConvPlan(wide, 1, 16, 16).load_weights(np.zeros(64 * 32, np.float32), np.zeros(64, np.float32))
     p2 = ConvPlan(Conv2d.pointwise(64, 16), 1, 16, 16).load_weights(np.zeros(16 * 64, np.float32), b2)
     with pytest.raises(AieError) as e:
         run_conv_pw(p1, p2, gx)
     assert e.value.status == -3
-    p1 = ConvPlan(Conv2d.pointwise(32, 32), 1, 16, 16, has_res=True, split_k=1).load_weights(np.zeros(1024, np.float32),
+    p1 = ConvPlan(Conv2d.pointwise(32, 32), 1, 16, 16, has_res=True).load_weights(np.zeros(1024, np.float32),
                                                                                    np.zeros(32, np.float32))
     p2 = ConvPlan(op2, 1, 16, 16).load_weights(w2, b2)
     with pytest.raises(AieError) as e:
@@ -70,16 +69,14 @@ def test_conv_pw_rejects_other_shapes(cuda_ok):
 
 def test_segnet_with_and_without_the_chain(cuda_ok):
     """The benchmark network with e1.conv -> e1.pw chained equals the network
-    without the chain (the graph-level choice: at this batch e1.conv needs
-    no K split, so the executor chains it)."""
+    without the chain."""
     from ai_engine_b200 import segnet
     from ai_engine_b200.graph import Model
     g = segnet.build_graph()
     wts = segnet.init_weights(g)
-    # 64 frames: enough tiles that e1.conv runs without a K split
-    x = torch.from_numpy(segnet.synthetic_input(64, seed=4)).cuda()
-    a = Model(g, wts, 64, (segnet.H, segnet.W, 3), fuse_chain=True)
-    b = Model(g, wts, 64, (segnet.H, segnet.W, 3), fuse_chain=False)
+    x = torch.from_numpy(segnet.synthetic_input(2, seed=4)).cuda()
+    a = Model(g, wts, 2, (segnet.H, segnet.W, 3), fuse_chain=True)
+    b = Model(g, wts, 2, (segnet.H, segnet.W, 3), fuse_chain=False)
     chained = [r for r in a.ops if r.kind == "convpw"]
     assert [(r.out, r.out2) for r in chained] == [("e1.conv", "e1.pw")]
     ya, yb = a.infer(x).cpu().numpy(), b.infer(x).cpu().numpy()
