@@ -76,7 +76,6 @@ SIGNATURES = {
     "aie_conv_run_dw_pw_up2": (C.c_int, [_vp, _vp, _vp, _vp, C.c_uint32, C.c_uint32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "aie_conv_run_mbconv": (C.c_int, [_vp] * 13),
     "aie_conv_run_stem_pw": (C.c_int, [_vp] * 10),
-    "aie_conv_run_conv_pw": (C.c_int, [_vp] * 10),
     "aie_input_u8": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _vp, C.c_int32, _vp, _vp]),
     "aie_selftest_wait_timeout": (C.c_int, [C.c_uint32, _vp]),
     "aie_binary": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, C.c_int32, C.c_int32, TView, C.c_float,

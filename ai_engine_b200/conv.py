@@ -252,22 +252,6 @@ def run_stem_pw(stem: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, stem_out: Opt
     return stem_out, pw_out
 
 
-def run_conv_pw(p1: "ConvPlan", p2: "ConvPlan", x: torch.Tensor, out2: Optional[torch.Tensor] = None,
-                out1: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """A TF32 conv with 32 output channels and a TF32 1x1 over its output
-    (cout <= 32) in one launch (aie_conv_run_conv_pw).  With `out1` the first
-    conv's output is stored too; without it only the 1x1's.  Raises
-    AieError(AIE_E_UNSUPPORTED) for plans outside that shape."""
-    if p1.w is None or p2.w is None:
-        raise RuntimeError("load_weights() first")
-    if out2 is None:
-        out2 = torch.empty(p2.out_shape(), dtype=torch.float32, device=x.device)
-    check(p1.lib.aie_conv_run_conv_pw(p1._h, p2._h, _dptr(x), C.c_void_p(p1.w.data_ptr()), C.c_void_p(p1.b.data_ptr()),
-                                      C.c_void_p(p2.w.data_ptr()), C.c_void_p(p2.b.data_ptr()), _dptr(out1),
-                                      _dptr(out2), C.c_void_p(_stream_handle(stream))), "aie_conv_run_conv_pw")
-    return out2
-
-
 def input_u8(frames: torch.Tensor, layout: str = "nhwc", out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """u8 RGB / RGBA frames [n, h, w, 3|4] on the GPU -> the network's f32
     input [n, h, w, 3] (NHWC) or [n, h, w, 4] (NHWC-C4), value / 255

@@ -818,39 +818,6 @@ extern "C" int aie_conv_run_stem_pw(const aie_plan *stem, const aie_plan *pw, co
     return AIE_OK;
 }
 
-extern "C" int aie_conv_run_conv_pw(const aie_plan *p1, const aie_plan *p2, const void *in, const void *w1,
-                                    const void *b1, const void *w2, const void *b2, void *out1, void *out2,
-                                    void *stream)
-{
-    if (!p1 || !p2 || !in || !w1 || !b1 || !w2 || !b2 || !out2) return fail(AIE_E_INVALID, "null argument");
-    const aie_conv_desc &d = p1->d, &q = p2->d;
-    if (p1->math != AIE_MATH_TF32 || p1->stem_tc || (p1->kernel != AIE_KERNEL_PW && p1->kernel != AIE_KERNEL_IGEMM) ||
-        d.has_res || d.cout != 32 || p1->wsbytes)
-        return fail(AIE_E_UNSUPPORTED, "conv + 1x1: the first plan must be a TF32 tensor-core conv with cout 32, "
-                                       "no residual and no K split");
-    if (p2->kernel != AIE_KERNEL_PW || p2->math != AIE_MATH_TF32 || q.has_res || q.cin != 32 || q.cout > 32 ||
-        q.cout % 4 || q.n != d.n || q.ih != p1->oh || q.iw != p1->ow || q.layout != AIE_LAYOUT_NHWC ||
-        p2->y_stride != (long long)q.cout || p2->y_coff || p2->cin_pad != 32)
-        return fail(AIE_E_UNSUPPORTED, "conv + 1x1: the second plan must be a dense TF32 1x1 over the first's "
-                                       "output, cin 32, cout <= 32 and a multiple of 4, no residual");
-    if (((uintptr_t)w2 | (uintptr_t)b2 | (uintptr_t)out2) % 16)
-        return fail(AIE_E_ALIGN, "the 1x1's weights, bias and output must be 16-byte aligned");
-    if (((uintptr_t)w1 | (uintptr_t)b1) % 16) return fail(AIE_E_ALIGN, "weights/bias must be 16-byte aligned");
-    // without out1 the first conv's output is never stored (its epilogue
-    // still stages it for the 1x1), so any aligned pointer stands in for it
-    const ConvArgs a = make_args(p1, in, w1, b1, nullptr, out1 ? out1 : out2);
-    TcChain ch;
-    ch.w = (const float *)w2;
-    ch.b = (const float *)b2;
-    ch.y = (float *)out2;
-    ch.cout = (int)q.cout;
-    ch.act = q.act;
-    ch.write1 = out1 != nullptr;
-    int rc = tc_launch(p1->tc, a, nullptr, (cudaStream_t)stream, t_err, sizeof t_err, &ch);
-    if (rc) return rc;
-    return AIE_OK;
-}
-
 extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const aie_plan *pj, const void *in,
                                    const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b,
                                    const void *pj_w, const void *pj_b, const void *res, void *out, void *stream)

@@ -106,22 +106,6 @@ struct TcArgs {
     float *ws;            // split-K partials [tile][split][128][bn]
     uint32_t *tickets;    // split-K tickets [tile][4 row quadrants]
     uint32_t out_off, shared_off;  // shared-memory carve-up (bytes)
-    // CHAIN: a 1x1 conv (cin = bn = 32, cout2 <= 32) over this conv's output,
-    // run from the epilogue's staged tile (aie_conv_run_conv_pw)
-    uint32_t b2_off;      // its weights, [32 rows][32] K-major, 128-byte swizzle
-    const float *c2w;     // [cout2][32]
-    const float *c2b;     // [>= cout2]
-    float *c2y;           // [M][cout2]
-    int c2_cout, c2_act;
-    uint32_t c2_write1;   // also store this conv's own output
-};
-
-// Host-side description of the chained 1x1 (tc_launch).
-struct TcChain {
-    const float *w, *b;
-    float *y;
-    int cout, act;
-    bool write1;
 };
 
 // Exact-2x residual patch of one epilogue warp.  On 1x1 tiles a warp's 32
@@ -287,8 +271,6 @@ struct TcShared {
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
     uint64_t bfull;  // resident B landed
-    uint64_t staged[2];  // CHAIN: an epilogue group's four chunks are staged (128 arrivals)
-    uint64_t done2[2];   // CHAIN: the group's 1x1 MMAs completed
     uint32_t tmem_base;
     uint32_t abort;
 };
@@ -346,7 +328,7 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
 // 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches.
 // ACT: the activation when it is kNone or kRelu, else -1 (any kind, chosen
 // at run time)
-template <int RES, int ACT, bool CHAIN = false>
+template <int RES, int ACT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
 {
@@ -368,10 +350,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&sh.acc_empty[b], 4);
         }
         mbar_init(&sh.bfull, 1);
-        for (int b = 0; b < 2; b++) {
-            mbar_init(&sh.staged[b], 4 * 32);
-            mbar_init(&sh.done2[b], 1);
-        }
         sh.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -383,19 +361,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
                      "r"(a.tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    if constexpr (CHAIN) {
-        // the chained 1x1's weights as a B operand: row n = output channel,
-        // 32 K values of 4 bytes, 128-byte swizzle (16-byte chunk ^ row % 8);
-        // rows past cout2 are zero
-        if (warp >= 1 && warp <= kTcEpiWarps) {
-            for (int i = threadIdx.x - 32; i < 32 * 32; i += 32 * kTcEpiWarps) {
-                const int n = i >> 5, kk = i & 31;
-                *reinterpret_cast<float *>(smem + a.b2_off + n * 128 + ((((kk >> 2) ^ n) & 7) << 4) + ((kk & 3) << 2)) =
-                    n < a.c2_cout ? __ldg(a.c2w + n * 32 + kk) : 0.0f;
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        }
     }
     tc_fence_before();
     __syncthreads();
@@ -698,9 +663,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 pt = up2_patch(c, max(wm0, 0));
             }
             if (col >= c.y_pad_to) return;
-            if constexpr (CHAIN) {
-                if (!a.c2_write1) return;  // only the chained 1x1's output is wanted
-            }
             // four rows at a time: their residual loads are issued together
 #pragma unroll
             for (int h = 0; h < 2; h++) {
@@ -811,70 +773,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     report_error(0x01000004);
                     *abort_flag = 1;
                     break;
-                }
-                if constexpr (CHAIN) {
-                    // The group's four staged 32 x 32 chunks (this conv's
-                    // output after bias and activation, one per warp,
-                    // contiguous, 128-byte rows, swizzled) are the A operand
-                    // of the chained 1x1: region row j*32 + l is row l of the
-                    // chunk of warp ew = 4*grp + j, i.e. accumulator row
-                    // ((j + 1) & 3)*32 + l of this tile.
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    tc_fence_before();
-                    mbar_arrive(&sh.staged[grp]);
-                    if ((ew & 3) == 0 && lane == 0) {
-                        if (!*abort_flag && mbar_wait(&sh.staged[grp], k & 1)) {
-                            tc_fence_after();
-                            const uint64_t ad = smem_desc_sw128(smem_u32(smem + a.out_off + grp * 4 * kTcStageOut));
-                            const uint64_t bd = smem_desc_sw128(smem_u32(smem + a.b2_off));
-                            const uint32_t d2 = tmem + 2 * a.bn + grp * 32;
-#pragma unroll
-                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                mma_tf32(d2, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc_tf32(kTcBM, 32),
-                                         kk > 0 ? 1u : 0u);
-                            mma_commit(&sh.done2[grp]);
-                        } else {
-                            report_error(0x01000006);
-                            *abort_flag = 1;
-                        }
-                    }
-                    if (!__all_sync(0xffffffffu, mbar_wait_sleep(&sh.done2[grp], k & 1))) {
-                        report_error(0x01000007);
-                        *abort_flag = 1;
-                        break;
-                    }
-                    tc_fence_after();
-                    // TMEM lanes quad*32.. hold region rows quad*32.. = the
-                    // chunk of warp 4*grp + quad = accumulator rows
-                    // ((quad + 1) & 3)*32.. of the tile
-                    uint32_t r2[32];
-                    tmem_ld32_issue(tmem + ((quad * 32) << 16) + 2 * a.bn + grp * 32, 32, r2);
-                    tmem_wait32(32, r2);
-                    float v2[32];
-#pragma unroll
-                    for (int i = 0; i < 32; i++) v2[i] = __uint_as_float(r2[i]) + (i < a.c2_cout ? __ldg(a.c2b + i) : 0.0f);
-                    act_apply_n<32>(a.c2_act, v2);
-                    __syncwarp();  // every lane is done with this warp's chunk (its own stores above)
-                    {
-                        uint8_t *st = obuf + lane * 128;
-#pragma unroll
-                        for (int ch = 0; ch < 8; ch++)
-                            *reinterpret_cast<float4 *>(st + ((ch ^ (lane & 7)) * 16)) =
-                                make_float4(v2[4 * ch], v2[4 * ch + 1], v2[4 * ch + 2], v2[4 * ch + 3]);
-                    }
-                    __syncwarp();
-                    const int col2 = seg * 4;
-                    if (col2 < a.c2_cout) {
-                        const uint32_t rbase = ((quad + 1) & 3) * 32;
-#pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const int r = i * 4 + (lane >> 3);
-                            const long long px = tc_row_pixel(a, t.mt, org, rbase + (uint32_t)r);
-                            if (px < 0) continue;
-                            const float4 x2 = *reinterpret_cast<const float4 *>(obuf + r * 128 + ((seg ^ (r & 7)) * 16));
-                            *reinterpret_cast<float4 *>(a.c2y + px * a.c2_cout + col2) = x2;
-                        }
-                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -1102,7 +1000,7 @@ static int tc_sm_count()
 }
 
 static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace, cudaStream_t stream, char *err,
-                            size_t errlen, const TcChain *chain = nullptr)
+                            size_t errlen)
 {
     PFN_encodeTiled enc = tc_encoder();
     if (!enc) {
@@ -1193,26 +1091,6 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         }
     }
     const int kind = !c.res ? 0 : !c.res_mode ? 1 : a.res_patch ? 3 : 2;
-    uint32_t smem_bytes = g.smem_bytes;
-    a.b2_off = 0; a.c2w = nullptr; a.c2b = nullptr; a.c2y = nullptr; a.c2_cout = 0; a.c2_act = 0; a.c2_write1 = 1;
-    if (chain) {
-        // one 32-column n-tile without K split or residual: each epilogue
-        // group then holds a whole tile's output as the 1x1's A operand
-        if (g.bn != 32 || g.n_tiles != 1 || g.split != 1 || kind != 0 || chain->cout < 1 || chain->cout > 32) {
-            snprintf(err, errlen, "chained 1x1: the first conv must produce one 32-channel tile per 128 pixels "
-                                  "without K split or residual");
-            return -3;
-        }
-        a.b2_off = (g.shared_off + (uint32_t)sizeof(TcShared) + 1023) / 1024 * 1024;
-        smem_bytes = a.b2_off + 32 * 128 + 1024;
-        if (smem_bytes > 227 * 1024) {
-            snprintf(err, errlen, "chained 1x1: no shared memory left for its weights");
-            return -3;
-        }
-        a.tmem_cols = tc_pow2_ceil(2 * g.bn + 64);  // two accumulators + one 32-column 1x1 result per group
-        a.c2w = chain->w; a.c2b = chain->b; a.c2y = chain->y;
-        a.c2_cout = chain->cout; a.c2_act = chain->act; a.c2_write1 = chain->write1 ? 1u : 0u;
-    }
     // the activation as a template argument where it is none or ReLU (one
     // inlined switch over every kind per chunk costs instruction-cache misses)
     using Kern = void (*)(CUtensorMap, CUtensorMap, TcArgs);
@@ -1221,10 +1099,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         {tc_conv_kernel<1, kNone>, tc_conv_kernel<1, kRelu>, tc_conv_kernel<1, -1>},
         {tc_conv_kernel<2, kNone>, tc_conv_kernel<2, kRelu>, tc_conv_kernel<2, -1>},
         {tc_conv_kernel<3, kNone>, tc_conv_kernel<3, kRelu>, tc_conv_kernel<3, -1>}};
-    static const Kern chained[3] = {tc_conv_kernel<0, kNone, true>, tc_conv_kernel<0, kRelu, true>,
-                                    tc_conv_kernel<0, -1, true>};
-    const int ai = c.act == kNone ? 0 : c.act == kRelu ? 1 : 2;
-    auto kern = chain ? chained[ai] : kerns[kind][ai];
+    auto kern = kerns[kind][c.act == kNone ? 0 : c.act == kRelu ? 1 : 2];
     {
         cudaError_t e = ensure_smem_attr((const void *)kern, 227 * 1024);
         if (e != cudaSuccess) {
@@ -1233,7 +1108,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         }
     }
     const unsigned grid = (unsigned)std::min<uint64_t>(g.units, (uint64_t)tc_sm_count());
-    kern<<<grid, kTcThreads, smem_bytes, stream>>>(tmA, tmB, a);
+    kern<<<grid, kTcThreads, g.smem_bytes, stream>>>(tmA, tmB, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(err, errlen, "tc_conv_kernel launch: %s", cudaGetErrorString(e));

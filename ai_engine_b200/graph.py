@@ -22,7 +22,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_conv_pw, run_dw_pw, run_mbconv, run_stem_pw
+from .conv import Conv2d, ConvPlan, input_u8, resize_bilinear, run_dw_pw, run_mbconv, run_stem_pw
 
 
 @dataclass
@@ -37,7 +37,7 @@ class OpRecord:
     head: Optional[ConvPlan] = None   # kind "dwpw": the fused 1x1 (cout <= 4) after the depthwise plan
     up: Optional[str] = None          # kind "dwpw": source whose exact-2x resize is added to the depthwise input
     blk: Optional[Tuple[ConvPlan, ConvPlan, ConvPlan]] = None  # kind "mb": expand, depthwise, project plans
-    out2: Optional[str] = None        # kinds "stempw" / "convpw": the fused 1x1's output (its plan in `head`)
+    out2: Optional[str] = None        # kind "stempw": the fused 1x1's output (its plan in `head`)
 
 
 def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
@@ -68,8 +68,8 @@ class Model:
 
     def __init__(self, graph: Sequence[tuple], weights: Dict[str, Tuple[np.ndarray, np.ndarray]], n: int,
                  in_hwc: Tuple[int, int, int], *, math: str = "auto", fuse: bool = False, fuse_heads: bool = True,
-                 fuse_tail: bool = True, fuse_blocks: bool = True, fuse_stem: bool = True, fuse_chain: bool = True,
-                 input_u8: bool = False, device=None):
+                 fuse_tail: bool = True, fuse_blocks: bool = True, fuse_stem: bool = True, input_u8: bool = False,
+                 device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.graph = list(graph)
@@ -240,22 +240,6 @@ class Model:
                     continue
                 st.kind, st.head, st.out2 = "stempw", pw.plan, pw.out
                 self.ops.remove(pw)
-        # Conv + 1x1 (fuse_chain): a TF32 conv with 32 output channels whose
-        # output feeds only a TF32 1x1 (cout <= 32) runs that 1x1 inside its
-        # epilogue (aie_conv_run_conv_pw); the intermediate is never stored.
-        if fuse_chain:
-            for cv in [r for r in self.ops if r.kind == "conv" and r.plan.math == "tf32"
-                       and r.plan.kernel in ("pw", "igemm") and r.conv.cout == 32 and r.res is None
-                       and r.plan.info.split_k == 1 and r.plan.workspace is None]:
-                if uses.get(cv.out, 0) != 1 or cv.out == self.output:
-                    continue
-                pw = next((r for r in self.ops if r.kind == "conv" and r.src == cv.out and r.res is None
-                           and r.plan.kernel == "pw" and r.plan.math == "tf32" and r.conv.cin == 32
-                           and r.conv.cout <= 32 and r.conv.cout % 4 == 0), None)
-                if pw is None:
-                    continue
-                cv.kind, cv.head, cv.out2 = "convpw", pw.plan, pw.out
-                self.ops.remove(pw)
         self.graph_exec = None
 
     # -- accounting ------------------------------------------------------------
@@ -289,8 +273,6 @@ class Model:
                 run_mbconv(*r.blk, src, res=self.bufs[r.res] if r.res else None, out=out, stream=stream)
             elif r.kind == "stempw":
                 run_stem_pw(r.plan, r.head, src, stem_out=out, pw_out=self.bufs[r.out2], stream=stream)
-            elif r.kind == "convpw":
-                run_conv_pw(r.plan, r.head, src, out2=self.bufs[r.out2], stream=stream)
             elif r.kind == "u8in":
                 input_u8(src, out=out, stream=stream)
             else:

@@ -398,8 +398,6 @@ def main():
                     help="fold each resize that only feeds a conv residual into that conv (default: Model's)")
     ap.add_argument("--fuse-stem", type=int, default=None, choices=[0, 1],
                     help="run the 1x1 over the stem's output inside the stem's launch (default: Model's)")
-    ap.add_argument("--fuse-chain", type=int, default=None, choices=[0, 1],
-                    help="run a 1x1 inside the epilogue of the 32-channel conv that feeds it (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
     ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm"],
                     help="segnet: BASELINE config 4 (default); rvm: the recurrent matting net of config 5")
@@ -424,7 +422,7 @@ def main():
         return run_rvm(args, world, rank, dev)
 
     from ai_engine_b200 import segnet
-    from ai_engine_b200.conv import resize_bilinear, run_conv_pw, run_dw_pw, run_mbconv, run_stem_pw
+    from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv, run_stem_pw
     from ai_engine_b200.graph import Model
 
     n = args.batch
@@ -435,8 +433,6 @@ def main():
         fuse_kw["fuse_blocks"] = bool(args.fuse_blocks)
     if args.fuse_stem is not None:
         fuse_kw["fuse_stem"] = bool(args.fuse_stem)
-    if args.fuse_chain is not None:
-        fuse_kw["fuse_chain"] = bool(args.fuse_chain)
     model = Model(g, weights, n, (H, W, 3), math=args.math, device=dev, **fuse_kw)
     x_host = torch.from_numpy(segnet.synthetic_input(n, seed=100 + rank)).pin_memory()
     model.bufs["input"].copy_(x_host)
@@ -497,8 +493,6 @@ def main():
                 run_mbconv(*r.blk, src, res=model.bufs[r.res] if r.res else None, out=out)
             elif r.kind == "stempw":
                 run_stem_pw(r.plan, r.head, src, stem_out=out, pw_out=model.bufs[r.out2])
-            elif r.kind == "convpw":
-                run_conv_pw(r.plan, r.head, src, out2=model.bufs[r.out2])
             else:
                 resize_bilinear(src, r.size[0], r.size[1], add=model.bufs[r.res] if r.res else None, out=out)
             ev[i + 1].record(stream)
@@ -589,11 +583,6 @@ def main():
             inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout
             fl, by = r.plan.flops + r.head.flops, r.plan.min_bytes + r.head.min_bytes - inter
             kern, math = "stem+pw", "tf32"
-        elif r.kind == "convpw":
-            # conv + 1x1: the intermediate is neither written nor read back
-            inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout
-            fl, by = r.plan.flops + r.head.flops, r.plan.min_bytes + r.head.min_bytes - 2 * inter
-            kern, math = f"{r.plan.kernel}+pw", "tf32"
         elif r.plan is not None:
             fl, by = r.plan.flops, r.plan.min_bytes
             kern, math = r.plan.kernel, r.plan.math

@@ -260,19 +260,6 @@ AIE_API int aie_conv_run_stem_pw(const aie_plan *stem, const aie_plan *pw, const
                                  const void *stem_b, const void *pw_w, const void *pw_b, void *stem_out,
                                  void *pw_out, void *stream);
 
-/* A TF32 tensor-core conv with 32 output channels (1x1 or k x k, no
- * residual, no K split) and a TF32 1x1 conv over its output (cin 32, cout
- * <= 32 and a multiple of 4, no residual, dense) in one launch: each
- * 128-pixel tile of the first conv's output, staged in shared memory by the
- * epilogue, is the second GEMM's A operand.  out1 receives the first
- * conv's output, or NULL when nothing else reads it (it is then never
- * written); out2 the 1x1's.  Replaces two dispatches of ai-gpu-runtime's
- * lowered conv chain (crates/ai-gpu-runtime/src/lowering.rs:99-187,
- * kernel.rs:181-191).  AIE_E_UNSUPPORTED for other plans. */
-AIE_API int aie_conv_run_conv_pw(const aie_plan *p1, const aie_plan *p2, const void *in, const void *w1,
-                                 const void *b1, const void *w2, const void *b2, void *out1, void *out2,
-                                 void *stream);
-
 /* Input staging: a batch of interleaved u8 RGB (cin = 3) or RGBA (cin = 4,
  * alpha dropped) frames [n, h, w, cin] -> the network's f32 input
  * [n, h, w, 3] (layout NHWC) or [n, h, w, 4] (NHWC_C4, 4th lane 0), each
