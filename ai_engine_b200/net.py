@@ -130,6 +130,7 @@ class NetModel:
         self.states = dict(states or {})
         self.outputs = list(outputs)
         self.shapes = infer_shapes(self.nodes, inputs)
+        self.feeds = [k for k in inputs if k not in self.states]  # per-step inputs (not recurrent state)
         for si, so in self.states.items():
             if self.shapes[si] != self.shapes[so]:
                 raise ValueError(f"state {si} {self.shapes[si]} != {so} {self.shapes[so]}")
@@ -280,28 +281,95 @@ class NetModel:
             self.bufs[si].zero_()
         self.step_index = 0
 
-    def capture(self):
+    def capture(self, io_slots: bool = False):
         """Capture one CUDA graph per state parity (the buffers swap roles
-        every step).  Replays with `replay()`."""
+        every step).  Replays with `replay()`.  With io_slots the per-step
+        inputs and the non-state outputs get a second buffer, graph p reading
+        and writing slot p, so that `run_pipelined` can copy the neighbouring
+        steps' frames and results while a step computes."""
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             self.record(s)  # warm-up outside capture (plans, allocator)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
-        saved = {k: self.bufs[k] for k in (*self.states.keys(), *self.states.values())}
-        for parity in (0, 1):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self.record()
-            self.graphs[parity] = g
-            for si, so in self.states.items():
-                self.bufs[si], self.bufs[so] = self.bufs[so], self.bufs[si]
-        self.bufs.update(saved)
+        io = []
+        if io_slots:
+            io = [k for k in (*self.feeds, *self.outputs) if k not in self.states.values()]
+            for k in io:
+                if k in self.alias or k in self.cpad:
+                    raise ValueError(f"{k} is a view; pipelined I/O needs whole tensors")
+            self.io_slots = {k: [self.bufs[k], torch.empty_like(self.bufs[k])] for k in io}
+        saved = {k: self.bufs[k] for k in (*self.states.keys(), *self.states.values(), *io)}
+        try:
+            for parity in (0, 1):
+                for k in io:
+                    self.bufs[k] = self.io_slots[k][parity]
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self.record()
+                self.graphs[parity] = g
+                for si, so in self.states.items():
+                    self.bufs[si], self.bufs[so] = self.bufs[so], self.bufs[si]
+        finally:
+            self.bufs.update(saved)
         self.reset_state()
+
+    def run_pipelined(self, host_in: Sequence[Dict[str, torch.Tensor]], host_out: Sequence[Dict[str, torch.Tensor]],
+                      stream=None):
+        """Run consecutive steps end to end: step k copies host_in[k] (pinned
+        tensors per per-step input) in, replays the graph of its state parity
+        and copies its non-state outputs into host_out[k] (pinned).  The
+        upload of step k+1 and the read-back of step k-1 run on their own
+        copy streams while step k computes (ai-gpu-runtime uploads, infers and
+        reads back one frame per call, crates/ai-gpu-runtime/src/model.rs:
+        387-470).  Recurrent state advances by one step per entry.
+        Asynchronous on `stream` (default: current stream)."""
+        if len(host_in) != len(host_out):
+            raise ValueError("one output set per input set")
+        if not getattr(self, "io_slots", None):
+            self.capture(io_slots=True)
+        compute = torch.cuda.current_stream(self.device) if stream is None else stream
+        if not hasattr(self, "_copy_in"):
+            self._copy_in = torch.cuda.Stream(device=self.device)
+            self._copy_out = torch.cuda.Stream(device=self.device)
+        cin, cout = self._copy_in, self._copy_out
+        h2d = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        d2h = [torch.cuda.Event() for _ in range(2)]
+        start = torch.cuda.Event()
+        start.record(compute)
+        cin.wait_event(start)
+        cout.wait_event(start)
+        for k, (hi, ho) in enumerate(zip(host_in, host_out)):
+            p = self.step_index % 2
+            if k >= 2:
+                cin.wait_event(done[p])      # step k-2 no longer reads input slot p
+            with torch.cuda.stream(cin):
+                for name, t in hi.items():
+                    self.io_slots[name][p].copy_(t, non_blocking=True)
+            h2d[p].record(cin)
+            compute.wait_event(h2d[p])
+            if k >= 2:
+                compute.wait_event(d2h[p])   # output slot p of step k-2 has been read back
+            with torch.cuda.stream(compute):
+                self.graphs[p].replay()
+            self.advance()
+            done[p].record(compute)
+            cout.wait_event(done[p])
+            with torch.cuda.stream(cout):
+                for name, t in ho.items():
+                    t.copy_(self.io_slots[name][p], non_blocking=True)
+            d2h[p].record(cout)
+        for p in range(min(2, len(host_in))):
+            compute.wait_event(d2h[p])
+            compute.wait_event(h2d[p])
+        return host_out
 
     def replay(self):
         """One step from the captured graphs (state advances)."""
+        if getattr(self, "io_slots", None):
+            raise RuntimeError("captured with I/O slots: step it with run_pipelined")
         self.graphs[self.step_index % 2].replay()
         self.advance()
 
@@ -321,3 +389,4 @@ class NetModel:
 
     def release(self):
         self.graphs.clear()
+        self.io_slots = None
