@@ -12,8 +12,8 @@ PyTorch supplies device memory and streams only; all arithmetic runs in
 from __future__ import annotations
 
 import ctypes as C
-from dataclasses import dataclass, field
-from typing import Optional, Sequence, Tuple
+from dataclasses import dataclass
+from typing import Optional, Tuple
 
 import numpy as np
 import torch

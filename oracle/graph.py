@@ -16,7 +16,7 @@ real parallelism here.
 from __future__ import annotations
 
 import concurrent.futures as cf
-from typing import Dict, Optional, Tuple
+from typing import Dict, Tuple
 
 import numpy as np
 
