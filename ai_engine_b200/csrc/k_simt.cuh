@@ -1278,16 +1278,11 @@ __global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, const D
     }
     constexpr int NJ = (PB - 1) * S + (K - 1) * D + 1;  // input columns one row needs (dilation D)
     const int ixb = ox0 * S - a.pl;
-    // segments whose columns all lie inside the frame (most of them) load
-    // without a per-column bounds check, stepping a pointer by the pixel stride
-    const bool inside = ixb >= 0 && ixb + NJ <= a.iw;
-    const long long xs = a.x_stride;
 #pragma unroll
     for (int ky = 0; ky < K; ky++) {
         const int iy = oy * S - a.pt + ky * D;
         if (iy < 0 || iy >= a.ih) continue;
-        const float *row = a.x + ((long long)(img * a.ih + iy) * a.iw) * xs + a.x_coff + c0;
-        const float *colp = row + (inside ? (long long)ixb * xs : 0);
+        const float *row = a.x + ((long long)(img * a.ih + iy) * a.iw) * a.x_stride + a.x_coff + c0;
         float4 wk[K];
 #pragma unroll
         for (int kx = 0; kx < K; kx++)
@@ -1296,12 +1291,7 @@ __global__ void __launch_bounds__(256) dw_block_kernel(const ConvArgs a, const D
         for (int j = 0; j < NJ; j++) {
             const int ix = ixb + j;
             float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (inside) {
-                xv = __ldg(reinterpret_cast<const float4 *>(colp));
-                colp += xs;
-            } else if (ix >= 0 && ix < a.iw) {
-                xv = __ldg(reinterpret_cast<const float4 *>(row + (long long)ix * xs));
-            }
+            if (ix >= 0 && ix < a.iw) xv = __ldg(reinterpret_cast<const float4 *>(row + (long long)ix * a.x_stride));
 #pragma unroll
             for (int p = 0; p < PB; p++) {
                 // column j feeds tap kx of pixel p when j = p S + kx D
