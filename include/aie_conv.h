@@ -26,6 +26,14 @@
  *   aie_resize_bilinear    ResizeBilinearSpec (crates/ai-gpu/src/kernels/
  *                          resize_bilinear.rs) fused with an optional Binary
  *                          add (crates/ai-gpu/src/kernels/elementwise.rs).
+ *   aie_binary, aie_mix,   the non-conv SwOps between the convs: Binary, Mix,
+ *   aie_gpool, aie_avgpool, Gpool, Avgpool, Concat, Chcopy / Act
+ *   aie_concat,            (crates/ai-core/src/format/model.rs:111-214),
+ *   aie_channel_copy       in ai-cpu's rounding (crates/ai-cpu/src/kernels/
+ *                          elementwise.rs, segate.rs).
+ *   aie_conv_run_dw_pw(_up2), aie_conv_run_mbconv, aie_conv_run_stem_pw
+ *                          two or three consecutive dispatches of a lowered
+ *                          graph as one launch (see each declaration).
  *   aie_status_string      RuntimeError's Display
  *                          (crates/ai-gpu-runtime/src/error.rs:5-13).
  *   aie_device_status      GpuContext::lost_reason polling
