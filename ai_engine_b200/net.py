@@ -225,9 +225,10 @@ class NetModel:
         return sum(r.plan.flops for r in self.recs if r.plan is not None)
 
     # -- execution -----------------------------------------------------------------
-    def record(self, stream=None):
-        """Issue every op of one step on `stream` (default: current stream)."""
-        for r in self.recs:
+    def record(self, stream=None, ops=None):
+        """Issue every op of one step on `stream` (default: current stream),
+        or only the records in `ops` (a per-op timing pass)."""
+        for r in (self.recs if ops is None else ops):
             nd = r.node
             k = nd.kind
             if k in ("split", "view"):

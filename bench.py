@@ -297,13 +297,10 @@ def run_rvm(args, world, rank, dev):
     # ---- per-op eager timing (dominant op)
     recs = [r for r in model.recs if r.node.kind not in ("split", "view")]
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(recs) + 1)]
-    saved = model.recs
     evs[0].record(stream)
     for i, r in enumerate(recs):
-        model.recs = [r]
-        model.record()
+        model.record(ops=[r])
         evs[i + 1].record(stream)
-    model.recs = saved
     torch.cuda.synchronize()
     per_op = [evs[i].elapsed_time(evs[i + 1]) for i in range(len(recs))]
     model.advance()
