@@ -147,3 +147,24 @@ def test_rvm_pipelined_io_matches_eager(cuda_ok, net):
     with pytest.raises(RuntimeError):
         pm.replay()
     pm.release()
+
+
+@pytest.mark.parametrize("math,emulate,tol,mean_tol", [("ffma", False, 1e-3, 1e-4), ("auto", True, 6e-2, 4e-3)])
+def test_rvm_full_size(cuda_ok, math, emulate, tol, mean_tol):
+    """BASELINE config 5 at its own size, 144x256: two streams, two recurrent
+    steps against the oracle (the FP32 path directly, the TF32 path against
+    the oracle with the same convs' operands truncated to TF32)."""
+    g = rvm.build_graph()
+    wts = rvm.init_weights(g, seed=12)
+    n = 2
+    m = NetModel(g, wts, n, rvm.inputs(), rvm.OUTPUTS, rvm.STATES, rvm.consts(), math=math)
+    o = OracleNet(g, wts, rvm.inputs(), rvm.STATES, rvm.consts(), tf32=m.tf32_convs() if emulate else ())
+    x = rvm.synthetic_frames(n, 2, seed=26)
+    st = o.zero_state(n)
+    for t in range(2):
+        got = m.step({"src": torch.from_numpy(x[t]).cuda()})
+        want = o.step({"src": x[t]}, st, threads=8)
+        st = {k: want[v] for k, v in rvm.STATES.items()}
+        for k in rvm.OUTPUTS:
+            d = np.abs(got[k].cpu().numpy() - want[k])
+            assert float(d.max()) <= tol and float(d.mean()) <= mean_tol, (t, k, float(d.max()), float(d.mean()))
