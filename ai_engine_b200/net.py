@@ -296,7 +296,8 @@ class NetModel:
         torch.cuda.synchronize(self.device)
         io = []
         if io_slots:
-            io = [k for k in (*self.feeds, *self.outputs) if k not in self.states.values()]
+            io = list(dict.fromkeys(self._io_name(k) for k in (*self.feeds, *self.outputs)
+                                    if k not in self.states.values()))
             for k in io:
                 if k in self.alias or k in self.cpad:
                     raise ValueError(f"{k} is a view; pipelined I/O needs whole tensors")
@@ -315,6 +316,14 @@ class NetModel:
         finally:
             self.bufs.update(saved)
         self.reset_state()
+
+    def _io_name(self, k: str) -> str:
+        """The tensor behind `k`: an alias spanning all of its base tensor's
+        channels is that tensor (a .sw model's output alias)."""
+        a = self.alias.get(k)
+        if a is not None and a[1] == 0 and a[2] == self.bufs[a[0]].shape[-1]:
+            return a[0]
+        return k
 
     def run_pipelined(self, host_in: Sequence[Dict[str, torch.Tensor]], host_out: Sequence[Dict[str, torch.Tensor]],
                       stream=None):
@@ -348,7 +357,7 @@ class NetModel:
                 cin.wait_event(done[p])      # step k-2 no longer reads input slot p
             with torch.cuda.stream(cin):
                 for name, t in hi.items():
-                    self.io_slots[name][p].copy_(t, non_blocking=True)
+                    self.io_slots[self._io_name(name)][p].copy_(t, non_blocking=True)
             h2d[p].record(cin)
             compute.wait_event(h2d[p])
             if k >= 2:
@@ -360,7 +369,7 @@ class NetModel:
             cout.wait_event(done[p])
             with torch.cuda.stream(cout):
                 for name, t in ho.items():
-                    t.copy_(self.io_slots[name][p], non_blocking=True)
+                    t.copy_(self.io_slots[self._io_name(name)][p], non_blocking=True)
             d2h[p].record(cout)
         for p in range(min(2, len(host_in))):
             compute.wait_event(d2h[p])

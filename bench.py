@@ -380,6 +380,101 @@ def run_rvm(args, world, rank, dev):
     return 0
 
 
+# ------------------------------------- ai_engine's shipped model (segm_r11) ---
+
+SEGM_R11 = os.path.join(ROOT, "tests", "golden", "segm_r11.npz")  # the .sw container, committed as a fixture
+
+
+def run_segm_r11(args, world, rank, dev):
+    """ai_engine's shipped segmentation model web/models/segm_r11_160x288.sw
+    (44 ops, real weights) read by the .sw reader and run by the node
+    executor: `--batch` frames per GPU (weak scaling), frames resident for
+    `value`, pinned host frames in and logits out per step for `e2e`."""
+    import torch
+    import torch.distributed as dist
+
+    from ai_engine_b200.net import NetModel
+    from ai_engine_b200.swfile import load_sw
+
+    sw = load_sw(np.load(SEGM_R11)["sw"].tobytes())
+    n = args.batch
+    (inp, (h, w, c)), = sw.inputs.items()
+    out = sw.outputs[0]
+    model = NetModel(sw.nodes, sw.weights, n, sw.inputs, sw.outputs, sw.states, sw.consts, math=args.math, device=dev)
+    x = torch.from_numpy(np.random.default_rng(300 + rank).random((n, h, w, c), dtype=np.float32)).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    model.bufs[inp].copy_(x)
+    for _ in range(max(args.warmup, 3)):
+        model.record()
+    model.capture()
+    for _ in range(max(args.warmup, 3)):
+        model.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = max_over_ranks(e0.elapsed_time(e1))
+    value = n * world * args.steps / (total_ms / 1000.0)
+    launches = sum(1 for r in model.recs if r.node.kind not in ("split", "view"))
+    # end to end: pinned frames in, logits out, copies overlapping the steps
+    model.release()
+    oshape = model.tensor(out).shape
+    outs = [{out: torch.empty(oshape).pin_memory()} for _ in range(2)]
+    model.run_pipelined([{inp: x}] * 2, outs)
+    torch.cuda.synchronize()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    model.run_pipelined([{inp: x}] * args.steps, [outs[k % 2] for k in range(args.steps)])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    e2e_value = n * world * args.steps / (max_over_ranks(t0.elapsed_time(t1)) / 1000.0)
+    flops = model.conv_flops
+    model.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "segm_r11 160x288 frames/s (ai_engine's shipped .sw model)", "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "tf32" if args.math in ("auto", "tf32") else "f32",
+        "data": "synthetic frames, the model's real weights",
+        "config": {"workload": "web/models/segm_r11_160x288.sw through the .sw reader and the node executor",
+                   "per_gpu_batch": n, "h": h, "w": w, "ops": len(sw.nodes), "math": args.math,
+                   "conv_mflop_per_frame": round(flops / n / 1e6, 2)},
+        "conv_tflops": round(flops * world / (total_ms / args.steps / 1000.0) / 1e12, 3),
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(x.numel() * 4),
+                "d2h_bytes_per_step": int(np.prod(oshape) * 4)},
+        "gpu_launches": launches * args.steps,
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # --------------------------------------------------------------- GPU arm ---
 
 def main():
@@ -398,8 +493,9 @@ def main():
     ap.add_argument("--fuse-stem", type=int, default=None, choices=[0, 1],
                     help="run the 1x1 over the stem's output inside the stem's launch (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
-    ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm"],
-                    help="segnet: BASELINE config 4 (default); rvm: the recurrent matting net of config 5")
+    ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm", "segm_r11"],
+                    help="segnet: BASELINE config 4 (default); rvm: the recurrent matting net of config 5; "
+                         "segm_r11: ai_engine's shipped segmentation model (.sw, real weights)")
     ap.add_argument("--streams", type=int, default=1024, help="rvm: video streams over all GPUs")
     args = ap.parse_args()
 
@@ -419,6 +515,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if args.workload == "rvm":
         return run_rvm(args, world, rank, dev)
+    if args.workload == "segm_r11":
+        return run_segm_r11(args, world, rank, dev)
 
     from ai_engine_b200 import segnet
     from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv, run_stem_pw

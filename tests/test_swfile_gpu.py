@@ -80,3 +80,20 @@ def test_segm_r11_op_by_op(cuda_ok, model):
     o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
     kinds = check_net_ops(m, o, sw.weights, "segm_r11")
     assert ("pw", "tf32") in kinds and ("dw", "ffma") in kinds, kinds
+
+
+def test_segm_r11_pipelined_io(cuda_ok, model):
+    """The shipped model through run_pipelined (its output is a channel alias
+    of the last resize, resolved to that tensor) equals eager steps."""
+    sw, fx = model
+    inp, x = _input(sw, [5, 6, 7])
+    out = sw.outputs[0]
+    eager = NetModel(sw.nodes, sw.weights, 1, sw.inputs, sw.outputs, sw.states, sw.consts)
+    want = [eager.step({inp: torch.from_numpy(x[k:k + 1]).cuda()})[out].cpu().numpy() for k in range(3)]
+    pm = NetModel(sw.nodes, sw.weights, 1, sw.inputs, sw.outputs, sw.states, sw.consts)
+    host_in = [{inp: torch.from_numpy(x[k:k + 1]).pin_memory()} for k in range(3)]
+    host_out = [{out: torch.empty(want[0].shape).pin_memory()} for _ in range(3)]
+    pm.run_pipelined(host_in, host_out)
+    torch.cuda.synchronize()
+    for k in range(3):
+        assert np.array_equal(host_out[k][out].numpy(), want[k]), k
