@@ -312,7 +312,7 @@ def run_rvm(args, world, rank, dev):
                "pha": torch.empty((n, rvm.H, rvm.W, 1)).pin_memory()} for _ in range(2)]
     fgr_h, pha_h = outs_h[0]["fgr"], outs_h[0]["pha"]
     ins_h = [{"src": frames[k % 2]} for k in range(args.steps)]
-    model.run_pipelined(ins_h[:2], outs_h)  # warm-up (captures the slot graphs)
+    model.run_pipelined([{"src": frames[k]} for k in range(2)], outs_h)  # warm-up (captures the slot graphs)
     torch.cuda.synchronize()
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
