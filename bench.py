@@ -218,6 +218,10 @@ def run_reference(args, rank):
 # ------------------------------------------------------ config 5: RVM net ---
 
 RVM_METRIC = "RVM 144x256 frames/s, 1024 streams x 8 frames"
+# DRAM bytes per frame of the config-5 step's dominant launch (ncu at 16
+# streams, read + write, divided by 16; the capture's summary sits with the
+# ncu summaries under profiles/)
+RVM_TRAFFIC_PER_FRAME = {"d0.conv1": 6253072}
 
 
 def rvm_cpu_baseline(threads: int, min_seconds: float = 10.0):
@@ -345,7 +349,9 @@ def run_rvm(args, world, rank, dev):
         roof = {"bound": "tensor", "achieved": fl / sec / 1e12, "peak": pk["bf16_tflops"] / 2.0, "unit": "TFLOP/s"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
     roof["achieved"] = round(roof["achieved"], 3)
-    roof["traffic"] = None
+    tpf = RVM_TRAFFIC_PER_FRAME.get(top.node.out)
+    roof["traffic"] = int(tpf * n) if tpf is not None else None
+    roof["traffic_src"] = "ncu dram bytes at 16 streams, scaled by frames" if tpf is not None else None
     roof["kernel"] = f"{top.node.out} ({top.node.kind}" + (f" {top.plan.kernel}/{top.plan.math})" if top.plan else ")")
     roof["share"] = round(per_op[i] / sum(per_op), 4)
     line = {
