@@ -183,11 +183,40 @@ def cpu_model_name():
     return "unknown"
 
 
+def run_reference_rvm(args, threads):
+    """--impl reference --workload rvm: the oracle chain of the RVM net, one
+    stream-frame per core, each step a ~2 s sample."""
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, _, _ = rvm_cpu_baseline(threads, min_seconds=2.0)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    return value, wall, {"workload": "RVM-style matting net 144x256 (BASELINE config 5), CPU sample",
+                         "h": 144, "w": 256}, "stream-frames (zero recurrent state)"
+
+
 def run_reference(args, rank):
     """--impl reference: the CPU restatement of ai-cpu on all host cores."""
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
+    if getattr(args, "workload", "segnet") == "rvm":
+        value, wall, config, what = run_reference_rvm(args, threads)
+        line = {
+            "impl": "reference", "metric": RVM_METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / max(args.steps, 1), 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config,
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{what}, one per core, ~2 s per step; CPU restatement of crates/ai-cpu "
+                                       f"compiled -O3 -ffp-contract=off; {cpu_model_name()}"},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the Rust reference cannot be built here (no Rust toolchain); this arm runs its C restatement",
+        }
+        print(json.dumps(line), flush=True)
+        return 0
     frames = max(threads, 64)
     for _ in range(args.warmup):
         cpu_baseline(threads, threads)
