@@ -79,3 +79,72 @@ def test_oracle_matches_golden(fixture):
     x = oracle.XorShift32(int(fixture["seed"])).vec_f32(h * w * c).reshape(1, h, w, c)
     t = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts).step({inp: x}, {})
     assert np.array_equal(t[sw.outputs[0]][0], fixture["output"])
+
+
+def _container(graph: dict, blob: bytes) -> bytes:
+    """A .sw container (crates/ai-core/src/format/header.rs:1-14 layout)."""
+    import json as _json
+    js = _json.dumps(graph).encode()
+    off = 32
+    blob_off = -(-(off + len(js)) // 256) * 256
+    hdr = b"SW1\x00" + struct.pack("<IIIQQ", 1, 0, 256, off, len(js))
+    return hdr + js + b"\x00" * (blob_off - off - len(js)) + blob
+
+
+def test_synthetic_container_every_op_kind():
+    """A small recurrent graph with the op kinds segm_r11 does not use: SE
+    gate (two FCs), scalar-first and channel-vector Binary operands, Act,
+    Chcopy, Mix, Avgpool and a state pair; the reader lowers it and the
+    oracle runs two steps, the state feeding back."""
+    rng = np.random.default_rng(0)
+    parts, offs = [], {}
+
+    def put(name, arr):
+        a = np.ascontiguousarray(arr, np.float32).reshape(-1)
+        offs[name] = {"off": sum(len(p) for p in parts), "len": a.nbytes}
+        parts.append(a.tobytes())
+
+    c = 8
+    w_pw, kg = pack.pack_weights_conv(rng.standard_normal(c * c).astype(np.float32), c, c, 1, 1, 4)
+    put("w", w_pw); put("b", pack.pack_bias(rng.uniform(-0.1, 0.1, c), c))
+    w1, _ = pack.pack_weights_conv(rng.standard_normal(4 * c).astype(np.float32), 4, c, 1, 1, 4)
+    put("w1", w1); put("b1", pack.pack_bias(np.zeros(4), 4))
+    w2, _ = pack.pack_weights_conv(rng.standard_normal(4 * c).astype(np.float32), c, 4, 1, 1, 4)
+    put("w2", w2); put("b2", pack.pack_bias(np.zeros(c), c))
+    put("cv", pack.pack_nhwc(rng.uniform(0.5, 1.5, c)))
+    T = lambda name, h, w, ch: {"name": name, "h": h, "w": w, "c": ch, "dt": "f32", "alias": None, "last_use": 0}
+    tensors = [T("x", 8, 8, c), T("h", 8, 8, c), T("y", 8, 8, c), T("g", 1, 1, c), T("ys", 8, 8, c),
+               T("z", 8, 8, c), T("zz", 8, 8, c), T("h_out", 8, 8, c), T("p", 4, 4, c), T("q", 4, 4, 4),
+               T("r", 4, 4, 4)]
+    ops = [
+        {"kind": "conv", "in": 0, "out": 2, "res": None, "cin": c, "cout": c, "kh": 1, "kw": 1, "sh": 1, "sw": 1,
+         "pad": [0, 0, 0, 0], "d": 1, "groups": 1, "act": "relu", "w": offs["w"], "b": offs["b"], "kg_pad": kg},
+        {"kind": "se_gate", "in": 2, "out": 3, "c_mid": 4, "act1": "relu", "w1": offs["w1"], "b1": offs["b1"],
+         "fc2": {"c_out": c, "act": "hardsigmoid", "w": offs["w2"], "b": offs["b2"]}},
+        {"kind": "binary", "a": 2, "b": {"cvectensor": {"tid": 3}}, "out": 4, "op": "mul", "act": "none"},
+        {"kind": "binary", "a": 4, "b": {"scalar": {"v": 1.0, "first": True}}, "out": 5, "op": "sub", "act": "none"},
+        {"kind": "binary", "a": 5, "b": {"cvec": {"w": offs["cv"], "c": c}}, "out": 6, "op": "mul",
+         "act": "sigmoid"},
+        {"kind": "mix", "z": 6, "a": 1, "b": 4, "out": 7},
+        {"kind": "avgpool", "in": 7, "out": 8, "kh": 2, "kw": 2, "sh": 2, "sw": 2, "pad": [0, 0, 0, 0]},
+        {"kind": "chcopy", "in": 8, "out": 9, "src_c": 2, "n": 4},
+        {"kind": "act", "in": 9, "out": 10, "act": "tanh"},
+    ]
+    graph = {"name": "synthetic", "size": {"h": 8, "w": 8}, "dt_default": "f32", "tensors": tensors,
+             "inputs": [0, 1], "outputs": [10, 7], "states": [{"input": 1, "output": 7}], "ops": ops}
+    sw = load_sw(_container(graph, b"".join(parts)))
+    kinds = collections.Counter(nd.kind for nd in sw.nodes)
+    assert kinds == {"conv": 3, "gpool": 1, "binary": 3, "mix": 1, "avgpool": 1, "chcopy": 2}
+    assert sw.states == {"t1": "t7"} and sw.inputs == {"t0": (8, 8, c), "t1": (8, 8, c)}
+    assert sw.outputs == ["t10", "t7"]
+    o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
+    x = rng.uniform(-1, 1, (2, 8, 8, c)).astype(np.float32)
+    st = o.zero_state(2)
+    out1 = o.step({"t0": x}, st)
+    out2 = o.step({"t0": x}, {"t1": out1["t7"]})
+    # step 1 from zero state: h' = 0 + z (y_se - 0) = z * y_se
+    assert np.allclose(out1["t7"], out1["t6"] * out1["t4"], rtol=1e-6, atol=1e-7)
+    # step 2 mixes the carried state: h' = h + z (y_se - h)
+    h = out1["t7"]
+    assert np.allclose(out2["t7"], h + out2["t6"] * (out2["t4"] - h), rtol=1e-5, atol=1e-6)
+    assert out2["t10"].shape == (2, 4, 4, 4) and np.all(np.abs(out2["t10"]) <= 1.0)
