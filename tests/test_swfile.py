@@ -91,11 +91,10 @@ def _container(graph: dict, blob: bytes) -> bytes:
     return hdr + js + b"\x00" * (blob_off - off - len(js)) + blob
 
 
-def test_synthetic_container_every_op_kind():
-    """A small recurrent graph with the op kinds segm_r11 does not use: SE
-    gate (two FCs), scalar-first and channel-vector Binary operands, Act,
-    Chcopy, Mix, Avgpool and a state pair; the reader lowers it and the
-    oracle runs two steps, the state feeding back."""
+def synthetic_sw():
+    """A small recurrent .sw graph with the op kinds segm_r11 does not use:
+    SE gate (two FCs), scalar-first and channel-vector Binary operands, Act,
+    Chcopy, Mix, Avgpool and a state pair."""
     rng = np.random.default_rng(0)
     parts, offs = [], {}
 
@@ -132,7 +131,15 @@ def test_synthetic_container_every_op_kind():
     ]
     graph = {"name": "synthetic", "size": {"h": 8, "w": 8}, "dt_default": "f32", "tensors": tensors,
              "inputs": [0, 1], "outputs": [10, 7], "states": [{"input": 1, "output": 7}], "ops": ops}
-    sw = load_sw(_container(graph, b"".join(parts)))
+    return load_sw(_container(graph, b"".join(parts)))
+
+
+def test_synthetic_container_every_op_kind():
+    """The reader lowers every op kind of synthetic_sw() and the oracle runs
+    two steps, the state feeding back."""
+    rng = np.random.default_rng(1)
+    c = 8
+    sw = synthetic_sw()
     kinds = collections.Counter(nd.kind for nd in sw.nodes)
     assert kinds == {"conv": 3, "gpool": 1, "binary": 3, "mix": 1, "avgpool": 1, "chcopy": 2}
     assert sw.states == {"t1": "t7"} and sw.inputs == {"t0": (8, 8, c), "t1": (8, 8, c)}

@@ -97,3 +97,20 @@ def test_segm_r11_pipelined_io(cuda_ok, model):
     torch.cuda.synchronize()
     for k in range(3):
         assert np.array_equal(host_out[k][out].numpy(), want[k]), k
+
+
+def test_synthetic_sw_graph_op_by_op(cuda_ok):
+    """The synthetic .sw graph (SE gate FCs over n frames of 1x1, scalar /
+    channel-vector operands, Mix with carried state, Avgpool, Chcopy, Act)
+    on the GPU, every op of two steps within its own bar."""
+    from tests.test_swfile import synthetic_sw
+    sw = synthetic_sw()
+    m = NetModel(sw.nodes, sw.weights, 3, sw.inputs, sw.outputs, sw.states, sw.consts)
+    o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
+    x = np.random.default_rng(2).uniform(-1, 1, (3, 8, 8, 8)).astype(np.float32)
+    for t in range(2):
+        m.bufs["t0"].copy_(torch.from_numpy(x))
+        m.record()
+        torch.cuda.synchronize()
+        check_net_ops(m, o, sw.weights, f"synthetic step {t}")
+        m.advance()
