@@ -84,7 +84,6 @@ SIGNATURES = {
     "aie_gpool": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, _vp, _vp]),
     "aie_avgpool": (C.c_int, [C.c_uint32] * 8 + [C.POINTER(C.c_uint32), _vp, _vp, _vp]),
     "aie_channel_copy": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, C.c_int32, TView, _vp]),
-    "aie_resize_up2_view": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _vp, C.c_int32, TView, _vp]),
     "aie_concat": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(TView), C.POINTER(C.c_uint32), C.c_uint32,
                              TView, _vp]),
 }

@@ -948,8 +948,6 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
             u.x = (const float *)in;
             u.add = (const float *)add;
             u.y = (float *)out;
-            u.y_stride = c;
-            u.y_coff = 0;
             u.n = n; u.ih = ih; u.iw = iw; u.c = c; u.act = act;
             const int G = c1 ? 1 : (int)(c / 4), Wt = c1 ? (int)(iw / 4) : (int)iw;
             u.div_g = make_fastdiv(G);
@@ -1170,10 +1168,6 @@ extern "C" int aie_concat(uint32_t n, uint32_t px, uint32_t nparts, const aie_tv
     a.y = (float *)y.p;
     a.y_stride = y.stride;
     a.y_coff = y.coff;
-    a.inplace = 0;
-    for (uint32_t i = 0; i < nparts; i++)
-        if (a.part[i].p == y.p && a.part[i].stride == y.stride && a.part[i].coff == y.coff + a.poff[i])
-            a.inplace |= 1u << i;
     a.c_out = (int)out_c;
     a.groups = (int)((out_c + 3) / 4);
     if ((uint64_t)n * px * a.groups >= (1ull << 31)) return fail(AIE_E_UNSUPPORTED, "concat larger than 2^31 groups");
@@ -1182,36 +1176,6 @@ extern "C" int aie_concat(uint32_t n, uint32_t px, uint32_t nparts, const aie_tv
     concat_kernel<<<elem_grid((long long)a.Q * a.groups), 256, 0, (cudaStream_t)stream>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "concat launch");
-    return AIE_OK;
-}
-
-extern "C" int aie_resize_up2_view(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, int32_t act,
-                                   aie_tview out, void *stream)
-{
-    int s;
-    if ((s = elem_sizes(n, ih * iw, c, "resize into a view"))) return s;
-    if (!in) return fail(AIE_E_INVALID, "resize into a view: null input");
-    if (act < 0 || act > AIE_ACT_RECIP) return fail(AIE_E_INVALID, "activation %d out of range", act);
-    EView y;
-    if ((s = make_eview(out, c, "resize out", &y))) return s;
-    if (c % 4 || (uintptr_t)in % 16 || !eview_vec(y))
-        return fail(AIE_E_ALIGN, "resize into a view: c %% 4 == 0, a 16-byte aligned input and output view "
-                                 "(pixel stride and first channel multiples of 4)");
-    Up2Args u;
-    u.x = (const float *)in;
-    u.add = nullptr;
-    u.y = (float *)y.p;
-    u.y_stride = y.stride;
-    u.y_coff = y.coff;
-    u.n = n; u.ih = ih; u.iw = iw; u.c = c; u.act = act;
-    u.div_g = make_fastdiv((int)(c / 4));
-    u.div_w = make_fastdiv((int)iw);
-    u.div_h = make_fastdiv((int)ih);
-    const long long threads = (long long)n * ih * iw * (c / 4);
-    if (threads + 256 >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "resize larger than 2^31 groups; split the batch");
-    resize_up2_kernel<false><<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(u);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "resize launch");
     return AIE_OK;
 }
 

@@ -315,10 +315,7 @@ __global__ void __launch_bounds__(256) chcopy_kernel(CopyArgs a)
 
 namespace aie {
 
-// Channel concat of up to kConcatMax parts into one output view, one pass
-// (a part that is already the output's own slice -- its producer wrote it
-// there -- is left in place, only groups it shares with a neighbour are
-// rewritten):
+// Channel concat of up to kConcatMax parts into one output view, one pass:
 // a thread owns one output pixel's group of four channels, gathers them
 // from whichever parts hold them and writes the group as one 16-byte store
 // where the output allows.  Lanes past the parts' total (the zero padding
@@ -338,7 +335,6 @@ struct ConcatArgs {
     int y_coff;
     unsigned Q;                 // n * px (< 2^31 / groups)
     int c_out, groups;          // output channels (>= the parts' total), ceil(c_out / 4)
-    unsigned inplace;           // parts already in place in the output (a producer wrote its slice)
     bool y_vec;
 };
 
@@ -351,8 +347,6 @@ __global__ void __launch_bounds__(256) concat_kernel(ConcatArgs a)
         float r[4];
         int p = 0;
         while (p + 1 < a.nparts && a.poff[p + 1] <= ch0) p++;
-        // a group wholly inside a part that is already in place stays as it is
-        if (((a.inplace >> p) & 1u) && ch0 + 4 <= a.poff[p + 1]) continue;
         const int lc = ch0 - a.poff[p];
         const EView &v = a.part[p];
         if (ch0 + 4 <= a.poff[p + 1] && ((uintptr_t)(v.p + (long long)q * v.stride + v.coff + lc) & 15) == 0) {

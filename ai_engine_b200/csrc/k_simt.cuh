@@ -559,8 +559,6 @@ __global__ void __launch_bounds__(256) input_u8_kernel(const uint8_t *__restrict
 struct Up2Args {
     const float *x, *add;
     float *y;
-    long long y_stride;  // C4 path: output pixel stride in floats (c when dense)
-    int y_coff;          // ... and first output channel (a channel slice of a wider tensor)
     int n, ih, iw, c, act;
     FastDiv div_g, div_w, div_h;  // thread -> (group, source column, source row)
 };
@@ -608,7 +606,7 @@ __global__ void __launch_bounds__(256) resize_up2_kernel(const Up2Args a)
                     o[2] = __fadd_rn(o[2], ad.z); o[3] = __fadd_rn(o[3], ad.w);
                 }
                 act_apply_strict_n<4>(a.act, o, c0, a.c);
-                *reinterpret_cast<float4 *>(a.y + px * a.y_stride + a.y_coff + c0) = make_float4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<float4 *>(a.y + px * a.c + c0) = make_float4(o[0], o[1], o[2], o[3]);
             }
         }
     } else {

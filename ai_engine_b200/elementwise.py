@@ -144,16 +144,3 @@ def concat(parts: Sequence[ViewLike], out: ViewLike, stream=None) -> None:
     cs = (C.c_uint32 * len(ps))(*[p.c for p in ps])
     check(_lib.load().aie_concat(out.frames, out.px, len(ps), arr, cs, out.c, out.tview(), _stream(stream)),
           "aie_concat")
-
-
-def resize_up2(x: torch.Tensor, out: ViewLike, act: str = "none", stream=None) -> None:
-    """Exact 2x half_pixel upsampling of a dense [n, h, w, c] tensor into a
-    channel view of a [n, 2h, 2w, C] tensor (aie_resize_up2_view)."""
-    out = _v(out)
-    n, ih, iw, c = x.shape
-    if (out.frames, out.px, out.c) != (n, 4 * ih * iw, c):
-        raise ValueError("the output view must be [n, 2h, 2w, c] channels of the input")
-    if not x.is_contiguous() or x.dtype != torch.float32:
-        raise TypeError("resize input must be a contiguous float32 tensor")
-    check(_lib.load().aie_resize_up2_view(n, ih, iw, c, C.c_void_p(x.data_ptr()), ACT_ID[act], out.tview(),
-                                          _stream(stream)), "aie_resize_up2_view")

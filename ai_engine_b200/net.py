@@ -150,25 +150,6 @@ class NetModel:
                 if c % 4 and users and all(u.kind == "conv" and u.ins[0] == nd.out for u in users) \
                         and nd.out not in self.outputs:
                     self.cpad[nd.out] = _pad4(c)
-        # an exact-2x resize whose output is only a concat part writes that
-        # part's channel slice of the concat buffer directly
-        # (aie_resize_up2_view); the concat leaves it in place
-        self.into_concat: Dict[str, Tuple[str, int]] = {}  # resize output -> (concat, first channel)
-        producer = {nd.out: nd for nd in self.nodes if isinstance(nd.out, str)}
-        for nd in self.nodes:
-            if nd.kind != "concat":
-                continue
-            width = self.cpad.get(nd.out, self.shapes[nd.out][2])
-            coff = 0
-            for part in nd.ins:
-                pr = producer.get(part)
-                h, w, c = self.shapes[part]
-                if (pr is not None and pr.kind == "resize" and len(consumers.get(part, [])) == 1
-                        and part not in self.outputs and c % 4 == 0 and coff % 4 == 0 and width % 4 == 0):
-                    sh_, sw_, _ = self.shapes[pr.ins[0]]
-                    if (h, w) == (2 * sh_, 2 * sw_):
-                        self.into_concat[part] = (nd.out, coff)
-                coff += c
         self.alias: Dict[str, Tuple[str, int, int]] = {}  # split output -> (base tensor, coff, c)
         self.bufs: Dict[str, torch.Tensor] = {}
         self.recs: List[_Rec] = []
@@ -191,11 +172,6 @@ class NetModel:
                         for name, c in zip(nd.out, nd.parts):
                             self.alias[name] = (base, coff, c)
                             coff += c
-                    self.recs.append(rec)
-                    continue
-                if nd.out in self.into_concat:
-                    cat, coff = self.into_concat[nd.out]
-                    self.alias[nd.out] = (cat, coff, self.shapes[nd.out][2])
                     self.recs.append(rec)
                     continue
                 alloc(nd.out, zero=nd.out in self.cpad)
@@ -281,11 +257,8 @@ class NetModel:
             elif k == "avgpool":
                 ew.avgpool(self.bufs[nd.ins[0]], self.bufs[nd.out], nd.size[:2], nd.size[2:], stream=stream)
             elif k == "resize":
-                if nd.out in self.into_concat:
-                    ew.resize_up2(self.tensor_for_resize(nd.ins[0]), self.view(nd.out), stream=stream)
-                else:
-                    resize_bilinear(self.tensor_for_resize(nd.ins[0]), nd.size[0], nd.size[1],
-                                    out=self.bufs[nd.out], stream=stream)
+                resize_bilinear(self.tensor_for_resize(nd.ins[0]), nd.size[0], nd.size[1], out=self.bufs[nd.out],
+                                stream=stream)
             elif k == "concat":
                 ew.concat([self.view(p) for p in nd.ins], ew.ChView(self.bufs[nd.out]), stream=stream)
             elif k == "chcopy":

@@ -359,20 +359,9 @@ AIE_API int aie_channel_copy(uint32_t n, uint32_t px, uint32_t c, aie_tview in, 
  * format/model.rs:156-160) and the conv's concat-into-conv parts
  * (Conv.srcs, model.rs:83-86; SrcView, crates/ai-gpu/src/kernels/common/
  * source.rs:17-80).  out_c may exceed the parts' total: those trailing
- * lanes are written as zero (a buffer padded to a multiple of 4 channels).
- * A part whose view is the output's own slice (its producer wrote it
- * there) is left in place. */
+ * lanes are written as zero (a buffer padded to a multiple of 4 channels). */
 AIE_API int aie_concat(uint32_t n, uint32_t px, uint32_t nparts, const aie_tview *parts, const uint32_t *part_c,
                        uint32_t out_c, aie_tview out, void *stream);
-
-/* Exact 2x half_pixel bilinear upsampling (the aie_resize_bilinear case
- * oh = 2 ih, ow = 2 iw, c % 4 == 0, no add) of a dense [n, ih, iw, c] batch
- * into a channel view: a Resize whose output is one part of a channel
- * concat writes that part's slice of the concat's buffer directly (the
- * concat-into-resize fusion of SwOp::Resize.srcs, crates/ai-core/src/format/
- * model.rs:144-154), and aie_concat then leaves the slice in place. */
-AIE_API int aie_resize_up2_view(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, int32_t act,
-                                aie_tview out, void *stream);
 
 /* Human-readable status, and the detail message of this thread's last
  * failure (copied into buf, NUL-terminated; returns its full length). */

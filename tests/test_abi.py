@@ -224,13 +224,3 @@ def test_concat_rejects_bad_arguments(lib):
     cs0 = (C.c_uint32 * 2)(2, 0)
     assert lib.aie_concat(1, 4, 2, parts, cs0, 4, good, None) == -2
     assert lib.aie_concat(1, 4, 2, None, cs, 4, good, None) == -2
-
-
-def test_resize_up2_view_rejects_bad_arguments(lib):
-    TV = _lib.TView
-    buf = (C.c_float * 256)()
-    good = TV(C.cast(buf, C.c_void_p), 8, 0)
-    assert lib.aie_resize_up2_view(1, 2, 2, 4, None, 0, good, None) == -2
-    assert lib.aie_resize_up2_view(0, 2, 2, 4, C.cast(buf, C.c_void_p), 0, good, None) == -2
-    assert lib.aie_resize_up2_view(1, 2, 2, 4, C.cast(buf, C.c_void_p), 0, TV(C.cast(buf, C.c_void_p), 8, 2), None) == -5
-    assert lib.aie_resize_up2_view(1, 2, 2, 3, C.cast(buf, C.c_void_p), 0, good, None) == -5

@@ -186,24 +186,3 @@ def test_concat(cuda_ok, widths, pad):
     got = out.cpu().numpy()
     _check(got[..., :want.shape[-1]], want)
     assert not got[..., want.shape[-1]:].any()
-
-
-def test_resize_into_concat_slice(cuda_ok):
-    """An exact-2x resize written straight into its slice of a concat buffer
-    (aie_resize_up2_view) and the concat run afterwards with that part in
-    place: the buffer equals resize-then-concat, and the in-place channels
-    are left untouched by the concat."""
-    from ai_engine_b200.conv import resize_bilinear
-    rng = XorShift32(7701)
-    n, h, w = 2, 5, 7
-    lo = _rand(rng, n, h, w, 32)
-    skip = _rand(rng, n, 2 * h, 2 * w, 40)
-    img = _rand(rng, n, 2 * h, 2 * w, 3)
-    glo = torch.from_numpy(lo).cuda()
-    up = resize_bilinear(glo, 2 * h, 2 * w)
-    want = np.concatenate([up.cpu().numpy(), skip, img, np.zeros((n, 2 * h, 2 * w, 1), np.float32)], -1)
-    cat = torch.full((n, 2 * h, 2 * w, 76), 9.0, device="cuda")
-    ew.resize_up2(glo, ew.ChView(cat, 0, 32))
-    assert np.array_equal(cat[..., :32].cpu().numpy(), up.cpu().numpy())
-    ew.concat([ew.ChView(cat, 0, 32), torch.from_numpy(skip).cuda(), torch.from_numpy(img).cuda()], cat)
-    _check(cat.cpu().numpy(), want)
