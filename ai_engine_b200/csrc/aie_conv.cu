@@ -1201,14 +1201,14 @@ extern "C" int aie_device_status(void *stream, uint32_t *code_out)
 
 // ------------------------------------------------- no-allocation entry ---
 //
-// Some callers cannot allocate device memory once they are running.
-// Examples: a real-time frame loop whose latency budget cannot absorb
-// cudaMalloc's device synchronisation; a plugin inside a host application
-// that hands over only its own tensors; code that runs while a stream is
-// being captured into a CUDA graph.  For them the split-K scratch comes from
-// this fixed array inside the library instead of a caller workspace.
+// Some callers cannot allocate device memory once they are running: a
+// real-time frame loop whose latency budget cannot absorb cudaMalloc's
+// implicit device synchronisation, or a plugin inside a host application
+// that owns the device allocator and hands over only its own tensors.  For
+// them the split-K scratch comes from this fixed array inside the library
+// instead of a caller workspace.
 //
-// The array lives in every GPU's memory that loads this library, from
+// The array lives in the memory of every GPU that loads this library, from
 // module load until process exit.  All calls share it and it keeps the
 // previous call's contents: the split-K tickets are cleared on the stream
 // before every launch and the partials are written before they are read,
@@ -1216,8 +1216,14 @@ extern "C" int aie_device_status(void *stream, uint32_t *code_out)
 // (e.g. on different streams) race on it.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[AIE_NOALLOC_SCRATCH_BYTES];
 
+typedef CUresult (*PFN_ctxGetCurrent)(CUcontext *);
+
 static std::mutex g_noalloc_mu;
-static void *g_noalloc_addr[64];  // device address of the array, per device ordinal
+// The array's device address per device ordinal, with the context it was
+// looked up in: after cudaDeviceReset (or under another context on the same
+// ordinal) the address is looked up again instead of reused.
+static void *g_noalloc_addr[64];
+static CUcontext g_noalloc_ctx[64];
 
 extern "C" int aie_conv_run_noalloc(const aie_plan *p, const void *in, const void *w, const void *b,
                                     const void *res, void *out, void *stream)
@@ -1234,13 +1240,29 @@ extern "C" int aie_conv_run_noalloc(const aie_plan *p, const void *in, const voi
         CUDA_TRY(cudaGetDevice(&dev));
         if (dev < 0 || dev >= 64) return fail(AIE_E_UNSUPPORTED, "device ordinal %d out of range", dev);
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        if (!g_noalloc_addr[dev]) {
-            // first call on this device (which is current): the array's name is
-            // only a host-side stand-in; ask the runtime for its device address
+        static PFN_ctxGetCurrent ctx_current = nullptr;
+        if (!ctx_current) {
+            void *fn = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+                q != cudaDriverEntryPointSuccess || !fn)
+                return fail(AIE_E_CUDA, "cuCtxGetCurrent unavailable");
+            ctx_current = (PFN_ctxGetCurrent)fn;
+        }
+        CUcontext ctx = nullptr;
+        if (ctx_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+        if (!ctx || !g_noalloc_addr[dev] || g_noalloc_ctx[dev] != ctx) {
+            // first call on this device (which is current) or in this context:
+            // the array's name is only a host-side stand-in for it; ask the
+            // runtime for its device address
             void *addr = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
             if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+            // the lookup made the runtime's context current if none was
+            if (!ctx && (ctx_current(&ctx) != CUDA_SUCCESS || !ctx))
+                return fail(AIE_E_CUDA, "no current CUDA context");
             g_noalloc_addr[dev] = addr;
+            g_noalloc_ctx[dev] = ctx;
         }
         ws = g_noalloc_addr[dev];
     }

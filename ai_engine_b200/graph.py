@@ -38,6 +38,7 @@ class OpRecord:
     up: Optional[str] = None          # kind "dwpw": source whose exact-2x resize is added to the depthwise input
     blk: Optional[Tuple[ConvPlan, ConvPlan, ConvPlan]] = None  # kind "mb": expand, depthwise, project plans
     out2: Optional[str] = None        # kind "stempw": the fused 1x1's output (its plan in `head`)
+    members: Tuple[str, ...] = ()     # fused kinds: the graph's conv (and resize) names this launch runs
 
 
 def infer_shapes(graph: Sequence[tuple], in_hwc: Tuple[int, int, int]) -> Dict[str, Tuple[int, int, int]]:
@@ -200,13 +201,14 @@ class Model:
                     continue  # recorded with its depthwise producer / its block
                 if out in block_of:
                     eop, dop, pop, plans = block_of[out]
-                    rec = OpRecord("mb", out, eop[2], conv=pop[3], res=pop[4], blk=plans)
+                    rec = OpRecord("mb", out, eop[2], conv=pop[3], res=pop[4], blk=plans,
+                                   members=(eop[1], dop[1], pop[1]))
                     self.bufs[out] = torch.empty((n, *self.shapes[out]), dtype=torch.float32, device=self.device)
                     self.ops.append(rec)
                     continue
                 if out in head_of:
                     hop = head_of[out]
-                    rec = OpRecord("dwpw", hop[1], src, conv=op[3], up=tail_up.get(src))
+                    rec = OpRecord("dwpw", hop[1], src, conv=op[3], up=tail_up.get(src), members=(out, hop[1]))
                     rec.plan, rec.head = head_plans[out]
                     self.bufs[hop[1]] = torch.empty((n, *self.shapes[hop[1]]), dtype=torch.float32, device=self.device)
                     self.ops.append(rec)
@@ -239,6 +241,7 @@ class Model:
                 if pw is None:
                     continue
                 st.kind, st.head, st.out2 = "stempw", pw.plan, pw.out
+                st.members = (st.out, pw.out)
                 self.ops.remove(pw)
         self.graph_exec = None
 
@@ -251,6 +254,23 @@ class Model:
             elif r.plan is not None:
                 total += r.plan.flops + (r.head.flops if r.head is not None else 0)
         return total
+
+    def tf32_convs(self) -> set:
+        """Names of the graph's convs that run on the TF32 tensor cores
+        (fused launches included): the convs whose operands a TF32-emulating
+        oracle truncates."""
+        names = set()
+        for r in self.ops:
+            if r.kind == "conv" and r.plan.math == "tf32":
+                names.add(r.out)
+            elif r.kind == "stempw":
+                names.update(r.members)
+            elif r.kind == "mb":  # the two 1x1 GEMMs; the depthwise between them runs on the CUDA cores
+                ex, _, pj = r.blk
+                names.update(m for m, p in ((r.members[0], ex), (r.members[2], pj)) if p.math == "tf32")
+            elif r.kind == "dwpw" and r.plan.math == "tf32":
+                names.add(r.members[0])
+        return names
 
     def layer_table(self):
         rows = []

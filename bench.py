@@ -2,18 +2,22 @@
 """Benchmark: MNv4-style segmentation net at 160x288, 256 frames per GPU.
 
 One step = one forward pass of the conv graph over a batch of 256 frames
-resident in HBM (configs 1-3 are parity-test cases).
-Frames shard across GPUs with no collective on the hot path (weak
-scaling); the only collective is a max-reduce of the timings.
+resident in HBM.  Frames shard across GPUs with no
+collective on the hot path (weak scaling); the only collective is a
+max-reduce of the timings.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload rvm [--streams S]
+  python bench.py --workload cfg2 | cfg3          # BASELINE configs 2 / 3, one line per shape
 
 Prints one JSON line (rank 0).  ``--workload rvm`` measures the recurrent
 matting net instead (144x256, S = 1024 streams sharded across the GPUs, one
-step = one frame of every stream, recurrent state resident on the GPU).  --impl reference times the CPU
-restatement of ai_engine's ai-cpu path on all host cores (the Rust
-reference itself cannot be built here: no Rust toolchain).
+step = one frame of every stream, recurrent state resident on the GPU).
+``--workload cfg2`` / ``cfg3`` time each conv of the config's sweep as one
+launch over its batch and report TFLOP/s against the TF32 tensor peak.
+--impl reference times the CPU restatement of ai_engine's ai-cpu path on
+all host cores (the Rust reference itself cannot be built here: no Rust
+toolchain).
 """
 from __future__ import annotations
 
@@ -24,6 +28,7 @@ import statistics
 import sys
 import threading
 import time
+import zlib
 
 import numpy as np
 
@@ -83,8 +88,9 @@ def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
 # ------------------------------------------------------------------ clocks ---
@@ -123,7 +129,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.02)
+            self._stop.wait(0.004)
 
     def __enter__(self):
         if self._h is not None:
@@ -148,10 +154,12 @@ class ClockSampler:
 _CPU_MODEL = {}
 
 
-def cpu_baseline(frames: int, threads: int, min_seconds: float = 0.0):
-    """ai-cpu restatement, throughput mode (one frame per core): `frames`
-    frames of the same workload per pass, passes repeated until at least
-    `min_seconds` have elapsed.  Returns (frames/s, seconds, frames run)."""
+def cpu_baseline(frames: int, threads: int, min_seconds: float = 0.0, mode: str = "throughput"):
+    """ai-cpu restatement: `frames` frames of the same workload per pass,
+    passes repeated until at least `min_seconds` have elapsed.  mode
+    "throughput": one frame per core; "bands": ai-cpu's own threading, one
+    frame at a time with each conv's output rows split over `threads`.
+    Returns (frames/s, seconds, frames run)."""
     from ai_engine_b200 import segnet
     from oracle.graph import OracleModel
     if "m" not in _CPU_MODEL:
@@ -165,7 +173,7 @@ def cpu_baseline(frames: int, threads: int, min_seconds: float = 0.0):
     done = 0
     t0 = time.perf_counter()
     while True:
-        m.run_batch(x[:frames], threads=threads)
+        m.run_batch(x[:frames], threads=threads, mode=mode)
         done += frames
         dt = time.perf_counter() - t0
         if dt >= min_seconds:
@@ -202,6 +210,33 @@ def run_reference(args, rank):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
+    if args.workload in ("cfg2", "cfg3"):
+        for label, op, n, ih, iw, split in sweep_shapes(args.workload, args.batch):
+            rng = np.random.default_rng(zlib.crc32(label.encode()))
+            fan_in = op.cin * op.kh * op.kw
+            w = (rng.standard_normal(op.cout * fan_in) / np.sqrt(fan_in)).astype(np.float32)
+            b = rng.uniform(-0.1, 0.1, op.cout).astype(np.float32)
+            gfs, t0 = [], time.perf_counter()
+            for _ in range(args.steps):
+                gf, fps, done = conv_cpu_baseline(op, ih, iw, w, b, threads, min_seconds=0.5)
+                gfs.append(gf)
+            value = statistics.median(gfs) / 1000.0
+            line = {
+                "impl": "reference", "metric": SWEEP_METRIC[args.workload], "value": round(value, 6),
+                "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(1000 * (time.perf_counter() - t0) / max(args.steps, 1), 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": f"BASELINE {args.workload}: {label}, CPU sample (one frame per step)"},
+                "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                                 "sample": f"one frame per step, ai-cpu row bands over {threads} threads, "
+                                           f">= 0.5 s per step; {cpu_model_name()}"},
+                "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "the Rust reference cannot be built here (no Rust toolchain); this arm runs its C restatement",
+            }
+            print(json.dumps(line), flush=True)
+        return 0
     if getattr(args, "workload", "segnet") == "rvm":
         value, wall, config, what = run_reference_rvm(args, threads)
         line = {
@@ -510,6 +545,178 @@ def run_segm_r11(args, world, rank, dev):
     return 0
 
 
+# ------------------------------------------- configs 2 and 3: single convs ---
+
+CFG2 = [(16, 16), (32, 64), (64, 128), (128, 256)]          # (Cin, Cout), 3x3 pad 1 at 160x288
+CFG3 = [(960, 1280), (1280, 960), (512, 2048)]              # (K, N), 1x1 at 10x18
+SWEEP_METRIC = {"cfg2": "conv GEMM TFLOP/s vs TF32 peak (BASELINE config 2: 3x3 implicit GEMM at 160x288)",
+                "cfg3": "conv GEMM TFLOP/s vs TF32 peak (BASELINE config 3: split-K 1x1 GEMM at 10x18)"}
+L2_BYTES = 126 << 20
+
+
+def sweep_shapes(which: str, batch: int):
+    """(label, Conv2d, n, ih, iw, split) of the BASELINE config's sweep, in the
+    reference's own shape-table spirit (crates/ai-gpu/src/bench.rs:166-260):
+    config 2 at `batch` frames for every (Cin, Cout) and stride; config 3 at
+    batch 1, 64 and 256 with the auto split, plus batch 1 at every split factor."""
+    from ai_engine_b200 import Conv2d
+    out = []
+    if which == "cfg2":
+        for cin, cout in CFG2:
+            for s in (1, 2):
+                out.append((f"3x3 s{s} {cin}->{cout} B={batch}", Conv2d.same(cin, cout, 3, s, "hardswish"),
+                            batch, 160, 288, 0))
+    else:
+        for k, n in CFG3:
+            for b in (256, 64, 1):
+                out.append((f"1x1 {k}->{n} B={b} split auto", Conv2d.pointwise(k, n, "none"), b, 10, 18, 0))
+            for sp in (1, 4, 8, 16):
+                out.append((f"1x1 {k}->{n} B=1 split {sp}", Conv2d.pointwise(k, n, "none"), 1, 10, 18, sp))
+    return out
+
+
+def conv_cpu_baseline(op, ih, iw, w, b, threads, min_seconds=1.5):
+    """One frame through the ai-cpu restatement in ai-cpu's own threading
+    (row bands over all cores, crates/ai-cpu/src/model.rs:421-441), repeated
+    for at least `min_seconds`: (GFLOP/s, frames/s, frames run)."""
+    import oracle
+    p = oracle.Plan(op, ih, iw, w, b)
+    x = np.random.default_rng(5).uniform(-1, 1, (ih, iw, op.cin)).astype(np.float32)
+    y = np.empty((p.oh, p.ow, op.cout), np.float32)
+    p.run_frame(x, y, threads=threads)  # warm-up
+    done, t0 = 0, time.perf_counter()
+    while True:
+        p.run_frame(x, y, threads=threads)
+        done += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    flops = 2 * p.oh * p.ow * op.cout * (op.cin // op.groups) * op.kh * op.kw
+    return flops * done / dt / 1e9, done / dt, done
+
+
+def run_sweep(args, world, rank, dev):
+    """BASELINE configs 2 and 3: each shape of the sweep as one conv launch
+    over its batch (frames resident in HBM), K launches timed one by one
+    with CUDA events on the launching stream, the L2 flushed (a 256 MB
+    write) before every launch so that small shapes are not served from L2.
+    One JSON line per shape; frames shard across GPUs (each rank runs the
+    same shapes on its own batch, weak scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from ai_engine_b200.conv import ConvPlan
+
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    pk = peaks()
+    hbm = pk["hbm_gbs"]
+    tf32 = pk["bf16_tflops"] / 2.0            # TF32 dense = half the bf16 rate
+    tf32_sus = pk["bf16_tflops_sustained"] / 2.0
+    threads = os.cpu_count() or 1
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for label, op, n, ih, iw, split in sweep_shapes(args.workload, args.batch):
+        rng = np.random.default_rng(zlib.crc32(label.encode()))
+        fan_in = op.cin * op.kh * op.kw
+        if args.workload == "cfg2":  # Kaiming-normal W, U(-0.1, 0.1) bias
+            w = (rng.standard_normal(op.cout * fan_in) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+            b = rng.uniform(-0.1, 0.1, op.cout).astype(np.float32)
+        else:                        # W ~ N(0, 1/K), no bias
+            w = (rng.standard_normal(op.cout * fan_in) / np.sqrt(fan_in)).astype(np.float32)
+            b = np.zeros(op.cout, np.float32)
+        plan = ConvPlan(op, n, ih, iw, math=args.math, split_k=split, device=dev).load_weights(w, b)
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + rank)
+        x = torch.rand((n, ih, iw, op.cin), device=dev, generator=g).mul_(2).sub_(1)
+        out = torch.empty(plan.out_shape(), dtype=torch.float32, device=dev)
+        for _ in range(max(args.warmup, 3)):
+            plan(x, out=out)
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        sampler = ClockSampler(dev.index)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with sampler:
+            for e0, e1 in evs:
+                flush.zero_()
+                e0.record(stream)
+                plan(x, out=out)
+                e1.record(stream)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs) / len(evs))
+        fl, by = plan.flops, plan.min_bytes
+        tflops = fl / (ms / 1000.0) / 1e12
+        ai = fl / by
+        roof_t = min(tf32, ai * hbm / 1000.0)  # TFLOP/s the launch could reach: min(peak, AI x HBM)
+        if ai * hbm / 1000.0 >= tf32:
+            roof = {"bound": "tensor", "achieved": tflops, "peak": tf32, "unit": "TFLOP/s",
+                    "frac_sustained": round(tflops / tf32_sus, 4), "peak_src": pk["src"] + " (TF32 = bf16/2, burst)"}
+        else:
+            roof = {"bound": "hbm", "achieved": by / (ms / 1000.0) / 1e9, "peak": hbm, "unit": "GB/s",
+                    "peak_src": pk["src"]}
+        roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+        roof["achieved"] = round(roof["achieved"], 3)
+        roof["traffic"] = None
+        roof["kernel"] = f"{plan.kernel}/{plan.math}" + (f" split {plan.info.split_k}" if plan.info.split_k > 1 else "")
+        # end to end through the public API: pinned input up, the conv, output down, every step
+        e2e_steps = min(args.steps, 5)
+        xh = torch.empty(x.shape, dtype=torch.float32).pin_memory()
+        xh.copy_(x)
+        oh_ = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+        xd = torch.empty_like(x)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(e2e_steps):
+            xd.copy_(xh, non_blocking=True)
+            plan(xd, out=out)
+            oh_.copy_(out, non_blocking=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1)) / e2e_steps
+        line = {
+            "metric": SWEEP_METRIC[args.workload], "value": round(tflops * world, 3), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": plan.math,
+            "data": "synthetic",
+            "config": {"workload": f"BASELINE {args.workload}: {label}", "per_gpu_batch": n, "h": ih, "w": iw,
+                       "cin": op.cin, "cout": op.cout, "stride": op.sh, "act": op.act, "math": args.math,
+                       "split_k": plan.info.split_k, "flop_per_launch": fl, "min_bytes_per_launch": by,
+                       "arith_intensity": round(ai, 2), "l2": "flushed before every timed launch (256 MB write)"},
+            "frames_per_s": round(n * world / (ms / 1000.0), 2),
+            "of_roofline": round(tflops / roof_t, 4),
+            "roofline": roof,
+            "e2e": {"value": round(fl * world / (e2e_ms / 1000.0) / 1e12, 4), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(x.numel() * 4), "d2h_bytes_per_step": int(out.numel() * 4)},
+            "gpu_launches": args.steps,
+            "clocks": sampler.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline and rank == 0:
+            gf, fps, done = conv_cpu_baseline(op, ih, iw, w, b, threads)
+            line["cpu_baseline"] = {"value": round(gf / 1000.0, 6), "unit": "TFLOP/s", "cores": threads,
+                                    "kind": "port", "gflops": round(gf, 2), "frames_per_s": round(fps, 3),
+                                    "sample": f"{done} frame(s) of the same conv, ai-cpu row bands over {threads} "
+                                              f"threads, >= 1.5 s on {cpu_model_name()}"}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        del plan, x, out, xh, oh_, xd
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # --------------------------------------------------------------- GPU arm ---
 
 def main():
@@ -521,6 +728,7 @@ def main():
     ap.add_argument("--math", default="auto", choices=["auto", "ffma", "tf32", "fp32_strict"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ffma", action="store_true", help="segnet: skip the FP32 FFMA (value_ffma) timing")
     ap.add_argument("--fuse-blocks", type=int, default=None, choices=[0, 1],
                     help="run each small-frame inverted-bottleneck block as one launch (default: Model's)")
     ap.add_argument("--fuse-resize", type=int, default=None, choices=[0, 1],
@@ -528,9 +736,10 @@ def main():
     ap.add_argument("--fuse-stem", type=int, default=None, choices=[0, 1],
                     help="run the 1x1 over the stem's output inside the stem's launch (default: Model's)")
     ap.add_argument("--layers", action="store_true", help="print the per-layer table to stderr")
-    ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm", "segm_r11"],
+    ap.add_argument("--workload", default="segnet", choices=["segnet", "rvm", "segm_r11", "cfg2", "cfg3"],
                     help="segnet: BASELINE config 4 (default); rvm: the recurrent matting net of config 5; "
-                         "segm_r11: ai_engine's shipped segmentation model (.sw, real weights)")
+                         "segm_r11: ai_engine's shipped segmentation model (.sw, real weights); "
+                         "cfg2 / cfg3: the single-conv sweeps of configs 2 and 3 (one line per shape)")
     ap.add_argument("--streams", type=int, default=1024, help="rvm: video streams over all GPUs")
     args = ap.parse_args()
 
@@ -552,6 +761,8 @@ def main():
         return run_rvm(args, world, rank, dev)
     if args.workload == "segm_r11":
         return run_segm_r11(args, world, rank, dev)
+    if args.workload in ("cfg2", "cfg3"):
+        return run_sweep(args, world, rank, dev)
 
     from ai_engine_b200 import segnet
     from ai_engine_b200.conv import resize_bilinear, run_dw_pw, run_mbconv, run_stem_pw
@@ -660,6 +871,26 @@ def main():
 
     e2e_f32_value = time_e2e(model, x_host)
     model.release()
+    # ---- the same network at the reference's own precision: FP32 FFMA on the
+    # CUDA cores for every conv (math "ffma"), timed the same way (graph replay)
+    ffma_value = None
+    if not args.no_ffma:
+        model_ffma = Model(g, weights, n, (H, W, 3), math="ffma", device=dev, **fuse_kw)
+        model_ffma.bufs["input"].copy_(x_host)
+        model_ffma.capture()
+        for _ in range(max(args.warmup, 3)):
+            model_ffma.infer()
+        torch.cuda.synchronize()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            model_ffma.infer()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ffma_value = n * world * args.steps / (max_over_ranks(f0.elapsed_time(f1)) / 1000.0)
+        model_ffma.release()
+        del model_ffma
     model_u8 = Model(g, weights, n, (H, W, 3), math=args.math, input_u8=True, device=dev, **fuse_kw)
     x_host_u8 = torch.from_numpy(np.rint(x_host.numpy() * 255.0).astype(np.uint8)).pin_memory()
     e2e_value = time_e2e(model_u8, x_host_u8)
@@ -758,11 +989,13 @@ def main():
                    "conv_mflop_per_frame": round(conv_flops / n / 1e6, 2)},
         "conv_tflops": round(conv_flops * world / (total_ms / args.steps / 1000.0) / 1e12, 3),
         "roofline": roof,
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(x_host_u8.numel()),
+        "e2e": {"value": round(e2e_f32_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(x_host.numel() * 4),
                 "d2h_bytes_per_step": int(out_host.numel() * 4),
-                "input": "u8 RGB frames, normalised on the GPU (aie_input_u8)"},
-        "e2e_f32_input": {"value": round(e2e_f32_value, 2), "unit": UNIT,
-                          "h2d_bytes_per_step": int(x_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
+                "input": "config 4's f32 U(0,1) frames, uploaded from pinned host memory every step"},
+        "e2e_u8": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(x_host_u8.numel()),
+                   "d2h_bytes_per_step": int(out_host.numel() * 4),
+                   "input": "u8 RGB frames (the f32 frames quantised), normalised on the GPU (aie_input_u8)"},
+        "value_ffma": None if ffma_value is None else round(ffma_value, 2),
         "eager_value": round(eager_value, 2),
         "gpu_launches": len(ops) * args.steps,
         "clocks": sampler.summary(),
@@ -772,9 +1005,16 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         v, dt, done = cpu_baseline(2 * threads, threads, min_seconds=10.0)
+        vb, dtb, doneb = cpu_baseline(1, threads, min_seconds=4.0, mode="bands")
         line["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": f"{done} frames of the same workload, one frame per core, "
-                                          f"{dt:.1f} s on {cpu_model_name()}"}
+                                "gflops": round(v * conv_flops / n / 1e9, 2),
+                                "sample": f"{done} frames of the same workload, one frame per core (ai-cpu "
+                                          f"throughput mode), {dt:.1f} s on {cpu_model_name()}",
+                                "aicpu_mode": {"value": round(vb, 3), "unit": UNIT, "threads": threads,
+                                               "gflops": round(vb * conv_flops / n / 1e9, 2),
+                                               "sample": f"{doneb} frames one at a time, each conv's output rows "
+                                                         f"split over {threads} threads (crates/ai-cpu/src/"
+                                                         f"model.rs:421-441), {dtb:.1f} s"}}
     if args.layers:
         for l in layers:
             t = l["ms"] / 1000

@@ -372,15 +372,17 @@ AIE_API int aie_last_error(char *buf, size_t len);
 #define AIE_NOALLOC_SCRATCH_BYTES (16u << 20)
 
 /* aie_conv_run for callers that cannot allocate device memory while they
- * run -- a real-time loop that cannot afford cudaMalloc's synchronisation,
- * a plugin that only receives its host's tensors, code running during
- * CUDA-graph capture.  No counterpart in the reference.  Instead of a caller
- * workspace, split-K partials use a fixed AIE_NOALLOC_SCRATCH_BYTES array
- * inside the library (held by every GPU that loads it, until exit); plans
- * needing more are rejected with AIE_E_UNSUPPORTED.  The first call on each
- * device (with that device current) looks up the array's device address;
- * make that first call before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race on it.  Allocates nothing. */
+ * run: a real-time frame loop that cannot absorb cudaMalloc's implicit
+ * device synchronisation, or a plugin inside a host application that owns
+ * the device allocator and hands over only its own tensors.  No counterpart
+ * in the reference.  Instead of a caller workspace, split-K partials use a
+ * fixed AIE_NOALLOC_SCRATCH_BYTES array inside the library (held by every
+ * GPU that loads it, until exit); plans needing more are rejected with
+ * AIE_E_UNSUPPORTED.  The first call on each device (with that device
+ * current, and `stream` belonging to it) looks up the array's device
+ * address; make that first call before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race on it.  Allocates
+ * nothing. */
 AIE_API int aie_conv_run_noalloc(const aie_plan *plan, const void *in, const void *dev_w, const void *dev_b,
                                  const void *res, void *out, void *stream);
 

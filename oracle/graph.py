@@ -21,6 +21,7 @@ from typing import Dict, Tuple
 import numpy as np
 
 from . import Plan, lib, resize_bilinear
+from .net import tf32_truncate
 
 
 def _shapes(graph, in_hwc):
@@ -38,15 +39,23 @@ def _shapes(graph, in_hwc):
 
 
 class OracleModel:
-    def __init__(self, graph, weights: Dict[str, Tuple[np.ndarray, np.ndarray]], in_hwc):
+    """``tf32`` names convs whose operands are first truncated to TF32 (the
+    low 13 mantissa bits of every activation and weight cleared), the
+    operand format the GPU's tensor cores read fp32 data in; naming the
+    GPU's own TF32 convs makes the chain follow the GPU's arithmetic."""
+
+    def __init__(self, graph, weights: Dict[str, Tuple[np.ndarray, np.ndarray]], in_hwc, tf32=()):
         lib()
         self.graph = list(graph)
         self.shapes = _shapes(self.graph, in_hwc)
+        self.tf32 = set(tf32)
         self.plans = {}
         for op in self.graph:
             if op[0] == "conv":
                 h, w, _ = self.shapes[op[2]]
                 wt, b = weights[op[1]]
+                if op[1] in self.tf32:
+                    wt = tf32_truncate(wt)
                 self.plans[op[1]] = Plan(op[3], h, w, wt, b, True, op[4] is not None)
         self.output = self.graph[-1][1]
 
@@ -58,7 +67,8 @@ class OracleModel:
             oh, ow, oc = self.shapes[out]
             if kind == "conv":
                 y = np.empty((oh, ow, oc), np.float32)
-                self.plans[out].run_frame(t[src], y, t[res] if res else None, threads=threads)
+                xin = tf32_truncate(t[src]) if out in self.tf32 else t[src]
+                self.plans[out].run_frame(xin, y, t[res] if res else None, threads=threads)
             else:
                 y = resize_bilinear(t[src][None], oh, ow)[0]
                 if res:

@@ -25,6 +25,27 @@ def normalised_error(got, want, scale) -> float:
     return float(np.max(np.abs(got - want) / den)) if got.size else 0.0
 
 
+def plain_rel_error(got, want, floor: float = 1e-3) -> float:
+    """The north-star's plain max relative error max |got - want| / |want|,
+    over the outputs with |want| >= floor * max|want| (below that a
+    relative error measures cancellation, not the kernel).  Reported beside
+    the normalised error so the contract's own figure is visible."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    if not want.size:
+        return 0.0
+    m = np.abs(want) >= floor * np.max(np.abs(want))
+    if not m.any():
+        return 0.0
+    return float(np.max(np.abs(got[m] - want[m]) / np.abs(want[m])))
+
+
+def errors(got, want, scale) -> str:
+    """Both error figures, for assertion messages."""
+    return (f"normalised {normalised_error(got, want, scale):.3e}, plain relative "
+            f"{plain_rel_error(got, want):.3e} (|want| >= 1e-3 max)")
+
+
 def case_tensors(op, n, ih, iw, seed, with_res):
     """Inputs in ai-gpu testsuite draw order: input, weights, bias, residual
     (crates/ai-gpu/src/testsuite.rs:337-341)."""
