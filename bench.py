@@ -211,7 +211,7 @@ def run_reference(args, rank):
         return 0
     threads = os.cpu_count() or 1
     if args.workload in ("cfg2", "cfg3"):
-        for label, op, n, ih, iw, split in sweep_shapes(args.workload, args.batch):
+        for label, op, n, ih, iw, split in sweep_shapes(args.workload, args.batch, args.shape):
             rng = np.random.default_rng(zlib.crc32(label.encode()))
             fan_in = op.cin * op.kh * op.kw
             w = (rng.standard_normal(op.cout * fan_in) / np.sqrt(fan_in)).astype(np.float32)
@@ -554,11 +554,16 @@ SWEEP_METRIC = {"cfg2": "conv GEMM TFLOP/s vs TF32 peak (BASELINE config 2: 3x3 
 L2_BYTES = 126 << 20
 
 
-def sweep_shapes(which: str, batch: int):
+def sweep_shapes(which: str, batch: int, only: str = ""):
     """(label, Conv2d, n, ih, iw, split) of the BASELINE config's sweep, in the
     reference's own shape-table spirit (crates/ai-gpu/src/bench.rs:166-260):
     config 2 at `batch` frames for every (Cin, Cout) and stride; config 3 at
-    batch 1, 64 and 256 with the auto split, plus batch 1 at every split factor."""
+    batch 1, 64 and 256 with the auto split, plus batch 1 at every split factor.
+    `only`: keep the shapes whose label contains it."""
+    return [s for s in _sweep_shapes(which, batch) if only in s[0]]
+
+
+def _sweep_shapes(which: str, batch: int):
     from ai_engine_b200 import Conv2d
     out = []
     if which == "cfg2":
@@ -622,7 +627,7 @@ def run_sweep(args, world, rank, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for label, op, n, ih, iw, split in sweep_shapes(args.workload, args.batch):
+    for label, op, n, ih, iw, split in sweep_shapes(args.workload, args.batch, args.shape):
         rng = np.random.default_rng(zlib.crc32(label.encode()))
         fan_in = op.cin * op.kh * op.kw
         if args.workload == "cfg2":  # Kaiming-normal W, U(-0.1, 0.1) bias
@@ -741,6 +746,7 @@ def main():
                          "segm_r11: ai_engine's shipped segmentation model (.sw, real weights); "
                          "cfg2 / cfg3: the single-conv sweeps of configs 2 and 3 (one line per shape)")
     ap.add_argument("--streams", type=int, default=1024, help="rvm: video streams over all GPUs")
+    ap.add_argument("--shape", default="", help="cfg2 / cfg3: only the shapes whose label contains this")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
