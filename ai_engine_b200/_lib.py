@@ -53,6 +53,13 @@ class TView(C.Structure):
     _fields_ = [("data", C.c_void_p), ("stride", C.c_uint32), ("coff", C.c_uint32)]
 
 
+class Yuv420(C.Structure):
+    """aie_yuv420: the planes of a batch of YUV 4:2:0 frames."""
+    _fields_ = [("y", C.c_void_p), ("u", C.c_void_p), ("v", C.c_void_p), ("stride_y", C.c_uint32),
+                ("stride_u", C.c_uint32), ("stride_v", C.c_uint32), ("uv_step", C.c_uint32),
+                ("frame_y", C.c_uint64), ("frame_u", C.c_uint64), ("frame_v", C.c_uint64)]
+
+
 BIN_OPS = {"add": 0, "sub": 1, "mul": 2, "prelu": 3}          # aie_binop
 OPND_TENSOR, OPND_SCALAR, OPND_SCALAR_FIRST, OPND_CVEC, OPND_CVEC_TENSOR, OPND_PVEC_TENSOR = range(6)
 
@@ -77,6 +84,7 @@ SIGNATURES = {
     "aie_conv_run_mbconv": (C.c_int, [_vp] * 13),
     "aie_conv_run_stem_pw": (C.c_int, [_vp] * 10),
     "aie_input_u8": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _vp, C.c_int32, _vp, _vp]),
+    "aie_input_yuv420": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(Yuv420), C.c_int32, _vp, _vp]),
     "aie_selftest_wait_timeout": (C.c_int, [C.c_uint32, _vp]),
     "aie_binary": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, C.c_int32, C.c_int32, TView, C.c_float,
                              C.c_int32, TView, _vp]),

@@ -266,6 +266,40 @@ def input_u8(frames: torch.Tensor, layout: str = "nhwc", out: Optional[torch.Ten
     return out
 
 
+def input_yuv420(y: torch.Tensor, u: torch.Tensor, v: Optional[torch.Tensor] = None, *, h: Optional[int] = None,
+                 w: Optional[int] = None, nv21: bool = False, layout: str = "nhwc", out: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+    """YUV 4:2:0 frames on the GPU -> the network's f32 RGB input
+    (aie_input_yuv420; ai-ffi's i420_to_rgba, then v / 255).
+
+    I420: y [n, h, stride_y], u and v [n, ceil(h/2), stride_uv] uint8 planes.
+    NV12 (v None): u is the interleaved chroma plane [n, ceil(h/2), stride]
+    (U first; V first with nv21=True).  h, w default to y's rows and row
+    length."""
+    planes = [y, u] + ([v] if v is not None else [])
+    if any((not p.is_cuda) or p.dtype != torch.uint8 or p.dim() != 3 or not p.is_contiguous() for p in planes):
+        raise TypeError("planes must be contiguous uint8 CUDA tensors [n, rows, stride]")
+    n = y.shape[0]
+    h = y.shape[1] if h is None else h
+    w = y.shape[2] if w is None else w
+    d = _lib.Yuv420()
+    d.y, d.stride_y, d.frame_y = y.data_ptr(), y.shape[2], y.shape[1] * y.shape[2]
+    if v is not None:
+        d.u, d.v, d.uv_step = u.data_ptr(), v.data_ptr(), 1
+        d.stride_u, d.stride_v = u.shape[2], v.shape[2]
+        d.frame_u, d.frame_v = u.shape[1] * u.shape[2], v.shape[1] * v.shape[2]
+    else:
+        base = u.data_ptr()
+        d.u, d.v, d.uv_step = (base + 1, base, 2) if nv21 else (base, base + 1, 2)
+        d.stride_u = d.stride_v = u.shape[2]
+        d.frame_u = d.frame_v = u.shape[1] * u.shape[2]
+    if out is None:
+        out = torch.empty((n, h, w, 4 if layout == "nhwc_c4" else 3), dtype=torch.float32, device=y.device)
+    check(_lib.load().aie_input_yuv420(n, h, w, C.byref(d), LAYOUT[layout], _dptr(out),
+                                       C.c_void_p(_stream_handle(stream))), "aie_input_yuv420")
+    return out
+
+
 def lower_conv(op: Conv2d, n: int, ih: int, iw: int, w: np.ndarray, bias: Optional[np.ndarray] = None, *,
                has_res: bool = False, layout: str = "nhwc", math: str = "auto", wfmt: str = "oihw",
                **kw) -> ConvPlan:

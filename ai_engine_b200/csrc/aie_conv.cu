@@ -919,6 +919,47 @@ extern "C" int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, co
     return AIE_OK;
 }
 
+extern "C" int aie_input_yuv420(uint32_t n, uint32_t h, uint32_t w, const aie_yuv420 *src, int32_t layout,
+                                void *out, void *stream)
+{
+    if (!src || !out || !src->y || !src->u || !src->v) return fail(AIE_E_INVALID, "null plane or output pointer");
+    if (!n || !h || !w) return fail(AIE_E_INVALID, "zero-sized frame batch");
+    if (layout != AIE_LAYOUT_NHWC && layout != AIE_LAYOUT_NHWC_C4)
+        return fail(AIE_E_INVALID, "layout %d out of range", layout);
+    if (src->uv_step != 1 && src->uv_step != 2)
+        return fail(AIE_E_INVALID, "uv_step must be 1 (I420) or 2 (NV12 / NV21), got %u", src->uv_step);
+    const uint64_t ch = (h + 1) / 2, cw = (w + 1) / 2;
+    if (src->stride_y < w) return fail(AIE_E_INVALID, "stride_y %u < width %u", src->stride_y, w);
+    const uint64_t cbytes = (cw - 1) * src->uv_step + 1;  // bytes a chroma row spans
+    if (src->stride_u < cbytes || src->stride_v < cbytes)
+        return fail(AIE_E_INVALID, "chroma strides (%u, %u) shorter than a chroma row (%llu bytes)", src->stride_u,
+                    src->stride_v, (unsigned long long)cbytes);
+    const uint64_t fy = src->frame_y ? src->frame_y : (uint64_t)src->stride_y * h;
+    const uint64_t fu = src->frame_u ? src->frame_u : (uint64_t)src->stride_u * ch;
+    const uint64_t fv = src->frame_v ? src->frame_v : (uint64_t)src->stride_v * ch;
+    if (fy < (uint64_t)src->stride_y * (h - 1) + w || fu < (uint64_t)src->stride_u * (ch - 1) + cbytes ||
+        fv < (uint64_t)src->stride_v * (ch - 1) + cbytes)
+        return fail(AIE_E_INVALID, "frame strides shorter than a frame's planes");
+    const int stride = layout == AIE_LAYOUT_NHWC_C4 ? 4 : 3;
+    if (stride == 4 && (uintptr_t)out % 16) return fail(AIE_E_ALIGN, "C4 output must be 16-byte aligned");
+    const uint64_t threads = (uint64_t)n * ch * cw;
+    if (threads >= (1ull << 31) * 256ull || (uint64_t)n * h * w * stride >= (1ull << 62))
+        return fail(AIE_E_UNSUPPORTED, "frame batch too large");
+    Yuv420Args a;
+    a.y = (const uint8_t *)src->y;
+    a.u = (const uint8_t *)src->u;
+    a.v = (const uint8_t *)src->v;
+    a.fy = (long long)fy; a.fu = (long long)fu; a.fv = (long long)fv;
+    a.sy = (int)src->stride_y; a.su = (int)src->stride_u; a.sv = (int)src->stride_v; a.uv_step = (int)src->uv_step;
+    a.n = (int)n; a.h = (int)h; a.w = (int)w; a.ch = (int)ch; a.cw = (int)cw;
+    a.out = (float *)out;
+    a.ostride = stride;
+    input_yuv420_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "YUV input staging launch");
+    return AIE_OK;
+}
+
 extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_t c, const void *in, uint32_t oh,
                                    uint32_t ow, int32_t mode, const void *add, int32_t act, void *out, void *stream)
 {

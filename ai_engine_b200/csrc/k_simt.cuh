@@ -547,6 +547,63 @@ __global__ void __launch_bounds__(256) input_u8_kernel(const uint8_t *__restrict
     }
 }
 
+// YUV 4:2:0 camera frames (I420 planar, or NV12 / NV21 with interleaved
+// chroma) -> the network's f32 RGB input.  The reference converts on the
+// CPU, I420 -> RGBA8 (crates/ai-ffi/src/yuv.rs:7-31: BT.601 full range, f32
+// with separate multiplies and adds, clamped to [0, 255] and truncated),
+// and the model then reads each byte as v / 255.  One thread owns the 2 x 2
+// pixel block that shares a chroma sample: the chroma products are formed
+// once (the same products the reference forms per pixel), every sum is
+// rounded on its own, so the result is bit for bit the reference's bytes
+// divided by 255.
+struct Yuv420Args {
+    const uint8_t *y, *u, *v;
+    long long fy, fu, fv;     // bytes between frames' planes
+    int sy, su, sv, uv_step;  // row strides; bytes between horizontal chroma samples (1 planar, 2 interleaved)
+    int n, h, w, ch, cw;      // ch, cw: chroma rows / columns = ceil(h / 2), ceil(w / 2)
+    float *out;
+    int ostride;              // 3 (NHWC) or 4 (NHWC-C4, 4th lane 0)
+};
+
+__device__ __forceinline__ float yuv_unorm(float c)
+{
+    c = fminf(fmaxf(c, 0.0f), 255.0f);                // Rust's clamp(0.0, 255.0)
+    return __fdiv_rn((float)__float2int_rz(c), 255.0f);  // `as u8`, then v / 255
+}
+
+__global__ void __launch_bounds__(256) input_yuv420_kernel(const Yuv420Args a)
+{
+    const long long t = (long long)blockIdx.x * 256 + threadIdx.x;
+    const long long per = (long long)a.ch * a.cw;
+    if (t >= per * a.n) return;
+    const int f = (int)(t / per);
+    const int r = (int)(t - (long long)f * per);
+    const int ci = r / a.cw, cj = r - ci * a.cw;
+    const float uv = (float)__ldg(a.u + f * a.fu + (long long)ci * a.su + (long long)cj * a.uv_step) - 128.0f;
+    const float vv = (float)__ldg(a.v + f * a.fv + (long long)ci * a.sv + (long long)cj * a.uv_step) - 128.0f;
+    const float rv = __fmul_rn(1.402f, vv), gu = __fmul_rn(0.344136f, uv), gv = __fmul_rn(0.714136f, vv),
+                bu = __fmul_rn(1.772f, uv);
+#pragma unroll
+    for (int dy = 0; dy < 2; dy++) {
+        const int yy = 2 * ci + dy;
+        if (yy >= a.h) break;
+        const uint8_t *yrow = a.y + f * a.fy + (long long)yy * a.sy;
+        float *orow = a.out + ((long long)f * a.h + yy) * a.w * a.ostride;
+#pragma unroll
+        for (int dx = 0; dx < 2; dx++) {
+            const int xx = 2 * cj + dx;
+            if (xx >= a.w) break;
+            const float yv = (float)__ldg(yrow + xx);
+            const float rr = yuv_unorm(__fadd_rn(yv, rv));
+            const float gg = yuv_unorm(__fsub_rn(__fsub_rn(yv, gu), gv));
+            const float bb = yuv_unorm(__fadd_rn(yv, bu));
+            float *o = orow + (long long)xx * a.ostride;
+            if (a.ostride == 4) *reinterpret_cast<float4 *>(o) = make_float4(rr, gg, bb, 0.0f);
+            else { o[0] = rr; o[1] = gg; o[2] = bb; }
+        }
+    }
+}
+
 // Exact 2x upsampling in half_pixel mode (oh = 2*ih, ow = 2*iw; the FPN's
 // and the mask's resizes).  Output (2i+a, 2j+b) samples source rows
 // clamp(i-1+a), clamp(i+a) and columns clamp(j-1+b), clamp(j+b) with far

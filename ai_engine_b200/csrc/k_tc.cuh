@@ -786,15 +786,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 // raw partial -> workspace, release the accumulator, then take
                 // this warp's ticket for its 32 rows (no cross-warp barrier:
-                // every warp finishes on its own even if another gave up)
-                float *wrow = a.ws + ((tile * a.split + t.s) * kTcBM + row) * a.bn;
+                // every warp finishes on its own even if another gave up).
+                // Layout [tile][split][quadrant][bn / 4][32 lanes] of float4:
+                // the warp's 32 rows of one 4-column group are 512 contiguous
+                // bytes, so every store (and every load of the reduction
+                // below, made by the same lanes) is one coalesced transaction.
+                const uint64_t qstride = (uint64_t)(a.bn / 4) * 32;  // float4s per (split, quadrant)
+                float4 *wq = reinterpret_cast<float4 *>(a.ws) + ((tile * a.split + t.s) * 4 + quad) * qstride + lane;
                 for (int c0 = 0; c0 < (int)a.bn; c0 += 16) {
                     float v[16];
                     tmem_ld16(tbase + c0, v);
 #pragma unroll
                     for (int q = 0; q < 4; q++)
-                        *reinterpret_cast<float4 *>(wrow + c0 + 4 * q) =
-                            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                        wq[(uint32_t)(c0 / 4 + q) * 32] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -807,23 +811,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
-                    const float *base = a.ws + (tile * a.split * kTcBM + row) * a.bn;
-                    for (int c0 = 0; c0 < ncol; c0 += 32) {
+                    // this warp's rows of split 0; split s is s * sstride further
+                    const float4 *base = reinterpret_cast<const float4 *>(a.ws) + (tile * a.split * 4 + quad) * qstride + lane;
+                    const uint64_t sstride = 4 * qstride;
+                    for (int c0 = 0; c0 < ncol; c0 += 32) {  // a.bn is a multiple of 32
                         if (res_tensor) {
                             __syncwarp();  // every lane has read its rows of the buffer
                             prefetch_any(nbase + c0);  // lands while the partials are summed
                         }
+                        const float4 *p = base + (uint32_t)(c0 / 4) * 32;
                         float v[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) v[j] = 0.0f;
-                        for (uint32_t s = 0; s < a.split; s++) {
-                            const float *p = base + (uint64_t)s * kTcBM * a.bn + c0;
+                        // summed in split order from zero (deterministic); two
+                        // splits' loads in flight at a time
+                        uint32_t s = 0;
+                        for (; s + 2 <= a.split; s += 2) {
+                            float4 x0[8], x1[8];
 #pragma unroll
                             for (int q = 0; q < 8; q++) {
-                                if (c0 + 4 * q < (int)a.bn) {
-                                    const float4 x = __ldcg(reinterpret_cast<const float4 *>(p + 4 * q));
-                                    v[4 * q] += x.x; v[4 * q + 1] += x.y; v[4 * q + 2] += x.z; v[4 * q + 3] += x.w;
-                                }
+                                x0[q] = __ldcg(p + s * sstride + q * 32);
+                                x1[q] = __ldcg(p + (s + 1) * sstride + q * 32);
+                            }
+#pragma unroll
+                            for (int q = 0; q < 8; q++) {
+                                v[4 * q] += x0[q].x; v[4 * q + 1] += x0[q].y; v[4 * q + 2] += x0[q].z; v[4 * q + 3] += x0[q].w;
+                            }
+#pragma unroll
+                            for (int q = 0; q < 8; q++) {
+                                v[4 * q] += x1[q].x; v[4 * q + 1] += x1[q].y; v[4 * q + 2] += x1[q].z; v[4 * q + 3] += x1[q].w;
+                            }
+                        }
+                        if (s < a.split) {
+#pragma unroll
+                            for (int q = 0; q < 8; q++) {
+                                const float4 x = __ldcg(p + s * sstride + q * 32);
+                                v[4 * q] += x.x; v[4 * q + 1] += x.y; v[4 * q + 2] += x.z; v[4 * q + 3] += x.w;
                             }
                         }
                         emit_any(nbase + c0, v);
@@ -918,12 +941,44 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
         const uint64_t M = (uint64_t)n * oh * ow;
         g->m_tiles = (uint32_t)((M + kTcBM - 1) / kTcBM);
     }
-    const uint64_t tiles = (uint64_t)g->m_tiles * g->n_tiles;
+    uint64_t tiles = (uint64_t)g->m_tiles * g->n_tiles;
     uint32_t split = 1;
     if (split_req == 0) {
         if (tiles < 148 && g->k_iters >= 8) {
-            split = (uint32_t)std::min<uint64_t>(16, std::max<uint64_t>(1, 148 / tiles));
-            split = std::min(split, g->k_iters / 4 ? g->k_iters / 4 : 1u);
+            // Too few tiles to fill the SMs: split K, and for 1x1 GEMMs
+            // consider narrower N tiles too (more tiles share the work, and
+            // each tile's last arrival sums fewer partial bytes).  Pick the
+            // (N tile, split) with the lowest modelled time per CTA: MMA
+            // issue (~0.072 us per tcgen05.mma) against operand loads
+            // (~100 GB/s per SM from HBM), whichever is longer, per wave of
+            // units, plus the partial write (~200 GB/s per SM) and the
+            // reduction's L2 round trips (~0.5 us per two splits of a
+            // 32-column chunk).
+            double best = 1e30;
+            uint32_t best_bn = g->bn, best_split = 1;
+            for (uint32_t bn = g->bn;; bn = std::max(64u, (bn / 2 + 31) / 32 * 32)) {
+                const uint64_t nt2 = (cout + bn - 1) / bn, t2 = (uint64_t)g->m_tiles * nt2;
+                uint32_t sp = (uint32_t)std::min<uint64_t>(16, std::max<uint64_t>(1, 148 / t2));
+                sp = std::min(sp, g->k_iters / 4 ? g->k_iters / 4 : 1u);
+                const uint32_t kps = (g->k_iters + sp - 1) / sp;
+                const uint64_t waves = (t2 * ((g->k_iters + kps - 1) / kps) + 147) / 148;
+                const double mma = kps * 4 * 0.072;
+                const double load = kps * (double)(g->a_bytes + bn * kTcBK * 4) / 1e5;
+                double t = waves * std::max(mma, load);
+                if (sp > 1) t += 128.0 * bn * 4 / 2e5 + 0.5 * ((sp + 1) / 2) * (bn / 32);
+                if (t < best) {
+                    best = t;
+                    best_bn = bn;
+                    best_split = sp;
+                }
+                if (g->igemm || bn <= 64) break;  // k x k tiles keep their N tile
+            }
+            if (best_bn != g->bn) {
+                g->bn = best_bn;
+                g->n_tiles = (cout + g->bn - 1) / g->bn;
+                tiles = (uint64_t)g->m_tiles * g->n_tiles;
+            }
+            split = best_split;
         }
     } else {
         split = std::min(split_req, g->k_iters);

@@ -280,6 +280,30 @@ AIE_API int aie_conv_run_stem_pw(const aie_plan *stem, const aie_plan *pw, const
 AIE_API int aie_input_u8(uint32_t n, uint32_t h, uint32_t w, uint32_t cin, const void *in, int32_t layout,
                  void *out, void *stream);
 
+/* A batch of YUV 4:2:0 camera frames, one set of planes per frame, all on
+ * the device.  I420 (planar): u and v are separate planes, uv_step = 1.
+ * NV12: u points at the interleaved chroma plane and v = u + 1, uv_step = 2
+ * (NV21: v at the plane, u = v + 1).  Chroma planes hold ceil(h/2) rows of
+ * ceil(w/2) samples.  Strides are in bytes; frame_* is the distance between
+ * consecutive frames' planes (0 = stride * rows, tightly packed). */
+typedef struct aie_yuv420 {
+    const void *y, *u, *v;
+    uint32_t stride_y, stride_u, stride_v;
+    uint32_t uv_step;
+    uint64_t frame_y, frame_u, frame_v;
+} aie_yuv420;
+
+/* Input staging from YUV 4:2:0 frames: [n] frames of h x w -> the network's
+ * f32 RGB input [n, h, w, 3] (layout NHWC) or [n, h, w, 4] (NHWC_C4, 4th
+ * lane 0).  Each pixel is converted exactly as ai-ffi's i420_to_rgba
+ * (crates/ai-ffi/src/yuv.rs:7-31: BT.601 full range, chroma sample
+ * (y/2, x/2), f32 arithmetic, clamped and truncated to a byte) and that byte
+ * read as v / 255, as the model's input normalisation does -- on the GPU,
+ * with no RGBA intermediate.  Replaces the reference's CPU round trip
+ * (i420_to_rgba in ai-ffi, then the frame upload). */
+AIE_API int aie_input_yuv420(uint32_t n, uint32_t h, uint32_t w, const aie_yuv420 *src, int32_t layout, void *out,
+                             void *stream);
+
 /* Bilinear resize of a dense NHWC batch [n, ih, iw, c] to [n, oh, ow, c]
  * (crates/ai-core/src/reference/resize.rs:5-42; mode 0 = half_pixel,
  * 1 = asymmetric), then out = act(resized + add) when add is non-NULL

@@ -72,6 +72,9 @@ def lib():
         L.orc_gpool.argtypes = [sz, sz, sz, _fp, sz, sz, _fp]
         L.orc_avgpool.argtypes = [C.c_uint32] * 11 + [_fp, _fp]
         L.orc_channel_copy.argtypes = [sz, sz, sz, _fp, sz, sz, C.c_int, _fp, sz, sz]
+        _u8 = C.POINTER(C.c_uint8)
+        L.orc_i420_to_rgba.argtypes = [_u8, _u8, _u8, sz, sz, sz, sz, sz, _u8]
+        L.orc_rgba_to_i420.argtypes = [_u8, sz, sz, _u8, _u8, _u8, sz, sz, sz]
         _LIB = L
     return _LIB
 
@@ -323,3 +326,29 @@ def channel_copy(x, out, act="none") -> None:
     oa, os_, oo, _ = _view(out)
     n, px = _npx(xa)
     lib().orc_channel_copy(n, px, c, _ptr(xa), xs, xo, _act(act), _ptr(oa), os_, oo)
+
+
+# ----------------------------------------------------------- frame formats ---
+
+def _u8p(a: np.ndarray):
+    assert a.dtype == np.uint8 and a.flags["C_CONTIGUOUS"], "oracle wants contiguous uint8"
+    return a.ctypes.data_as(C.POINTER(C.c_uint8))
+
+
+def i420_to_rgba(y: np.ndarray, u: np.ndarray, v: np.ndarray, w: int, h: int) -> np.ndarray:
+    """One I420 frame (planes [h][stride_y], [ceil(h/2)][stride_u], ...) ->
+    RGBA8 [h, w, 4] (crates/ai-ffi/src/yuv.rs:7-31)."""
+    out = np.empty((h, w, 4), np.uint8)
+    lib().orc_i420_to_rgba(_u8p(y), _u8p(u), _u8p(v), w, h, y.shape[-1], u.shape[-1], v.shape[-1], _u8p(out))
+    return out
+
+
+def rgba_to_i420(rgba: np.ndarray):
+    """RGBA8 [h, w, 4] -> I420 planes, tightly packed (yuv.rs:33-58)."""
+    h, w, _ = rgba.shape
+    y = np.zeros((h, w), np.uint8)
+    u = np.zeros(((h + 1) // 2, (w + 1) // 2), np.uint8)
+    v = np.zeros_like(u)
+    lib().orc_rgba_to_i420(_u8p(np.ascontiguousarray(rgba)), w, h, _u8p(y), _u8p(u), _u8p(v), w, u.shape[1],
+                           v.shape[1])
+    return y, u, v

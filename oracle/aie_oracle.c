@@ -22,6 +22,8 @@
  *     Act, Concat/Chcopy copies              crates/ai-core/src/reference/elementwise.rs:7-26
  *   - Gpool, Avgpool                         crates/ai-cpu/src/kernels/segate.rs:46-57,
  *                                            crates/ai-core/src/reference/pool.rs:5-46
+ *   - I420 <-> RGBA8 frame conversion        crates/ai-ffi/src/yuv.rs:7-58
+ *     (BT.601 full range)
  *
  * Rounding.  ai-cpu on x86 runs its scalar F32x4 fallback
  * (crates/ai-cpu/src/simd.rs:189-300): `fma` is a separate multiply then add,
@@ -760,4 +762,50 @@ ORC_API void orc_channel_copy(size_t n, size_t px, size_t c, const float *x, siz
 {
     for (size_t q = 0; q < n * px; q++)
         for (size_t ch = 0; ch < c; ch++) out[q * os + oo + ch] = epi_act(act, x[q * xs + xo + ch], ch, c);
+}
+
+/* I420 (YUV 4:2:0, planar) -> RGBA8, alpha 255 (crates/ai-ffi/src/yuv.rs:7-31).
+ * Chroma sample (y/2, x/2) serves pixel (y, x); each channel is computed in
+ * f32 with unfused multiplies and adds, clamped to [0, 255] and truncated
+ * (Rust's `as u8`). */
+ORC_API void orc_i420_to_rgba(const uint8_t *y, const uint8_t *u, const uint8_t *v, size_t w, size_t h,
+                              size_t stride_y, size_t stride_u, size_t stride_v, uint8_t *out)
+{
+    for (size_t yy = 0; yy < h; yy++)
+        for (size_t xx = 0; xx < w; xx++) {
+            const float yv = (float)y[yy * stride_y + xx];
+            const float uv = (float)u[(yy / 2) * stride_u + xx / 2] - 128.0f;
+            const float vv = (float)v[(yy / 2) * stride_v + xx / 2] - 128.0f;
+            float r = yv + 1.402f * vv;
+            float g = yv - 0.344136f * uv - 0.714136f * vv;
+            float b = yv + 1.772f * uv;
+            r = r < 0.0f ? 0.0f : r > 255.0f ? 255.0f : r;
+            g = g < 0.0f ? 0.0f : g > 255.0f ? 255.0f : g;
+            b = b < 0.0f ? 0.0f : b > 255.0f ? 255.0f : b;
+            uint8_t *o = out + (yy * w + xx) * 4;
+            o[0] = (uint8_t)r;
+            o[1] = (uint8_t)g;
+            o[2] = (uint8_t)b;
+            o[3] = 255;
+        }
+}
+
+/* RGBA8 -> I420 (crates/ai-ffi/src/yuv.rs:33-58): chroma from the top-left
+ * pixel of each 2 x 2 block, not an average. */
+ORC_API void orc_rgba_to_i420(const uint8_t *rgba, size_t w, size_t h, uint8_t *y, uint8_t *u, uint8_t *v,
+                              size_t stride_y, size_t stride_u, size_t stride_v)
+{
+    for (size_t yy = 0; yy < h; yy++)
+        for (size_t xx = 0; xx < w; xx++) {
+            const uint8_t *px = rgba + (yy * w + xx) * 4;
+            const float r = (float)px[0], g = (float)px[1], b = (float)px[2];
+            float l = 0.299f * r + 0.587f * g + 0.114f * b;
+            y[yy * stride_y + xx] = (uint8_t)(l < 0.0f ? 0.0f : l > 255.0f ? 255.0f : l);
+            if (yy % 2 == 0 && xx % 2 == 0) {
+                float cu = -0.168736f * r - 0.331264f * g + 0.5f * b + 128.0f;
+                float cv = 0.5f * r - 0.418688f * g - 0.081312f * b + 128.0f;
+                u[(yy / 2) * stride_u + xx / 2] = (uint8_t)(cu < 0.0f ? 0.0f : cu > 255.0f ? 255.0f : cu);
+                v[(yy / 2) * stride_v + xx / 2] = (uint8_t)(cv < 0.0f ? 0.0f : cv > 255.0f ? 255.0f : cv);
+            }
+        }
 }

@@ -182,6 +182,27 @@ def test_input_u8_argument_checks(lib):
     assert lib.aie_input_u8(1, 2, 2, 3, p, 1, C.c_void_p(20), None) == -5  # C4 output must be 16-byte aligned
 
 
+def test_input_yuv420_argument_checks(lib):
+    p = 16
+    def desc(**kw):
+        d = _lib.Yuv420(p, p, p, 8, 4, 4, 1, 0, 0, 0)
+        for k, v in kw.items():
+            setattr(d, k, v)
+        return C.byref(d)
+    out = C.c_void_p(16)
+    assert lib.aie_input_yuv420(1, 4, 8, None, 0, out, None) == -2                 # no planes
+    assert lib.aie_input_yuv420(1, 4, 8, desc(y=None), 0, out, None) == -2
+    assert lib.aie_input_yuv420(0, 4, 8, desc(), 0, out, None) == -2              # empty batch
+    assert lib.aie_input_yuv420(1, 4, 8, desc(), 7, out, None) == -2               # bad layout
+    assert lib.aie_input_yuv420(1, 4, 8, desc(uv_step=3), 0, out, None) == -2      # neither planar nor interleaved
+    assert lib.aie_input_yuv420(1, 4, 8, desc(stride_y=7), 0, out, None) == -2     # luma row shorter than w
+    assert lib.aie_input_yuv420(1, 4, 8, desc(stride_u=3), 0, out, None) == -2     # chroma row shorter than w/2
+    assert lib.aie_input_yuv420(1, 4, 8, desc(uv_step=2), 0, out, None) == -2      # interleaved row spans 7 bytes
+    assert lib.aie_input_yuv420(2, 4, 8, desc(frame_y=16), 0, out, None) == -2     # frames overlap
+    assert lib.aie_input_yuv420(1, 4, 8, desc(), 1, C.c_void_p(20), None) == -5    # C4 output alignment
+    assert "stride" in _lib.last_error() or "align" in _lib.last_error()
+
+
 def test_glue_entry_points_reject_bad_arguments(lib):
     """The graph-glue entry points validate on the host and return a status
     (no launch, no CUDA call) for null pointers, zero sizes, out-of-range

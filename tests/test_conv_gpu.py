@@ -449,3 +449,43 @@ def test_model_u8_input_equals_normalised_f32(cuda_ok):
         yb = b.infer(torch.from_numpy(f.astype(np.float32) / np.float32(255.0)).cuda()).cpu()
         assert torch.equal(o, yb)
     a.release()
+
+
+def _yuv_oracle(yp, up, vp, h, w):
+    """Oracle: ai-ffi's i420_to_rgba per frame, then the model's v / 255."""
+    import oracle
+    out = np.empty((yp.shape[0], h, w, 3), np.float32)
+    for f in range(yp.shape[0]):
+        rgba = oracle.i420_to_rgba(np.ascontiguousarray(yp[f]), np.ascontiguousarray(up[f]),
+                                   np.ascontiguousarray(vp[f]), w, h)
+        out[f] = rgba[..., :3].astype(np.float32) / np.float32(255.0)
+    return out
+
+
+@pytest.mark.parametrize("n,h,w,pad", [(2, 160, 288, 0), (3, 37, 51, 5), (1, 1, 1, 0), (2, 6, 9, 3)])
+@pytest.mark.parametrize("fmt", ["i420", "nv12", "nv21"])
+@pytest.mark.parametrize("layout", ["nhwc", "nhwc_c4"])
+def test_input_yuv420_bit_exact(cuda_ok, n, h, w, pad, fmt, layout):
+    """YUV 4:2:0 staging (aie_input_yuv420) equals ai-ffi's i420_to_rgba
+    followed by v / 255, bit for bit: I420 planes and NV12 / NV21
+    interleaved chroma, odd sizes (the last chroma row / column serves one
+    pixel), padded row strides, both output layouts."""
+    from ai_engine_b200.conv import input_yuv420
+    rng = np.random.default_rng(h * w + pad)
+    ch, cw = (h + 1) // 2, (w + 1) // 2
+    y = rng.integers(0, 256, (n, h, w + pad), dtype=np.uint8)
+    u = rng.integers(0, 256, (n, ch, cw + pad), dtype=np.uint8)
+    v = rng.integers(0, 256, (n, ch, cw + pad), dtype=np.uint8)
+    want = _yuv_oracle(y, u, v, h, w)
+    yd = torch.from_numpy(y).cuda()
+    if fmt == "i420":
+        got = input_yuv420(yd, torch.from_numpy(u).cuda(), torch.from_numpy(v).cuda(), w=w, layout=layout)
+    else:
+        first, second = (u, v) if fmt == "nv12" else (v, u)
+        uv = np.zeros((n, ch, 2 * cw + pad), np.uint8)
+        uv[..., 0:2 * cw:2], uv[..., 1:2 * cw:2] = first[..., :cw], second[..., :cw]
+        got = input_yuv420(yd, torch.from_numpy(uv).cuda(), w=w, nv21=fmt == "nv21", layout=layout)
+    got = got.cpu().numpy()
+    assert np.array_equal(got[..., :3], want)
+    if layout == "nhwc_c4":
+        assert (got[..., 3] == 0).all()

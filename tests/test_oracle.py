@@ -341,3 +341,35 @@ def test_se_gate_known_answers():
     ident = oracle.conv_aicpu(conv(2, 2, 1, 1), mean, np.array([1, 0, 0, 1], np.float32), np.zeros(2, np.float32))
     got = oracle.conv_aicpu(conv(2, 2, 1, 1), ident, np.array([2, 0, 0, 2], np.float32), np.ones(2, np.float32))
     assert got.ravel().tolist() == [5.0, 7.0]
+
+
+# ---- YUV 4:2:0 frames (crates/ai-ffi/src/yuv.rs) ---------------------------
+
+def test_yuv_roundtrip_flat_colors():
+    """yuv.rs:106-124 (roundtrip_flat_colors): flat 4 x 2 frames of red,
+    green, blue and grey survive RGBA -> I420 -> RGBA within 3 per channel."""
+    w, h = 4, 2
+    for color in ([255, 0, 0], [0, 255, 0], [0, 0, 255], [128, 128, 128]):
+        rgba = np.empty((h, w, 4), np.uint8)
+        rgba[..., :3] = color
+        rgba[..., 3] = 255
+        y, u, v = oracle.rgba_to_i420(rgba)
+        back = oracle.i420_to_rgba(y, u, v, w, h)
+        d = np.abs(back[..., :3].astype(int) - np.array(color))
+        assert d.max() <= 3, (color, d.max())
+        assert (back[..., 3] == 255).all()
+
+
+def test_yuv_known_values():
+    """Hand-computed BT.601 full-range values of yuv.rs:24-27: neutral
+    chroma gives grey; U = V = 255 saturates R and B, G = floor of the sum."""
+    y = np.array([[0, 128], [255, 77]], np.uint8)
+    u = np.array([[128]], np.uint8)
+    v = np.array([[128]], np.uint8)
+    out = oracle.i420_to_rgba(y, u, v, 2, 2)
+    assert out[..., 0].tolist() == [[0, 128], [255, 77]] and (out[..., 1] == out[..., 0]).all()
+    out = oracle.i420_to_rgba(np.array([[200, 100]], np.uint8), np.array([[255]], np.uint8),
+                              np.array([[255]], np.uint8), 2, 1)
+    g = np.float32(200) - np.float32(0.344136) * np.float32(127) - np.float32(0.714136) * np.float32(127)
+    assert out[0, 0].tolist() == [255, int(g), 255, 255] and int(g) == 65
+    assert out[0, 1].tolist() == [255, 0, 255, 255]  # G below zero clamps to 0

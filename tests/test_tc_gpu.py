@@ -142,9 +142,11 @@ CFG3 = [(960, 1280), (1280, 960), (512, 2048)]
 
 
 @pytest.mark.parametrize("k,n", CFG3)
-@pytest.mark.parametrize("split", [1, 4, 8, 16])
+@pytest.mark.parametrize("split", [0, 1, 4, 8, 16])
 def test_config3_splitk_b1(cuda_ok, k, n, split):
-    """BASELINE config 3 at batch 1 (M=180): every split factor against the oracle."""
+    """BASELINE config 3 at batch 1 (M=180): every split factor, and the
+    automatic choice (split 0: narrower N tiles and a K split), against the
+    oracle."""
     rng = np.random.default_rng(k + n + split)
     op = Conv2d.pointwise(k, n, "none")
     x = rng.uniform(-1, 1, (1, 10, 18, k)).astype(np.float32)
@@ -153,7 +155,7 @@ def test_config3_splitk_b1(cuda_ok, k, n, split):
     want, scale = oracle_conv(op, x, w, b, None)
     plan, got = run_gpu(op, x, w, b, math="tf32", split_k=split)
     assert plan.info.split_k == min(split, plan.info.split_k) and plan.info.split_k >= 1
-    if split > 1:
+    if split != 1:
         assert plan.info.split_k > 1 and plan.info.workspace_bytes > 0
     assert normalised_error(got, want, scale) <= TOL_TF32
 
