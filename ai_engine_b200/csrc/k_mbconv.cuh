@@ -22,15 +22,17 @@
 //   1. the MMA warp accumulates E over cin from an input ring (two [192][32]
 //      K-blocks) and a weight ring (four [128][32] K-blocks);
 //   2. eight channel warps (thread = expanded channel; warp w reads TMEM
-//      lanes 32 (w % 4).. and takes half the frame's rows) load E a frame
-//      row at a time (2-column tcgen05.ld), add the expand bias and
-//      activation, run the 3x3 depthwise on a sliding three-row register
-//      window (zero padding at the frame's edges), add its bias and
+//      lanes 32 (w % 4).. and takes half the frame's rows) copy the seven E
+//      rows their five output rows need into registers and release E at
+//      once; then they add the expand bias and activation, run the 3x3
+//      depthwise (zero padding at the frame's edges), add its bias and
 //      activation, and write D[p][channel] into shared memory as the project
 //      GEMM's K-major B operand (128-byte swizzle, one 32-channel K-block per
 //      lane quarter);
-//   3. the MMA warp accumulates P over the chunk's four K-blocks; their
-//      weights were loaded into the weight ring while the depthwise ran.
+//   3. the MMA warp accumulates P over the chunk's four K-blocks.
+// The MMA warp issues the expand of chunk g + 1 before the project of chunk
+// g, so the next chunk's expand GEMM overlaps this chunk's depthwise on the
+// CUDA cores; the producer loads the weights in that same order.
 // After the last chunk the channel warps add the project bias, activation
 // and residual and store the frame (thread = output channel: 32 lanes write
 // one pixel's 128 contiguous bytes).
@@ -103,6 +105,19 @@ __device__ __forceinline__ void tmem_row18(uint32_t taddr, float (&v)[kMbRowStri
                  : "memory");
 #pragma unroll
     for (int i = 0; i < kMbRowStride; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// tcgen05.wait::ld naming 18 load destinations as read-write operands, so
+// no use of them moves above the wait (after the first wait the loads have
+// all landed; further ones only pin their registers)
+__device__ __forceinline__ void tmem_wait_pin18(uint32_t (&r)[kMbRowStride])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17])
+                 :
+                 : "memory");
 }
 
 // AE, AD: the expand and depthwise activations (kRelu / kRelu6 / kNone, or
@@ -181,6 +196,15 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                 return true;
             };
             bool ok = true;
+            // a chunk's project weights, loaded after the next chunk's expand operands
+            auto load_project = [&](int pch) {
+                for (int kb = 0; ok && kb < 4; kb++) {
+                    uint32_t t;
+                    if (*abort_flag || !take_w(t)) { ok = false; break; }
+                    tma_load_2d(smem + kMbWOff + t * kMbWBytes, &tmWp, &sh.wfull[t], pch * kMbChunk + kb * 32, 0);
+                }
+            };
+            int prev_ch = -1;
             for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x) {
                 for (int ch = 0; ok && ch < nchunks; ch++) {
                     for (int kb = 0; kb < kx; kb++) {
@@ -190,13 +214,11 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                         if (!take_w(t)) { ok = false; break; }
                         tma_load_2d(smem + kMbWOff + t * kMbWBytes, &tmWe, &sh.wfull[t], kb * 32, ch * kMbChunk);
                     }
-                    for (int kb = 0; ok && kb < 4; kb++) {
-                        uint32_t t;
-                        if (*abort_flag || !take_w(t)) { ok = false; break; }
-                        tma_load_2d(smem + kMbWOff + t * kMbWBytes, &tmWp, &sh.wfull[t], ch * kMbChunk + kb * 32, 0);
-                    }
+                    if (ok && prev_ch >= 0) load_project(prev_ch);
+                    prev_ch = ch;
                 }
             }
+            if (ok && prev_ch >= 0) load_project(prev_ch);
             if (!ok) {
                 report_error(0x06000001u);
                 *abort_flag = 1;
@@ -227,9 +249,32 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                 wi++;
                 return mbar_wait(&sh.wfull[s], ph);
             };
+            // the project GEMM of chunk pg (chunk pch of the CTA's frame pj)
+            auto project = [&](uint32_t pg, int pch, uint32_t pj) {
+                // D of that chunk written; P free (first chunk of a frame)
+                if (!mbar_wait(&sh.d_full, pg & 1)) { ok = false; return; }
+                if (pch == 0 && pj > 0 && !mbar_wait(&sh.p_empty, (pj - 1) & 1)) { ok = false; return; }
+                tc_fence_after();
+                for (int kb = 0; kb < 4; kb++) {
+                    uint32_t t;
+                    if (*abort_flag || !wstage(t)) { ok = false; return; }
+                    tc_fence_after();
+                    const uint32_t sw = smem_u32(smem + kMbWOff + t * kMbWBytes);
+                    const uint32_t sd = smem_u32(smem + kMbDOff + kb * kMbXBytes);
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        mma_tf32(tmem + kMbPCol, smem_desc_sw128(sw) + 2 * k, smem_desc_sw128(sd) + 2 * k, idesc,
+                                 (pch > 0 || kb > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(&sh.wempty[t]);
+                }
+                mma_commit(&sh.d_empty);
+                if (pch == nchunks - 1) mma_commit(&sh.p_full);
+            };
+            int prev_ch = -1;
+            uint32_t prev_g = 0, prev_j = 0;
             for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x, j++) {
                 for (int ch = 0; ok && ch < nchunks; ch++, g++) {
-                    // E is free once the channel warps have read the previous chunk's
+                    // E is free once the channel warps have copied the previous chunk's
                     if (g > 0 && !mbar_wait(&sh.e_empty, (g - 1) & 1)) { ok = false; break; }
                     tc_fence_after();
                     for (int kb = 0; kb < kx; kb++) {
@@ -247,27 +292,14 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     }
                     if (!ok) break;
                     mma_commit(&sh.e_full);
-                    // D of this chunk written; P free (first chunk of a frame)
-                    if (!mbar_wait(&sh.d_full, g & 1)) { ok = false; break; }
-                    if (ch == 0 && j > 0 && !mbar_wait(&sh.p_empty, (j - 1) & 1)) { ok = false; break; }
-                    tc_fence_after();
-                    for (int kb = 0; kb < 4; kb++) {
-                        uint32_t t;
-                        if (*abort_flag || !wstage(t)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t sw = smem_u32(smem + kMbWOff + t * kMbWBytes);
-                        const uint32_t sd = smem_u32(smem + kMbDOff + kb * kMbXBytes);
-#pragma unroll
-                        for (int k = 0; k < 4; k++)
-                            mma_tf32(tmem + kMbPCol, smem_desc_sw128(sw) + 2 * k, smem_desc_sw128(sd) + 2 * k, idesc,
-                                     (ch > 0 || kb > 0 || k > 0) ? 1u : 0u);
-                        mma_commit(&sh.wempty[t]);
-                    }
-                    if (!ok) break;
-                    mma_commit(&sh.d_empty);
-                    if (ch == nchunks - 1) mma_commit(&sh.p_full);
+                    // the previous chunk's project GEMM, behind this expand
+                    if (prev_ch >= 0) project(prev_g, prev_ch, prev_j);
+                    prev_ch = ch;
+                    prev_g = g;
+                    prev_j = j;
                 }
             }
+            if (ok && prev_ch >= 0) project(prev_g, prev_ch, prev_j);
             if (!ok) {
                 report_error(0x06000002u);
                 *abort_flag = 1;
@@ -300,33 +332,51 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                 const float be = cv ? __ldg(a.b_exp + c) : 0.0f, bd = cv ? __ldg(a.b_dw + c) : 0.0f;
                 // the warp's lanes decide together (the TMEM loads are warp-collective)
                 if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_sleep(&sh.e_full, g & 1))) { ok = false; break; }
-                if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
                 tc_fence_after();
-                // expand epilogue of frame row r: bias, activation, zero outside the frame
-                auto erow = [&](int r, float (&v)[kMbRowStride]) {
-                    if (r < 0 || r >= a.h) {
+                // copy the seven E rows y0 - 1 .. y0 + 5 of this lane's channel
+                // into registers (rows outside the frame are not read), then
+                // release E so the next chunk's expand GEMM can start
+                constexpr int kWin = kMbHalfRows + 2;
+                uint32_t wr[kWin][kMbRowStride];
 #pragma unroll
-                        for (int x = 0; x < kMbRowStride; x++) v[x] = 0.0f;
-                        return;
+                for (int r = 0; r < kWin; r++) {
+                    const int row = y0 - 1 + r;
+                    if (row >= 0 && row < a.h) {  // warp-uniform
+#pragma unroll
+                        for (int k = 0; k < kMbRowStride / 2; k++)
+                            tmem_ld2(tlane + kMbECol + row * kMbRowStride + 2 * k, wr[r][2 * k], wr[r][2 * k + 1]);
+                    } else {
+#pragma unroll
+                        for (int x = 0; x < kMbRowStride; x++) wr[r][x] = 0u;
                     }
-                    tmem_row18(tlane + kMbECol + r * kMbRowStride, v);
+                }
 #pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++) v[x] += be;
-                    act_fixed_n<AE, kMbRowStride>(a.act_exp, v);
+                for (int r = 0; r < kWin; r++) tmem_wait_pin18(wr[r]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.e_empty);
+                // expand epilogue: bias, activation, zero outside the frame
+                float win[kWin][kMbRowStride];
+#pragma unroll
+                for (int r = 0; r < kWin; r++) {
+                    const int row = y0 - 1 + r;
+                    const bool rv = row >= 0 && row < a.h;
+#pragma unroll
+                    for (int x = 0; x < kMbRowStride; x++) win[r][x] = __uint_as_float(wr[r][x]) + be;
+                    act_fixed_n<AE, kMbRowStride>(a.act_exp, win[r]);
 #pragma unroll
                     for (int x = 0; x < kMbRowStride; x++)
-                        if (x >= a.w) v[x] = 0.0f;
-                };
-                float rw[3][kMbRowStride];  // rows y-1, y, y+1 of the window (renamed by the unrolled loop)
-                erow(y0 - 1, rw[0]);
-                erow(y0, rw[1]);
+                        if (!rv || x >= a.w) win[r][x] = 0.0f;
+                }
+                // D is free once the previous chunk's project GEMM has read it
+                if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
                 for (int i = 0; i < kMbHalfRows; i++) {
                     const int y = y0 + i;
-                    float(&ra)[kMbRowStride] = rw[i % 3];
-                    float(&rb)[kMbRowStride] = rw[(i + 1) % 3];
-                    float(&rc)[kMbRowStride] = rw[(i + 2) % 3];
-                    erow(y + 1, rc);
+                    const float(&ra)[kMbRowStride] = win[i];
+                    const float(&rb)[kMbRowStride] = win[i + 1];
+                    const float(&rc)[kMbRowStride] = win[i + 2];
                     // taps in (ky, kx) order from the bias, as the depthwise kernels
                     float o[kMbRowStride];
 #pragma unroll
@@ -353,13 +403,9 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                         *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ ((ysw + x) & 7)) << 4)) =
                             (yv && x < a.w) ? o[x] : 0.0f;
                 }
-                tc_fence_before();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&sh.e_empty);
-                    mbar_arrive(&sh.d_full);
-                }
+                if (lane == 0) mbar_arrive(&sh.d_full);
             }
             if (!ok) break;
             // ---- project epilogue of frame f: thread = output channel, this warp's rows
