@@ -12,11 +12,12 @@
 //                every 8th stage of its pipeline (TMA issue is limited per
 //                issuing thread, about one box in flight each: on B200 one
 //                lane moves ~0.65 us per 16 KB box per SM, four ~0.23 us)
-//   warp 10      second MMA issuer.  A tcgen05.mma costs its issuing thread
-//                ~80-90 ns whatever N is (M=128, K=8 TF32), so narrow tiles
-//                (N <= 64) run two pipelines: the CTA's even units use stage
-//                ring 0, MMA warp 0, accumulator 0 and epilogue group 0, the
-//                odd units ring 1, warp 10, accumulator 1 and group 1.
+//   warp 10      second MMA issuer.  One issuing thread sustains one
+//                M=128 K=8 TF32 MMA per ~55 SM clocks at N <= 64 (and ~43
+//                per SM with more issuers), so narrow k x k tiles run two
+//                pipelines: the CTA's even units use stage ring 0, MMA warp
+//                0, accumulator 0 and epilogue group 0, the odd units ring 1,
+//                warp 10, accumulator 1 and group 1.
 // Accumulators are double-buffered in TMEM so the epilogue of one tile
 // overlaps the mainloop of the next.  Operands are fp32 in HBM and are read
 // by the tensor core as TF32; both are K-major with the 128-byte swizzle.
@@ -30,6 +31,16 @@
 //              bh x bw block of output pixels of one frame, and each tap is
 //              the same box shifted by (kx*dil - pl, ky*dil - pt).  TMA's
 //              out-of-bounds zero fill is the convolution's zero padding.
+//   flat     : k x k, stride 1, narrow N.  One box of (16 + kw - 1) x bhx
+//              input pixels per K block serves every tap: the box's pixels
+//              in row-major order are the A rows, so tap (ky, kx)'s A
+//              operand is the 128 rows starting at row ky*bwx + kx, and
+//              accumulator row r is output pixel (r / bwx, r % bwx) of the
+//              tile (valid for r % bwx < 16 and r / bwx < 128 / bwx).  A
+//              stage feeds kh*kw MMA groups from one copy.  The tensor core
+//              applies the 128-byte swizzle to absolute shared-memory
+//              addresses, as the TMA wrote them, so a start row that is not
+//              a multiple of 8 reads the right bytes.
 // B operand (weights [tap][cout][cin_pad]): 3-D map, box (32, bn, 1).
 //
 // Split-K (small M, deep K): units = m_tiles x n_tiles x split.  Each unit
@@ -85,7 +96,10 @@ struct TcGeom {
     uint32_t b_bytes;
     uint32_t pipes;            // independent MMA pipelines (1 or 2), see tc_conv_kernel
     uint32_t halo;             // k x k stride 1: one A box per (kx, K block), see tc_conv_kernel
-    uint32_t a_bytes;          // A bytes per stage
+    uint32_t flat;             // k x k stride 1: one A box per K block serving every tap, see tc_conv_kernel
+    uint32_t bwx, bhx;         // flat mode: the box's width and height in input pixels
+    uint32_t a_bytes;          // A bytes per stage (flat: the box rounded up to 1 KB)
+    uint32_t a_box;            // bytes the A copy of a stage writes
     uint32_t b_resident;       // 1: the CTA's whole B (all taps and K blocks) is loaded once
     uint32_t bres_off;         // shared-memory offset of the resident B
     uint32_t res_off;          // per-warp residual prefetch buffers (0 = none)
@@ -98,6 +112,7 @@ struct TcArgs {
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
     uint32_t b_resident, bres_off, res_off, pipes, halo, a_bytes;
+    uint32_t flat, bwx, a_box;        // flat mode (see tc_conv_kernel)
     uint32_t res_patch;               // RES 3 epilogue: residual from per-warp exact-2x patches
     uint64_t units;                   // < 2^31 (checked at launch)
     FastDiv div_ntiles, div_split;    // unit -> (m tile, n tile, split)
@@ -318,7 +333,16 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
         const long long m = (long long)mt * kTcBM + row;
         return m < a.c.M ? m : -1;
     }
-    const int oy = o.oy0 + (int)(row >> a.lbw), ox = o.ox0 + (int)(row & (a.bw - 1));
+    int oy, ox;
+    if (a.flat) {
+        const uint32_t y = row / a.bwx, x = row - y * a.bwx;
+        if (x >= a.bw || y >= a.bh) return -1;  // a column of the right halo, or past the tile's rows
+        oy = o.oy0 + (int)y;
+        ox = o.ox0 + (int)x;
+    } else {
+        oy = o.oy0 + (int)(row >> a.lbw);
+        ox = o.ox0 + (int)(row & (a.bw - 1));
+    }
     if (oy >= a.c.oh || ox >= a.c.ow) return -1;
     return ((long long)o.img * a.c.oh + oy) * a.c.ow + ox;
 }
@@ -336,7 +360,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // 1024-align the stage buffers (128-byte swizzle atoms)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // stage = A tile (+ B tile unless B is resident for the whole kernel)
-    const uint32_t stage_bytes = a.a_bytes + (a.b_resident ? 0u : (a.halo ? a.c.kh : 1u) * a.b_bytes);
+    const uint32_t btiles = a.b_resident ? 0u : a.flat ? (uint32_t)(a.c.kh * a.c.kw) : a.halo ? (uint32_t)a.c.kh : 1u;
+    const uint32_t stage_bytes = a.a_bytes + btiles * a.b_bytes;
+    const uint32_t stage_tx = a.a_box + btiles * a.b_bytes;  // bytes the stage's copies write
     TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.shared_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -424,11 +450,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const TcUnit t = tc_unit(a, cur.u);
                 uint8_t *sa = smem + s * stage_bytes;
                 uint8_t *sb = sa + a.a_bytes;
-                mbar_expect_tx(&sh.full[s], stage_bytes);
+                mbar_expect_tx(&sh.full[s], stage_tx);
                 const uint32_t k = cur.k;
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
                 const int kc = (int)(kb * kTcBK);
-                if (a.halo) {
+                if (a.flat) {
+                    // stage = K block k: the tile's whole input window, every tap's B
+                    const TcOrigin o = tc_origin(a, t.mt);
+                    tma_load_4d(sa, &tmA, &sh.full[s], (int)(k * kTcBK), o.ox0 - a.c.pl, o.oy0 - a.c.pt, o.img);
+                    if (!a.b_resident)
+                        for (int tp = 0; tp < a.c.kh * a.c.kw; tp++)
+                            tma_load_3d(sb + tp * a.b_bytes, &tmB, &sh.full[s], (int)(k * kTcBK), (int)(t.nt * a.bn),
+                                        tp);
+                } else if (a.halo) {
                     // stage = column shift kx (= tap here), K block kb: rows
                     // [ybase, ybase + bh + kh - 1) x the bw columns at xbase + kx
                     const TcOrigin o = tc_origin(a, t.mt);
@@ -446,7 +480,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 } else {
                     tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                 }
-                if (!a.b_resident && !a.halo) tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
+                if (!a.b_resident && !a.halo && !a.flat)
+                    tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
                 last_mine = s | (ph << 16);
                 for (uint32_t i = 0; i < LQ && cur.u < a.units; i++, it++) advance(cur);
             }
@@ -497,7 +532,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * stage_bytes);
-                    if (a.halo) {
+                    if (a.flat) {
+                        // K block k; tap (ky, kx) reads the box from row ky * bwx + kx
+                        const uint32_t taps = (uint32_t)(a.c.kh * a.c.kw);
+                        for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++)
+                            for (uint32_t kx = 0; kx < (uint32_t)a.c.kw; kx++) {
+                                const uint32_t tap = ky * a.c.kw + kx;
+                                const uint32_t sb = a.b_resident
+                                                        ? smem_u32(smem + a.bres_off + (tap * a.kblocks + k) * a.b_bytes)
+                                                        : sa + a.a_bytes + tap * a.b_bytes;
+                                const uint64_t ad = smem_desc_sw128(sa + (ky * a.bwx + kx) * 128),
+                                               bd = smem_desc_sw128(sb);
+#pragma unroll
+                                for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
+                                    mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                             (k > k0 || tap > 0 || kk > 0) ? 1u : 0u);
+                            }
+                        (void)taps;
+                    } else if (a.halo) {
                         // tap (ky, kx): the stage's copy shifted down ky rows
                         // (ky * bw A rows, a multiple of 8 rows: swizzle-aligned)
                         const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
@@ -888,7 +940,8 @@ static inline bool tc_igemm_supported(uint32_t kh, uint32_t kw, uint32_t sh, uin
 // Plan the tensor-core launch.  Returns 0 or a negative code.
 static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, uint32_t cout, uint32_t kh, uint32_t kw,
                           uint32_t sh, uint32_t sw, uint32_t dil, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
-                          uint32_t split_req, uint32_t res_kind, TcGeom *g, bool allow_halo = true)
+                          uint32_t split_req, uint32_t res_kind, TcGeom *g, bool allow_halo = true,
+                          bool allow_flat = true)
 {
     (void)ih; (void)iw; (void)pt; (void)pl;
     *g = TcGeom{};
@@ -905,16 +958,39 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     // kh x kw x kblocks.
     g->halo = (allow_halo && !pw && sh == 1 && sw == 1 && dil == 1 && kh >= 2 && kh <= 7) ? 1u : 0u;
     g->a_bytes = kTcABytes;
-    if (g->halo) {
-        g->k_iters = kw * g->kblocks;
-        g->a_bytes = (8 + kh - 1) * 16 * kTcBK * 4;
-    }
     // N tile: fewest tiles of <= 256 columns, each a multiple of 32 so the
     // epilogue's 32-column store boxes never reach into the next tile
     const uint32_t nt = (cout + 255) / 256;
     g->bn = ((cout + nt - 1) / nt + 31) / 32 * 32;
     g->n_tiles = (cout + g->bn - 1) / g->bn;
+    // Flat mode for narrow k x k stride-1 convs (N <= 64): their MMAs are
+    // short, so the per-tap (or per-kx) TMA boxes set the pace; one box per
+    // K block, 16 + kw - 1 pixels wide, serves every tap.  Accumulator rows
+    // past the tile's 16 columns (and its last partial row) are computed
+    // and dropped: 112 of 128 rows are outputs for a 3 x 3 kernel.
+    if (g->halo && allow_flat && g->bn <= 64 && kw <= 7) {
+        const uint32_t bwx = 16 + kw - 1, tr = kTcBM / bwx;
+        const uint32_t rows = ((kh - 1) * bwx + (kw - 1) + kTcBM + bwx - 1) / bwx;
+        g->flat = 1;
+        g->halo = 0;
+        g->bwx = bwx;
+        g->bhx = rows;
+        g->bw = 16;
+        g->bh = tr;
+        g->k_iters = g->kblocks;
+        g->a_box = bwx * rows * kTcBK * 4;
+        g->a_bytes = (g->a_box + 1023) / 1024 * 1024;  // the next stage's copy stays 1 KB aligned
+    }
     if (g->halo) {
+        g->k_iters = kw * g->kblocks;
+        g->a_bytes = (8 + kh - 1) * 16 * kTcBK * 4;
+    }
+    if (!g->flat) g->a_box = g->a_bytes;
+    if (g->flat) {
+        g->tiles_x = (ow + g->bw - 1) / g->bw;
+        g->tiles_y = (oh + g->bh - 1) / g->bh;
+        g->m_tiles = n * g->tiles_x * g->tiles_y;
+    } else if (g->halo) {
         g->bw = 16;
         g->bh = 8;
         g->tiles_x = (ow + g->bw - 1) / g->bw;
@@ -1000,11 +1076,13 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     const uint64_t bres = (uint64_t)g->taps * g->kblocks * g->b_bytes;
     g->b_resident = (g->n_tiles == 1 && g->split == 1 && bres <= kTcBResidentMax &&
                      (limit - out_bytes - bres) / g->a_bytes >= 4) ? 1u : 0u;
-    const uint32_t stage = g->a_bytes + (g->b_resident ? 0u : (g->halo ? kh : 1u) * g->b_bytes);
+    const uint32_t stage = g->a_bytes + (g->b_resident ? 0u : (g->flat ? kh * kw : g->halo ? kh : 1u) * g->b_bytes);
     const uint32_t fixed = out_bytes + (g->b_resident ? (uint32_t)bres : 0u);
     g->stages = std::min<uint32_t>(8, (limit - fixed) / stage);
+    if (g->flat && g->stages < 3)  // flat stages too large: the per-kx halo boxes
+        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, true, false);
     if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
-        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false);
+        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false, false);
     if (g->stages < 2) return -2;
     // narrow k x k tiles (long K loops, N <= 128) are bound by the per-thread
     // MMA issue cost: two pipelines.  1x1 GEMMs keep one deep ring (their
@@ -1073,8 +1151,8 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         const cuuint64_t dims[4] = {(cuuint64_t)c.cin, (cuuint64_t)c.iw, (cuuint64_t)c.ih, (cuuint64_t)c.n};
         const cuuint64_t strides[3] = {(cuuint64_t)c.x_stride * 4, (cuuint64_t)c.x_stride * 4 * c.iw,
                                        (cuuint64_t)c.x_stride * 4 * c.iw * c.ih};
-        const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.bw * (cuuint32_t)c.sw,
-                                   g.halo ? g.bh + (cuuint32_t)c.kh - 1 : g.bh * (cuuint32_t)c.sh, 1};
+        const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.flat ? g.bwx : g.bw * (cuuint32_t)c.sw,
+                                   g.flat ? g.bhx : g.halo ? g.bh + (cuuint32_t)c.kh - 1 : g.bh * (cuuint32_t)c.sh, 1};
         const cuuint32_t estr[4] = {1, (cuuint32_t)c.sw, (cuuint32_t)c.sh, 1};
         r = enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)abase, dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1114,6 +1192,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
     a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
     a.halo = g.halo; a.a_bytes = g.a_bytes;
+    a.flat = g.flat; a.bwx = g.bwx; a.a_box = g.a_box;
     // patches need 16-byte residual rows (the plan checked the shapes)
     a.res_patch = (g.res_patch && c.res && c.res_mode && c.vec_y) ? 1u : 0u;
     if (g.units >= (1ull << 31) || (uint64_t)g.m_tiles * g.n_tiles * g.split >= (1ull << 31)) {
