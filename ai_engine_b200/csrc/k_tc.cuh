@@ -13,11 +13,13 @@
 //                issuing thread, about one box in flight each: on B200 one
 //                lane moves ~0.65 us per 16 KB box per SM, four ~0.23 us)
 //   warp 10      second MMA issuer.  One issuing thread sustains one
-//                M=128 K=8 TF32 MMA per ~55 SM clocks at N <= 64 (and ~43
-//                per SM with more issuers), so narrow k x k tiles run two
+//                M=128 K=8 TF32 MMA per ~55-75 SM clocks at N <= 64 (~45 per
+//                SM with two issuers), so narrow k x k tiles run two
 //                pipelines: the CTA's even units use stage ring 0, MMA warp
-//                0, accumulator 0 and epilogue group 0, the odd units ring 1,
-//                warp 10, accumulator 1 and group 1.
+//                0, accumulators 0-1 and epilogue group 0, the odd units ring
+//                1, warp 10, accumulators 2-3 and group 1 (each pipeline's
+//                tiles alternate between its two accumulators, so its MMAs
+//                never wait for the epilogue of its previous tile).
 // Accumulators are double-buffered in TMEM so the epilogue of one tile
 // overlaps the mainloop of the next.  Operands are fp32 in HBM and are read
 // by the tensor core as TF32; both are K-major with the 128-byte swizzle.
@@ -283,8 +285,8 @@ __device__ __forceinline__ void tmem_wait32(int remaining, uint32_t (&r)[32])
 struct TcShared {
     uint64_t full[8];
     uint64_t empty[8];
-    uint64_t acc_full[2];
-    uint64_t acc_empty[2];
+    uint64_t acc_full[4];
+    uint64_t acc_empty[4];
     uint64_t bfull;  // resident B landed
     uint32_t tmem_base;
     uint32_t abort;
@@ -327,6 +329,7 @@ __device__ __forceinline__ TcOrigin tc_origin(const TcArgs &a, uint32_t mt)
 
 // Output pixel of accumulator row `row` of M tile `mt` (origin o for k x k
 // tiles), or -1 if outside.
+template <bool FLAT>
 __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, const TcOrigin &o, uint32_t row)
 {
     if (!a.igemm) {
@@ -334,7 +337,7 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
         return m < a.c.M ? m : -1;
     }
     int oy, ox;
-    if (a.flat) {
+    if constexpr (FLAT) {
         const uint32_t y = row / a.bwx, x = row - y * a.bwx;
         if (x >= a.bw || y >= a.bh) return -1;  // a column of the right halo, or past the tile's rows
         oy = o.oy0 + (int)y;
@@ -352,7 +355,7 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
 // 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches.
 // ACT: the activation when it is kNone or kRelu, else -1 (any kind, chosen
 // at run time)
-template <int RES, int ACT>
+template <int RES, int ACT, bool FLAT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
 {
@@ -360,7 +363,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // 1024-align the stage buffers (128-byte swizzle atoms)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // stage = A tile (+ B tile unless B is resident for the whole kernel)
-    const uint32_t btiles = a.b_resident ? 0u : a.flat ? (uint32_t)(a.c.kh * a.c.kw) : a.halo ? (uint32_t)a.c.kh : 1u;
+    const uint32_t btiles = a.b_resident ? 0u : FLAT ? (uint32_t)(a.c.kh * a.c.kw) : a.halo ? (uint32_t)a.c.kh : 1u;
     const uint32_t stage_bytes = a.a_bytes + btiles * a.b_bytes;
     const uint32_t stage_tx = a.a_box + btiles * a.b_bytes;  // bytes the stage's copies write
     TcShared &sh = *reinterpret_cast<TcShared *>(smem + a.shared_off);
@@ -371,7 +374,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&sh.full[s], 1);
             mbar_init(&sh.empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < 4; b++) {
             mbar_init(&sh.acc_full[b], 1);
             mbar_init(&sh.acc_empty[b], 4);
         }
@@ -454,7 +457,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t k = cur.k;
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
                 const int kc = (int)(kb * kTcBK);
-                if (a.flat) {
+                if (FLAT) {
                     // stage = K block k: the tile's whole input window, every tap's B
                     const TcOrigin o = tc_origin(a, t.mt);
                     tma_load_4d(sa, &tmA, &sh.full[s], (int)(k * kTcBK), o.ox0 - a.c.pl, o.oy0 - a.c.pt, o.img);
@@ -480,7 +483,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 } else {
                     tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
                 }
-                if (!a.b_resident && !a.halo && !a.flat)
+                if (!a.b_resident && !a.halo && !FLAT)
                     tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
                 last_mine = s | (ph << 16);
                 for (uint32_t i = 0; i < LQ && cur.u < a.units; i++, it++) advance(cur);
@@ -512,9 +515,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const TcUnit t = tc_unit(a, u);
                 const uint32_t k0 = t.s * a.k_per_split;
                 const uint32_t k1 = min(a.k_iters, k0 + a.k_per_split);
-                // accumulator buffer: with two pipelines each owns one; with one,
+                // accumulator buffer: with two pipelines each owns two (its
+                // tiles alternate between them, so a tile's MMAs never wait
+                // for the epilogue of the pipeline's previous tile); with one,
                 // tiles alternate between the two buffers
-                const uint32_t ab = P == 2 ? p : (nt & 1), aph = P == 2 ? (nt & 1) : ((nt >> 1) & 1);
+                const uint32_t ab = P == 2 ? p * 2 + (nt & 1) : (nt & 1), aph = (nt >> 1) & 1;
                 if (*abort_flag || !mbar_wait(&sh.acc_empty[ab], aph ^ 1)) {
                     report_error(0x01000002);
                     *abort_flag = 1;
@@ -532,9 +537,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * stage_bytes);
-                    if (a.flat) {
+                    if constexpr (FLAT) {
                         // K block k; tap (ky, kx) reads the box from row ky * bwx + kx
-                        const uint32_t taps = (uint32_t)(a.c.kh * a.c.kw);
+                        // (a fully unrolled 3 x 3 loop with precomputed descriptors
+                        // measured 10-50% slower: smooth4 141 -> 168 us)
                         for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++)
                             for (uint32_t kx = 0; kx < (uint32_t)a.c.kw; kx++) {
                                 const uint32_t tap = ky * a.c.kw + kx;
@@ -548,7 +554,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                     mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
                                              (k > k0 || tap > 0 || kk > 0) ? 1u : 0u);
                             }
-                        (void)taps;
                     } else if (a.halo) {
                         // tap (ky, kx): the stage's copy shifted down ky rows
                         // (ky * bw A rows, a multiple of 8 rows: swizzle-aligned)
@@ -779,14 +784,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t k = 0;  // tiles this group has drained: the phase of its buffer
         for (uint64_t u = blockIdx.x + (uint64_t)grp * gridDim.x; u < a.units; u += 2ull * gridDim.x, k++) {
             const TcUnit t = tc_unit(a, u);
-            const uint32_t ab = grp, aph = k & 1;
+            // the group's k-th tile: buffer grp (one pipeline) or 2 grp + k % 2
+            // (two pipelines, pipeline grp's tiles), see the MMA issuers
+            const uint32_t ab = a.pipes == 2 ? grp * 2 + (k & 1) : grp, aph = a.pipes == 2 ? (k >> 1) & 1 : k & 1;
             const int ncol = (int)min(a.bn, (uint32_t)c.y_pad_to - t.nt * a.bn);
             const int nbase = (int)(t.nt * a.bn);
             const uint32_t tbase = tmem + ((quad * 32) << 16) + ab * a.bn;
             const uint64_t tile = (uint64_t)t.mt * a.n_tiles + t.nt;
             const TcOrigin org = a.igemm ? tc_origin(a, t.mt) : TcOrigin{0, 0, 0};
 #pragma unroll
-            for (int i = 0; i < 8; i++) mrow[i] = (int)tc_row_pixel(a, t.mt, org, quad * 32 + i * 4 + (lane >> 3));
+            for (int i = 0; i < 8; i++) mrow[i] = (int)tc_row_pixel<FLAT>(a, t.mt, org, quad * 32 + i * 4 + (lane >> 3));
             if constexpr (RES == 3) {
                 const long long m0 = (long long)t.mt * kTcBM + quad * 32;
                 wm0 = m0 < c.M ? (int)m0 : -1;
@@ -1093,7 +1100,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->res_off = res_buf ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;
     g->res_patch = (res_kind == kTcResUp2 && !g->igemm) ? 1u : 0u;
     g->shared_off = g->out_off + out_bytes;
-    g->tmem_cols = tc_pow2_ceil(2 * g->bn);
+    g->tmem_cols = tc_pow2_ceil((g->pipes == 2 ? 4 : 2) * g->bn);  // two accumulators per pipeline
     if (g->tmem_cols > 512) return -3;
     g->smem_bytes = g->shared_off + 1024 + (uint32_t)sizeof(TcShared);
     g->grid = std::min<uint64_t>(g->units, 148);
@@ -1227,13 +1234,24 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     const int kind = !c.res ? 0 : !c.res_mode ? 1 : a.res_patch ? 3 : 2;
     // the activation as a template argument where it is none or ReLU (one
     // inlined switch over every kind per chunk costs instruction-cache misses)
+    // flat mode is its own instantiation, so the other layers' kernels
+    // carry none of its code (1x1 GEMMs measured 25% slower with it inline)
     using Kern = void (*)(CUtensorMap, CUtensorMap, TcArgs);
     static const Kern kerns[4][3] = {
-        {tc_conv_kernel<0, kNone>, tc_conv_kernel<0, kRelu>, tc_conv_kernel<0, -1>},
-        {tc_conv_kernel<1, kNone>, tc_conv_kernel<1, kRelu>, tc_conv_kernel<1, -1>},
-        {tc_conv_kernel<2, kNone>, tc_conv_kernel<2, kRelu>, tc_conv_kernel<2, -1>},
-        {tc_conv_kernel<3, kNone>, tc_conv_kernel<3, kRelu>, tc_conv_kernel<3, -1>}};
-    auto kern = kerns[kind][c.act == kNone ? 0 : c.act == kRelu ? 1 : 2];
+        {tc_conv_kernel<0, kNone, false>, tc_conv_kernel<0, kRelu, false>, tc_conv_kernel<0, -1, false>},
+        {tc_conv_kernel<1, kNone, false>, tc_conv_kernel<1, kRelu, false>, tc_conv_kernel<1, -1, false>},
+        {tc_conv_kernel<2, kNone, false>, tc_conv_kernel<2, kRelu, false>, tc_conv_kernel<2, -1, false>},
+        {tc_conv_kernel<3, kNone, false>, tc_conv_kernel<3, kRelu, false>, tc_conv_kernel<3, -1, false>}};
+    static const Kern kerns_flat[3][3] = {
+        {tc_conv_kernel<0, kNone, true>, tc_conv_kernel<0, kRelu, true>, tc_conv_kernel<0, -1, true>},
+        {tc_conv_kernel<1, kNone, true>, tc_conv_kernel<1, kRelu, true>, tc_conv_kernel<1, -1, true>},
+        {tc_conv_kernel<2, kNone, true>, tc_conv_kernel<2, kRelu, true>, tc_conv_kernel<2, -1, true>}};
+    const int ak = c.act == kNone ? 0 : c.act == kRelu ? 1 : 2;
+    if (g.flat && kind == 3) {
+        snprintf(err, errlen, "flat tiles take no exact-2x residual patches");
+        return -2;
+    }
+    auto kern = g.flat ? kerns_flat[kind][ak] : kerns[kind][ak];
     {
         cudaError_t e = ensure_smem_attr((const void *)kern, 227 * 1024);
         if (e != cudaSuccess) {
