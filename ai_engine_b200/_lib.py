@@ -74,6 +74,7 @@ SIGNATURES = {
     "aie_conv_pack_weights": (C.c_int, [_vp, C.c_int32, _fp, _fp, _vp, _vp, _vp]),
     "aie_conv_run": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "aie_conv_run_noalloc": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "aie_conv_plan_parts": (C.c_int, [C.POINTER(ConvDesc), C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(_vp)]),
     "aie_resize_bilinear": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _vp, C.c_uint32,
                                       C.c_uint32, C.c_int32, _vp, C.c_int32, _vp, _vp]),
     "aie_status_string": (C.c_char_p, [C.c_int]),
@@ -94,6 +95,7 @@ SIGNATURES = {
     "aie_channel_copy": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, TView, C.c_int32, TView, _vp]),
     "aie_concat": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(TView), C.POINTER(C.c_uint32), C.c_uint32,
                              TView, _vp]),
+    "aie_conv_run_parts": (C.c_int, [_vp, C.POINTER(TView), _vp, _vp, _vp, _vp, _vp, _vp]),
 }
 
 _LIB = None

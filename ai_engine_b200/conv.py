@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass
-from typing import Optional, Tuple
+from typing import Sequence, Optional, Tuple
 
 import numpy as np
 import torch
@@ -99,7 +99,8 @@ class ConvPlan:
     def __init__(self, op: Conv2d, n: int, ih: int, iw: int, *, has_res: bool = False, layout: str = "nhwc",
                  math: str = "auto", split_k: int = 0, in_view: Optional[View] = None,
                  res_view: Optional[View] = None, out_view: Optional[View] = None,
-                 res_resize: Optional[Tuple[int, int, str]] = None, device=None):
+                 res_resize: Optional[Tuple[int, int, str]] = None, parts: Optional[Sequence[int]] = None,
+                 device=None):
         self.lib = _lib.load()
         self.op, self.n, self.ih, self.iw = op, n, ih, iw
         self.layout = layout
@@ -124,7 +125,14 @@ class ConvPlan:
         self.res_resize = res_resize
         self.desc = d
         h = C.c_void_p()
-        check(self.lib.aie_conv_plan(C.byref(d), C.byref(h)), "aie_conv_plan")
+        self.parts = tuple(int(c) for c in parts) if parts else None
+        if self.parts:
+            # concat-into-conv: the input is the channel concat of these
+            # parts, read in place (aie_conv_plan_parts)
+            pc = (C.c_uint32 * len(self.parts))(*self.parts)
+            check(self.lib.aie_conv_plan_parts(C.byref(d), len(self.parts), pc, C.byref(h)), "aie_conv_plan_parts")
+        else:
+            check(self.lib.aie_conv_plan(C.byref(d), C.byref(h)), "aie_conv_plan")
         self._h = h
         info = _lib.PlanInfo()
         check(self.lib.aie_conv_plan_info(h, C.byref(info)), "aie_conv_plan_info")
@@ -186,6 +194,29 @@ class ConvPlan:
         check(self.lib.aie_conv_run(self._h, _dptr(x), C.c_void_p(self.w.data_ptr()), C.c_void_p(self.b.data_ptr()),
                                     _dptr(res), _dptr(out), ws, C.c_void_p(_stream_handle(stream))), "aie_conv_run")
         return out
+
+
+def run_parts(plan: "ConvPlan", parts: Sequence, res: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+              stream=None) -> torch.Tensor:
+    """Run a concat-into-conv plan (ConvPlan(..., parts=...)) over its parts,
+    read in place (aie_conv_run_parts).  Each part is a dense [n, h, w, c_i]
+    tensor or a (tensor, coff) channel view of a wider buffer [n, h, w,
+    stride] holding the part at channels coff .. coff + c_i."""
+    if not plan.parts or len(parts) != len(plan.parts):
+        raise ValueError("plan and parts disagree")
+    if plan.w is None:
+        raise RuntimeError("load_weights() first")
+    tv = (_lib.TView * len(parts))()
+    for i, pt in enumerate(parts):
+        t, coff = (pt, 0) if isinstance(pt, torch.Tensor) else pt
+        tv[i] = _lib.TView(C.c_void_p(t.data_ptr()), t.shape[-1], coff)
+    if out is None:
+        out = torch.empty(plan.out_shape(), dtype=torch.float32, device=plan.device)
+    ws = None if plan.workspace is None else C.c_void_p(plan.workspace.data_ptr())
+    check(plan.lib.aie_conv_run_parts(plan._h, tv, C.c_void_p(plan.w.data_ptr()), C.c_void_p(plan.b.data_ptr()),
+                                      _dptr(res), _dptr(out), ws, C.c_void_p(_stream_handle(stream))),
+          "aie_conv_run_parts")
+    return out
 
 
 def run_dw_pw(dw: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, out: Optional[torch.Tensor] = None,

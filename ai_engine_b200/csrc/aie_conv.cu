@@ -75,6 +75,9 @@ struct aie_plan {
     StemGeom sg;
     uint32_t stem_smem;
     bool pws;          // 1x1 on the FP32 pipes for cin, cout in {32, 64}, see pw_simt_kernel
+    // concat parts read in place (aie_conv_plan_parts): 0 = a plain plan
+    uint32_t nparts;
+    uint32_t part_c[3], part_kb0[3];
 };
 
 static const int kMathStrict = AIE_MATH_FP32_STRICT;
@@ -206,7 +209,9 @@ static bool dw_up2_tmap(const void *q, uint32_t n, uint32_t h, uint32_t w, uint3
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
+// nparts > 0: the input is the channel concat of nparts views of part_c[i]
+// channels (aie_conv_plan_parts); the plan must resolve to the tensor cores.
+static int plan_impl(const aie_conv_desc *desc, uint32_t nparts, const uint32_t *part_c, aie_plan **out)
 {
     if (!desc || !out) return fail(AIE_E_INVALID, "null argument");
     *out = nullptr;
@@ -228,9 +233,31 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
     const long long ww = (long long)d.iw + d.pad[1] + d.pad[3] - ekw;
     if (hh < 0 || ww < 0) return fail(AIE_E_INVALID, "kernel larger than padded input");
 
+    uint32_t kblocks_parts = 0, part_kb0[3] = {0, 0, 0};
+    if (nparts) {
+        if (nparts > 3 || !part_c) return fail(AIE_E_INVALID, "1 to 3 concat parts, got %u", nparts);
+        uint64_t sum = 0;
+        for (uint32_t i = 0; i < nparts; i++) {
+            if (!part_c[i]) return fail(AIE_E_INVALID, "concat part %u has no channels", i);
+            part_kb0[i] = kblocks_parts;
+            kblocks_parts += (part_c[i] + kTcBK - 1) / kTcBK;
+            sum += part_c[i];
+        }
+        if (sum != d.cin) return fail(AIE_E_INVALID, "concat parts hold %llu channels, cin is %u",
+                                       (unsigned long long)sum, d.cin);
+        if (d.groups != 1 || d.layout != AIE_LAYOUT_NHWC || d.in_stride || d.in_coff ||
+            (d.math != AIE_MATH_AUTO && d.math != AIE_MATH_TF32))
+            return fail(AIE_E_UNSUPPORTED, "concat parts need a dense-layout, non-grouped conv on the tensor cores "
+                                           "(math auto or tf32; each part's view is given at run time)");
+    }
     aie_plan *p = new (std::nothrow) aie_plan();
     if (!p) return fail(AIE_E_NOMEM, "plan allocation");
     p->d = d;
+    p->nparts = nparts;
+    for (uint32_t i = 0; i < nparts; i++) {
+        p->part_c[i] = part_c[i];
+        p->part_kb0[i] = part_kb0[i];
+    }
     p->oh = (uint32_t)(hh / d.sh + 1);
     p->ow = (uint32_t)(ww / d.sw + 1);
     p->M = (long long)d.n * p->oh * p->ow;
@@ -293,7 +320,18 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
 
     // Math.
     const char *why = "";
-    if (stem_tc_shape && (d.math == AIE_MATH_AUTO || d.math == AIE_MATH_TF32)) {
+    if (nparts) {
+        // parts are read by the tensor-core GEMM's TMA copies only
+        if (p->kernel != AIE_KERNEL_PW && p->kernel != AIE_KERNEL_IGEMM) {
+            delete p;
+            return fail(AIE_E_UNSUPPORTED, "concat parts: 1x1 with cout <= 4 runs the dot kernel; concat first");
+        }
+        if (d.sh > 2 || d.sw > 2 || !tc_igemm_supported(d.kh, d.kw, d.sh, d.sw, p->ow)) {
+            delete p;
+            return fail(AIE_E_UNSUPPORTED, "concat parts: conv geometry outside the tensor-core kernel");
+        }
+        p->math = AIE_MATH_TF32;
+    } else if (stem_tc_shape && (d.math == AIE_MATH_AUTO || d.math == AIE_MATH_TF32)) {
         p->math = AIE_MATH_TF32;
         p->stem_tc = true;
     } else if (p->kernel == AIE_KERNEL_DW || p->kernel == AIE_KERNEL_PW_DOT) {
@@ -332,7 +370,9 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
         p->wbytes = (uint64_t)d.cout * d.cin * 4;
         p->grid = (uint64_t)((p->M + 255) / 256);
     } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
-        p->cin_pad = (int)rup(d.cin, 4);
+        // weights [tap][cout][cin_pad]; with parts every part's channels
+        // start on a 32-channel K block (zero weight rows between parts)
+        p->cin_pad = nparts ? (int)(kblocks_parts * kTcBK) : (int)rup(d.cin, 4);
         p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
         // residual buffers: rows of a residual tensor, or per-warp patches
         // of an exact-2x half_pixel residual on 1x1 tiles (32 consecutive
@@ -346,8 +386,8 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
                                      p->r_coff % 4 == 0)
                                       ? kTcResUp2
                                       : kTcResNone;
-        int rc = tc_plan(d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw, d.dil, d.pad[0], d.pad[1], p->oh, p->ow,
-                         d.split_k, res_kind, &p->tc);
+        int rc = tc_plan(d.n, d.ih, d.iw, nparts ? (uint32_t)p->cin_pad : d.cin, d.cout, d.kh, d.kw, d.sh, d.sw,
+                         d.dil, d.pad[0], d.pad[1], p->oh, p->ow, d.split_k, res_kind, &p->tc);
         if (rc) {
             delete p;
             return fail(AIE_E_UNSUPPORTED, "tensor-core geometry rejected (%d)", rc);
@@ -392,6 +432,14 @@ extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out)
                            (uint64_t)p->M * d.cout + res_px * d.cout);
     *out = p;
     return AIE_OK;
+}
+
+extern "C" int aie_conv_plan(const aie_conv_desc *desc, aie_plan **out) { return plan_impl(desc, 0, nullptr, out); }
+
+extern "C" int aie_conv_plan_parts(const aie_conv_desc *desc, uint32_t nparts, const uint32_t *part_c, aie_plan **out)
+{
+    if (!nparts) return fail(AIE_E_INVALID, "1 to 3 concat parts, got 0");
+    return plan_impl(desc, nparts, part_c, out);
 }
 
 extern "C" int aie_conv_plan_info(const aie_plan *p, aie_plan_info *info)
@@ -464,11 +512,22 @@ extern "C" int aie_conv_pack_weights(const aie_plan *p, int32_t wfmt, const floa
     } else if (p->kernel == AIE_KERNEL_PW_DOT) {
         memcpy(pw.data(), w, (size_t)d.cout * d.cin * 4);  // [cout][cin]
     } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
-        // [tap][cout][cin_pad]: K-major rows for the tcgen05 B operand
+        // [tap][cout][cin_pad]: K-major rows for the tcgen05 B operand; with
+        // concat parts, input channel ic of part i sits at K position
+        // 32 * part_kb0[i] + (ic - the part's first channel)
+        std::vector<uint32_t> kpos(d.cin);
+        for (uint32_t ic = 0, i = 0, c0 = 0; ic < d.cin; ic++) {
+            if (p->nparts) {
+                while (ic >= c0 + p->part_c[i]) c0 += p->part_c[i++];
+                kpos[ic] = p->part_kb0[i] * kTcBK + (ic - c0);
+            } else {
+                kpos[ic] = ic;
+            }
+        }
         for (uint32_t t = 0; t < taps; t++)
             for (uint32_t oc = 0; oc < d.cout; oc++)
                 for (uint32_t ic = 0; ic < d.cin; ic++)
-                    pw[((size_t)t * d.cout + oc) * p->cin_pad + ic] = w[((size_t)oc * cin_g + ic) * taps + t];
+                    pw[((size_t)t * d.cout + oc) * p->cin_pad + kpos[ic]] = w[((size_t)oc * cin_g + ic) * taps + t];
     } else {
         // [tap][cin][wn] (conv.rs:44-66 with cout padded to 4)
         for (uint32_t t = 0; t < taps; t++)
@@ -530,6 +589,7 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
     if (p->d.has_res && !res) return fail(AIE_E_INVALID, "plan has a residual but res is NULL");
     if (p->wsbytes && !workspace) return fail(AIE_E_INVALID, "plan needs %llu workspace bytes",
                                               (unsigned long long)p->wsbytes);
+    if (p->nparts) return fail(AIE_E_INVALID, "the plan reads concat parts: run it with aie_conv_run_parts");
     if (((uintptr_t)w | (uintptr_t)b) % 16) return fail(AIE_E_ALIGN, "weights/bias must be 16-byte aligned");
     cudaStream_t s = (cudaStream_t)stream;
     const ConvArgs a = make_args(p, in, w, b, res, out);
@@ -760,6 +820,38 @@ static int run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, con
 #undef AIE_DWH
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "fused head launch");
+    return AIE_OK;
+}
+
+extern "C" int aie_conv_run_parts(const aie_plan *p, const aie_tview *parts, const void *w, const void *b,
+                                  const void *res, void *out, void *workspace, void *stream)
+{
+    if (!p || !parts || !w || !b || !out) return fail(AIE_E_INVALID, "null argument");
+    if (!p->nparts) return fail(AIE_E_INVALID, "the plan was made without concat parts: run it with aie_conv_run");
+    if (p->d.has_res && !res) return fail(AIE_E_INVALID, "plan has a residual but res is NULL");
+    if (p->wsbytes && !workspace) return fail(AIE_E_INVALID, "plan needs %llu workspace bytes",
+                                              (unsigned long long)p->wsbytes);
+    if (((uintptr_t)w | (uintptr_t)b) % 16) return fail(AIE_E_ALIGN, "weights/bias must be 16-byte aligned");
+    TcParts tp;
+    tp.n = (int)p->nparts;
+    for (uint32_t i = 0; i < p->nparts; i++) {
+        if (!parts[i].data) return fail(AIE_E_INVALID, "concat part %u: null data", i);
+        const long long st = parts[i].stride ? parts[i].stride : p->part_c[i];
+        if ((long long)parts[i].coff + p->part_c[i] > st)
+            return fail(AIE_E_INVALID, "concat part %u: channel view exceeds its pixel stride", i);
+        tp.x[i] = (const float *)parts[i].data;
+        tp.stride[i] = st;
+        tp.coff[i] = (int)parts[i].coff;
+        tp.c[i] = p->part_c[i];
+        tp.kb0[i] = p->part_kb0[i];
+    }
+    ConvArgs a = make_args(p, parts[0].data, w, b, res, out);
+    a.x_stride = tp.stride[0];
+    a.x_coff = tp.coff[0];
+    int rc = tc_launch(p->tc, a, workspace, (cudaStream_t)stream, t_err, sizeof t_err, &tp);
+    if (rc) return rc;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core conv launch");
     return AIE_OK;
 }
 

@@ -140,6 +140,36 @@ __device__ __forceinline__ float madd(float acc, float a, float b)
     else return fmaf(a, b, acc);
 }
 
+// madd on one packed pair (a0, a1) += (x0, x1) * (w0, w1), see madd4
+template <bool kStrict>
+__device__ __forceinline__ void madd2(float &a0, float &a1, const float2 &x, const float2 &w)
+{
+    float2 a = make_float2(a0, a1);
+    if constexpr (kStrict) a = __fadd2_rn(a, __fmul2_rn(x, w));
+    else a = __ffma2_rn(x, w, a);
+    a0 = a.x;
+    a1 = a.y;
+}
+
+// madd over four channels as two packed pairs: sm_100's two-wide FP32
+// instructions do one pair per instruction, each lane rounded exactly as the
+// scalar form (fused, or multiply then add in ai-cpu's order).
+template <bool kStrict>
+__device__ __forceinline__ void madd4(float (&acc)[4], const float4 &x, const float4 &w)
+{
+    float2 a0 = make_float2(acc[0], acc[1]), a1 = make_float2(acc[2], acc[3]);
+    const float2 x0 = make_float2(x.x, x.y), x1 = make_float2(x.z, x.w);
+    const float2 w0 = make_float2(w.x, w.y), w1 = make_float2(w.z, w.w);
+    if constexpr (kStrict) {
+        a0 = __fadd2_rn(a0, __fmul2_rn(x0, w0));
+        a1 = __fadd2_rn(a1, __fmul2_rn(x1, w1));
+    } else {
+        a0 = __ffma2_rn(x0, w0, a0);
+        a1 = __ffma2_rn(x1, w1, a1);
+    }
+    acc[0] = a0.x; acc[1] = a0.y; acc[2] = a1.x; acc[3] = a1.y;
+}
+
 // act_apply_strict over N consecutive channels starting at ch0, switch hoisted.
 template <int N>
 __device__ __forceinline__ void act_apply_strict_n(int act, float (&v)[N], int ch0, int c)

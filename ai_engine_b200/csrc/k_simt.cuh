@@ -230,11 +230,15 @@ __global__ void __launch_bounds__(kFfmaThreads) igemm_ffma_kernel(const ConvArgs
             const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 8 + 4]);
             const float4 b = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * 4]);
             const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            const float bv[4] = {b.x, b.y, b.z, b.w};
+            const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
+            // output columns in packed pairs (two-wide FP32 instructions);
+            // every output still accumulates over k in order
 #pragma unroll
-            for (int i = 0; i < 8; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = madd<kStrict>(acc[i][j], av[i], bv[j]);
+            for (int i = 0; i < 8; i++) {
+                const float2 ai = make_float2(av[i], av[i]);
+                madd2<kStrict>(acc[i][0], acc[i][1], ai, b01);
+                madd2<kStrict>(acc[i][2], acc[i][3], ai, b23);
+            }
         }
     }
 
@@ -377,10 +381,7 @@ __global__ void __launch_bounds__(256) pw_dot_tile_kernel(const ConvArgs a)
         for (int o = 0; o < 4; o++) {
             if (o < a.cout) {
                 const float4 w = reinterpret_cast<const float4 *>(ws + o * CIN)[q];
-                acc[o][0] = madd<kStrict>(acc[o][0], v.x, w.x);
-                acc[o][1] = madd<kStrict>(acc[o][1], v.y, w.y);
-                acc[o][2] = madd<kStrict>(acc[o][2], v.z, w.z);
-                acc[o][3] = madd<kStrict>(acc[o][3], v.w, w.w);
+                madd4<kStrict>(acc[o], v, w);
             }
         }
     }
@@ -1102,12 +1103,7 @@ __device__ __forceinline__ void dw_tile_compute(const float4 *halo4, const ConvA
 #pragma unroll
             for (int p = 0; p < PB; p++) {
                 const int kx = j - p * S;
-                if (kx >= 0 && kx < K) {
-                    acc[p][0] = madd<kStrict>(acc[p][0], xv.x, wk[kx].x);
-                    acc[p][1] = madd<kStrict>(acc[p][1], xv.y, wk[kx].y);
-                    acc[p][2] = madd<kStrict>(acc[p][2], xv.z, wk[kx].z);
-                    acc[p][3] = madd<kStrict>(acc[p][3], xv.w, wk[kx].w);
-                }
+                if (kx >= 0 && kx < K) madd4<kStrict>(acc[p], xv, wk[kx]);
             }
         }
     }
@@ -1358,12 +1354,7 @@ __global__ void __launch_bounds__(256, 4) dw_block_kernel(const ConvArgs a, cons
                 // column j feeds tap kx of pixel p when j = p S + kx D
                 const int r = j - p * S;
                 const int kx = r / D;
-                if (r >= 0 && r % D == 0 && kx < K) {
-                    acc[p][0] = madd<kStrict>(acc[p][0], xv.x, wk[kx].x);
-                    acc[p][1] = madd<kStrict>(acc[p][1], xv.y, wk[kx].y);
-                    acc[p][2] = madd<kStrict>(acc[p][2], xv.z, wk[kx].z);
-                    acc[p][3] = madd<kStrict>(acc[p][3], xv.w, wk[kx].w);
-                }
+                if (r >= 0 && r % D == 0 && kx < K) madd4<kStrict>(acc[p], xv, wk[kx]);
             }
         }
     }

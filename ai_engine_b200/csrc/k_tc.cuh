@@ -43,6 +43,10 @@
 //              applies the 128-byte swizzle to absolute shared-memory
 //              addresses, as the TMA wrote them, so a start row that is not
 //              a multiple of 8 reads the right bytes.
+// Concat parts (up to 3): the input is the channel concat of separate
+// views read in place, one A tensor map each; part p owns whole K blocks
+// (its channels padded with zero fill to a multiple of 32), so a K block's
+// copy comes from one part's map at that part's own channel coordinate.
 // B operand (weights [tap][cout][cin_pad]): 3-D map, box (32, bn, 1).
 //
 // Split-K (small M, deep K): units = m_tiles x n_tiles x split.  Each unit
@@ -115,6 +119,7 @@ struct TcArgs {
     uint32_t stages, tmem_cols, b_bytes, igemm;
     uint32_t b_resident, bres_off, res_off, pipes, halo, a_bytes;
     uint32_t flat, bwx, a_box;        // flat mode (see tc_conv_kernel)
+    uint32_t nparts, kb1, kb2;        // concat parts: 1-3 A tensor maps; parts 1 and 2 start at K blocks kb1, kb2
     uint32_t res_patch;               // RES 3 epilogue: residual from per-warp exact-2x patches
     uint64_t units;                   // < 2^31 (checked at launch)
     FastDiv div_ntiles, div_split;    // unit -> (m tile, n tile, split)
@@ -357,7 +362,8 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
 // at run time)
 template <int RES, int ACT, bool FLAT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a)
+    tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a,
+                   const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-align the stage buffers (128-byte swizzle atoms)
@@ -385,6 +391,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 32) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+        if (a.nparts > 1) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA1)) : "memory");
+        if (a.nparts > 2) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA2)) : "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
@@ -457,10 +465,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t k = cur.k;
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
                 const int kc = (int)(kb * kTcBK);
+                // the A copy of K block kbx: its part's tensor map and channel coordinate
+                auto amap = [&](uint32_t kbx, int &ac) -> const CUtensorMap * {
+                    if (a.nparts > 2 && kbx >= a.kb2) {
+                        ac = (int)((kbx - a.kb2) * kTcBK);
+                        return &tmA2;
+                    }
+                    if (a.nparts > 1 && kbx >= a.kb1) {
+                        ac = (int)((kbx - a.kb1) * kTcBK);
+                        return &tmA1;
+                    }
+                    ac = (int)(kbx * kTcBK);
+                    return &tmA;
+                };
+                int ac;
                 if (FLAT) {
                     // stage = K block k: the tile's whole input window, every tap's B
                     const TcOrigin o = tc_origin(a, t.mt);
-                    tma_load_4d(sa, &tmA, &sh.full[s], (int)(k * kTcBK), o.ox0 - a.c.pl, o.oy0 - a.c.pt, o.img);
+                    const CUtensorMap *tm = amap(k, ac);
+                    tma_load_4d(sa, tm, &sh.full[s], ac, o.ox0 - a.c.pl, o.oy0 - a.c.pt, o.img);
                     if (!a.b_resident)
                         for (int tp = 0; tp < a.c.kh * a.c.kw; tp++)
                             tma_load_3d(sb + tp * a.b_bytes, &tmB, &sh.full[s], (int)(k * kTcBK), (int)(t.nt * a.bn),
@@ -469,7 +492,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     // stage = column shift kx (= tap here), K block kb: rows
                     // [ybase, ybase + bh + kh - 1) x the bw columns at xbase + kx
                     const TcOrigin o = tc_origin(a, t.mt);
-                    tma_load_4d(sa, &tmA, &sh.full[s], kc, o.ox0 - a.c.pl + (int)tap, o.oy0 - a.c.pt, o.img);
+                    const CUtensorMap *tm = amap(kb, ac);
+                    tma_load_4d(sa, tm, &sh.full[s], ac, o.ox0 - a.c.pl + (int)tap, o.oy0 - a.c.pt, o.img);
                     if (!a.b_resident)
                         for (int ky = 0; ky < a.c.kh; ky++)
                             tma_load_3d(sb + ky * a.b_bytes, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn),
@@ -479,9 +503,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const int ybase = o.oy0 * a.c.sh - a.c.pt;
                     const int xbase = o.ox0 * a.c.sw - a.c.pl;
                     const int ky = (int)(tap / a.c.kw), kx = (int)(tap - ky * a.c.kw);
-                    tma_load_4d(sa, &tmA, &sh.full[s], kc, xbase + kx * a.c.dil, ybase + ky * a.c.dil, o.img);
+                    const CUtensorMap *tm = amap(kb, ac);
+                    tma_load_4d(sa, tm, &sh.full[s], ac, xbase + kx * a.c.dil, ybase + ky * a.c.dil, o.img);
                 } else {
-                    tma_load_2d(sa, &tmA, &sh.full[s], kc, (int)(t.mt * kTcBM));
+                    const CUtensorMap *tm = amap(kb, ac);
+                    tma_load_2d(sa, tm, &sh.full[s], ac, (int)(t.mt * kTcBM));
                 }
                 if (!a.b_resident && !a.halo && !FLAT)
                     tma_load_3d(sb, &tmB, &sh.full[s], kc, (int)(t.nt * a.bn), (int)tap);
@@ -1139,46 +1165,77 @@ static int tc_sm_count()
     return n;
 }
 
+// Concat parts of a tensor-core conv's input (see tc_conv_kernel): part p is
+// the channel view x[p] (pixel stride stride[p], first channel coff[p]) of
+// c[p] channels, starting at K block kb0[p].
+struct TcParts {
+    int n = 0;
+    const float *x[3] = {nullptr, nullptr, nullptr};
+    long long stride[3] = {0, 0, 0};
+    int coff[3] = {0, 0, 0};
+    uint32_t c[3] = {0, 0, 0};
+    uint32_t kb0[3] = {0, 0, 0};
+};
+
 static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace, cudaStream_t stream, char *err,
-                            size_t errlen)
+                            size_t errlen, const TcParts *parts = nullptr)
 {
     PFN_encodeTiled enc = tc_encoder();
     if (!enc) {
         snprintf(err, errlen, "cuTensorMapEncodeTiled unavailable");
         return -4;
     }
-    const uintptr_t abase = (uintptr_t)(c.x + c.x_coff);
-    if (abase % 16 || (c.x_stride * 4) % 16 || (uintptr_t)c.w % 16) {
-        snprintf(err, errlen, "TMA operands must be 16-byte aligned (input + channel offset, pixel stride, weights)");
+    if ((uintptr_t)c.w % 16) {
+        snprintf(err, errlen, "TMA operands must be 16-byte aligned (weights)");
         return -5;
     }
-    CUtensorMap tmA, tmB;
-    CUresult r;
-    if (g.igemm) {
-        const cuuint64_t dims[4] = {(cuuint64_t)c.cin, (cuuint64_t)c.iw, (cuuint64_t)c.ih, (cuuint64_t)c.n};
-        const cuuint64_t strides[3] = {(cuuint64_t)c.x_stride * 4, (cuuint64_t)c.x_stride * 4 * c.iw,
-                                       (cuuint64_t)c.x_stride * 4 * c.iw * c.ih};
-        const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.flat ? g.bwx : g.bw * (cuuint32_t)c.sw,
-                                   g.flat ? g.bhx : g.halo ? g.bh + (cuuint32_t)c.kh - 1 : g.bh * (cuuint32_t)c.sh, 1};
-        const cuuint32_t estr[4] = {1, (cuuint32_t)c.sw, (cuuint32_t)c.sh, 1};
-        r = enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)abase, dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    } else {
-        const cuuint64_t dims[2] = {(cuuint64_t)c.cin, (cuuint64_t)c.M};
-        const cuuint64_t strides[1] = {(cuuint64_t)c.x_stride * 4};
-        const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
-        const cuuint32_t estr[2] = {1, 1};
-        r = enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)abase, dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    // one A map per concat part (a plain conv is one part: its input view)
+    TcParts one;
+    if (!parts) {
+        one.n = 1;
+        one.x[0] = c.x;
+        one.stride[0] = c.x_stride;
+        one.coff[0] = c.x_coff;
+        one.c[0] = (uint32_t)c.cin;
+        parts = &one;
     }
+    CUtensorMap tmAp[3], tmB;
+    CUresult r = CUDA_SUCCESS;
+    for (int pi = 0; pi < parts->n && r == CUDA_SUCCESS; pi++) {
+        const uintptr_t abase = (uintptr_t)(parts->x[pi] + parts->coff[pi]);
+        const long long xs = parts->stride[pi];
+        if (abase % 16 || (xs * 4) % 16) {
+            snprintf(err, errlen, "TMA operands must be 16-byte aligned (input part %d + channel offset, pixel stride)", pi);
+            return -5;
+        }
+        if (g.igemm) {
+            const cuuint64_t dims[4] = {(cuuint64_t)parts->c[pi], (cuuint64_t)c.iw, (cuuint64_t)c.ih, (cuuint64_t)c.n};
+            const cuuint64_t strides[3] = {(cuuint64_t)xs * 4, (cuuint64_t)xs * 4 * c.iw, (cuuint64_t)xs * 4 * c.iw * c.ih};
+            const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.flat ? g.bwx : g.bw * (cuuint32_t)c.sw,
+                                       g.flat ? g.bhx : g.halo ? g.bh + (cuuint32_t)c.kh - 1 : g.bh * (cuuint32_t)c.sh, 1};
+            const cuuint32_t estr[4] = {1, (cuuint32_t)c.sw, (cuuint32_t)c.sh, 1};
+            r = enc(&tmAp[pi], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)abase, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        } else {
+            const cuuint64_t dims[2] = {(cuuint64_t)parts->c[pi], (cuuint64_t)c.M};
+            const cuuint64_t strides[1] = {(cuuint64_t)xs * 4};
+            const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+            const cuuint32_t estr[2] = {1, 1};
+            r = enc(&tmAp[pi], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)abase, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        }
+    }
+    for (int pi = parts->n; pi < 3; pi++) tmAp[pi] = tmAp[0];  // unused
     if (r != CUDA_SUCCESS) {
         snprintf(err, errlen, "cuTensorMapEncodeTiled(A) failed: %d", (int)r);
         return -4;
     }
     {
-        const uint32_t cin_pad = (c.cin + 3) / 4 * 4;
+        // weights [tap][cout][kpad]: kpad = cin rounded up to 4, or with
+        // parts every part's channels rounded up to whole K blocks
+        const uint32_t cin_pad = parts != &one ? g.kblocks * kTcBK : (c.cin + 3) / 4 * 4;
         const cuuint64_t dims[3] = {(cuuint64_t)cin_pad, (cuuint64_t)c.cout, (cuuint64_t)(c.kh * c.kw)};
         const cuuint64_t strides[2] = {(cuuint64_t)cin_pad * 4, (cuuint64_t)cin_pad * 4 * c.cout};
         const cuuint32_t box[3] = {(cuuint32_t)kTcBK, g.bn, 1};
@@ -1200,6 +1257,9 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
     a.halo = g.halo; a.a_bytes = g.a_bytes;
     a.flat = g.flat; a.bwx = g.bwx; a.a_box = g.a_box;
+    a.nparts = (uint32_t)parts->n;
+    a.kb1 = parts->kb0[1];
+    a.kb2 = parts->kb0[2];
     // patches need 16-byte residual rows (the plan checked the shapes)
     a.res_patch = (g.res_patch && c.res && c.res_mode && c.vec_y) ? 1u : 0u;
     if (g.units >= (1ull << 31) || (uint64_t)g.m_tiles * g.n_tiles * g.split >= (1ull << 31)) {
@@ -1236,7 +1296,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     // inlined switch over every kind per chunk costs instruction-cache misses)
     // flat mode is its own instantiation, so the other layers' kernels
     // carry none of its code (1x1 GEMMs measured 25% slower with it inline)
-    using Kern = void (*)(CUtensorMap, CUtensorMap, TcArgs);
+    using Kern = void (*)(CUtensorMap, CUtensorMap, TcArgs, CUtensorMap, CUtensorMap);
     static const Kern kerns[4][3] = {
         {tc_conv_kernel<0, kNone, false>, tc_conv_kernel<0, kRelu, false>, tc_conv_kernel<0, -1, false>},
         {tc_conv_kernel<1, kNone, false>, tc_conv_kernel<1, kRelu, false>, tc_conv_kernel<1, -1, false>},
@@ -1260,7 +1320,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         }
     }
     const unsigned grid = (unsigned)std::min<uint64_t>(g.units, (uint64_t)tc_sm_count());
-    kern<<<grid, kTcThreads, g.smem_bytes, stream>>>(tmA, tmB, a);
+    kern<<<grid, kTcThreads, g.smem_bytes, stream>>>(tmAp[0], tmB, a, tmAp[1], tmAp[2]);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(err, errlen, "tc_conv_kernel launch: %s", cudaGetErrorString(e));

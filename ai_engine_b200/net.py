@@ -35,7 +35,8 @@ import numpy as np
 import torch
 
 from . import elementwise as ew
-from .conv import Conv2d, ConvPlan, View, resize_bilinear
+from ._lib import AieError
+from .conv import Conv2d, ConvPlan, View, resize_bilinear, run_parts
 
 
 @dataclass
@@ -150,6 +151,13 @@ class NetModel:
                 if c % 4 and users and all(u.kind == "conv" and u.ins[0] == nd.out for u in users) \
                         and nd.out not in self.outputs:
                     self.cpad[nd.out] = _pad4(c)
+        # Concat-into-conv: a concat whose only consumer is one tensor-core
+        # conv, with every part a 16-byte aligned view (pixel stride and
+        # first channel multiples of 4), is not materialised: the conv reads
+        # the parts in place (aie_conv_run_parts), as ai-gpu's implicit GEMM
+        # reads its SrcView parts (crates/ai-gpu/src/kernels/conv_igemm.rs:49-76).
+        # The other concats are written by one aie_concat pass.
+        self.fused_concat: Dict[str, Tuple[str, ...]] = {}  # concat name -> its parts
         self.alias: Dict[str, Tuple[str, int, int]] = {}  # split output -> (base tensor, coff, c)
         self.bufs: Dict[str, torch.Tensor] = {}
         self.recs: List[_Rec] = []
@@ -162,8 +170,13 @@ class NetModel:
 
             for name in inputs:
                 alloc(name, zero=name in self.states)
+            concat_nodes = {nd.out: nd for nd in self.nodes if nd.kind == "concat"}
             for nd in self.nodes:
                 rec = _Rec(nd)
+                if nd.kind == "concat" and self._fusable_concat(nd, consumers, math):
+                    self.fused_concat[nd.out] = tuple(nd.ins)
+                    self.recs.append(rec)  # kept in the node list, issued by its conv
+                    continue
                 if nd.kind in ("split", "view"):
                     base, coff = self._base(nd.ins[0])
                     if nd.kind == "view":
@@ -175,6 +188,21 @@ class NetModel:
                     self.recs.append(rec)
                     continue
                 alloc(nd.out, zero=nd.out in self.cpad)
+                if nd.kind == "conv" and nd.ins[0] in self.fused_concat:
+                    h, w, c = self.shapes[nd.ins[0]]
+                    parts = [self.shapes[pn][2] for pn in self.fused_concat[nd.ins[0]]]
+                    try:
+                        rec.plan = ConvPlan(nd.conv, n, h, w, has_res=nd.res is not None, math=math, parts=parts,
+                                            device=dev).load_weights(*weights[nd.out])
+                    except AieError:
+                        # not a tensor-core conv after all: materialise the concat
+                        cn = concat_nodes[nd.ins[0]]
+                        del self.fused_concat[cn.out]
+                        alloc(cn.out)
+                        rec.plan = None
+                    if rec.plan is not None:
+                        self.recs.append(rec)
+                        continue
                 if nd.kind == "conv":
                     src = nd.ins[0]
                     h, w, c = self.shapes[src]
@@ -200,6 +228,21 @@ class NetModel:
         self.step_index = 0
         self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
 
+    def _fusable_concat(self, nd: Node, consumers, math: str) -> bool:
+        users = consumers.get(nd.out, [])
+        if math not in ("auto", "tf32") or len(nd.ins) > 3 or nd.out in self.outputs or nd.out in self.states.values():
+            return False
+        if len(users) != 1 or users[0].kind != "conv" or users[0].ins[0] != nd.out or users[0].conv.groups != 1:
+            return False
+        for pn in nd.ins:
+            if pn in self.fused_concat:
+                return False
+            base, coff = self._base(pn)
+            stride = self.shapes[base][2] if base not in self.cpad else self.cpad[base]
+            if base in self.fused_concat or stride % 4 or coff % 4:
+                return False
+        return True
+
     # -- tensors -----------------------------------------------------------------
     def _base(self, name: str) -> Tuple[str, int]:
         if name in self.alias:
@@ -214,7 +257,10 @@ class NetModel:
         return ew.ChView(self.bufs[name], 0, self.shapes[name][2])
 
     def tensor(self, name: str) -> torch.Tensor:
-        """The logical [n, h, w, c] tensor (a copy if it is a view or padded)."""
+        """The logical [n, h, w, c] tensor (a copy if it is a view or padded;
+        a concat read in place by its conv is assembled from its parts)."""
+        if name in self.fused_concat:
+            return torch.cat([self.tensor(p) for p in self.fused_concat[name]], dim=-1)
         v = self.view(name)
         if v.coff == 0 and v.c == v.t.shape[-1]:
             return v.t
@@ -233,7 +279,14 @@ class NetModel:
             k = nd.kind
             if k in ("split", "view"):
                 continue
-            if k == "conv":
+            if k == "conv" and nd.ins[0] in self.fused_concat:
+                parts = []
+                for pn in self.fused_concat[nd.ins[0]]:
+                    base, coff = self._base(pn)
+                    parts.append((self.bufs[base], coff))
+                run_parts(r.plan, parts, res=None if nd.res is None else self.bufs[nd.res], out=self.bufs[nd.out],
+                          stream=stream)
+            elif k == "conv":
                 base, _ = self._base(nd.ins[0])
                 r.plan(self.bufs[base], res=None if nd.res is None else self.bufs[nd.res], out=self.bufs[nd.out],
                        stream=stream)
@@ -259,7 +312,7 @@ class NetModel:
             elif k == "resize":
                 resize_bilinear(self.tensor_for_resize(nd.ins[0]), nd.size[0], nd.size[1], out=self.bufs[nd.out],
                                 stream=stream)
-            elif k == "concat":
+            elif k == "concat" and nd.out not in self.fused_concat:
                 ew.concat([self.view(p) for p in nd.ins], ew.ChView(self.bufs[nd.out]), stream=stream)
             elif k == "chcopy":
                 coff, c = nd.parts

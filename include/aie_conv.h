@@ -31,6 +31,9 @@
  *   aie_concat,            (crates/ai-core/src/format/model.rs:111-214),
  *   aie_channel_copy       in ai-cpu's rounding (crates/ai-cpu/src/kernels/
  *                          elementwise.rs, segate.rs).
+ *   aie_conv_plan_parts, aie_conv_run_parts
+ *                          ConvIgemmSpec's concat parts (conv_igemm.rs:49-76)
+ *                          read in place by the GEMM.
  *   aie_conv_run_dw_pw(_up2), aie_conv_run_mbconv, aie_conv_run_stem_pw
  *                          two or three consecutive dispatches of a lowered
  *                          graph as one launch (see each declaration).
@@ -386,6 +389,28 @@ AIE_API int aie_channel_copy(uint32_t n, uint32_t px, uint32_t c, aie_tview in, 
  * lanes are written as zero (a buffer padded to a multiple of 4 channels). */
 AIE_API int aie_concat(uint32_t n, uint32_t px, uint32_t nparts, const aie_tview *parts, const uint32_t *part_c,
                        uint32_t out_c, aie_tview out, void *stream);
+
+/* ---- Concat-into-conv.  A conv whose input is the channel concat of up to
+ * three separate views, read in place by the tensor-core GEMM: ai-gpu's
+ * implicit-GEMM conv with concat parts (ConvIgemmSpec srcs, crates/ai-gpu/
+ * src/kernels/conv_igemm.rs:49-76; SrcView, crates/ai-gpu/src/kernels/
+ * common/source.rs:17-80; the Conv op's srcs, crates/ai-core/src/format/
+ * model.rs:83-86), so the concatenated tensor is never written.
+ *
+ * aie_conv_plan_parts: desc describes the conv over the concatenated input
+ * (cin = the sum of part_c[0..nparts), layout NHWC, no input view, math
+ * AUTO or TF32, not depthwise); weights are packed from the ordinary OIHW /
+ * .sw forms by aie_conv_pack_weights.  Returns AIE_E_UNSUPPORTED when the
+ * conv does not run on the tensor cores (a 1x1 with cout <= 4, strides
+ * above 2): concat first and use aie_conv_plan.
+ * aie_conv_run_parts: parts[i] is part i's view (its data, pixel stride and
+ * first channel; stride 0 = dense), 16-byte aligned with a pixel stride
+ * that is a multiple of 4 channels (TMA); otherwise AIE_E_ALIGN.  The other
+ * arguments are aie_conv_run's.  A parts plan is refused by aie_conv_run
+ * and an ordinary plan by aie_conv_run_parts. */
+AIE_API int aie_conv_plan_parts(const aie_conv_desc *desc, uint32_t nparts, const uint32_t *part_c, aie_plan **out);
+AIE_API int aie_conv_run_parts(const aie_plan *plan, const aie_tview *parts, const void *dev_w, const void *dev_b,
+                               const void *res, void *out, void *workspace, void *stream);
 
 /* Human-readable status, and the detail message of this thread's last
  * failure (copied into buf, NUL-terminated; returns its full length). */

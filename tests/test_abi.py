@@ -182,6 +182,45 @@ def test_input_u8_argument_checks(lib):
     assert lib.aie_input_u8(1, 2, 2, 3, p, 1, C.c_void_p(20), None) == -5  # C4 output must be 16-byte aligned
 
 
+def test_concat_parts_plan_checks(lib):
+    """aie_conv_plan_parts validates on the host: 1-3 parts summing to cin,
+    a dense non-grouped conv on the tensor cores; a parts plan is refused by
+    aie_conv_run and an ordinary plan by aie_conv_run_parts (both before any
+    CUDA call)."""
+    def desc(cin, cout, k, groups=1, math=0):
+        d = _lib.ConvDesc()
+        d.n, d.ih, d.iw, d.cin, d.cout, d.kh, d.kw, d.sh, d.sw = 2, 12, 20, cin, cout, k, k, 1, 1
+        for i in range(4):
+            d.pad[i] = k // 2
+        d.dil, d.groups, d.act, d.math = 1, groups, 1, math
+        return d
+    h = C.c_void_p()
+    pc = (C.c_uint32 * 3)(40, 24, 3)
+    assert lib.aie_conv_plan_parts(C.byref(desc(67, 32, 3)), 3, pc, C.byref(h)) == 0
+    info = _lib.PlanInfo()
+    assert lib.aie_conv_plan_info(h, C.byref(info)) == 0
+    assert info.math == _lib.MATH_TF32 and info.kernel == _lib.KERNEL_IGEMM
+    # weights: [9 taps][32 cout][(2 + 1 + 1) K blocks x 32]
+    assert info.weight_bytes == 9 * 32 * 4 * 32 * 4
+    p = C.c_void_p(16)
+    tv = (_lib.TView * 3)()
+    assert lib.aie_conv_run(h, p, p, p, None, p, None, None) == -2
+    lib.aie_plan_free(h)
+    bad = [(desc(66, 32, 3), 3, (40, 24, 3), -2),       # parts sum to 67, not 66
+           (desc(67, 32, 3), 0, (40, 24, 3), -2),       # no parts
+           (desc(67, 32, 3), 4, (40, 24, 3), -2),       # more than 3
+           (desc(64, 64, 3, groups=64), 2, (32, 32, 0), -3),  # depthwise
+           (desc(64, 2, 1), 2, (32, 32, 0), -3),        # 1x1 with cout <= 4: the dot kernel
+           (desc(64, 32, 3, math=1), 2, (32, 32, 0), -3)]     # FFMA
+    for d, n, parts, want in bad:
+        pcs = (C.c_uint32 * 4)(*parts, 0)
+        assert lib.aie_conv_plan_parts(C.byref(d), n, pcs, C.byref(h)) == want, (n, parts, want)
+        assert _lib.last_error()
+    assert lib.aie_conv_plan(C.byref(desc(64, 32, 3)), C.byref(h)) == 0
+    assert lib.aie_conv_run_parts(h, tv, p, p, None, p, None, None) == -2
+    lib.aie_plan_free(h)
+
+
 def test_input_yuv420_argument_checks(lib):
     p = 16
     def desc(**kw):
