@@ -140,20 +140,26 @@ __device__ __forceinline__ float madd(float acc, float a, float b)
     else return fmaf(a, b, acc);
 }
 
-// madd on one packed pair (a0, a1) += (x0, x1) * (w0, w1), see madd4
+// madd on one pair (a0, a1) += (x0, x1) * (w0, w1), see madd4
 template <bool kStrict>
 __device__ __forceinline__ void madd2(float &a0, float &a1, const float2 &x, const float2 &w)
 {
-    float2 a = make_float2(a0, a1);
-    if constexpr (kStrict) a = __fadd2_rn(a, __fmul2_rn(x, w));
-    else a = __ffma2_rn(x, w, a);
-    a0 = a.x;
-    a1 = a.y;
+    if constexpr (kStrict) {
+        // separate scalar roundings (the packed multiply and add measured
+        // not bit-identical to them)
+        a0 = __fadd_rn(a0, __fmul_rn(x.x, w.x));
+        a1 = __fadd_rn(a1, __fmul_rn(x.y, w.y));
+    } else {
+        const float2 a = __ffma2_rn(x, w, make_float2(a0, a1));
+        a0 = a.x;
+        a1 = a.y;
+    }
 }
 
-// madd over four channels as two packed pairs: sm_100's two-wide FP32
-// instructions do one pair per instruction, each lane rounded exactly as the
-// scalar form (fused, or multiply then add in ai-cpu's order).
+// madd over four channels: the fused form as two packed pairs (sm_100's
+// two-wide FP32 FMA, one instruction per pair, each lane rounded exactly as
+// fmaf); the strict form as separate scalar multiplies and adds in ai-cpu's
+// order.
 template <bool kStrict>
 __device__ __forceinline__ void madd4(float (&acc)[4], const float4 &x, const float4 &w)
 {
@@ -161,8 +167,11 @@ __device__ __forceinline__ void madd4(float (&acc)[4], const float4 &x, const fl
     const float2 x0 = make_float2(x.x, x.y), x1 = make_float2(x.z, x.w);
     const float2 w0 = make_float2(w.x, w.y), w1 = make_float2(w.z, w.w);
     if constexpr (kStrict) {
-        a0 = __fadd2_rn(a0, __fmul2_rn(x0, w0));
-        a1 = __fadd2_rn(a1, __fmul2_rn(x1, w1));
+        acc[0] = __fadd_rn(acc[0], __fmul_rn(x.x, w.x));
+        acc[1] = __fadd_rn(acc[1], __fmul_rn(x.y, w.y));
+        acc[2] = __fadd_rn(acc[2], __fmul_rn(x.z, w.z));
+        acc[3] = __fadd_rn(acc[3], __fmul_rn(x.w, w.w));
+        return;
     } else {
         a0 = __ffma2_rn(x0, w0, a0);
         a1 = __ffma2_rn(x1, w1, a1);
