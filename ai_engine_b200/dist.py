@@ -34,6 +34,39 @@ def init(backend: str = "nccl", timeout_s: float = 120.0, device: Optional[torch
     dist.init_process_group(backend, **kw)
 
 
+def gpu_local_cpus(device_index: int, nvml=None) -> Optional[list]:
+    """The host CPUs NVML reports as closest to GPU `device_index` (its
+    NUMA node's cores), or None when NVML cannot tell.  `nvml` is the
+    pynvml module (a stand-in in tests)."""
+    try:
+        if nvml is None:
+            import pynvml as nvml
+        nvml.nvmlInit()
+        h = nvml.nvmlDeviceGetHandleByIndex(device_index)
+        words = (os.cpu_count() + 63) // 64
+        mask = nvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = [64 * i + b for i, wd in enumerate(mask) for b in range(64) if (int(wd) >> b) & 1]
+        return [c for c in cpus if c < os.cpu_count()] or None
+    except Exception:
+        return None
+
+
+def bind_to_gpu_numa(device_index: int, nvml=None) -> Optional[list]:
+    """Pin this process to the CPUs local to its GPU before it allocates
+    pinned host buffers, so their pages are placed on the GPU's NUMA node
+    (first touch) and each rank's host<->device copies use its own socket's
+    memory.  With one process per GPU on a two-socket host, unbound ranks
+    place every rank's staging buffers wherever the scheduler ran them.
+    Returns the CPU list, or None (nothing changed) when it is unknown."""
+    cpus = gpu_local_cpus(device_index, nvml)
+    if cpus:
+        try:
+            os.sched_setaffinity(0, cpus)
+        except OSError:
+            return None
+    return cpus
+
+
 def shard_range(n_total: int, rank: int, world: int) -> Tuple[int, int]:
     """Contiguous [start, end) slice of n_total frames for `rank`; the first
     n_total % world ranks take one extra frame."""

@@ -761,6 +761,10 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        # each rank's pinned host buffers on its GPU's NUMA node
+        from ai_engine_b200.dist import bind_to_gpu_numa
+        bind_to_gpu_numa(local)
+    if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if args.workload == "rvm":

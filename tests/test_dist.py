@@ -62,3 +62,34 @@ def test_gather_and_max_over_two_ranks(n_total):
     assert res[0][0] == 2.0 and res[1][0] == 2.0
     assert res[0][1] == [float(i) for i in range(n_total)]
     assert res[1][1] is None
+
+
+class _FakeNvml:
+    """NVML stand-in: GPU i's local CPUs are the bits of a fixed mask."""
+
+    def __init__(self, masks):
+        self.masks = masks
+
+    def nvmlInit(self):
+        pass
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return i
+
+    def nvmlDeviceGetCpuAffinity(self, h, words):
+        return self.masks[h][:words]
+
+
+def test_gpu_local_cpus_from_nvml_mask():
+    import os
+    from ai_engine_b200.dist import gpu_local_cpus
+    n = os.cpu_count()
+    words = (n + 63) // 64
+    lo = [(1 << min(n, 2)) - 1] + [0] * (words - 1)   # CPUs 0, 1
+    assert gpu_local_cpus(0, _FakeNvml([lo])) == list(range(min(n, 2)))
+    assert gpu_local_cpus(0, _FakeNvml([[0] * words])) is None   # empty mask: unknown
+
+    class Broken(_FakeNvml):
+        def nvmlInit(self):
+            raise RuntimeError("no NVML")
+    assert gpu_local_cpus(0, Broken([lo])) is None
