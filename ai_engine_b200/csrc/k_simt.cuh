@@ -1021,8 +1021,41 @@ struct PwHead {
 // clamp(k-1), clamp(k) (with row weights 0.25 / 0.75 swapped), and columns
 // likewise, so one thread takes a 2 x 2 block of halo pixels for one channel
 // group: four corner loads, the resize's top / bot rows for its two columns,
-// then each pixel's mix -- every product and sum rounded on its own, in the
-// resize kernels' order.  The caller synchronises afterwards.
+// then each pixel's mix: each lerp is a multiply and a fused multiply-add,
+// the final mix two fused multiply-adds into the halo value, two channels
+// per packed instruction (the head runs on the fused FFMA path; its bar is
+// the FFMA tolerance, not the separate resize kernel's bits).  A tile whose
+// halo starts on an odd row and column (pairs aligned with the halo: one
+// pixel of padding, stride 1), lies inside the frame and samples no clamped
+// source row or column mixes every pair without per-pixel range checks or
+// clamps (with 8 x 16 tiles: every tile away from the frame's edge, 62% of
+// them at 80 x 144).  Edge tiles keep the checks: replicating the patch's
+// edge and re-zeroing the padding instead measured 4% slower.  The caller
+// synchronises afterwards.
+struct Up2Mix {  // a 4-channel value as two packed pairs
+    float2 lo, hi;
+};
+
+__device__ __forceinline__ Up2Mix up2_split(const float4 v) { return {make_float2(v.x, v.y), make_float2(v.z, v.w)}; }
+
+// p (1 - w) + q w, w in {0.25, 0.75}
+__device__ __forceinline__ Up2Mix up2_lerp(const float4 p, const float4 q, float w1, float w)
+{
+    const float2 ww1 = make_float2(w1, w1), ww = make_float2(w, w);
+    const Up2Mix pp = up2_split(p), qq = up2_split(q);
+    return {__ffma2_rn(qq.lo, ww, __fmul2_rn(pp.lo, ww1)), __ffma2_rn(qq.hi, ww, __fmul2_rn(pp.hi, ww1))};
+}
+
+// dst += top (1 - w) + bot w
+__device__ __forceinline__ void up2_mix_add(float4 *dst, const Up2Mix &top, const Up2Mix &bot, float w1, float w)
+{
+    const float4 v = *dst;
+    const float2 ww1 = make_float2(w1, w1), ww = make_float2(w, w);
+    const float2 lo = __ffma2_rn(bot.lo, ww, __ffma2_rn(top.lo, ww1, make_float2(v.x, v.y)));
+    const float2 hi = __ffma2_rn(bot.hi, ww, __ffma2_rn(top.hi, ww1, make_float2(v.z, v.w)));
+    *dst = make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
 template <int K, int S, int TW>
 __device__ __forceinline__ void dw_up2_add(float4 *halo4, const float4 *qp, const ConvArgs &a, const DwUp2 &up, int iy0,
                                            int ix0, int qy0, int qx0)
@@ -1037,10 +1070,31 @@ __device__ __forceinline__ void dw_up2_add(float4 *halo4, const float4 *qp, cons
     const int hx_lo = max(0, -ix0), hx_hi = min(HW, a.iw - ix0);
     // first halo row / column of pair 0 (-1 when the halo starts at its second row)
     const int hy_k0 = 2 * ky0 - 1 - iy0, hx_k0 = 2 * kx0 - 1 - ix0;
-    auto lerp = [](float4 p, float4 q, float w1, float w) {  // p (1 - w) + q w, rounded step by step
-        return make_float4(__fadd_rn(__fmul_rn(p.x, w1), __fmul_rn(q.x, w)), __fadd_rn(__fmul_rn(p.y, w1), __fmul_rn(q.y, w)),
-                           __fadd_rn(__fmul_rn(p.z, w1), __fmul_rn(q.z, w)), __fadd_rn(__fmul_rn(p.w, w1), __fmul_rn(q.w, w)));
-    };
+    if constexpr (HH % 2 == 0 && HW % 2 == 0) {
+        if (hy_k0 == 0 && hx_k0 == 0 && hy_lo == 0 && hy_hi == HH && hx_lo == 0 && hx_hi == HW && ky0 >= 1 &&
+            ky0 + HH / 2 <= up.rh && kx0 >= 1 && kx0 + HW / 2 <= up.rw) {
+            // pair (kyi, kxi) covers halo rows 2 kyi, 2 kyi + 1 and columns
+            // 2 kxi, 2 kxi + 1, and samples patch rows kyi, kyi + 1 and
+            // columns kxi, kxi + 1 (the patch starts at source row ky0 - 1
+            // and column kx0 - 1)
+            constexpr int PY = HH / 2, PX = HW / 2;
+            static_assert(PY + 1 <= G::HHQ && PX + 1 <= HWQ, "the pairs' source rows lie in the patch");
+            for (int t = threadIdx.x; t < PY * PX * 8; t += NT) {
+                const int cg = t & 7, pk = t >> 3;
+                const int kyi = pk / PX, kxi = pk - kyi * PX;  // compile-time divisor
+                const float4 *q = qp + (kyi * HWQ + kxi) * 8 + cg;
+                const float4 g00 = q[0], g01 = q[8], g10 = q[HWQ * 8], g11 = q[HWQ * 8 + 8];
+                const Up2Mix top0 = up2_lerp(g00, g01, 0.75f, 0.25f), top1 = up2_lerp(g00, g01, 0.25f, 0.75f);
+                const Up2Mix bot0 = up2_lerp(g10, g11, 0.75f, 0.25f), bot1 = up2_lerp(g10, g11, 0.25f, 0.75f);
+                float4 *h = halo4 + (2 * kyi * HW + 2 * kxi) * 8 + cg;
+                up2_mix_add(h, top0, bot0, 0.75f, 0.25f);
+                up2_mix_add(h + 8, top1, bot1, 0.75f, 0.25f);
+                up2_mix_add(h + HW * 8, top0, bot0, 0.25f, 0.75f);
+                up2_mix_add(h + HW * 8 + 8, top1, bot1, 0.25f, 0.75f);
+            }
+            return;
+        }
+    }
     for (int t = threadIdx.x; t < NKY * NKX * 8; t += NT) {
         const int cg = t & 7, pk = t >> 3;
         const int kyi = pk / NKX, kxi = pk - kyi * NKX;  // compile-time divisor
@@ -1055,18 +1109,13 @@ __device__ __forceinline__ void dw_up2_add(float4 *halo4, const float4 *qp, cons
         const float4 g00 = qp[(r0 * HWQ + c0) * 8 + cg], g01 = qp[(r0 * HWQ + c1) * 8 + cg];
         const float4 g10 = qp[(r1 * HWQ + c0) * 8 + cg], g11 = qp[(r1 * HWQ + c1) * 8 + cg];
         // columns 2j-1 (weight 0.25 on column clamp(j)) and 2j (0.75); rows likewise
-        const float4 top0 = lerp(g00, g01, 0.75f, 0.25f), top1 = lerp(g00, g01, 0.25f, 0.75f);
-        const float4 bot0 = lerp(g10, g11, 0.75f, 0.25f), bot1 = lerp(g10, g11, 0.25f, 0.75f);
+        const Up2Mix top0 = up2_lerp(g00, g01, 0.75f, 0.25f), top1 = up2_lerp(g00, g01, 0.25f, 0.75f);
+        const Up2Mix bot0 = up2_lerp(g10, g11, 0.75f, 0.25f), bot1 = up2_lerp(g10, g11, 0.25f, 0.75f);
         float4 *h = halo4 + (hy0 * HW + hx0) * 8 + cg;
-        auto add = [&](float4 *dst, float4 u) {
-            float4 v = *dst;
-            v.x = __fadd_rn(v.x, u.x); v.y = __fadd_rn(v.y, u.y); v.z = __fadd_rn(v.z, u.z); v.w = __fadd_rn(v.w, u.w);
-            *dst = v;
-        };
-        if (ry0 && rx0) add(h, lerp(top0, bot0, 0.75f, 0.25f));
-        if (ry0 && rx1) add(h + 8, lerp(top1, bot1, 0.75f, 0.25f));
-        if (ry1 && rx0) add(h + HW * 8, lerp(top0, bot0, 0.25f, 0.75f));
-        if (ry1 && rx1) add(h + HW * 8 + 8, lerp(top1, bot1, 0.25f, 0.75f));
+        if (ry0 && rx0) up2_mix_add(h, top0, bot0, 0.75f, 0.25f);
+        if (ry0 && rx1) up2_mix_add(h + 8, top1, bot1, 0.75f, 0.25f);
+        if (ry1 && rx0) up2_mix_add(h + HW * 8, top0, bot0, 0.25f, 0.75f);
+        if (ry1 && rx1) up2_mix_add(h + HW * 8 + 8, top1, bot1, 0.25f, 0.75f);
     }
 }
 
@@ -1108,58 +1157,63 @@ __device__ __forceinline__ void dw_tile_compute(const float4 *halo4, const ConvA
         }
     }
     if constexpr (HEAD) {
-        // partial dots of this lane's 4 channels, reduced over the 8 lanes of
-        // the pixel group: afterwards every lane holds every pixel's sums
-        float tot[PB][4];
+        static_assert(PB == 4, "the head's reduce-scatter spreads 4 pixels over 8 lanes");
+        // partial dots of this lane's 4 channels for each of the group's 4
+        // pixels, then a reduce-scatter over the 8 lanes of the pixel group:
+        // the xor-4 step sums pixels {0, 1} into lanes with bit 2 clear and
+        // {2, 3} into the others, xor-2 halves that again and xor-1 finishes,
+        // so lanes 2p and 2p + 1 hold pixel p's sum (4 shuffles per output
+        // instead of 12 for an all-reduce of every pixel)
+        const bool b2 = (cgi & 4) != 0, b1 = (cgi & 2) != 0;
 #pragma unroll
-        for (int p = 0; p < PB; p++) {
-            epi_act_n<kStrict, 4>(a.act, acc[p], ch, a.cout);
+        for (int p = 0; p < PB; p++) epi_act_n<kStrict, 4>(a.act, acc[p], ch, a.cout);
+        float sum[4];
 #pragma unroll
-            for (int o = 0; o < 4; o++) {
-                tot[p][o] = 0.0f;
-                if (o < hd.cout) {
-                    if (valid) {
-                        const float4 w = __ldg(reinterpret_cast<const float4 *>(hd.w + o * a.cout + ch));
-                        tot[p][o] = fmaf(acc[p][3], w.w, fmaf(acc[p][2], w.z, fmaf(acc[p][1], w.y, acc[p][0] * w.x)));
-                    }
+        for (int o = 0; o < 4; o++) {
+            sum[o] = 0.0f;
+            if (o < hd.cout) {
+                const float4 w = valid ? __ldg(reinterpret_cast<const float4 *>(hd.w + o * a.cout + ch))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                float d[PB];
 #pragma unroll
-                    for (int sh = 1; sh < 8; sh <<= 1) tot[p][o] += __shfl_xor_sync(0xffffffffu, tot[p][o], sh);
-                }
+                for (int p = 0; p < PB; p++)
+                    d[p] = fmaf(acc[p][3], w.w, fmaf(acc[p][2], w.z, fmaf(acc[p][1], w.y, acc[p][0] * w.x)));
+                float k0 = b2 ? d[2] : d[0], k1 = b2 ? d[3] : d[1];
+                k0 += __shfl_xor_sync(0xffffffffu, b2 ? d[0] : d[2], 4);
+                k1 += __shfl_xor_sync(0xffffffffu, b2 ? d[1] : d[3], 4);
+                float k = b1 ? k1 : k0;
+                k += __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
+                k += __shfl_xor_sync(0xffffffffu, k, 1);
+                sum[o] = k;
             }
         }
-        // lane cgi < PB of the group finishes pixel cgi: bias, activation on
+        // the even lane of each pair finishes its pixel: bias, activation on
         // the real outputs only, store (padding lanes of a C4 view are zero)
-        const int ox = ox0 + cgi;
-        if (cgi < PB && oy < a.oh && ox < a.ow) {
+        const int ox = ox0 + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+        if (!(cgi & 1) && oy < a.oh && ox < a.ow) {
             float v[4];
 #pragma unroll
-            for (int o = 0; o < 4; o++) {
-                float t = tot[0][o];
-#pragma unroll
-                for (int q = 1; q < PB; q++)
-                    if (cgi == q) t = tot[q][o];
-                v[o] = o < hd.cout ? act_apply(hd.act, t + __ldg(hd.bias + o)) : 0.0f;
-            }
+            for (int o = 0; o < 4; o++) v[o] = o < hd.cout ? act_apply(hd.act, sum[o] + __ldg(hd.bias + o)) : 0.0f;
             float *yr = hd.y + (((long long)img * a.oh + oy) * a.ow + ox) * hd.y_stride + hd.y_coff;
 #pragma unroll
             for (int o = 0; o < 4; o++)
                 if (o < hd.y_pad_to) yr[o] = v[o];
         }
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int p = 0; p < PB; p++) {
-        const int ox = ox0 + p;
-        if (ox >= a.ow) break;
-        epi_act_n<kStrict, 4>(a.act, acc[p], ch, a.cout);
-        const long long m = ((long long)img * a.oh + oy) * a.ow + ox;
-        if (a.res) {
-            const float4 r = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.r_stride + a.r_coff + ch));
-            acc[p][0] = add_res<kStrict>(acc[p][0], r.x); acc[p][1] = add_res<kStrict>(acc[p][1], r.y);
-            acc[p][2] = add_res<kStrict>(acc[p][2], r.z); acc[p][3] = add_res<kStrict>(acc[p][3], r.w);
+        for (int p = 0; p < PB; p++) {
+            const int ox = ox0 + p;
+            if (ox >= a.ow) break;
+            epi_act_n<kStrict, 4>(a.act, acc[p], ch, a.cout);
+            const long long m = ((long long)img * a.oh + oy) * a.ow + ox;
+            if (a.res) {
+                const float4 r = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.r_stride + a.r_coff + ch));
+                acc[p][0] = add_res<kStrict>(acc[p][0], r.x); acc[p][1] = add_res<kStrict>(acc[p][1], r.y);
+                acc[p][2] = add_res<kStrict>(acc[p][2], r.z); acc[p][3] = add_res<kStrict>(acc[p][3], r.w);
+            }
+            *reinterpret_cast<float4 *>(a.y + m * a.y_stride + a.y_coff + ch) =
+                make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
         }
-        *reinterpret_cast<float4 *>(a.y + m * a.y_stride + a.y_coff + ch) =
-            make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
     }
 }
 
@@ -1167,12 +1221,17 @@ __device__ __forceinline__ void dw_tile_compute(const float4 *halo4, const ConvA
 // (cin, iw, ih, n) tensor map, issued by one thread -- out-of-range pixels and
 // channels read as zeros -- instead of one 16-byte cp.async per chunk with its
 // index arithmetic (the staging was a sixth of the kernel's instructions).
+// The up-sampled head asks for five CTAs per SM (at most 51 registers, a few
+// bytes of spill): a CTA waits for its two TMA boxes with nothing else to
+// do, and the fifth CTA hides more of that wait (head 194.7 -> 186.2 us at
+// 256 frames).
 template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false, bool UP2 = false>
-__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT, UP2 ? 5 : 1)
     dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq, const ConvArgs a,
                    const DwTile g, const PwHead hd, const DwUp2 up)
 {
     static_assert(!UP2 || kTma, "the up-sampled input is staged by TMA");
+    static_assert(!UP2 || !kStrict, "the up-sampled input is mixed with fused multiply-adds");
     using G = DwTileGeom<K, S, TW>;
     constexpr int TH = G::TH, NT = G::NT, HH = G::HH, HW = G::HW;
     extern __shared__ __align__(128) uint8_t dw_smem_raw[];

@@ -629,7 +629,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t ew = (uint32_t)(warp - 1);  // 0..7: staging buffer, bias cache
         const uint32_t grp = ew >> 2;              // accumulator buffer this group drains
         const uint32_t quad = warp & 3;            // TMEM lane quadrant this warp may access
-        const uint32_t row = quad * 32 + lane;     // accumulator row = TMEM lane
         uint8_t *obuf = smem + a.out_off + ew * kTcStageOut;  // 32 x 32 fp32 staging
         // this warp's copy of the n-tile's bias (zero past cout), reloaded
         // only when the n-tile changes; read as broadcasts
