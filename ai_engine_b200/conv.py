@@ -245,20 +245,23 @@ def run_dw_pw(dw: "ConvPlan", pw: "ConvPlan", x: torch.Tensor, out: Optional[tor
     return out
 
 
-def run_mbconv(ex: "ConvPlan", dw: "ConvPlan", pj: "ConvPlan", x: torch.Tensor, res: Optional[torch.Tensor] = None,
-               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+def run_mbconv(ex: "ConvPlan", dw: Optional["ConvPlan"], pj: "ConvPlan", x: torch.Tensor,
+               res: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """An inverted-bottleneck block -- 1x1 expand `ex`, depthwise 3x3 `dw`,
     1x1 project `pj` (+ `res`) -- in one launch (aie_conv_run_mbconv) for
-    frames up to 10 x 18: the expanded tensor never reaches memory.  Raises
+    frames up to 10 x 18: the expanded tensor never reaches memory.  `dw`
+    None: the expand feeds the project directly.  Raises
     AieError(AIE_E_UNSUPPORTED) for blocks the fused kernel does not cover."""
     for p in (ex, dw, pj):
-        if p.w is None:
+        if p is not None and p.w is None:
             raise RuntimeError("load_weights() first")
     if out is None:
         out = torch.empty(pj.out_shape(), dtype=torch.float32, device=x.device)
-    check(ex.lib.aie_conv_run_mbconv(ex._h, dw._h, pj._h, _dptr(x), C.c_void_p(ex.w.data_ptr()),
-                                     C.c_void_p(ex.b.data_ptr()), C.c_void_p(dw.w.data_ptr()),
-                                     C.c_void_p(dw.b.data_ptr()), C.c_void_p(pj.w.data_ptr()),
+    check(ex.lib.aie_conv_run_mbconv(ex._h, dw._h if dw is not None else None, pj._h, _dptr(x),
+                                     C.c_void_p(ex.w.data_ptr()), C.c_void_p(ex.b.data_ptr()),
+                                     C.c_void_p(dw.w.data_ptr() if dw is not None else None),
+                                     C.c_void_p(dw.b.data_ptr() if dw is not None else None),
+                                     C.c_void_p(pj.w.data_ptr()),
                                      C.c_void_p(pj.b.data_ptr()), _dptr(res), _dptr(out),
                                      C.c_void_p(_stream_handle(stream))), "aie_conv_run_mbconv")
     return out

@@ -914,9 +914,9 @@ extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const
                                    const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b,
                                    const void *pj_w, const void *pj_b, const void *res, void *out, void *stream)
 {
-    if (!ex || !dw || !pj || !in || !ex_w || !ex_b || !dw_w || !dw_b || !pj_w || !pj_b || !out)
+    if (!ex || !pj || !in || !ex_w || !ex_b || !pj_w || !pj_b || !out || (dw && (!dw_w || !dw_b)))
         return fail(AIE_E_INVALID, "null argument");
-    const aie_conv_desc &e = ex->d, &d = dw->d, &q = pj->d;
+    const aie_conv_desc &e = ex->d, &q = pj->d;
     auto dense = [](const aie_plan *p) {
         return p->d.layout == AIE_LAYOUT_NHWC && p->x_stride == (long long)p->d.cin && p->x_coff == 0 &&
                p->y_stride == (long long)p->d.cout && p->y_coff == 0;
@@ -924,11 +924,14 @@ extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const
     if (ex->kernel != AIE_KERNEL_PW || ex->math != AIE_MATH_TF32 || e.has_res || !dense(ex) || e.cin % 32)
         return fail(AIE_E_UNSUPPORTED, "fused block: the expand plan must be a dense TF32 1x1 without residual, "
                                        "cin %% 32 == 0");
-    if (dw->kernel != AIE_KERNEL_DW || dw->strict || d.has_res || d.kh != 3 || d.kw != 3 || d.sh != 1 || d.sw != 1 ||
-        d.dil != 1 || d.pad[0] != 1 || d.pad[1] != 1 || d.pad[2] != 1 || d.pad[3] != 1 || d.cin != e.cout ||
-        d.n != e.n || d.ih != e.ih || d.iw != e.iw || !dense(dw))
-        return fail(AIE_E_UNSUPPORTED, "fused block: the depthwise plan must be a dense 3x3, stride 1, pad 1 conv "
-                                       "over the expand output, not FP32_STRICT");
+    if (dw) {
+        const aie_conv_desc &d = dw->d;
+        if (dw->kernel != AIE_KERNEL_DW || dw->strict || d.has_res || d.kh != 3 || d.kw != 3 || d.sh != 1 ||
+            d.sw != 1 || d.dil != 1 || d.pad[0] != 1 || d.pad[1] != 1 || d.pad[2] != 1 || d.pad[3] != 1 ||
+            d.cin != e.cout || d.n != e.n || d.ih != e.ih || d.iw != e.iw || !dense(dw))
+            return fail(AIE_E_UNSUPPORTED, "fused block: the depthwise plan must be a dense 3x3, stride 1, pad 1 "
+                                           "conv over the expand output, not FP32_STRICT");
+    }
     if (pj->kernel != AIE_KERNEL_PW || pj->math != AIE_MATH_TF32 || q.cin != e.cout || q.cout > 128 || q.n != e.n ||
         q.ih != e.ih || q.iw != e.iw || !dense(pj) || (q.has_res && q.res_mode != AIE_RES_TENSOR) ||
         (q.has_res && (pj->r_stride != (long long)q.cout || pj->r_coff != 0)))
@@ -977,12 +980,14 @@ extern "C" int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const
     a.y = (float *)out;
     a.n = (int)e.n; a.h = (int)e.ih; a.w = (int)e.iw;
     a.cin = (int)e.cin; a.cexp = (int)e.cout; a.cout = (int)q.cout; a.cexp_pad4 = (int)rup(e.cout, 4);
-    a.act_exp = e.act; a.act_dw = d.act; a.act_proj = q.act;
+    a.act_exp = e.act; a.act_dw = dw ? dw->d.act : AIE_ACT_NONE; a.act_proj = q.act;
     cudaStream_t s = (cudaStream_t)stream;
     // compile-time activations for the usual ReLU / ReLU6 blocks
-    auto kern = (e.act == AIE_ACT_RELU && d.act == AIE_ACT_RELU)      ? mbconv_kernel<kRelu, kRelu>
-                : (e.act == AIE_ACT_RELU6 && d.act == AIE_ACT_RELU6) ? mbconv_kernel<kRelu6, kRelu6>
-                                                                     : mbconv_kernel<-1, -1>;
+    const int ad = a.act_dw;
+    auto kern = !dw ? (e.act == AIE_ACT_RELU ? mbconv_kernel<kRelu, -1, false> : mbconv_kernel<-1, -1, false>)
+                : (e.act == AIE_ACT_RELU && ad == AIE_ACT_RELU)      ? mbconv_kernel<kRelu, kRelu>
+                : (e.act == AIE_ACT_RELU6 && ad == AIE_ACT_RELU6) ? mbconv_kernel<kRelu6, kRelu6>
+                                                                  : mbconv_kernel<-1, -1>;
     CUDA_TRY(ensure_smem_attr((const void *)kern, (int)kMbSmem));
     const unsigned grid = (unsigned)std::min<long long>(e.n, tc_sm_count());
     kern<<<grid, kMbThreads, kMbSmem, s>>>(tmX, tmWe, tmWp, a);

@@ -121,8 +121,10 @@ __device__ __forceinline__ void tmem_wait_pin18(uint32_t (&r)[kMbRowStride])
 }
 
 // AE, AD: the expand and depthwise activations (kRelu / kRelu6 / kNone, or
-// -1 for any kind at run time)
-template <int AE, int AD>
+// -1 for any kind at run time).  DW = false: no depthwise (a 1x1 expand
+// straight into a 1x1 project): the channel warps store the activated E
+// rows as D.
+template <int AE, int AD, bool DW = true>
 __global__ void __launch_bounds__(kMbThreads, 1)
     mbconv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmWe,
                   const __grid_constant__ CUtensorMap tmWp, const MbArgs a)
@@ -324,88 +326,130 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         bool ok = true;
         for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x, j++) {
             for (int ch = 0; ch < nchunks; ch++, g++) {
-                const int c = ch * kMbChunk + q * 32 + lane;  // expanded channel of this thread
-                const bool cv = c < a.cexp;
-                float wd[9];
+                if constexpr (DW) {
+                    const int c = ch * kMbChunk + q * 32 + lane;  // expanded channel of this thread
+                    const bool cv = c < a.cexp;
+                    float wd[9];
 #pragma unroll
-                for (int t = 0; t < 9; t++) wd[t] = cv ? __ldg(a.w_dw + t * a.cexp_pad4 + c) : 0.0f;
-                const float be = cv ? __ldg(a.b_exp + c) : 0.0f, bd = cv ? __ldg(a.b_dw + c) : 0.0f;
-                // the warp's lanes decide together (the TMEM loads are warp-collective)
-                if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_sleep(&sh.e_full, g & 1))) { ok = false; break; }
-                tc_fence_after();
-                // copy the seven E rows y0 - 1 .. y0 + 5 of this lane's channel
-                // into registers (rows outside the frame are not read), then
-                // release E so the next chunk's expand GEMM can start
-                constexpr int kWin = kMbHalfRows + 2;
-                uint32_t wr[kWin][kMbRowStride];
+                    for (int t = 0; t < 9; t++) wd[t] = cv ? __ldg(a.w_dw + t * a.cexp_pad4 + c) : 0.0f;
+                    const float be = cv ? __ldg(a.b_exp + c) : 0.0f, bd = cv ? __ldg(a.b_dw + c) : 0.0f;
+                    // the warp's lanes decide together (the TMEM loads are warp-collective)
+                    if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_sleep(&sh.e_full, g & 1))) { ok = false; break; }
+                    tc_fence_after();
+                    // copy the seven E rows y0 - 1 .. y0 + 5 of this lane's channel
+                    // into registers (rows outside the frame are not read), then
+                    // release E so the next chunk's expand GEMM can start
+                    constexpr int kWin = kMbHalfRows + 2;
+                    uint32_t wr[kWin][kMbRowStride];
 #pragma unroll
-                for (int r = 0; r < kWin; r++) {
-                    const int row = y0 - 1 + r;
-                    if (row >= 0 && row < a.h) {  // warp-uniform
+                    for (int r = 0; r < kWin; r++) {
+                        const int row = y0 - 1 + r;
+                        if (row >= 0 && row < a.h) {  // warp-uniform
+#pragma unroll
+                            for (int k = 0; k < kMbRowStride / 2; k++)
+                                tmem_ld2(tlane + kMbECol + row * kMbRowStride + 2 * k, wr[r][2 * k], wr[r][2 * k + 1]);
+                        } else {
+#pragma unroll
+                            for (int x = 0; x < kMbRowStride; x++) wr[r][x] = 0u;
+                        }
+                    }
+#pragma unroll
+                    for (int r = 0; r < kWin; r++) tmem_wait_pin18(wr[r]);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.e_empty);
+                    // expand epilogue: bias, activation, zero outside the frame
+                    float win[kWin][kMbRowStride];
+#pragma unroll
+                    for (int r = 0; r < kWin; r++) {
+                        const int row = y0 - 1 + r;
+                        const bool rv = row >= 0 && row < a.h;
+#pragma unroll
+                        for (int x = 0; x < kMbRowStride; x++) win[r][x] = __uint_as_float(wr[r][x]) + be;
+                        act_fixed_n<AE, kMbRowStride>(a.act_exp, win[r]);
+#pragma unroll
+                        for (int x = 0; x < kMbRowStride; x++)
+                            if (!rv || x >= a.w) win[r][x] = 0.0f;
+                    }
+                    // D is free once the previous chunk's project GEMM has read it
+                    if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll
+                    for (int i = 0; i < kMbHalfRows; i++) {
+                        const int y = y0 + i;
+                        const float(&ra)[kMbRowStride] = win[i];
+                        const float(&rb)[kMbRowStride] = win[i + 1];
+                        const float(&rc)[kMbRowStride] = win[i + 2];
+                        // taps in (ky, kx) order from the bias, as the depthwise kernels
+                        float o[kMbRowStride];
+#pragma unroll
+                        for (int x = 0; x < kMbRowStride; x++) {
+                            float acc = bd;
+#pragma unroll
+                            for (int dx = -1; dx <= 1; dx++)
+                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(ra[x + dx], wd[dx + 1], acc);
+#pragma unroll
+                            for (int dx = -1; dx <= 1; dx++)
+                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rb[x + dx], wd[3 + dx + 1], acc);
+#pragma unroll
+                            for (int dx = -1; dx <= 1; dx++)
+                                if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rc[x + dx], wd[6 + dx + 1], acc);
+                            o[x] = acc;
+                        }
+                        act_fixed_n<AD, kMbRowStride>(a.act_dw, o);
+                        // D[p][lane], p = 18 y + x: K-major, 128-byte swizzle
+                        uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
+                        const bool yv = y < a.h;
+                        const int ysw = 2 * y;
+#pragma unroll
+                        for (int x = 0; x < kMbRowStride; x++)
+                            *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ ((ysw + x) & 7)) << 4)) =
+                                (yv && x < a.w) ? o[x] : 0.0f;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.d_full);
+                            } else {
+                    const int c = ch * kMbChunk + q * 32 + lane;  // expanded channel of this thread
+                    const float be = c < a.cexp ? __ldg(a.b_exp + c) : 0.0f;
+                    if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_sleep(&sh.e_full, g & 1))) { ok = false; break; }
+                    tc_fence_after();
+                    // copy this warp's five E rows into registers and release E
+                    // (no halo: D[p] depends on E[p] alone; rows past the frame
+                    // hold the expand of zero fill and feed no stored output)
+                    uint32_t wr[kMbHalfRows][kMbRowStride];
+#pragma unroll
+                    for (int r = 0; r < kMbHalfRows; r++)
 #pragma unroll
                         for (int k = 0; k < kMbRowStride / 2; k++)
-                            tmem_ld2(tlane + kMbECol + row * kMbRowStride + 2 * k, wr[r][2 * k], wr[r][2 * k + 1]);
-                    } else {
+                            tmem_ld2(tlane + kMbECol + (y0 + r) * kMbRowStride + 2 * k, wr[r][2 * k], wr[r][2 * k + 1]);
 #pragma unroll
-                        for (int x = 0; x < kMbRowStride; x++) wr[r][x] = 0u;
+                    for (int r = 0; r < kMbHalfRows; r++) tmem_wait_pin18(wr[r]);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.e_empty);
+                    float v[kMbHalfRows][kMbRowStride];
+#pragma unroll
+                    for (int r = 0; r < kMbHalfRows; r++) {
+#pragma unroll
+                        for (int x = 0; x < kMbRowStride; x++) v[r][x] = __uint_as_float(wr[r][x]) + be;
+                        act_fixed_n<AE, kMbRowStride>(a.act_exp, v[r]);
                     }
-                }
+                    // D is free once the previous chunk's project GEMM has read it
+                    if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
+                    tc_fence_after();
 #pragma unroll
-                for (int r = 0; r < kWin; r++) tmem_wait_pin18(wr[r]);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.e_empty);
-                // expand epilogue: bias, activation, zero outside the frame
-                float win[kWin][kMbRowStride];
+                    for (int r = 0; r < kMbHalfRows; r++) {
+                        const int y = y0 + r;
+                        uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
 #pragma unroll
-                for (int r = 0; r < kWin; r++) {
-                    const int row = y0 - 1 + r;
-                    const bool rv = row >= 0 && row < a.h;
-#pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++) win[r][x] = __uint_as_float(wr[r][x]) + be;
-                    act_fixed_n<AE, kMbRowStride>(a.act_exp, win[r]);
-#pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++)
-                        if (!rv || x >= a.w) win[r][x] = 0.0f;
-                }
-                // D is free once the previous chunk's project GEMM has read it
-                if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
-                tc_fence_after();
-#pragma unroll
-                for (int i = 0; i < kMbHalfRows; i++) {
-                    const int y = y0 + i;
-                    const float(&ra)[kMbRowStride] = win[i];
-                    const float(&rb)[kMbRowStride] = win[i + 1];
-                    const float(&rc)[kMbRowStride] = win[i + 2];
-                    // taps in (ky, kx) order from the bias, as the depthwise kernels
-                    float o[kMbRowStride];
-#pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++) {
-                        float acc = bd;
-#pragma unroll
-                        for (int dx = -1; dx <= 1; dx++)
-                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(ra[x + dx], wd[dx + 1], acc);
-#pragma unroll
-                        for (int dx = -1; dx <= 1; dx++)
-                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rb[x + dx], wd[3 + dx + 1], acc);
-#pragma unroll
-                        for (int dx = -1; dx <= 1; dx++)
-                            if (x + dx >= 0 && x + dx < kMbRowStride) acc = fmaf(rc[x + dx], wd[6 + dx + 1], acc);
-                        o[x] = acc;
+                        for (int x = 0; x < kMbRowStride; x++)
+                            *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ ((2 * y + x) & 7)) << 4)) = v[r][x];
                     }
-                    act_fixed_n<AD, kMbRowStride>(a.act_dw, o);
-                    // D[p][lane], p = 18 y + x: K-major, 128-byte swizzle
-                    uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
-                    const bool yv = y < a.h;
-                    const int ysw = 2 * y;
-#pragma unroll
-                    for (int x = 0; x < kMbRowStride; x++)
-                        *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ ((ysw + x) & 7)) << 4)) =
-                            (yv && x < a.w) ? o[x] : 0.0f;
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.d_full);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.d_full);
             }
             if (!ok) break;
             // ---- project epilogue of frame f: thread = output channel, this warp's rows

@@ -181,6 +181,31 @@ class Model:
                     continue
                 block_of[op[1]] = (eop, dop, op, (ex, dw, pj))
                 block_inner.update((eop[1], dop[1]))
+            # a 1x1 expand read only by a 1x1 project (no depthwise between
+            # them: a wide head conv and the pyramid lateral on it) runs the
+            # same way with the expanded tensor kept on chip
+            for op in self.graph:
+                if op[0] != "conv" or not is_pw(op[3]) or op[3].cout > 128 or op[1] in block_of:
+                    continue
+                if op[1] in tail_up or (op[4] is not None and (op[4] in fused_resize or op[4] in dropped_resize)):
+                    continue  # its residual is an up-sampling folded elsewhere
+                eop = next((p for p in self.graph if p[1] == op[2]), None)
+                if eop is None or eop[0] != "conv" or eop[4] is not None or not is_pw(eop[3]):
+                    continue
+                if eop[1] in block_of or eop[1] in block_inner or eop[1] in head_of:
+                    continue
+                if uses.get(eop[1], 0) != 1 or self.output == eop[1]:
+                    continue
+                h, w, c = self.shapes[eop[2]]
+                if h > 10 or w > 18 or c % 32:
+                    continue
+                ex = ConvPlan(eop[3], n, h, w, math=math, device=self.device).load_weights(*weights[eop[1]])
+                pj = ConvPlan(op[3], n, h, w, has_res=op[4] is not None, math=math,
+                              device=self.device).load_weights(*weights[op[1]])
+                if ex.math != "tf32" or pj.math != "tf32":
+                    continue
+                block_of[op[1]] = (eop, None, op, (ex, None, pj))
+                block_inner.add(eop[1])
         # input_u8: the batch arrives as u8 RGB frames ("input_u8", 3 bytes per
         # pixel); the first op normalises them into the f32 "input" (u8 / 255)
         self.input_u8 = input_u8
@@ -202,7 +227,7 @@ class Model:
                 if out in block_of:
                     eop, dop, pop, plans = block_of[out]
                     rec = OpRecord("mb", out, eop[2], conv=pop[3], res=pop[4], blk=plans,
-                                   members=(eop[1], dop[1], pop[1]))
+                                   members=(eop[1], pop[1]) if dop is None else (eop[1], dop[1], pop[1]))
                     self.bufs[out] = torch.empty((n, *self.shapes[out]), dtype=torch.float32, device=self.device)
                     self.ops.append(rec)
                     continue
@@ -250,7 +275,7 @@ class Model:
         total = 0
         for r in self.ops:
             if r.blk is not None:
-                total += sum(p.flops for p in r.blk)
+                total += sum(p.flops for p in r.blk if p is not None)
             elif r.plan is not None:
                 total += r.plan.flops + (r.head.flops if r.head is not None else 0)
         return total
@@ -267,7 +292,7 @@ class Model:
                 names.update(r.members)
             elif r.kind == "mb":  # the two 1x1 GEMMs; the depthwise between them runs on the CUDA cores
                 ex, _, pj = r.blk
-                names.update(m for m, p in ((r.members[0], ex), (r.members[2], pj)) if p.math == "tf32")
+                names.update(m for m, p in ((r.members[0], ex), (r.members[-1], pj)) if p.math == "tf32")
             elif r.kind == "dwpw" and r.plan.math == "tf32":
                 names.add(r.members[0])
         return names

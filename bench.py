@@ -941,9 +941,13 @@ def main():
             # neither written nor read
             ex, dw, pj = r.blk
             inter = 4 * n * ex.oh * ex.ow * ex.op.cout
-            fl = ex.flops + dw.flops + pj.flops
-            by = ex.min_bytes + dw.min_bytes + pj.min_bytes - 4 * inter
-            kern, math = "ex+dw+pj", "tf32"
+            if dw is None:  # expand straight into project: the wide tensor is neither written nor read
+                fl, by, kern = ex.flops + pj.flops, ex.min_bytes + pj.min_bytes - 2 * inter, "ex+pj"
+            else:
+                fl = ex.flops + dw.flops + pj.flops
+                by = ex.min_bytes + dw.min_bytes + pj.min_bytes - 4 * inter
+                kern = "ex+dw+pj"
+            math = "tf32"
         elif r.kind == "dwpw":
             # fused depthwise + 1x1 head: the intermediate is neither written nor read
             inter = 4 * n * r.plan.oh * r.plan.ow * r.plan.op.cout

@@ -229,9 +229,9 @@ AIE_API int aie_conv_run_dw_pw(const aie_plan *dw, const aie_plan *pw, const voi
  * [n][up_h][up_w][C] tensor (C = the depthwise channels, 16-byte aligned)
  * with 2 up_h, 2 up_w the depthwise input's height and width, and up2 the
  * exact-2x half_pixel bilinear resize (crates/ai-core/src/reference/
- * resize.rs:5-42).  The sum is formed in the kernel's staged input tile,
- * rounded as resize-then-add rounds it, so neither the up-sampled tensor
- * nor the sum reaches memory.  Replaces the tail of a feature pyramid that
+ * resize.rs:5-42).  The sum is formed in the kernel's staged input tile
+ * (the resize's lerps as fused multiply-adds: the FFMA path's rounding), so
+ * neither the up-sampled tensor nor the sum reaches memory.  Replaces the tail of a feature pyramid that
  * the reference dispatches as Resize, Conv(residual = the resize's output),
  * depthwise Conv, 1x1 Conv (ai-gpu-runtime lowering.rs:99-187, one spec per
  * op): `in` is the lateral conv's output computed without its residual.
@@ -250,10 +250,13 @@ AIE_API int aie_conv_run_dw_pw_up2(const aie_plan *dw, const aie_plan *pw, const
  * aie_conv_plan results over dense NHWC tensors: `ex` and `pj` 1x1 plans
  * that resolved to TF32 (cin % 32 == 0, pj cout <= 128), `dw` a non-strict
  * depthwise plan; weights and biases as packed for each plan; `res` is the
- * project plan's residual (NULL without one).  Otherwise AIE_E_UNSUPPORTED:
- * run the three plans with aie_conv_run.  Replaces the three dispatches
- * ai-gpu-runtime's lower_op makes for the block (GemmPwSpec, ConvDwSpec,
- * GemmPwSpec; crates/ai-gpu-runtime/src/lowering.rs:99-187). */
+ * project plan's residual (NULL without one).  `dw` NULL (dw_w, dw_b
+ * ignored): a 1x1 expand straight into a 1x1 project, e.g. a wide head conv
+ * whose only reader is a pyramid lateral -- the wide tensor never reaches
+ * memory either.  Otherwise AIE_E_UNSUPPORTED: run the plans with
+ * aie_conv_run.  Replaces the three (two) dispatches ai-gpu-runtime's
+ * lower_op makes for the block (GemmPwSpec, ConvDwSpec, GemmPwSpec;
+ * crates/ai-gpu-runtime/src/lowering.rs:99-187). */
 AIE_API int aie_conv_run_mbconv(const aie_plan *ex, const aie_plan *dw, const aie_plan *pj, const void *in,
                         const void *ex_w, const void *ex_b, const void *dw_w, const void *dw_b, const void *pj_w,
                         const void *pj_b, const void *res, void *out, void *stream);

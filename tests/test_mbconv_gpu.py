@@ -58,6 +58,37 @@ def test_fused_block_matches_chain(cuda_ok, n, h, w, cin, cexp, cout, res, acts)
     assert np.isfinite(got).all()
 
 
+# (n, h, w, cin, cexp, cout, residual, expand / project activations)
+PAIRS = [
+    (3, 10, 18, 128, 960, 64, False, ("relu", "none")),    # head960 -> fpn.lat16: 7.5 chunks
+    (2, 10, 18, 64, 256, 128, True, ("hardswish", "relu")),
+    (149, 7, 11, 32, 96, 16, False, ("relu", "sigmoid")),  # more frames than SMs, a partial chunk
+]
+
+
+@pytest.mark.parametrize("n,h,w,cin,cexp,cout,res,acts", PAIRS)
+def test_fused_expand_project_matches_chain(cuda_ok, n, h, w, cin, cexp, cout, res, acts):
+    """No depthwise (dw = None): a 1x1 expand read only by a 1x1 project in
+    one launch, the expanded tensor kept on chip."""
+    rng = XorShift32(500 + cexp + h)
+    x = rng.vec_f32(n * h * w * cin).reshape(n, h, w, cin)
+    we, be = rng.vec_f32(cexp * cin), rng.vec_f32(cexp)
+    wp, bp = rng.vec_f32(cout * cexp), rng.vec_f32(cout)
+    eop, pop = Conv2d.pointwise(cin, cexp, acts[0]), Conv2d.pointwise(cexp, cout, acts[1])
+    ex = ConvPlan(eop, n, h, w, math="tf32").load_weights(we, be)
+    pj = ConvPlan(pop, n, h, w, has_res=res, math="tf32").load_weights(wp, bp)
+    r = rng.vec_f32(n * h * w * cout).reshape(n, h, w, cout) if res else None
+    xd = torch.from_numpy(x).cuda()
+    rd = torch.from_numpy(r).cuda() if res else None
+    got = run_mbconv(ex, None, pj, xd, res=rd).cpu().numpy()
+    chain = pj(ex(xd), rd).cpu().numpy()
+    e_o, _ = oracle_conv(eop, x, we, be, None)
+    want, scale = oracle_conv(pop, e_o, wp, bp, r)
+    assert normalised_error(got, chain, scale) <= TOL_TF32
+    assert normalised_error(got, want, scale) <= TOL_TF32
+    assert np.isfinite(got).all()
+
+
 def test_fused_block_rejects_unsupported(cuda_ok):
     """Frames above 10 x 18, cin not a multiple of 32, an FP32_STRICT
     depthwise plan and a missing residual are refused, not run."""
@@ -82,8 +113,9 @@ def test_fused_block_rejects_unsupported(cuda_ok):
 
 def test_model_fuses_the_small_frame_blocks(cuda_ok):
     """The benchmark network runs its five 10x18 inverted-bottleneck blocks
-    (e4.0, e4.1, e5, e5.0, e5.1) as fused launches; the mask equals the
-    network run block by block within the TF32 bar."""
+    (e4.0, e4.1, e5, e5.0, e5.1) and the 960-channel head conv with the
+    pyramid lateral on it (head960 -> fpn.lat16) as fused launches; the mask
+    equals the network run op by op within the TF32 bar."""
     from ai_engine_b200 import segnet
     from ai_engine_b200.graph import Model
     g = segnet.build_graph()
@@ -92,8 +124,8 @@ def test_model_fuses_the_small_frame_blocks(cuda_ok):
     a = Model(g, wts, 2, (segnet.H, segnet.W, 3), fuse_blocks=True)
     b = Model(g, wts, 2, (segnet.H, segnet.W, 3), fuse_blocks=False)
     blocks = [r.out for r in a.ops if r.kind == "mb"]
-    assert blocks == ["e4.0.proj", "e4.1.proj", "e5.proj", "e5.0.proj", "e5.1.proj"]
-    assert len(a.ops) == len(b.ops) - 10
+    assert blocks == ["e4.0.proj", "e4.1.proj", "e5.proj", "e5.0.proj", "e5.1.proj", "fpn.lat16"]
+    assert len(a.ops) == len(b.ops) - 11
     ya, yb = a.infer(x), b.infer(x)
     assert torch.isfinite(ya).all()
     assert (ya - yb).abs().max().item() <= 5e-3

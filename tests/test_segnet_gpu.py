@@ -3,8 +3,9 @@
 bench.py times BASELINE config 4: ``graph.Model`` over the synthetic
 MNv4-style segmentation net at 160x288, 256 frames, math "auto" (TF32
 tensor cores where the operands allow TMA), every default fusion on (stem +
-lateral, the five small-frame inverted-bottleneck blocks, the depthwise +
-1x1 head with the feature-pyramid tail folded in).  This file builds that
+lateral, the five small-frame inverted-bottleneck blocks, the 960-channel
+head conv with the pyramid lateral on it, the depthwise + 1x1 head with the
+feature-pyramid tail folded in).  This file builds that
 same model with bench.py's own weights and rank-0 input, runs one step on
 the GPU, and checks sampled frames of it against the CPU oracle (the C
 restatement of ai-cpu):
@@ -95,7 +96,7 @@ def test_bench_model_is_the_fused_config4_net(cuda_ok, bench_step):
     """The model under test has the launches bench.py times."""
     g, wts, m, x, host = bench_step
     kinds = [r.kind for r in m.ops]
-    assert kinds.count("mb") == 5 and kinds.count("stempw") == 1 and kinds.count("dwpw") == 1
+    assert kinds.count("mb") == 6 and kinds.count("stempw") == 1 and kinds.count("dwpw") == 1
     dwpw = next(r for r in m.ops if r.kind == "dwpw")
     assert dwpw.up is not None, "the feature-pyramid tail is folded into the head"
     assert all(r.plan.math == "tf32" for r in m.ops if r.kind == "conv" and r.plan.kernel in ("pw", "igemm"))
