@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <mutex>
+#include <type_traits>
 #include <utility>
 #include <vector>
 #include <cuda_runtime.h>

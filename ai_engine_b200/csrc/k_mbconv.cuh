@@ -45,6 +45,9 @@
 
 namespace aie {
 
+template <int V>
+using Int = std::integral_constant<int, V>;
+
 constexpr int kMbRowStride = 18;                   // pixels per frame row in the N layout (frame width <= 18)
 constexpr int kMbRows = 10;                        // frame rows (frame height <= 10)
 constexpr int kMbPix = kMbRowStride * kMbRows;     // 180
@@ -322,6 +325,55 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         // is (lane / 4) ^ (p % 8); p = 18 y + x, so p % 8 = (2 y + x) % 8
         const uint32_t lane_off = (uint32_t)((lane & 3) << 2);
         const int lane_chunk = lane >> 2;
+        // this lane's D column in each of the eight swizzle phases (row p % 8),
+        // as shared-memory addresses; a store adds the row's constant offset
+        uint32_t dcol[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) dcol[k] = smem_u32(dk) + lane_off + ((lane_chunk ^ k) << 4);
+        auto st_d = [](uint32_t addr, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory"); };
+        // One chunk without a depthwise (DW = false): this warp's five E rows
+        // (no halo: D[p] depends on E[p] alone; rows past the frame hold the
+        // expand of zero fill and feed no stored output) become D after the
+        // expand bias and activation.  Y0 (the warp's first row, 0 or 5) is
+        // compile-time, so the D stores' swizzled addresses fold into constants.
+        auto pw_chunk = [&](auto Y0, int ch, uint32_t g) -> bool {
+            constexpr int yb = decltype(Y0)::value;
+            const int c = ch * kMbChunk + q * 32 + lane;  // expanded channel of this thread
+            const float be = c < a.cexp ? __ldg(a.b_exp + c) : 0.0f;
+            if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_sleep(&sh.e_full, g & 1))) return false;
+            tc_fence_after();
+            uint32_t wr[kMbHalfRows][kMbRowStride];
+#pragma unroll
+            for (int r = 0; r < kMbHalfRows; r++)
+#pragma unroll
+                for (int k = 0; k < kMbRowStride / 2; k++)
+                    tmem_ld2(tlane + kMbECol + (yb + r) * kMbRowStride + 2 * k, wr[r][2 * k], wr[r][2 * k + 1]);
+#pragma unroll
+            for (int r = 0; r < kMbHalfRows; r++) tmem_wait_pin18(wr[r]);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.e_empty);
+            float v[kMbHalfRows][kMbRowStride];
+#pragma unroll
+            for (int r = 0; r < kMbHalfRows; r++) {
+#pragma unroll
+                for (int x = 0; x < kMbRowStride; x++) v[r][x] = __uint_as_float(wr[r][x]) + be;
+                act_fixed_n<AE, kMbRowStride>(a.act_exp, v[r]);
+            }
+            // D is free once the previous chunk's project GEMM has read it
+            if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int r = 0; r < kMbHalfRows; r++) {
+                const int y = yb + r;
+#pragma unroll
+                for (int x = 0; x < kMbRowStride; x++) st_d(dcol[(2 * y + x) & 7] + (y * kMbRowStride + x) * 128, v[r][x]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.d_full);
+            return true;
+        };
         uint32_t g = 0, j = 0;
         bool ok = true;
         for (int f = blockIdx.x; ok && f < a.n; f += gridDim.x, j++) {
@@ -409,46 +461,9 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sh.d_full);
-                            } else {
-                    const int c = ch * kMbChunk + q * 32 + lane;  // expanded channel of this thread
-                    const float be = c < a.cexp ? __ldg(a.b_exp + c) : 0.0f;
-                    if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_sleep(&sh.e_full, g & 1))) { ok = false; break; }
-                    tc_fence_after();
-                    // copy this warp's five E rows into registers and release E
-                    // (no halo: D[p] depends on E[p] alone; rows past the frame
-                    // hold the expand of zero fill and feed no stored output)
-                    uint32_t wr[kMbHalfRows][kMbRowStride];
-#pragma unroll
-                    for (int r = 0; r < kMbHalfRows; r++)
-#pragma unroll
-                        for (int k = 0; k < kMbRowStride / 2; k++)
-                            tmem_ld2(tlane + kMbECol + (y0 + r) * kMbRowStride + 2 * k, wr[r][2 * k], wr[r][2 * k + 1]);
-#pragma unroll
-                    for (int r = 0; r < kMbHalfRows; r++) tmem_wait_pin18(wr[r]);
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&sh.e_empty);
-                    float v[kMbHalfRows][kMbRowStride];
-#pragma unroll
-                    for (int r = 0; r < kMbHalfRows; r++) {
-#pragma unroll
-                        for (int x = 0; x < kMbRowStride; x++) v[r][x] = __uint_as_float(wr[r][x]) + be;
-                        act_fixed_n<AE, kMbRowStride>(a.act_exp, v[r]);
-                    }
-                    // D is free once the previous chunk's project GEMM has read it
-                    if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
-                    tc_fence_after();
-#pragma unroll
-                    for (int r = 0; r < kMbHalfRows; r++) {
-                        const int y = y0 + r;
-                        uint8_t *drow = dk + y * (kMbRowStride * 128) + lane_off;
-#pragma unroll
-                        for (int x = 0; x < kMbRowStride; x++)
-                            *reinterpret_cast<float *>(drow + x * 128 + ((lane_chunk ^ ((2 * y + x) & 7)) << 4)) = v[r][x];
-                    }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&sh.d_full);
+                } else if (y0 == 0 ? !pw_chunk(Int<0>(), ch, g) : !pw_chunk(Int<kMbHalfRows>(), ch, g)) {
+                    ok = false;
+                    break;
                 }
             }
             if (!ok) break;
