@@ -861,10 +861,11 @@ def main():
 
     # ---- end to end through the public API: every step uploads its pinned
     # host frames and reads its mask back (Model.run_pipelined overlaps the
-    # copies of neighbouring batches with compute).  Headline: u8 RGB camera
-    # frames (3 bytes per pixel, normalised on the GPU by the graph's first
-    # op, as ai_engine's camera pipeline feeds its models); also reported:
-    # the f32-input upload (12 bytes per pixel).
+    # copies of neighbouring batches with compute).  Headline (`e2e`):
+    # config 4's own f32 frames (12 bytes per pixel); also reported
+    # (`e2e_u8`): u8 RGB camera frames (3 bytes per pixel, normalised on the
+    # GPU by the graph's first op, as ai_engine's camera pipeline feeds its
+    # models).
     outs_host = [out_host, torch.empty_like(out_host).pin_memory()]
 
     def time_e2e(m, xh):
