@@ -20,7 +20,7 @@
 // Per chunk of 128 expanded channels (TMEM: E at columns [0, 192), P at
 // [256, 448)):
 //   1. the MMA warp accumulates E over cin from an input ring (two [192][32]
-//      K-blocks) and a weight ring (four [128][32] K-blocks);
+//      K-blocks) and a weight ring (two [128][32] K-blocks);
 //   2. eight channel warps (thread = expanded channel; warp w reads TMEM
 //      lanes 32 (w % 4).. and takes half the frame's rows) copy the seven E
 //      rows their five output rows need into registers and release E at
@@ -28,8 +28,10 @@
 //      depthwise (zero padding at the frame's edges), add its bias and
 //      activation, and write D[p][channel] into shared memory as the project
 //      GEMM's K-major B operand (128-byte swizzle, one 32-channel K-block per
-//      lane quarter);
-//   3. the MMA warp accumulates P over the chunk's four K-blocks.
+//      lane quarter, in a ring of six K-block slots);
+//   3. the MMA warp accumulates P over the chunk's four K-blocks, each as
+//      soon as its two warps have written it; a slot is free again when the
+//      project MMAs that read it complete (per-slot barriers).
 // The MMA warp issues the expand of chunk g + 1 before the project of chunk
 // g, so the next chunk's expand GEMM overlaps this chunk's depthwise on the
 // CUDA cores; the producer loads the weights in that same order.
@@ -56,10 +58,15 @@ constexpr int kMbChunk = 128;                      // expanded channels per chun
 constexpr uint32_t kMbXBytes = kMbN * 128;         // one [192][32] operand K-block: 24 KB
 constexpr uint32_t kMbXBox = kMbPix * 128;         // the bytes a [10][18][32] TMA box writes
 constexpr uint32_t kMbWBytes = kMbChunk * 128;     // one [128][32] weight K-block: 16 KB
-constexpr int kMbXStages = 2, kMbWStages = 4;
+constexpr int kMbXStages = 2, kMbWStages = 2;
+// D K-blocks ([192][32], one per lane quarter) rotate through six slots: the
+// quarter-q block of chunk g takes slot (4 g + q) % 6, so the next chunk's
+// first two quarters write while the project GEMM still reads this chunk's,
+// and its last two wait only for this chunk's first two K-blocks
+constexpr int kMbDSlots = 6;
 constexpr uint32_t kMbWOff = kMbXStages * kMbXBytes;
-constexpr uint32_t kMbDOff = kMbWOff + kMbWStages * kMbWBytes;  // D: 4 K-blocks of [192][32]
-constexpr uint32_t kMbBarOff = kMbDOff + 4 * kMbXBytes;
+constexpr uint32_t kMbDOff = kMbWOff + kMbWStages * kMbWBytes;  // D: kMbDSlots K-blocks of [192][32]
+constexpr uint32_t kMbBarOff = kMbDOff + kMbDSlots * kMbXBytes;
 constexpr uint32_t kMbSmem = kMbBarOff + 256 + 1024;  // + barriers + alignment slack
 constexpr int kMbChanWarps = 8;                     // two per TMEM lane quarter: frame rows 0-4 / 5-9
 constexpr int kMbHalfRows = kMbRows / 2;
@@ -83,7 +90,8 @@ struct MbArgs {
 
 struct MbShared {
     uint64_t xfull[kMbXStages], xempty[kMbXStages], wfull[kMbWStages], wempty[kMbWStages];
-    uint64_t e_full, e_empty, d_full, d_empty, p_full, p_empty, drain;
+    uint64_t d_full[kMbDSlots], d_empty[kMbDSlots];
+    uint64_t e_full, e_empty, p_full, p_empty, drain;
     uint32_t tmem_base;
     uint32_t abort;
 };
@@ -150,8 +158,10 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         }
         mbar_init(&sh.e_full, 1);
         mbar_init(&sh.e_empty, kMbChanWarps);
-        mbar_init(&sh.d_full, kMbChanWarps);
-        mbar_init(&sh.d_empty, 1);
+        for (int s = 0; s < kMbDSlots; s++) {
+            mbar_init(&sh.d_full[s], 2);  // the two warps of a lane quarter
+            mbar_init(&sh.d_empty[s], 1);
+        }
         mbar_init(&sh.p_full, 1);
         mbar_init(&sh.p_empty, kMbChanWarps);
         mbar_init(&sh.drain, 1);
@@ -166,7 +176,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
     // the operand rows past the frame's 180 pixels stay zero: the TMA boxes
     // and the depthwise never write them
     constexpr int kPadFloats = (kMbN - kMbPix) * 32;
-    for (int i = threadIdx.x; i < (kMbXStages + 4) * kPadFloats; i += kMbThreads) {
+    for (int i = threadIdx.x; i < (kMbXStages + kMbDSlots) * kPadFloats; i += kMbThreads) {
         const int blk = i / kPadFloats, e = i - blk * kPadFloats;
         const uint32_t base = blk < kMbXStages ? blk * kMbXBytes : kMbDOff + (blk - kMbXStages) * kMbXBytes;
         reinterpret_cast<float *>(smem + base + kMbXBox)[e] = 0.0f;
@@ -256,23 +266,26 @@ __global__ void __launch_bounds__(kMbThreads, 1)
             };
             // the project GEMM of chunk pg (chunk pch of the CTA's frame pj)
             auto project = [&](uint32_t pg, int pch, uint32_t pj) {
-                // D of that chunk written; P free (first chunk of a frame)
-                if (!mbar_wait(&sh.d_full, pg & 1)) { ok = false; return; }
+                // P free (first chunk of a frame)
                 if (pch == 0 && pj > 0 && !mbar_wait(&sh.p_empty, (pj - 1) & 1)) { ok = false; return; }
-                tc_fence_after();
                 for (int kb = 0; kb < 4; kb++) {
+                    // K-block kb of that chunk's D written (slot use u)
+                    const uint32_t u = 4 * pg + kb, slot = u % kMbDSlots;
                     uint32_t t;
-                    if (*abort_flag || !wstage(t)) { ok = false; return; }
+                    if (*abort_flag || !mbar_wait(&sh.d_full[slot], (u / kMbDSlots) & 1) || !wstage(t)) {
+                        ok = false;
+                        return;
+                    }
                     tc_fence_after();
                     const uint32_t sw = smem_u32(smem + kMbWOff + t * kMbWBytes);
-                    const uint32_t sd = smem_u32(smem + kMbDOff + kb * kMbXBytes);
+                    const uint32_t sd = smem_u32(smem + kMbDOff + slot * kMbXBytes);
 #pragma unroll
                     for (int k = 0; k < 4; k++)
                         mma_tf32(tmem + kMbPCol, smem_desc_sw128(sw) + 2 * k, smem_desc_sw128(sd) + 2 * k, idesc,
                                  (pch > 0 || kb > 0 || k > 0) ? 1u : 0u);
                     mma_commit(&sh.wempty[t]);
+                    mma_commit(&sh.d_empty[slot]);
                 }
-                mma_commit(&sh.d_empty);
                 if (pch == nchunks - 1) mma_commit(&sh.p_full);
             };
             int prev_ch = -1;
@@ -320,7 +333,13 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         const int q = warp & 3;
         const int y0 = ((warp - 2) >> 2) * kMbHalfRows;
         const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
-        uint8_t *dk = smem + kMbDOff + q * kMbXBytes;  // this warp's K-block of D
+        // this warp's K-block of chunk g's D: slot (4 g + q) % kMbDSlots, free once
+        // the project GEMM has read the slot's previous K-block (use u - 1)
+        auto dslot = [&](uint32_t g) { return (4 * g + (uint32_t)q) % kMbDSlots; };
+        auto d_free = [&](uint32_t g) {
+            const uint32_t u = (4 * g + (uint32_t)q) / kMbDSlots;
+            return u == 0 || mbar_wait_sleep(&sh.d_empty[dslot(g)], (u - 1) & 1);
+        };
         // 128-byte swizzle: the 16-byte chunk of this lane's channel in row p
         // is (lane / 4) ^ (p % 8); p = 18 y + x, so p % 8 = (2 y + x) % 8
         const uint32_t lane_off = (uint32_t)((lane & 3) << 2);
@@ -329,7 +348,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         // as shared-memory addresses; a store adds the row's constant offset
         uint32_t dcol[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) dcol[k] = smem_u32(dk) + lane_off + ((lane_chunk ^ k) << 4);
+        for (int k = 0; k < 8; k++) dcol[k] = smem_u32(smem + kMbDOff) + lane_off + ((lane_chunk ^ k) << 4);
         auto st_d = [](uint32_t addr, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory"); };
         // One chunk without a depthwise (DW = false): this warp's five E rows
         // (no halo: D[p] depends on E[p] alone; rows past the frame hold the
@@ -360,18 +379,20 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                 for (int x = 0; x < kMbRowStride; x++) v[r][x] = __uint_as_float(wr[r][x]) + be;
                 act_fixed_n<AE, kMbRowStride>(a.act_exp, v[r]);
             }
-            // D is free once the previous chunk's project GEMM has read it
-            if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) return false;
+            // the D slot is free once the project GEMM has read its previous K-block
+            if (!__all_sync(0xffffffffu, d_free(g))) return false;
             tc_fence_after();
+            const uint32_t soff = dslot(g) * kMbXBytes;
 #pragma unroll
             for (int r = 0; r < kMbHalfRows; r++) {
                 const int y = yb + r;
 #pragma unroll
-                for (int x = 0; x < kMbRowStride; x++) st_d(dcol[(2 * y + x) & 7] + (y * kMbRowStride + x) * 128, v[r][x]);
+                for (int x = 0; x < kMbRowStride; x++)
+                    st_d(dcol[(2 * y + x) & 7] + soff + (y * kMbRowStride + x) * 128, v[r][x]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sh.d_full);
+            if (lane == 0) mbar_arrive(&sh.d_full[dslot(g)]);
             return true;
         };
         uint32_t g = 0, j = 0;
@@ -423,9 +444,10 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                         for (int x = 0; x < kMbRowStride; x++)
                             if (!rv || x >= a.w) win[r][x] = 0.0f;
                     }
-                    // D is free once the previous chunk's project GEMM has read it
-                    if (g > 0 && !__all_sync(0xffffffffu, mbar_wait_sleep(&sh.d_empty, (g - 1) & 1))) { ok = false; break; }
+                    // the D slot is free once the project GEMM has read its previous K-block
+                    if (!__all_sync(0xffffffffu, d_free(g))) { ok = false; break; }
                     tc_fence_after();
+                    uint8_t *dk = smem + kMbDOff + dslot(g) * kMbXBytes;
 #pragma unroll
                     for (int i = 0; i < kMbHalfRows; i++) {
                         const int y = y0 + i;
@@ -460,7 +482,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // D is read by the MMA (async proxy)
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&sh.d_full);
+                    if (lane == 0) mbar_arrive(&sh.d_full[dslot(g)]);
                 } else if (y0 == 0 ? !pw_chunk(Int<0>(), ch, g) : !pw_chunk(Int<kMbHalfRows>(), ch, g)) {
                     ok = false;
                     break;
