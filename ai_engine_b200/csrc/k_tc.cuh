@@ -101,6 +101,7 @@ struct TcGeom {
     uint32_t smem_bytes;
     uint32_t b_bytes;
     uint32_t pipes;            // independent MMA pipelines (1 or 2), see tc_conv_kernel
+    uint32_t bias_smem;        // the epilogue warps keep the n-tile's bias in shared memory
     uint32_t halo;             // k x k stride 1: one A box per (kx, K block), see tc_conv_kernel
     uint32_t flat;             // k x k stride 1: one A box per K block serving every tap, see tc_conv_kernel
     uint32_t bwx, bhx;         // flat mode: the box's width and height in input pixels
@@ -118,6 +119,7 @@ struct TcArgs {
     uint32_t bn, bw, bh, tiles_x, tiles_y, m_tiles, n_tiles, split, k_iters, k_per_split, kblocks;
     uint32_t stages, tmem_cols, b_bytes, igemm;
     uint32_t b_resident, bres_off, res_off, pipes, halo, a_bytes;
+    uint32_t bias_smem;               // per-warp shared copies of the n-tile's bias (else L1 reads)
     uint32_t flat, bwx, a_box;        // flat mode (see tc_conv_kernel)
     uint32_t nparts, kb1, kb2;        // concat parts: 1-3 A tensor maps; parts 1 and 2 start at K blocks kb1, kb2
     uint32_t res_patch;               // RES 3 epilogue: residual from per-warp exact-2x patches
@@ -360,7 +362,7 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
 // 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches.
 // ACT: the activation when it is kNone or kRelu, else -1 (any kind, chosen
 // at run time)
-template <int RES, int ACT, bool FLAT>
+template <int RES, int ACT, bool FLAT, bool GBIAS = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a,
                    const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2)
@@ -626,7 +628,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Two groups of four warps; group g drains TMEM accumulator buffer g,
         // i.e. every other tile, so two tiles' epilogues run at once.  Within
         // a group, warp w owns TMEM lane quadrant w % 4 (= accumulator rows).
-        const uint32_t ew = (uint32_t)(warp - 1);  // 0..7: staging buffer, bias cache
+        const uint32_t ew = (uint32_t)(warp - 1);  // 0..7: staging buffer
         const uint32_t grp = ew >> 2;              // accumulator buffer this group drains
         const uint32_t quad = warp & 3;            // TMEM lane quadrant this warp may access
         uint8_t *obuf = smem + a.out_off + ew * kTcStageOut;  // 32 x 32 fp32 staging
@@ -719,12 +721,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         auto emit = [&](int col0, float (&v)[32]) {
             const int col = col0 + seg * 4;
             const bool vec = c.vec_y && col + 4 <= c.cout;
-            {
+            // the chunk's bias: the warp's shared copy, or read by every lane
+            // from the same global addresses (L1 broadcasts; the bias is
+            // 16-byte aligned, checked at launch), zero past cout
+            if constexpr (!GBIAS) {
                 const float4 *bb = reinterpret_cast<const float4 *>(bcache + (col0 - bias_base));
 #pragma unroll
                 for (int q4 = 0; q4 < 8; q4++) {
                     const float4 b = bb[q4];
                     v[4 * q4] += b.x; v[4 * q4 + 1] += b.y; v[4 * q4 + 2] += b.z; v[4 * q4 + 3] += b.w;
+                }
+            } else if (col0 + 32 <= c.cout) {
+                const float4 *bb = reinterpret_cast<const float4 *>(c.bias + col0);
+#pragma unroll
+                for (int q4 = 0; q4 < 8; q4++) {
+                    const float4 b = __ldg(bb + q4);
+                    v[4 * q4] += b.x; v[4 * q4 + 1] += b.y; v[4 * q4 + 2] += b.z; v[4 * q4 + 3] += b.w;
+                }
+            } else {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; q4++) {
+                    const int cb = col0 + 4 * q4;
+                    if (cb + 4 <= c.cout) {
+                        const float4 b = __ldg(reinterpret_cast<const float4 *>(c.bias + cb));
+                        v[4 * q4] += b.x; v[4 * q4 + 1] += b.y; v[4 * q4 + 2] += b.z; v[4 * q4 + 3] += b.w;
+                    } else if (cb < c.cout) {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) v[4 * q4 + i] += cb + i < c.cout ? __ldg(c.bias + cb + i) : 0.0f;
+                    }
                 }
             }
             act_fixed_n<ACT, 32>(c.act, v);
@@ -823,7 +847,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const long long m0 = (long long)t.mt * kTcBM + quad * 32;
                 wm0 = m0 < c.M ? (int)m0 : -1;
             }
-            if (t.nt != bias_nt) {
+            if (!GBIAS && t.nt != bias_nt) {
                 __syncwarp();
                 for (int i = lane; i < 256; i += 32) bcache[i] = (nbase + i < c.cout) ? __ldg(c.bias + nbase + i) : 0.0f;
                 __syncwarp();
@@ -1096,11 +1120,18 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->split = (g->k_iters + g->k_per_split - 1) / g->k_per_split;  // no empty splits
     g->units = tiles * g->split;
     g->b_bytes = g->bn * kTcBK * 4;
-    // shared memory: [stages][resident B][epilogue staging + bias caches]
-    // [barriers]; stage buffers and the resident B are 1024-aligned
-    // staging + per-warp bias caches (+ residual prefetch buffers)
+    // shared memory: [stages][resident B][epilogue staging][barriers]; stage
+    // buffers and the resident B are 1024-aligned.  Per epilogue warp: a
+    // 32 x 32 staging tile, a copy of the n-tile's bias (+ residual prefetch
+    // buffers).  Where the ring would have fewer than four stages and the
+    // bias copies are what costs the next one, they are dropped (the
+    // epilogue then reads the bias from global memory, L1 broadcasts): the
+    // wide (N = 256) tiles get their fourth 48 KB stage that way (config 2
+    // 128 -> 256: 444 -> 507 TFLOP/s), while the shallow-K layers keep the
+    // copies (global bias reads slowed their epilogue: e3.exp 43 -> 52 us).
     const uint32_t res_buf = res_kind == kTcResTensor ? kTcStageOut : res_kind == kTcResUp2 ? kTcPatchBytes : 0u;
-    const uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + 256 * 4 + res_buf);
+    const uint32_t bias_bytes = kTcEpiWarps * 256 * 4;
+    uint32_t out_bytes = kTcEpiWarps * (kTcStageOut + res_buf) + bias_bytes;
     const uint32_t limit = 227 * 1024 - 1024 /*align slack*/ - 256 /*barriers*/;
     // Resident B: with one n-tile and no K split every unit of a CTA uses the
     // same B, so it is loaded once (one TMA box per tap and K block) and each
@@ -1111,6 +1142,12 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     const uint32_t stage = g->a_bytes + (g->b_resident ? 0u : (g->flat ? kh * kw : g->halo ? kh : 1u) * g->b_bytes);
     const uint32_t fixed = out_bytes + (g->b_resident ? (uint32_t)bres : 0u);
     g->stages = std::min<uint32_t>(8, (limit - fixed) / stage);
+    g->bias_smem = 1;
+    if (g->stages < 4 && !g->flat && res_kind <= kTcResTensor && (limit - fixed + bias_bytes) / stage > g->stages) {
+        g->stages = std::min<uint32_t>(8, (limit - fixed + bias_bytes) / stage);
+        g->bias_smem = 0;
+        out_bytes -= bias_bytes;
+    }
     if (g->flat && g->stages < 3)  // flat stages too large: the per-kx halo boxes
         return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, true, false);
     if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
@@ -1122,7 +1159,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->pipes = (g->igemm && g->bn <= 128 && g->stages >= 4) ? 2u : 1u;
     g->bres_off = g->stages * stage;
     g->out_off = g->bres_off + (g->b_resident ? (uint32_t)bres : 0u);
-    g->res_off = res_buf ? g->out_off + kTcEpiWarps * (kTcStageOut + 256 * 4) : 0u;
+    g->res_off = res_buf ? g->out_off + kTcEpiWarps * kTcStageOut + (g->bias_smem ? bias_bytes : 0u) : 0u;
     g->res_patch = (res_kind == kTcResUp2 && !g->igemm) ? 1u : 0u;
     g->shared_off = g->out_off + out_bytes;
     g->tmem_cols = tc_pow2_ceil((g->pipes == 2 ? 4 : 2) * g->bn);  // two accumulators per pipeline
@@ -1253,7 +1290,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     a.m_tiles = g.m_tiles; a.n_tiles = g.n_tiles; a.split = g.split; a.k_iters = g.k_iters;
     a.k_per_split = g.k_per_split; a.kblocks = g.kblocks; a.stages = g.stages; a.tmem_cols = g.tmem_cols;
     a.b_bytes = g.b_bytes; a.igemm = g.igemm; a.units = g.units;
-    a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes;
+    a.b_resident = g.b_resident; a.bres_off = g.bres_off; a.res_off = g.res_off; a.pipes = g.pipes; a.bias_smem = g.bias_smem;
     a.halo = g.halo; a.a_bytes = g.a_bytes;
     a.flat = g.flat; a.bwx = g.bwx; a.a_box = g.a_box;
     a.nparts = (uint32_t)parts->n;
@@ -1301,16 +1338,22 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         {tc_conv_kernel<1, kNone, false>, tc_conv_kernel<1, kRelu, false>, tc_conv_kernel<1, -1, false>},
         {tc_conv_kernel<2, kNone, false>, tc_conv_kernel<2, kRelu, false>, tc_conv_kernel<2, -1, false>},
         {tc_conv_kernel<3, kNone, false>, tc_conv_kernel<3, kRelu, false>, tc_conv_kernel<3, -1, false>}};
+    // global bias reads (the ring's fourth stage in place of the bias copies;
+    // never with exact-2x residual patches, see tc_plan)
+    static const Kern kerns_gbias[3][3] = {
+        {tc_conv_kernel<0, kNone, false, true>, tc_conv_kernel<0, kRelu, false, true>, tc_conv_kernel<0, -1, false, true>},
+        {tc_conv_kernel<1, kNone, false, true>, tc_conv_kernel<1, kRelu, false, true>, tc_conv_kernel<1, -1, false, true>},
+        {tc_conv_kernel<2, kNone, false, true>, tc_conv_kernel<2, kRelu, false, true>, tc_conv_kernel<2, -1, false, true>}};
     static const Kern kerns_flat[3][3] = {
         {tc_conv_kernel<0, kNone, true>, tc_conv_kernel<0, kRelu, true>, tc_conv_kernel<0, -1, true>},
         {tc_conv_kernel<1, kNone, true>, tc_conv_kernel<1, kRelu, true>, tc_conv_kernel<1, -1, true>},
         {tc_conv_kernel<2, kNone, true>, tc_conv_kernel<2, kRelu, true>, tc_conv_kernel<2, -1, true>}};
     const int ak = c.act == kNone ? 0 : c.act == kRelu ? 1 : 2;
-    if (g.flat && kind == 3) {
-        snprintf(err, errlen, "flat tiles take no exact-2x residual patches");
+    if ((g.flat || !g.bias_smem) && kind == 3) {
+        snprintf(err, errlen, "flat tiles and global-bias tiles take no exact-2x residual patches");
         return -2;
     }
-    auto kern = g.flat ? kerns_flat[kind][ak] : kerns[kind][ak];
+    auto kern = g.flat ? kerns_flat[kind][ak] : !g.bias_smem ? kerns_gbias[kind][ak] : kerns[kind][ak];
     {
         cudaError_t e = ensure_smem_attr((const void *)kern, 227 * 1024);
         if (e != cudaSuccess) {
