@@ -366,3 +366,41 @@ def test_tc_stem_views_and_fallback(cuda_ok):
         g = buf.cpu().numpy()
         assert normalised_error(g[..., coff:coff + 32], want, scale) <= TOL_TF32
         assert (g[..., :coff] == 7.0).all() and (g[..., coff + 32:] == 7.0).all()
+
+
+@pytest.mark.parametrize("case", ["3x3 128->250", "3x3 128->256 res", "1x1 512->256 res", "1x1 512->256 bilinear res"])
+def test_wide_tiles_read_bias_from_global(cuda_ok, case):
+    """Wide (N = 256) tiles whose 48 KB stages leave room for only three
+    ring stages drop the epilogue's shared bias copies for a fourth stage
+    and read the bias from global memory: a partial last 32-column chunk
+    (cout 250), a 1x1 with a long K, and a resized (bilinear, not exact-2x)
+    residual read by the epilogue; with a tensor residual the prefetch
+    buffers keep the ring at three stages either way, so that case keeps
+    the copies.  Against the oracle at the TF32 bar."""
+    import oracle
+    from oracle import XorShift32
+    rng = XorShift32(1700 + len(case))
+    if case.startswith("3x3"):
+        n, h, w = 2, 9, 16  # few tiles: split-K, the N tile stays 256
+        cout = 250 if "250" in case else 256
+        op = Conv2d.same(128, cout, 3, 1, "hardswish")
+    else:
+        n, h, w = 1, 100, 192  # 150 M tiles: no split, so the 1x1 keeps its 256-wide N tile
+        cout = 256
+        op = Conv2d.pointwise(512, cout, "relu")
+    x = rng.vec_f32(n * h * w * op.cin).reshape(n, h, w, op.cin)
+    wt = rng.vec_f32(op.cout * op.cin * op.kh * op.kw)
+    b = rng.vec_f32(op.cout)
+    if "bilinear" in case:
+        lh, lw = 37, 71
+        lo = rng.vec_f32(n * lh * lw * cout).reshape(n, lh, lw, cout)
+        res = oracle.resize_bilinear(lo, h, w, "half_pixel")
+        plan = ConvPlan(op, n, h, w, has_res=True, math="tf32", res_resize=(lh, lw, "half_pixel")).load_weights(wt, b)
+        got = plan(torch.from_numpy(x).cuda(), torch.from_numpy(lo).cuda()).cpu().numpy()
+    else:
+        res = rng.vec_f32(n * h * w * cout).reshape(n, h, w, cout) if "res" in case else None
+        plan = ConvPlan(op, n, h, w, has_res=res is not None, math="tf32").load_weights(wt, b)
+        got = plan(torch.from_numpy(x).cuda(), None if res is None else torch.from_numpy(res).cuda()).cpu().numpy()
+    assert plan.math == "tf32" and plan.info.tile_n == 256
+    want, scale = oracle_conv(op, x, wt, b, res)
+    assert normalised_error(got, want, scale) <= TOL_TF32
