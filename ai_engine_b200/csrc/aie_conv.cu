@@ -794,7 +794,7 @@ static int run_dw_pw(const aie_plan *dw, const aie_plan *pw, const void *in, con
             return fail(AIE_E_UNSUPPORTED, "up-sampled input: operands are not TMA-compatible");              \
         if (up) {                                                                                             \
             /* one tile per CTA: four CTAs per SM overlap their staging */                                   \
-            auto ku_ = dw_tile_kernel<false, K_, ST_, TW_, true, true, true>;                                 \
+            auto ku_ = dw_tile_up2_kernel<K_, ST_, TW_>;                                 \
             CUDA_TRY(ensure_smem_attr((const void *)ku_, G_::SMEM + G_::QSMEM));                              \
             ku_<<<(unsigned)blocks, G_::NT, G_::SMEM + G_::QSMEM, s>>>(tm_, tmq, a, tg, hd,                   \
                                                                       DwUp2{(int)up_h, (int)up_w});           \

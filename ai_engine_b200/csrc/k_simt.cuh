@@ -1221,14 +1221,10 @@ __device__ __forceinline__ void dw_tile_compute(const float4 *halo4, const ConvA
 // (cin, iw, ih, n) tensor map, issued by one thread -- out-of-range pixels and
 // channels read as zeros -- instead of one 16-byte cp.async per chunk with its
 // index arithmetic (the staging was a sixth of the kernel's instructions).
-// The up-sampled head asks for five CTAs per SM (at most 51 registers, a few
-// bytes of spill): a CTA waits for its two TMA boxes with nothing else to
-// do, and the fifth CTA hides more of that wait (head 194.7 -> 186.2 us at
-// 256 frames).
-template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false, bool UP2 = false>
-__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT, UP2 ? 5 : 1)
-    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq, const ConvArgs a,
-                   const DwTile g, const PwHead hd, const DwUp2 up)
+// The body of dw_tile_kernel and dw_tile_up2_kernel (below).
+template <bool kStrict, int K, int S, int TW, bool HEAD, bool kTma, bool UP2>
+__device__ __forceinline__ void dw_tile_body(const CUtensorMap &tmx, const CUtensorMap &tmq, const ConvArgs &a,
+                                             const DwTile &g, const PwHead &hd, const DwUp2 &up)
 {
     static_assert(!UP2 || kTma, "the up-sampled input is staged by TMA");
     static_assert(!UP2 || !kStrict, "the up-sampled input is mixed with fused multiply-adds");
@@ -1287,6 +1283,28 @@ __global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT, UP2 ? 5 : 1)
         __syncthreads();
     }
     dw_tile_compute<kStrict, K, S, TW, HEAD>(halo4, a, hd, img, ty, tx, c0, ncg);
+}
+
+template <bool kStrict, int K, int S, int TW, bool HEAD = false, bool kTma = false>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT)
+    dw_tile_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq, const ConvArgs a,
+                   const DwTile g, const PwHead hd, const DwUp2 up)
+{
+    dw_tile_body<kStrict, K, S, TW, HEAD, kTma, false>(tmx, tmq, a, g, hd, up);
+}
+
+// The fused head with the up-sampled input asks for five CTAs per SM (at most
+// 51 registers, a few bytes of spill): a CTA waits for its two TMA boxes with
+// nothing else to do, and the fifth CTA hides more of that wait (head 194.7
+// -> 186.2 us at 256 frames).  The other tile kernels keep the compiler's
+// own register choice (an explicit minimum of one block let it take 128
+// registers and halve their occupancy: 164 -> 242 us on 80x144x32).
+template <int K, int S, int TW>
+__global__ void __launch_bounds__(DwTileGeom<K, S, TW>::NT, 5)
+    dw_tile_up2_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmq,
+                       const ConvArgs a, const DwTile g, const PwHead hd, const DwUp2 up)
+{
+    dw_tile_body<false, K, S, TW, true, true, true>(tmx, tmq, a, g, hd, up);
 }
 
 // Persistent fused head (head mode, TMA staging): a CTA walks the tiles

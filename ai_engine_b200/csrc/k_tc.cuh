@@ -1148,7 +1148,11 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
         g->bias_smem = 0;
         out_bytes -= bias_bytes;
     }
-    if (g->flat && g->stages < 3)  // flat stages too large: the per-kx halo boxes
+    // flat tiles want the weights resident: streamed, a stage carries kh*kw
+    // B tiles (36 KB for a 3 x 3 at N = 32) and the ring shrinks to three
+    // stages (a 3 x 3 72 -> 32 at 40 x 72 took 346 us flat against 234 us
+    // with the per-kx halo boxes, whose stages carry kh B tiles)
+    if (g->flat && (g->stages < 3 || !g->b_resident))  // the per-kx halo boxes instead
         return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, true, false);
     if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
         return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false, false);
