@@ -77,7 +77,6 @@ constexpr int kTcThreads = 32 * (kTcMmaWarp1 + 1);           // MMA 0, epilogue,
 constexpr uint32_t kTcStageOut = 32 * 32 * 4;      // one 32x32 fp32 epilogue chunk per warp
 constexpr int kTcBM = 128;
 constexpr int kTcBK = 32;                 // fp32 elements per K block = 128 B (one swizzle row)
-constexpr uint32_t kTcABytes = kTcBM * kTcBK * 4;  // 16 KB
 constexpr uint32_t kTcBResidentMax = 112 * 1024;   // largest B kept in shared memory for a whole kernel
 constexpr int kTcPatchCols = 18;                   // source columns per segment of an exact-2x residual patch
 constexpr uint32_t kTcPatchBytes = 2 * 2 * kTcPatchCols * 128;  // [segment][source row][column] x 32 channels
@@ -101,6 +100,7 @@ struct TcGeom {
     uint32_t smem_bytes;
     uint32_t b_bytes;
     uint32_t pipes;            // independent MMA pipelines (1 or 2), see tc_conv_kernel
+    uint32_t bk;               // channels per K block: 32 (128-byte rows) or 16 (64-byte rows)
     uint32_t bias_smem;        // the epilogue warps keep the n-tile's bias in shared memory
     uint32_t halo;             // k x k stride 1: one A box per (kx, K block), see tc_conv_kernel
     uint32_t flat;             // k x k stride 1: one A box per K block serving every tap, see tc_conv_kernel
@@ -199,6 +199,26 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr)
     d |= (uint64_t)1 << 46;                        // version
     d |= (uint64_t)2 << 61;                        // layout: SWIZZLE_128B
     return d;
+}
+
+// The same for 16-channel K blocks (64-byte rows, 64-byte swizzle: 8-row
+// groups 512 bytes apart), and the descriptor of a K block of bk channels.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);       // start address
+    d |= (uint64_t)1 << 16;                        // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32;               // stride byte offset
+    d |= (uint64_t)1 << 46;                        // version
+    d |= (uint64_t)4 << 61;                        // layout: SWIZZLE_64B
+    return d;
+}
+
+template <int BK>
+__device__ __forceinline__ uint64_t smem_desc_k(uint32_t saddr)
+{
+    if constexpr (BK == 16) return smem_desc_sw64(saddr);
+    else return smem_desc_sw128(saddr);
 }
 
 // Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major.
@@ -362,7 +382,7 @@ __device__ __forceinline__ long long tc_row_pixel(const TcArgs &a, uint32_t mt, 
 // 2 bilinear sample read directly, 3 exact-2x sample from per-warp patches.
 // ACT: the activation when it is kNone or kRelu, else -1 (any kind, chosen
 // at run time)
-template <int RES, int ACT, bool FLAT, bool GBIAS = false>
+template <int RES, int ACT, bool FLAT, bool GBIAS = false, int BK = 32>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs a,
                    const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2)
@@ -444,7 +464,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_expect_tx(&sh.bfull, nb * a.b_bytes);
             for (uint32_t k = 0; k < nb; k++) {
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
-                tma_load_3d(smem + a.bres_off + k * a.b_bytes, &tmB, &sh.bfull, (int)(kb * kTcBK), 0, (int)tap);
+                tma_load_3d(smem + a.bres_off + k * a.b_bytes, &tmB, &sh.bfull, (int)(kb * BK), 0, (int)tap);
             }
         }
         uint32_t last_mine = 0xFFFFFFFFu;
@@ -466,7 +486,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_expect_tx(&sh.full[s], stage_tx);
                 const uint32_t k = cur.k;
                 const uint32_t tap = k / a.kblocks, kb = k - tap * a.kblocks;
-                const int kc = (int)(kb * kTcBK);
+                const int kc = (int)(kb * BK);
                 // the A copy of K block kbx: its part's tensor map and channel coordinate
                 auto amap = [&](uint32_t kbx, int &ac) -> const CUtensorMap * {
                     if (a.nparts > 2 && kbx >= a.kb2) {
@@ -477,7 +497,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         ac = (int)((kbx - a.kb1) * kTcBK);
                         return &tmA1;
                     }
-                    ac = (int)(kbx * kTcBK);
+                    ac = (int)(kbx * BK);  // concat parts take 32-channel K blocks only
                     return &tmA;
                 };
                 int ac;
@@ -488,7 +508,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tma_load_4d(sa, tm, &sh.full[s], ac, o.ox0 - a.c.pl, o.oy0 - a.c.pt, o.img);
                     if (!a.b_resident)
                         for (int tp = 0; tp < a.c.kh * a.c.kw; tp++)
-                            tma_load_3d(sb + tp * a.b_bytes, &tmB, &sh.full[s], (int)(k * kTcBK), (int)(t.nt * a.bn),
+                            tma_load_3d(sb + tp * a.b_bytes, &tmB, &sh.full[s], (int)(k * BK), (int)(t.nt * a.bn),
                                         tp);
                 } else if (a.halo) {
                     // stage = column shift kx (= tap here), K block kb: rows
@@ -565,6 +585,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * stage_bytes);
+                    // one K block: bk / 8 MMAs, each 8 tf32 = 32 bytes further
+                    // along K inside the swizzle row
+                    constexpr uint32_t rowb = BK * 4;
+                    auto kblock = [&](uint64_t ad, uint64_t bd, bool acc0) {
+                        if constexpr (BK == 16) {
+                            mma_tf32(d, ad, bd, idesc, acc0 ? 0u : 1u);
+                            mma_tf32(d, ad + 2, bd + 2, idesc, 1u);
+                        } else {
+#pragma unroll
+                            for (uint32_t kk = 0; kk < 4; kk++)
+                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                         (acc0 && kk == 0) ? 0u : 1u);
+                        }
+                    };
                     if constexpr (FLAT) {
                         // K block k; tap (ky, kx) reads the box from row ky * bwx + kx
                         // (a fully unrolled 3 x 3 loop with precomputed descriptors
@@ -575,12 +609,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 const uint32_t sb = a.b_resident
                                                         ? smem_u32(smem + a.bres_off + (tap * a.kblocks + k) * a.b_bytes)
                                                         : sa + a.a_bytes + tap * a.b_bytes;
-                                const uint64_t ad = smem_desc_sw128(sa + (ky * a.bwx + kx) * 128),
-                                               bd = smem_desc_sw128(sb);
-#pragma unroll
-                                for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                    mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                             (k > k0 || tap > 0 || kk > 0) ? 1u : 0u);
+                                kblock(smem_desc_k<BK>(sa + (ky * a.bwx + kx) * rowb), smem_desc_k<BK>(sb),
+                                       k == k0 && tap == 0);
                             }
                     } else if (a.halo) {
                         // tap (ky, kx): the stage's copy shifted down ky rows
@@ -591,21 +621,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             const uint32_t sb = a.b_resident
                                                     ? smem_u32(smem + a.bres_off + (tap * a.kblocks + kb) * a.b_bytes)
                                                     : sa + a.a_bytes + ky * a.b_bytes;
-                            const uint64_t ad = smem_desc_sw128(sa + ky * a.bw * 128), bd = smem_desc_sw128(sb);
-#pragma unroll
-                            for (uint32_t kk = 0; kk < kTcBK / 8; kk++)
-                                mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                         (k > k0 || ky > 0 || kk > 0) ? 1u : 0u);
+                            kblock(smem_desc_k<BK>(sa + ky * a.bw * rowb), smem_desc_k<BK>(sb), k == k0 && ky == 0);
                         }
                     } else {
-                        const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + kTcABytes;
-                        const uint64_t ad = smem_desc_sw128(sa), bd = smem_desc_sw128(sb);
-#pragma unroll
-                        for (uint32_t kk = 0; kk < kTcBK / 8; kk++) {
-                            // advance 8 tf32 = 32 bytes along K inside the swizzle row
-                            mma_tf32(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                     (k > k0 || kk > 0) ? 1u : 0u);
-                        }
+                        const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + a.a_bytes;
+                        kblock(smem_desc_k<BK>(sa), smem_desc_k<BK>(sb), k == k0);
                     }
                     mma_commit(&sh.empty[s]);
                 }
@@ -1005,7 +1025,16 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     const bool pw = kh == 1 && kw == 1 && sh == 1 && sw == 1;
     g->igemm = pw ? 0 : 1;
     g->taps = kh * kw;
-    g->kblocks = (cin + kTcBK - 1) / kTcBK;
+    // K blocks of 32 channels (128-byte rows); one block of 16 (64-byte
+    // rows, 64-byte swizzle) for cin <= 16, whose 32-wide block would be
+    // half or more zero fill: half the MMAs (bound by the A operand's
+    // shared-memory reads, which cost the same for data and padding) for
+    // the same number of K blocks.  Where 16-channel blocks would need more
+    // blocks than 32-channel ones (36 channels: 3 against 2) the per-block
+    // copies and waits cost more than the MMAs saved (RVM's 3x3 36 -> 16:
+    // 1415 -> 1820 us), so those keep 32.
+    g->bk = (cin <= 16 && res_kind != kTcResUp2) ? 16u : (uint32_t)kTcBK;
+    g->kblocks = (cin + g->bk - 1) / g->bk;
     g->k_iters = g->taps * g->kblocks;
     // Halo mode (k x k, stride 1, dilation 1): a 16 x 8 pixel tile's A for
     // tap (ky, kx) is rows [ky*16, ky*16 + 128) of one (8 + kh - 1) x 16
@@ -1013,7 +1042,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     // and feeds kh MMA groups: kw x kblocks boxes per tile instead of
     // kh x kw x kblocks.
     g->halo = (allow_halo && !pw && sh == 1 && sw == 1 && dil == 1 && kh >= 2 && kh <= 7) ? 1u : 0u;
-    g->a_bytes = kTcABytes;
+    g->a_bytes = kTcBM * g->bk * 4;
     // N tile: fewest tiles of <= 256 columns, each a multiple of 32 so the
     // epilogue's 32-column store boxes never reach into the next tile
     const uint32_t nt = (cout + 255) / 256;
@@ -1034,12 +1063,12 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
         g->bw = 16;
         g->bh = tr;
         g->k_iters = g->kblocks;
-        g->a_box = bwx * rows * kTcBK * 4;
+        g->a_box = bwx * rows * g->bk * 4;
         g->a_bytes = (g->a_box + 1023) / 1024 * 1024;  // the next stage's copy stays 1 KB aligned
     }
     if (g->halo) {
         g->k_iters = kw * g->kblocks;
-        g->a_bytes = (8 + kh - 1) * 16 * kTcBK * 4;
+        g->a_bytes = (8 + kh - 1) * 16 * g->bk * 4;
     }
     if (!g->flat) g->a_box = g->a_bytes;
     if (g->flat) {
@@ -1095,7 +1124,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
                 const uint32_t kps = (g->k_iters + sp - 1) / sp;
                 const uint64_t waves = (t2 * ((g->k_iters + kps - 1) / kps) + 147) / 148;
                 const double mma = kps * 4 * 0.072;
-                const double load = kps * (double)(g->a_bytes + bn * kTcBK * 4) / 1e5;
+                const double load = kps * (double)(g->a_bytes + bn * g->bk * 4) / 1e5;
                 double t = waves * std::max(mma, load);
                 if (sp > 1) t += 128.0 * bn * 4 / 2e5 + 0.5 * ((sp + 1) / 2) * (bn / 32);
                 if (t < best) {
@@ -1119,7 +1148,7 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     g->k_per_split = (g->k_iters + split - 1) / split;
     g->split = (g->k_iters + g->k_per_split - 1) / g->k_per_split;  // no empty splits
     g->units = tiles * g->split;
-    g->b_bytes = g->bn * kTcBK * 4;
+    g->b_bytes = g->bn * g->bk * 4;
     // shared memory: [stages][resident B][epilogue staging][barriers]; stage
     // buffers and the resident B are 1024-aligned.  Per epilogue warp: a
     // 32 x 32 staging tile, a copy of the n-tile's bias (+ residual prefetch
@@ -1241,6 +1270,12 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     }
     CUtensorMap tmAp[3], tmB;
     CUresult r = CUDA_SUCCESS;
+    // 128-byte rows for 32-channel K blocks, 64-byte rows for 16-channel ones
+    const CUtensorMapSwizzle swz = g.bk == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    if (parts != &one && g.bk != (uint32_t)kTcBK) {
+        snprintf(err, errlen, "concat parts take 32-channel K blocks");
+        return -2;
+    }
     for (int pi = 0; pi < parts->n && r == CUDA_SUCCESS; pi++) {
         const uintptr_t abase = (uintptr_t)(parts->x[pi] + parts->coff[pi]);
         const long long xs = parts->stride[pi];
@@ -1251,19 +1286,19 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         if (g.igemm) {
             const cuuint64_t dims[4] = {(cuuint64_t)parts->c[pi], (cuuint64_t)c.iw, (cuuint64_t)c.ih, (cuuint64_t)c.n};
             const cuuint64_t strides[3] = {(cuuint64_t)xs * 4, (cuuint64_t)xs * 4 * c.iw, (cuuint64_t)xs * 4 * c.iw * c.ih};
-            const cuuint32_t box[4] = {(cuuint32_t)kTcBK, g.flat ? g.bwx : g.bw * (cuuint32_t)c.sw,
+            const cuuint32_t box[4] = {(cuuint32_t)g.bk, g.flat ? g.bwx : g.bw * (cuuint32_t)c.sw,
                                        g.flat ? g.bhx : g.halo ? g.bh + (cuuint32_t)c.kh - 1 : g.bh * (cuuint32_t)c.sh, 1};
             const cuuint32_t estr[4] = {1, (cuuint32_t)c.sw, (cuuint32_t)c.sh, 1};
             r = enc(&tmAp[pi], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)abase, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         } else {
             const cuuint64_t dims[2] = {(cuuint64_t)parts->c[pi], (cuuint64_t)c.M};
             const cuuint64_t strides[1] = {(cuuint64_t)xs * 4};
-            const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+            const cuuint32_t box[2] = {(cuuint32_t)g.bk, (cuuint32_t)kTcBM};
             const cuuint32_t estr[2] = {1, 1};
             r = enc(&tmAp[pi], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)abase, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         }
     }
@@ -1278,10 +1313,10 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         const uint32_t cin_pad = parts != &one ? g.kblocks * kTcBK : (c.cin + 3) / 4 * 4;
         const cuuint64_t dims[3] = {(cuuint64_t)cin_pad, (cuuint64_t)c.cout, (cuuint64_t)(c.kh * c.kw)};
         const cuuint64_t strides[2] = {(cuuint64_t)cin_pad * 4, (cuuint64_t)cin_pad * 4 * c.cout};
-        const cuuint32_t box[3] = {(cuuint32_t)kTcBK, g.bn, 1};
+        const cuuint32_t box[3] = {(cuuint32_t)g.bk, g.bn, 1};
         const cuuint32_t estr[3] = {1, 1, 1};
         r = enc(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)c.w, dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) {
             snprintf(err, errlen, "cuTensorMapEncodeTiled(B) failed: %d", (int)r);
@@ -1348,6 +1383,21 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         {tc_conv_kernel<0, kNone, false, true>, tc_conv_kernel<0, kRelu, false, true>, tc_conv_kernel<0, -1, false, true>},
         {tc_conv_kernel<1, kNone, false, true>, tc_conv_kernel<1, kRelu, false, true>, tc_conv_kernel<1, -1, false, true>},
         {tc_conv_kernel<2, kNone, false, true>, tc_conv_kernel<2, kRelu, false, true>, tc_conv_kernel<2, -1, false, true>}};
+    // 16-channel K blocks (cin <= 16): the plain and flat kernels again
+    static const Kern kerns_k16[3][3] = {
+        {tc_conv_kernel<0, kNone, false, false, 16>, tc_conv_kernel<0, kRelu, false, false, 16>,
+         tc_conv_kernel<0, -1, false, false, 16>},
+        {tc_conv_kernel<1, kNone, false, false, 16>, tc_conv_kernel<1, kRelu, false, false, 16>,
+         tc_conv_kernel<1, -1, false, false, 16>},
+        {tc_conv_kernel<2, kNone, false, false, 16>, tc_conv_kernel<2, kRelu, false, false, 16>,
+         tc_conv_kernel<2, -1, false, false, 16>}};
+    static const Kern kerns_flat_k16[3][3] = {
+        {tc_conv_kernel<0, kNone, true, false, 16>, tc_conv_kernel<0, kRelu, true, false, 16>,
+         tc_conv_kernel<0, -1, true, false, 16>},
+        {tc_conv_kernel<1, kNone, true, false, 16>, tc_conv_kernel<1, kRelu, true, false, 16>,
+         tc_conv_kernel<1, -1, true, false, 16>},
+        {tc_conv_kernel<2, kNone, true, false, 16>, tc_conv_kernel<2, kRelu, true, false, 16>,
+         tc_conv_kernel<2, -1, true, false, 16>}};
     static const Kern kerns_flat[3][3] = {
         {tc_conv_kernel<0, kNone, true>, tc_conv_kernel<0, kRelu, true>, tc_conv_kernel<0, -1, true>},
         {tc_conv_kernel<1, kNone, true>, tc_conv_kernel<1, kRelu, true>, tc_conv_kernel<1, -1, true>},
@@ -1357,7 +1407,14 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
         snprintf(err, errlen, "flat tiles and global-bias tiles take no exact-2x residual patches");
         return -2;
     }
-    auto kern = g.flat ? kerns_flat[kind][ak] : !g.bias_smem ? kerns_gbias[kind][ak] : kerns[kind][ak];
+    if (g.bk == 16 && (kind == 3 || !g.bias_smem)) {
+        snprintf(err, errlen, "16-channel K blocks take no exact-2x residual patches nor global bias reads");
+        return -2;
+    }
+    auto kern = g.bk == 16 ? (g.flat ? kerns_flat_k16[kind][ak] : kerns_k16[kind][ak])
+                : g.flat   ? kerns_flat[kind][ak]
+                : !g.bias_smem ? kerns_gbias[kind][ak]
+                               : kerns[kind][ak];
     {
         cudaError_t e = ensure_smem_attr((const void *)kern, 227 * 1024);
         if (e != cudaSuccess) {
