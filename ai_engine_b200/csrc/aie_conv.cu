@@ -78,6 +78,7 @@ struct aie_plan {
     // concat parts read in place (aie_conv_plan_parts): 0 = a plain plan
     uint32_t nparts;
     uint32_t part_c[3], part_kb0[3];
+    uint32_t part_bk;  // channels per K block of a parts plan: 16 when every part has <= 16, else 32
 };
 
 static const int kMathStrict = AIE_MATH_FP32_STRICT;
@@ -233,14 +234,20 @@ static int plan_impl(const aie_conv_desc *desc, uint32_t nparts, const uint32_t 
     const long long ww = (long long)d.iw + d.pad[1] + d.pad[3] - ekw;
     if (hh < 0 || ww < 0) return fail(AIE_E_INVALID, "kernel larger than padded input");
 
-    uint32_t kblocks_parts = 0, part_kb0[3] = {0, 0, 0};
+    // concat parts: each part starts on a K block; 16-channel blocks when
+    // every part has at most 16 channels (two 16-channel parts then fill
+    // one 32-channel block's MMAs instead of two half-padded blocks)
+    uint32_t kblocks_parts = 0, part_kb0[3] = {0, 0, 0}, part_bk = kTcBK;
     if (nparts) {
         if (nparts > 3 || !part_c) return fail(AIE_E_INVALID, "1 to 3 concat parts, got %u", nparts);
         uint64_t sum = 0;
+        part_bk = 16;
+        for (uint32_t i = 0; i < nparts; i++)
+            if (part_c[i] > 16) part_bk = kTcBK;
         for (uint32_t i = 0; i < nparts; i++) {
             if (!part_c[i]) return fail(AIE_E_INVALID, "concat part %u has no channels", i);
             part_kb0[i] = kblocks_parts;
-            kblocks_parts += (part_c[i] + kTcBK - 1) / kTcBK;
+            kblocks_parts += (part_c[i] + part_bk - 1) / part_bk;
             sum += part_c[i];
         }
         if (sum != d.cin) return fail(AIE_E_INVALID, "concat parts hold %llu channels, cin is %u",
@@ -254,6 +261,7 @@ static int plan_impl(const aie_conv_desc *desc, uint32_t nparts, const uint32_t 
     if (!p) return fail(AIE_E_NOMEM, "plan allocation");
     p->d = d;
     p->nparts = nparts;
+    p->part_bk = part_bk;
     for (uint32_t i = 0; i < nparts; i++) {
         p->part_c[i] = part_c[i];
         p->part_kb0[i] = part_kb0[i];
@@ -371,8 +379,8 @@ static int plan_impl(const aie_conv_desc *desc, uint32_t nparts, const uint32_t 
         p->grid = (uint64_t)((p->M + 255) / 256);
     } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         // weights [tap][cout][cin_pad]; with parts every part's channels
-        // start on a 32-channel K block (zero weight rows between parts)
-        p->cin_pad = nparts ? (int)(kblocks_parts * kTcBK) : (int)rup(d.cin, 4);
+        // start on a K block (zero weight rows between parts)
+        p->cin_pad = nparts ? (int)(kblocks_parts * part_bk) : (int)rup(d.cin, 4);
         p->wbytes = (uint64_t)taps * d.cout * p->cin_pad * 4;
         // residual buffers: rows of a residual tensor, or per-warp patches
         // of an exact-2x half_pixel residual on 1x1 tiles (32 consecutive
@@ -387,7 +395,8 @@ static int plan_impl(const aie_conv_desc *desc, uint32_t nparts, const uint32_t 
                                       ? kTcResUp2
                                       : kTcResNone;
         int rc = tc_plan(d.n, d.ih, d.iw, nparts ? (uint32_t)p->cin_pad : d.cin, d.cout, d.kh, d.kw, d.sh, d.sw,
-                         d.dil, d.pad[0], d.pad[1], p->oh, p->ow, d.split_k, res_kind, &p->tc);
+                         d.dil, d.pad[0], d.pad[1], p->oh, p->ow, d.split_k, res_kind, &p->tc, true, true,
+                         nparts ? part_bk : 0u);
         if (rc) {
             delete p;
             return fail(AIE_E_UNSUPPORTED, "tensor-core geometry rejected (%d)", rc);
@@ -514,12 +523,12 @@ extern "C" int aie_conv_pack_weights(const aie_plan *p, int32_t wfmt, const floa
     } else if (p->math == AIE_MATH_TF32 && !p->stem_tc) {
         // [tap][cout][cin_pad]: K-major rows for the tcgen05 B operand; with
         // concat parts, input channel ic of part i sits at K position
-        // 32 * part_kb0[i] + (ic - the part's first channel)
+        // part_bk * part_kb0[i] + (ic - the part's first channel)
         std::vector<uint32_t> kpos(d.cin);
         for (uint32_t ic = 0, i = 0, c0 = 0; ic < d.cin; ic++) {
             if (p->nparts) {
                 while (ic >= c0 + p->part_c[i]) c0 += p->part_c[i++];
-                kpos[ic] = p->part_kb0[i] * kTcBK + (ic - c0);
+                kpos[ic] = p->part_kb0[i] * p->part_bk + (ic - c0);
             } else {
                 kpos[ic] = ic;
             }

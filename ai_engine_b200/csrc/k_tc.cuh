@@ -45,7 +45,8 @@
 //              a multiple of 8 reads the right bytes.
 // Concat parts (up to 3): the input is the channel concat of separate
 // views read in place, one A tensor map each; part p owns whole K blocks
-// (its channels padded with zero fill to a multiple of 32), so a K block's
+// (its channels padded with zero fill to a multiple of the block width: 16
+// when every part has at most 16 channels, else 32), so a K block's
 // copy comes from one part's map at that part's own channel coordinate.
 // B operand (weights [tap][cout][cin_pad]): 3-D map, box (32, bn, 1).
 //
@@ -202,7 +203,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr)
 }
 
 // The same for 16-channel K blocks (64-byte rows, 64-byte swizzle: 8-row
-// groups 512 bytes apart), and the descriptor of a K block of bk channels.
+// groups 512 bytes apart), and the descriptor of a K block of BK channels.
 __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr)
 {
     uint64_t d = 0;
@@ -490,14 +491,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // the A copy of K block kbx: its part's tensor map and channel coordinate
                 auto amap = [&](uint32_t kbx, int &ac) -> const CUtensorMap * {
                     if (a.nparts > 2 && kbx >= a.kb2) {
-                        ac = (int)((kbx - a.kb2) * kTcBK);
+                        ac = (int)((kbx - a.kb2) * BK);
                         return &tmA2;
                     }
                     if (a.nparts > 1 && kbx >= a.kb1) {
-                        ac = (int)((kbx - a.kb1) * kTcBK);
+                        ac = (int)((kbx - a.kb1) * BK);
                         return &tmA1;
                     }
-                    ac = (int)(kbx * BK);  // concat parts take 32-channel K blocks only
+                    ac = (int)(kbx * BK);
                     return &tmA;
                 };
                 int ac;
@@ -1017,7 +1018,7 @@ static inline bool tc_igemm_supported(uint32_t kh, uint32_t kw, uint32_t sh, uin
 static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, uint32_t cout, uint32_t kh, uint32_t kw,
                           uint32_t sh, uint32_t sw, uint32_t dil, uint32_t pt, uint32_t pl, uint32_t oh, uint32_t ow,
                           uint32_t split_req, uint32_t res_kind, TcGeom *g, bool allow_halo = true,
-                          bool allow_flat = true)
+                          bool allow_flat = true, uint32_t bk_req = 0)
 {
     (void)ih; (void)iw; (void)pt; (void)pl;
     *g = TcGeom{};
@@ -1033,7 +1034,8 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     // blocks than 32-channel ones (36 channels: 3 against 2) the per-block
     // copies and waits cost more than the MMAs saved (RVM's 3x3 36 -> 16:
     // 1415 -> 1820 us), so those keep 32.
-    g->bk = (cin <= 16 && res_kind != kTcResUp2) ? 16u : (uint32_t)kTcBK;
+    // (bk_req: the K block width a concat-parts plan laid its weights out in)
+    g->bk = bk_req ? bk_req : (cin <= 16 && res_kind != kTcResUp2) ? 16u : (uint32_t)kTcBK;
     g->kblocks = (cin + g->bk - 1) / g->bk;
     g->k_iters = g->taps * g->kblocks;
     // Halo mode (k x k, stride 1, dilation 1): a 16 x 8 pixel tile's A for
@@ -1182,9 +1184,11 @@ static inline int tc_plan(uint32_t n, uint32_t ih, uint32_t iw, uint32_t cin, ui
     // stages (a 3 x 3 72 -> 32 at 40 x 72 took 346 us flat against 234 us
     // with the per-kx halo boxes, whose stages carry kh B tiles)
     if (g->flat && (g->stages < 3 || !g->b_resident))  // the per-kx halo boxes instead
-        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, true, false);
+        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, true, false,
+                       bk_req);
     if (g->halo && g->stages < 3)  // halo stages too large (wide N): per-tap boxes
-        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false, false);
+        return tc_plan(n, ih, iw, cin, cout, kh, kw, sh, sw, dil, pt, pl, oh, ow, split_req, res_kind, g, false, false,
+                       bk_req);
     if (g->stages < 2) return -2;
     // narrow k x k tiles (long K loops, N <= 128) are bound by the per-thread
     // MMA issue cost: two pipelines.  1x1 GEMMs keep one deep ring (their
@@ -1272,10 +1276,6 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     CUresult r = CUDA_SUCCESS;
     // 128-byte rows for 32-channel K blocks, 64-byte rows for 16-channel ones
     const CUtensorMapSwizzle swz = g.bk == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
-    if (parts != &one && g.bk != (uint32_t)kTcBK) {
-        snprintf(err, errlen, "concat parts take 32-channel K blocks");
-        return -2;
-    }
     for (int pi = 0; pi < parts->n && r == CUDA_SUCCESS; pi++) {
         const uintptr_t abase = (uintptr_t)(parts->x[pi] + parts->coff[pi]);
         const long long xs = parts->stride[pi];
@@ -1310,7 +1310,7 @@ static inline int tc_launch(const TcGeom &g, const ConvArgs &c, void *workspace,
     {
         // weights [tap][cout][kpad]: kpad = cin rounded up to 4, or with
         // parts every part's channels rounded up to whole K blocks
-        const uint32_t cin_pad = parts != &one ? g.kblocks * kTcBK : (c.cin + 3) / 4 * 4;
+        const uint32_t cin_pad = parts != &one ? g.kblocks * g.bk : (c.cin + 3) / 4 * 4;
         const cuuint64_t dims[3] = {(cuuint64_t)cin_pad, (cuuint64_t)c.cout, (cuuint64_t)(c.kh * c.kw)};
         const cuuint64_t strides[2] = {(cuuint64_t)cin_pad * 4, (cuuint64_t)cin_pad * 4 * c.cout};
         const cuuint32_t box[3] = {(cuuint32_t)g.bk, g.bn, 1};

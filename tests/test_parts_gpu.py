@@ -22,6 +22,8 @@ CASES = [  # n, h, w, parts, cout, k, stride, residual
     (2, 21, 37, (64, 36), 96, 3, 2, False),       # stride 2 (general mode), ragged frame
     (2, 10, 18, (96, 64, 128), 128, 1, 1, True),  # 1x1 GEMM, residual
     (4, 9, 16, (128, 40), 200, 3, 1, False),      # wide N (per-tap boxes), two N tiles
+    (2, 18, 30, (8, 16, 12), 24, 3, 1, False),    # three parts of <= 16 channels: 16-channel K blocks
+    (2, 10, 18, (16, 16), 48, 1, 1, True),        # 1x1 over two 16-channel parts
 ]
 
 
