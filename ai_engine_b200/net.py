@@ -28,7 +28,7 @@ Nodes (``Node.kind``):
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -108,6 +108,35 @@ def _pad4(c: int) -> int:
     return (c + 3) // 4 * 4
 
 
+def _pad_narrow_inputs(nodes: List[Node], inputs: Dict[str, Tuple[int, int, int]]) -> Tuple[List[Node], set]:
+    """A graph input whose channel count is not a multiple of 4 and that is
+    a concat part (RVM's 3-channel frame in its output block's concat) gets
+    a copy with its pixels padded to 4 lanes (a zero lane), made once per
+    step by a one-part concat (which writes each padded pixel whole, the
+    zero lane included, as one 16-byte store): the concat's part and the average pools that build the image
+    pyramid from it (whose outputs are the other concats' parts) read the
+    copy, so every such part is a TMA-compatible view and the concat can
+    be read in place by its conv.  Returns the rewritten nodes and the
+    names whose buffers carry the padding."""
+    shapes = infer_shapes(nodes, inputs)
+    narrow = {p for nd in nodes if nd.kind == "concat" for p in nd.ins
+              if p in inputs and shapes[p][2] % 4}
+    if not narrow:
+        return nodes, set()
+    shadow = {p: p + ".c4" for p in narrow}
+    padded = set(shadow.values())
+    out: List[Node] = [Node("concat", shadow[p], (p,)) for p in sorted(narrow)]
+    for nd in nodes:
+        if nd.kind == "concat" and any(p in shadow for p in nd.ins):
+            nd = replace(nd, ins=tuple(shadow.get(p, p) for p in nd.ins))
+        elif nd.kind == "avgpool" and nd.ins[0] in shadow:
+            nd = replace(nd, ins=(shadow[nd.ins[0]],))
+        if nd.kind == "avgpool" and nd.ins[0] in padded:
+            padded.add(nd.out)  # pools the zero lane too: stays zero
+        out.append(nd)
+    return out, padded
+
+
 @dataclass
 class _Rec:
     node: Node
@@ -127,7 +156,7 @@ class NetModel:
                  math: str = "auto", device=None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n = n
-        self.nodes = list(nodes)
+        self.nodes, padded = _pad_narrow_inputs(list(nodes), inputs)
         self.states = dict(states or {})
         self.outputs = list(outputs)
         self.shapes = infer_shapes(self.nodes, inputs)
@@ -143,7 +172,7 @@ class NetModel:
         # a concat whose consumers are all convs gets its channels padded to a
         # multiple of 4 (zero lanes, zero weights): the conv then reads it
         # through TMA on the tensor cores
-        self.cpad: Dict[str, int] = {}
+        self.cpad: Dict[str, int] = {name: _pad4(self.shapes[name][2]) for name in padded}
         for nd in self.nodes:
             if nd.kind == "concat":
                 c = self.shapes[nd.out][2]
@@ -241,7 +270,13 @@ class NetModel:
             stride = self.shapes[base][2] if base not in self.cpad else self.cpad[base]
             if base in self.fused_concat or stride % 4 or coff % 4:
                 return False
-        return True
+        # every part starts on a K block of the conv (16 channels when all
+        # parts have at most 16, else 32): at most one K block more than the
+        # concatenated tensor takes, or the extra MMAs cost more than the
+        # concat pass saves
+        cs = [self.shapes[pn][2] for pn in nd.ins]
+        bk = 16 if max(cs) <= 16 else 32
+        return sum((c + bk - 1) // bk * bk for c in cs) <= (sum(cs) + 31) // 32 * 32 + 32
 
     # -- tensors -----------------------------------------------------------------
     def _base(self, name: str) -> Tuple[str, int]:

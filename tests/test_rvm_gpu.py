@@ -33,7 +33,7 @@ def net():
 def _models(net, n, math="auto"):
     g, wts = net
     m = NetModel(g, wts, n, rvm.inputs(H, W), rvm.OUTPUTS, rvm.STATES, rvm.consts(), math=math)
-    o = OracleNet(g, wts, rvm.inputs(H, W), rvm.STATES, rvm.consts())
+    o = OracleNet(m.nodes, wts, rvm.inputs(H, W), rvm.STATES, rvm.consts())
     return m, o
 
 
@@ -156,7 +156,7 @@ def test_rvm_full_size_op_by_op(cuda_ok):
     g = rvm.build_graph()
     wts = rvm.init_weights(g, seed=12)
     m = NetModel(g, wts, 1, rvm.inputs(), rvm.OUTPUTS, rvm.STATES, rvm.consts())
-    o = OracleNet(g, wts, rvm.inputs(), rvm.STATES, rvm.consts())
+    o = OracleNet(m.nodes, wts, rvm.inputs(), rvm.STATES, rvm.consts())
     x = rvm.synthetic_frames(1, 2, seed=26)
     for t in range(2):
         m.bufs["src"].copy_(torch.from_numpy(x[t]))

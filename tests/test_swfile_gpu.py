@@ -77,7 +77,7 @@ def test_segm_r11_op_by_op(cuda_ok, model):
     m.bufs[inp].copy_(torch.from_numpy(x))
     m.record()
     torch.cuda.synchronize()
-    o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
+    o = OracleNet(m.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
     kinds = check_net_ops(m, o, sw.weights, "segm_r11")
     assert ("pw", "tf32") in kinds and ("dw", "ffma") in kinds, kinds
 
@@ -106,7 +106,7 @@ def test_synthetic_sw_graph_op_by_op(cuda_ok):
     from tests.test_swfile import synthetic_sw
     sw = synthetic_sw()
     m = NetModel(sw.nodes, sw.weights, 3, sw.inputs, sw.outputs, sw.states, sw.consts)
-    o = OracleNet(sw.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
+    o = OracleNet(m.nodes, sw.weights, sw.inputs, sw.states, sw.consts)
     x = np.random.default_rng(2).uniform(-1, 1, (3, 8, 8, 8)).astype(np.float32)
     for t in range(2):
         m.bufs["t0"].copy_(torch.from_numpy(x))
