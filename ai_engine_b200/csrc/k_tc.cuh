@@ -242,6 +242,21 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// The same MMA with each descriptor given as its low word (start address
+// and leading offset, which the k x k loops step with 32-bit adds) and its
+// high word (stride offset, version, swizzle: constant per kernel).
+__device__ __forceinline__ void mma_tf32_lo(uint32_t tmem_d, uint32_t alo, uint32_t blo, uint32_t hi, uint32_t idesc,
+                                            uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .b64 ad, bd;\n\t.reg .pred p;\n\t"
+        "mov.b64 ad, {%1, %3};\n\t"
+        "mov.b64 bd, {%2, %3};\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], ad, bd, %4, p;\n\t}" ::"r"(tmem_d),
+        "r"(alo), "r"(blo), "r"(hi), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t *bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -600,10 +615,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                          (acc0 && kk == 0) ? 0u : 1u);
                         }
                     };
-                    if constexpr (FLAT) {
+                    // k x k stride-1 tiles, 32-channel K blocks: the descriptors'
+                    // low words (start address / 16) step by 32-bit adds from tap
+                    // to tap and by 2 (32 bytes) from MMA to MMA; the high word
+                    // is constant (the issuing thread's instructions per MMA set
+                    // the pace of these narrow tiles: fpn.smooth4 148 -> 130 us,
+                    // RVM's d0.conv1 1422 -> 1231 us against 64-bit descriptors
+                    // built per tap; 16-channel blocks measured slower this way,
+                    // d0.conv2 638 -> 679 us, and keep them)
+                    const uint64_t d0 = smem_desc_k<BK>(sa);
+                    const uint32_t dhi = (uint32_t)(d0 >> 32);
+                    auto kblock_lo = [&](uint32_t al, uint32_t bl, uint32_t acc) {
+                        mma_tf32_lo(d, al, bl, dhi, idesc, acc);
+#pragma unroll
+                        for (uint32_t kk = 1; kk < BK / 8; kk++) mma_tf32_lo(d, al + kk * 2, bl + kk * 2, dhi, idesc, 1u);
+                    };
+                    if constexpr (FLAT && BK == 16) {
                         // K block k; tap (ky, kx) reads the box from row ky * bwx + kx
-                        // (a fully unrolled 3 x 3 loop with precomputed descriptors
-                        // measured 10-50% slower: smooth4 141 -> 168 us)
                         for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++)
                             for (uint32_t kx = 0; kx < (uint32_t)a.c.kw; kx++) {
                                 const uint32_t tap = ky * a.c.kw + kx;
@@ -613,7 +641,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 kblock(smem_desc_k<BK>(sa + (ky * a.bwx + kx) * rowb), smem_desc_k<BK>(sb),
                                        k == k0 && tap == 0);
                             }
-                    } else if (a.halo) {
+                    } else if constexpr (FLAT) {
+                        // K block k; tap (ky, kx) reads the box from row ky * bwx + kx
+                        // (a fully unrolled 3 x 3 loop with precomputed descriptors
+                        // measured 10-50% slower: smooth4 141 -> 168 us)
+                        const uint32_t a_lo = (uint32_t)d0;
+                        uint32_t bl = (uint32_t)smem_desc_k<BK>(
+                            a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + a.a_bytes);
+                        const uint32_t b_step = (a.b_resident ? a.kblocks * a.b_bytes : a.b_bytes) >> 4;
+                        uint32_t acc = k == k0 ? 0u : 1u;
+                        for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++) {
+                            uint32_t al = a_lo + ky * a.bwx * (rowb >> 4);
+                            for (uint32_t kx = 0; kx < (uint32_t)a.c.kw; kx++) {
+                                kblock_lo(al, bl, acc);
+                                acc = 1u;
+                                al += rowb >> 4;
+                                bl += b_step;
+                            }
+                        }
+                    } else if (a.halo && BK == 16) {
                         // tap (ky, kx): the stage's copy shifted down ky rows
                         // (ky * bw A rows, a multiple of 8 rows: swizzle-aligned)
                         const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
@@ -623,6 +669,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                     ? smem_u32(smem + a.bres_off + (tap * a.kblocks + kb) * a.b_bytes)
                                                     : sa + a.a_bytes + ky * a.b_bytes;
                             kblock(smem_desc_k<BK>(sa + ky * a.bw * rowb), smem_desc_k<BK>(sb), k == k0 && ky == 0);
+                        }
+                    } else if (a.halo) {
+                        const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
+                        uint32_t al = (uint32_t)d0;
+                        uint32_t bl = (uint32_t)smem_desc_k<BK>(
+                            a.b_resident ? smem_u32(smem + a.bres_off + (kx * a.kblocks + kb) * a.b_bytes) : sa + a.a_bytes);
+                        const uint32_t a_step = (a.bw * rowb) >> 4;
+                        const uint32_t b_step = (a.b_resident ? a.c.kw * a.kblocks * a.b_bytes : a.b_bytes) >> 4;
+                        uint32_t acc = k == k0 ? 0u : 1u;
+                        for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++) {
+                            kblock_lo(al, bl, acc);
+                            acc = 1u;
+                            al += a_step;
+                            bl += b_step;
                         }
                     } else {
                         const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + a.a_bytes;
