@@ -567,6 +567,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t P = a.pipes, RS = a.stages / a.pipes;
             const uint32_t idesc = idesc_tf32(kTcBM, a.bn);
             uint32_t it = 0, nt = 0;
+            uint32_t rs_slot = 0, rs_phase = 0;  // it % RS, (it / RS) & 1
             bool ok = true;
             if (a.b_resident && blockIdx.x + p * gridDim.x < a.units) {
                 if (*abort_flag || !mbar_wait(&sh.bfull, 0)) {
@@ -591,9 +592,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + ab * a.bn;
+                // halo mode: K iteration k = (column shift kx, K block kb)
+                uint32_t hkx = k0 / a.kblocks, hkb = k0 - hkx * a.kblocks;
                 for (uint32_t k = k0; k < k1; k++, it++) {
-                    const uint32_t s = p * RS + it % RS, ph = (it / RS) & 1;
-                    if (*abort_flag || !mbar_wait(&sh.full[s], ph)) {
+                    // (the ring slot and phase advance with the iteration; a
+                    // role that gave up leaves this wait to run out, so the
+                    // abort flag is read per tile, not per K block)
+                    const uint32_t s = p * RS + rs_slot, ph = rs_phase;
+                    if (++rs_slot == RS) {
+                        rs_slot = 0;
+                        rs_phase ^= 1u;
+                    }
+                    if (!mbar_wait(&sh.full[s], ph)) {
                         report_error(0x01000003);
                         *abort_flag = 1;
                         ok = false;
@@ -662,7 +672,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     } else if (a.halo && BK == 16) {
                         // tap (ky, kx): the stage's copy shifted down ky rows
                         // (ky * bw A rows, a multiple of 8 rows: swizzle-aligned)
-                        const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
+                        const uint32_t kx = hkx, kb = hkb;
                         for (uint32_t ky = 0; ky < (uint32_t)a.c.kh; ky++) {
                             const uint32_t tap = ky * a.c.kw + kx;
                             const uint32_t sb = a.b_resident
@@ -671,7 +681,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             kblock(smem_desc_k<BK>(sa + ky * a.bw * rowb), smem_desc_k<BK>(sb), k == k0 && ky == 0);
                         }
                     } else if (a.halo) {
-                        const uint32_t kx = k / a.kblocks, kb = k - kx * a.kblocks;
+                        const uint32_t kx = hkx, kb = hkb;
                         uint32_t al = (uint32_t)d0;
                         uint32_t bl = (uint32_t)smem_desc_k<BK>(
                             a.b_resident ? smem_u32(smem + a.bres_off + (kx * a.kblocks + kb) * a.b_bytes) : sa + a.a_bytes);
@@ -684,9 +694,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             al += a_step;
                             bl += b_step;
                         }
-                    } else {
+                    } else if constexpr (BK == 16) {
                         const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + a.a_bytes;
                         kblock(smem_desc_k<BK>(sa), smem_desc_k<BK>(sb), k == k0);
+                    } else {
+                        const uint32_t sb = a.b_resident ? smem_u32(smem + a.bres_off + k * a.b_bytes) : sa + a.a_bytes;
+                        kblock_lo((uint32_t)d0, (uint32_t)smem_desc_k<BK>(sb), k == k0 ? 0u : 1u);
+                    }
+                    if (++hkb == a.kblocks) {
+                        hkb = 0;
+                        hkx++;
                     }
                     mma_commit(&sh.empty[s]);
                 }
