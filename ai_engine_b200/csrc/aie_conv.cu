@@ -1236,7 +1236,10 @@ extern "C" int aie_gpool(uint32_t n, uint32_t px, uint32_t c, aie_tview in, void
     g.vec = c % 4 == 0 && eview_vec(g.x);
     const long long threads = (long long)n * g.groups;
     if (threads >= (1ll << 31)) return fail(AIE_E_UNSUPPORTED, "gpool: too many frames x channel groups");
-    gpool_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, (cudaStream_t)stream>>>(g);
+    if (g.vec && n <= 65535u)
+        gpool_staged_kernel<<<dim3((unsigned)((g.groups + kGpSlab - 1) / kGpSlab), n), 256, 0, (cudaStream_t)stream>>>(g);
+    else
+        gpool_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, (cudaStream_t)stream>>>(g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gpool launch");
     return AIE_OK;

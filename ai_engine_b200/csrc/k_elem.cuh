@@ -224,6 +224,78 @@ __global__ void __launch_bounds__(128) gpool_kernel(GpoolArgs g)
     for (int k = 0; k < nc; k++) yp[k] = r[k];
 }
 
+// The same pool for 16-byte channel views, fed through shared memory: a CTA
+// owns one frame and a slab of up to 128 channels (32 groups of four).  All
+// 256 threads stream the frame's pixels into a ring of kGpStages stages of
+// kGpStage float4 each (as many pixels per stage as fit: 512 / groups) with
+// 16-byte cp.async copies, and thread t < groups folds group t's four
+// channels over each landed stage in pixel order -- the same additions in
+// the same order as gpool_kernel, bit for bit.  One thread per channel group
+// walking the frame itself keeps too few bytes in flight (RVM's 36 x 64 x 72
+// pools: 4,608 threads, ~1.8 TB/s); here every thread of the CTA has copies
+// in flight for the stages ahead of the fold.
+constexpr int kGpSlab = 32;     // channel groups (of four) per CTA
+constexpr int kGpStage = 512;   // float4 per ring stage (8 KB)
+constexpr int kGpStages = 6;    // ring stages (48 KB)
+
+__global__ void __launch_bounds__(256) gpool_staged_kernel(GpoolArgs g)
+{
+    __shared__ __align__(16) float4 ring[kGpStages][kGpStage];
+    const int f = (int)blockIdx.y;
+    const int gbase = (int)blockIdx.x * kGpSlab;
+    const int gs = min(kGpSlab, g.groups - gbase);  // groups in this slab
+    const int ppc = kGpStage / gs;                   // pixels per stage
+    const long long q0 = (long long)f * g.px;
+    const int nchunks = (int)((g.px + ppc - 1) / ppc);
+    const int items = ppc * gs;
+    auto issue = [&](int chunk) {
+        if (chunk < nchunks) {
+            const unsigned p0 = (unsigned)chunk * ppc;
+            float4 *st = ring[chunk % kGpStages];
+            for (int i = threadIdx.x; i < items; i += blockDim.x) {
+                const int pp = i / gs, gr = i - pp * gs;
+                const bool ok = p0 + pp < g.px;
+                const float *src = ok ? g.x.p + (q0 + p0 + pp) * g.x.stride + g.x.coff + (gbase + gr) * 4 : g.x.p;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                                 (uint32_t)__cvta_generic_to_shared(st + i)),
+                             "l"(src), "r"(ok ? 16 : 0)
+                             : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");  // one group per stage, empty past the last
+    };
+    for (int c = 0; c < kGpStages - 1; c++) issue(c);
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    for (int j = 0; j < nchunks; j++) {
+        issue(j + kGpStages - 1);
+        asm volatile("cp.async.wait_group %0;" ::"n"(kGpStages - 1) : "memory");  // stage j (this thread's part)
+        __syncthreads();                                                         // everyone's part of stage j
+        if ((int)threadIdx.x < gs) {
+            const unsigned p0 = (unsigned)j * ppc;
+            const int np = (int)min((unsigned)ppc, g.px - p0);
+            const float4 *st = ring[j % kGpStages] + threadIdx.x;
+            for (int pp = 0; pp < np; pp++) {
+                const float4 v = st[pp * gs];
+                s0 = __fadd_rn(s0, v.x); s1 = __fadd_rn(s1, v.y); s2 = __fadd_rn(s2, v.z); s3 = __fadd_rn(s3, v.w);
+            }
+        }
+        __syncthreads();  // stage j is refilled by the next issue
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if ((int)threadIdx.x < gs) {
+        const float4 r = make_float4(__fmul_rn(s0, g.inv), __fmul_rn(s1, g.inv), __fmul_rn(s2, g.inv),
+                                     __fmul_rn(s3, g.inv));
+        const int ch0 = (gbase + (int)threadIdx.x) * 4;
+        float *yp = g.y + (long long)f * g.c + ch0;
+        if (ch0 + 4 <= g.c && ((uintptr_t)yp % 16) == 0) {
+            *reinterpret_cast<float4 *>(yp) = r;
+        } else {
+            const float rr[4] = {r.x, r.y, r.z, r.w};
+            for (int k = 0; k < 4 && ch0 + k < g.c; k++) yp[k] = rr[k];
+        }
+    }
+}
+
 // Average pool with a fixed kh * kw divisor (SwOp::Avgpool;
 // crates/ai-core/src/reference/pool.rs:22-46, the form RVM's decoder uses
 // for its 2x2 / stride-2 input pyramid): taps summed in (ky, kx) order from

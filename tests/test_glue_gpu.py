@@ -105,7 +105,8 @@ def test_mix(cuda_ok, c, views):
     assert np.all(got >= lo - 1e-5 * np.abs(lo) - 1e-6) and np.all(got <= hi + 1e-5 * np.abs(hi) + 1e-6)
 
 
-@pytest.mark.parametrize("n,h,w,c", [(3, 18, 32, 72), (2, 9, 16, 960), (2, 5, 7, 5), (1, 1, 1, 8), (4, 3, 3, 12)])
+@pytest.mark.parametrize("n,h,w,c", [(3, 18, 32, 72), (2, 9, 16, 960), (2, 5, 7, 5), (1, 1, 1, 8), (4, 3, 3, 12),
+                                     (2, 36, 64, 72), (3, 7, 9, 200), (2, 1, 1, 132)])
 def test_gpool(cuda_ok, n, h, w, c):
     rng = XorShift32(7301 + c)
     x = _rand(rng, n, h, w, c)
