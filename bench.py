@@ -285,7 +285,7 @@ RVM_METRIC = "RVM 144x256 frames/s, 1024 streams x 8 frames"
 # DRAM bytes per frame of the config-5 step's dominant launch (ncu at 16
 # streams, read + write, divided by 16; the capture's summary sits with the
 # ncu summaries under profiles/)
-RVM_TRAFFIC_PER_FRAME = {"d0.conv1": 6253072}
+RVM_TRAFFIC_PER_FRAME = {"d0.conv1": 6185696}
 
 
 def rvm_cpu_baseline(threads: int, min_seconds: float = 10.0):
