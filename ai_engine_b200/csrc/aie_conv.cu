@@ -612,8 +612,12 @@ extern "C" int aie_conv_run(const aie_plan *p, const void *in, const void *w, co
         // Large frames take the shared-memory halo tiles (8 x 16 output
         // pixels at stride 1, else 8 x 8; one 32-channel slice per CTA);
         // small frames (the deep 10x18 / 20x36 layers) would waste most of a
-        // tile and re-read wide halos, and keep the register-blocked kernel.
-        const bool tiled = blocked && d.dil == 1 && p->oh >= 40 && p->ow >= 64;
+        // tile and re-read wide halos, and keep the register-blocked kernel,
+        // as do channel counts whose last 32-channel slice would be mostly
+        // idle lanes (44 channels: 20 of 64 lanes idle; the blocked kernel
+        // works in groups of four).
+        const bool tiled = blocked && d.dil == 1 && p->oh >= 40 && p->ow >= 64 &&
+                           (d.cout % 32 == 0 || d.cout % 32 > 24);
         if (tiled) {
             DwTile tg;
             const bool wide = d.sh == 1 && p->ow > 12;
