@@ -1094,6 +1094,24 @@ extern "C" int aie_resize_bilinear(uint32_t n, uint32_t ih, uint32_t iw, uint32_
     if (mode == 0 && oh == 2 * ih && ow == 2 * iw) {
         const bool c4 = c % 4 == 0 && a.vec;
         const bool c1 = c == 1 && iw % 4 == 0 && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0;
+        const bool c2 = c == 2 && iw % 2 == 0 && (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0;
+        if (c2) {
+            Up2Args u;
+            u.x = (const float *)in;
+            u.add = (const float *)add;
+            u.y = (float *)out;
+            u.n = n; u.ih = ih; u.iw = iw; u.c = c; u.act = act;
+            u.div_g = make_fastdiv(1);
+            u.div_w = make_fastdiv((int)(iw / 2));
+            u.div_h = make_fastdiv((int)ih);
+            const long long threads = (long long)n * ih * (iw / 2);
+            if (threads + 256 < (1ll << 31)) {
+                resize_up2_c2_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(u);
+                cudaError_t e = cudaGetLastError();
+                if (e != cudaSuccess) return cuda_fail(e, "resize launch");
+                return AIE_OK;
+            }
+        }
         if (c4 || c1) {
             Up2Args u;
             u.x = (const float *)in;

@@ -703,6 +703,58 @@ __global__ void __launch_bounds__(256) resize_up2_kernel(const Up2Args a)
     }
 }
 
+// C == 2 (the shipped segmentation model's two logits): a thread owns two
+// source pixels (one float4 per source row: both channels of pixels j0 and
+// j0 + 1) plus their left and right neighbours and writes 4 output columns x
+// 2 output rows x 2 channels, with the same weights and lerp order as the
+// other cases (iw even, 16-byte aligned input and output).
+__global__ void __launch_bounds__(256) resize_up2_c2_kernel(const Up2Args a)
+{
+    const int W = a.iw >> 1;                         // thread columns per source row
+    const int idx = blockIdx.x * 256 + threadIdx.x;  // < n*ih*W < 2^31 (checked on the host)
+    if (idx >= a.n * a.ih * W) return;
+    const int r = fdiv(idx, a.div_w), jw = idx - r * W;
+    const int img = fdiv(r, a.div_h), i = r - img * a.ih;
+    const int oh = 2 * a.ih, ow = 2 * a.iw;
+    const int rows[3] = {max(i - 1, 0), i, min(i + 1, a.ih - 1)};
+    const float *xb = a.x + (long long)img * a.ih * a.iw * 2;
+    const int j0 = jw * 2;
+    float s[3][4][2];  // source rows i-1..i+1 x columns j0-1..j0+2 x channels
+#pragma unroll
+    for (int rr = 0; rr < 3; rr++) {
+        const float *row = xb + (long long)rows[rr] * a.iw * 2;
+        const float4 m = __ldg(reinterpret_cast<const float4 *>(row + j0 * 2));
+        const float2 lf = __ldg(reinterpret_cast<const float2 *>(row + max(j0 - 1, 0) * 2));
+        const float2 rt = __ldg(reinterpret_cast<const float2 *>(row + min(j0 + 2, a.iw - 1) * 2));
+        s[rr][0][0] = lf.x; s[rr][0][1] = lf.y;
+        s[rr][1][0] = m.x;  s[rr][1][1] = m.y;
+        s[rr][2][0] = m.z;  s[rr][2][1] = m.w;
+        s[rr][3][0] = rt.x; s[rr][3][1] = rt.y;
+    }
+#pragma unroll
+    for (int ar = 0; ar < 2; ar++) {
+        const float ty = ar ? 0.25f : 0.75f;
+        float o[8];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int bc = q & 1, k = (q >> 1) + bc;  // source columns k, k+1 of s (s[.][0] = j0-1)
+            const float tx = bc ? 0.25f : 0.75f;
+#pragma unroll
+            for (int ch = 0; ch < 2; ch++)
+                o[2 * q + ch] = up2_lerp(s[ar][k][ch], s[ar][k + 1][ch], s[ar + 1][k][ch], s[ar + 1][k + 1][ch], tx, ty);
+        }
+        const long long px = ((long long)img * oh + 2 * i + ar) * ow + 2 * j0;
+        if (a.add) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = __fadd_rn(o[e], __ldg(a.add + px * 2 + e));
+        }
+        act_apply_strict_n<8>(a.act, o, 0, 2);  // two channels: ai-cpu's scalar activation for both
+        float4 *yr = reinterpret_cast<float4 *>(a.y + px * 2);
+        yr[0] = make_float4(o[0], o[1], o[2], o[3]);
+        yr[1] = make_float4(o[4], o[5], o[6], o[7]);
+    }
+}
+
 __global__ void __launch_bounds__(256) resize_bilinear_kernel(const ResizeArgs a)
 {
     const int cg = (a.c + 3) >> 2;

@@ -267,7 +267,10 @@ def test_canary_no_write_outside_output(cuda_ok):
     # exact 2x (the dedicated source-pixel kernel): C4, one channel, the
     # benchmark's mask and lateral shapes, and 2x shapes it must leave to the
     # general kernel (width not a multiple of 4 with one channel)
-    (32, 9, 13, 18, 26), (1, 5, 8, 10, 16), (1, 80, 144, 160, 288), (32, 40, 72, 80, 144), (1, 5, 9, 10, 18)])
+    (32, 9, 13, 18, 26), (1, 5, 8, 10, 16), (1, 80, 144, 160, 288), (32, 40, 72, 80, 144), (1, 5, 9, 10, 18),
+    # two channels (the shipped model's logits): even widths take the
+    # two-pixel kernel, an odd width the general one
+    (2, 5, 8, 10, 16), (2, 1, 2, 2, 4), (2, 80, 144, 160, 288), (2, 5, 9, 10, 18)])
 def test_resize_bilinear_bit_exact(cuda_ok, c, ih, iw, oh, ow):
     """GPU resize (+ fused add) equals the CPU restatement bit for bit:
     vector channel groups, ragged channel tails, the 4-pixel single-channel
